@@ -1,0 +1,412 @@
+"""Benchmark of the MoE-expert decode hot path (BASELINE config 1 on one B200).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one MoE-layer forward (router -> top-k -> gate/up dequant-GEMV +
+SwiGLU -> down dequant-GEMV + weighted combine + shared expert) over one batch
+of T seeded bf16 tokens, on the DeepSeek-V3-shape layer of config 1 (H 7168,
+256 routed + 1 shared experts, top-8, I 2048, 4-bit g64 MLX affine). Weights
+of several distinct seeded layers are resident and steps cycle through them,
+so every step streams a different layer's experts (>= 227 MB, larger than
+L2) — no L2 flush is needed.
+
+Prints one JSON line (rank 0). `value` is tokens/s over the timed steps with
+inputs resident in HBM; `e2e` is the same metric through the host-buffer
+C-ABI call (pinned host x in, host out, copies inside the timed region);
+`roofline` is for the dominant kernel (gate/up GEMV), from CUDA events on the
+launching stream; `cpu_baseline` times the CPU oracle on the host cores.
+Under torchrun (N > 1) every rank runs the same workload on its own GPU
+(replicas) and the time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "minirun-app_b200"))
+
+METRIC = ("MoE-layer decode tokens/s; dequant-GEMV HBM GB/s (% of ~8 TB/s) at 1/2/4/8 GPUs")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--tokens", type=int, default=64)
+    p.add_argument("--layers", type=int, default=4, help="distinct resident layers cycled")
+    p.add_argument("--sweep", default="1,8", help="extra token counts measured (no e2e)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------- ours
+
+def run_ours(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    import minirun_moe as M
+    from minirun_moe import synth as S
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=300))
+    spec = S.CONFIGS[1]
+    T = args.tokens
+    NL = max(1, args.layers)
+    layers = [S.synth_layer(spec, layer=l, device=local) for l in range(NL)]
+    NB = NL + 1
+    token_counts = [T] + [int(t) for t in args.sweep.split(",") if t and int(t) != T]
+    xs = {t: [S.synth_x(spec, t, layer=0, batch=b, device=local) for b in range(NB)]
+          for t in token_counts}
+    ctx = M.Context.get(local)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def schedule(i):
+        return layers[i % NL], i % NB
+
+    def timed(tok, steps, warm):
+        outs = torch.empty((tok, spec.hidden), dtype=torch.bfloat16, device=dev)
+        for i in range(warm):
+            lay, b = schedule(i)
+            lay.forward(xs[tok][b], out=outs, selection=False)
+        torch.cuda.synchronize()
+        barrier()
+        st = torch.cuda.current_stream()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(steps):
+            lay, b = schedule(i)
+            lay.forward(xs[tok][b], out=outs, selection=False)
+        e1.record(st)
+        torch.cuda.synchronize()
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    def distinct_experts(tok, steps):
+        us = []
+        for i in range(steps):
+            lay, b = schedule(i)
+            _, sel = lay.forward(xs[tok][b])
+            us.append(len(set(sel.ids.cpu().view(-1).tolist())))
+        return us
+
+    def step_bytes(tok, U):
+        eb = spec.expert_bytes()
+        return (U + 1) * eb + spec.router_bytes() + 2 * tok * spec.hidden * 2
+
+    def gate_up_bytes(tok, U):
+        return ((U + 1) * 2 * spec.proj_bytes(spec.inter, spec.hidden) + tok * spec.hidden * 2
+                + (tok * spec.top_k + 2 * tok) * spec.inter * 2)
+
+    hbm, peak_kind = peaks()
+    K, W = args.steps, max(3, args.warmup)
+    with ClockSampler(local) as clk:
+        ms = timed(T, K, W)
+    clocks = clk.summary()
+    us = distinct_experts(T, K)
+    avg_bytes = sum(step_bytes(T, u) for u in us) / len(us)
+    ms_step = ms / K
+    value = world * T * K / (ms / 1e3)
+
+    # per-kernel durations (CUDA events around each launch, same stream)
+    ctx.profile(True)
+    timed(T, K, 0)
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    gu_ms, gu_n = prof["gate_up"]
+    gu_avg_ms = gu_ms / max(gu_n, 1)
+    gu_bytes = sum(gate_up_bytes(T, u) for u in us) / len(us)
+    achieved = gu_bytes / (gu_avg_ms / 1e3) / 1e9
+    kern = {k: {"ms_per_launch": v[0] / max(v[1], 1), "launches": v[1]} for k, v in prof.items()}
+    traffic = read_traffic()
+
+    sweep = {}
+    for tok in token_counts[1:]:
+        m2 = timed(tok, K, W)
+        u2 = distinct_experts(tok, K)
+        b2 = sum(step_bytes(tok, u) for u in u2) / len(u2)
+        sweep[str(tok)] = {"tokens_per_s": world * tok * K / (m2 / 1e3),
+                           "ms_per_step": m2 / K,
+                           "layer_gbs": b2 / (m2 / K / 1e3) / 1e9,
+                           "layer_frac_of_hbm": b2 / (m2 / K / 1e3) / 1e9 / hbm,
+                           "distinct_experts_avg": sum(u2) / len(u2)}
+
+    # e2e: pinned host x in, host out, through the host-buffer C-ABI call
+    xh = [x.cpu().pin_memory() for x in xs[T]]
+    oh = torch.empty((T, spec.hidden), dtype=torch.bfloat16).pin_memory()
+    for i in range(W):
+        lay, b = schedule(i)
+        lay.forward_host(xh[b], oh, device=local)
+    torch.cuda.synchronize()
+    barrier()
+    st = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(K):
+        lay, b = schedule(i)
+        lay.forward_host(xh[b], oh, device=local)
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    ctx.sync_check()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(T)
+
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 activations, 4-bit affine weights (u4 codes, bf16 scale/bias), fp32 "
+                 "accumulate",
+        "data": "synthetic (SplitMix64-seeded, BASELINE config 1 distributions)",
+        "config": {
+            "workload": f"config1 decode T={T}: H7168, 256+1 experts, top-8, I2048, 4-bit g64",
+            "tokens": T,
+            "global_batch": world * T,
+            "layers_cycled": NL,
+            "l2": "inputs larger than L2: consecutive steps read different layers' experts "
+                  "(>= 227 MB each)",
+            "parallelism": "single GPU" if world == 1 else f"{world} replicas (one per GPU)",
+            "distinct_experts_avg": sum(us) / len(us),
+            "layer_bytes_per_step": avg_bytes,
+            "layer_gbs": avg_bytes / (ms_step / 1e3) / 1e9,
+            "layer_frac_of_hbm": avg_bytes / (ms_step / 1e3) / 1e9 / hbm,
+            "kernels": kern,
+            "sweep": sweep,
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "gemv gate/up (+SwiGLU)",
+            "achieved": achieved,
+            "peak": hbm,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / hbm,
+            "algorithmic_bytes_per_launch": gu_bytes,
+            "traffic": traffic,
+        },
+        "e2e": {
+            "value": world * T * K / (e2e_ms / 1e3),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": T * spec.hidden * 2,
+            "d2h_bytes_per_step": T * spec.hidden * 2,
+        },
+        "gpu_launches": K * 4,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def read_traffic():
+    """DRAM bytes per gate/up launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "gemv_gate_up_config1.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ------------------------------------------------------------- CPU baseline
+
+def cpu_baseline(T: int, steps: int = 1):
+    """The CPU oracle (C, OpenMP, all host threads) on config 1 with T tokens."""
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+    cfg = O.CONFIGS[1]
+    x = O.gen_x(cfg, T, layer=0, batch=0)
+    L = O.gen_layer(cfg, layer=0, experts=O.selected_experts(cfg, x))
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        O.moe_layer_forward(L, x)
+        times.append(time.perf_counter() - t0)
+    dt = sum(times) / len(times)
+    return {"value": T / dt, "unit": "tokens/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"config1 layer 0, one {T}-token batch, {steps} forward(s), "
+                      f"{dt:.2f} s each (weights generation excluded)"}
+
+
+def run_reference(args, world, rank, local):
+    """The reference arm: the CPU restatement of the path (the reference's
+    own implementation is Swift/MLX on Apple GPUs and cannot run here)."""
+    if rank != 0:
+        return
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+    cfg = O.CONFIGS[1]
+    T = args.tokens
+    x = O.gen_x(cfg, T, layer=0, batch=0)
+    L = O.gen_layer(cfg, layer=0, experts=O.selected_experts(cfg, x))
+    t0 = time.perf_counter()
+    O.moe_layer_forward(L, x)
+    est = time.perf_counter() - t0
+    K = max(2, min(args.steps, int(150 / max(est, 1e-3))))
+    W = max(1, min(args.warmup, 1))
+    for _ in range(W):
+        O.moe_layer_forward(L, x)
+    t0 = time.perf_counter()
+    for _ in range(K):
+        O.moe_layer_forward(L, x)
+    dt = time.perf_counter() - t0
+    value = T * K / dt
+    cores = O.num_threads()
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": dt / K * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 activations, 4-bit affine weights, exact (fp64) accumulation",
+        "data": "synthetic (SplitMix64-seeded, BASELINE config 1 distributions)",
+        "config": {"workload": f"config1 decode T={T}: H7168, 256+1 experts, top-8, I2048, "
+                               f"4-bit g64", "tokens": T,
+                   "note": "the reference's MLX/Metal path is unavailable on this box (no "
+                           "Apple GPU, Swift or mlx); the CPU restatement of its arithmetic "
+                           "(oracle/, C + OpenMP) stands in"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"config1 layer 0, one {T}-token batch per step"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, world, rank, local)
+    else:
+        run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,285 @@
+/*
+ * minirun_moe.h — C ABI of the B200 (sm_100a) MoE-expert hot path.
+ *
+ * This library replaces, for one path, the Swift/MLX operators that Minirun's
+ * ModelAdapters call through MLXBridge:
+ *
+ *   router scoring + top-k  ->  gathered affine-quantized matmul over only the
+ *   selected experts (gate/up, SwiGLU, down)  ->  routing-weighted combine
+ *   + shared expert.
+ *
+ * Every entry point names the reference interface it replaces as
+ * `Sources/<path>:<line>` relative to the reference repository
+ * (nanguoyu/minirun-app).
+ *
+ * Conventions
+ *   - Every function returns an mr_status. No exception, trap or abort crosses
+ *     this boundary; mr_last_error(ctx) gives a message for the last failure
+ *     on that context.
+ *   - Tensors are plain device pointers in row-major order. bf16 is passed as
+ *     uint16_t bit patterns. The caller owns every pointer it passes.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream). All device work of a call is enqueued on it; calls return
+ *     without waiting for the GPU.
+ *   - One mr_ctx per host thread. A context owns a device workspace that grows
+ *     on demand (mr_ctx_reserve pre-sizes it, e.g. before CUDA graph capture).
+ *   - Device-side faults are never raised: invalid expert ids or non-finite
+ *     router scores set a device error word, which mr_ctx_check() reads.
+ *   - Affine format (MLX `mode: .affine`): packed uint32 [experts?, out,
+ *     in*bits/32], element j of a row at bit (j mod (32/bits))*bits of word
+ *     j/(32/bits); scales and biases [experts?, out, in/group] in one float
+ *     dtype; w = scale*q + bias.
+ */
+#ifndef MINIRUN_MOE_H
+#define MINIRUN_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MR_ABI_VERSION 1
+
+typedef enum mr_status {
+  MR_OK = 0,
+  MR_ERR_INVALID_ARGUMENT = 1, /* shape/dtype/config rejected before launch */
+  MR_ERR_UNSUPPORTED = 2,      /* legal in the reference, not built here   */
+  MR_ERR_CUDA = 3,             /* a CUDA runtime call failed               */
+  MR_ERR_OUT_OF_MEMORY = 4,    /* workspace or cache allocation failed     */
+  MR_ERR_DEVICE = 5,           /* device error word set (see mr_ctx_check) */
+  MR_ERR_TIMEOUT = 6,          /* a bounded device/host wait expired       */
+  MR_ERR_BUDGET = 7,           /* refused: byte budget cannot hold the set */
+  MR_ERR_NCCL = 8,             /* an NCCL call failed                      */
+  MR_ERR_STATE = 9             /* call out of order (e.g. EP not initialised) */
+} mr_status;
+
+typedef enum mr_dtype {
+  MR_DTYPE_BF16 = 0,
+  MR_DTYPE_F16 = 1,
+  MR_DTYPE_F32 = 2
+} mr_dtype;
+
+/* Device error word bits (mr_ctx_check). */
+#define MR_DEVERR_BAD_EXPERT_ID 0x1u   /* an id outside [0, experts)     */
+#define MR_DEVERR_NONFINITE_SCORE 0x2u /* router produced NaN/Inf score  */
+#define MR_DEVERR_RENORM_ZERO 0x4u     /* selected weights sum <= 0      */
+
+typedef struct mr_ctx mr_ctx;
+
+/* ---------------------------------------------------------------- context */
+
+/* Library ABI version (MR_ABI_VERSION of the build). */
+int mr_abi_version(void);
+/* Static text for a status code. */
+const char* mr_status_string(mr_status status);
+
+/* Create a context bound to CUDA device `device`. */
+mr_status mr_ctx_create(int device, mr_ctx** out);
+mr_status mr_ctx_destroy(mr_ctx* ctx);
+/* Message of the last failure on this context ("" if none). */
+const char* mr_last_error(const mr_ctx* ctx);
+/* Synchronise `stream`, read and clear the device error word. Returns
+ * MR_ERR_DEVICE (and writes the bits to *bits_out if non-NULL) when set. */
+mr_status mr_ctx_check(mr_ctx* ctx, void* stream, uint32_t* bits_out);
+/* Pre-size the workspace for layers up to these sizes (graph capture needs
+ * a workspace that will not grow). */
+mr_status mr_ctx_reserve(mr_ctx* ctx, int64_t max_tokens, int32_t top_k,
+                         int32_t experts, int64_t hidden, int64_t inter);
+
+/* ----------------------------------------------------- affine op API
+ * Mirrors Sources/MLXBridge/AffineWeights.swift. */
+
+/* AffineWeights (AffineWeights.swift:65-157). experts == 0 means a single
+ * [out, in] matrix; experts > 0 an expert stack. */
+typedef struct mr_affine_desc {
+  const uint32_t* packed; /* [experts?, out, in*bits/32] */
+  const void* scales;     /* [experts?, out, in/group], scale_dtype */
+  const void* biases;     /* same shape and dtype as scales */
+  int32_t experts;
+  int64_t out_features;
+  int64_t in_features;
+  int32_t group_size;
+  int32_t bits;
+  mr_dtype scale_dtype;
+} mr_affine_desc;
+
+/* Host-only validation, the checks of AffineWeights.init
+ * (AffineWeights.swift:84-157): bits divide 32, group > 0, in % group == 0,
+ * pointers non-NULL. Needs no GPU. `msg` (may be NULL) receives the reason. */
+mr_status mr_affine_validate(const mr_affine_desc* w, char* msg, size_t msg_len);
+
+/* affineMM (AffineWeights.swift:239-254): out[T, out] = x[T, in] . W^T.
+ * x, out bf16; fp32 accumulation; output rounded to bf16. */
+mr_status mr_affine_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens,
+                       const mr_affine_desc* w, uint16_t* out, void* stream);
+
+/* affineGatherMM (AffineWeights.swift:283-318):
+ * out[t, j, :] = W[ids[t, j]] . x[t, :], ids int32 [T, k] on the device,
+ * out bf16 [T, k, out]. x is broadcast per token exactly as the reference's
+ * [T,1,1,in] reshape; ids need not be sorted and may repeat. */
+mr_status mr_affine_gather_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens,
+                              const int32_t* ids, int32_t top_k,
+                              const mr_affine_desc* w, uint16_t* out,
+                              void* stream);
+
+/* affineDequantize (AffineWeights.swift:328-342): dense fp32 copy
+ * [experts?, out, in] of w = scale*q + bias. Validation only. */
+mr_status mr_affine_dequantize(mr_ctx* ctx, const mr_affine_desc* w, float* out,
+                               void* stream);
+
+/* ---------------------------------------------------------------- router
+ * K3Router.select (Sources/ModelAdapters/Operators/MoE.swift:77-150),
+ * DeepSeekV4Router.select (Operators/DeepSeekV4Routing.swift:100-280),
+ * QwenRouter.select (Model/QwenMoEModel.swift:74-131). */
+
+typedef enum mr_scoring {
+  MR_SCORING_SIGMOID = 0,      /* MoE.swift:106                     */
+  MR_SCORING_SOFTMAX = 1,      /* QwenMoEModel.swift:89             */
+  MR_SCORING_SQRT_SOFTPLUS = 2 /* DeepSeekV4Routing.swift:148       */
+} mr_scoring;
+
+typedef enum mr_renorm {
+  MR_RENORM_NONE = 0,  /* weights = gathered scores                      */
+  MR_RENORM_PLAIN = 1, /* w / sum(w) (DeepSeekV4Routing.swift:259-270,
+                          QwenMoEModel.swift:122-127)                     */
+  MR_RENORM_EPS = 2    /* if k > 1: w / (sum(w) + eps) (MoE.swift:142-144) */
+} mr_renorm;
+
+typedef struct mr_router_config {
+  int32_t experts;
+  int32_t top_k;         /* 1 <= top_k < experts */
+  mr_scoring scoring;
+  mr_renorm renorm;
+  float renorm_eps;      /* MR_RENORM_EPS only (K3: 1e-20) */
+  float routed_scale;    /* multiplies the final weights (1.0 = none) */
+  const float* correction_bias; /* [experts] device fp32 or NULL; steers the
+                                   choice only (MoE.swift:107) */
+} mr_router_config;
+
+mr_status mr_router_config_validate(const mr_router_config* cfg, char* msg,
+                                    size_t msg_len);
+
+/* logits = fp32(x) . fp32(W_r)^T (k3Linear, Operators/Linear.swift:55),
+ * then the selection: descending choice score, ties to the lower expert id;
+ * weights gathered from the unbiased scores; renorm; x routed_scale.
+ * x bf16 [T, H]; router_w bf16 [E, H]; ids int32 [T, k]; weights fp32 [T, k];
+ * margins fp32 [T] or NULL ((kth - first rejected) / max(|kth|, |rej|));
+ * logits_out fp32 [T, E] or NULL. */
+mr_status mr_router_select(mr_ctx* ctx, const uint16_t* x, int64_t tokens,
+                           int64_t hidden, const uint16_t* router_w,
+                           const mr_router_config* cfg, int32_t* ids,
+                           float* weights, float* margins, float* logits_out,
+                           void* stream);
+
+/* The same selection from logits produced elsewhere
+ * (MoE.swift:98-150 `select(logits:...)`). logits fp32 [T, E] on device. */
+mr_status mr_router_select_logits(mr_ctx* ctx, const float* logits,
+                                  int64_t tokens, const mr_router_config* cfg,
+                                  int32_t* ids, float* weights, float* margins,
+                                  void* stream);
+
+/* ------------------------------------------------------------- MoE layer
+ * DeepSeekV4MoEFFN router -> routed -> shared section
+ * (Model/DeepSeekV4HashFFN.swift:75-106), DeepSeekV4RoutedExperts.forward
+ * (Loading/DeepSeekV4ExpertBackend.swift:267-344), shared expert
+ * (DeepSeekV4HashFFN.swift:223-255) and QwenMoEBlock.forward
+ * (Model/QwenMoEModel.swift:312-362). */
+
+typedef enum mr_weight_placement {
+  /* h = silu(gate)*up*w before w2; routed = bf16(sum_j down_j)
+   * (DeepSeekV4ExpertBackend.swift:329-342) */
+  MR_WEIGHT_BEFORE_DOWN = 0,
+  /* h = silu(gate)*up; out = sum_j down_j * w_j
+   * (QwenMoEModel.swift:340-351, MoE.swift:250-251) */
+  MR_WEIGHT_AFTER_DOWN = 1
+} mr_weight_placement;
+
+/* One routed expert's three projections, for experts addressed through a
+ * pointer table (an HBM expert cache) instead of a contiguous stack. */
+typedef struct mr_expert_ptrs {
+  const uint32_t* packed[3]; /* gate (w1), up (w3), down (w2) */
+  const void* scales[3];
+  const void* biases[3];
+} mr_expert_ptrs;
+
+typedef struct mr_moe_layer {
+  int64_t hidden;        /* H */
+  int64_t inter;         /* routed expert intermediate I */
+  int64_t shared_inter;  /* shared expert intermediate; 0 = no shared expert */
+  mr_router_config router;
+  const uint16_t* router_w;   /* bf16 [E, H] */
+  /* Routed experts, as stacks [E, ...] (used when expert_table == NULL). */
+  mr_affine_desc gate, up, down;
+  /* Or a device table of E mr_expert_ptrs (same bits/group/scale dtype as
+   * gate/up/down, whose pointers are then ignored). */
+  const mr_expert_ptrs* expert_table;
+  /* Shared expert, single matrices (experts == 0). */
+  mr_affine_desc shared_gate, shared_up, shared_down;
+  float swiglu_limit;    /* > 0: gate <= L, -L <= up <= L; 0 = off */
+  mr_weight_placement weight_placement;
+} mr_moe_layer;
+
+mr_status mr_moe_layer_validate(const mr_moe_layer* layer, char* msg,
+                                size_t msg_len);
+
+/* out bf16 [T, H] = routed + shared for x bf16 [T, H]. ids_out int32 [T, k],
+ * weights_out fp32 [T, k] and margins_out fp32 [T] are optional (NULL). */
+mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* layer,
+                               const uint16_t* x, int64_t tokens, uint16_t* out,
+                               int32_t* ids_out, float* weights_out,
+                               float* margins_out, void* stream);
+
+/* Host-buffer form of mr_moe_layer_forward, the view of a caller that holds
+ * arrays in host memory (the reference's per-layer `eval` boundary,
+ * Model/DeepSeekV4HashFFN.swift:113-115): copies x_host (bf16 [T, H],
+ * preferably pinned) in, runs the layer and copies out_host (bf16 [T, H]) and
+ * ids_host (int32 [T, k], may be NULL) back, all on `stream`. Returns without
+ * waiting; synchronise `stream` before reading the outputs. */
+mr_status mr_moe_layer_forward_host(mr_ctx* ctx, const mr_moe_layer* layer,
+                                    const uint16_t* x_host, int64_t tokens,
+                                    uint16_t* out_host, int32_t* ids_host,
+                                    void* stream);
+
+/* ----------------------------------------------------------- profiling
+ * CUDA-event timing of the kernels mr_moe_layer_forward launches (off by
+ * default; the events are recorded on the caller's stream around each
+ * launch). Kernel classes: */
+#define MR_KERNEL_ROUTER_LOGITS 0
+#define MR_KERNEL_TOPK_PLAN 1
+#define MR_KERNEL_GATE_UP 2
+#define MR_KERNEL_DOWN_COMBINE 3
+#define MR_KERNEL_CLASSES 4
+
+mr_status mr_ctx_profile(mr_ctx* ctx, int enable);
+/* Wait for the recorded launches, then return per class the accumulated
+ * milliseconds and launch counts since the last read (arrays of length n,
+ * n <= MR_KERNEL_CLASSES), and reset them. */
+mr_status mr_ctx_profile_read(mr_ctx* ctx, double* ms, int64_t* launches, int n);
+
+/* ------------------------------------------------------ synthetic inputs
+ * Counter-based SplitMix64 generators (StorageCore/Generator/SplitMix64.swift
+ * :13-50) used to build the benchmark configurations on the device. */
+
+/* label for a seeded tensor: (layer << 40) | (kind << 32) | (expert << 8) | proj */
+uint64_t mr_synth_label(uint32_t layer, uint32_t kind, uint32_t expert,
+                        uint32_t proj);
+/* SplitMix64.derive(seed, label) */
+uint64_t mr_synth_derive(uint64_t seed, uint64_t label);
+/* n uint32 words; word i = 32-bit half (i & 1) of SplitMix64.value(seed, i/2) */
+mr_status mr_synth_words(mr_ctx* ctx, uint64_t seed, int64_t n, uint32_t* out,
+                         void* stream);
+/* n bf16 values: bf16(std * N(0,1)) (|.| if absval), Box-Muller over
+ * value(seed, 2i), value(seed, 2i+1). */
+mr_status mr_synth_normal_bf16(mr_ctx* ctx, uint64_t seed, int64_t n, float std,
+                               int absval, uint16_t* out, void* stream);
+/* biases[i] = bf16(-2^(bits-1) * scales[i]) */
+mr_status mr_synth_affine_biases(mr_ctx* ctx, const uint16_t* scales, int64_t n,
+                                 int32_t bits, uint16_t* biases, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINIRUN_MOE_H */

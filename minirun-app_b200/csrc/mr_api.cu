@@ -1,0 +1,971 @@
+// mr_api.cu — the C ABI of libminirun_moe (include/minirun_moe.h): context,
+// host-side validation (the reference's AffineWeights / router / MoE guards),
+// workspace layout and kernel launches.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "mr_launch.h"
+#include "mr_router.cuh"
+
+namespace mr {
+
+mr_status fail(mr_ctx* ctx, mr_status st, const std::string& msg) {
+  if (ctx) ctx->last_error = msg;
+  return st;
+}
+
+mr_status cuda_check(mr_ctx* ctx, cudaError_t err, const char* what) {
+  if (err == cudaSuccess) return MR_OK;
+  std::string m = std::string(what) + ": " + cudaGetErrorString(err);
+  return fail(ctx, err == cudaErrorMemoryAllocation ? MR_ERR_OUT_OF_MEMORY : MR_ERR_CUDA, m);
+}
+
+mr_status ensure_workspace(mr_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->ws_bytes) return MR_OK;
+  if (ctx->ws) {
+    cudaError_t e = cudaFree(ctx->ws);  // synchronises the device
+    ctx->ws = nullptr;
+    ctx->ws_bytes = 0;
+    if (e != cudaSuccess) return cuda_check(ctx, e, "cudaFree(workspace)");
+  }
+  const size_t want = bytes + bytes / 4 + (1 << 20);
+  cudaError_t e = cudaMalloc(&ctx->ws, want);
+  if (e != cudaSuccess) {
+    ctx->ws = nullptr;
+    return cuda_check(ctx, e, "cudaMalloc(workspace)");
+  }
+  ctx->ws_bytes = want;
+  return MR_OK;
+}
+
+// Bump allocator over the workspace; a first pass with base == nullptr sizes it.
+struct Bump {
+  char* base;
+  size_t off = 0;
+  template <class T>
+  T* take(size_t count) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+static void set_msg(char* msg, size_t len, const std::string& s) {
+  if (msg && len > 0) snprintf(msg, len, "%s", s.c_str());
+}
+
+// AffineWeights.init (Sources/MLXBridge/AffineWeights.swift:84-157), plus the
+// limits of this build (group 64; bits 2/4/8).
+static mr_status validate_affine(const mr_affine_desc* w, std::string& why) {
+  if (!w) {
+    why = "affine descriptor is NULL";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (w->scale_dtype != MR_DTYPE_BF16 && w->scale_dtype != MR_DTYPE_F16 &&
+      w->scale_dtype != MR_DTYPE_F32) {
+    why = "affine scales must be a floating-point type — .bfloat16 for this checkpoint, "
+          ".float16 or .float32 for others";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (w->bits <= 0 || 32 % w->bits != 0) {
+    why = "bits " + std::to_string(w->bits) + " must divide 32 for the uint32 packing";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (w->group_size <= 0) {
+    why = "group size must be positive";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (w->experts < 0 || w->out_features <= 0 || w->in_features <= 0) {
+    why = "packed shape must be positive (experts " + std::to_string(w->experts) + ", out " +
+          std::to_string(w->out_features) + ", in " + std::to_string(w->in_features) + ")";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (w->in_features % w->group_size != 0) {
+    why = "inFeatures " + std::to_string(w->in_features) +
+          " is not a multiple of the group size " + std::to_string(w->group_size) +
+          "; partial final groups are not supported";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (!w->packed || !w->scales || !w->biases) {
+    why = "packed, scales and biases pointers must be non-NULL";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (w->bits != 2 && w->bits != 4 && w->bits != 8) {
+    why = "bits " + std::to_string(w->bits) + " is valid MLX affine but not built here (2, 4, 8)";
+    return MR_ERR_UNSUPPORTED;
+  }
+  if (w->group_size != kGroup) {
+    why = "group size " + std::to_string(w->group_size) +
+          " is valid MLX affine but not built here (64)";
+    return MR_ERR_UNSUPPORTED;
+  }
+  if ((reinterpret_cast<uintptr_t>(w->packed) & 15u) != 0) {
+    why = "packed pointer must be 16-byte aligned";
+    return MR_ERR_UNSUPPORTED;
+  }
+  return MR_OK;
+}
+
+static mr_status validate_router(const mr_router_config* c, std::string& why) {
+  if (!c) {
+    why = "router config is NULL";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (c->experts <= 1 || c->top_k <= 0 || c->top_k >= c->experts) {
+    why = "expertsPerToken must be in 1..<expertCount (experts " + std::to_string(c->experts) +
+          ", top_k " + std::to_string(c->top_k) + ")";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (c->scoring != MR_SCORING_SIGMOID && c->scoring != MR_SCORING_SOFTMAX &&
+      c->scoring != MR_SCORING_SQRT_SOFTPLUS) {
+    why = "unknown scoring function";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (c->renorm != MR_RENORM_NONE && c->renorm != MR_RENORM_PLAIN && c->renorm != MR_RENORM_EPS) {
+    why = "unknown renormalisation mode";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (!(c->routed_scale > 0.0f) || !std::isfinite(c->routed_scale)) {
+    why = "routing scale must be finite and positive";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (c->experts > kMaxExperts || c->top_k > 32) {
+    why = "router limits of this build: experts <= 1024, top_k <= 32";
+    return MR_ERR_UNSUPPORTED;
+  }
+  return MR_OK;
+}
+
+static ExpertSource stack_source(const mr_affine_desc& d, int proj) {
+  ExpertSource s{};
+  s.packed = d.packed;
+  s.scales = d.scales;
+  s.biases = d.biases;
+  s.packed_stride = d.out_features * d.in_features * d.bits / 32;
+  s.sb_stride = d.out_features * (d.in_features / d.group_size);
+  s.table = nullptr;
+  s.proj = proj;
+  return s;
+}
+
+static cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+static cudaEvent_t pool_event(mr_ctx* ctx) {
+  if (!ctx->event_pool.empty()) {
+    cudaEvent_t e = ctx->event_pool.back();
+    ctx->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+// Records CUDA events around one launch when profiling is on.
+struct ProfScope {
+  mr_ctx* ctx;
+  int cls;
+  cudaStream_t s;
+  cudaEvent_t a = nullptr, b = nullptr;
+  ProfScope(mr_ctx* c, int k, cudaStream_t st) : ctx(c), cls(k), s(st) {
+    if (!ctx->profiling) return;
+    a = pool_event(ctx);
+    b = pool_event(ctx);
+    if (a && b) cudaEventRecord(a, s);
+  }
+  ~ProfScope() {
+    if (a && b) {
+      cudaEventRecord(b, s);
+      ctx->pending.push_back({cls, a, b});
+    }
+  }
+};
+
+static mr_status ensure_io(mr_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->io_bytes) return MR_OK;
+  if (ctx->io) {
+    cudaError_t e = cudaFree(ctx->io);
+    ctx->io = nullptr;
+    ctx->io_bytes = 0;
+    if (e != cudaSuccess) return cuda_check(ctx, e, "cudaFree(io)");
+  }
+  cudaError_t e = cudaMalloc(&ctx->io, bytes);
+  if (e != cudaSuccess) {
+    ctx->io = nullptr;
+    return cuda_check(ctx, e, "cudaMalloc(io)");
+  }
+  ctx->io_bytes = bytes;
+  return MR_OK;
+}
+
+}  // namespace mr
+
+using namespace mr;
+
+extern "C" {
+
+int mr_abi_version(void) { return MR_ABI_VERSION; }
+
+const char* mr_status_string(mr_status st) {
+  switch (st) {
+    case MR_OK: return "ok";
+    case MR_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case MR_ERR_UNSUPPORTED: return "unsupported";
+    case MR_ERR_CUDA: return "CUDA error";
+    case MR_ERR_OUT_OF_MEMORY: return "out of memory";
+    case MR_ERR_DEVICE: return "device error word set";
+    case MR_ERR_TIMEOUT: return "timeout";
+    case MR_ERR_BUDGET: return "budget refused";
+    case MR_ERR_NCCL: return "NCCL error";
+    case MR_ERR_STATE: return "call out of order";
+  }
+  return "unknown status";
+}
+
+mr_status mr_ctx_create(int device, mr_ctx** out) {
+  if (!out) return MR_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return MR_ERR_CUDA;
+  mr_ctx* ctx = new mr_ctx();
+  ctx->device = device;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0)
+    ctx->sm_count = sms;
+  ctx->fixed_bytes = sizeof(unsigned) * (kMaxCounters + 64);
+  e = cudaMalloc(&ctx->fixed, ctx->fixed_bytes);
+  if (e == cudaSuccess) e = cudaMemset(ctx->fixed, 0, ctx->fixed_bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    if (ctx->fixed) cudaFree(ctx->fixed);
+    delete ctx;
+    return e == cudaErrorMemoryAllocation ? MR_ERR_OUT_OF_MEMORY : MR_ERR_CUDA;
+  }
+  ctx->d_error = reinterpret_cast<unsigned*>(ctx->fixed);
+  ctx->d_counters = ctx->d_error + 32;
+  *out = ctx;
+  return MR_OK;
+}
+
+mr_status mr_ctx_destroy(mr_ctx* ctx) {
+  if (!ctx) return MR_OK;
+  cudaSetDevice(ctx->device);
+  cudaDeviceSynchronize();
+  if (ctx->ws) cudaFree(ctx->ws);
+  if (ctx->io) cudaFree(ctx->io);
+  if (ctx->fixed) cudaFree(ctx->fixed);
+  for (auto& p : ctx->pending) {
+    cudaEventDestroy(p.a);
+    cudaEventDestroy(p.b);
+  }
+  for (auto e : ctx->event_pool) cudaEventDestroy(e);
+  delete ctx;
+  return MR_OK;
+}
+
+const char* mr_last_error(const mr_ctx* ctx) { return ctx ? ctx->last_error.c_str() : ""; }
+
+mr_status mr_ctx_check(mr_ctx* ctx, void* stream, uint32_t* bits_out) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = as_stream(stream);
+  mr_status st = cuda_check(ctx, cudaStreamSynchronize(s), "cudaStreamSynchronize");
+  if (st) return st;
+  unsigned bits = 0;
+  st = cuda_check(ctx, cudaMemcpy(&bits, ctx->d_error, sizeof bits, cudaMemcpyDeviceToHost),
+                  "read device error word");
+  if (st) return st;
+  if (bits_out) *bits_out = bits;
+  if (bits) {
+    cudaMemset(ctx->d_error, 0, sizeof(unsigned));
+    std::string m = "device error word 0x";
+    char buf[16];
+    snprintf(buf, sizeof buf, "%x", bits);
+    m += buf;
+    if (bits & MR_DEVERR_BAD_EXPERT_ID) m += " (expert id out of range)";
+    if (bits & MR_DEVERR_NONFINITE_SCORE) m += " (non-finite router score)";
+    if (bits & MR_DEVERR_RENORM_ZERO) m += " (selected router scores cannot be normalized)";
+    return fail(ctx, MR_ERR_DEVICE, m);
+  }
+  return MR_OK;
+}
+
+mr_status mr_affine_validate(const mr_affine_desc* w, char* msg, size_t msg_len) {
+  std::string why;
+  mr_status st = validate_affine(w, why);
+  set_msg(msg, msg_len, why);
+  return st;
+}
+
+mr_status mr_router_config_validate(const mr_router_config* cfg, char* msg, size_t msg_len) {
+  std::string why;
+  mr_status st = validate_router(cfg, why);
+  set_msg(msg, msg_len, why);
+  return st;
+}
+
+static mr_status validate_layer(const mr_moe_layer* L, std::string& why) {
+  if (!L) {
+    why = "layer is NULL";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  mr_status st = validate_router(&L->router, why);
+  if (st) return st;
+  if (!L->router_w) {
+    why = "router weight is NULL";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (L->hidden <= 0 || L->inter <= 0 || L->shared_inter < 0) {
+    why = "hidden and intermediate sizes must be positive";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (!(L->swiglu_limit >= 0.0f) || !std::isfinite(L->swiglu_limit)) {
+    why = "SwiGLU limit must be finite and nonnegative";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  const mr_affine_desc* ds[3] = {&L->gate, &L->up, &L->down};
+  const int64_t outs[3] = {L->inter, L->inter, L->hidden};
+  const int64_t ins[3] = {L->hidden, L->hidden, L->inter};
+  const char* names[3] = {"gate", "up", "down"};
+  for (int i = 0; i < 3; ++i) {
+    mr_affine_desc d = *ds[i];
+    if (L->expert_table) {  // pointers come from the table
+      static const uint32_t dummy[4] = {0, 0, 0, 0};
+      d.packed = dummy;
+      d.scales = dummy;
+      d.biases = dummy;
+    }
+    st = validate_affine(&d, why);
+    if (st) {
+      why = std::string(names[i]) + ": " + why;
+      return st;
+    }
+    if (d.experts != L->router.experts || d.out_features != outs[i] || d.in_features != ins[i]) {
+      why = std::string(names[i]) + " stack must be [" + std::to_string(L->router.experts) + ", " +
+            std::to_string(outs[i]) + ", " + std::to_string(ins[i]) + "]";
+      return MR_ERR_INVALID_ARGUMENT;
+    }
+    if (d.bits != L->gate.bits || d.scale_dtype != L->gate.scale_dtype) {
+      why = "gate, up and down must share bits and scale dtype";
+      return MR_ERR_UNSUPPORTED;
+    }
+  }
+  if (L->shared_inter > 0) {
+    const mr_affine_desc* ss[3] = {&L->shared_gate, &L->shared_up, &L->shared_down};
+    const int64_t so[3] = {L->shared_inter, L->shared_inter, L->hidden};
+    const int64_t si[3] = {L->hidden, L->hidden, L->shared_inter};
+    for (int i = 0; i < 3; ++i) {
+      st = validate_affine(ss[i], why);
+      if (st) {
+        why = std::string("shared ") + names[i] + ": " + why;
+        return st;
+      }
+      if (ss[i]->experts != 0 || ss[i]->out_features != so[i] || ss[i]->in_features != si[i]) {
+        why = std::string("shared ") + names[i] + " must be a single [" + std::to_string(so[i]) +
+              ", " + std::to_string(si[i]) + "] matrix";
+        return MR_ERR_INVALID_ARGUMENT;
+      }
+      if (ss[i]->bits != L->gate.bits || ss[i]->scale_dtype != L->gate.scale_dtype) {
+        why = "shared expert must share bits and scale dtype with the routed experts";
+        return MR_ERR_UNSUPPORTED;
+      }
+    }
+    if (L->shared_inter != L->inter) {
+      why = "shared intermediate size must equal the routed one in this build";
+      return MR_ERR_UNSUPPORTED;
+    }
+  }
+  if ((L->hidden + kRowsPlain - 1) / kRowsPlain > kMaxCounters - 8) {
+    why = "hidden size exceeds the combine counter table";
+    return MR_ERR_UNSUPPORTED;
+  }
+  if (L->weight_placement != MR_WEIGHT_BEFORE_DOWN && L->weight_placement != MR_WEIGHT_AFTER_DOWN) {
+    why = "unknown weight placement";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  return MR_OK;
+}
+
+mr_status mr_moe_layer_validate(const mr_moe_layer* layer, char* msg, size_t msg_len) {
+  std::string why;
+  mr_status st = validate_layer(layer, why);
+  set_msg(msg, msg_len, why);
+  return st;
+}
+
+// ------------------------------------------------------------------ affine
+
+static mr_status affine_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const int32_t* ids,
+                               int32_t k, const mr_affine_desc* w, uint16_t* out, void* stream,
+                               bool dense) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  std::string why;
+  mr_status st = validate_affine(w, why);
+  if (st) return fail(ctx, st, why);
+  if (dense && w->experts != 0)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "affineMM needs a single matrix; use affineGatherMM for an expert stack");
+  if (!dense && w->experts == 0)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "affineGatherMM needs a stacked AffineWeights; use affineMM for a single matrix");
+  if (T <= 0 || !x || !out || (!dense && (!ids || k <= 0)))
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "x must be [tokens, inFeatures] with tokens > 0 and ids [tokens, k] with k > 0");
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0)
+    return fail(ctx, MR_ERR_UNSUPPORTED, "x must be 16-byte aligned");
+  const int kk = dense ? 1 : k;
+  const int64_t Tk = T * kk;
+  if (Tk > (int64_t)1 << 30) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
+  const int E = dense ? 1 : w->experts;
+  if (!dense && E > kMaxExperts)
+    return fail(ctx, MR_ERR_UNSUPPORTED, "expert stacks larger than 1024 are not built here");
+  const int64_t in = w->in_features;
+  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / kMaxCols + 1;
+
+  Bump b{nullptr};
+  for (int pass = 0; pass < 2; ++pass) {
+    b.off = 0;
+    b.take<uint16_t>(T * in);
+    b.take<float>(T * (in / kGroup));
+    b.take<int>(4);
+    b.take<int4>(max_seg);
+    b.take<int>(Tk);
+    if (pass == 0) {
+      st = ensure_workspace(ctx, b.off);
+      if (st) return st;
+      b.base = reinterpret_cast<char*>(ctx->ws);
+    }
+  }
+  b.off = 0;
+  uint16_t* xperm = b.take<uint16_t>(T * in);
+  float* xsum = b.take<float>(T * (in / kGroup));
+  int* nseg = b.take<int>(4);
+  int4* segs = b.take<int4>(max_seg);
+  int* cols = b.take<int>(Tk);
+  cudaStream_t s = as_stream(stream);
+
+  PrepParams pp{x, T, in, w->bits, xperm, xsum};
+  const int64_t chunks = T * (in / 16);
+  const int pgrid = (int)std::min<int64_t>((chunks + 255) / 256, 4 * ctx->sm_count);
+  prep_kernel<<<pgrid, 256, 0, s>>>(pp);
+  if ((st = cuda_check(ctx, cudaGetLastError(), "prep_kernel"))) return st;
+  if (dense) {
+    dense_plan_kernel<<<(int)std::min<int64_t>((T + 255) / 256, 1024), 256, 0, s>>>((int)T, nseg,
+                                                                                   segs, cols);
+  } else {
+    PlanParams plan{ids, (int)Tk, E, nseg, segs, cols, ctx->d_error};
+    plan_kernel<<<1, 256, 0, s>>>(plan);
+  }
+  if ((st = cuda_check(ctx, cudaGetLastError(), "plan kernel"))) return st;
+
+  GemvParams g{};
+  g.src_a = stack_source(*w, 0);
+  g.src_b = g.src_a;
+  g.sh_a = g.src_a;
+  g.sh_b = g.src_a;
+  g.rows = w->out_features;
+  g.in = in;
+  g.n_routed_segments = nseg;
+  g.segments = segs;
+  g.cols = cols;
+  g.shared_segments = 0;
+  g.shared_cols = 0;
+  g.rb_count = (int)((w->out_features + kRowsPlain - 1) / kRowsPlain);
+  g.Tk = (int)Tk;
+  g.in_div = kk;
+  g.shared_in_off = 0;
+  g.xperm = xperm;
+  g.xsum = xsum;
+  g.out_bf16 = out;
+  const int64_t grid = max_seg * g.rb_count;
+  const int nt = pick_nt((int)std::min<int64_t>(kMaxCols, Tk));
+  return cuda_check(ctx, launch_gemv(g, w->bits, w->scale_dtype, EPI_STORE, nt, (int)grid, s),
+                    "gemv(store)");
+}
+
+mr_status mr_affine_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens, const mr_affine_desc* w,
+                       uint16_t* out, void* stream) {
+  return affine_common(ctx, x, tokens, nullptr, 1, w, out, stream, true);
+}
+
+mr_status mr_affine_gather_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens, const int32_t* ids,
+                              int32_t top_k, const mr_affine_desc* w, uint16_t* out, void* stream) {
+  return affine_common(ctx, x, tokens, ids, top_k, w, out, stream, false);
+}
+
+}  // extern "C"
+
+namespace mr {
+template <int SD>
+__global__ void dequant_kernel(mr_affine_desc w, int64_t n, float* out) {
+  const int64_t wpr = w.in_features * w.bits / 32;
+  const int64_t groups = w.in_features / w.group_size;
+  const int per = 32 / w.bits;
+  const uint32_t mask = (1u << w.bits) - 1u;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / w.in_features;  // includes the expert index
+    const int64_t col = i - row * w.in_features;
+    const uint32_t word = __ldg(w.packed + row * wpr + col / per);
+    const float q = (float)((word >> ((col % per) * w.bits)) & mask);
+    const float sc = scale_to_f32<SD>(load_scale_raw<SD>(w.scales, row * groups + col / w.group_size));
+    const float bi = scale_to_f32<SD>(load_scale_raw<SD>(w.biases, row * groups + col / w.group_size));
+    out[i] = fmaf(sc, q, bi);
+  }
+}
+}  // namespace mr
+
+extern "C" {
+
+mr_status mr_affine_dequantize(mr_ctx* ctx, const mr_affine_desc* w, float* out, void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  std::string why;
+  mr_status st = validate_affine(w, why);
+  if (st == MR_ERR_UNSUPPORTED && w && w->group_size > 0 && w->bits > 0 && 32 % w->bits == 0 &&
+      w->bits <= 8)
+    st = MR_OK;  // dequantize handles any group size / bit width
+  if (st) return fail(ctx, st, why);
+  if (!out) return fail(ctx, MR_ERR_INVALID_ARGUMENT, "output is NULL");
+  const int64_t n = std::max<int32_t>(w->experts, 1) * w->out_features * w->in_features;
+  const int grid = (int)std::min<int64_t>((n + 255) / 256, 16 * ctx->sm_count);
+  cudaStream_t s = as_stream(stream);
+  switch (w->scale_dtype) {
+    case MR_DTYPE_BF16: dequant_kernel<MR_DTYPE_BF16><<<grid, 256, 0, s>>>(*w, n, out); break;
+    case MR_DTYPE_F16: dequant_kernel<MR_DTYPE_F16><<<grid, 256, 0, s>>>(*w, n, out); break;
+    default: dequant_kernel<MR_DTYPE_F32><<<grid, 256, 0, s>>>(*w, n, out); break;
+  }
+  return cuda_check(ctx, cudaGetLastError(), "dequant_kernel");
+}
+
+// ------------------------------------------------------------------ router
+
+struct LogitsShape {
+  int mtiles, tblocks, ks, kchunk, blocks;
+};
+
+static LogitsShape logits_shape(const mr_ctx* ctx, int64_t T, int E, int64_t H) {
+  LogitsShape s{};
+  s.mtiles = (E + 15) / 16;
+  s.tblocks = (int)((T + 63) / 64);
+  const int64_t base = (int64_t)s.mtiles * s.tblocks;
+  const int64_t target = 8LL * ctx->sm_count;  // warps
+  int64_t ks = std::max<int64_t>(1, target / std::max<int64_t>(base, 1));
+  ks = std::min<int64_t>(ks, std::max<int64_t>(1, H / 256));
+  int64_t chunk = (H + ks - 1) / ks;
+  chunk = (chunk + 31) / 32 * 32;
+  s.kchunk = (int)chunk;
+  s.ks = (int)((H + chunk - 1) / chunk);
+  s.blocks = (int)((base * s.ks + 3) / 4);
+  return s;
+}
+
+static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
+                             const mr_router_config* c, int32_t* ids, float* weights,
+                             float* margins, float* logits_out, bool plan, int* nseg, int4* segs,
+                             int* cols, cudaStream_t s) {
+  TopkParams tp{};
+  tp.part = part;
+  tp.ks = ks;
+  tp.T = (int)T;
+  tp.E = c->experts;
+  tp.k = c->top_k;
+  tp.scoring = c->scoring;
+  tp.bias = c->correction_bias;
+  tp.renorm = c->renorm;
+  tp.eps = c->renorm_eps;
+  tp.scale = c->routed_scale;
+  tp.ids = ids;
+  tp.weights = weights;
+  tp.margins = margins;
+  tp.logits_out = logits_out;
+  tp.error = ctx->d_error;
+  tp.build_plan = plan ? 1 : 0;
+  tp.plan = PlanParams{ids, (int)(T * c->top_k), c->experts, nseg, segs, cols, ctx->d_error};
+  tp.counter = ctx->d_counters + (kMaxCounters - 1);
+  topk_kernel<<<(int)((T + 7) / 8), 256, 0, s>>>(tp);
+  return cuda_check(ctx, cudaGetLastError(), "topk_kernel");
+}
+
+mr_status mr_router_select(mr_ctx* ctx, const uint16_t* x, int64_t T, int64_t H,
+                           const uint16_t* router_w, const mr_router_config* cfg, int32_t* ids,
+                           float* weights, float* margins, float* logits_out, void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  std::string why;
+  mr_status st = validate_router(cfg, why);
+  if (st) return fail(ctx, st, why);
+  if (T <= 0 || H <= 0 || !x || !router_w || !ids || !weights)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "router logits must contain at least one token");
+  if (H % 32 != 0) return fail(ctx, MR_ERR_UNSUPPORTED, "hidden size must be a multiple of 32");
+  const LogitsShape ls = logits_shape(ctx, T, cfg->experts, H);
+  Bump b{nullptr};
+  b.take<float>((size_t)ls.ks * T * cfg->experts);
+  if ((st = ensure_workspace(ctx, b.off))) return st;
+  b.base = reinterpret_cast<char*>(ctx->ws);
+  b.off = 0;
+  float* part = b.take<float>((size_t)ls.ks * T * cfg->experts);
+  cudaStream_t s = as_stream(stream);
+  LogitsParams lp{};
+  lp.x = x;
+  lp.w = router_w;
+  lp.T = (int)T;
+  lp.E = cfg->experts;
+  lp.H = H;
+  lp.mtiles = ls.mtiles;
+  lp.tblocks = ls.tblocks;
+  lp.ks = ls.ks;
+  lp.kchunk = ls.kchunk;
+  lp.part = part;
+  lp.logit_blocks = ls.blocks;
+  lp.do_prep = 0;
+  logits_kernel<<<ls.blocks, 128, 0, s>>>(lp);
+  if ((st = cuda_check(ctx, cudaGetLastError(), "logits_kernel"))) return st;
+  return topk_launch(ctx, part, ls.ks, T, cfg, ids, weights, margins, logits_out, false, nullptr,
+                     nullptr, nullptr, s);
+}
+
+mr_status mr_router_select_logits(mr_ctx* ctx, const float* logits, int64_t T,
+                                  const mr_router_config* cfg, int32_t* ids, float* weights,
+                                  float* margins, void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  std::string why;
+  mr_status st = validate_router(cfg, why);
+  if (st) return fail(ctx, st, why);
+  if (T <= 0 || !logits || !ids || !weights)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "router logits must contain at least one token");
+  return topk_launch(ctx, logits, 1, T, cfg, ids, weights, margins, nullptr, false, nullptr,
+                     nullptr, nullptr, as_stream(stream));
+}
+
+// ------------------------------------------------------------------ layer
+
+mr_status mr_ctx_reserve(mr_ctx* ctx, int64_t max_tokens, int32_t top_k, int32_t experts,
+                         int64_t hidden, int64_t inter) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  if (max_tokens <= 0 || top_k <= 0 || experts <= 0 || hidden <= 0 || inter <= 0)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "reserve sizes must be positive");
+  const int64_t T = max_tokens, Tk = T * top_k, R = Tk + 2 * T;
+  const int64_t max_seg = std::min<int64_t>(experts, Tk) + Tk / kMaxCols + 1;
+  size_t bytes = 0;
+  bytes += (size_t)64 * T * experts * 4 + 256;  // logits partials (ks <= 64)
+  bytes += (size_t)T * hidden * 2 + 256 + (size_t)T * (hidden / kGroup) * 4 + 256;
+  bytes += (size_t)Tk * 8 + (size_t)T * 4 + 1024;
+  bytes += (size_t)max_seg * 16 + (size_t)Tk * 4 + 1024;
+  bytes += (size_t)R * inter * 2 + (size_t)R * (inter / kGroup) * 4 + (size_t)R * hidden * 4 + 1024;
+  return ensure_workspace(ctx, bytes);
+}
+
+mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x,
+                               int64_t T, uint16_t* out, int32_t* ids_out, float* weights_out,
+                               float* margins_out, void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  std::string why;
+  mr_status st = validate_layer(L, why);
+  if (st) return fail(ctx, st, why);
+  if (T <= 0 || !x || !out)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "input must be a non-empty [tokens, hidden] matrix");
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0)
+    return fail(ctx, MR_ERR_UNSUPPORTED, "x must be 16-byte aligned");
+  const int E = L->router.experts, k = L->router.top_k;
+  const int64_t H = L->hidden, I = L->inter, Tk = T * k;
+  const bool has_shared = L->shared_inter > 0;
+  const int64_t R = Tk + (has_shared ? 2 * T : 0);  // h / partial rows
+  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / kMaxCols + 1;
+  const LogitsShape ls = logits_shape(ctx, T, E, H);
+  if (Tk > (int64_t)1 << 28) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
+
+  uint16_t* xperm = nullptr;
+  float *xsum = nullptr, *part = nullptr, *wts = nullptr, *hsum = nullptr, *part2 = nullptr;
+  int32_t* ids = nullptr;
+  int *nseg = nullptr, *cols = nullptr;
+  int4* segs = nullptr;
+  uint16_t* h = nullptr;
+  Bump b{nullptr};
+  for (int pass = 0; pass < 2; ++pass) {
+    b.off = 0;
+    part = b.take<float>((size_t)ls.ks * T * E);
+    xperm = b.take<uint16_t>(T * H);
+    xsum = b.take<float>(T * (H / kGroup));
+    ids = b.take<int32_t>(Tk);
+    wts = b.take<float>(Tk);
+    nseg = b.take<int>(4);
+    segs = b.take<int4>(max_seg);
+    cols = b.take<int>(Tk);
+    h = b.take<uint16_t>(R * I);
+    hsum = b.take<float>(R * (I / kGroup));
+    part2 = b.take<float>(R * H);
+    if (pass == 0) {
+      if ((st = ensure_workspace(ctx, b.off))) return st;
+      b.base = reinterpret_cast<char*>(ctx->ws);
+    }
+  }
+  if (ids_out) ids = ids_out;
+  if (weights_out) wts = weights_out;
+  cudaStream_t s = as_stream(stream);
+
+  // K0a: router logits (+ permuted input for the gate/up GEMV)
+  LogitsParams lp{};
+  lp.x = x;
+  lp.w = L->router_w;
+  lp.T = (int)T;
+  lp.E = E;
+  lp.H = H;
+  lp.mtiles = ls.mtiles;
+  lp.tblocks = ls.tblocks;
+  lp.ks = ls.ks;
+  lp.kchunk = ls.kchunk;
+  lp.part = part;
+  lp.logit_blocks = ls.blocks;
+  lp.prep = PrepParams{x, T, H, L->gate.bits, xperm, xsum};
+  lp.do_prep = 1;
+  const int64_t chunks = T * (H / 16);
+  const int prep_blocks = (int)std::min<int64_t>((chunks + 127) / 128, 2 * ctx->sm_count);
+  {
+    ProfScope ps(ctx, MR_KERNEL_ROUTER_LOGITS, s);
+    logits_kernel<<<ls.blocks + prep_blocks, 128, 0, s>>>(lp);
+  }
+  if ((st = cuda_check(ctx, cudaGetLastError(), "logits_kernel"))) return st;
+
+  // K0b: scores, top-k, weights; the last CTA builds the routing plan
+  {
+    ProfScope ps(ctx, MR_KERNEL_TOPK_PLAN, s);
+    st = topk_launch(ctx, part, ls.ks, T, &L->router, ids, wts, margins_out, nullptr, true, nseg,
+                     segs, cols, s);
+  }
+  if (st) return st;
+
+  // K1: gate/up dequant-GEMV + SwiGLU (+ routing weight) -> h, hsum
+  GemvParams g{};
+  if (L->expert_table) {
+    g.src_a = ExpertSource{nullptr, nullptr, nullptr, 0, 0, L->expert_table, 0};
+    g.src_b = ExpertSource{nullptr, nullptr, nullptr, 0, 0, L->expert_table, 1};
+  } else {
+    g.src_a = stack_source(L->gate, 0);
+    g.src_b = stack_source(L->up, 1);
+  }
+  if (has_shared) {
+    g.sh_a = stack_source(L->shared_gate, 0);
+    g.sh_b = stack_source(L->shared_up, 1);
+  } else {
+    g.sh_a = g.src_a;
+    g.sh_b = g.src_b;
+  }
+  g.rows = I;
+  g.in = H;
+  g.n_routed_segments = nseg;
+  g.segments = segs;
+  g.cols = cols;
+  g.shared_segments = has_shared ? (int)((T + kMaxCols - 1) / kMaxCols) : 0;
+  g.shared_cols = has_shared ? (int)T : 0;
+  g.rb_count = (int)(I / kRowsUp);
+  g.Tk = (int)Tk;
+  g.in_div = k;
+  g.shared_in_off = (int)Tk;
+  g.xperm = xperm;
+  g.xsum = xsum;
+  g.out_bf16 = h;
+  g.hsum = hsum;
+  g.weights = wts;
+  g.weight_after_down = L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0;
+  g.swiglu_limit = L->swiglu_limit;
+  g.h_bits = L->down.bits;
+  g.shared_lo_off = (int)T;
+  const int bits = L->gate.bits, sd = L->gate.scale_dtype;
+  int64_t grid = (max_seg + g.shared_segments) * g.rb_count;
+  int nt = pick_nt((int)std::min<int64_t>(kMaxCols, T));
+  {
+    ProfScope ps(ctx, MR_KERNEL_GATE_UP, s);
+    st = cuda_check(ctx, launch_gemv(g, bits, sd, EPI_SWIGLU, nt, (int)grid, s), "gemv(swiglu)");
+  }
+  if (st) return st;
+
+  // K2: down dequant-GEMV -> per-slot partials; the last CTA of each row
+  // block sums slots in order (+ shared) into out
+  GemvParams d{};
+  if (L->expert_table) {
+    d.src_a = ExpertSource{nullptr, nullptr, nullptr, 0, 0, L->expert_table, 2};
+  } else {
+    d.src_a = stack_source(L->down, 2);
+  }
+  d.src_b = d.src_a;
+  d.sh_a = has_shared ? stack_source(L->shared_down, 2) : d.src_a;
+  d.sh_b = d.sh_a;
+  d.rows = H;
+  d.in = I;
+  d.n_routed_segments = nseg;
+  d.segments = segs;
+  d.cols = cols;
+  d.shared_segments = has_shared ? (int)((2 * T + kMaxCols - 1) / kMaxCols) : 0;
+  d.shared_cols = has_shared ? (int)(2 * T) : 0;
+  d.rb_count = (int)((H + kRowsPlain - 1) / kRowsPlain);
+  d.Tk = (int)Tk;
+  d.in_div = 1;
+  d.shared_in_off = 0;
+  d.xperm = h;
+  d.xsum = hsum;
+  d.part = part2;
+  d.weights = wts;
+  d.weight_after_down = g.weight_after_down;
+  d.counters = ctx->d_counters;
+  d.T = (int)T;
+  d.k = k;
+  d.has_shared = has_shared ? 1 : 0;
+  d.out = out;
+  grid = (max_seg + d.shared_segments) * d.rb_count;
+  nt = pick_nt((int)std::min<int64_t>(kMaxCols, has_shared ? 2 * T : T));
+  ProfScope ps(ctx, MR_KERNEL_DOWN_COMBINE, s);
+  return cuda_check(ctx, launch_gemv(d, bits, sd, EPI_PARTIAL, nt, (int)grid, s), "gemv(down)");
+}
+
+mr_status mr_moe_layer_forward_host(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x_host,
+                                    int64_t T, uint16_t* out_host, int32_t* ids_host,
+                                    void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  std::string why;
+  mr_status st = validate_layer(L, why);
+  if (st) return fail(ctx, st, why);
+  if (T <= 0 || !x_host || !out_host)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "input must be a non-empty [tokens, hidden] matrix");
+  const int64_t xbytes = T * L->hidden * 2;
+  const int64_t ibytes = T * L->router.top_k * 4;
+  const size_t need = (size_t)(2 * ((xbytes + 255) / 256 * 256) + ibytes + 256);
+  if ((st = ensure_io(ctx, need))) return st;
+  char* base = reinterpret_cast<char*>(ctx->io);
+  uint16_t* dx = reinterpret_cast<uint16_t*>(base);
+  uint16_t* dout = reinterpret_cast<uint16_t*>(base + (xbytes + 255) / 256 * 256);
+  int32_t* dids = reinterpret_cast<int32_t*>(base + 2 * ((xbytes + 255) / 256 * 256));
+  cudaStream_t s = as_stream(stream);
+  if ((st = cuda_check(ctx, cudaMemcpyAsync(dx, x_host, xbytes, cudaMemcpyHostToDevice, s),
+                       "copy x to device")))
+    return st;
+  if ((st = mr_moe_layer_forward(ctx, L, dx, T, dout, ids_host ? dids : nullptr, nullptr, nullptr,
+                                 stream)))
+    return st;
+  if ((st = cuda_check(ctx, cudaMemcpyAsync(out_host, dout, xbytes, cudaMemcpyDeviceToHost, s),
+                       "copy out to host")))
+    return st;
+  if (ids_host)
+    st = cuda_check(ctx, cudaMemcpyAsync(ids_host, dids, ibytes, cudaMemcpyDeviceToHost, s),
+                    "copy ids to host");
+  return st;
+}
+
+mr_status mr_ctx_profile(mr_ctx* ctx, int enable) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  ctx->profiling = enable != 0;
+  return MR_OK;
+}
+
+mr_status mr_ctx_profile_read(mr_ctx* ctx, double* ms, int64_t* launches, int n) {
+  if (!ctx || n < 0 || n > MR_KERNEL_CLASSES) return MR_ERR_INVALID_ARGUMENT;
+  mr_status st = MR_OK;
+  for (auto& p : ctx->pending) {
+    float dt = 0.0f;
+    cudaError_t e = cudaEventSynchronize(p.b);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&dt, p.a, p.b);
+    if (e != cudaSuccess && st == MR_OK) st = cuda_check(ctx, e, "profile event");
+    ctx->prof_ms[p.cls] += dt;
+    ctx->prof_n[p.cls] += 1;
+    ctx->event_pool.push_back(p.a);
+    ctx->event_pool.push_back(p.b);
+  }
+  ctx->pending.clear();
+  for (int i = 0; i < n; ++i) {
+    if (ms) ms[i] = ctx->prof_ms[i];
+    if (launches) launches[i] = ctx->prof_n[i];
+  }
+  for (int i = 0; i < MR_KERNEL_CLASSES; ++i) {
+    ctx->prof_ms[i] = 0;
+    ctx->prof_n[i] = 0;
+  }
+  return st;
+}
+
+// ------------------------------------------------------------------ synth
+
+__device__ __forceinline__ uint64_t sm_mix(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ uint64_t sm_value(uint64_t seed, uint64_t i) {
+  return sm_mix(seed + (i + 1) * 0x9E3779B97F4A7C15ULL);
+}
+
+__global__ void synth_words_kernel(uint64_t seed, int64_t n, uint32_t* out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t v = sm_value(seed, (uint64_t)(i >> 1));
+    out[i] = (uint32_t)(v >> (32 * (i & 1)));
+  }
+}
+
+__global__ void synth_normal_kernel(uint64_t seed, int64_t n, double stdv, int absval,
+                                    uint16_t* out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t a = sm_value(seed, (uint64_t)(2 * i));
+    const uint64_t b = sm_value(seed, (uint64_t)(2 * i + 1));
+    const double u1 = ((double)(a >> 11) + 1.0) * 0x1.0p-53;
+    const double u2 = (double)(b >> 11) * 0x1.0p-53;
+    double v = stdv * (sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2));
+    if (absval) v = fabs(v);
+    out[i] = __bfloat16_as_ushort(__float2bfloat16_rn((float)v));
+  }
+}
+
+__global__ void synth_biases_kernel(const uint16_t* scales, int64_t n, float m, uint16_t* out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float s = __uint_as_float((uint32_t)scales[i] << 16);
+    out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(m * s));
+  }
+}
+
+uint64_t mr_synth_label(uint32_t layer, uint32_t kind, uint32_t expert, uint32_t proj) {
+  return ((uint64_t)layer << 40) | ((uint64_t)(kind & 0xffu) << 32) |
+         ((uint64_t)(expert & 0xffffffu) << 8) | (uint64_t)(proj & 0xffu);
+}
+
+static uint64_t host_mix(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+uint64_t mr_synth_derive(uint64_t seed, uint64_t label) {
+  return host_mix(seed ^ host_mix(label + 0xD1B54A32D192ED03ULL));
+}
+
+static int synth_grid(const mr_ctx* ctx, int64_t n) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 32 * ctx->sm_count));
+}
+
+mr_status mr_synth_words(mr_ctx* ctx, uint64_t seed, int64_t n, uint32_t* out, void* stream) {
+  if (!ctx || n < 0 || (n > 0 && !out)) return MR_ERR_INVALID_ARGUMENT;
+  if (n == 0) return MR_OK;
+  synth_words_kernel<<<synth_grid(ctx, n), 256, 0, as_stream(stream)>>>(seed, n, out);
+  return cuda_check(ctx, cudaGetLastError(), "synth_words");
+}
+
+mr_status mr_synth_normal_bf16(mr_ctx* ctx, uint64_t seed, int64_t n, float std, int absval,
+                               uint16_t* out, void* stream) {
+  if (!ctx || n < 0 || (n > 0 && !out)) return MR_ERR_INVALID_ARGUMENT;
+  if (n == 0) return MR_OK;
+  synth_normal_kernel<<<synth_grid(ctx, n), 256, 0, as_stream(stream)>>>(seed, n, (double)std,
+                                                                           absval, out);
+  return cuda_check(ctx, cudaGetLastError(), "synth_normal");
+}
+
+mr_status mr_synth_affine_biases(mr_ctx* ctx, const uint16_t* scales, int64_t n, int32_t bits,
+                                 uint16_t* biases, void* stream) {
+  if (!ctx || n < 0 || bits <= 0 || bits > 16) return MR_ERR_INVALID_ARGUMENT;
+  if (n == 0) return MR_OK;
+  synth_biases_kernel<<<synth_grid(ctx, n), 256, 0, as_stream(stream)>>>(
+      scales, n, -(float)(1 << (bits - 1)), biases);
+  return cuda_check(ctx, cudaGetLastError(), "synth_biases");
+}
+
+}  // extern "C"

@@ -1,0 +1,166 @@
+// mr_common.cuh — shared device helpers and internal structures of the
+// sm_100a MoE-expert library (libminirun_moe).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "minirun_moe.h"
+
+#define MR_DEVICE __device__ __forceinline__
+
+namespace mr {
+
+constexpr int kGroup = 64;         // supported affine group size
+constexpr int kMaxCols = 64;       // columns (token rows) per GEMV segment
+constexpr int kMaxExperts = 1024;  // router / plan limit
+constexpr int kGemvThreads = 256;  // 8 warps per GEMV CTA
+constexpr int kRowsUp = 64;        // gate/up rows per CTA (one h group)
+constexpr int kRowsPlain = 128;    // rows per CTA for plain / down projections
+
+// ------------------------------------------------------------ bf16 / f16
+
+MR_DEVICE float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
+
+MR_DEVICE uint16_t f32_to_bf16_bits(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+MR_DEVICE float bf16_round(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); }
+
+// Scale/bias element size by dtype.
+template <int SD>
+struct ScaleT {
+  static constexpr int kBytes = (SD == MR_DTYPE_F32) ? 4 : 2;
+};
+
+template <int SD>
+MR_DEVICE uint32_t load_scale_raw(const void* p, int64_t i) {
+  if constexpr (SD == MR_DTYPE_F32) {
+    return __float_as_uint(__ldg(reinterpret_cast<const float*>(p) + i));
+  } else {
+    return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p) + i);
+  }
+}
+
+template <int SD>
+MR_DEVICE float scale_to_f32(uint32_t raw) {
+  if constexpr (SD == MR_DTYPE_BF16) {
+    return __uint_as_float(raw << 16);
+  } else if constexpr (SD == MR_DTYPE_F16) {
+    return __half2float(__ushort_as_half((unsigned short)raw));
+  } else {
+    return __uint_as_float(raw);
+  }
+}
+
+// ------------------------------------------------------------ memory ops
+
+// Streaming read-only loads of packed weights: no L1 allocation, the bytes
+// are used once per launch.
+MR_DEVICE uint32_t ldg_stream_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+MR_DEVICE uint2 ldg_stream_u64(const uint32_t* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.b32 {%0, %1}, [%2];"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p));
+  return v;
+}
+MR_DEVICE uint4 ldg_stream_u128(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+// Activations: read-only within a launch and reused by every warp -> L1.
+MR_DEVICE uint4 ldg_u128(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+// ------------------------------------------------------------ tensor core
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
+MR_DEVICE void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------------ structures
+
+// How a GEMV finds the weights of expert e: a stack (base + e*stride) or a
+// device table of mr_expert_ptrs (an expert cache).
+struct ExpertSource {
+  const uint32_t* packed;
+  const void* scales;
+  const void* biases;
+  int64_t packed_stride;  // words per expert
+  int64_t sb_stride;      // scale/bias elements per expert
+  const mr_expert_ptrs* table;
+  int proj;               // entry of the table (0 gate, 1 up, 2 down)
+};
+
+struct ProjPtr {
+  const uint32_t* packed;
+  const void* scales;
+  const void* biases;
+};
+
+template <int SD>
+MR_DEVICE ProjPtr resolve(const ExpertSource& s, int e) {
+  if (s.table) {
+    const mr_expert_ptrs& t = s.table[e];
+    return ProjPtr{t.packed[s.proj], t.scales[s.proj], t.biases[s.proj]};
+  }
+  const int64_t sb = (int64_t)e * s.sb_stride * ScaleT<SD>::kBytes;
+  return ProjPtr{s.packed + (int64_t)e * s.packed_stride,
+                 reinterpret_cast<const char*>(s.scales) + sb,
+                 reinterpret_cast<const char*>(s.biases) + sb};
+}
+
+}  // namespace mr
+
+// Host-side context (the opaque mr_ctx of the C ABI).
+struct mr_ctx {
+  int device = 0;
+  int sm_count = 148;
+  std::string last_error;
+  void* ws = nullptr;  // growable device workspace
+  size_t ws_bytes = 0;
+  // Fixed block (never reallocated): error word + combine counters.
+  void* fixed = nullptr;
+  size_t fixed_bytes = 0;
+  unsigned* d_error = nullptr;
+  unsigned* d_counters = nullptr;  // kMaxCounters
+  // device staging of the host-buffer entry point
+  void* io = nullptr;
+  size_t io_bytes = 0;
+  // CUDA-event profiling of layer launches (mr_ctx_profile)
+  struct Pending {
+    int cls;
+    cudaEvent_t a, b;
+  };
+  bool profiling = false;
+  std::vector<Pending> pending;
+  std::vector<cudaEvent_t> event_pool;
+  double prof_ms[MR_KERNEL_CLASSES] = {0, 0, 0, 0};
+  int64_t prof_n[MR_KERNEL_CLASSES] = {0, 0, 0, 0};
+};
+
+namespace mr {
+constexpr int kMaxCounters = 4096;
+mr_status fail(mr_ctx* ctx, mr_status st, const std::string& msg);
+mr_status cuda_check(mr_ctx* ctx, cudaError_t err, const char* what);
+mr_status ensure_workspace(mr_ctx* ctx, size_t bytes);
+}  // namespace mr

@@ -1,0 +1,437 @@
+// mr_router.cuh — router logits, scoring + top-k, the device routing plan,
+// and the activation prep (permuted bf16 copy + per-group sums) that the
+// dequant-GEMV reads.
+#pragma once
+
+#include "mr_common.cuh"
+#include "mr_gemv.cuh"
+
+namespace mr {
+
+// ---------------------------------------------------------------- prep
+// xperm[t][i'] = x[t][src(i')] (halves of each B-block interleaved, B by
+// bits), xsum[t][g] = sum of the group's 64 bf16 values (fp32).
+struct PrepParams {
+  const uint16_t* x;
+  int64_t rows;
+  int64_t in;
+  int bits;
+  uint16_t* xperm;
+  float* xsum;
+};
+
+// Called by whole warps (the group sum is a 4-lane shuffle); lanes past the
+// end pass valid == false and only take part in the shuffle.
+MR_DEVICE void prep_chunk(const PrepParams& p, int64_t chunk, bool valid) {
+  // one thread = 16 consecutive elements; 4 threads = one group of 64
+  const int64_t per_row = p.in / 16;
+  if (!valid) chunk = 0;
+  const int64_t r = chunk / per_row;
+  const int64_t c16 = chunk - r * per_row;
+  const uint16_t* src = p.x + r * p.in + c16 * 16;
+  uint4 v0 = ldg_u128(src);
+  uint4 v1 = ldg_u128(src + 8);
+  uint16_t e[16];
+  memcpy(e, &v0, 16);
+  memcpy(e + 8, &v1, 16);
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) s += bf16_bits_to_f32(e[i]);
+  uint16_t o[16];
+  const int B = perm_block(p.bits);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int base = i & ~(B - 1);
+    const int e2 = i - base;
+    const int h = B >> 1;
+    const int src_i = base + ((e2 & 1) ? (e2 >> 1) + h : (e2 >> 1));
+    o[i] = e[src_i];
+  }
+  uint4 w0, w1;
+  memcpy(&w0, o, 16);
+  memcpy(&w1, o + 8, 16);
+  uint16_t* dst = p.xperm + r * p.in + c16 * 16;
+  if (valid) {
+    *reinterpret_cast<uint4*>(dst) = w0;
+    *reinterpret_cast<uint4*>(dst + 8) = w1;
+  }
+  // reduce the 4 chunks of a group (consecutive lanes)
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  if (valid && (c16 & 3) == 0) p.xsum[r * (p.in / kGroup) + c16 / 4] = s;
+}
+
+// Grid-stride over chunks, in whole warps (n rounded up to a warp multiple).
+MR_DEVICE void prep_range(const PrepParams& p, int64_t first, int64_t stride) {
+  const int64_t n = p.rows * (p.in / 16);
+  const int64_t n_round = (n + 31) / 32 * 32;
+  for (int64_t i = first; i < n_round; i += stride) prep_chunk(p, i, i < n);
+}
+
+__global__ void prep_kernel(const PrepParams p) {
+  prep_range(p, (int64_t)blockIdx.x * blockDim.x + threadIdx.x, (int64_t)gridDim.x * blockDim.x);
+}
+
+// ---------------------------------------------------------------- logits
+// part[kc][t][e] = sum over the kc-th K chunk of x[t,:] . W_r[e,:] (fp32),
+// on the tensor core (bf16 products are exact in fp32). Chunks are summed in
+// fixed order by the top-k kernel, so logits are deterministic.
+struct LogitsParams {
+  const uint16_t* x;
+  const uint16_t* w;
+  int T;
+  int E;
+  int64_t H;
+  int mtiles;
+  int tblocks;
+  int ks;
+  int kchunk;  // multiple of 32
+  float* part;
+  // fused prep of the expert GEMV input (optional, blocks past the logits)
+  int logit_blocks;
+  PrepParams prep;
+  int do_prep;
+};
+
+__global__ void __launch_bounds__(128) logits_kernel(const LogitsParams p) {
+  if ((int)blockIdx.x >= p.logit_blocks) {
+    if (!p.do_prep) return;
+    const int64_t nb = gridDim.x - p.logit_blocks;
+    prep_range(p.prep, (int64_t)(blockIdx.x - p.logit_blocks) * blockDim.x + threadIdx.x,
+               nb * blockDim.x);
+    return;
+  }
+  const int lane = threadIdx.x & 31;
+  const int r8 = lane >> 2, c = lane & 3;
+  const int witem = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int n_items = p.mtiles * p.tblocks * p.ks;
+  if (witem >= n_items) return;
+  const int m = witem % p.mtiles;
+  const int rest = witem / p.mtiles;
+  const int tb = rest % p.tblocks;
+  const int kc = rest / p.tblocks;
+  const int ea = min(m * 16 + r8, p.E - 1);
+  const int eb = min(m * 16 + 8 + r8, p.E - 1);
+  const int64_t k0 = (int64_t)kc * p.kchunk;
+  const int64_t k1 = (k0 + p.kchunk < p.H) ? k0 + p.kchunk : p.H;
+  const int t0 = tb * 64;
+  const int ntiles = min(8, (p.T - t0 + 7) / 8);
+  const uint16_t* xr[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const int tok = min(t0 + t * 8 + r8, p.T - 1);
+    xr[t] = p.x + (int64_t)tok * p.H + 8 * c;
+  }
+  const uint16_t* wa = p.w + (int64_t)ea * p.H + 8 * c;
+  const uint16_t* wb = p.w + (int64_t)eb * p.H + 8 * c;
+  float acc[8][4];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+  for (int64_t k = k0; k < k1; k += 32) {
+    const uint4 A = ldg_u128(wa + k);
+    const uint4 Bv = ldg_u128(wb + k);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (t < ntiles) {
+        const uint4 X = ldg_u128(xr[t] + k);
+        mma_bf16_16816(acc[t], A.x, Bv.x, A.y, Bv.y, X.x, X.y);
+        mma_bf16_16816(acc[t], A.z, Bv.z, A.w, Bv.w, X.z, X.w);
+      }
+    }
+  }
+  float* out = p.part + (int64_t)kc * p.T * p.E;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    if (t < ntiles) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int tok = t0 + t * 8 + 2 * c + i;
+        if (tok < p.T) {
+          const int e_a = m * 16 + r8, e_b = m * 16 + 8 + r8;
+          if (e_a < p.E) out[(int64_t)tok * p.E + e_a] = acc[t][i];
+          if (e_b < p.E) out[(int64_t)tok * p.E + e_b] = acc[t][2 + i];
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- plan
+// Group (token, slot) pairs by expert: segments of <= kMaxCols columns, in
+// ascending expert order (the reference's gather visits experts ascending,
+// Loading/QwenExpertBackends.swift:77-112). Run by one whole CTA.
+struct PlanParams {
+  const int32_t* ids;  // [Tk]
+  int Tk;
+  int E;
+  int* n_segments;
+  int4* segments;
+  int* cols;
+  unsigned* error;
+};
+
+template <int NTHREADS>
+__device__ void build_plan_cta(const PlanParams& p) {
+  __shared__ int cnt[kMaxExperts];
+  __shared__ int colofs[kMaxExperts];
+  __shared__ int segofs[kMaxExperts];
+  __shared__ int warp_tot[NTHREADS / 32][2];
+  const int tid = threadIdx.x;
+  for (int e = tid; e < p.E; e += NTHREADS) cnt[e] = 0;
+  __syncthreads();
+  for (int i = tid; i < p.Tk; i += NTHREADS) {
+    const int e = __ldcg(p.ids + i);
+    if (e >= 0 && e < p.E) {
+      atomicAdd(&cnt[e], 1);
+    } else {
+      atomicOr(p.error, MR_DEVERR_BAD_EXPERT_ID);
+    }
+  }
+  __syncthreads();
+  // exclusive scans of column counts and segment counts; each thread owns
+  // a contiguous run of experts
+  constexpr int kPer = kMaxExperts / NTHREADS;
+  int lc = 0, ls = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = tid * kPer + i;
+    if (e < p.E) {
+      lc += cnt[e];
+      ls += (cnt[e] + kMaxCols - 1) / kMaxCols;
+    }
+  }
+  const int lane = tid & 31, wid = tid >> 5;
+  int ic = lc, is = ls;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int a = __shfl_up_sync(0xffffffffu, ic, off);
+    const int b = __shfl_up_sync(0xffffffffu, is, off);
+    if (lane >= off) {
+      ic += a;
+      is += b;
+    }
+  }
+  if (lane == 31) {
+    warp_tot[wid][0] = ic;
+    warp_tot[wid][1] = is;
+  }
+  __syncthreads();
+  int wc = 0, wsg = 0, tot_s = 0;
+  for (int w = 0; w < NTHREADS / 32; ++w) {
+    if (w < wid) {
+      wc += warp_tot[w][0];
+      wsg += warp_tot[w][1];
+    }
+    tot_s += warp_tot[w][1];
+  }
+  int oc = wc + ic - lc, os = wsg + is - ls;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = tid * kPer + i;
+    if (e < p.E) {
+      colofs[e] = oc;
+      segofs[e] = os;
+      const int n = cnt[e];
+      for (int s = 0; s * kMaxCols < n; ++s)
+        p.segments[os + s] = make_int4(e, oc + s * kMaxCols, min(kMaxCols, n - s * kMaxCols), 0);
+      oc += n;
+      os += (n + kMaxCols - 1) / kMaxCols;
+    }
+  }
+  if (tid == 0) *p.n_segments = tot_s;
+  __syncthreads();
+  for (int e = tid; e < p.E; e += NTHREADS) cnt[e] = 0;
+  __syncthreads();
+  for (int i = tid; i < p.Tk; i += NTHREADS) {
+    const int e = __ldcg(p.ids + i);
+    if (e >= 0 && e < p.E) {
+      const int pos = atomicAdd(&cnt[e], 1);
+      p.cols[colofs[e] + pos] = i;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) plan_kernel(const PlanParams p) { build_plan_cta<256>(p); }
+
+// Dense affineMM plan: one expert (0), columns = tokens.
+__global__ void dense_plan_kernel(int T, int* n_segments, int4* segments, int* cols) {
+  const int nseg = (T + kMaxCols - 1) / kMaxCols;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < T; i += gridDim.x * blockDim.x) {
+    cols[i] = i;
+    if (i % kMaxCols == 0) segments[i / kMaxCols] = make_int4(0, i, min(kMaxCols, T - i), 0);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *n_segments = nseg;
+}
+
+// ---------------------------------------------------------------- top-k
+struct TopkParams {
+  const float* part;  // [ks][T][E]
+  int ks;
+  int T;
+  int E;
+  int k;
+  int scoring;
+  const float* bias;
+  int renorm;
+  float eps;
+  float scale;
+  int32_t* ids;
+  float* weights;
+  float* margins;     // optional
+  float* logits_out;  // optional
+  unsigned* error;
+  // plan (built by the last CTA) — optional
+  int build_plan;
+  PlanParams plan;
+  unsigned* counter;
+};
+
+MR_DEVICE bool better(float va, int ia, float vb, int ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+// One warp per token. Descending choice score, ties to the lower index
+// (Operators/MoE.swift:128, Operators/DeepSeekV4Routing.swift:215-219).
+__global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t < p.T) {
+    constexpr int kPer = kMaxExperts / 32;
+    float sc[kPer], ch[kPer];
+    unsigned nonfinite = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = lane + 32 * i;
+      float l = 0.0f;
+      if (e < p.E) {
+        for (int s = 0; s < p.ks; ++s) l += p.part[((int64_t)s * p.T + t) * p.E + e];
+        if (p.logits_out) p.logits_out[(int64_t)t * p.E + e] = l;
+      }
+      sc[i] = l;
+    }
+    if (p.scoring == MR_SCORING_SOFTMAX) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i)
+        if (lane + 32 * i < p.E) m = fmaxf(m, sc[i]);
+#pragma unroll
+      for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      float s = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        if (lane + 32 * i < p.E) {
+          sc[i] = expf(sc[i] - m);
+          s += sc[i];
+        }
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) sc[i] = sc[i] / s;
+    } else if (p.scoring == MR_SCORING_SQRT_SOFTPLUS) {
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) sc[i] = sqrtf(fmaxf(sc[i], 0.0f) + log1pf(expf(-fabsf(sc[i]))));
+    } else {
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) sc[i] = 1.0f / (1.0f + expf(-sc[i]));
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = lane + 32 * i;
+      if (e < p.E) {
+        if (!isfinite(sc[i])) nonfinite = 1;
+        float v = p.bias ? sc[i] + __ldg(p.bias + e) : sc[i];
+        ch[i] = isnan(v) ? -INFINITY : v;
+      } else {
+        ch[i] = -INFINITY;
+      }
+    }
+    if (__any_sync(0xffffffffu, nonfinite) && lane == 0) atomicOr(p.error, MR_DEVERR_NONFINITE_SCORE);
+    unsigned taken = 0;
+    int my_id = 0;
+    float my_w = 0.0f, kth = 0.0f, rej = 0.0f;
+    for (int r = 0; r <= p.k; ++r) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff, bslot = -1;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int e = lane + 32 * i;
+        if (e < p.E && !((taken >> i) & 1u) && (bslot < 0 || better(ch[i], e, bv, bi))) {
+          bv = ch[i];
+          bi = e;
+          bslot = i;
+        }
+      }
+      float wv = bv;
+      int wi = bi;
+#pragma unroll
+      for (int off = 16; off; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, wv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, wi, off);
+        if (better(ov, oi, wv, wi)) {
+          wv = ov;
+          wi = oi;
+        }
+      }
+      if (r < p.k) {
+        // the owner marks the expert and publishes its unbiased score
+        float s_un = 0.0f;
+        if (wi != 0x7fffffff && (wi & 31) == lane) {
+          const int slot = wi >> 5;
+#pragma unroll
+          for (int i = 0; i < kPer; ++i)
+            if (i == slot) {
+              taken |= 1u << i;
+              s_un = sc[i];
+            }
+        }
+        s_un = __shfl_sync(0xffffffffu, s_un, wi & 31);
+        if (lane == r) {
+          my_id = wi;
+          my_w = s_un;
+        }
+        if (r == p.k - 1) kth = wv;
+      } else {
+        rej = wv;
+      }
+    }
+    // renormalisation, slot-ordered sum (MoE.swift:142-145,
+    // DeepSeekV4Routing.swift:259-271, QwenMoEModel.swift:122-127)
+    float den = 0.0f;
+    for (int j = 0; j < p.k; ++j) den += __shfl_sync(0xffffffffu, my_w, j);
+    float w = my_w;
+    if (p.renorm == MR_RENORM_PLAIN) {
+      if (!(isfinite(den) && den > 0.0f)) {
+        if (lane == 0) atomicOr(p.error, MR_DEVERR_RENORM_ZERO);
+      }
+      w = w / den;
+    } else if (p.renorm == MR_RENORM_EPS && p.k > 1) {
+      w = w / (den + p.eps);
+    }
+    w = w * p.scale;
+    if (lane < p.k) {
+      p.ids[(int64_t)t * p.k + lane] = my_id;
+      p.weights[(int64_t)t * p.k + lane] = w;
+    }
+    if (p.margins && lane == 0) {
+      const double a = (double)kth, b = (double)rej;
+      const double s = fmax(fabs(a), fabs(b));
+      p.margins[t] = (float)(s > 0 ? (a - b) / s : 0.0);
+    }
+  }
+  if (!p.build_plan) return;
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned old = atomicAdd(p.counter, 1u);
+    s_last = (old == gridDim.x - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  build_plan_cta<256>(p.plan);
+  if (threadIdx.x == 0) *p.counter = 0u;
+}
+
+}  // namespace mr

@@ -1,0 +1,19 @@
+"""minirun_moe — B200 (sm_100a) MoE-expert hot path of Minirun, over a C ABI.
+
+The package is the host-side mirror of the reference's MLXBridge affine op
+API and its MoE block (nanguoyu/minirun-app); all arithmetic runs in
+libminirun_moe.so (``minirun-app_b200/csrc``), which must be built — there is
+no CPU fallback.
+"""
+from ._lib import LIB_PATH, LibraryMissing, load as load_library
+from .bridge import (AffineBridgeError, AffineWeights, Context, MoeError, Selection,
+                     affine_dequantize, affine_gather_mm, affine_mm, validate_desc)
+from .moe import (MoELayer, ResidentExpertBackend, RouterConfig, router_select,
+                  router_select_logits)
+
+__all__ = [
+    "LIB_PATH", "LibraryMissing", "load_library", "AffineBridgeError", "AffineWeights",
+    "Context", "MoeError", "Selection", "affine_dequantize", "affine_gather_mm", "affine_mm",
+    "validate_desc", "MoELayer", "ResidentExpertBackend", "RouterConfig", "router_select",
+    "router_select_logits",
+]

@@ -1,0 +1,116 @@
+"""ctypes binding of libminirun_moe.so (include/minirun_moe.h).
+
+This module is the reference-side binding a host would add: every struct and
+function below mirrors the C header one to one. Loading fails loudly when the
+library has not been built — there is no CPU fallback anywhere in the package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libminirun_moe.so")
+
+MR_OK = 0
+MR_ERR_INVALID_ARGUMENT = 1
+MR_ERR_UNSUPPORTED = 2
+MR_ERR_CUDA = 3
+MR_ERR_OUT_OF_MEMORY = 4
+MR_ERR_DEVICE = 5
+MR_ERR_TIMEOUT = 6
+MR_ERR_BUDGET = 7
+MR_ERR_NCCL = 8
+MR_ERR_STATE = 9
+
+MR_DTYPE_BF16, MR_DTYPE_F16, MR_DTYPE_F32 = 0, 1, 2
+MR_SCORING_SIGMOID, MR_SCORING_SOFTMAX, MR_SCORING_SQRT_SOFTPLUS = 0, 1, 2
+MR_RENORM_NONE, MR_RENORM_PLAIN, MR_RENORM_EPS = 0, 1, 2
+MR_WEIGHT_BEFORE_DOWN, MR_WEIGHT_AFTER_DOWN = 0, 1
+MR_DEVERR_BAD_EXPERT_ID, MR_DEVERR_NONFINITE_SCORE, MR_DEVERR_RENORM_ZERO = 1, 2, 4
+
+vp = C.c_void_p
+
+
+class mr_affine_desc(C.Structure):
+    _fields_ = [("packed", vp), ("scales", vp), ("biases", vp), ("experts", C.c_int32),
+                ("out_features", C.c_int64), ("in_features", C.c_int64),
+                ("group_size", C.c_int32), ("bits", C.c_int32), ("scale_dtype", C.c_int)]
+
+
+class mr_router_config(C.Structure):
+    _fields_ = [("experts", C.c_int32), ("top_k", C.c_int32), ("scoring", C.c_int),
+                ("renorm", C.c_int), ("renorm_eps", C.c_float), ("routed_scale", C.c_float),
+                ("correction_bias", vp)]
+
+
+class mr_expert_ptrs(C.Structure):
+    _fields_ = [("packed", vp * 3), ("scales", vp * 3), ("biases", vp * 3)]
+
+
+class mr_moe_layer(C.Structure):
+    _fields_ = [("hidden", C.c_int64), ("inter", C.c_int64), ("shared_inter", C.c_int64),
+                ("router", mr_router_config), ("router_w", vp),
+                ("gate", mr_affine_desc), ("up", mr_affine_desc), ("down", mr_affine_desc),
+                ("expert_table", vp),
+                ("shared_gate", mr_affine_desc), ("shared_up", mr_affine_desc),
+                ("shared_down", mr_affine_desc),
+                ("swiglu_limit", C.c_float), ("weight_placement", C.c_int)]
+
+
+# name -> (restype, argtypes); the complete exported surface of the header
+SIGNATURES = {
+    "mr_abi_version": (C.c_int, []),
+    "mr_status_string": (C.c_char_p, [C.c_int]),
+    "mr_ctx_create": (C.c_int, [C.c_int, C.POINTER(vp)]),
+    "mr_ctx_destroy": (C.c_int, [vp]),
+    "mr_last_error": (C.c_char_p, [vp]),
+    "mr_ctx_check": (C.c_int, [vp, vp, C.POINTER(C.c_uint32)]),
+    "mr_ctx_reserve": (C.c_int, [vp, C.c_int64, C.c_int32, C.c_int32, C.c_int64, C.c_int64]),
+    "mr_affine_validate": (C.c_int, [C.POINTER(mr_affine_desc), C.c_char_p, C.c_size_t]),
+    "mr_affine_mm": (C.c_int, [vp, vp, C.c_int64, C.POINTER(mr_affine_desc), vp, vp]),
+    "mr_affine_gather_mm": (C.c_int, [vp, vp, C.c_int64, vp, C.c_int32,
+                                      C.POINTER(mr_affine_desc), vp, vp]),
+    "mr_affine_dequantize": (C.c_int, [vp, C.POINTER(mr_affine_desc), vp, vp]),
+    "mr_router_config_validate": (C.c_int, [C.POINTER(mr_router_config), C.c_char_p,
+                                            C.c_size_t]),
+    "mr_router_select": (C.c_int, [vp, vp, C.c_int64, C.c_int64, vp,
+                                   C.POINTER(mr_router_config), vp, vp, vp, vp, vp]),
+    "mr_router_select_logits": (C.c_int, [vp, vp, C.c_int64, C.POINTER(mr_router_config),
+                                          vp, vp, vp, vp]),
+    "mr_moe_layer_validate": (C.c_int, [C.POINTER(mr_moe_layer), C.c_char_p, C.c_size_t]),
+    "mr_moe_layer_forward": (C.c_int, [vp, C.POINTER(mr_moe_layer), vp, C.c_int64, vp, vp, vp,
+                                       vp, vp]),
+    "mr_moe_layer_forward_host": (C.c_int, [vp, C.POINTER(mr_moe_layer), vp, C.c_int64, vp, vp,
+                                            vp]),
+    "mr_ctx_profile": (C.c_int, [vp, C.c_int]),
+    "mr_ctx_profile_read": (C.c_int, [vp, C.POINTER(C.c_double), C.POINTER(C.c_int64), C.c_int]),
+    "mr_synth_label": (C.c_uint64, [C.c_uint32] * 4),
+    "mr_synth_derive": (C.c_uint64, [C.c_uint64, C.c_uint64]),
+    "mr_synth_words": (C.c_int, [vp, C.c_uint64, C.c_int64, vp, vp]),
+    "mr_synth_normal_bf16": (C.c_int, [vp, C.c_uint64, C.c_int64, C.c_float, C.c_int, vp, vp]),
+    "mr_synth_affine_biases": (C.c_int, [vp, vp, C.c_int64, C.c_int32, vp, vp]),
+}
+
+_lib = None
+
+
+class LibraryMissing(RuntimeError):
+    pass
+
+
+def load():
+    """Load the built library (raises LibraryMissing if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise LibraryMissing(
+                f"{LIB_PATH} is missing: build it with `make -C minirun-app_b200/csrc` "
+                "(or __graft_entry__.build()); there is no CPU fallback")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
