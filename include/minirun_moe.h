@@ -65,6 +65,7 @@ typedef enum mr_dtype {
 #define MR_DEVERR_BAD_EXPERT_ID 0x1u   /* an id outside [0, experts)     */
 #define MR_DEVERR_NONFINITE_SCORE 0x2u /* router produced NaN/Inf score  */
 #define MR_DEVERR_RENORM_ZERO 0x4u     /* selected weights sum <= 0      */
+#define MR_DEVERR_TIMEOUT 0x8u         /* a bounded device wait expired  */
 
 typedef struct mr_ctx mr_ctx;
 
@@ -83,6 +84,11 @@ const char* mr_last_error(const mr_ctx* ctx);
 /* Synchronise `stream`, read and clear the device error word. Returns
  * MR_ERR_DEVICE (and writes the bits to *bits_out if non-NULL) when set. */
 mr_status mr_ctx_check(mr_ctx* ctx, void* stream, uint32_t* bits_out);
+/* Selects the dequant-GEMV implementation (a tuning/testing knob; results
+ * agree to fp32 summation order): 0 auto (TMA-pipelined where in % 512 == 0
+ * and scale/bias rows are 16-byte aligned), 1 register-streaming, 2 TMA
+ * (falls back to 1 where its layout conditions do not hold). */
+mr_status mr_ctx_set_kernel_path(mr_ctx* ctx, int path);
 /* Pre-size the workspace for layers up to these sizes (graph capture needs
  * a workspace that will not grow). */
 mr_status mr_ctx_reserve(mr_ctx* ctx, int64_t max_tokens, int32_t top_k,
@@ -272,7 +278,7 @@ mr_status mr_synth_words(mr_ctx* ctx, uint64_t seed, int64_t n, uint32_t* out,
                          void* stream);
 /* n bf16 values: bf16(std * N(0,1)) (|.| if absval), Box-Muller over
  * value(seed, 2i), value(seed, 2i+1). */
-mr_status mr_synth_normal_bf16(mr_ctx* ctx, uint64_t seed, int64_t n, float std,
+mr_status mr_synth_normal_bf16(mr_ctx* ctx, uint64_t seed, int64_t n, double std,
                                int absval, uint16_t* out, void* stream);
 /* biases[i] = bf16(-2^(bits-1) * scales[i]) */
 mr_status mr_synth_affine_biases(mr_ctx* ctx, const uint16_t* scales, int64_t n,

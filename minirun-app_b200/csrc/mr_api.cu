@@ -154,6 +154,120 @@ static ExpertSource stack_source(const mr_affine_desc& d, int proj) {
 
 static cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Whether the TMA-pipelined GEMV can stream this projection: whole 8-group
+// stages, 16-byte aligned tensor bases, and experts addressable as one 2-D
+// tensor (a stack; pointer tables use the register-streaming kernel).
+static bool tma_layout_ok(int64_t in, const mr_affine_desc* d, bool table) {
+  if (in % (kTmaGps * kGroup) != 0) return false;
+  if (table) return false;
+  return aligned16(d->packed) && aligned16(d->scales) && aligned16(d->biases);
+}
+
+static bool use_tma(const mr_ctx* ctx, bool layout_ok) {
+  return ctx->kernel_path != 1 && layout_ok;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// kind 0: packed codes (uint32 words, 32-word x box_rows boxes, 128-byte
+// swizzle); kind 1/2/3: bf16/f16/f32 scales or biases (8 x box_rows boxes).
+static bool tensor_map(mr_ctx* ctx, CUtensorMap* out, const void* base, int64_t rows,
+                       int64_t width, int box_rows, int kind) {
+  const mr_ctx::MapKey key{base, rows, width, box_rows, kind};
+  for (auto& e : ctx->map_cache)
+    if (e.first == key) {
+      memcpy(out, e.second.data(), sizeof(CUtensorMap));
+      return true;
+    }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const int esz = kind == 0 ? 4 : (kind == 3 ? 4 : 2);
+  const CUtensorMapDataType dt = kind == 0   ? CU_TENSOR_MAP_DATA_TYPE_UINT32
+                                 : kind == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : kind == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(width * esz)};
+  const cuuint32_t box[2] = {(cuuint32_t)(kind == 0 ? 32 : kTmaGps), (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(out, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  kind == 0 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  if (ctx->map_cache.size() > 256) ctx->map_cache.clear();
+  std::vector<unsigned char> bytes(sizeof(CUtensorMap));
+  memcpy(bytes.data(), out, sizeof(CUtensorMap));
+  ctx->map_cache.emplace_back(key, std::move(bytes));
+  return true;
+}
+
+// One matrix (stack of `experts` or a single matrix) for the TMA kernel.
+struct MapSpec {
+  const mr_affine_desc* d;
+  int64_t experts;  // 1 for a single matrix
+};
+
+static bool encode_matrix(mr_ctx* ctx, const MapSpec& m, int box_rows, CUtensorMap* packed,
+                          CUtensorMap* scales, CUtensorMap* biases) {
+  const mr_affine_desc* d = m.d;
+  const int64_t rows = m.experts * d->out_features;
+  const int64_t words = d->in_features * d->bits / 32;
+  const int64_t groups = d->in_features / d->group_size;
+  const int kind = 1 + (int)d->scale_dtype;
+  return tensor_map(ctx, packed, d->packed, rows, words, box_rows, 0) &&
+         tensor_map(ctx, scales, d->scales, rows, groups, box_rows, kind) &&
+         tensor_map(ctx, biases, d->biases, rows, groups, box_rows, kind);
+}
+
+// Issues one GEMV over the plan with the chosen implementation.
+// TMA items are 64 plain rows (32 gate + 32 up for SwiGLU); register-kernel
+// CTAs cover 128 plain rows (64 + 64). maps[0..3] = a, b, shared a, shared b
+// (b and the shared ones may be NULL).
+static cudaError_t run_gemv(mr_ctx* ctx, GemvParams g, int64_t max_segments, bool tma,
+                            const MapSpec* maps, int bits, int sd, int epi, int nt,
+                            cudaStream_t s) {
+  if (tma) {
+    TmaMaps tm;
+    const int box_rows = epi == EPI_SWIGLU ? kTmaRows / 2 : kTmaRows;
+    bool ok = encode_matrix(ctx, maps[0], box_rows, &tm.a_packed, &tm.a_scales, &tm.a_biases);
+    const MapSpec& mb = maps[1].d ? maps[1] : maps[0];
+    ok = ok && encode_matrix(ctx, mb, box_rows, &tm.b_packed, &tm.b_scales, &tm.b_biases);
+    const MapSpec& sa = maps[2].d ? maps[2] : maps[0];
+    const MapSpec& sb = maps[3].d ? maps[3] : (maps[2].d ? maps[2] : maps[0]);
+    ok = ok && encode_matrix(ctx, sa, box_rows, &tm.sa_packed, &tm.sa_scales, &tm.sa_biases);
+    ok = ok && encode_matrix(ctx, sb, box_rows, &tm.sb_packed, &tm.sb_scales, &tm.sb_biases);
+    if (ok) {
+      g.rb_count = (int)(epi == EPI_SWIGLU ? g.rows / 32 : (g.rows + kTmaRows - 1) / kTmaRows);
+      const int64_t items = (max_segments + g.shared_segments) * g.rb_count;
+      const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
+      return launch_tma(g, tm, bits, sd, epi, nt, grid, s);
+    }
+    // no driver entry point / map refused: stream with the register kernel
+  }
+  g.rb_count = (int)(epi == EPI_SWIGLU ? g.rows / kRowsUp : (g.rows + kRowsPlain - 1) / kRowsPlain);
+  const int64_t items = (max_segments + g.shared_segments) * g.rb_count;
+  return launch_gemv(g, bits, sd, epi, nt, (int)items, s);
+}
+
 static cudaEvent_t pool_event(mr_ctx* ctx) {
   if (!ctx->event_pool.empty()) {
     cudaEvent_t e = ctx->event_pool.back();
@@ -378,7 +492,7 @@ static mr_status validate_layer(const mr_moe_layer* L, std::string& why) {
       return MR_ERR_UNSUPPORTED;
     }
   }
-  if ((L->hidden + kRowsPlain - 1) / kRowsPlain > kMaxCounters - 8) {
+  if ((L->hidden + kTmaRows - 1) / kTmaRows > kMaxCounters - 8) {
     why = "hidden size exceeds the combine counter table";
     return MR_ERR_UNSUPPORTED;
   }
@@ -423,7 +537,8 @@ static mr_status affine_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const 
   if (!dense && E > kMaxExperts)
     return fail(ctx, MR_ERR_UNSUPPORTED, "expert stacks larger than 1024 are not built here");
   const int64_t in = w->in_features;
-  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / kMaxCols + 1;
+  const int seg_cols = pick_seg_cols(Tk);
+  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / seg_cols + 1;
 
   Bump b{nullptr};
   for (int pass = 0; pass < 2; ++pass) {
@@ -453,10 +568,10 @@ static mr_status affine_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const 
   prep_kernel<<<pgrid, 256, 0, s>>>(pp);
   if ((st = cuda_check(ctx, cudaGetLastError(), "prep_kernel"))) return st;
   if (dense) {
-    dense_plan_kernel<<<(int)std::min<int64_t>((T + 255) / 256, 1024), 256, 0, s>>>((int)T, nseg,
+    dense_plan_kernel<<<(int)std::min<int64_t>((T + 255) / 256, 1024), 256, 0, s>>>((int)T, seg_cols, nseg,
                                                                                    segs, cols);
   } else {
-    PlanParams plan{ids, (int)Tk, E, nseg, segs, cols, ctx->d_error};
+    PlanParams plan{ids, (int)Tk, E, nseg, segs, cols, ctx->d_error, seg_cols};
     plan_kernel<<<1, 256, 0, s>>>(plan);
   }
   if ((st = cuda_check(ctx, cudaGetLastError(), "plan kernel"))) return st;
@@ -473,17 +588,29 @@ static mr_status affine_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const 
   g.cols = cols;
   g.shared_segments = 0;
   g.shared_cols = 0;
-  g.rb_count = (int)((w->out_features + kRowsPlain - 1) / kRowsPlain);
   g.Tk = (int)Tk;
   g.in_div = kk;
   g.shared_in_off = 0;
   g.xperm = xperm;
   g.xsum = xsum;
+  g.xsum_parts = 1;
+  g.error = ctx->d_error;
   g.out_bf16 = out;
-  const int64_t grid = max_seg * g.rb_count;
-  const int nt = pick_nt((int)std::min<int64_t>(kMaxCols, Tk));
-  return cuda_check(ctx, launch_gemv(g, w->bits, w->scale_dtype, EPI_STORE, nt, (int)grid, s),
-                    "gemv(store)");
+  g.seg_cols = seg_cols;
+  const int nt = seg_cols / 8;
+  const bool tma = use_tma(ctx, tma_layout_ok(in, w, false));
+  const MapSpec maps[4] = {{w, dense ? 1 : (int64_t)w->experts}, {nullptr, 0}, {nullptr, 0},
+                           {nullptr, 0}};
+  return cuda_check(
+      ctx, run_gemv(ctx, g, max_seg, tma, maps, w->bits, w->scale_dtype, EPI_STORE, nt, s),
+      "gemv(store)");
+}
+
+mr_status mr_ctx_set_kernel_path(mr_ctx* ctx, int path) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  if (path < 0 || path > 2) return fail(ctx, MR_ERR_INVALID_ARGUMENT, "kernel path must be 0, 1 or 2");
+  ctx->kernel_path = path;
+  return MR_OK;
 }
 
 mr_status mr_affine_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens, const mr_affine_desc* w,
@@ -544,6 +671,7 @@ mr_status mr_affine_dequantize(mr_ctx* ctx, const mr_affine_desc* w, float* out,
 
 struct LogitsShape {
   int mtiles, tblocks, ks, kchunk, blocks;
+  int kq;  // partial logits written (one per CTA K range of 4 chunks)
 };
 
 static LogitsShape logits_shape(const mr_ctx* ctx, int64_t T, int E, int64_t H) {
@@ -558,14 +686,15 @@ static LogitsShape logits_shape(const mr_ctx* ctx, int64_t T, int E, int64_t H) 
   chunk = (chunk + 31) / 32 * 32;
   s.kchunk = (int)chunk;
   s.ks = (int)((H + chunk - 1) / chunk);
-  s.blocks = (int)((base * s.ks + 3) / 4);
+  s.kq = (s.ks + 3) / 4;
+  s.blocks = (int)(base * s.kq);
   return s;
 }
 
 static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
                              const mr_router_config* c, int32_t* ids, float* weights,
                              float* margins, float* logits_out, bool plan, int* nseg, int4* segs,
-                             int* cols, cudaStream_t s) {
+                             int* cols, int seg_cols, cudaStream_t s) {
   TopkParams tp{};
   tp.part = part;
   tp.ks = ks;
@@ -583,9 +712,18 @@ static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
   tp.logits_out = logits_out;
   tp.error = ctx->d_error;
   tp.build_plan = plan ? 1 : 0;
-  tp.plan = PlanParams{ids, (int)(T * c->top_k), c->experts, nseg, segs, cols, ctx->d_error};
+  tp.plan = PlanParams{ids, (int)(T * c->top_k), c->experts, nseg, segs, cols, ctx->d_error,
+                       seg_cols};
   tp.counter = ctx->d_counters + (kMaxCounters - 1);
-  topk_kernel<<<(int)((T + 7) / 8), 256, 0, s>>>(tp);
+  const int grid = (int)((T + 7) / 8);
+  const int epl = (c->experts + 31) / 32;
+  if (epl <= 1) topk_kernel<1><<<grid, 256, 0, s>>>(tp);
+  else if (epl <= 2) topk_kernel<2><<<grid, 256, 0, s>>>(tp);
+  else if (epl <= 4) topk_kernel<4><<<grid, 256, 0, s>>>(tp);
+  else if (epl <= 8) topk_kernel<8><<<grid, 256, 0, s>>>(tp);
+  else if (epl <= 12) topk_kernel<12><<<grid, 256, 0, s>>>(tp);
+  else if (epl <= 16) topk_kernel<16><<<grid, 256, 0, s>>>(tp);
+  else topk_kernel<32><<<grid, 256, 0, s>>>(tp);
   return cuda_check(ctx, cudaGetLastError(), "topk_kernel");
 }
 
@@ -601,11 +739,11 @@ mr_status mr_router_select(mr_ctx* ctx, const uint16_t* x, int64_t T, int64_t H,
   if (H % 32 != 0) return fail(ctx, MR_ERR_UNSUPPORTED, "hidden size must be a multiple of 32");
   const LogitsShape ls = logits_shape(ctx, T, cfg->experts, H);
   Bump b{nullptr};
-  b.take<float>((size_t)ls.ks * T * cfg->experts);
+  b.take<float>((size_t)ls.kq * T * cfg->experts);
   if ((st = ensure_workspace(ctx, b.off))) return st;
   b.base = reinterpret_cast<char*>(ctx->ws);
   b.off = 0;
-  float* part = b.take<float>((size_t)ls.ks * T * cfg->experts);
+  float* part = b.take<float>((size_t)ls.kq * T * cfg->experts);
   cudaStream_t s = as_stream(stream);
   LogitsParams lp{};
   lp.x = x;
@@ -622,8 +760,8 @@ mr_status mr_router_select(mr_ctx* ctx, const uint16_t* x, int64_t T, int64_t H,
   lp.do_prep = 0;
   logits_kernel<<<ls.blocks, 128, 0, s>>>(lp);
   if ((st = cuda_check(ctx, cudaGetLastError(), "logits_kernel"))) return st;
-  return topk_launch(ctx, part, ls.ks, T, cfg, ids, weights, margins, logits_out, false, nullptr,
-                     nullptr, nullptr, s);
+  return topk_launch(ctx, part, ls.kq, T, cfg, ids, weights, margins, logits_out, false, nullptr,
+                     nullptr, nullptr, 8, s);
 }
 
 mr_status mr_router_select_logits(mr_ctx* ctx, const float* logits, int64_t T,
@@ -636,7 +774,7 @@ mr_status mr_router_select_logits(mr_ctx* ctx, const float* logits, int64_t T,
   if (T <= 0 || !logits || !ids || !weights)
     return fail(ctx, MR_ERR_INVALID_ARGUMENT, "router logits must contain at least one token");
   return topk_launch(ctx, logits, 1, T, cfg, ids, weights, margins, nullptr, false, nullptr,
-                     nullptr, nullptr, as_stream(stream));
+                     nullptr, nullptr, 8, as_stream(stream));
 }
 
 // ------------------------------------------------------------------ layer
@@ -647,13 +785,13 @@ mr_status mr_ctx_reserve(mr_ctx* ctx, int64_t max_tokens, int32_t top_k, int32_t
   if (max_tokens <= 0 || top_k <= 0 || experts <= 0 || hidden <= 0 || inter <= 0)
     return fail(ctx, MR_ERR_INVALID_ARGUMENT, "reserve sizes must be positive");
   const int64_t T = max_tokens, Tk = T * top_k, R = Tk + 2 * T;
-  const int64_t max_seg = std::min<int64_t>(experts, Tk) + Tk / kMaxCols + 1;
+  const int64_t max_seg = std::min<int64_t>(experts, Tk) + Tk / 8 + 1;
   size_t bytes = 0;
   bytes += (size_t)64 * T * experts * 4 + 256;  // logits partials (ks <= 64)
   bytes += (size_t)T * hidden * 2 + 256 + (size_t)T * (hidden / kGroup) * 4 + 256;
   bytes += (size_t)Tk * 8 + (size_t)T * 4 + 1024;
   bytes += (size_t)max_seg * 16 + (size_t)Tk * 4 + 1024;
-  bytes += (size_t)R * inter * 2 + (size_t)R * (inter / kGroup) * 4 + (size_t)R * hidden * 4 + 1024;
+  bytes += (size_t)R * inter * 2 + (size_t)R * (inter / 32) * 4 + (size_t)R * hidden * 4 + 1024;
   return ensure_workspace(ctx, bytes);
 }
 
@@ -672,7 +810,8 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   const int64_t H = L->hidden, I = L->inter, Tk = T * k;
   const bool has_shared = L->shared_inter > 0;
   const int64_t R = Tk + (has_shared ? 2 * T : 0);  // h / partial rows
-  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / kMaxCols + 1;
+  const int seg_cols = pick_seg_cols(T);  // a routed expert has <= T columns
+  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / seg_cols + 1;
   const LogitsShape ls = logits_shape(ctx, T, E, H);
   if (Tk > (int64_t)1 << 28) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
 
@@ -685,7 +824,7 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   Bump b{nullptr};
   for (int pass = 0; pass < 2; ++pass) {
     b.off = 0;
-    part = b.take<float>((size_t)ls.ks * T * E);
+    part = b.take<float>((size_t)ls.kq * T * E);
     xperm = b.take<uint16_t>(T * H);
     xsum = b.take<float>(T * (H / kGroup));
     ids = b.take<int32_t>(Tk);
@@ -694,7 +833,7 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
     segs = b.take<int4>(max_seg);
     cols = b.take<int>(Tk);
     h = b.take<uint16_t>(R * I);
-    hsum = b.take<float>(R * (I / kGroup));
+    hsum = b.take<float>(R * (I / 32));  // two 32-row partial sums per group
     part2 = b.take<float>(R * H);
     if (pass == 0) {
       if ((st = ensure_workspace(ctx, b.off))) return st;
@@ -731,8 +870,8 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   // K0b: scores, top-k, weights; the last CTA builds the routing plan
   {
     ProfScope ps(ctx, MR_KERNEL_TOPK_PLAN, s);
-    st = topk_launch(ctx, part, ls.ks, T, &L->router, ids, wts, margins_out, nullptr, true, nseg,
-                     segs, cols, s);
+    st = topk_launch(ctx, part, ls.kq, T, &L->router, ids, wts, margins_out, nullptr, true, nseg,
+                     segs, cols, seg_cols, s);
   }
   if (st) return st;
 
@@ -757,14 +896,16 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   g.n_routed_segments = nseg;
   g.segments = segs;
   g.cols = cols;
-  g.shared_segments = has_shared ? (int)((T + kMaxCols - 1) / kMaxCols) : 0;
+  g.shared_segments = has_shared ? (int)((T + seg_cols - 1) / seg_cols) : 0;
+  g.seg_cols = seg_cols;
   g.shared_cols = has_shared ? (int)T : 0;
-  g.rb_count = (int)(I / kRowsUp);
   g.Tk = (int)Tk;
   g.in_div = k;
   g.shared_in_off = (int)Tk;
   g.xperm = xperm;
   g.xsum = xsum;
+  g.xsum_parts = 1;
+  g.error = ctx->d_error;
   g.out_bf16 = h;
   g.hsum = hsum;
   g.weights = wts;
@@ -773,11 +914,19 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   g.h_bits = L->down.bits;
   g.shared_lo_off = (int)T;
   const int bits = L->gate.bits, sd = L->gate.scale_dtype;
-  int64_t grid = (max_seg + g.shared_segments) * g.rb_count;
-  int nt = pick_nt((int)std::min<int64_t>(kMaxCols, T));
+  const bool table = L->expert_table != nullptr;
+  const bool tma1 = use_tma(ctx, tma_layout_ok(H, &L->gate, table) &&
+                                     tma_layout_ok(H, &L->up, table) &&
+                                     (!has_shared || (tma_layout_ok(H, &L->shared_gate, false) &&
+                                                      tma_layout_ok(H, &L->shared_up, false))));
+  const int nt = seg_cols / 8;
   {
     ProfScope ps(ctx, MR_KERNEL_GATE_UP, s);
-    st = cuda_check(ctx, launch_gemv(g, bits, sd, EPI_SWIGLU, nt, (int)grid, s), "gemv(swiglu)");
+    const MapSpec maps[4] = {{&L->gate, E}, {&L->up, E},
+                             {has_shared ? &L->shared_gate : nullptr, 1},
+                             {has_shared ? &L->shared_up : nullptr, 1}};
+    st = cuda_check(ctx, run_gemv(ctx, g, max_seg, tma1, maps, bits, sd, EPI_SWIGLU, nt, s),
+                    "gemv(swiglu)");
   }
   if (st) return st;
 
@@ -797,14 +946,16 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   d.n_routed_segments = nseg;
   d.segments = segs;
   d.cols = cols;
-  d.shared_segments = has_shared ? (int)((2 * T + kMaxCols - 1) / kMaxCols) : 0;
+  d.shared_segments = has_shared ? (int)((2 * T + seg_cols - 1) / seg_cols) : 0;
+  d.seg_cols = seg_cols;
   d.shared_cols = has_shared ? (int)(2 * T) : 0;
-  d.rb_count = (int)((H + kRowsPlain - 1) / kRowsPlain);
   d.Tk = (int)Tk;
   d.in_div = 1;
   d.shared_in_off = 0;
   d.xperm = h;
   d.xsum = hsum;
+  d.xsum_parts = 2;
+  d.error = ctx->d_error;
   d.part = part2;
   d.weights = wts;
   d.weight_after_down = g.weight_after_down;
@@ -813,10 +964,13 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   d.k = k;
   d.has_shared = has_shared ? 1 : 0;
   d.out = out;
-  grid = (max_seg + d.shared_segments) * d.rb_count;
-  nt = pick_nt((int)std::min<int64_t>(kMaxCols, has_shared ? 2 * T : T));
+  const bool tma2 = use_tma(ctx, tma_layout_ok(I, &L->down, table) &&
+                                     (!has_shared || tma_layout_ok(I, &L->shared_down, false)));
   ProfScope ps(ctx, MR_KERNEL_DOWN_COMBINE, s);
-  return cuda_check(ctx, launch_gemv(d, bits, sd, EPI_PARTIAL, nt, (int)grid, s), "gemv(down)");
+  const MapSpec maps[4] = {{&L->down, E}, {nullptr, 0},
+                           {has_shared ? &L->shared_down : nullptr, 1}, {nullptr, 0}};
+  return cuda_check(ctx, run_gemv(ctx, d, max_seg, tma2, maps, bits, sd, EPI_PARTIAL, nt, s),
+                    "gemv(down)");
 }
 
 mr_status mr_moe_layer_forward_host(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x_host,
@@ -950,12 +1104,12 @@ mr_status mr_synth_words(mr_ctx* ctx, uint64_t seed, int64_t n, uint32_t* out, v
   return cuda_check(ctx, cudaGetLastError(), "synth_words");
 }
 
-mr_status mr_synth_normal_bf16(mr_ctx* ctx, uint64_t seed, int64_t n, float std, int absval,
+mr_status mr_synth_normal_bf16(mr_ctx* ctx, uint64_t seed, int64_t n, double std, int absval,
                                uint16_t* out, void* stream) {
   if (!ctx || n < 0 || (n > 0 && !out)) return MR_ERR_INVALID_ARGUMENT;
   if (n == 0) return MR_OK;
-  synth_normal_kernel<<<synth_grid(ctx, n), 256, 0, as_stream(stream)>>>(seed, n, (double)std,
-                                                                           absval, out);
+  synth_normal_kernel<<<synth_grid(ctx, n), 256, 0, as_stream(stream)>>>(seed, n, std, absval,
+                                                                           out);
   return cuda_check(ctx, cudaGetLastError(), "synth_normal");
 }
 

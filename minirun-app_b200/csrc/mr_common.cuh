@@ -17,7 +17,7 @@
 namespace mr {
 
 constexpr int kGroup = 64;         // supported affine group size
-constexpr int kMaxCols = 64;       // columns (token rows) per GEMV segment
+constexpr int kMaxCols = 16;       // max columns (token rows) per GEMV segment
 constexpr int kMaxExperts = 1024;  // router / plan limit
 constexpr int kGemvThreads = 256;  // 8 warps per GEMV CTA
 constexpr int kRowsUp = 64;        // gate/up rows per CTA (one h group)
@@ -97,6 +97,68 @@ MR_DEVICE void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// ------------------------------------------------ mbarrier + bulk copy (TMA)
+
+MR_DEVICE uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+MR_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+// Makes initialised barriers visible to the async (TMA) proxy.
+MR_DEVICE void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+MR_DEVICE void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+MR_DEVICE void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+MR_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// try_wait with a suspend-time hint (ns): the thread sleeps until the phase
+// completes or the hint expires instead of re-polling the barrier.
+MR_DEVICE bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+// Global -> shared bulk copy (TMA, non-tensor), completing on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+MR_DEVICE void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Named barrier among `count` threads (id 0 is __syncthreads).
+MR_DEVICE void named_bar(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Iteration cap of every device-side wait (one try_wait each, which blocks
+// for at most a hardware time slice): seconds, well above any legitimate
+// wait, after which the kernel reports MR_DEVERR_TIMEOUT and returns.
+constexpr uint32_t kSpinLimit = 1u << 26;
+
 // ------------------------------------------------------------ structures
 
 // How a GEMV finds the weights of expert e: a stack (base + e*stride) or a
@@ -143,6 +205,19 @@ struct mr_ctx {
   size_t fixed_bytes = 0;
   unsigned* d_error = nullptr;
   unsigned* d_counters = nullptr;  // kMaxCounters
+  int kernel_path = 0;  // 0 auto, 1 register-streaming GEMV, 2 TMA-pipelined GEMV
+  // encoded TMA tensor maps (128-byte CUtensorMap each), keyed by
+  // (base, rows, width, box rows, kind)
+  struct MapKey {
+    const void* base;
+    int64_t rows, width;
+    int box_rows, kind;
+    bool operator==(const MapKey& o) const {
+      return base == o.base && rows == o.rows && width == o.width && box_rows == o.box_rows &&
+             kind == o.kind;
+    }
+  };
+  std::vector<std::pair<MapKey, std::vector<unsigned char>>> map_cache;
   // device staging of the host-buffer entry point
   void* io = nullptr;
   size_t io_bytes = 0;

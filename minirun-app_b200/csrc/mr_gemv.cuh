@@ -66,13 +66,16 @@ struct GemvParams {
   const int* cols;
   int shared_segments;
   int shared_cols;
+  int seg_cols;        // columns per segment (8 * NT)
   int rb_count;
   int Tk;              // routed pairs (T*k)
   int in_div;          // routed column v reads input row v / in_div
   int shared_in_off;   // shared column v reads input row v - shared_in_off
   // activations
   const uint16_t* xperm;  // [*, in] bf16, permuted per BITS
-  const float* xsum;      // [*, in/64]
+  const float* xsum;      // [*, in/64 * xsum_parts]: per-group sums, in parts
+  int xsum_parts;         // 1 (router prep) or 2 (32-row partial sums of h)
+  unsigned* error;        // device error word
   // epilogues
   uint16_t* out_bf16;     // STORE: [*, rows]; SWIGLU: h [*, rows] permuted
   float* hsum;            // SWIGLU: [*, rows/64]
@@ -153,6 +156,61 @@ MR_DEVICE void group_mma(float (&acc)[4], const uint32_t (&wa)[QTraits<BITS>::kL
   }
 }
 
+// acc += lo(a)*lo(b) + hi(a)*hi(b): two bf16 x bf16 products accumulated in
+// fp32 (mixed-precision fma, one full-rate instruction each).
+MR_DEVICE void fma2_bf16(float& acc, uint32_t a, uint32_t b) {
+  asm("{\n .reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %1;\n mov.b32 {bl, bh}, %2;\n"
+      " fma.rn.f32.bf16 %0, al, bl, %0;\n fma.rn.f32.bf16 %0, ah, bh, %0;\n}"
+      : "+f"(acc)
+      : "r"(a), "r"(b));
+}
+
+// Single-column form of group_mma: this lane's 16 codes of rows a and b
+// against the same 16 activations (the lane's own B-fragment registers, whose
+// pairs line up with the code pairs), summed in fp32. acc[0..1] row a,
+// acc[2..3] row b (two chains each).
+template <int BITS>
+MR_DEVICE void group_fma(float (&acc)[4], const uint32_t (&wa)[QTraits<BITS>::kLaneWords],
+                         const uint32_t (&wb)[QTraits<BITS>::kLaneWords], const uint32_t (&xb)[8]) {
+  if constexpr (BITS == 4) {
+#pragma unroll
+    for (int wi = 0; wi < 2; ++wi) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int sh = 8 * h;
+        const uint32_t x0 = xb[4 * wi + 2 * h], x1 = xb[4 * wi + 2 * h + 1];
+        fma2_bf16(acc[0], ((wa[wi] >> sh) & 0x000F000Fu) | 0x43004300u, x0);
+        fma2_bf16(acc[1], ((wa[wi] >> (sh + 4)) & 0x000F000Fu) | 0x43004300u, x1);
+        fma2_bf16(acc[2], ((wb[wi] >> sh) & 0x000F000Fu) | 0x43004300u, x0);
+        fma2_bf16(acc[3], ((wb[wi] >> (sh + 4)) & 0x000F000Fu) | 0x43004300u, x1);
+      }
+    }
+  } else if constexpr (BITS == 2) {
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int sh = 4 * h;
+      const uint32_t x0 = xb[2 * h], x1 = xb[2 * h + 1];
+      fma2_bf16(acc[0], ((wa[0] >> sh) & 0x00030003u) | 0x43004300u, x0);
+      fma2_bf16(acc[1], ((wa[0] >> (sh + 2)) & 0x00030003u) | 0x43004300u, x1);
+      fma2_bf16(acc[2], ((wb[0] >> sh) & 0x00030003u) | 0x43004300u, x0);
+      fma2_bf16(acc[3], ((wb[0] >> (sh + 2)) & 0x00030003u) | 0x43004300u, x1);
+    }
+  } else {
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+      const uint32_t x0 = xb[2 * wi], x1 = xb[2 * wi + 1];
+      fma2_bf16(acc[0], (wa[wi] & 0x000F000Fu) | 0x43004300u, x0);
+      fma2_bf16(acc[1], ((wa[wi] >> 8) & 0x000F000Fu) | 0x43004300u, x1);
+      fma2_bf16(acc[0], ((wa[wi] >> 4) & 0x000F000Fu) | 0x45004500u, x0);
+      fma2_bf16(acc[1], ((wa[wi] >> 12) & 0x000F000Fu) | 0x45004500u, x1);
+      fma2_bf16(acc[2], (wb[wi] & 0x000F000Fu) | 0x43004300u, x0);
+      fma2_bf16(acc[3], ((wb[wi] >> 8) & 0x000F000Fu) | 0x43004300u, x1);
+      fma2_bf16(acc[2], ((wb[wi] >> 4) & 0x000F000Fu) | 0x45004500u, x0);
+      fma2_bf16(acc[3], ((wb[wi] >> 12) & 0x000F000Fu) | 0x45004500u, x1);
+    }
+  }
+}
+
 template <int BITS, int SD, int EPI, int NT, int D>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) {
   constexpr int LW = QTraits<BITS>::kLaneWords;
@@ -166,6 +224,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
   const int64_t wpr = p.in * BITS / 32;
   const int n_routed = *p.n_routed_segments;
   const int n_items = (n_routed + p.shared_segments) * p.rb_count;
+  const int parts = p.xsum_parts;
 
   __shared__ float red[8][kMaxCols][2];
   __shared__ int s_last;
@@ -183,8 +242,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
       shared = false;
     } else {
       const int ss = seg - n_routed;
-      col0 = ss * kMaxCols;
-      ncols = min(kMaxCols, p.shared_cols - col0);
+      col0 = ss * p.seg_cols;
+      ncols = min(p.seg_cols, p.shared_cols - col0);
       shared = true;
     }
     auto col_value = [&](int ci) -> int {
@@ -229,8 +288,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
       const int c0 = min(t * 8 + 2 * c, ncols - 1);
       const int c1 = min(t * 8 + 2 * c + 1, ncols - 1);
       xrow[t] = p.xperm + in_row(col_value(cb)) * p.in + c * 16;
-      xs0[t] = in_row(col_value(c0)) * ngroups;
-      xs1[t] = in_row(col_value(c1)) * ngroups;
+      xs0[t] = in_row(col_value(c0)) * ngroups * parts;
+      xs1[t] = in_row(col_value(c1)) * ngroups * parts;
     }
 
     float y[NT][4];
@@ -282,8 +341,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
               const uint4 x0 = ldg_u128(xrow[t] + (int64_t)g * kGroup);
               const uint4 x1 = ldg_u128(xrow[t] + (int64_t)g * kGroup + 8);
               const uint32_t xb[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-              const float X0 = __ldg(p.xsum + xs0[t] + g);
-              const float X1 = __ldg(p.xsum + xs1[t] + g);
+              float X0 = __ldg(p.xsum + xs0[t] + g * parts);
+              float X1 = __ldg(p.xsum + xs1[t] + g * parts);
+              if (parts == 2) {
+                X0 += __ldg(p.xsum + xs0[t] + g * 2 + 1);
+                X1 += __ldg(p.xsum + xs1[t] + g * 2 + 1);
+              }
               float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
               group_mma<BITS>(acc, wa, wb, xb);
               y[t][0] = fmaf(s_a, acc[0], fmaf(zc_a, X0, y[t][0]));
@@ -367,18 +430,21 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
         }
       }
       __syncthreads();
-      if ((int)threadIdx.x < ncols) {
-        const int ci = threadIdx.x;
+      // 32-row partial sums: warps 0-3 cover h rows rb*64 + [0, 32), warps 4-7
+      // the next 32 (the layout the TMA kernel writes)
+      if ((int)threadIdx.x < 2 * ncols) {
+        const int part = (int)threadIdx.x / ncols;
+        const int ci = (int)threadIdx.x - part * ncols;
         float shi = 0.0f, slo = 0.0f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          shi += red[w][ci][0];
-          slo += red[w][ci][1];
+        for (int w = 0; w < 4; ++w) {
+          shi += red[part * 4 + w][ci][0];
+          slo += red[part * 4 + w][ci][1];
         }
         const int v = col_value(ci);
-        const int64_t hg = p.rows / kGroup;
-        p.hsum[(int64_t)v * hg + rb] = shi;
-        if (shared) p.hsum[(int64_t)(v + p.shared_lo_off) * hg + rb] = slo;
+        const int64_t hp = p.rows / 32;
+        p.hsum[(int64_t)v * hp + rb * 2 + part] = shi;
+        if (shared) p.hsum[(int64_t)(v + p.shared_lo_off) * hp + rb * 2 + part] = slo;
       }
       __syncthreads();
     } else {  // EPI_PARTIAL + fused combine

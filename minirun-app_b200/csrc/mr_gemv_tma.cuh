@@ -1,0 +1,610 @@
+// mr_gemv_tma.cuh — persistent, TMA-fed gathered affine dequant-GEMV.
+//
+// One CTA per SM loops over work items (segment of <= 16 columns sharing an
+// expert) x (64 rows: 64 plain rows, or 32 gate + 32 up rows for SwiGLU).
+// The last warp is the producer: for every stage (8 quantisation groups of
+// the item's rows) one lane posts the byte count on the stage's "full"
+// mbarrier and issues 2-D tensor TMA loads (cp.async.bulk.tensor) of the
+// packed codes — boxes of rows x 128 bytes, 128-byte swizzled — and of the
+// rows' 8 scales and 8 biases, into an NST-deep ring of shared-memory
+// stages. The producer runs ahead across items, so the HBM stream does not
+// drain between items; bytes in flight per SM are set by the ring depth, not
+// by register pressure.
+// 16 consumer warps: warp w owns m-tile (w & 3) and K-quarter (w >> 2) — 2
+// of the stage's 8 groups — reading codes from shared memory and running the
+// same register dequant + mma.m16n8k16 + exact per-group fold as the
+// register-streaming kernel. At the end of an item the four K-quarters are
+// summed in a fixed order through shared memory (deterministic), then the
+// epilogue (bf16 store / SwiGLU / partial + fused combine) runs.
+// Requires in % 512 == 0 (whole stages) and expert stacks addressable by one
+// 2-D tensor map per projection (stack base + expert * rows).
+#pragma once
+
+#include <cuda.h>
+
+#include "mr_gemv.cuh"
+
+namespace mr {
+
+constexpr int kTmaRows = 64;
+constexpr int kTmaGps = 8;  // groups per stage
+constexpr int kTmaConsumerWarps = 16;                   // 4 m-tiles x kKSplit
+constexpr int kKSplit = kTmaConsumerWarps / 4;           // warps sharing an m-tile
+constexpr int kGpw = kTmaGps / kKSplit;                  // groups per warp per stage
+constexpr int kTmaConsumers = kTmaConsumerWarps * 32;
+constexpr int kTmaThreads = kTmaConsumers + 32;
+constexpr int kSmemBudget = 227 * 1024;
+
+// Tensor maps of one launch: a/b = gate/up (SwiGLU) or the projection (a);
+// sa/sb = the shared expert's matrices.
+struct TmaMaps {
+  CUtensorMap a_packed, a_scales, a_biases;
+  CUtensorMap b_packed, b_scales, b_biases;
+  CUtensorMap sa_packed, sa_scales, sa_biases;
+  CUtensorMap sb_packed, sb_scales, sb_biases;
+};
+
+template <int BITS, int SD, int EPI>
+struct TmaStage {
+  static constexpr int kMats = (EPI == EPI_SWIGLU) ? 2 : 1;
+  static constexpr int kBoxRows = kTmaRows / kMats;  // rows per box
+  static constexpr int kBoxBytes = kBoxRows * 128;   // one 128-byte-wide box
+  static constexpr int kBoxes = BITS / 2;            // boxes per matrix per stage (64*bits B)
+  static constexpr int kGroupBytes = 8 * BITS;       // packed bytes per row per group
+  static constexpr int kEsz = ScaleT<SD>::kBytes;
+  static constexpr int kABytes = kMats * kBoxes * kBoxBytes;
+  static constexpr int kSBytes = kTmaRows * kTmaGps * kEsz;  // scales (or biases)
+  static constexpr int kBytes = (kABytes + 2 * kSBytes + 1023) / 1024 * 1024;
+  static constexpr uint32_t kTx = kABytes + 2 * kSBytes;
+};
+
+template <int NT>
+struct TmaFixed {
+  static constexpr int kRedFloats = (kKSplit - 1) * 4 * NT * 32 * 4;
+  static constexpr int kHsFloats = 4 * kMaxCols * 2;
+  static constexpr int kBytes = (kRedFloats + kHsFloats) * 4 + 16;  // + flags
+};
+
+template <int BITS, int SD, int EPI, int NT>
+inline int tma_stages() {
+  const int fixed = TmaFixed<NT>::kBytes + 2 * 16 * 8 + 1024;  // + barriers, alignment slack
+  int n = (kSmemBudget - fixed) / TmaStage<BITS, SD, EPI>::kBytes;
+  return n > 16 ? 16 : n;
+}
+template <int BITS, int SD, int EPI, int NT>
+inline int tma_smem_bytes(int nst) {
+  return 1024 + nst * TmaStage<BITS, SD, EPI>::kBytes + TmaFixed<NT>::kBytes + 2 * nst * 8;
+}
+
+struct ItemInfo {
+  int expert;
+  int col0;
+  int ncols;
+  bool shared;
+  int rb;
+};
+
+MR_DEVICE ItemInfo decode_item(const GemvParams& p, int n_routed, int item) {
+  ItemInfo it;
+  const int seg = item / p.rb_count;
+  it.rb = item - seg * p.rb_count;
+  if (seg < n_routed) {
+    const int4 s = p.segments[seg];
+    it.expert = s.x;
+    it.col0 = s.y;
+    it.ncols = s.z;
+    it.shared = false;
+  } else {
+    const int ss = seg - n_routed;
+    it.expert = 0;
+    it.col0 = ss * p.seg_cols;
+    it.ncols = min(p.seg_cols, p.shared_cols - it.col0);
+    it.shared = true;
+  }
+  return it;
+}
+
+// 2-D tiled TMA load of box {x, y} into shared memory, completing on `bar`.
+MR_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Byte b (< 128) of row r of a 128-byte-swizzled box (box base 1024-aligned).
+MR_DEVICE const char* swz128(const char* box, int r, int b) {
+  return box + r * 128 + ((((b >> 4) ^ r) & 7) << 4) + (b & 15);
+}
+
+template <int LW>
+MR_DEVICE void lds_words(uint32_t (&w)[LW], const char* p) {
+  if constexpr (LW == 1) {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  } else if constexpr (LW == 2) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    w[0] = v.x;
+    w[1] = v.y;
+  } else {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    w[0] = v.x;
+    w[1] = v.y;
+    w[2] = v.z;
+    w[3] = v.w;
+  }
+}
+
+template <int SD>
+MR_DEVICE float lds_scale(const char* base, int idx) {
+  if constexpr (SD == MR_DTYPE_F32) {
+    return reinterpret_cast<const float*>(base)[idx];
+  } else {
+    return scale_to_f32<SD>((uint32_t)reinterpret_cast<const unsigned short*>(base)[idx]);
+  }
+}
+
+// Two consecutive scales (or biases) from shared memory, as fp32.
+template <int SD>
+MR_DEVICE void lds_scale2(float (&v)[2], const char* p) {
+  if constexpr (SD == MR_DTYPE_F32) {
+    const float2 f = *reinterpret_cast<const float2*>(p);
+    v[0] = f.x;
+    v[1] = f.y;
+  } else {
+    const uint32_t r = *reinterpret_cast<const uint32_t*>(p);
+    if constexpr (SD == MR_DTYPE_BF16) {
+      v[0] = __uint_as_float(r << 16);
+      v[1] = __uint_as_float(r & 0xffff0000u);
+    } else {
+      v[0] = __half2float(__ushort_as_half((unsigned short)(r & 0xffffu)));
+      v[1] = __half2float(__ushort_as_half((unsigned short)(r >> 16)));
+    }
+  }
+}
+
+// Group sums of x for 2 consecutive groups; with XP == 2 each group's sum is
+// stored as two 32-row partials, added here in order.
+template <int XP>
+MR_DEVICE void ldg_xsum2(float (&X)[2], const float* p) {
+  if constexpr (XP == 1) {
+    const float2 a = __ldg(reinterpret_cast<const float2*>(p));
+    X[0] = a.x;
+    X[1] = a.y;
+  } else {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    X[0] = a.x + a.y;
+    X[1] = a.z + a.w;
+  }
+}
+
+// Bounded wait. On expiry (or once another thread has flagged an abort) it
+// sets the device error word and the CTA's abort flag and returns, so the
+// caller carries on to every barrier it owes: results are then garbage but
+// the kernel ends and the host reads MR_DEVERR_TIMEOUT.
+MR_DEVICE void wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                            unsigned* error) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return;
+    if ((i & 1023u) == 1023u && *abort_flag) return;
+  }
+  *abort_flag = 1;
+  atomicOr(error, MR_DEVERR_TIMEOUT);
+}
+
+// Warp-level wait: lane 0 sleeps on the barrier, the other lanes wait at
+// __syncwarp, then every lane takes one (already complete) try_wait for its
+// own acquire of the stage's data. Keeps 8 pollers per CTA instead of 256.
+MR_DEVICE void warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                         unsigned* error) {
+  if ((threadIdx.x & 31) == 0) wait_bounded(bar, parity, abort_flag, error);
+  __syncwarp();
+  (void)mbar_try_wait(bar, parity);
+}
+
+template <int BITS, int SD, int EPI, int NT>
+__global__ void __launch_bounds__(kTmaThreads, 1)
+    gemv_tma_kernel(const GemvParams p, const __grid_constant__ TmaMaps maps, const int nst) {
+  using ST = TmaStage<BITS, SD, EPI>;
+  constexpr int LW = QTraits<BITS>::kLaneWords;
+  constexpr float kC = QTraits<BITS>::kMagic;
+  extern __shared__ char smem_raw[];
+  char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* red = reinterpret_cast<float*>(smem + nst * ST::kBytes);
+  float* hs = red + TmaFixed<NT>::kRedFloats;
+  volatile int* flags = reinterpret_cast<volatile int*>(hs + TmaFixed<NT>::kHsFloats);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * ST::kBytes + TmaFixed<NT>::kBytes);
+  uint64_t* empty = full + nst;
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int ngroups = (int)(p.in / kGroup);
+  const int nstages = ngroups / kTmaGps;
+  const int n_routed = *p.n_routed_segments;
+  const int n_items = (n_routed + p.shared_segments) * p.rb_count;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nst; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, kTmaConsumerWarps);
+    }
+    flags[0] = 0;  // abort
+    flags[1] = 0;  // last-CTA flag of the combine
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kTmaConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0, slot = 0, phase = 0;
+      for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const ItemInfo info = decode_item(p, n_routed, item);
+        const CUtensorMap* mp[2];
+        const CUtensorMap* ms[2];
+        const CUtensorMap* mz[2];
+        int y0;  // first row of the item in the tensor maps
+        if (!info.shared) {
+          mp[0] = &maps.a_packed; ms[0] = &maps.a_scales; mz[0] = &maps.a_biases;
+          mp[1] = &maps.b_packed; ms[1] = &maps.b_scales; mz[1] = &maps.b_biases;
+          y0 = info.expert * (int)p.rows + info.rb * ST::kBoxRows;
+        } else {
+          mp[0] = &maps.sa_packed; ms[0] = &maps.sa_scales; mz[0] = &maps.sa_biases;
+          mp[1] = &maps.sb_packed; ms[1] = &maps.sb_scales; mz[1] = &maps.sb_biases;
+          y0 = info.rb * ST::kBoxRows;
+        }
+        for (int st = 0; st < nstages; ++st, ++it) {
+          wait_bounded(empty + slot, phase ^ 1u, flags, p.error);
+          char* A = smem + slot * ST::kBytes;
+          char* S = A + ST::kABytes;
+          char* Z = S + ST::kSBytes;
+          mbar_arrive_expect_tx(full + slot, ST::kTx);
+#pragma unroll
+          for (int m = 0; m < ST::kMats; ++m) {
+#pragma unroll
+            for (int j = 0; j < ST::kBoxes; ++j)
+              tma_load_2d(A + (m * ST::kBoxes + j) * ST::kBoxBytes, mp[m],
+                          (st * ST::kBoxes + j) * 32, y0, full + slot);
+            const int sbytes = ST::kBoxRows * kTmaGps * ST::kEsz;
+            tma_load_2d(S + m * sbytes, ms[m], st * kTmaGps, y0, full + slot);
+            tma_load_2d(Z + m * sbytes, mz[m], st * kTmaGps, y0, full + slot);
+          }
+          if (++slot == (uint32_t)nst) {
+            slot = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (flags[0]) {
+        // after an abort, let every copy this CTA issued land before it exits
+        const uint32_t issued = it;
+        for (uint32_t j = (issued > (uint32_t)nst ? issued - nst : 0); j < issued; ++j) {
+          for (uint32_t i = 0; i < kSpinLimit; ++i)
+            if (mbar_try_wait(full + (j % nst), (j / nst) & 1u)) break;
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int r8 = lane >> 2;
+  const int c = lane & 3;
+  const int mt = warp & 3;
+  const int kq = warp >> 2;      // K split: groups [kq*kGpw, kq*kGpw + kGpw) of a stage
+  const int ctid = threadIdx.x;  // 0 .. kTmaConsumers-1
+  // (matrix, row within the matrix's boxes) of this lane's two A rows
+  int ma, ra, mb, rbr;
+  if constexpr (EPI == EPI_SWIGLU) {
+    ma = 0;
+    ra = mt * 8 + r8;
+    mb = 1;
+    rbr = mt * 8 + r8;
+  } else {
+    ma = 0;
+    ra = mt * 16 + r8;
+    mb = 0;
+    rbr = ra + 8;
+  }
+  // xsum granularity: K2 reads h's two 32-row partial sums per group
+  constexpr int XP = (EPI == EPI_PARTIAL) ? 2 : 1;
+  // Per-lane byte offsets inside a stage, fixed for the whole kernel: the
+  // swizzled positions of this lane's codes for its 4 groups, and of its
+  // rows' 4 consecutive scales / biases.
+  int offA[kGpw], offB[kGpw];
+#pragma unroll
+  for (int j = 0; j < kGpw; ++j) {
+    const int b = (kq * kGpw + j) * ST::kGroupBytes + c * LW * 4;  // byte in the stage row
+    const int box = b >> 7, bb = b & 127;
+    offA[j] = (ma * ST::kBoxes + box) * ST::kBoxBytes + ra * 128 +
+              ((((bb >> 4) ^ ra) & 7) << 4) + (bb & 15);
+    offB[j] = (mb * ST::kBoxes + box) * ST::kBoxBytes + rbr * 128 +
+              ((((bb >> 4) ^ rbr) & 7) << 4) + (bb & 15);
+  }
+  const int offSa = ST::kABytes + ((ma * ST::kBoxRows + ra) * kTmaGps + kq * kGpw) * ST::kEsz;
+  const int offSb = ST::kABytes + ((mb * ST::kBoxRows + rbr) * kTmaGps + kq * kGpw) * ST::kEsz;
+  uint32_t slot = 0, phase = 0;
+  const char* stg = smem;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const ItemInfo info = decode_item(p, n_routed, item);
+    const bool shared = info.shared;
+    const int col0 = info.col0, ncols = info.ncols;
+    auto col_value = [&](int ci) -> int {
+      return shared ? p.Tk + col0 + ci : __ldg(p.cols + col0 + ci);
+    };
+    auto in_row = [&](int v) -> int64_t {
+      return v < p.Tk ? (int64_t)(v / p.in_div) : (int64_t)(v - p.shared_in_off);
+    };
+    const int ntiles = (ncols + 7) >> 3;
+    const bool single = ncols == 1;  // FMA path instead of an 8-column mma tile
+    // activation pointers at this warp's first group, walked one stage at a time
+    const uint16_t* xr[NT];
+    const float* xp0[NT];
+    const float* xp1[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int cb = min(t * 8 + r8, ncols - 1);
+      const int c0 = min(t * 8 + 2 * c, ncols - 1);
+      const int c1 = min(t * 8 + 2 * c + 1, ncols - 1);
+      xr[t] = p.xperm + in_row(col_value(cb)) * p.in + c * 16 + kq * kGpw * kGroup;
+      xp0[t] = p.xsum + in_row(col_value(c0)) * ngroups * XP + kq * kGpw * XP;
+      xp1[t] = p.xsum + in_row(col_value(c1)) * ngroups * XP + kq * kGpw * XP;
+    }
+    float y[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) y[t][0] = y[t][1] = y[t][2] = y[t][3] = 0.0f;
+
+    for (int st = 0; st < nstages; ++st) {
+      warp_wait(full + slot, phase, flags, p.error);
+      uint32_t wa[kGpw][LW], wb[kGpw][LW];
+      float sa[kGpw], za[kGpw], sb[kGpw], zb[kGpw];
+#pragma unroll
+      for (int j = 0; j < kGpw; ++j) {
+        lds_words<LW>(wa[j], stg + offA[j]);
+        lds_words<LW>(wb[j], stg + offB[j]);
+      }
+      lds_scale2<SD>(sa, stg + offSa);
+      lds_scale2<SD>(za, stg + offSa + ST::kSBytes);
+      lds_scale2<SD>(sb, stg + offSb);
+      lds_scale2<SD>(zb, stg + offSb + ST::kSBytes);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + slot);  // this warp's stage data is in registers
+      if (++slot == (uint32_t)nst) {
+        slot = 0;
+        phase ^= 1u;
+        stg = smem;
+      } else {
+        stg += ST::kBytes;
+      }
+#pragma unroll
+      for (int j = 0; j < kGpw; ++j) {
+        za[j] = fmaf(-kC, sa[j], za[j]);
+        zb[j] = fmaf(-kC, sb[j], zb[j]);
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (t == 0 || t < ntiles) {
+          uint32_t xb[kGpw][8];
+#pragma unroll
+          for (int j = 0; j < kGpw; ++j) {
+            const uint4 v0 = ldg_u128(xr[t] + j * kGroup);
+            const uint4 v1 = ldg_u128(xr[t] + j * kGroup + 8);
+            xb[j][0] = v0.x; xb[j][1] = v0.y; xb[j][2] = v0.z; xb[j][3] = v0.w;
+            xb[j][4] = v1.x; xb[j][5] = v1.y; xb[j][6] = v1.z; xb[j][7] = v1.w;
+          }
+          float X0[kGpw], X1[kGpw];
+          ldg_xsum2<XP>(X0, xp0[t]);
+          float acc[kGpw][4];
+          if (t == 0 && single) {
+            // one column: fp32 FMAs on the lane's own 16 codes x 16
+            // activations per row; the group's bias term is added once per
+            // quad (lane c == 0), lanes are summed at the end of the item
+#pragma unroll
+            for (int j = 0; j < kGpw; ++j) {
+              acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+              group_fma<BITS>(acc[j], wa[j], wb[j], xb[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < kGpw; ++j) {
+              y[0][0] = fmaf(sa[j], acc[j][0] + acc[j][1], y[0][0]);
+              y[0][2] = fmaf(sb[j], acc[j][2] + acc[j][3], y[0][2]);
+              if (c == 0) {
+                y[0][0] = fmaf(za[j], X0[j], y[0][0]);
+                y[0][2] = fmaf(zb[j], X0[j], y[0][2]);
+              }
+            }
+          } else {
+            ldg_xsum2<XP>(X1, xp1[t]);
+#pragma unroll
+            for (int j = 0; j < kGpw; ++j) {
+              acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+              group_mma<BITS>(acc[j], wa[j], wb[j], xb[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < kGpw; ++j) {
+              y[t][0] = fmaf(sa[j], acc[j][0], fmaf(za[j], X0[j], y[t][0]));
+              y[t][1] = fmaf(sa[j], acc[j][1], fmaf(za[j], X1[j], y[t][1]));
+              y[t][2] = fmaf(sb[j], acc[j][2], fmaf(zb[j], X0[j], y[t][2]));
+              y[t][3] = fmaf(sb[j], acc[j][3], fmaf(zb[j], X1[j], y[t][3]));
+            }
+          }
+        }
+        xr[t] += kTmaGps * kGroup;
+        xp0[t] += kTmaGps * XP;
+        xp1[t] += kTmaGps * XP;
+      }
+    }
+
+    if (single) {  // sum the quad's partial dot products (same order on every lane)
+      y[0][0] += __shfl_xor_sync(0xffffffffu, y[0][0], 1);
+      y[0][2] += __shfl_xor_sync(0xffffffffu, y[0][2], 1);
+      y[0][0] += __shfl_xor_sync(0xffffffffu, y[0][0], 2);
+      y[0][2] += __shfl_xor_sync(0xffffffffu, y[0][2], 2);
+    }
+    // ---------------------------------------- K-split reduction (fixed order)
+    if (kq > 0) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < ntiles)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            red[((((kq - 1) * 4 + mt) * NT + t) * 32 + lane) * 4 + i] = y[t][i];
+    }
+    named_bar(1, kTmaConsumers);
+    if (kq == 0) {
+#pragma unroll
+      for (int q = 0; q < kKSplit - 1; ++q)
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+          if (t < ntiles)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) y[t][i] += red[(((q * 4 + mt) * NT + t) * 32 + lane) * 4 + i];
+    }
+
+    // ------------------------------------------------------------ epilogues
+    if constexpr (EPI == EPI_STORE) {
+      if (kq == 0) {
+        const int64_t row_a = (int64_t)info.rb * kTmaRows + mt * 16 + r8;
+        const int64_t row_b = row_a + 8;
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int ci = t * 8 + 2 * c + i;
+            if (t < ntiles && ci < ncols) {
+              const int64_t v = col_value(ci);
+              if (row_a < p.rows) p.out_bf16[v * p.rows + row_a] = f32_to_bf16_bits(y[t][i]);
+              if (row_b < p.rows) p.out_bf16[v * p.rows + row_b] = f32_to_bf16_bits(y[t][2 + i]);
+            }
+          }
+      }
+    } else if constexpr (EPI == EPI_SWIGLU) {
+      if (kq == 0) {
+        const int hrow = info.rb * 32 + mt * 8 + r8;  // intermediate index (< rows)
+        const int pos = perm_pos(hrow, p.h_bits);
+        const float lim = p.swiglu_limit;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int ci = t * 8 + 2 * c + i;
+            float shi = 0.0f, slo = 0.0f;
+            if (t < ntiles && ci < ncols) {
+              const int v = col_value(ci);
+              float g = bf16_round(y[t][i]);
+              float u = bf16_round(y[t][2 + i]);
+              if (lim > 0.0f) {
+                g = fminf(g, lim);
+                u = fminf(fmaxf(u, -lim), lim);
+              }
+              uint16_t hb;
+              if (!shared) {
+                if (!p.weight_after_down) {
+                  float a = g * sigmoid_f32(g);
+                  a = a * u;
+                  a = a * __ldg(p.weights + v);
+                  hb = f32_to_bf16_bits(a);
+                } else {
+                  const float sg = bf16_round(sigmoid_f32(g));
+                  const float a = bf16_round(g * sg);
+                  hb = f32_to_bf16_bits(a * u);
+                }
+                p.out_bf16[(int64_t)v * p.rows + pos] = hb;
+                shi = bf16_bits_to_f32(hb);
+              } else {
+                float a = g * sigmoid_f32(g);
+                a = a * u;
+                hb = f32_to_bf16_bits(a);
+                const uint16_t lb16 = f32_to_bf16_bits(a - bf16_bits_to_f32(hb));
+                p.out_bf16[(int64_t)v * p.rows + pos] = hb;
+                p.out_bf16[(int64_t)(v + p.shared_lo_off) * p.rows + pos] = lb16;
+                shi = bf16_bits_to_f32(hb);
+                slo = bf16_bits_to_f32(lb16);
+              }
+            }
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+              shi += __shfl_xor_sync(0xffffffffu, shi, off);
+              slo += __shfl_xor_sync(0xffffffffu, slo, off);
+            }
+            if (r8 == 0 && t < ntiles && ci < ncols) {
+              hs[(mt * kMaxCols + ci) * 2 + 0] = shi;
+              hs[(mt * kMaxCols + ci) * 2 + 1] = slo;
+            }
+          }
+        }
+      }
+      named_bar(1, kTmaConsumers);
+      if (ctid < ncols) {
+        float shi = 0.0f, slo = 0.0f;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          shi += hs[(m * kMaxCols + ctid) * 2 + 0];
+          slo += hs[(m * kMaxCols + ctid) * 2 + 1];
+        }
+        const int v = col_value(ctid);
+        const int64_t hp = p.rows / 32;  // 32-row partial sums per h row
+        p.hsum[(int64_t)v * hp + info.rb] = shi;
+        if (shared) p.hsum[(int64_t)(v + p.shared_lo_off) * hp + info.rb] = slo;
+      }
+    } else {  // EPI_PARTIAL + fused combine
+      if (kq == 0) {
+        const int64_t row_a = (int64_t)info.rb * kTmaRows + mt * 16 + r8;
+        const int64_t row_b = row_a + 8;
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int ci = t * 8 + 2 * c + i;
+            if (t < ntiles && ci < ncols) {
+              const int64_t v = col_value(ci);
+              const bool routed = v < p.Tk;
+              if (row_a < p.rows) p.part[v * p.rows + row_a] = routed ? bf16_round(y[t][i]) : y[t][i];
+              if (row_b < p.rows)
+                p.part[v * p.rows + row_b] = routed ? bf16_round(y[t][2 + i]) : y[t][2 + i];
+            }
+          }
+      }
+      __threadfence();
+      named_bar(1, kTmaConsumers);
+      if (ctid == 0) {
+        const unsigned target = (unsigned)(n_routed + p.shared_segments);
+        const unsigned old = atomicAdd(p.counters + info.rb, 1u);
+        flags[1] = (old == target - 1u) ? 1 : 0;
+      }
+      named_bar(1, kTmaConsumers);
+      if (flags[1]) {
+        __threadfence();
+        const int64_t r0 = (int64_t)info.rb * kTmaRows;
+        const int T = p.T, k = p.k;
+        for (int idx = ctid; idx < T * kTmaRows; idx += kTmaConsumers) {
+          const int t = idx / kTmaRows;
+          const int64_t row = r0 + (idx - t * kTmaRows);
+          if (row >= p.rows) continue;
+          float tot;
+          if (!p.weight_after_down) {
+            float s = 0.0f;
+            for (int j = 0; j < k; ++j) s += __ldcg(p.part + (int64_t)(t * k + j) * p.rows + row);
+            tot = bf16_round(s);
+          } else {
+            float s = 0.0f;
+            for (int j = 0; j < k; ++j)
+              s += __ldcg(p.part + (int64_t)(t * k + j) * p.rows + row) *
+                   __ldg(p.weights + t * k + j);
+            tot = s;
+          }
+          if (p.has_shared) {
+            const float hi = __ldcg(p.part + (int64_t)(p.Tk + t) * p.rows + row);
+            const float lo = __ldcg(p.part + (int64_t)(p.Tk + T + t) * p.rows + row);
+            tot = tot + (hi + lo);
+          }
+          p.out[(int64_t)t * p.rows + row] = f32_to_bf16_bits(tot);
+        }
+        if (ctid == 0) p.counters[info.rb] = 0u;
+      }
+    }
+    named_bar(1, kTmaConsumers);  // red / hs / flags reused by the next item
+  }
+}
+
+}  // namespace mr

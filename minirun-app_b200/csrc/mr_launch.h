@@ -1,16 +1,25 @@
-// mr_launch.h — host launchers of the templated kernels (one .cu per bit
+// mr_launch.h — host launchers of the templated GEMV kernels (one .cu per bit
 // width, compiled in parallel).
 #pragma once
 
 #include "mr_gemv.cuh"
+#include "mr_gemv_tma.cuh"
 
 namespace mr {
 
-constexpr int kPrefetch = 4;  // groups of codes in flight per lane
+constexpr int kPrefetch = 4;  // groups of codes in flight per lane (register kernel)
 
+// Register-streaming kernel (any in % 64 == 0).
 cudaError_t launch_gemv_b2(const GemvParams& p, int sd, int epi, int nt, int grid, cudaStream_t s);
 cudaError_t launch_gemv_b4(const GemvParams& p, int sd, int epi, int nt, int grid, cudaStream_t s);
 cudaError_t launch_gemv_b8(const GemvParams& p, int sd, int epi, int nt, int grid, cudaStream_t s);
+// TMA-pipelined persistent kernel (in % 512 == 0).
+cudaError_t launch_tma_b2(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, int grid,
+                          cudaStream_t s);
+cudaError_t launch_tma_b4(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, int grid,
+                          cudaStream_t s);
+cudaError_t launch_tma_b8(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, int grid,
+                          cudaStream_t s);
 
 inline cudaError_t launch_gemv(const GemvParams& p, int bits, int sd, int epi, int nt, int grid,
                                cudaStream_t s) {
@@ -22,40 +31,94 @@ inline cudaError_t launch_gemv(const GemvParams& p, int bits, int sd, int epi, i
   }
 }
 
-inline int pick_nt(int max_cols) {
-  const int tiles = (max_cols + 7) / 8;
-  return tiles <= 1 ? 1 : (tiles <= 2 ? 2 : 8);
+inline cudaError_t launch_tma(const GemvParams& p, const TmaMaps& m, int bits, int sd, int epi,
+                              int nt, int grid, cudaStream_t s) {
+  switch (bits) {
+    case 2: return launch_tma_b2(p, m, sd, epi, nt, grid, s);
+    case 4: return launch_tma_b4(p, m, sd, epi, nt, grid, s);
+    case 8: return launch_tma_b8(p, m, sd, epi, nt, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// Columns per segment for a launch whose segments can hold up to `max_cols`
+// columns: one 8-column mma tile when that covers them, else two.
+inline int pick_seg_cols(int64_t max_cols) { return max_cols <= 8 ? 8 : 16; }
+
+// Sets the dynamic shared-memory opt-in of `kernel` once per device; `done`
+// must be owned by that one kernel.
+template <class K>
+inline cudaError_t opt_in_smem(K kernel, int bytes, bool (&done)[64]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
+  return e;
+}
+
+template <int BITS, int SD, int EPI, int NT>
+inline cudaError_t launch_tma_inst(const GemvParams& p, const TmaMaps& m, int grid,
+                                   cudaStream_t s) {
+  static bool done[64] = {};  // one per instantiation
+  const int nst = tma_stages<BITS, SD, EPI, NT>();
+  const int smem = tma_smem_bytes<BITS, SD, EPI, NT>(nst);
+  auto kern = gemv_tma_kernel<BITS, SD, EPI, NT>;
+  cudaError_t e = opt_in_smem(kern, smem, done);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kTmaThreads, smem, s>>>(p, m, nst);
+  return cudaGetLastError();
 }
 
 }  // namespace mr
 
-// Instantiates launch_gemv_b<BITS> in a translation unit.
+// Instantiates launch_gemv_b<BITS> and launch_tma_b<BITS> in a translation unit.
 #define MR_DEFINE_GEMV_LAUNCHER(BITS)                                                          \
   namespace mr {                                                                               \
   template <int SD, int EPI>                                                                   \
   static cudaError_t launch_nt_##BITS(const GemvParams& p, int nt, int grid, cudaStream_t s) { \
-    switch (nt) {                                                                              \
-      case 1: gemv_kernel<BITS, SD, EPI, 1, kPrefetch><<<grid, kGemvThreads, 0, s>>>(p); break; \
-      case 2: gemv_kernel<BITS, SD, EPI, 2, kPrefetch><<<grid, kGemvThreads, 0, s>>>(p); break; \
-      default: gemv_kernel<BITS, SD, EPI, 8, kPrefetch><<<grid, kGemvThreads, 0, s>>>(p); break; \
-    }                                                                                          \
+    if (nt == 1)                                                                               \
+      gemv_kernel<BITS, SD, EPI, 1, kPrefetch><<<grid, kGemvThreads, 0, s>>>(p);               \
+    else                                                                                       \
+      gemv_kernel<BITS, SD, EPI, 2, kPrefetch><<<grid, kGemvThreads, 0, s>>>(p);               \
     return cudaGetLastError();                                                                 \
   }                                                                                            \
+  template <int SD, int EPI>                                                                   \
+  static cudaError_t tma_nt_##BITS(const GemvParams& p, const TmaMaps& m, int nt, int grid,    \
+                                   cudaStream_t s) {                                           \
+    return nt == 1 ? launch_tma_inst<BITS, SD, EPI, 1>(p, m, grid, s)                          \
+                   : launch_tma_inst<BITS, SD, EPI, 2>(p, m, grid, s);                         \
+  }                                                                                            \
   template <int SD>                                                                            \
-  static cudaError_t launch_epi_##BITS(const GemvParams& p, int epi, int nt, int grid,         \
-                                       cudaStream_t s) {                                       \
+  static cudaError_t launch_epi_##BITS(const GemvParams& p, const TmaMaps* m, int epi, int nt, \
+                                       int grid, cudaStream_t s) {                             \
     switch (epi) {                                                                             \
-      case EPI_STORE: return launch_nt_##BITS<SD, EPI_STORE>(p, nt, grid, s);                  \
-      case EPI_SWIGLU: return launch_nt_##BITS<SD, EPI_SWIGLU>(p, nt, grid, s);                \
-      default: return launch_nt_##BITS<SD, EPI_PARTIAL>(p, nt, grid, s);                       \
+      case EPI_STORE:                                                                          \
+        return m ? tma_nt_##BITS<SD, EPI_STORE>(p, *m, nt, grid, s)                            \
+                 : launch_nt_##BITS<SD, EPI_STORE>(p, nt, grid, s);                            \
+      case EPI_SWIGLU:                                                                         \
+        return m ? tma_nt_##BITS<SD, EPI_SWIGLU>(p, *m, nt, grid, s)                           \
+                 : launch_nt_##BITS<SD, EPI_SWIGLU>(p, nt, grid, s);                           \
+      default:                                                                                 \
+        return m ? tma_nt_##BITS<SD, EPI_PARTIAL>(p, *m, nt, grid, s)                          \
+                 : launch_nt_##BITS<SD, EPI_PARTIAL>(p, nt, grid, s);                          \
+    }                                                                                          \
+  }                                                                                            \
+  static cudaError_t dispatch_##BITS(const GemvParams& p, const TmaMaps* m, int sd, int epi,   \
+                                     int nt, int grid, cudaStream_t s) {                       \
+    switch (sd) {                                                                              \
+      case MR_DTYPE_BF16: return launch_epi_##BITS<MR_DTYPE_BF16>(p, m, epi, nt, grid, s);     \
+      case MR_DTYPE_F16: return launch_epi_##BITS<MR_DTYPE_F16>(p, m, epi, nt, grid, s);       \
+      default: return launch_epi_##BITS<MR_DTYPE_F32>(p, m, epi, nt, grid, s);                 \
     }                                                                                          \
   }                                                                                            \
   cudaError_t launch_gemv_b##BITS(const GemvParams& p, int sd, int epi, int nt, int grid,      \
                                   cudaStream_t s) {                                            \
-    switch (sd) {                                                                              \
-      case MR_DTYPE_BF16: return launch_epi_##BITS<MR_DTYPE_BF16>(p, epi, nt, grid, s);        \
-      case MR_DTYPE_F16: return launch_epi_##BITS<MR_DTYPE_F16>(p, epi, nt, grid, s);          \
-      default: return launch_epi_##BITS<MR_DTYPE_F32>(p, epi, nt, grid, s);                    \
-    }                                                                                          \
+    return dispatch_##BITS(p, nullptr, sd, epi, nt, grid, s);                                  \
+  }                                                                                            \
+  cudaError_t launch_tma_b##BITS(const GemvParams& p, const TmaMaps& m, int sd, int epi,       \
+                                 int nt, int grid, cudaStream_t s) {                           \
+    return dispatch_##BITS(p, &m, sd, epi, nt, grid, s);                                       \
   }                                                                                            \
   }

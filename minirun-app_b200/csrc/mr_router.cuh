@@ -84,9 +84,9 @@ struct LogitsParams {
   int64_t H;
   int mtiles;
   int tblocks;
-  int ks;
+  int ks;      // K chunks (warps); CTAs cover 4 consecutive chunks
   int kchunk;  // multiple of 32
-  float* part;
+  float* part; // [ceil(ks/4)][T][E]
   // fused prep of the expert GEMV input (optional, blocks past the logits)
   int logit_blocks;
   PrepParams prep;
@@ -101,15 +101,18 @@ __global__ void __launch_bounds__(128) logits_kernel(const LogitsParams p) {
                nb * blockDim.x);
     return;
   }
+  // CTA = (m-tile, token block, group of 4 K chunks); warp w takes chunk
+  // 4*kq + w and the 4 partial results are summed in warp order in smem.
+  __shared__ float cred[4][8][32][4];
   const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
   const int r8 = lane >> 2, c = lane & 3;
-  const int witem = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int n_items = p.mtiles * p.tblocks * p.ks;
-  if (witem >= n_items) return;
-  const int m = witem % p.mtiles;
-  const int rest = witem / p.mtiles;
+  const int cta = blockIdx.x;
+  const int m = cta % p.mtiles;
+  const int rest = cta / p.mtiles;
   const int tb = rest % p.tblocks;
-  const int kc = rest / p.tblocks;
+  const int kq = rest / p.tblocks;
+  const int kc = kq * 4 + wid;
   const int ea = min(m * 16 + r8, p.E - 1);
   const int eb = min(m * 16 + 8 + r8, p.E - 1);
   const int64_t k0 = (int64_t)kc * p.kchunk;
@@ -127,19 +130,36 @@ __global__ void __launch_bounds__(128) logits_kernel(const LogitsParams p) {
   float acc[8][4];
 #pragma unroll
   for (int t = 0; t < 8; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
-  for (int64_t k = k0; k < k1; k += 32) {
-    const uint4 A = ldg_u128(wa + k);
-    const uint4 Bv = ldg_u128(wb + k);
+  if (kc < p.ks) {
+#pragma unroll 4
+    for (int64_t k = k0; k < k1; k += 32) {
+      const uint4 A = ldg_u128(wa + k);
+      const uint4 Bv = ldg_u128(wb + k);
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      if (t < ntiles) {
-        const uint4 X = ldg_u128(xr[t] + k);
-        mma_bf16_16816(acc[t], A.x, Bv.x, A.y, Bv.y, X.x, X.y);
-        mma_bf16_16816(acc[t], A.z, Bv.z, A.w, Bv.w, X.z, X.w);
+      for (int t = 0; t < 8; ++t) {
+        if (t < ntiles) {
+          const uint4 X = ldg_u128(xr[t] + k);
+          mma_bf16_16816(acc[t], A.x, Bv.x, A.y, Bv.y, X.x, X.y);
+          mma_bf16_16816(acc[t], A.z, Bv.z, A.w, Bv.w, X.z, X.w);
+        }
       }
     }
   }
-  float* out = p.part + (int64_t)kc * p.T * p.E;
+  if (wid > 0) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) cred[wid][t][lane][i] = acc[t][i];
+  }
+  __syncthreads();
+  if (wid != 0) return;
+#pragma unroll
+  for (int w = 1; w < 4; ++w)
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[t][i] += cred[w][t][lane][i];
+  float* out = p.part + (int64_t)kq * p.T * p.E;
 #pragma unroll
   for (int t = 0; t < 8; ++t) {
     if (t < ntiles) {
@@ -168,6 +188,7 @@ struct PlanParams {
   int4* segments;
   int* cols;
   unsigned* error;
+  int seg_cols;  // columns per segment (8 or 16)
 };
 
 template <int NTHREADS>
@@ -191,13 +212,14 @@ __device__ void build_plan_cta(const PlanParams& p) {
   // exclusive scans of column counts and segment counts; each thread owns
   // a contiguous run of experts
   constexpr int kPer = kMaxExperts / NTHREADS;
+  const int sc = p.seg_cols;
   int lc = 0, ls = 0;
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
     const int e = tid * kPer + i;
     if (e < p.E) {
       lc += cnt[e];
-      ls += (cnt[e] + kMaxCols - 1) / kMaxCols;
+      ls += (cnt[e] + sc - 1) / sc;
     }
   }
   const int lane = tid & 31, wid = tid >> 5;
@@ -232,10 +254,10 @@ __device__ void build_plan_cta(const PlanParams& p) {
       colofs[e] = oc;
       segofs[e] = os;
       const int n = cnt[e];
-      for (int s = 0; s * kMaxCols < n; ++s)
-        p.segments[os + s] = make_int4(e, oc + s * kMaxCols, min(kMaxCols, n - s * kMaxCols), 0);
+      for (int s = 0; s * sc < n; ++s)
+        p.segments[os + s] = make_int4(e, oc + s * sc, min(sc, n - s * sc), 0);
       oc += n;
-      os += (n + kMaxCols - 1) / kMaxCols;
+      os += (n + sc - 1) / sc;
     }
   }
   if (tid == 0) *p.n_segments = tot_s;
@@ -254,11 +276,12 @@ __device__ void build_plan_cta(const PlanParams& p) {
 __global__ void __launch_bounds__(256) plan_kernel(const PlanParams p) { build_plan_cta<256>(p); }
 
 // Dense affineMM plan: one expert (0), columns = tokens.
-__global__ void dense_plan_kernel(int T, int* n_segments, int4* segments, int* cols) {
-  const int nseg = (T + kMaxCols - 1) / kMaxCols;
+__global__ void dense_plan_kernel(int T, int seg_cols, int* n_segments, int4* segments,
+                                  int* cols) {
+  const int nseg = (T + seg_cols - 1) / seg_cols;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < T; i += gridDim.x * blockDim.x) {
     cols[i] = i;
-    if (i % kMaxCols == 0) segments[i / kMaxCols] = make_int4(0, i, min(kMaxCols, T - i), 0);
+    if (i % seg_cols == 0) segments[i / seg_cols] = make_int4(0, i, min(seg_cols, T - i), 0);
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) *n_segments = nseg;
 }
@@ -292,22 +315,30 @@ MR_DEVICE bool better(float va, int ia, float vb, int ib) {
 
 // One warp per token. Descending choice score, ties to the lower index
 // (Operators/MoE.swift:128, Operators/DeepSeekV4Routing.swift:215-219).
+template <int EPL>  // experts per lane (E <= 32 * EPL)
 __global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t < p.T) {
-    constexpr int kPer = kMaxExperts / 32;
+    constexpr int kPer = EPL;
     float sc[kPer], ch[kPer];
     unsigned nonfinite = 0;
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int e = lane + 32 * i;
-      float l = 0.0f;
-      if (e < p.E) {
-        for (int s = 0; s < p.ks; ++s) l += p.part[((int64_t)s * p.T + t) * p.E + e];
-        if (p.logits_out) p.logits_out[(int64_t)t * p.E + e] = l;
-      }
-      sc[i] = l;
+    for (int i = 0; i < kPer; ++i) sc[i] = 0.0f;
+    // partial logits summed in partial order; the loads of one partial are
+    // independent of each other
+    for (int s = 0; s < p.ks; ++s) {
+      const float* ps = p.part + ((int64_t)s * p.T + t) * p.E;
+      float v[kPer];
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) v[i] = (lane + 32 * i < p.E) ? __ldcg(ps + lane + 32 * i) : 0.0f;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) sc[i] += v[i];
+    }
+    if (p.logits_out) {
+#pragma unroll
+      for (int i = 0; i < kPer; ++i)
+        if (lane + 32 * i < p.E) p.logits_out[(int64_t)t * p.E + lane + 32 * i] = sc[i];
     }
     if (p.scoring == MR_SCORING_SOFTMAX) {
       float m = -INFINITY;

@@ -67,6 +67,7 @@ SIGNATURES = {
     "mr_last_error": (C.c_char_p, [vp]),
     "mr_ctx_check": (C.c_int, [vp, vp, C.POINTER(C.c_uint32)]),
     "mr_ctx_reserve": (C.c_int, [vp, C.c_int64, C.c_int32, C.c_int32, C.c_int64, C.c_int64]),
+    "mr_ctx_set_kernel_path": (C.c_int, [vp, C.c_int]),
     "mr_affine_validate": (C.c_int, [C.POINTER(mr_affine_desc), C.c_char_p, C.c_size_t]),
     "mr_affine_mm": (C.c_int, [vp, vp, C.c_int64, C.POINTER(mr_affine_desc), vp, vp]),
     "mr_affine_gather_mm": (C.c_int, [vp, vp, C.c_int64, vp, C.c_int32,
@@ -88,7 +89,7 @@ SIGNATURES = {
     "mr_synth_label": (C.c_uint64, [C.c_uint32] * 4),
     "mr_synth_derive": (C.c_uint64, [C.c_uint64, C.c_uint64]),
     "mr_synth_words": (C.c_int, [vp, C.c_uint64, C.c_int64, vp, vp]),
-    "mr_synth_normal_bf16": (C.c_int, [vp, C.c_uint64, C.c_int64, C.c_float, C.c_int, vp, vp]),
+    "mr_synth_normal_bf16": (C.c_int, [vp, C.c_uint64, C.c_int64, C.c_double, C.c_int, vp, vp]),
     "mr_synth_affine_biases": (C.c_int, [vp, vp, C.c_int64, C.c_int32, vp, vp]),
 }
 

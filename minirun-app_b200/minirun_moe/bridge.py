@@ -87,6 +87,12 @@ class Context:
         self.check("mr_ctx_reserve", L.load().mr_ctx_reserve(
             self.handle, max_tokens, top_k, experts, hidden, inter))
 
+    KERNEL_PATHS = {"auto": 0, "register": 1, "tma": 2}
+
+    def set_kernel_path(self, path: str) -> None:
+        self.check("mr_ctx_set_kernel_path", L.load().mr_ctx_set_kernel_path(
+            self.handle, self.KERNEL_PATHS[path]))
+
     KERNEL_CLASSES = ("router_logits", "topk_plan", "gate_up", "down_combine")
 
     def profile(self, enable: bool) -> None:
