@@ -33,6 +33,8 @@ sys.path.insert(0, os.path.join(ROOT, "minirun-app_b200"))
 
 METRIC = ("MoE-layer decode tokens/s; dequant-GEMV HBM GB/s (% of ~8 TB/s) at 1/2/4/8 GPUs")
 FALLBACK_HBM_GBS = 6650.0
+# kernels one layer forward launches: logits(+prep), top-k(+plan), gate/up, down, combine
+LAUNCHES_PER_STEP = 5
 
 
 def parse():
@@ -45,6 +47,10 @@ def parse():
     p.add_argument("--layers", type=int, default=4, help="distinct resident layers cycled")
     p.add_argument("--sweep", default="1,8", help="extra token counts measured (no e2e)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--experts", type=int, default=0,
+                   help="routed experts (0 = config 1's 256); smaller values only for "
+                        "profiling captures that must fit a few GB")
+    p.add_argument("--no-e2e", action="store_true")
     return p.parse_args()
 
 
@@ -140,6 +146,9 @@ def run_ours(args, world, rank, local):
         dist.init_process_group("nccl", device_id=dev,
                                 timeout=__import__("datetime").timedelta(seconds=300))
     spec = S.CONFIGS[1]
+    if args.experts:
+        import dataclasses
+        spec = dataclasses.replace(spec, experts=args.experts)
     T = args.tokens
     NL = max(1, args.layers)
     layers = [S.synth_layer(spec, layer=l, device=local) for l in range(NL)]
@@ -217,7 +226,7 @@ def run_ours(args, world, rank, local):
     gu_bytes = sum(gate_up_bytes(T, u) for u in us) / len(us)
     achieved = gu_bytes / (gu_avg_ms / 1e3) / 1e9
     kern = {k: {"ms_per_launch": v[0] / max(v[1], 1), "launches": v[1]} for k, v in prof.items()}
-    traffic = read_traffic()
+    traffic = read_traffic(gu_bytes)
 
     sweep = {}
     for tok in token_counts[1:]:
@@ -230,29 +239,7 @@ def run_ours(args, world, rank, local):
                            "layer_frac_of_hbm": b2 / (m2 / K / 1e3) / 1e9 / hbm,
                            "distinct_experts_avg": sum(u2) / len(u2)}
 
-    # e2e: pinned host x in, host out, through the host-buffer C-ABI call
-    xh = [x.cpu().pin_memory() for x in xs[T]]
-    oh = torch.empty((T, spec.hidden), dtype=torch.bfloat16).pin_memory()
-    for i in range(W):
-        lay, b = schedule(i)
-        lay.forward_host(xh[b], oh, device=local)
-    torch.cuda.synchronize()
-    barrier()
-    st = torch.cuda.current_stream()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for i in range(K):
-        lay, b = schedule(i)
-        lay.forward_host(xh[b], oh, device=local)
-    e1.record(st)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e = e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local)
     ctx.sync_check()
 
     cpu = None
@@ -274,7 +261,8 @@ def run_ours(args, world, rank, local):
                  "accumulate",
         "data": "synthetic (SplitMix64-seeded, BASELINE config 1 distributions)",
         "config": {
-            "workload": f"config1 decode T={T}: H7168, 256+1 experts, top-8, I2048, 4-bit g64",
+            "workload": f"config1 decode T={T}: H7168, {spec.experts}+1 experts, top-8, I2048, "
+                        "4-bit g64",
             "tokens": T,
             "global_batch": world * T,
             "layers_cycled": NL,
@@ -299,13 +287,8 @@ def run_ours(args, world, rank, local):
             "algorithmic_bytes_per_launch": gu_bytes,
             "traffic": traffic,
         },
-        "e2e": {
-            "value": world * T * K / (e2e_ms / 1e3),
-            "unit": "tokens/s",
-            "h2d_bytes_per_step": T * spec.hidden * 2,
-            "d2h_bytes_per_step": T * spec.hidden * 2,
-        },
-        "gpu_launches": K * 4,
+        "e2e": e2e,
+        "gpu_launches": K * LAUNCHES_PER_STEP,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
@@ -316,16 +299,60 @@ def run_ours(args, world, rank, local):
         dist.destroy_process_group()
 
 
-def read_traffic():
-    """DRAM bytes per gate/up launch from the committed ncu summary, if any."""
+def e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local):
+    """Same metric through the host-buffer C-ABI call: pinned host x in, host out,
+    both copies inside the timed region."""
+    if args.no_e2e:
+        return None
+    xh = [x.cpu().pin_memory() for x in xs[T]]
+    oh = torch.empty((T, spec.hidden), dtype=torch.bfloat16).pin_memory()
+    for i in range(W):
+        lay, b = schedule(i)
+        lay.forward_host(xh[b], oh, device=local)
+    torch.cuda.synchronize()
+    barrier()
+    st = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(K):
+        lay, b = schedule(i)
+        lay.forward_host(xh[b], oh, device=local)
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    return {
+        "value": world * T * K / (e2e_ms / 1e3),
+        "unit": "tokens/s",
+        "h2d_bytes_per_step": T * spec.hidden * 2,
+        "d2h_bytes_per_step": T * spec.hidden * 2,
+    }
+
+
+def read_traffic(algorithmic_bytes):
+    """DRAM bytes per gate/up launch, scaled from the committed ncu summary.
+
+    The summary records one captured launch (a small case that fits the capture
+    rules): its dram read+write bytes and its algorithmic bytes. Traffic grows
+    with the weight bytes a launch streams, so the bench launch's traffic is the
+    captured ratio times its own algorithmic bytes."""
     path = os.path.join(ROOT, "profiles", "gemv_gate_up_config1.md")
+    vals = {}
     try:
         for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].split()[0])
-    except OSError:
-        pass
-    return None
+            for key in ("traffic_bytes_per_launch", "algorithmic_bytes_per_launch"):
+                if line.startswith(key + ":"):
+                    vals[key] = float(line.split(":", 1)[1].split()[0])
+    except (OSError, ValueError):
+        return None
+    if len(vals) != 2 or vals["algorithmic_bytes_per_launch"] <= 0:
+        return None
+    return vals["traffic_bytes_per_launch"] / vals["algorithmic_bytes_per_launch"] * algorithmic_bytes
 
 
 # ------------------------------------------------------------- CPU baseline

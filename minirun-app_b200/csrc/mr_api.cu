@@ -154,6 +154,37 @@ static ExpertSource stack_source(const mr_affine_desc& d, int proj) {
 
 static cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Slot-ordered sum of the w2 partials (+ the shared expert's hi/lo parts):
+// out[t, r] = bf16(bf16(sum_j part[t*k + j, r]) + (hi + lo))   (weight before w2)
+// out[t, r] = bf16(sum_j part[t*k + j, r] * w[t, j] + (hi + lo)) (weight after w2)
+// (Loading/DeepSeekV4ExpertBackend.swift:341-342, Model/QwenMoEModel.swift:350-351,
+// Model/DeepSeekV4HashFFN.swift:106). Deterministic: fixed order per element.
+__global__ void combine_kernel(const float* __restrict__ part, const float* __restrict__ weights,
+                               int T, int k, int64_t H, int weight_after_down, int has_shared,
+                               uint16_t* __restrict__ out) {
+  const int64_t n = (int64_t)T * H;
+  const int Tk = T * k;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / H);
+    const int64_t row = i - (int64_t)t * H;
+    float s = 0.0f;
+    if (!weight_after_down) {
+      for (int j = 0; j < k; ++j) s += __ldg(part + (int64_t)(t * k + j) * H + row);
+      s = bf16_round(s);
+    } else {
+      for (int j = 0; j < k; ++j)
+        s += __ldg(part + (int64_t)(t * k + j) * H + row) * __ldg(weights + t * k + j);
+    }
+    if (has_shared) {
+      const float hi = __ldg(part + (int64_t)(Tk + t) * H + row);
+      const float lo = __ldg(part + (int64_t)(Tk + T + t) * H + row);
+      s = s + (hi + lo);
+    }
+    out[i] = f32_to_bf16_bits(s);
+  }
+}
+
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Whether the TMA-pipelined GEMV can stream this projection: whole 8-group
@@ -969,8 +1000,14 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   ProfScope ps(ctx, MR_KERNEL_DOWN_COMBINE, s);
   const MapSpec maps[4] = {{&L->down, E}, {nullptr, 0},
                            {has_shared ? &L->shared_down : nullptr, 1}, {nullptr, 0}};
-  return cuda_check(ctx, run_gemv(ctx, d, max_seg, tma2, maps, bits, sd, EPI_PARTIAL, nt, s),
-                    "gemv(down)");
+  if ((st = cuda_check(ctx, run_gemv(ctx, d, max_seg, tma2, maps, bits, sd, EPI_PARTIAL, nt, s),
+                       "gemv(down)")))
+    return st;
+  const int64_t n_out = T * H;
+  const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 4 * ctx->sm_count));
+  combine_kernel<<<cgrid, 256, 0, s>>>(part2, wts, (int)T, k, H, d.weight_after_down,
+                                        d.has_shared, out);
+  return cuda_check(ctx, cudaGetLastError(), "combine_kernel");
 }
 
 mr_status mr_moe_layer_forward_host(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x_host,

@@ -149,6 +149,24 @@ MR_DEVICE void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* ba
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Shared-memory loads by 32-bit shared address.
+MR_DEVICE uint32_t lds_b32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+MR_DEVICE uint2 lds_b64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+MR_DEVICE uint4 lds_b128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a));
+  return v;
+}
 // Named barrier among `count` threads (id 0 is __syncthreads).
 MR_DEVICE void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -227,7 +227,6 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
   const int parts = p.xsum_parts;
 
   __shared__ float red[8][kMaxCols][2];
-  __shared__ int s_last;
 
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
     const int seg = item / p.rb_count;
@@ -447,7 +446,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
         if (shared) p.hsum[(int64_t)(v + p.shared_lo_off) * hp + rb * 2 + part] = slo;
       }
       __syncthreads();
-    } else {  // EPI_PARTIAL + fused combine
+    } else {  // EPI_PARTIAL: per-slot w2 outputs
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
 #pragma unroll
@@ -463,42 +462,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
           }
         }
       }
-      __threadfence();
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        const unsigned target = (unsigned)(n_routed + p.shared_segments);
-        const unsigned old = atomicAdd(p.counters + rb, 1u);
-        s_last = (old == target - 1u) ? 1 : 0;
-      }
-      __syncthreads();
-      if (s_last) {
-        __threadfence();
-        const int64_t r0 = (int64_t)rb * kRowsPlain;
-        const int T = p.T, k = p.k;
-        for (int idx = threadIdx.x; idx < T * kRowsPlain; idx += blockDim.x) {
-          const int t = idx / kRowsPlain;
-          const int64_t row = r0 + (idx - t * kRowsPlain);
-          if (row >= p.rows) continue;
-          float tot;
-          if (!p.weight_after_down) {
-            float s = 0.0f;
-            for (int j = 0; j < k; ++j) s += __ldcg(p.part + (int64_t)(t * k + j) * p.rows + row);
-            tot = bf16_round(s);
-          } else {
-            float s = 0.0f;
-            for (int j = 0; j < k; ++j)
-              s += __ldcg(p.part + (int64_t)(t * k + j) * p.rows + row) * __ldg(p.weights + t * k + j);
-            tot = s;
-          }
-          if (p.has_shared) {
-            const float hi = __ldcg(p.part + (int64_t)(p.Tk + t) * p.rows + row);
-            const float lo = __ldcg(p.part + (int64_t)(p.Tk + T + t) * p.rows + row);
-            tot = tot + (hi + lo);
-          }
-          p.out[(int64_t)t * p.rows + row] = f32_to_bf16_bits(tot);
-        }
-        if (threadIdx.x == 0) p.counters[rb] = 0u;
-      }
+      // (the slot-ordered sum runs in combine_kernel)
     }
   }
 }

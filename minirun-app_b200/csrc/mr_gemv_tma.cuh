@@ -15,7 +15,8 @@
 // same register dequant + mma.m16n8k16 + exact per-group fold as the
 // register-streaming kernel. At the end of an item the four K-quarters are
 // summed in a fixed order through shared memory (deterministic), then the
-// epilogue (bf16 store / SwiGLU / partial + fused combine) runs.
+// epilogue (bf16 store / SwiGLU / per-slot partial) runs; combine_kernel
+// then sums the slots in order.
 // Requires in % 512 == 0 (whole stages) and expert stacks addressable by one
 // 2-D tensor map per projection (stack base + expert * rows).
 #pragma once
@@ -308,10 +309,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   }
   // xsum granularity: K2 reads h's two 32-row partial sums per group
   constexpr int XP = (EPI == EPI_PARTIAL) ? 2 : 1;
-  // Per-lane byte offsets inside a stage, fixed for the whole kernel: the
-  // swizzled positions of this lane's codes for its 4 groups, and of its
-  // rows' 4 consecutive scales / biases.
-  int offA[kGpw], offB[kGpw];
+  // Per-lane shared-memory offsets inside a stage, fixed for the whole
+  // kernel: the swizzled positions of this lane's codes for its groups, and
+  // of its rows' consecutive scales (biases are kSBytes further).
+  uint32_t offA[kGpw], offB[kGpw];
 #pragma unroll
   for (int j = 0; j < kGpw; ++j) {
     const int b = (kq * kGpw + j) * ST::kGroupBytes + c * LW * 4;  // byte in the stage row
@@ -321,20 +322,129 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     offB[j] = (mb * ST::kBoxes + box) * ST::kBoxBytes + rbr * 128 +
               ((((bb >> 4) ^ rbr) & 7) << 4) + (bb & 15);
   }
-  const int offSa = ST::kABytes + ((ma * ST::kBoxRows + ra) * kTmaGps + kq * kGpw) * ST::kEsz;
-  const int offSb = ST::kABytes + ((mb * ST::kBoxRows + rbr) * kTmaGps + kq * kGpw) * ST::kEsz;
-  uint32_t slot = 0, phase = 0;
-  const char* stg = smem;
+  const uint32_t offSa = ST::kABytes + ((ma * ST::kBoxRows + ra) * kTmaGps + kq * kGpw) * ST::kEsz;
+  const uint32_t offSb = ST::kABytes + ((mb * ST::kBoxRows + rbr) * kTmaGps + kq * kGpw) * ST::kEsz;
+  const uint32_t sbase = smem_u32(smem);
+  uint32_t slot = 0, phase = 0, stg = sbase;
+
+  // One stage's codes and scales for this lane -> registers; then release
+  // the slot to the producer and advance the ring.
+  auto take_stage = [&](uint32_t (&wa)[kGpw][LW], uint32_t (&wb)[kGpw][LW], float (&sa)[kGpw],
+                        float (&za)[kGpw], float (&sb)[kGpw], float (&zb)[kGpw]) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+      if (mbar_try_wait(full + slot, phase)) break;
+      if ((i & 1023u) == 1023u && flags[0]) break;
+      if (i + 1 == kSpinLimit) {
+        flags[0] = 1;
+        atomicOr(p.error, MR_DEVERR_TIMEOUT);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kGpw; ++j) {
+      if constexpr (LW == 1) {
+        wa[j][0] = lds_b32(stg + offA[j]);
+        wb[j][0] = lds_b32(stg + offB[j]);
+      } else if constexpr (LW == 2) {
+        const uint2 u = lds_b64(stg + offA[j]);
+        const uint2 v = lds_b64(stg + offB[j]);
+        wa[j][0] = u.x; wa[j][1] = u.y;
+        wb[j][0] = v.x; wb[j][1] = v.y;
+      } else {
+        const uint4 u = lds_b128(stg + offA[j]);
+        const uint4 v = lds_b128(stg + offB[j]);
+        wa[j][0] = u.x; wa[j][1] = u.y; wa[j][2] = u.z; wa[j][3] = u.w;
+        wb[j][0] = v.x; wb[j][1] = v.y; wb[j][2] = v.z; wb[j][3] = v.w;
+      }
+    }
+    if constexpr (SD == MR_DTYPE_F32) {
+      const uint2 s0 = lds_b64(stg + offSa), z0 = lds_b64(stg + offSa + ST::kSBytes);
+      const uint2 s1 = lds_b64(stg + offSb), z1 = lds_b64(stg + offSb + ST::kSBytes);
+      sa[0] = __uint_as_float(s0.x); sa[1] = __uint_as_float(s0.y);
+      za[0] = __uint_as_float(z0.x); za[1] = __uint_as_float(z0.y);
+      sb[0] = __uint_as_float(s1.x); sb[1] = __uint_as_float(s1.y);
+      zb[0] = __uint_as_float(z1.x); zb[1] = __uint_as_float(z1.y);
+    } else {
+      const uint32_t s0 = lds_b32(stg + offSa), z0 = lds_b32(stg + offSa + ST::kSBytes);
+      const uint32_t s1 = lds_b32(stg + offSb), z1 = lds_b32(stg + offSb + ST::kSBytes);
+      if constexpr (SD == MR_DTYPE_BF16) {
+        sa[0] = __uint_as_float(s0 << 16); sa[1] = __uint_as_float(s0 & 0xffff0000u);
+        za[0] = __uint_as_float(z0 << 16); za[1] = __uint_as_float(z0 & 0xffff0000u);
+        sb[0] = __uint_as_float(s1 << 16); sb[1] = __uint_as_float(s1 & 0xffff0000u);
+        zb[0] = __uint_as_float(z1 << 16); zb[1] = __uint_as_float(z1 & 0xffff0000u);
+      } else {
+        sa[0] = __half2float(__ushort_as_half((unsigned short)(s0 & 0xffffu)));
+        sa[1] = __half2float(__ushort_as_half((unsigned short)(s0 >> 16)));
+        za[0] = __half2float(__ushort_as_half((unsigned short)(z0 & 0xffffu)));
+        za[1] = __half2float(__ushort_as_half((unsigned short)(z0 >> 16)));
+        sb[0] = __half2float(__ushort_as_half((unsigned short)(s1 & 0xffffu)));
+        sb[1] = __half2float(__ushort_as_half((unsigned short)(s1 >> 16)));
+        zb[0] = __half2float(__ushort_as_half((unsigned short)(z1 & 0xffffu)));
+        zb[1] = __half2float(__ushort_as_half((unsigned short)(z1 >> 16)));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + slot);  // this warp's stage data is in registers
+    if (++slot == (uint32_t)nst) {
+      slot = 0;
+      phase ^= 1u;
+      stg = sbase;
+    } else {
+      stg += ST::kBytes;
+    }
+#pragma unroll
+    for (int j = 0; j < kGpw; ++j) {
+      za[j] = fmaf(-kC, sa[j], za[j]);
+      zb[j] = fmaf(-kC, sb[j], zb[j]);
+    }
+  };
+
+  // Item metadata for this lane: the item, the column values its B loads
+  // (cb), its accumulator columns (c0, c1) read, and — for the SwiGLU
+  // epilogue — their routing weights. Fetched one item ahead so that the
+  // dependent global loads (segment -> column ids -> weights) overlap the
+  // previous item's stages.
+  struct Meta {
+    ItemInfo info;
+    int vb[NT], v0[NT], v1[NT];
+    float w0[NT], w1[NT];
+  };
+  auto fetch_cols = [&](Meta& m) {
+    const int nc = m.info.ncols;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int cb = min(t * 8 + r8, nc - 1);
+      const int c0 = min(t * 8 + 2 * c, nc - 1);
+      const int c1 = min(t * 8 + 2 * c + 1, nc - 1);
+      if (m.info.shared) {
+        m.vb[t] = p.Tk + m.info.col0 + cb;
+        m.v0[t] = p.Tk + m.info.col0 + c0;
+        m.v1[t] = p.Tk + m.info.col0 + c1;
+      } else {
+        m.vb[t] = __ldg(p.cols + m.info.col0 + cb);
+        m.v0[t] = __ldg(p.cols + m.info.col0 + c0);
+        m.v1[t] = __ldg(p.cols + m.info.col0 + c1);
+      }
+      if constexpr (EPI == EPI_SWIGLU) {
+        m.w0[t] = m.info.shared ? 1.0f : __ldg(p.weights + m.v0[t]);
+        m.w1[t] = m.info.shared ? 1.0f : __ldg(p.weights + m.v1[t]);
+      }
+    }
+  };
+  auto in_row = [&](int v) -> int64_t {
+    return v < p.Tk ? (int64_t)(v / p.in_div) : (int64_t)(v - p.shared_in_off);
+  };
+
+  Meta cur, nxt;
+  if ((int)blockIdx.x < n_items) {
+    cur.info = decode_item(p, n_routed, blockIdx.x);
+    fetch_cols(cur);
+  }
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-    const ItemInfo info = decode_item(p, n_routed, item);
+    const bool has_next = item + (int)gridDim.x < n_items;
+    if (has_next) nxt.info = decode_item(p, n_routed, item + gridDim.x);  // in flight
+    const ItemInfo& info = cur.info;
     const bool shared = info.shared;
-    const int col0 = info.col0, ncols = info.ncols;
-    auto col_value = [&](int ci) -> int {
-      return shared ? p.Tk + col0 + ci : __ldg(p.cols + col0 + ci);
-    };
-    auto in_row = [&](int v) -> int64_t {
-      return v < p.Tk ? (int64_t)(v / p.in_div) : (int64_t)(v - p.shared_in_off);
-    };
+    const int ncols = info.ncols;
     const int ntiles = (ncols + 7) >> 3;
     const bool single = ncols == 1;  // FMA path instead of an 8-column mma tile
     // activation pointers at this warp's first group, walked one stage at a time
@@ -343,78 +453,78 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const float* xp1[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
-      const int cb = min(t * 8 + r8, ncols - 1);
-      const int c0 = min(t * 8 + 2 * c, ncols - 1);
-      const int c1 = min(t * 8 + 2 * c + 1, ncols - 1);
-      xr[t] = p.xperm + in_row(col_value(cb)) * p.in + c * 16 + kq * kGpw * kGroup;
-      xp0[t] = p.xsum + in_row(col_value(c0)) * ngroups * XP + kq * kGpw * XP;
-      xp1[t] = p.xsum + in_row(col_value(c1)) * ngroups * XP + kq * kGpw * XP;
+      xr[t] = p.xperm + in_row(cur.vb[t]) * p.in + c * 16 + kq * kGpw * kGroup;
+      xp0[t] = p.xsum + in_row(cur.v0[t]) * ngroups * XP + kq * kGpw * XP;
+      xp1[t] = p.xsum + in_row(cur.v1[t]) * ngroups * XP + kq * kGpw * XP;
     }
     float y[NT][4];
 #pragma unroll
     for (int t = 0; t < NT; ++t) y[t][0] = y[t][1] = y[t][2] = y[t][3] = 0.0f;
 
-    for (int st = 0; st < nstages; ++st) {
-      warp_wait(full + slot, phase, flags, p.error);
-      uint32_t wa[kGpw][LW], wb[kGpw][LW];
-      float sa[kGpw], za[kGpw], sb[kGpw], zb[kGpw];
+    if (single) {
+      // One column: fp32 FMAs of this lane's 16 codes per row and group
+      // against the matching 16 activations; the group's bias term is added
+      // once per quad (lane c == 0); the quad is summed after the K loop.
+      const bool add_bias = c == 0;
+      const uint16_t* xq = xr[0];
+      const float* xs = xp0[0];
+      for (int st = 0; st < nstages; ++st) {
+        if (st == 1 && has_next) fetch_cols(nxt);
+        uint32_t wa[kGpw][LW], wb[kGpw][LW];
+        float sa[kGpw], za[kGpw], sb[kGpw], zb[kGpw];
+        take_stage(wa, wb, sa, za, sb, zb);
+        uint32_t xb[kGpw][8];
 #pragma unroll
-      for (int j = 0; j < kGpw; ++j) {
-        lds_words<LW>(wa[j], stg + offA[j]);
-        lds_words<LW>(wb[j], stg + offB[j]);
+        for (int j = 0; j < kGpw; ++j) {
+          const uint4 v0 = ldg_u128(xq + j * kGroup);
+          const uint4 v1 = ldg_u128(xq + j * kGroup + 8);
+          xb[j][0] = v0.x; xb[j][1] = v0.y; xb[j][2] = v0.z; xb[j][3] = v0.w;
+          xb[j][4] = v1.x; xb[j][5] = v1.y; xb[j][6] = v1.z; xb[j][7] = v1.w;
+        }
+        float X[kGpw];
+        ldg_xsum2<XP>(X, xs);
+        xq += kTmaGps * kGroup;
+        xs += kTmaGps * XP;
+        float acc[kGpw][4];
+#pragma unroll
+        for (int j = 0; j < kGpw; ++j) {
+          acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+          group_fma<BITS>(acc[j], wa[j], wb[j], xb[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < kGpw; ++j) {
+          y[0][0] = fmaf(sa[j], acc[j][0] + acc[j][1], y[0][0]);
+          y[0][2] = fmaf(sb[j], acc[j][2] + acc[j][3], y[0][2]);
+          y[0][0] = fmaf(add_bias ? za[j] : 0.0f, X[j], y[0][0]);
+          y[0][2] = fmaf(add_bias ? zb[j] : 0.0f, X[j], y[0][2]);
+        }
       }
-      lds_scale2<SD>(sa, stg + offSa);
-      lds_scale2<SD>(za, stg + offSa + ST::kSBytes);
-      lds_scale2<SD>(sb, stg + offSb);
-      lds_scale2<SD>(zb, stg + offSb + ST::kSBytes);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty + slot);  // this warp's stage data is in registers
-      if (++slot == (uint32_t)nst) {
-        slot = 0;
-        phase ^= 1u;
-        stg = smem;
-      } else {
-        stg += ST::kBytes;
-      }
+      // sum the quad's partial dot products (same order on every lane)
+      y[0][0] += __shfl_xor_sync(0xffffffffu, y[0][0], 1);
+      y[0][2] += __shfl_xor_sync(0xffffffffu, y[0][2], 1);
+      y[0][0] += __shfl_xor_sync(0xffffffffu, y[0][0], 2);
+      y[0][2] += __shfl_xor_sync(0xffffffffu, y[0][2], 2);
+    } else {
+      for (int st = 0; st < nstages; ++st) {
+        if (st == 1 && has_next) fetch_cols(nxt);
+        uint32_t wa[kGpw][LW], wb[kGpw][LW];
+        float sa[kGpw], za[kGpw], sb[kGpw], zb[kGpw];
+        take_stage(wa, wb, sa, za, sb, zb);
 #pragma unroll
-      for (int j = 0; j < kGpw; ++j) {
-        za[j] = fmaf(-kC, sa[j], za[j]);
-        zb[j] = fmaf(-kC, sb[j], zb[j]);
-      }
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (t == 0 || t < ntiles) {
-          uint32_t xb[kGpw][8];
-#pragma unroll
-          for (int j = 0; j < kGpw; ++j) {
-            const uint4 v0 = ldg_u128(xr[t] + j * kGroup);
-            const uint4 v1 = ldg_u128(xr[t] + j * kGroup + 8);
-            xb[j][0] = v0.x; xb[j][1] = v0.y; xb[j][2] = v0.z; xb[j][3] = v0.w;
-            xb[j][4] = v1.x; xb[j][5] = v1.y; xb[j][6] = v1.z; xb[j][7] = v1.w;
-          }
-          float X0[kGpw], X1[kGpw];
-          ldg_xsum2<XP>(X0, xp0[t]);
-          float acc[kGpw][4];
-          if (t == 0 && single) {
-            // one column: fp32 FMAs on the lane's own 16 codes x 16
-            // activations per row; the group's bias term is added once per
-            // quad (lane c == 0), lanes are summed at the end of the item
+        for (int t = 0; t < NT; ++t) {
+          if (t == 0 || t < ntiles) {
+            uint32_t xb[kGpw][8];
 #pragma unroll
             for (int j = 0; j < kGpw; ++j) {
-              acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-              group_fma<BITS>(acc[j], wa[j], wb[j], xb[j]);
+              const uint4 v0 = ldg_u128(xr[t] + j * kGroup);
+              const uint4 v1 = ldg_u128(xr[t] + j * kGroup + 8);
+              xb[j][0] = v0.x; xb[j][1] = v0.y; xb[j][2] = v0.z; xb[j][3] = v0.w;
+              xb[j][4] = v1.x; xb[j][5] = v1.y; xb[j][6] = v1.z; xb[j][7] = v1.w;
             }
-#pragma unroll
-            for (int j = 0; j < kGpw; ++j) {
-              y[0][0] = fmaf(sa[j], acc[j][0] + acc[j][1], y[0][0]);
-              y[0][2] = fmaf(sb[j], acc[j][2] + acc[j][3], y[0][2]);
-              if (c == 0) {
-                y[0][0] = fmaf(za[j], X0[j], y[0][0]);
-                y[0][2] = fmaf(zb[j], X0[j], y[0][2]);
-              }
-            }
-          } else {
+            float X0[kGpw], X1[kGpw];
+            ldg_xsum2<XP>(X0, xp0[t]);
             ldg_xsum2<XP>(X1, xp1[t]);
+            float acc[kGpw][4];
 #pragma unroll
             for (int j = 0; j < kGpw; ++j) {
               acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
@@ -428,19 +538,14 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
               y[t][3] = fmaf(sb[j], acc[j][3], fmaf(zb[j], X1[j], y[t][3]));
             }
           }
+          xr[t] += kTmaGps * kGroup;
+          xp0[t] += kTmaGps * XP;
+          xp1[t] += kTmaGps * XP;
         }
-        xr[t] += kTmaGps * kGroup;
-        xp0[t] += kTmaGps * XP;
-        xp1[t] += kTmaGps * XP;
       }
     }
+    if (nstages <= 1 && has_next) fetch_cols(nxt);
 
-    if (single) {  // sum the quad's partial dot products (same order on every lane)
-      y[0][0] += __shfl_xor_sync(0xffffffffu, y[0][0], 1);
-      y[0][2] += __shfl_xor_sync(0xffffffffu, y[0][2], 1);
-      y[0][0] += __shfl_xor_sync(0xffffffffu, y[0][0], 2);
-      y[0][2] += __shfl_xor_sync(0xffffffffu, y[0][2], 2);
-    }
     // ---------------------------------------- K-split reduction (fixed order)
     if (kq > 0) {
 #pragma unroll
@@ -462,7 +567,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
 
     // ------------------------------------------------------------ epilogues
-    if constexpr (EPI == EPI_STORE) {
+    // accumulator columns of this lane: ci = t*8 + 2c + i, value cur.v{i}[t]
+    if constexpr (EPI == EPI_STORE || EPI == EPI_PARTIAL) {
       if (kq == 0) {
         const int64_t row_a = (int64_t)info.rb * kTmaRows + mt * 16 + r8;
         const int64_t row_b = row_a + 8;
@@ -472,13 +578,23 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           for (int i = 0; i < 2; ++i) {
             const int ci = t * 8 + 2 * c + i;
             if (t < ntiles && ci < ncols) {
-              const int64_t v = col_value(ci);
-              if (row_a < p.rows) p.out_bf16[v * p.rows + row_a] = f32_to_bf16_bits(y[t][i]);
-              if (row_b < p.rows) p.out_bf16[v * p.rows + row_b] = f32_to_bf16_bits(y[t][2 + i]);
+              const int64_t v = i ? cur.v1[t] : cur.v0[t];
+              if constexpr (EPI == EPI_STORE) {
+                if (row_a < p.rows) p.out_bf16[v * p.rows + row_a] = f32_to_bf16_bits(y[t][i]);
+                if (row_b < p.rows) p.out_bf16[v * p.rows + row_b] = f32_to_bf16_bits(y[t][2 + i]);
+              } else {
+                // routed slots are the w2 gather's bf16 output; the shared
+                // expert's hi/lo columns stay fp32
+                const bool routed = v < p.Tk;
+                if (row_a < p.rows)
+                  p.part[v * p.rows + row_a] = routed ? bf16_round(y[t][i]) : y[t][i];
+                if (row_b < p.rows)
+                  p.part[v * p.rows + row_b] = routed ? bf16_round(y[t][2 + i]) : y[t][2 + i];
+              }
             }
           }
       }
-    } else if constexpr (EPI == EPI_SWIGLU) {
+    } else {  // EPI_SWIGLU
       if (kq == 0) {
         const int hrow = info.rb * 32 + mt * 8 + r8;  // intermediate index (< rows)
         const int pos = perm_pos(hrow, p.h_bits);
@@ -490,7 +606,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             const int ci = t * 8 + 2 * c + i;
             float shi = 0.0f, slo = 0.0f;
             if (t < ntiles && ci < ncols) {
-              const int v = col_value(ci);
+              const int v = i ? cur.v1[t] : cur.v0[t];
               float g = bf16_round(y[t][i]);
               float u = bf16_round(y[t][2 + i]);
               if (lim > 0.0f) {
@@ -502,7 +618,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
                 if (!p.weight_after_down) {
                   float a = g * sigmoid_f32(g);
                   a = a * u;
-                  a = a * __ldg(p.weights + v);
+                  a = a * (i ? cur.w1[t] : cur.w0[t]);
                   hb = f32_to_bf16_bits(a);
                 } else {
                   const float sg = bf16_round(sigmoid_f32(g));
@@ -534,6 +650,18 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           }
         }
       }
+      // thread ci < ncols of warp 0 sums column ci over the 4 m-tiles; the
+      // column's value sits in lane (ci & 7) >> 1 of any warp (v0 or v1)
+      int vci = 0;
+      if (warp == 0) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const int src = (lane & 7) >> 1;
+          const int a = __shfl_sync(0xffffffffu, cur.v0[t], src);
+          const int b = __shfl_sync(0xffffffffu, cur.v1[t], src);
+          if ((lane >> 3) == t) vci = (lane & 1) ? b : a;
+        }
+      }
       named_bar(1, kTmaConsumers);
       if (ctid < ncols) {
         float shi = 0.0f, slo = 0.0f;
@@ -542,68 +670,13 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           shi += hs[(m * kMaxCols + ctid) * 2 + 0];
           slo += hs[(m * kMaxCols + ctid) * 2 + 1];
         }
-        const int v = col_value(ctid);
         const int64_t hp = p.rows / 32;  // 32-row partial sums per h row
-        p.hsum[(int64_t)v * hp + info.rb] = shi;
-        if (shared) p.hsum[(int64_t)(v + p.shared_lo_off) * hp + info.rb] = slo;
-      }
-    } else {  // EPI_PARTIAL + fused combine
-      if (kq == 0) {
-        const int64_t row_a = (int64_t)info.rb * kTmaRows + mt * 16 + r8;
-        const int64_t row_b = row_a + 8;
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const int ci = t * 8 + 2 * c + i;
-            if (t < ntiles && ci < ncols) {
-              const int64_t v = col_value(ci);
-              const bool routed = v < p.Tk;
-              if (row_a < p.rows) p.part[v * p.rows + row_a] = routed ? bf16_round(y[t][i]) : y[t][i];
-              if (row_b < p.rows)
-                p.part[v * p.rows + row_b] = routed ? bf16_round(y[t][2 + i]) : y[t][2 + i];
-            }
-          }
-      }
-      __threadfence();
-      named_bar(1, kTmaConsumers);
-      if (ctid == 0) {
-        const unsigned target = (unsigned)(n_routed + p.shared_segments);
-        const unsigned old = atomicAdd(p.counters + info.rb, 1u);
-        flags[1] = (old == target - 1u) ? 1 : 0;
-      }
-      named_bar(1, kTmaConsumers);
-      if (flags[1]) {
-        __threadfence();
-        const int64_t r0 = (int64_t)info.rb * kTmaRows;
-        const int T = p.T, k = p.k;
-        for (int idx = ctid; idx < T * kTmaRows; idx += kTmaConsumers) {
-          const int t = idx / kTmaRows;
-          const int64_t row = r0 + (idx - t * kTmaRows);
-          if (row >= p.rows) continue;
-          float tot;
-          if (!p.weight_after_down) {
-            float s = 0.0f;
-            for (int j = 0; j < k; ++j) s += __ldcg(p.part + (int64_t)(t * k + j) * p.rows + row);
-            tot = bf16_round(s);
-          } else {
-            float s = 0.0f;
-            for (int j = 0; j < k; ++j)
-              s += __ldcg(p.part + (int64_t)(t * k + j) * p.rows + row) *
-                   __ldg(p.weights + t * k + j);
-            tot = s;
-          }
-          if (p.has_shared) {
-            const float hi = __ldcg(p.part + (int64_t)(p.Tk + t) * p.rows + row);
-            const float lo = __ldcg(p.part + (int64_t)(p.Tk + T + t) * p.rows + row);
-            tot = tot + (hi + lo);
-          }
-          p.out[(int64_t)t * p.rows + row] = f32_to_bf16_bits(tot);
-        }
-        if (ctid == 0) p.counters[info.rb] = 0u;
+        p.hsum[(int64_t)vci * hp + info.rb] = shi;
+        if (shared) p.hsum[(int64_t)(vci + p.shared_lo_off) * hp + info.rb] = slo;
       }
     }
-    named_bar(1, kTmaConsumers);  // red / hs / flags reused by the next item
+    named_bar(1, kTmaConsumers);  // red / hs reused by the next item
+    if (has_next) cur = nxt;
   }
 }
 

@@ -452,15 +452,15 @@ __global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
   }
   if (!p.build_plan) return;
   __shared__ int s_last;
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();  // release this CTA's ids/weights (cumulative after the barrier)
     const unsigned old = atomicAdd(p.counter, 1u);
     s_last = (old == gridDim.x - 1) ? 1 : 0;
+    __threadfence();
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   build_plan_cta<256>(p.plan);
   if (threadIdx.x == 0) *p.counter = 0u;
 }
