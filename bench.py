@@ -304,7 +304,9 @@ def e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local):
     both copies inside the timed region."""
     if args.no_e2e:
         return None
-    xh = [x.cpu().pin_memory() for x in xs[T]]
+    import torch
+    import torch.distributed as dist
+    xh =[x.cpu().pin_memory() for x in xs[T]]
     oh = torch.empty((T, spec.hidden), dtype=torch.bfloat16).pin_memory()
     for i in range(W):
         lay, b = schedule(i)
