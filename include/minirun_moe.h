@@ -135,6 +135,34 @@ mr_status mr_affine_gather_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens,
 mr_status mr_affine_dequantize(mr_ctx* ctx, const mr_affine_desc* w, float* out,
                                void* stream);
 
+/* Bytes of fixed device scratch behind mr_affine_gather_mm_noalloc. */
+#define MR_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+
+/* mr_affine_gather_mm without any device allocation. No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc when they call
+ * in — an engine whose allocator owns the device heap, a decode loop that
+ * must not synchronise or fail on an allocation, a binding with no place to
+ * keep an mr_ctx. Same arguments and result as mr_affine_gather_mm (results
+ * agree to fp32 summation order), minus the context; `msg` (may be NULL)
+ * receives the reason of a failure.
+ *   - Scratch is one static device array of MR_NOALLOC_SCRATCH_BYTES in the
+ *     library image; every GPU that loads the library holds it until the
+ *     process exits. Sizes whose scratch (about tokens * in_features * 2.07
+ *     bytes plus the routing plan) does not fit are rejected with
+ *     MR_ERR_UNSUPPORTED and the needed size in `msg`.
+ *   - The first call on a device resolves the array's address on that device
+ *     (no allocation); make that first call before any stream capture.
+ *   - Every call on a device shares the one array and finds the previous
+ *     call's contents in it: calls whose work overlaps on the GPU (other
+ *     streams, other host threads) race and corrupt each other's results.
+ *     Serialise them, e.g. on one stream.
+ *   - No context, so invalid expert ids cannot be reported: their output rows
+ *     are left unwritten. */
+mr_status mr_affine_gather_mm_noalloc(const uint16_t* x, int64_t tokens,
+                                      const int32_t* ids, int32_t top_k,
+                                      const mr_affine_desc* w, uint16_t* out,
+                                      void* stream, char* msg, size_t msg_len);
+
 /* ---------------------------------------------------------------- router
  * K3Router.select (Sources/ModelAdapters/Operators/MoE.swift:77-150),
  * DeepSeekV4Router.select (Operators/DeepSeekV4Routing.swift:100-280),

@@ -5,6 +5,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "mr_launch.h"
@@ -1160,3 +1161,180 @@ mr_status mr_synth_affine_biases(mr_ctx* ctx, const uint16_t* scales, int64_t n,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------- allocation-free gather
+//
+// mr_affine_gather_mm_noalloc is for callers that must not allocate device
+// memory when they call in: engines whose allocator reserves the whole device
+// heap up front and forbids cudaMalloc afterwards, decode loops where an
+// allocation (which can synchronise the device, or fail under memory
+// pressure) is not acceptable mid-step, and bindings that have nowhere to
+// keep a context that owns a workspace. Its only scratch is the fixed array
+// below, part of the library's own device image: every GPU that loads the
+// library holds these MR_NOALLOC_SCRATCH_BYTES until the process exits, and a
+// call allocates nothing.
+
+namespace {
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[MR_NOALLOC_SCRATCH_BYTES];
+
+struct NoAllocDevice {
+  bool ready = false;
+  char* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  int sm_count = 0;
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[64];
+
+// Once per device, with that device current: resolve the array's device
+// address (g_noalloc_scratch names a host-side stand-in in host code) and the
+// SM count. Allocates nothing.
+mr_status noalloc_device(NoAllocDevice* out, std::string& why) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    why = std::string("cudaGetDevice: ") + cudaGetErrorString(e);
+    return MR_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= 64) {
+    why = "device ordinal above 63";
+    return MR_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (!d.ready) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      why = std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e);
+      return MR_ERR_CUDA;
+    }
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) {
+      why = std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e);
+      return MR_ERR_CUDA;
+    }
+    d.scratch = static_cast<char*>(ptr);
+    d.sm_count = sms;
+    d.ready = true;
+  }
+  *out = d;
+  return MR_OK;
+}
+
+mr_status noalloc_gather(const uint16_t* x, int64_t T, const int32_t* ids, int32_t k,
+                         const mr_affine_desc* w, uint16_t* out, cudaStream_t s,
+                         std::string& why) {
+  mr_status st = validate_affine(w, why);
+  if (st) return st;
+  if (w->experts == 0) {
+    why = "affineGatherMM needs a stacked AffineWeights; use affineMM for a single matrix";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (T <= 0 || !x || !out || !ids || k <= 0) {
+    why = "x must be [tokens, inFeatures] with tokens > 0 and ids [tokens, k] with k > 0";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0) {
+    why = "x must be 16-byte aligned";
+    return MR_ERR_UNSUPPORTED;
+  }
+  if (w->experts > kMaxExperts) {
+    why = "expert stacks larger than 1024 are not built here";
+    return MR_ERR_UNSUPPORTED;
+  }
+  const int64_t Tk = T * k;
+  if (Tk > (int64_t)1 << 30) {
+    why = "token count too large";
+    return MR_ERR_UNSUPPORTED;
+  }
+  const int E = w->experts;
+  const int64_t in = w->in_features;
+  const int seg_cols = pick_seg_cols(Tk);
+  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / seg_cols + 1;
+
+  // scratch layout: permuted x, group sums of x, the routing plan, error word
+  Bump b{nullptr};
+  b.take<uint16_t>(T * in);
+  b.take<float>(T * (in / kGroup));
+  b.take<int>(4);
+  b.take<int4>(max_seg);
+  b.take<int>(Tk);
+  b.take<unsigned>(1);
+  if (b.off > (size_t)MR_NOALLOC_SCRATCH_BYTES) {
+    char m[256];
+    snprintf(m, sizeof m,
+             "these sizes need %zu bytes of scratch; the allocation-free entry point has a "
+             "fixed %u-byte scratch (about tokens * inFeatures * 2.07 bytes fit): use "
+             "mr_affine_gather_mm or split the tokens",
+             b.off, (unsigned)MR_NOALLOC_SCRATCH_BYTES);
+    why = m;
+    return MR_ERR_UNSUPPORTED;
+  }
+  NoAllocDevice dev;
+  if ((st = noalloc_device(&dev, why))) return st;
+  b.base = dev.scratch;
+  b.off = 0;
+  uint16_t* xperm = b.take<uint16_t>(T * in);
+  float* xsum = b.take<float>(T * (in / kGroup));
+  int* nseg = b.take<int>(4);
+  int4* segs = b.take<int4>(max_seg);
+  int* cols = b.take<int>(Tk);
+  unsigned* err = b.take<unsigned>(1);
+
+  auto check = [&](cudaError_t e, const char* what) -> mr_status {
+    if (e == cudaSuccess) return MR_OK;
+    why = std::string(what) + ": " + cudaGetErrorString(e);
+    return MR_ERR_CUDA;
+  };
+  // the error word collects bits with atomicOr: it must start at zero
+  if ((st = check(cudaMemsetAsync(err, 0, sizeof(unsigned), s), "clear error word"))) return st;
+  PrepParams pp{x, T, in, w->bits, xperm, xsum};
+  const int64_t chunks = T * (in / 16);
+  const int pgrid = (int)std::max<int64_t>(
+      1, std::min<int64_t>((chunks + 255) / 256, 4 * (int64_t)dev.sm_count));
+  prep_kernel<<<pgrid, 256, 0, s>>>(pp);
+  if ((st = check(cudaGetLastError(), "prep_kernel"))) return st;
+  PlanParams plan{ids, (int)Tk, E, nseg, segs, cols, err, seg_cols};
+  plan_kernel<<<1, 256, 0, s>>>(plan);
+  if ((st = check(cudaGetLastError(), "plan_kernel"))) return st;
+
+  GemvParams g{};
+  g.src_a = stack_source(*w, 0);
+  g.src_b = g.src_a;
+  g.sh_a = g.src_a;
+  g.sh_b = g.src_a;
+  g.rows = w->out_features;
+  g.in = in;
+  g.n_routed_segments = nseg;
+  g.segments = segs;
+  g.cols = cols;
+  g.shared_segments = 0;
+  g.shared_cols = 0;
+  g.seg_cols = seg_cols;
+  g.Tk = (int)Tk;
+  g.in_div = k;
+  g.shared_in_off = 0;
+  g.xperm = xperm;
+  g.xsum = xsum;
+  g.xsum_parts = 1;
+  g.error = err;
+  g.out_bf16 = out;
+  g.rb_count = (int)((g.rows + kRowsPlain - 1) / kRowsPlain);
+  const int64_t items = max_seg * g.rb_count;
+  return check(launch_gemv(g, w->bits, w->scale_dtype, EPI_STORE, seg_cols / 8, (int)items, s),
+               "gemv(store)");
+}
+
+}  // namespace
+
+extern "C" mr_status mr_affine_gather_mm_noalloc(const uint16_t* x, int64_t tokens,
+                                                const int32_t* ids, int32_t top_k,
+                                                const mr_affine_desc* w, uint16_t* out,
+                                                void* stream, char* msg, size_t msg_len) {
+  std::string why;
+  const mr_status st = noalloc_gather(x, tokens, ids, top_k, w, out, as_stream(stream), why);
+  set_msg(msg, msg_len, st ? why : std::string());
+  return st;
+}

@@ -73,6 +73,9 @@ SIGNATURES = {
     "mr_affine_gather_mm": (C.c_int, [vp, vp, C.c_int64, vp, C.c_int32,
                                       C.POINTER(mr_affine_desc), vp, vp]),
     "mr_affine_dequantize": (C.c_int, [vp, C.POINTER(mr_affine_desc), vp, vp]),
+    "mr_affine_gather_mm_noalloc": (C.c_int, [vp, C.c_int64, vp, C.c_int32,
+                                              C.POINTER(mr_affine_desc), vp, vp, C.c_char_p,
+                                              C.c_size_t]),
     "mr_router_config_validate": (C.c_int, [C.POINTER(mr_router_config), C.c_char_p,
                                             C.c_size_t]),
     "mr_router_select": (C.c_int, [vp, vp, C.c_int64, C.c_int64, vp,
