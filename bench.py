@@ -51,6 +51,8 @@ def parse():
                    help="routed experts (0 = config 1's 256); smaller values only for "
                         "profiling captures that must fit a few GB")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--kernel-path", choices=["auto", "register", "tma", "umma"], default="auto",
+                   help="dequant-GEMV implementation (mr_ctx_set_kernel_path)")
     return p.parse_args()
 
 
@@ -157,6 +159,7 @@ def run_ours(args, world, rank, local):
     xs = {t: [S.synth_x(spec, t, layer=0, batch=b, device=local) for b in range(NB)]
           for t in token_counts}
     ctx = M.Context.get(local)
+    ctx.set_kernel_path(args.kernel_path)
     torch.cuda.synchronize()
 
     def barrier():

@@ -85,9 +85,11 @@ const char* mr_last_error(const mr_ctx* ctx);
  * MR_ERR_DEVICE (and writes the bits to *bits_out if non-NULL) when set. */
 mr_status mr_ctx_check(mr_ctx* ctx, void* stream, uint32_t* bits_out);
 /* Selects the dequant-GEMV implementation (a tuning/testing knob; results
- * agree to fp32 summation order): 0 auto (TMA-pipelined where in % 512 == 0
- * and scale/bias rows are 16-byte aligned), 1 register-streaming, 2 TMA
- * (falls back to 1 where its layout conditions do not hold). */
+ * agree to fp32 summation order): 0 auto (= 2, the fastest for decode
+ * batches), 1 register-streaming, 2 TMA-pipelined with mma.sync / FMA
+ * (where in % 512 == 0 and scale/bias rows are 16-byte aligned), 3 tcgen05
+ * (tensor-memory MMA; MoE layer only, elsewhere as 2). Each falls back to
+ * the next simpler one where its layout conditions do not hold. */
 mr_status mr_ctx_set_kernel_path(mr_ctx* ctx, int path);
 /* Pre-size the workspace for layers up to these sizes (graph capture needs
  * a workspace that will not grow). */

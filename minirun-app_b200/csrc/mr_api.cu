@@ -201,6 +201,34 @@ static bool use_tma(const mr_ctx* ctx, bool layout_ok) {
   return ctx->kernel_path != 1 && layout_ok;
 }
 
+// Activation rows of routed columns in plan order (tcgen05 layer path with
+// more than 16 tokens): xg[c] = x_perm[cols[c] / in_div], and its group sums.
+// Positions past the plan's valid columns may hold stale ids; rows outside
+// [0, T) are skipped.
+__global__ void gather_act_kernel(const uint16_t* __restrict__ xperm,
+                                  const float* __restrict__ xsum, const int* __restrict__ cols,
+                                  int Tk, int in_div, int T, int64_t H, uint16_t* __restrict__ xg,
+                                  float* __restrict__ xsg) {
+  const int64_t cpr = H / 8;        // 16-byte chunks per row
+  const int64_t gpr = H / kGroup;   // group sums per row
+  const int64_t n = (int64_t)Tk * (cpr + gpr);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const bool sums = i >= (int64_t)Tk * cpr;
+    const int64_t j = sums ? i - (int64_t)Tk * cpr : i;
+    const int64_t per = sums ? gpr : cpr;
+    const int c = (int)(j / per);
+    const int64_t e = j - (int64_t)c * per;
+    const int t = __ldg(cols + c) / in_div;
+    if (t < 0 || t >= T) continue;
+    if (!sums)
+      reinterpret_cast<uint4*>(xg)[(int64_t)c * cpr + e] =
+          __ldg(reinterpret_cast<const uint4*>(xperm) + (int64_t)t * cpr + e);
+    else
+      xsg[(int64_t)c * gpr + e] = __ldg(xsum + (int64_t)t * gpr + e);
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -220,7 +248,9 @@ static EncodeTiledFn encode_fn() {
 }
 
 // kind 0: packed codes (uint32 words, 32-word x box_rows boxes, 128-byte
-// swizzle); kind 1/2/3: bf16/f16/f32 scales or biases (8 x box_rows boxes).
+// swizzle); kind 1/2/3: bf16/f16/f32 scales or biases (8 x box_rows boxes);
+// kind 4: bf16 activation rows (64 x box_rows boxes, 128-byte swizzle);
+// kind 5/6: f32 group sums (8 / 16 x box_rows boxes).
 static bool tensor_map(mr_ctx* ctx, CUtensorMap* out, const void* base, int64_t rows,
                        int64_t width, int box_rows, int kind) {
   const mr_ctx::MapKey key{base, rows, width, box_rows, kind};
@@ -231,18 +261,20 @@ static bool tensor_map(mr_ctx* ctx, CUtensorMap* out, const void* base, int64_t 
     }
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
-  const int esz = kind == 0 ? 4 : (kind == 3 ? 4 : 2);
-  const CUtensorMapDataType dt = kind == 0   ? CU_TENSOR_MAP_DATA_TYPE_UINT32
-                                 : kind == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                 : kind == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const int esz = (kind == 0 || kind == 3 || kind >= 5) ? 4 : 2;
+  const CUtensorMapDataType dt = kind == 0                 ? CU_TENSOR_MAP_DATA_TYPE_UINT32
+                                 : (kind == 1 || kind == 4) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : kind == 2               ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   const cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)(width * esz)};
-  const cuuint32_t box[2] = {(cuuint32_t)(kind == 0 ? 32 : kTmaGps), (cuuint32_t)box_rows};
+  const int inner = kind == 0 ? 32 : kind == 4 ? kGroup : kind == 6 ? 2 * kTmaGps : kTmaGps;
+  const cuuint32_t box[2] = {(cuuint32_t)inner, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(out, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  kind == 0 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  (kind == 0 || kind == 4) ? CU_TENSOR_MAP_SWIZZLE_128B
+                                           : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   if (ctx->map_cache.size() > 256) ctx->map_cache.clear();
@@ -268,6 +300,45 @@ static bool encode_matrix(mr_ctx* ctx, const MapSpec& m, int box_rows, CUtensorM
   return tensor_map(ctx, packed, d->packed, rows, words, box_rows, 0) &&
          tensor_map(ctx, scales, d->scales, rows, groups, box_rows, kind) &&
          tensor_map(ctx, biases, d->biases, rows, groups, box_rows, kind);
+}
+
+// Activation rows of the tcgen05 kernel (bf16 [rows, width]) and their
+// group sums (f32 [rows, width / 64 * parts]).
+struct ActSpec {
+  const void* base;
+  int64_t rows;
+  const float* sums;
+};
+
+// Encodes every tensor map of one tcgen05 launch (false: keep the other
+// kernels). maps[0..3] as run_gemv.
+static bool encode_umma(mr_ctx* ctx, const MapSpec* maps, int epi, int64_t width, ActSpec act,
+                        ActSpec act_sh, UmMaps* um) {
+  const int parts = epi == EPI_PARTIAL ? 2 : 1;
+  const int64_t swidth = width / kGroup * parts;
+  const int box_rows = epi == EPI_SWIGLU ? kUmRows / 2 : kUmRows;
+  bool ok = encode_matrix(ctx, maps[0], box_rows, &um->a_packed, &um->a_scales, &um->a_biases);
+  const MapSpec& mb = maps[1].d ? maps[1] : maps[0];
+  ok = ok && encode_matrix(ctx, mb, box_rows, &um->b_packed, &um->b_scales, &um->b_biases);
+  const MapSpec& sa = maps[2].d ? maps[2] : maps[0];
+  const MapSpec& sb = maps[3].d ? maps[3] : (maps[2].d ? maps[2] : maps[0]);
+  ok = ok && encode_matrix(ctx, sa, box_rows, &um->sa_packed, &um->sa_scales, &um->sa_biases);
+  ok = ok && encode_matrix(ctx, sb, box_rows, &um->sb_packed, &um->sb_scales, &um->sb_biases);
+  ok = ok && tensor_map(ctx, &um->act, act.base, act.rows, width, kUmN, 4);
+  ok = ok && tensor_map(ctx, &um->act_sh, act_sh.base, act_sh.rows, width, kUmN, 4);
+  ok = ok && tensor_map(ctx, &um->xs, act.sums, act.rows, swidth, kUmN, 4 + parts);
+  ok = ok && tensor_map(ctx, &um->xs_sh, act_sh.sums, act_sh.rows, swidth, kUmN, 4 + parts);
+  return ok;
+}
+
+// One tcgen05 GEMV over the plan: items are 128 weight rows (64 gate + 64 up
+// for SwiGLU) x one segment of <= 16 activation rows.
+static cudaError_t run_umma(mr_ctx* ctx, GemvParams g, int64_t max_segments, const UmMaps& um,
+                            int bits, int sd, int epi, cudaStream_t s) {
+  g.rb_count = (int)(epi == EPI_SWIGLU ? g.rows / 64 : (g.rows + kUmRows - 1) / kUmRows);
+  const int64_t items = (max_segments + g.shared_segments) * g.rb_count;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
+  return launch_umma(g, um, bits, sd, epi, grid, s);
 }
 
 // Issues one GEMV over the plan with the chosen implementation.
@@ -640,7 +711,8 @@ static mr_status affine_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const 
 
 mr_status mr_ctx_set_kernel_path(mr_ctx* ctx, int path) {
   if (!ctx) return MR_ERR_INVALID_ARGUMENT;
-  if (path < 0 || path > 2) return fail(ctx, MR_ERR_INVALID_ARGUMENT, "kernel path must be 0, 1 or 2");
+  if (path < 0 || path > 3)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "kernel path must be 0, 1, 2 or 3");
   ctx->kernel_path = path;
   return MR_OK;
 }
@@ -817,13 +889,14 @@ mr_status mr_ctx_reserve(mr_ctx* ctx, int64_t max_tokens, int32_t top_k, int32_t
   if (max_tokens <= 0 || top_k <= 0 || experts <= 0 || hidden <= 0 || inter <= 0)
     return fail(ctx, MR_ERR_INVALID_ARGUMENT, "reserve sizes must be positive");
   const int64_t T = max_tokens, Tk = T * top_k, R = Tk + 2 * T;
-  const int64_t max_seg = std::min<int64_t>(experts, Tk) + Tk / 8 + 1;
+  const int64_t max_seg = std::min<int64_t>(experts, Tk) + Tk / 8 + 1;  // seg_cols >= 8
   size_t bytes = 0;
   bytes += (size_t)64 * T * experts * 4 + 256;  // logits partials (ks <= 64)
   bytes += (size_t)T * hidden * 2 + 256 + (size_t)T * (hidden / kGroup) * 4 + 256;
   bytes += (size_t)Tk * 8 + (size_t)T * 4 + 1024;
   bytes += (size_t)max_seg * 16 + (size_t)Tk * 4 + 1024;
   bytes += (size_t)R * inter * 2 + (size_t)R * (inter / 32) * 4 + (size_t)R * hidden * 4 + 1024;
+  bytes += (size_t)Tk * hidden * 2 + (size_t)Tk * (hidden / kGroup) * 4 + 512;  // gathered x
   return ensure_workspace(ctx, bytes);
 }
 
@@ -842,7 +915,19 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   const int64_t H = L->hidden, I = L->inter, Tk = T * k;
   const bool has_shared = L->shared_inter > 0;
   const int64_t R = Tk + (has_shared ? 2 * T : 0);  // h / partial rows
-  const int seg_cols = pick_seg_cols(T);  // a routed expert has <= T columns
+  // tcgen05 path: whole 512-element stages, 64-row gate/up boxes, stacks
+  // addressable by tensor maps; both projections switch together (h rows are
+  // plan positions there, pair ids elsewhere)
+  const bool um_layout =
+      !L->expert_table && H % 512 == 0 && I % 512 == 0 && tma_layout_ok(H, &L->gate, false) &&
+      tma_layout_ok(H, &L->up, false) && tma_layout_ok(I, &L->down, false) &&
+      (!has_shared || (tma_layout_ok(H, &L->shared_gate, false) &&
+                       tma_layout_ok(H, &L->shared_up, false) &&
+                       tma_layout_ok(I, &L->shared_down, false)));
+  const bool um_try = ctx->kernel_path == 3 && um_layout;
+  const bool um_dense = T <= kUmN;  // routed activations are the token rows themselves
+  // a routed expert has <= T columns
+  const int seg_cols = um_try ? kUmN : pick_seg_cols(T);
   const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / seg_cols + 1;
   const LogitsShape ls = logits_shape(ctx, T, E, H);
   if (Tk > (int64_t)1 << 28) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
@@ -852,10 +937,15 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   int32_t* ids = nullptr;
   int *nseg = nullptr, *cols = nullptr;
   int4* segs = nullptr;
-  uint16_t* h = nullptr;
+  uint16_t *h = nullptr, *xg = nullptr;
+  float* xsg = nullptr;
   Bump b{nullptr};
   for (int pass = 0; pass < 2; ++pass) {
     b.off = 0;
+    if (um_try && !um_dense) {
+      xg = b.take<uint16_t>(Tk * H);
+      xsg = b.take<float>(Tk * (H / kGroup));
+    }
     part = b.take<float>((size_t)ls.kq * T * E);
     xperm = b.take<uint16_t>(T * H);
     xsum = b.take<float>(T * (H / kGroup));
@@ -875,6 +965,20 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   if (ids_out) ids = ids_out;
   if (weights_out) wts = weights_out;
   cudaStream_t s = as_stream(stream);
+
+  // tensor maps of both tcgen05 launches, before anything is enqueued
+  UmMaps um1, um2;
+  bool um = false;
+  if (um_try) {
+    const MapSpec m1[4] = {{&L->gate, E}, {&L->up, E},
+                           {has_shared ? &L->shared_gate : nullptr, 1},
+                           {has_shared ? &L->shared_up : nullptr, 1}};
+    const MapSpec m2[4] = {{&L->down, E}, {nullptr, 0},
+                           {has_shared ? &L->shared_down : nullptr, 1}, {nullptr, 0}};
+    const ActSpec xa = um_dense ? ActSpec{xperm, T, xsum} : ActSpec{xg, Tk, xsg};
+    um = encode_umma(ctx, m1, EPI_SWIGLU, H, xa, ActSpec{xperm, T, xsum}, &um1) &&
+         encode_umma(ctx, m2, EPI_PARTIAL, I, ActSpec{h, R, hsum}, ActSpec{h, R, hsum}, &um2);
+  }
 
   // K0a: router logits (+ permuted input for the gate/up GEMV)
   LogitsParams lp{};
@@ -906,6 +1010,13 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
                      segs, cols, seg_cols, s);
   }
   if (st) return st;
+  if (um && !um_dense) {
+    // routed activation rows in plan order for the tcgen05 gate/up launch
+    const int64_t n = Tk * (H / 8 + H / kGroup);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8 * ctx->sm_count));
+    gather_act_kernel<<<grid, 256, 0, s>>>(xperm, xsum, cols, (int)Tk, k, (int)T, H, xg, xsg);
+    if ((st = cuda_check(ctx, cudaGetLastError(), "gather_act_kernel"))) return st;
+  }
 
   // K1: gate/up dequant-GEMV + SwiGLU (+ routing weight) -> h, hsum
   GemvParams g{};
@@ -952,13 +1063,19 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
                                      (!has_shared || (tma_layout_ok(H, &L->shared_gate, false) &&
                                                       tma_layout_ok(H, &L->shared_up, false))));
   const int nt = seg_cols / 8;
+  g.um_dense = um_dense ? 1 : 0;
+  g.sh_row0 = 0;
+  g.h_by_pos = um ? 1 : 0;
+  g.T = (int)T;
   {
     ProfScope ps(ctx, MR_KERNEL_GATE_UP, s);
     const MapSpec maps[4] = {{&L->gate, E}, {&L->up, E},
                              {has_shared ? &L->shared_gate : nullptr, 1},
                              {has_shared ? &L->shared_up : nullptr, 1}};
-    st = cuda_check(ctx, run_gemv(ctx, g, max_seg, tma1, maps, bits, sd, EPI_SWIGLU, nt, s),
-                    "gemv(swiglu)");
+    st = um ? cuda_check(ctx, run_umma(ctx, g, max_seg, um1, bits, sd, EPI_SWIGLU, s),
+                         "gemv_umma(swiglu)")
+            : cuda_check(ctx, run_gemv(ctx, g, max_seg, tma1, maps, bits, sd, EPI_SWIGLU, nt, s),
+                         "gemv(swiglu)");
   }
   if (st) return st;
 
@@ -998,11 +1115,16 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   d.out = out;
   const bool tma2 = use_tma(ctx, tma_layout_ok(I, &L->down, table) &&
                                      (!has_shared || tma_layout_ok(I, &L->shared_down, false)));
+  d.um_dense = 0;
+  d.sh_row0 = (int)Tk;
   ProfScope ps(ctx, MR_KERNEL_DOWN_COMBINE, s);
   const MapSpec maps[4] = {{&L->down, E}, {nullptr, 0},
                            {has_shared ? &L->shared_down : nullptr, 1}, {nullptr, 0}};
-  if ((st = cuda_check(ctx, run_gemv(ctx, d, max_seg, tma2, maps, bits, sd, EPI_PARTIAL, nt, s),
-                       "gemv(down)")))
+  if ((st = um ? cuda_check(ctx, run_umma(ctx, d, max_seg, um2, bits, sd, EPI_PARTIAL, s),
+                            "gemv_umma(down)")
+               : cuda_check(ctx, run_gemv(ctx, d, max_seg, tma2, maps, bits, sd, EPI_PARTIAL, nt,
+                                          s),
+                            "gemv(down)")))
     return st;
   const int64_t n_out = T * H;
   const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 4 * ctx->sm_count));

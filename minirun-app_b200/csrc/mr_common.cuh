@@ -173,9 +173,10 @@ MR_DEVICE void named_bar(int id, int count) {
 }
 
 // Iteration cap of every device-side wait (one try_wait each, which blocks
-// for at most a hardware time slice): seconds, well above any legitimate
-// wait, after which the kernel reports MR_DEVERR_TIMEOUT and returns.
-constexpr uint32_t kSpinLimit = 1u << 26;
+// for at most a hardware time slice): at most a few seconds, far above any
+// legitimate wait (one pipeline stage, microseconds), after which the kernel
+// reports MR_DEVERR_TIMEOUT and returns.
+constexpr uint32_t kSpinLimit = 1u << 22;
 
 // ------------------------------------------------------------ structures
 

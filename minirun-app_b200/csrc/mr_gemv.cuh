@@ -91,6 +91,11 @@ struct GemvParams {
   int k;
   int has_shared;
   uint16_t* out;          // [T, rows] bf16
+  // tcgen05 kernel: activation rows come through tensor maps (routed, shared)
+  int um_dense;           // routed activations are the T <= 16 token rows; a
+                          // column's accumulator is its token's
+  int sh_row0;            // first shared activation-map row (K2: Tk, else 0)
+  int h_by_pos;           // SWIGLU: h / hsum rows are plan positions
 };
 
 MR_DEVICE float sigmoid_f32(float g) { return 1.0f / (1.0f + expf(-g)); }

@@ -4,6 +4,7 @@
 
 #include "mr_gemv.cuh"
 #include "mr_gemv_tma.cuh"
+#include "mr_gemv_umma.cuh"
 
 namespace mr {
 
@@ -20,6 +21,24 @@ cudaError_t launch_tma_b4(const GemvParams& p, const TmaMaps& m, int sd, int epi
                           cudaStream_t s);
 cudaError_t launch_tma_b8(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, int grid,
                           cudaStream_t s);
+
+// tcgen05 kernel (in % 512 == 0, activations through tensor maps).
+cudaError_t launch_umma_b2(const GemvParams& p, const UmMaps& m, int sd, int epi, int grid,
+                           cudaStream_t s);
+cudaError_t launch_umma_b4(const GemvParams& p, const UmMaps& m, int sd, int epi, int grid,
+                           cudaStream_t s);
+cudaError_t launch_umma_b8(const GemvParams& p, const UmMaps& m, int sd, int epi, int grid,
+                           cudaStream_t s);
+
+inline cudaError_t launch_umma(const GemvParams& p, const UmMaps& m, int bits, int sd, int epi,
+                               int grid, cudaStream_t s) {
+  switch (bits) {
+    case 2: return launch_umma_b2(p, m, sd, epi, grid, s);
+    case 4: return launch_umma_b4(p, m, sd, epi, grid, s);
+    case 8: return launch_umma_b8(p, m, sd, epi, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
 
 inline cudaError_t launch_gemv(const GemvParams& p, int bits, int sd, int epi, int nt, int grid,
                                cudaStream_t s) {
@@ -41,9 +60,15 @@ inline cudaError_t launch_tma(const GemvParams& p, const TmaMaps& m, int bits, i
   }
 }
 
-// Columns per segment for a launch whose segments can hold up to `max_cols`
-// columns: one 8-column mma tile when that covers them, else two.
-inline int pick_seg_cols(int64_t max_cols) { return max_cols <= 8 ? 8 : 16; }
+// Columns per segment: one 8-column mma tile. An expert with more columns
+// gets several segments (its weights are re-read, mostly from L2): measured
+// on config 1 at T = 64, one tile per segment is 1.55x faster than two,
+// because decode segments hold 1-4 columns and every mma.sync costs the same
+// whatever the number of live columns.
+inline int pick_seg_cols(int64_t max_cols) {
+  (void)max_cols;
+  return 8;
+}
 
 // Sets the dynamic shared-memory opt-in of `kernel` once per device; `done`
 // must be owned by that one kernel.
@@ -71,7 +96,43 @@ inline cudaError_t launch_tma_inst(const GemvParams& p, const TmaMaps& m, int gr
   return cudaGetLastError();
 }
 
+template <int BITS, int SD, int EPI>
+inline cudaError_t launch_umma_inst(const GemvParams& p, const UmMaps& m, int grid,
+                                    cudaStream_t s) {
+  static bool done[64] = {};  // one per instantiation
+  const int nst = um_stages<BITS, SD, EPI>();
+  const int smem = um_smem_bytes<BITS, SD, EPI>(nst);
+  auto kern = gemv_umma_kernel<BITS, SD, EPI>;
+  cudaError_t e = opt_in_smem(kern, smem, done);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kUmThreads, smem, s>>>(p, m, nst);
+  return cudaGetLastError();
+}
+
+template <int BITS, int SD>
+inline cudaError_t launch_umma_epi(const GemvParams& p, const UmMaps& m, int epi, int grid,
+                                   cudaStream_t s) {
+  switch (epi) {
+    case EPI_STORE: return launch_umma_inst<BITS, SD, EPI_STORE>(p, m, grid, s);
+    case EPI_SWIGLU: return launch_umma_inst<BITS, SD, EPI_SWIGLU>(p, m, grid, s);
+    default: return launch_umma_inst<BITS, SD, EPI_PARTIAL>(p, m, grid, s);
+  }
+}
+
 }  // namespace mr
+
+// Instantiates launch_umma_b<BITS> in a translation unit.
+#define MR_DEFINE_UMMA_LAUNCHER(BITS)                                                         \
+  namespace mr {                                                                              \
+  cudaError_t launch_umma_b##BITS(const GemvParams& p, const UmMaps& m, int sd, int epi,      \
+                                  int grid, cudaStream_t s) {                                 \
+    switch (sd) {                                                                             \
+      case MR_DTYPE_BF16: return launch_umma_epi<BITS, MR_DTYPE_BF16>(p, m, epi, grid, s);    \
+      case MR_DTYPE_F16: return launch_umma_epi<BITS, MR_DTYPE_F16>(p, m, epi, grid, s);      \
+      default: return launch_umma_epi<BITS, MR_DTYPE_F32>(p, m, epi, grid, s);                \
+    }                                                                                         \
+  }                                                                                           \
+  }
 
 // Instantiates launch_gemv_b<BITS> and launch_tma_b<BITS> in a translation unit.
 #define MR_DEFINE_GEMV_LAUNCHER(BITS)                                                          \

@@ -10,7 +10,9 @@ import ctypes as C
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "_lib", "libminirun_moe.so")
+# MINIRUN_MOE_LIB selects another build of the same library (e.g. one built
+# with different compile flags); the default is the in-tree build.
+LIB_PATH = os.environ.get("MINIRUN_MOE_LIB") or os.path.join(_HERE, "_lib", "libminirun_moe.so")
 
 MR_OK = 0
 MR_ERR_INVALID_ARGUMENT = 1

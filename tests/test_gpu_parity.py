@@ -54,7 +54,7 @@ def oracle_with_scales(w: O.Affine, scale_dtype) -> O.Affine:
     return O.Affine(w.packed, s.float().numpy(), b.float().numpy(), w.group, w.bits, 2)
 
 
-@pytest.fixture(params=["register", "tma"])
+@pytest.fixture(params=["register", "tma", "umma"])
 def kernel_path(request):
     """Runs a test once per dequant-GEMV implementation."""
     ctx = M.Context.get(0)
