@@ -15,8 +15,12 @@ inputs resident in HBM; `e2e` is the same metric through the host-buffer
 C-ABI call (pinned host x in, host out, copies inside the timed region);
 `roofline` is for the dominant kernel (gate/up GEMV), from CUDA events on the
 launching stream; `cpu_baseline` times the CPU oracle on the host cores.
-Under torchrun (N > 1) every rank runs the same workload on its own GPU
-(replicas) and the time is the max over ranks.
+Under torchrun (N > 1) the layer is expert-parallel: rank r holds routed
+experts [r*E/N, (r+1)*E/N) of every layer and T tokens of an N*T-token
+global batch (weak scaling: T per GPU fixed); one step = NCCL all-gather of
+the tokens, router over all of them, the rank's experts, NCCL reduce-scatter
+of the per-token sums, shared expert and combine. The time is the max over
+ranks; `value` counts all N*T tokens.
 """
 from __future__ import annotations
 
@@ -33,8 +37,11 @@ sys.path.insert(0, os.path.join(ROOT, "minirun-app_b200"))
 
 METRIC = ("MoE-layer decode tokens/s; dequant-GEMV HBM GB/s (% of ~8 TB/s) at 1/2/4/8 GPUs")
 FALLBACK_HBM_GBS = 6650.0
-# kernels one layer forward launches: logits(+prep), top-k(+plan), gate/up, down, combine
+# kernels one layer forward launches: logits(+prep), top-k(+plan), gate/up, down, combine;
+# expert-parallel: logits, top-k, routed gate/up and down, partial sums, shared gate/up and
+# down, combine (the NCCL collectives are not counted)
 LAUNCHES_PER_STEP = 5
+LAUNCHES_PER_STEP_EP = 8
 
 
 def parse():
@@ -153,14 +160,33 @@ def run_ours(args, world, rank, local):
         spec = dataclasses.replace(spec, experts=args.experts)
     T = args.tokens
     NL = max(1, args.layers)
-    layers = [S.synth_layer(spec, layer=l, device=local) for l in range(NL)]
+    # N > 1: expert parallelism, rank r holds experts [r*E/N, (r+1)*E/N) of
+    # every layer; its T tokens are rows r*T.. of the seeded global batch
+    ep = world > 1
+    e0, e1 = (rank * spec.experts // world, (rank + 1) * spec.experts // world)
+    layers = [S.synth_layer(spec, layer=l, device=local, shard=(rank, world) if ep else None)
+              for l in range(NL)]
     NB = NL + 1
     token_counts = [T] + [int(t) for t in args.sweep.split(",") if t and int(t) != T]
-    xs = {t: [S.synth_x(spec, t, layer=0, batch=b, device=local) for b in range(NB)]
-          for t in token_counts}
+
+    def xrows(t, b):
+        full = S.synth_x(spec, t * world, layer=0, batch=b, device=local)
+        return full[rank * t:(rank + 1) * t].contiguous()
+
+    xs = {t: [xrows(t, b) for b in range(NB)] for t in token_counts}
     ctx = M.Context.get(local)
     ctx.set_kernel_path(args.kernel_path)
+    group = M.ExpertGroup(local, rank, world) if ep else None
     torch.cuda.synchronize()
+
+    def step(lay, x, out, ids=None):
+        if ep:
+            group.forward(lay, x, out=out, ids=ids)
+        elif ids is None:
+            lay.forward(x, out=out, selection=False)
+        else:
+            _, sel = lay.forward(x, out=out)
+            ids.copy_(sel.ids)
 
     def barrier():
         if world > 1:
@@ -173,7 +199,7 @@ def run_ours(args, world, rank, local):
         outs = torch.empty((tok, spec.hidden), dtype=torch.bfloat16, device=dev)
         for i in range(warm):
             lay, b = schedule(i)
-            lay.forward(xs[tok][b], out=outs, selection=False)
+            step(lay, xs[tok][b], outs)
         torch.cuda.synchronize()
         barrier()
         st = torch.cuda.current_stream()
@@ -182,7 +208,7 @@ def run_ours(args, world, rank, local):
         e0.record(st)
         for i in range(steps):
             lay, b = schedule(i)
-            lay.forward(xs[tok][b], out=outs, selection=False)
+            step(lay, xs[tok][b], outs)
         e1.record(st)
         torch.cuda.synchronize()
         barrier()
@@ -194,11 +220,20 @@ def run_ours(args, world, rank, local):
         return ms
 
     def distinct_experts(tok, steps):
+        """Distinct routed experts this GPU streams per step (its own range,
+        selected by any token of the global batch)."""
         us = []
+        outs = torch.empty((tok, spec.hidden), dtype=torch.bfloat16, device=dev)
+        ids = torch.empty((tok, spec.top_k), dtype=torch.int32, device=dev)
         for i in range(steps):
             lay, b = schedule(i)
-            _, sel = lay.forward(xs[tok][b])
-            us.append(len(set(sel.ids.cpu().view(-1).tolist())))
+            step(lay, xs[tok][b], outs, ids)
+            allids = ids
+            if ep:
+                parts = [torch.empty_like(ids) for _ in range(world)]
+                dist.all_gather(parts, ids)
+                allids = torch.cat(parts)
+            us.append(len({e for e in allids.cpu().view(-1).tolist() if e0 <= e < e1}))
         return us
 
     def step_bytes(tok, U):
@@ -242,7 +277,8 @@ def run_ours(args, world, rank, local):
                            "layer_frac_of_hbm": b2 / (m2 / K / 1e3) / 1e9 / hbm,
                            "distinct_experts_avg": sum(u2) / len(u2)}
 
-    e2e = e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local)
+    e2e = e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local,
+                  group if ep else None)
     ctx.sync_check()
 
     cpu = None
@@ -271,7 +307,9 @@ def run_ours(args, world, rank, local):
             "layers_cycled": NL,
             "l2": "inputs larger than L2: consecutive steps read different layers' experts "
                   "(>= 227 MB each)",
-            "parallelism": "single GPU" if world == 1 else f"{world} replicas (one per GPU)",
+            "parallelism": "single GPU" if world == 1 else
+                           f"ep{world}: {spec.experts // world} routed experts per GPU, NCCL "
+                           "all-gather of tokens + reduce-scatter of expert outputs",
             "distinct_experts_avg": sum(us) / len(us),
             "layer_bytes_per_step": avg_bytes,
             "layer_gbs": avg_bytes / (ms_step / 1e3) / 1e9,
@@ -291,7 +329,7 @@ def run_ours(args, world, rank, local):
             "traffic": traffic,
         },
         "e2e": e2e,
-        "gpu_launches": K * LAUNCHES_PER_STEP,
+        "gpu_launches": K * (LAUNCHES_PER_STEP_EP if ep else LAUNCHES_PER_STEP),
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
@@ -299,21 +337,34 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        group.close()
         dist.destroy_process_group()
 
 
-def e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local):
-    """Same metric through the host-buffer C-ABI call: pinned host x in, host out,
-    both copies inside the timed region."""
+def e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local, group=None):
+    """Same metric with host buffers: pinned host x in, host out, both copies
+    inside the timed region — through the host-buffer C-ABI call on one GPU,
+    through copies + the expert-parallel call on N."""
     if args.no_e2e:
         return None
     import torch
     import torch.distributed as dist
-    xh =[x.cpu().pin_memory() for x in xs[T]]
+    xh = [x.cpu().pin_memory() for x in xs[T]]
     oh = torch.empty((T, spec.hidden), dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty((T, spec.hidden), dtype=torch.bfloat16, device=dev)
+    od = torch.empty_like(xd)
+
+    def host_step(lay, xhost):
+        if group is None:
+            lay.forward_host(xhost, oh, device=local)
+        else:
+            xd.copy_(xhost, non_blocking=True)
+            group.forward(lay, xd, out=od)
+            oh.copy_(od, non_blocking=True)
+
     for i in range(W):
         lay, b = schedule(i)
-        lay.forward_host(xh[b], oh, device=local)
+        host_step(lay, xh[b])
     torch.cuda.synchronize()
     barrier()
     st = torch.cuda.current_stream()
@@ -322,7 +373,7 @@ def e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local):
     e0.record(st)
     for i in range(K):
         lay, b = schedule(i)
-        lay.forward_host(xh[b], oh, device=local)
+        host_step(lay, xh[b])
     e1.record(st)
     torch.cuda.synchronize()
     barrier()

@@ -278,6 +278,36 @@ mr_status mr_moe_layer_forward_host(mr_ctx* ctx, const mr_moe_layer* layer,
                                     uint16_t* out_host, int32_t* ids_host,
                                     void* stream);
 
+/* ------------------------------------------------------ expert parallel
+ * Routed experts sharded across `world` ranks, one process per GPU: rank r
+ * holds experts [r*E/world, (r+1)*E/world) as stacks, the router and the
+ * shared expert are replicated. The multi-GPU replacement of the reference's
+ * per-process expert backend (RoutedExpertBackend.gather,
+ * Sources/ModelAdapters/Operators/MoE.swift:22-51), which has no multi-GPU
+ * form. One forward = NCCL all-gather of the ranks' tokens, the router over
+ * all of them (identical on every rank), this rank's experts' GEMVs over the
+ * pairs routed to them, per-token partial sums, NCCL reduce-scatter back to
+ * the tokens' home ranks, then the shared expert and the combine there.
+ * NCCL (libnccl.so.2) is loaded when the first group is created. */
+typedef struct mr_ep mr_ep;
+#define MR_EP_ID_BYTES 128
+
+/* A new group id (one rank creates it; the host gives its bytes to all). */
+mr_status mr_ep_unique_id(void* id);
+/* Join the group with this rank's context (its device). Collective: blocks
+ * until every rank has joined. */
+mr_status mr_ep_create(mr_ctx* ctx, const void* id, int rank, int world, mr_ep** out);
+mr_status mr_ep_destroy(mr_ep* ep);
+/* Expert-parallel mr_moe_layer_forward. layer->gate/up/down are this rank's
+ * E/world experts (experts == router.experts / world, stacks only);
+ * everything else as mr_moe_layer_forward. Every rank passes the same
+ * `tokens` T; out [T, H] and ids_out [T, k] (optional) are this rank's
+ * tokens. Results equal mr_moe_layer_forward over all ranks' tokens on one
+ * GPU up to fp32 summation order of the routed slots. */
+mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* layer,
+                                  const uint16_t* x, int64_t tokens, uint16_t* out,
+                                  int32_t* ids_out, void* stream);
+
 /* ----------------------------------------------------------- profiling
  * CUDA-event timing of the kernels mr_moe_layer_forward launches (off by
  * default; the events are recorded on the caller's stream around each

@@ -8,6 +8,9 @@
 #include <mutex>
 #include <string>
 
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include "mr_launch.h"
 #include "mr_router.cuh"
 
@@ -798,7 +801,8 @@ static LogitsShape logits_shape(const mr_ctx* ctx, int64_t T, int E, int64_t H) 
 static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
                              const mr_router_config* c, int32_t* ids, float* weights,
                              float* margins, float* logits_out, bool plan, int* nseg, int4* segs,
-                             int* cols, int seg_cols, cudaStream_t s) {
+                             int* cols, int seg_cols, cudaStream_t s, int plan_base = 0,
+                             int plan_experts = -1, bool foreign_ok = false) {
   TopkParams tp{};
   tp.part = part;
   tp.ks = ks;
@@ -816,8 +820,12 @@ static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
   tp.logits_out = logits_out;
   tp.error = ctx->d_error;
   tp.build_plan = plan ? 1 : 0;
-  tp.plan = PlanParams{ids, (int)(T * c->top_k), c->experts, nseg, segs, cols, ctx->d_error,
-                       seg_cols};
+  tp.plan = PlanParams{ids,     (int)(T * c->top_k),
+                       plan_experts < 0 ? c->experts : plan_experts,
+                       nseg,    segs,
+                       cols,    ctx->d_error,
+                       seg_cols, plan_base,
+                       foreign_ok ? 1 : 0};
   tp.counter = ctx->d_counters + (kMaxCounters - 1);
   const int grid = (int)((T + 7) / 8);
   const int epl = (c->experts + 31) / 32;
@@ -900,6 +908,201 @@ mr_status mr_ctx_reserve(mr_ctx* ctx, int64_t max_tokens, int32_t top_k, int32_t
   return ensure_workspace(ctx, bytes);
 }
 
+}  // extern "C"
+
+namespace mr {
+
+// Plan of the routed GEMV launches built by the top-k kernel: segments of at
+// most seg_cols columns per expert; with foreign_ok, ids outside
+// [base, base + experts) belong to other ranks and are left out.
+struct RoutePlan {
+  int* nseg;
+  int4* segs;
+  int* cols;
+  int seg_cols;
+  int base;
+  int experts;
+  bool foreign_ok;
+};
+
+// Router logits (fused with the activation prep: permuted x and group sums),
+// then scores, top-k, weights and the routing plan.
+static mr_status route_tokens(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x, int64_t T,
+                              const LogitsShape& ls, float* part, uint16_t* xperm, float* xsum,
+                              int32_t* ids, float* wts, float* margins, const RoutePlan& rp,
+                              cudaStream_t s) {
+  const int E = L->router.experts;
+  const int64_t H = L->hidden;
+  LogitsParams lp{};
+  lp.x = x;
+  lp.w = L->router_w;
+  lp.T = (int)T;
+  lp.E = E;
+  lp.H = H;
+  lp.mtiles = ls.mtiles;
+  lp.tblocks = ls.tblocks;
+  lp.ks = ls.ks;
+  lp.kchunk = ls.kchunk;
+  lp.part = part;
+  lp.logit_blocks = ls.blocks;
+  lp.prep = PrepParams{x, T, H, L->gate.bits, xperm, xsum};
+  lp.do_prep = 1;
+  const int64_t chunks = T * (H / 16);
+  const int prep_blocks = (int)std::min<int64_t>((chunks + 127) / 128, 2 * ctx->sm_count);
+  {
+    ProfScope ps(ctx, MR_KERNEL_ROUTER_LOGITS, s);
+    logits_kernel<<<ls.blocks + prep_blocks, 128, 0, s>>>(lp);
+  }
+  mr_status st = cuda_check(ctx, cudaGetLastError(), "logits_kernel");
+  if (st) return st;
+  ProfScope ps(ctx, MR_KERNEL_TOPK_PLAN, s);
+  return topk_launch(ctx, part, ls.kq, T, &L->router, ids, wts, margins, nullptr, true, rp.nseg,
+                     rp.segs, rp.cols, rp.seg_cols, s, rp.base, rp.experts, rp.foreign_ok);
+}
+
+// One K1 (gate/up + SwiGLU -> h, hsum) and K2 (down -> per-slot partials)
+// pass over a routing plan and/or the shared expert.
+struct ExpertsRun {
+  const uint16_t* xperm;  // activation rows (permuted) [*, H]
+  const float* xsum;      // their group sums
+  int64_t tokens;         // token rows (tcgen05 dense mode)
+  int64_t shared_tokens;  // shared expert over rows 0 .. shared_tokens-1 (0: none)
+  int64_t Tk;             // routed columns; column v reads row v / k
+  int k;
+  const int* nseg;        // device count of routed segments
+  const int4* segs;
+  const int* cols;
+  int64_t max_seg;
+  int seg_cols;
+  const float* wts;       // routing weights per routed column
+  uint16_t* h;            // [Tk + 2 * shared_tokens, I]
+  float* hsum;
+  float* part2;           // [Tk + 2 * shared_tokens, H] f32
+  bool um, um_dense;      // tcgen05 kernels (maps encoded by the caller)
+  const UmMaps* um1;
+  const UmMaps* um2;
+};
+
+static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRun& r,
+                             cudaStream_t s) {
+  const int E = L->gate.experts;
+  const int64_t H = L->hidden, I = L->inter;
+  const bool has_shared = r.shared_tokens > 0 && L->shared_inter > 0;
+  const int64_t T = r.shared_tokens;
+  const int seg_cols = r.seg_cols;
+  mr_status st;
+  // K1: gate/up dequant-GEMV + SwiGLU (+ routing weight) -> h, hsum
+  GemvParams g{};
+  if (L->expert_table) {
+    g.src_a = ExpertSource{nullptr, nullptr, nullptr, 0, 0, L->expert_table, 0};
+    g.src_b = ExpertSource{nullptr, nullptr, nullptr, 0, 0, L->expert_table, 1};
+  } else {
+    g.src_a = stack_source(L->gate, 0);
+    g.src_b = stack_source(L->up, 1);
+  }
+  if (has_shared) {
+    g.sh_a = stack_source(L->shared_gate, 0);
+    g.sh_b = stack_source(L->shared_up, 1);
+  } else {
+    g.sh_a = g.src_a;
+    g.sh_b = g.src_b;
+  }
+  g.rows = I;
+  g.in = H;
+  g.n_routed_segments = r.nseg;
+  g.segments = r.segs;
+  g.cols = r.cols;
+  g.shared_segments = has_shared ? (int)((T + seg_cols - 1) / seg_cols) : 0;
+  g.seg_cols = seg_cols;
+  g.shared_cols = has_shared ? (int)T : 0;
+  g.Tk = (int)r.Tk;
+  g.in_div = r.k;
+  g.shared_in_off = (int)r.Tk;
+  g.xperm = r.xperm;
+  g.xsum = r.xsum;
+  g.xsum_parts = 1;
+  g.error = ctx->d_error;
+  g.out_bf16 = r.h;
+  g.hsum = r.hsum;
+  g.weights = r.wts;
+  g.weight_after_down = L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0;
+  g.swiglu_limit = L->swiglu_limit;
+  g.h_bits = L->down.bits;
+  g.shared_lo_off = (int)T;
+  const int bits = L->gate.bits, sd = L->gate.scale_dtype;
+  const bool table = L->expert_table != nullptr;
+  const bool tma1 = use_tma(ctx, tma_layout_ok(H, &L->gate, table) &&
+                                     tma_layout_ok(H, &L->up, table) &&
+                                     (!has_shared || (tma_layout_ok(H, &L->shared_gate, false) &&
+                                                      tma_layout_ok(H, &L->shared_up, false))));
+  const int nt = seg_cols / 8;
+  g.um_dense = r.um_dense ? 1 : 0;
+  g.sh_row0 = 0;
+  g.h_by_pos = r.um ? 1 : 0;
+  g.T = (int)r.tokens;
+  {
+    ProfScope ps(ctx, MR_KERNEL_GATE_UP, s);
+    const MapSpec maps[4] = {{&L->gate, E}, {&L->up, E},
+                             {has_shared ? &L->shared_gate : nullptr, 1},
+                             {has_shared ? &L->shared_up : nullptr, 1}};
+    st = r.um ? cuda_check(ctx, run_umma(ctx, g, r.max_seg, *r.um1, bits, sd, EPI_SWIGLU, s),
+                           "gemv_umma(swiglu)")
+              : cuda_check(ctx, run_gemv(ctx, g, r.max_seg, tma1, maps, bits, sd, EPI_SWIGLU, nt,
+                                         s),
+                           "gemv(swiglu)");
+  }
+  if (st) return st;
+
+  // K2: down dequant-GEMV -> per-slot partials
+  GemvParams d{};
+  if (L->expert_table) {
+    d.src_a = ExpertSource{nullptr, nullptr, nullptr, 0, 0, L->expert_table, 2};
+  } else {
+    d.src_a = stack_source(L->down, 2);
+  }
+  d.src_b = d.src_a;
+  d.sh_a = has_shared ? stack_source(L->shared_down, 2) : d.src_a;
+  d.sh_b = d.sh_a;
+  d.rows = H;
+  d.in = I;
+  d.n_routed_segments = r.nseg;
+  d.segments = r.segs;
+  d.cols = r.cols;
+  d.shared_segments = has_shared ? (int)((2 * T + seg_cols - 1) / seg_cols) : 0;
+  d.seg_cols = seg_cols;
+  d.shared_cols = has_shared ? (int)(2 * T) : 0;
+  d.Tk = (int)r.Tk;
+  d.in_div = 1;
+  d.shared_in_off = 0;
+  d.xperm = r.h;
+  d.xsum = r.hsum;
+  d.xsum_parts = 2;
+  d.error = ctx->d_error;
+  d.part = r.part2;
+  d.weights = r.wts;
+  d.weight_after_down = g.weight_after_down;
+  d.counters = ctx->d_counters;
+  d.T = (int)T;
+  d.k = r.k;
+  d.has_shared = has_shared ? 1 : 0;
+  const bool tma2 = use_tma(ctx, tma_layout_ok(I, &L->down, table) &&
+                                     (!has_shared || tma_layout_ok(I, &L->shared_down, false)));
+  d.um_dense = 0;
+  d.sh_row0 = (int)r.Tk;
+  ProfScope ps(ctx, MR_KERNEL_DOWN_COMBINE, s);
+  const MapSpec maps[4] = {{&L->down, E}, {nullptr, 0},
+                           {has_shared ? &L->shared_down : nullptr, 1}, {nullptr, 0}};
+  return r.um ? cuda_check(ctx, run_umma(ctx, d, r.max_seg, *r.um2, bits, sd, EPI_PARTIAL, s),
+                           "gemv_umma(down)")
+              : cuda_check(ctx, run_gemv(ctx, d, r.max_seg, tma2, maps, bits, sd, EPI_PARTIAL, nt,
+                                         s),
+                           "gemv(down)");
+}
+
+}  // namespace mr
+
+extern "C" {
+
 mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x,
                                int64_t T, uint16_t* out, int32_t* ids_out, float* weights_out,
                                float* margins_out, void* stream) {
@@ -980,36 +1183,12 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
          encode_umma(ctx, m2, EPI_PARTIAL, I, ActSpec{h, R, hsum}, ActSpec{h, R, hsum}, &um2);
   }
 
-  // K0a: router logits (+ permuted input for the gate/up GEMV)
-  LogitsParams lp{};
-  lp.x = x;
-  lp.w = L->router_w;
-  lp.T = (int)T;
-  lp.E = E;
-  lp.H = H;
-  lp.mtiles = ls.mtiles;
-  lp.tblocks = ls.tblocks;
-  lp.ks = ls.ks;
-  lp.kchunk = ls.kchunk;
-  lp.part = part;
-  lp.logit_blocks = ls.blocks;
-  lp.prep = PrepParams{x, T, H, L->gate.bits, xperm, xsum};
-  lp.do_prep = 1;
-  const int64_t chunks = T * (H / 16);
-  const int prep_blocks = (int)std::min<int64_t>((chunks + 127) / 128, 2 * ctx->sm_count);
+  // K0a + K0b: router logits (+ permuted input), top-k, routing plan
   {
-    ProfScope ps(ctx, MR_KERNEL_ROUTER_LOGITS, s);
-    logits_kernel<<<ls.blocks + prep_blocks, 128, 0, s>>>(lp);
+    const RoutePlan rp{nseg, segs, cols, seg_cols, 0, E, false};
+    if ((st = route_tokens(ctx, L, x, T, ls, part, xperm, xsum, ids, wts, margins_out, rp, s)))
+      return st;
   }
-  if ((st = cuda_check(ctx, cudaGetLastError(), "logits_kernel"))) return st;
-
-  // K0b: scores, top-k, weights; the last CTA builds the routing plan
-  {
-    ProfScope ps(ctx, MR_KERNEL_TOPK_PLAN, s);
-    st = topk_launch(ctx, part, ls.kq, T, &L->router, ids, wts, margins_out, nullptr, true, nseg,
-                     segs, cols, seg_cols, s);
-  }
-  if (st) return st;
   if (um && !um_dense) {
     // routed activation rows in plan order for the tcgen05 gate/up launch
     const int64_t n = Tk * (H / 8 + H / kGroup);
@@ -1018,118 +1197,33 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
     if ((st = cuda_check(ctx, cudaGetLastError(), "gather_act_kernel"))) return st;
   }
 
-  // K1: gate/up dequant-GEMV + SwiGLU (+ routing weight) -> h, hsum
-  GemvParams g{};
-  if (L->expert_table) {
-    g.src_a = ExpertSource{nullptr, nullptr, nullptr, 0, 0, L->expert_table, 0};
-    g.src_b = ExpertSource{nullptr, nullptr, nullptr, 0, 0, L->expert_table, 1};
-  } else {
-    g.src_a = stack_source(L->gate, 0);
-    g.src_b = stack_source(L->up, 1);
-  }
-  if (has_shared) {
-    g.sh_a = stack_source(L->shared_gate, 0);
-    g.sh_b = stack_source(L->shared_up, 1);
-  } else {
-    g.sh_a = g.src_a;
-    g.sh_b = g.src_b;
-  }
-  g.rows = I;
-  g.in = H;
-  g.n_routed_segments = nseg;
-  g.segments = segs;
-  g.cols = cols;
-  g.shared_segments = has_shared ? (int)((T + seg_cols - 1) / seg_cols) : 0;
-  g.seg_cols = seg_cols;
-  g.shared_cols = has_shared ? (int)T : 0;
-  g.Tk = (int)Tk;
-  g.in_div = k;
-  g.shared_in_off = (int)Tk;
-  g.xperm = xperm;
-  g.xsum = xsum;
-  g.xsum_parts = 1;
-  g.error = ctx->d_error;
-  g.out_bf16 = h;
-  g.hsum = hsum;
-  g.weights = wts;
-  g.weight_after_down = L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0;
-  g.swiglu_limit = L->swiglu_limit;
-  g.h_bits = L->down.bits;
-  g.shared_lo_off = (int)T;
-  const int bits = L->gate.bits, sd = L->gate.scale_dtype;
-  const bool table = L->expert_table != nullptr;
-  const bool tma1 = use_tma(ctx, tma_layout_ok(H, &L->gate, table) &&
-                                     tma_layout_ok(H, &L->up, table) &&
-                                     (!has_shared || (tma_layout_ok(H, &L->shared_gate, false) &&
-                                                      tma_layout_ok(H, &L->shared_up, false))));
-  const int nt = seg_cols / 8;
-  g.um_dense = um_dense ? 1 : 0;
-  g.sh_row0 = 0;
-  g.h_by_pos = um ? 1 : 0;
-  g.T = (int)T;
-  {
-    ProfScope ps(ctx, MR_KERNEL_GATE_UP, s);
-    const MapSpec maps[4] = {{&L->gate, E}, {&L->up, E},
-                             {has_shared ? &L->shared_gate : nullptr, 1},
-                             {has_shared ? &L->shared_up : nullptr, 1}};
-    st = um ? cuda_check(ctx, run_umma(ctx, g, max_seg, um1, bits, sd, EPI_SWIGLU, s),
-                         "gemv_umma(swiglu)")
-            : cuda_check(ctx, run_gemv(ctx, g, max_seg, tma1, maps, bits, sd, EPI_SWIGLU, nt, s),
-                         "gemv(swiglu)");
-  }
-  if (st) return st;
-
-  // K2: down dequant-GEMV -> per-slot partials; the last CTA of each row
-  // block sums slots in order (+ shared) into out
-  GemvParams d{};
-  if (L->expert_table) {
-    d.src_a = ExpertSource{nullptr, nullptr, nullptr, 0, 0, L->expert_table, 2};
-  } else {
-    d.src_a = stack_source(L->down, 2);
-  }
-  d.src_b = d.src_a;
-  d.sh_a = has_shared ? stack_source(L->shared_down, 2) : d.src_a;
-  d.sh_b = d.sh_a;
-  d.rows = H;
-  d.in = I;
-  d.n_routed_segments = nseg;
-  d.segments = segs;
-  d.cols = cols;
-  d.shared_segments = has_shared ? (int)((2 * T + seg_cols - 1) / seg_cols) : 0;
-  d.seg_cols = seg_cols;
-  d.shared_cols = has_shared ? (int)(2 * T) : 0;
-  d.Tk = (int)Tk;
-  d.in_div = 1;
-  d.shared_in_off = 0;
-  d.xperm = h;
-  d.xsum = hsum;
-  d.xsum_parts = 2;
-  d.error = ctx->d_error;
-  d.part = part2;
-  d.weights = wts;
-  d.weight_after_down = g.weight_after_down;
-  d.counters = ctx->d_counters;
-  d.T = (int)T;
-  d.k = k;
-  d.has_shared = has_shared ? 1 : 0;
-  d.out = out;
-  const bool tma2 = use_tma(ctx, tma_layout_ok(I, &L->down, table) &&
-                                     (!has_shared || tma_layout_ok(I, &L->shared_down, false)));
-  d.um_dense = 0;
-  d.sh_row0 = (int)Tk;
-  ProfScope ps(ctx, MR_KERNEL_DOWN_COMBINE, s);
-  const MapSpec maps[4] = {{&L->down, E}, {nullptr, 0},
-                           {has_shared ? &L->shared_down : nullptr, 1}, {nullptr, 0}};
-  if ((st = um ? cuda_check(ctx, run_umma(ctx, d, max_seg, um2, bits, sd, EPI_PARTIAL, s),
-                            "gemv_umma(down)")
-               : cuda_check(ctx, run_gemv(ctx, d, max_seg, tma2, maps, bits, sd, EPI_PARTIAL, nt,
-                                          s),
-                            "gemv(down)")))
-    return st;
+  // K1 + K2: gate/up + SwiGLU -> h; down -> per-slot partials (+ shared)
+  ExpertsRun r{};
+  r.xperm = xperm;
+  r.xsum = xsum;
+  r.tokens = T;
+  r.shared_tokens = has_shared ? T : 0;
+  r.Tk = Tk;
+  r.k = k;
+  r.nseg = nseg;
+  r.segs = segs;
+  r.cols = cols;
+  r.max_seg = max_seg;
+  r.seg_cols = seg_cols;
+  r.wts = wts;
+  r.h = h;
+  r.hsum = hsum;
+  r.part2 = part2;
+  r.um = um;
+  r.um_dense = um_dense;
+  r.um1 = &um1;
+  r.um2 = &um2;
+  if ((st = run_experts(ctx, L, r, s))) return st;
   const int64_t n_out = T * H;
   const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 4 * ctx->sm_count));
-  combine_kernel<<<cgrid, 256, 0, s>>>(part2, wts, (int)T, k, H, d.weight_after_down,
-                                        d.has_shared, out);
+  combine_kernel<<<cgrid, 256, 0, s>>>(part2, wts, (int)T, k, H,
+                                        L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0,
+                                        has_shared ? 1 : 0, out);
   return cuda_check(ctx, cudaGetLastError(), "combine_kernel");
 }
 
@@ -1460,3 +1554,280 @@ extern "C" mr_status mr_affine_gather_mm_noalloc(const uint16_t* x, int64_t toke
   set_msg(msg, msg_len, st ? why : std::string());
   return st;
 }
+
+// ------------------------------------------------------- expert parallel
+
+namespace {
+
+// NCCL entry points, resolved from libnccl.so.2 on first use (a process that
+// already loaded NCCL, e.g. through torch, shares that copy).
+struct NcclApi {
+  decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+  decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+  decltype(&ncclCommDestroy) comm_destroy = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclReduceScatter) reduce_scatter = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+  bool ok = false;
+};
+
+const NcclApi& nccl_api() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.get_unique_id = reinterpret_cast<decltype(&ncclGetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank =
+        reinterpret_cast<decltype(&ncclCommInitRank)>(dlsym(h, "ncclCommInitRank"));
+    api.comm_destroy = reinterpret_cast<decltype(&ncclCommDestroy)>(dlsym(h, "ncclCommDestroy"));
+    api.all_gather = reinterpret_cast<decltype(&ncclAllGather)>(dlsym(h, "ncclAllGather"));
+    api.reduce_scatter =
+        reinterpret_cast<decltype(&ncclReduceScatter)>(dlsym(h, "ncclReduceScatter"));
+    api.error_string =
+        reinterpret_cast<decltype(&ncclGetErrorString)>(dlsym(h, "ncclGetErrorString"));
+    api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_gather &&
+             api.reduce_scatter && api.error_string;
+  });
+  return api;
+}
+
+mr_status nccl_check(mr_ctx* ctx, ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return MR_OK;
+  return fail(ctx, MR_ERR_NCCL, std::string(what) + ": " + nccl_api().error_string(r));
+}
+
+// Per token, the sum over its routed slots whose expert lives on this rank
+// (ids in [base, base + local)), in slot order; other slots contribute 0.
+__global__ void ep_partial_kernel(const float* __restrict__ part, const int32_t* __restrict__ ids,
+                                  const float* __restrict__ weights, int T, int k, int64_t H,
+                                  int base, int local, int weight_after_down,
+                                  float* __restrict__ y) {
+  const int64_t n = (int64_t)T * H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / H);
+    const int64_t row = i - (int64_t)t * H;
+    float s = 0.0f;
+    for (int j = 0; j < k; ++j) {
+      const int p = t * k + j;
+      const int e = __ldg(ids + p) - base;
+      if (e < 0 || e >= local) continue;
+      const float v = __ldg(part + (int64_t)p * H + row);
+      s += weight_after_down ? v * __ldg(weights + p) : v;
+    }
+    y[i] = s;
+  }
+}
+
+// out = routed (bf16-rounded sum for weight-before-down, as the one-GPU
+// combine) + the shared expert's hi + lo rows.
+__global__ void ep_combine_kernel(const float* __restrict__ y, const float* __restrict__ part_sh,
+                                  int T, int64_t H, int weight_after_down, int has_shared,
+                                  uint16_t* __restrict__ out) {
+  const int64_t n = (int64_t)T * H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float s = weight_after_down ? y[i] : bf16_round(y[i]);
+    if (has_shared) {
+      const int t = (int)(i / H);
+      const int64_t row = i - (int64_t)t * H;
+      s = s + (part_sh[(int64_t)t * H + row] + part_sh[(int64_t)(T + t) * H + row]);
+    }
+    out[i] = f32_to_bf16_bits(s);
+  }
+}
+
+}  // namespace
+
+struct mr_ep {
+  ncclComm_t comm = nullptr;
+  int rank = 0;
+  int world = 1;
+  int device = 0;
+};
+
+extern "C" {
+
+mr_status mr_ep_unique_id(void* id) {
+  if (!id) return MR_ERR_INVALID_ARGUMENT;
+  const NcclApi& api = nccl_api();
+  if (!api.ok) return MR_ERR_NCCL;
+  ncclUniqueId uid;
+  if (api.get_unique_id(&uid) != ncclSuccess) return MR_ERR_NCCL;
+  memcpy(id, &uid, sizeof(uid));
+  return MR_OK;
+}
+
+mr_status mr_ep_create(mr_ctx* ctx, const void* id, int rank, int world, mr_ep** out) {
+  if (!ctx || !id || !out || world < 1 || rank < 0 || rank >= world)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "expert-parallel group needs 0 <= rank < world");
+  *out = nullptr;
+  const NcclApi& api = nccl_api();
+  if (!api.ok) return fail(ctx, MR_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  mr_status st = cuda_check(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  if (st) return st;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  mr_ep* ep = new mr_ep;
+  ep->rank = rank;
+  ep->world = world;
+  ep->device = ctx->device;
+  if ((st = nccl_check(ctx, api.comm_init_rank(&ep->comm, world, uid, rank), "ncclCommInitRank"))) {
+    delete ep;
+    return st;
+  }
+  *out = ep;
+  return MR_OK;
+}
+
+mr_status mr_ep_destroy(mr_ep* ep) {
+  if (!ep) return MR_OK;
+  mr_status st = MR_OK;
+  if (ep->comm && nccl_api().comm_destroy(ep->comm) != ncclSuccess) st = MR_ERR_NCCL;
+  delete ep;
+  return st;
+}
+
+mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
+                                  const uint16_t* x, int64_t T, uint16_t* out, int32_t* ids_out,
+                                  void* stream) {
+  if (!ctx || !ep || !L) return fail(ctx, MR_ERR_INVALID_ARGUMENT, "context, group and layer required");
+  const int W = ep->world, rank = ep->rank;
+  const int E = L->router.experts, k = L->router.top_k;
+  if (L->expert_table)
+    return fail(ctx, MR_ERR_UNSUPPORTED, "expert-parallel layers take expert stacks");
+  if (E % W != 0 || L->gate.experts * W != E || L->up.experts * W != E ||
+      L->down.experts * W != E)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "each rank must hold router.experts / world routed experts (gate/up/down stacks)");
+  // validate as the layer it is a shard of
+  mr_moe_layer full = *L;
+  full.gate.experts = full.up.experts = full.down.experts = E;
+  std::string why;
+  mr_status st = validate_layer(&full, why);
+  if (st) return fail(ctx, st, why);
+  if (T <= 0 || !x || !out)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "input must be a non-empty [tokens, hidden] matrix");
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0)
+    return fail(ctx, MR_ERR_UNSUPPORTED, "x must be 16-byte aligned");
+  const int El = E / W, base = rank * El;
+  const int64_t H = L->hidden, I = L->inter;
+  const int64_t NT = T * W, NTk = NT * k;
+  if (NTk > (int64_t)1 << 28) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
+  const bool has_shared = L->shared_inter > 0;
+  const int seg_cols = pick_seg_cols(NT);
+  const int64_t max_seg = std::min<int64_t>(El, NTk) + NTk / seg_cols + 1;
+  const LogitsShape ls = logits_shape(ctx, NT, E, H);
+
+  uint16_t *xall = nullptr, *xperm = nullptr, *h = nullptr, *hs = nullptr;
+  float *part = nullptr, *xsum = nullptr, *wts = nullptr, *hsum = nullptr, *part2 = nullptr;
+  float *ypart = nullptr, *yred = nullptr, *hss = nullptr, *psh = nullptr;
+  int32_t* ids = nullptr;
+  int *nseg = nullptr, *cols = nullptr, *zero = nullptr;
+  int4* segs = nullptr;
+  Bump b{nullptr};
+  for (int pass = 0; pass < 2; ++pass) {
+    b.off = 0;
+    xall = b.take<uint16_t>(NT * H);
+    part = b.take<float>((size_t)ls.kq * NT * E);
+    xperm = b.take<uint16_t>(NT * H);
+    xsum = b.take<float>(NT * (H / kGroup));
+    ids = b.take<int32_t>(NTk);
+    wts = b.take<float>(NTk);
+    nseg = b.take<int>(4);
+    zero = b.take<int>(4);
+    segs = b.take<int4>(max_seg);
+    cols = b.take<int>(NTk);
+    h = b.take<uint16_t>(NTk * I);
+    hsum = b.take<float>(NTk * (I / 32));
+    part2 = b.take<float>(NTk * H);
+    ypart = b.take<float>(NT * H);
+    yred = b.take<float>(T * H);
+    hs = b.take<uint16_t>(2 * T * I);
+    hss = b.take<float>(2 * T * (I / 32));
+    psh = b.take<float>(2 * T * H);
+    if (pass == 0) {
+      if ((st = ensure_workspace(ctx, b.off))) return st;
+      b.base = reinterpret_cast<char*>(ctx->ws);
+    }
+  }
+  cudaStream_t s = as_stream(stream);
+  const NcclApi& api = nccl_api();
+
+  // every rank's tokens, in rank order
+  if ((st = nccl_check(ctx, api.all_gather(x, xall, (size_t)(T * H), ncclBfloat16, ep->comm, s),
+                       "ncclAllGather")))
+    return st;
+  // router over all tokens (the same on every rank); plan of this rank's experts
+  const RoutePlan rp{nseg, segs, cols, seg_cols, base, El, true};
+  if ((st = route_tokens(ctx, L, xall, NT, ls, part, xperm, xsum, ids, wts, nullptr, rp, s)))
+    return st;
+  // this rank's experts over the pairs routed to them
+  ExpertsRun r{};
+  r.xperm = xperm;
+  r.xsum = xsum;
+  r.tokens = NT;
+  r.shared_tokens = 0;
+  r.Tk = NTk;
+  r.k = k;
+  r.nseg = nseg;
+  r.segs = segs;
+  r.cols = cols;
+  r.max_seg = max_seg;
+  r.seg_cols = seg_cols;
+  r.wts = wts;
+  r.h = h;
+  r.hsum = hsum;
+  r.part2 = part2;
+  if ((st = run_experts(ctx, L, r, s))) return st;
+  const int wad = L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0;
+  {
+    const int64_t n = NT * H;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
+    ep_partial_kernel<<<grid, 256, 0, s>>>(part2, ids, wts, (int)NT, k, H, base, El, wad, ypart);
+    if ((st = cuda_check(ctx, cudaGetLastError(), "ep_partial_kernel"))) return st;
+  }
+  // each token's sum over all ranks, back on its home rank
+  if ((st = nccl_check(ctx,
+                       api.reduce_scatter(ypart, yred, (size_t)(T * H), ncclFloat32, ncclSum,
+                                          ep->comm, s),
+                       "ncclReduceScatter")))
+    return st;
+  // shared expert over this rank's own tokens
+  if (has_shared) {
+    if ((st = cuda_check(ctx, cudaMemsetAsync(zero, 0, 4 * sizeof(int), s), "clear count")))
+      return st;
+    ExpertsRun sh{};
+    sh.xperm = xperm + (int64_t)rank * T * H;
+    sh.xsum = xsum + (int64_t)rank * T * (H / kGroup);
+    sh.tokens = T;
+    sh.shared_tokens = T;
+    sh.Tk = 0;
+    sh.k = k;
+    sh.nseg = zero;
+    sh.segs = segs;
+    sh.cols = cols;
+    sh.max_seg = 0;
+    sh.seg_cols = seg_cols;
+    sh.wts = wts;
+    sh.h = hs;
+    sh.hsum = hss;
+    sh.part2 = psh;
+    if ((st = run_experts(ctx, L, sh, s))) return st;
+  }
+  {
+    const int64_t n = T * H;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
+    ep_combine_kernel<<<grid, 256, 0, s>>>(yred, psh, (int)T, H, wad, has_shared ? 1 : 0, out);
+    if ((st = cuda_check(ctx, cudaGetLastError(), "ep_combine_kernel"))) return st;
+  }
+  if (ids_out)
+    st = cuda_check(ctx,
+                    cudaMemcpyAsync(ids_out, ids + (int64_t)rank * T * k, T * k * sizeof(int32_t),
+                                    cudaMemcpyDeviceToDevice, s),
+                    "copy ids");
+  return st;
+}
+
+}  // extern "C"

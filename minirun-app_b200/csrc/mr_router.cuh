@@ -188,7 +188,9 @@ struct PlanParams {
   int4* segments;
   int* cols;
   unsigned* error;
-  int seg_cols;  // columns per segment (8 or 16)
+  int seg_cols;     // columns per segment (8 or 16)
+  int expert_base;  // ids are global; expert e here is id expert_base + e
+  int foreign_ok;   // ids outside [base, base + E) belong to other ranks: skipped
 };
 
 template <int NTHREADS>
@@ -201,10 +203,10 @@ __device__ void build_plan_cta(const PlanParams& p) {
   for (int e = tid; e < p.E; e += NTHREADS) cnt[e] = 0;
   __syncthreads();
   for (int i = tid; i < p.Tk; i += NTHREADS) {
-    const int e = __ldcg(p.ids + i);
+    const int e = __ldcg(p.ids + i) - p.expert_base;
     if (e >= 0 && e < p.E) {
       atomicAdd(&cnt[e], 1);
-    } else {
+    } else if (!p.foreign_ok) {
       atomicOr(p.error, MR_DEVERR_BAD_EXPERT_ID);
     }
   }
@@ -265,7 +267,7 @@ __device__ void build_plan_cta(const PlanParams& p) {
   for (int e = tid; e < p.E; e += NTHREADS) cnt[e] = 0;
   __syncthreads();
   for (int i = tid; i < p.Tk; i += NTHREADS) {
-    const int e = __ldcg(p.ids + i);
+    const int e = __ldcg(p.ids + i) - p.expert_base;
     if (e >= 0 && e < p.E) {
       const int pos = atomicAdd(&cnt[e], 1);
       p.cols[colofs[e] + pos] = i;

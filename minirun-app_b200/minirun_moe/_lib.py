@@ -89,6 +89,11 @@ SIGNATURES = {
                                        vp, vp]),
     "mr_moe_layer_forward_host": (C.c_int, [vp, C.POINTER(mr_moe_layer), vp, C.c_int64, vp, vp,
                                             vp]),
+    "mr_ep_unique_id": (C.c_int, [vp]),
+    "mr_ep_create": (C.c_int, [vp, vp, C.c_int, C.c_int, C.POINTER(vp)]),
+    "mr_ep_destroy": (C.c_int, [vp]),
+    "mr_moe_layer_forward_ep": (C.c_int, [vp, vp, C.POINTER(mr_moe_layer), vp, C.c_int64, vp, vp,
+                                          vp]),
     "mr_ctx_profile": (C.c_int, [vp, C.c_int]),
     "mr_ctx_profile_read": (C.c_int, [vp, C.POINTER(C.c_double), C.POINTER(C.c_int64), C.c_int]),
     "mr_synth_label": (C.c_uint64, [C.c_uint32] * 4),

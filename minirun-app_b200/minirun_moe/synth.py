@@ -19,6 +19,7 @@ import torch
 
 from . import _lib as L
 from .bridge import AffineWeights, Context, _stream
+from .ep import MoELayerShard
 from .moe import MoELayer, RouterConfig
 
 KIND_X, KIND_ROUTER, KIND_CODES, KIND_SCALES, KIND_BIAS = 1, 2, 3, 4, 5
@@ -125,18 +126,29 @@ def zipf_bias(experts: int, beta: float, s: float = 1.1) -> list[float]:
     return [beta * math.log(v / tot) for v in p]
 
 
-def synth_layer(spec: LayerSpec, layer: int = 0, device=None) -> MoELayer:
+def synth_layer(spec: LayerSpec, layer: int = 0, device=None,
+                shard: tuple[int, int] | None = None) -> MoELayer:
+    """The seeded layer; with ``shard=(rank, world)`` only that rank's routed
+    experts [rank*E/world, (rank+1)*E/world) (same seeds as in the full
+    layer), as a MoELayerShard for the expert-parallel forward."""
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
     H, E, I, S = spec.hidden, spec.experts, spec.inter, spec.shared_inter
+    e0, e1 = 0, E
+    if shard is not None:
+        rank, world = shard
+        if E % world:
+            raise ValueError(f"{E} experts do not split over {world} ranks")
+        e0, e1 = rank * E // world, (rank + 1) * E // world
     router_w = torch.empty((E, H), dtype=torch.bfloat16, device=dev)
     synth_normal_bf16(derive(spec.seed, label(layer, KIND_ROUTER, 0, 0)), E * H, 1.0 / 32.0,
                       False, router_w)
-    gate = alloc_affine(E, I, H, spec.bits, spec.group, dev)
-    up = alloc_affine(E, I, H, spec.bits, spec.group, dev)
-    down = alloc_affine(E, H, I, spec.bits, spec.group, dev)
-    for e in range(E):
+    gate = alloc_affine(e1 - e0, I, H, spec.bits, spec.group, dev)
+    up = alloc_affine(e1 - e0, I, H, spec.bits, spec.group, dev)
+    down = alloc_affine(e1 - e0, H, I, spec.bits, spec.group, dev)
+    for e in range(e0, e1):
         for proj, w in ((PROJ_GATE, gate), (PROJ_UP, up), (PROJ_DOWN, down)):
-            fill_affine(spec, layer, e, proj, w.packed[e], w.scales[e], w.biases[e])
+            fill_affine(spec, layer, e, proj, w.packed[e - e0], w.scales[e - e0],
+                        w.biases[e - e0])
     shared = None
     if S > 0:
         sg = alloc_affine(None, S, H, spec.bits, spec.group, dev)
@@ -150,8 +162,11 @@ def synth_layer(spec: LayerSpec, layer: int = 0, device=None) -> MoELayer:
         bias = torch.tensor(zipf_bias(E, spec.zipf_beta), dtype=torch.float32, device=dev)
     router = RouterConfig(E, spec.top_k, spec.scoring, spec.renorm, spec.renorm_eps,
                           spec.routed_scale, bias)
-    return MoELayer(router_w, gate, up, down, router, shared, spec.swiglu_limit,
-                    "after_down" if spec.weight_after_down else "before_down")
+    placement = "after_down" if spec.weight_after_down else "before_down"
+    if shard is not None:
+        return MoELayerShard(shard[1], router_w, gate, up, down, router, shared,
+                             spec.swiglu_limit, placement)
+    return MoELayer(router_w, gate, up, down, router, shared, spec.swiglu_limit, placement)
 
 
 def synth_x(spec: LayerSpec, tokens: int, layer: int = 0, batch: int = 0,

@@ -1,0 +1,64 @@
+"""One rank of the expert-parallel parity check (run by tests/test_ep_gpu.py
+under torchrun). Each rank holds its shard of a seeded layer and the whole
+layer; the expert-parallel forward of its tokens must equal the one-GPU
+forward of all ranks' tokens, restricted to its own rows."""
+import dataclasses
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "minirun-app_b200"))
+import minirun_moe as M  # noqa: E402
+from minirun_moe import synth as S  # noqa: E402
+
+
+def rel_l2(a, b):
+    a = a.float().cpu().numpy().astype(np.float64)
+    b = b.float().cpu().numpy().astype(np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def main():
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import datetime
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    group = M.ExpertGroup(rank, rank, world)
+    cases = [
+        ("config0", S.CONFIGS[0], 4),
+        ("config0_after_down", dataclasses.replace(S.CONFIGS[0], weight_after_down=True), 5),
+        ("config0_no_shared", dataclasses.replace(S.CONFIGS[0], shared_inter=0), 3),
+        ("config1_32e", dataclasses.replace(S.CONFIGS[1], experts=32), 8),
+    ]
+    results = {}
+    for name, spec, T in cases:
+        full = S.synth_layer(spec, layer=1, device=rank)
+        shard = S.synth_layer(spec, layer=1, device=rank, shard=(rank, world))
+        xall = S.synth_x(spec, T * world, layer=1, batch=7, device=rank)
+        x = xall[rank * T:(rank + 1) * T].contiguous()
+        ids = torch.empty((T, spec.top_k), dtype=torch.int32, device=dev)
+        out = group.forward(shard, x, ids=ids)
+        ref, sel = full(xall)
+        torch.cuda.synchronize()
+        mine = ref[rank * T:(rank + 1) * T]
+        results[name] = {
+            "rel_l2": rel_l2(out, mine),
+            "ids_equal": bool(torch.equal(ids, sel.ids[rank * T:(rank + 1) * T].int())),
+            "finite": bool(torch.isfinite(out.float()).all()),
+        }
+        M.Context.get(rank).sync_check()
+    group.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    print("EPRESULT " + json.dumps({"rank": rank, "results": results}), flush=True)
+
+
+if __name__ == "__main__":
+    main()
