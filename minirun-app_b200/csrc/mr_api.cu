@@ -316,7 +316,7 @@ struct ActSpec {
 // Encodes every tensor map of one tcgen05 launch (false: keep the other
 // kernels). maps[0..3] as run_gemv.
 static bool encode_umma(mr_ctx* ctx, const MapSpec* maps, int epi, int64_t width, ActSpec act,
-                        ActSpec act_sh, UmMaps* um) {
+                        ActSpec act_sh, UmMaps* um, int act_rows = kUmN) {
   const int parts = epi == EPI_PARTIAL ? 2 : 1;
   const int64_t swidth = width / kGroup * parts;
   const int box_rows = epi == EPI_SWIGLU ? kUmRows / 2 : kUmRows;
@@ -327,8 +327,8 @@ static bool encode_umma(mr_ctx* ctx, const MapSpec* maps, int epi, int64_t width
   const MapSpec& sb = maps[3].d ? maps[3] : (maps[2].d ? maps[2] : maps[0]);
   ok = ok && encode_matrix(ctx, sa, box_rows, &um->sa_packed, &um->sa_scales, &um->sa_biases);
   ok = ok && encode_matrix(ctx, sb, box_rows, &um->sb_packed, &um->sb_scales, &um->sb_biases);
-  ok = ok && tensor_map(ctx, &um->act, act.base, act.rows, width, kUmN, 4);
-  ok = ok && tensor_map(ctx, &um->act_sh, act_sh.base, act_sh.rows, width, kUmN, 4);
+  ok = ok && tensor_map(ctx, &um->act, act.base, act.rows, width, act_rows, 4);
+  ok = ok && tensor_map(ctx, &um->act_sh, act_sh.base, act_sh.rows, width, act_rows, 4);
   ok = ok && tensor_map(ctx, &um->xs, act.sums, act.rows, swidth, kUmN, 4 + parts);
   ok = ok && tensor_map(ctx, &um->xs_sh, act_sh.sums, act_sh.rows, swidth, kUmN, 4 + parts);
   return ok;
@@ -342,6 +342,16 @@ static cudaError_t run_umma(mr_ctx* ctx, GemvParams g, int64_t max_segments, con
   const int64_t items = (max_segments + g.shared_segments) * g.rb_count;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
   return launch_umma(g, um, bits, sd, epi, grid, s);
+}
+
+// One tcgen05 prefill GEMM over the plan: tiles of 128 weight rows (64 gate
+// + 64 up for SwiGLU) x one segment of <= 128 tokens.
+static cudaError_t run_pf(mr_ctx* ctx, GemvParams g, int64_t max_segments, const UmMaps& um,
+                          int bits, int sd, int epi, cudaStream_t s) {
+  g.rb_count = (int)(epi == EPI_SWIGLU ? g.rows / 64 : (g.rows + kPfRows - 1) / kPfRows);
+  const int64_t items = (max_segments + g.shared_segments) * g.rb_count;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
+  return launch_pf(g, um, bits, sd, epi, grid, s);
 }
 
 // Issues one GEMV over the plan with the chosen implementation.
@@ -978,7 +988,8 @@ struct ExpertsRun {
   uint16_t* h;            // [Tk + 2 * shared_tokens, I]
   float* hsum;
   float* part2;           // [Tk + 2 * shared_tokens, H] f32
-  bool um, um_dense;      // tcgen05 kernels (maps encoded by the caller)
+  bool um, um_dense;      // tcgen05 GEMV kernels (maps encoded by the caller)
+  bool pf;                // tcgen05 prefill GEMM (maps in um1 / um2)
   const UmMaps* um1;
   const UmMaps* um2;
 };
@@ -1038,18 +1049,20 @@ static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRu
   const int nt = seg_cols / 8;
   g.um_dense = r.um_dense ? 1 : 0;
   g.sh_row0 = 0;
-  g.h_by_pos = r.um ? 1 : 0;
+  g.h_by_pos = (r.um || r.pf) ? 1 : 0;
   g.T = (int)r.tokens;
   {
     ProfScope ps(ctx, MR_KERNEL_GATE_UP, s);
     const MapSpec maps[4] = {{&L->gate, E}, {&L->up, E},
                              {has_shared ? &L->shared_gate : nullptr, 1},
                              {has_shared ? &L->shared_up : nullptr, 1}};
-    st = r.um ? cuda_check(ctx, run_umma(ctx, g, r.max_seg, *r.um1, bits, sd, EPI_SWIGLU, s),
-                           "gemv_umma(swiglu)")
-              : cuda_check(ctx, run_gemv(ctx, g, r.max_seg, tma1, maps, bits, sd, EPI_SWIGLU, nt,
-                                         s),
-                           "gemv(swiglu)");
+    st = r.pf   ? cuda_check(ctx, run_pf(ctx, g, r.max_seg, *r.um1, bits, sd, EPI_SWIGLU, s),
+                             "gemm_umma(swiglu)")
+         : r.um ? cuda_check(ctx, run_umma(ctx, g, r.max_seg, *r.um1, bits, sd, EPI_SWIGLU, s),
+                             "gemv_umma(swiglu)")
+                : cuda_check(ctx, run_gemv(ctx, g, r.max_seg, tma1, maps, bits, sd, EPI_SWIGLU,
+                                           nt, s),
+                             "gemv(swiglu)");
   }
   if (st) return st;
 
@@ -1092,11 +1105,13 @@ static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRu
   ProfScope ps(ctx, MR_KERNEL_DOWN_COMBINE, s);
   const MapSpec maps[4] = {{&L->down, E}, {nullptr, 0},
                            {has_shared ? &L->shared_down : nullptr, 1}, {nullptr, 0}};
-  return r.um ? cuda_check(ctx, run_umma(ctx, d, r.max_seg, *r.um2, bits, sd, EPI_PARTIAL, s),
-                           "gemv_umma(down)")
-              : cuda_check(ctx, run_gemv(ctx, d, r.max_seg, tma2, maps, bits, sd, EPI_PARTIAL, nt,
-                                         s),
-                           "gemv(down)");
+  return r.pf   ? cuda_check(ctx, run_pf(ctx, d, r.max_seg, *r.um2, bits, sd, EPI_PARTIAL, s),
+                             "gemm_umma(down)")
+         : r.um ? cuda_check(ctx, run_umma(ctx, d, r.max_seg, *r.um2, bits, sd, EPI_PARTIAL, s),
+                             "gemv_umma(down)")
+                : cuda_check(ctx, run_gemv(ctx, d, r.max_seg, tma2, maps, bits, sd, EPI_PARTIAL,
+                                           nt, s),
+                             "gemv(down)");
 }
 
 }  // namespace mr
@@ -1127,11 +1142,16 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
       (!has_shared || (tma_layout_ok(H, &L->shared_gate, false) &&
                        tma_layout_ok(H, &L->shared_up, false) &&
                        tma_layout_ok(I, &L->shared_down, false)));
-  const bool um_try = ctx->kernel_path == 3 && um_layout;
-  const bool um_dense = T <= kUmN;  // routed activations are the token rows themselves
-  // a routed expert has <= T columns
-  const int seg_cols = um_try ? kUmN : pick_seg_cols(T);
-  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / seg_cols + 1;
+  // prefill-size batches (>= 32 routed columns per expert on average): the
+  // tcgen05 grouped GEMM (4/8-bit codes, whole 256-element stages)
+  const bool pf_try = (ctx->kernel_path == 0 || ctx->kernel_path == 3) && um_layout &&
+                      (L->gate.bits == 4 || L->gate.bits == 8) && L->down.bits == L->gate.bits &&
+                      (!has_shared || L->shared_gate.bits == L->gate.bits) && Tk >= 32 * (int64_t)E;
+  const bool um_try = !pf_try && ctx->kernel_path == 3 && um_layout;
+  const bool um_dense = !pf_try && T <= kUmN;  // routed activations are the token rows
+  // segments per expert of seg_cols columns; the workspace holds the plan of
+  // the narrowest segments, the width is fixed once the kernels are chosen
+  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / pick_seg_cols(T) + 1;
   const LogitsShape ls = logits_shape(ctx, T, E, H);
   if (Tk > (int64_t)1 << 28) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
 
@@ -1145,7 +1165,7 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   Bump b{nullptr};
   for (int pass = 0; pass < 2; ++pass) {
     b.off = 0;
-    if (um_try && !um_dense) {
+    if ((um_try || pf_try) && !um_dense) {
       xg = b.take<uint16_t>(Tk * H);
       xsg = b.take<float>(Tk * (H / kGroup));
     }
@@ -1171,7 +1191,18 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
 
   // tensor maps of both tcgen05 launches, before anything is enqueued
   UmMaps um1, um2;
-  bool um = false;
+  bool um = false, pf = false;
+  if (pf_try) {
+    const MapSpec m1[4] = {{&L->gate, E}, {&L->up, E},
+                           {has_shared ? &L->shared_gate : nullptr, 1},
+                           {has_shared ? &L->shared_up : nullptr, 1}};
+    const MapSpec m2[4] = {{&L->down, E}, {nullptr, 0},
+                           {has_shared ? &L->shared_down : nullptr, 1}, {nullptr, 0}};
+    pf = encode_umma(ctx, m1, EPI_SWIGLU, H, ActSpec{xg, Tk, xsg}, ActSpec{xperm, T, xsum}, &um1,
+                     kPfN) &&
+         encode_umma(ctx, m2, EPI_PARTIAL, I, ActSpec{h, R, hsum}, ActSpec{h, R, hsum}, &um2,
+                     kPfN);
+  }
   if (um_try) {
     const MapSpec m1[4] = {{&L->gate, E}, {&L->up, E},
                            {has_shared ? &L->shared_gate : nullptr, 1},
@@ -1182,6 +1213,7 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
     um = encode_umma(ctx, m1, EPI_SWIGLU, H, xa, ActSpec{xperm, T, xsum}, &um1) &&
          encode_umma(ctx, m2, EPI_PARTIAL, I, ActSpec{h, R, hsum}, ActSpec{h, R, hsum}, &um2);
   }
+  const int seg_cols = pf ? kPfN : um ? kUmN : pick_seg_cols(T);
 
   // K0a + K0b: router logits (+ permuted input), top-k, routing plan
   {
@@ -1189,7 +1221,7 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
     if ((st = route_tokens(ctx, L, x, T, ls, part, xperm, xsum, ids, wts, margins_out, rp, s)))
       return st;
   }
-  if (um && !um_dense) {
+  if ((um && !um_dense) || pf) {
     // routed activation rows in plan order for the tcgen05 gate/up launch
     const int64_t n = Tk * (H / 8 + H / kGroup);
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8 * ctx->sm_count));
@@ -1216,6 +1248,7 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   r.part2 = part2;
   r.um = um;
   r.um_dense = um_dense;
+  r.pf = pf;
   r.um1 = &um1;
   r.um2 = &um2;
   if ((st = run_experts(ctx, L, r, s))) return st;

@@ -1,0 +1,430 @@
+// mr_gemm_umma.cuh — prefill-size grouped affine dequant-GEMM on the
+// 5th-generation tensor cores (tcgen05, A operand and accumulators in TMEM).
+//
+// For batches where an expert sees many tokens the work is a grouped GEMM:
+// per expert, Y[rows x tokens] = W[rows x K] . X[K x tokens]. One CTA per SM
+// loops over tiles (segment of <= 128 tokens sharing an expert) x (128
+// weight rows: 128 plain rows, or 64 gate + 64 up rows for SwiGLU):
+//   - warp 0, one lane: TMA loads, per stage (one 128-byte box column of codes
+//     = 4 groups at 4 bits, 2 at 8 bits), of the packed codes and, per group,
+//     the 128 x 64 bf16 activation tile (128-byte swizzle);
+//   - 8 worker warps (2 per TMEM lane quadrant, each half of a stage's
+//     groups): each thread owns one weight row = one TMEM lane and
+//     dequantises its row's codes to bf16 weights s*q + z (one rounding, as
+//     MLX's own large-batch quantised matmul does) into a TMEM A buffer
+//     (tcgen05.st); scales and biases come from global memory one stage
+//     ahead;
+//   - warp 1, one lane: per stage, 4 tcgen05.mma per group (M 128, N 128,
+//     K 16; A from TMEM, activations from shared memory), all accumulating
+//     into the tile's TMEM accumulator, then one commit.
+// Two A buffers let dequantisation overlap the MMAs; two accumulators let
+// one tile's epilogue (tcgen05.ld in 32-column chunks: SwiGLU -> h, or
+// per-slot partials) overlap the next tile's MMAs. At N = 128 one MMA takes
+// ~64 cycles, the tensor core's full rate, so the kernel is bound by the
+// tensor pipe (and the L2 -> shared-memory feed of activations), not by the
+// per-instruction cost that limits small-N decode MMAs.
+// Every wait is bounded: on expiry the kernel flags MR_DEVERR_TIMEOUT and
+// runs to its end on garbage, drains its copies and MMAs, frees its TMEM.
+// Requires 4- or 8-bit codes, in % 256 == 0 (whole stages) and expert
+// stacks addressable by 2-D tensor maps.
+#pragma once
+
+#include "mr_gemv_umma.cuh"
+
+namespace mr {
+
+constexpr int kPfRows = 128;   // MMA M
+constexpr int kPfN = 128;      // MMA N: activation rows (tokens) of one tile
+constexpr int kPfWorkers = 8;
+constexpr int kPfThreads = (2 + kPfWorkers) * 32;
+constexpr int kPfChunk = 32;   // accumulator columns per epilogue step
+
+template <int BITS, int SD, int EPI>
+struct PfStage {
+  static_assert(BITS == 4 || BITS == 8, "prefill GEMM takes 4- or 8-bit codes");
+  static constexpr int kMats = EPI == EPI_SWIGLU ? 2 : 1;
+  static constexpr int kBoxRows = kPfRows / kMats;
+  static constexpr int kGroups = 16 / BITS;                 // groups per 128-byte box column
+  static constexpr int kChunks = BITS / 2;                  // 16-byte chunks of a row's group
+  static constexpr int kCodeBytes = kPfRows * 128;
+  static constexpr int kBTile = kPfN * 128;                 // one group's activations
+  static constexpr int kBOff = kCodeBytes;
+  static constexpr int kBytes = kBOff + kGroups * kBTile;   // multiple of 1024
+  static constexpr uint32_t kTx = kCodeBytes + kGroups * kBTile;
+  static constexpr int kGpw = kGroups / 2;                  // groups per warp per stage
+  static constexpr int kABuf = kGroups * 32;                // TMEM columns of a stage's A
+  static constexpr int kDCol0 = 2 * kABuf;
+  static constexpr int kTmemCols = 512;
+  static_assert(kDCol0 + 2 * kPfN <= 512, "TMEM holds 512 columns");
+  static_assert(kBytes % 1024 == 0, "stages must keep 1024-byte alignment");
+};
+
+struct PfFixed {
+  static constexpr int kUpBytes = 2 * 64 * (kPfChunk + 1) * 4;  // up rows of one chunk, per half
+  static constexpr int kBarBytes = (2 * 16 + 4 * 2 + 1) * 8;
+  static constexpr int kBytes = kUpBytes + kBarBytes + 16 + 1024;
+};
+
+template <int BITS, int SD, int EPI>
+inline int pf_stages() {
+  const int n = (kSmemBudget - PfFixed::kBytes) / PfStage<BITS, SD, EPI>::kBytes;
+  return n > 8 ? 8 : n;
+}
+template <int BITS, int SD, int EPI>
+inline int pf_smem_bytes(int nst) {
+  return PfFixed::kBytes + nst * PfStage<BITS, SD, EPI>::kBytes;
+}
+
+// bf16 pair a - b, a*b + c (round to nearest even).
+MR_DEVICE uint32_t bf2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+MR_DEVICE uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// One row's codes of one group -> 32 bf16 pairs of weights s*q + z in the K
+// order of the permuted activations. q is exact in bf16 (<= 255); the fma
+// rounds once. s2 / z2: the group's scale and bias in both halves.
+template <int BITS>
+MR_DEVICE void dequant_full(uint32_t (&wv)[32], const uint32_t* w, uint32_t s2, uint32_t z2) {
+  constexpr uint32_t c128 = 0x43004300u;   // 128 in both halves
+  constexpr uint32_t c2048 = 0x45004500u;  // 2048
+  if constexpr (BITS == 4) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const uint32_t v = ((w[i] >> (4 * m)) & 0x000F000Fu) | c128;
+        wv[4 * i + m] = bf2_fma(bf2_sub(v, c128), s2, z2);
+      }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const uint32_t lo = ((w[i] >> (8 * m)) & 0x000F000Fu) | c128;
+        const uint32_t hi = ((w[i] >> (8 * m + 4)) & 0x000F000Fu) | c2048;
+        // q = (hi - 2048) + (lo - 128): 16*h + l, exact
+        uint32_t q;
+        asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(q) : "r"(bf2_sub(hi, c2048)), "r"(0x3F803F80u),
+            "r"(bf2_sub(lo, c128)));
+        wv[2 * i + m] = bf2_fma(q, s2, z2);
+      }
+  }
+}
+
+// A group's scale (or bias) of one row as a bf16 pair.
+template <int SD>
+MR_DEVICE uint32_t scale_pair(float v) {
+  const uint32_t b = f32_to_bf16_bits(v);
+  return b | (b << 16);
+}
+
+template <int BITS, int SD, int EPI>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    gemm_umma_kernel(const GemvParams p, const __grid_constant__ UmMaps maps, const int nst) {
+  using ST = PfStage<BITS, SD, EPI>;
+  extern __shared__ char smem_raw[];
+  char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* upx = reinterpret_cast<float*>(smem + nst * ST::kBytes);  // [2 halves][64][33]
+  uint64_t* full = reinterpret_cast<uint64_t*>(upx + 2 * 64 * (kPfChunk + 1));
+  uint64_t* empty = full + nst;
+  uint64_t* afull = empty + nst;  // [2] a stage's A written (8 workers)
+  uint64_t* aempty = afull + 2;   // [2] a stage's A read by the MMAs (commit)
+  uint64_t* dfull = aempty + 2;   // [2] a tile's accumulator complete (commit)
+  uint64_t* dempty = dfull + 2;   // [2] a tile's accumulator read out (8 workers)
+  uint64_t* drain = dempty + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int ngroups = (int)(p.in / kGroup);
+  const int nstages = ngroups / ST::kGroups;
+  const int n_routed = *p.n_routed_segments;
+  const int n_items = (n_routed + p.shared_segments) * p.rb_count;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nst; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, kPfWorkers + 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(afull + b, kPfWorkers);
+      mbar_init(aempty + b, 1);
+      mbar_init(dfull + b, 1);
+      mbar_init(dempty + b, kPfWorkers);
+    }
+    mbar_init(drain, 1);
+    flags[0] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, ST::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0, slot = 0, phase = 0;
+      for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const ItemInfo info = decode_item(p, n_routed, item);
+        const CUtensorMap *mp0, *mp1, *ma;
+        int y0, ya;
+        if (!info.shared) {
+          mp0 = &maps.a_packed;
+          mp1 = &maps.b_packed;
+          y0 = info.expert * (int)p.rows + info.rb * ST::kBoxRows;
+          ma = &maps.act;
+          ya = info.col0;
+        } else {
+          mp0 = &maps.sa_packed;
+          mp1 = &maps.sb_packed;
+          y0 = info.rb * ST::kBoxRows;
+          ma = &maps.act_sh;
+          ya = p.sh_row0 + info.col0;
+        }
+        for (int st = 0; st < nstages; ++st, ++it) {
+          wait_bounded(empty + slot, phase ^ 1u, flags, p.error);
+          char* S = smem + slot * ST::kBytes;
+          mbar_arrive_expect_tx(full + slot, ST::kTx);
+          tma_load_2d(S, mp0, st * 32, y0, full + slot);
+          if constexpr (ST::kMats == 2) tma_load_2d(S + ST::kBoxRows * 128, mp1, st * 32, y0, full + slot);
+#pragma unroll
+          for (int g = 0; g < ST::kGroups; ++g)
+            tma_load_2d(S + ST::kBOff + g * ST::kBTile, ma, (st * ST::kGroups + g) * kGroup, ya,
+                        full + slot);
+          if (++slot == (uint32_t)nst) {
+            slot = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (flags[0]) {
+        const uint32_t issued = it;
+        for (uint32_t j = (issued > (uint32_t)nst ? issued - nst : 0); j < issued; ++j)
+          for (uint32_t i = 0; i < kSpinLimit; ++i)
+            if (mbar_try_wait(full + (j % nst), (j / nst) & 1u)) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kPfRows, kPfN);
+      uint32_t slot = 0, phase = 0, j = 0, t = 0;  // j: stage counter, t: tile counter
+      for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++t) {
+        const uint32_t db = t & 1u;
+        wait_bounded(dempty + db, ((t >> 1) & 1u) ^ 1u, flags, p.error);
+        const uint32_t d_t = tbase + ST::kDCol0 + db * kPfN;
+        for (int st = 0; st < nstages; ++st, ++j) {
+          const uint32_t ab = j & 1u;
+          wait_bounded(full + slot, phase, flags, p.error);
+          wait_bounded(afull + ab, (j >> 1) & 1u, flags, p.error);
+          tc_fence_after();
+          const uint32_t bt = smem_u32(smem + slot * ST::kBytes + ST::kBOff);
+#pragma unroll
+          for (int g = 0; g < ST::kGroups; ++g) {
+            const uint32_t a_t = tbase + ab * ST::kABuf + g * 32;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_ts(d_t, a_t + kk * 8, umma_desc_sw128(bt + g * ST::kBTile + kk * 32), idesc,
+                        (st | g | kk) ? 1u : 0u);
+          }
+          tc_commit(aempty + ab);     // the A buffer may be rewritten
+          tc_commit(empty + slot);    // the stage's activation tiles are read
+          if (++slot == (uint32_t)nst) {
+            slot = 0;
+            phase ^= 1u;
+          }
+        }
+        tc_commit(dfull + db);  // the tile's accumulator is complete
+      }
+      tc_commit(drain);
+      wait_bounded(drain, 0, flags, p.error);
+    }
+  } else {
+    // ------------------------------------------------------------- workers
+    const int wq = warp & 3;              // TMEM lane quadrant
+    const int half = (warp - 2) >> 2;     // which groups of a stage / columns of a chunk
+    const int row = wq * 32 + lane;       // weight row in the tile = TMEM lane
+    const uint32_t lane_t = tbase + ((uint32_t)(wq * 32) << 16);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t rowoff = (uint32_t)row * 128;
+    const uint32_t rsw = (uint32_t)(row & 7);
+    uint32_t slot = 0, phase = 0, stg = sbase, j = 0, t = 0;
+    float* up = upx + half * 64 * (kPfChunk + 1);
+
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++t) {
+      const ItemInfo info = decode_item(p, n_routed, item);
+      const int ncols = info.ncols;
+      // this row's scales / biases: expert stack row of gate (rows < 64) or up
+      const bool second = ST::kMats == 2 && row >= ST::kBoxRows;
+      const int mrow = second ? row - ST::kBoxRows : row;
+      const ExpertSource& src = info.shared ? (second ? p.sh_b : p.sh_a) : (second ? p.src_b : p.src_a);
+      const ProjPtr pp = resolve<SD>(src, info.shared ? 0 : info.expert);
+      const int64_t grow = (int64_t)info.rb * ST::kBoxRows + mrow;
+      const bool row_ok = grow < p.rows;
+      const int64_t srow = (row_ok ? grow : 0) * ngroups;
+      for (int st = 0; st < nstages; ++st, ++j) {
+        const uint32_t ab = j & 1u;
+        // this warp's groups' scales and biases (global, L2-resident)
+        uint32_t s2[ST::kGpw], z2[ST::kGpw];
+#pragma unroll
+        for (int i = 0; i < ST::kGpw; ++i) {
+          const int gi = st * ST::kGroups + half * ST::kGpw + i;
+          s2[i] = scale_pair<SD>(scale_to_f32<SD>(load_scale_raw<SD>(pp.scales, srow + gi)));
+          z2[i] = scale_pair<SD>(scale_to_f32<SD>(load_scale_raw<SD>(pp.biases, srow + gi)));
+        }
+        warp_wait_sleep(full + slot, phase, flags, p.error);
+        // the A buffer was last read by the MMAs of stage j-2
+        if (j >= 2) warp_wait_sleep(aempty + ab, ((j >> 1) & 1u) ^ 1u, flags, p.error);
+        tc_fence_after();
+#pragma unroll
+        for (int i = 0; i < ST::kGpw; ++i) {
+          const int g = half * ST::kGpw + i;  // stage-local group
+          uint32_t w[2 * BITS];
+#pragma unroll
+          for (int c = 0; c < ST::kChunks; ++c) {
+            const uint32_t ch = (uint32_t)(g * ST::kChunks + c);
+            const uint4 q = lds_b128(stg + rowoff + ((ch ^ rsw) << 4));
+            w[4 * c] = q.x;
+            w[4 * c + 1] = q.y;
+            w[4 * c + 2] = q.z;
+            w[4 * c + 3] = q.w;
+          }
+          uint32_t wv[32];
+          dequant_full<BITS>(wv, w, s2[i], z2[i]);
+          __syncwarp();
+          tmem_st32(lane_t + ab * ST::kABuf + g * 32, wv);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(afull + ab);
+          mbar_arrive(empty + slot);  // this warp's codes are read
+        }
+        if (++slot == (uint32_t)nst) {
+          slot = 0;
+          phase ^= 1u;
+          stg = sbase;
+        } else {
+          stg += ST::kBytes;
+        }
+      }
+
+      // ------------------------------------------------------------ epilogue
+      const uint32_t db = t & 1u;
+      warp_wait_sleep(dfull + db, (t >> 1) & 1u, flags, p.error);
+      tc_fence_after();
+      const uint32_t dcol = tbase + ST::kDCol0 + db * kPfN;
+      for (int cb = half * kPfChunk; cb < ncols; cb += 2 * kPfChunk) {
+        // columns cb .. cb+31 of the accumulator, this warp's lanes
+        uint32_t r[32];
+        float d[kPfChunk];
+        __syncwarp();
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+            "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+            "%28, %29, %30, %31}, [%32];\n\ttcgen05.wait::ld.sync.aligned;"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+              "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+              "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+              "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+              "=r"(r[31])
+            : "r"(lane_t + (dcol - tbase) + cb)
+            : "memory");
+#pragma unroll
+        for (int i = 0; i < kPfChunk; ++i) d[i] = __uint_as_float(r[i]);
+        const int nc = min(kPfChunk, ncols - cb);
+        // value id of column cb + lane (this lane's column of the chunk)
+        int mv = 0;
+        if (lane < nc) mv = info.shared ? (EPI == EPI_SWIGLU ? 0 : p.sh_row0) + info.col0 + cb + lane
+                                        : __ldg(p.cols + info.col0 + cb + lane);
+        if constexpr (EPI == EPI_STORE || EPI == EPI_PARTIAL) {
+#pragma unroll
+          for (int jj = 0; jj < kPfChunk; ++jj) {
+            if (jj >= nc) break;  // warp-uniform
+            const int v = __shfl_sync(0xffffffffu, mv, jj);
+            if (row_ok) {
+              if constexpr (EPI == EPI_STORE)
+                p.out_bf16[(int64_t)v * p.rows + grow] = f32_to_bf16_bits(d[jj]);
+              else
+                p.part[(int64_t)v * p.rows + grow] = (v < p.Tk) ? bf16_round(d[jj]) : d[jj];
+            }
+          }
+        } else {
+          // SwiGLU: the up rows (quadrants 2, 3) hand their values to the
+          // gate rows (quadrants 0, 1) of the same half through shared memory
+          if (row >= 64) {
+#pragma unroll
+            for (int i = 0; i < kPfChunk; ++i) up[(row - 64) * (kPfChunk + 1) + i] = d[i];
+          }
+          named_bar(2 + half, 128);
+          if (row < 64) {
+            const int hrow = info.rb * 64 + row;  // intermediate index
+            const int pos = perm_pos(hrow, p.h_bits);
+            const float lim = p.swiglu_limit;
+#pragma unroll
+            for (int jj = 0; jj < kPfChunk; ++jj) {
+              if (jj >= nc) break;  // warp-uniform
+              const int v = __shfl_sync(0xffffffffu, mv, jj);
+              float g = bf16_round(d[jj]);
+              float u = bf16_round(up[row * (kPfChunk + 1) + jj]);
+              if (lim > 0.0f) {
+                g = fminf(g, lim);
+                u = fminf(fmaxf(u, -lim), lim);
+              }
+              const int64_t hr = info.shared ? (int64_t)p.Tk + v : (int64_t)(info.col0 + cb + jj);
+              if (!info.shared) {
+                uint16_t hb;
+                if (!p.weight_after_down) {
+                  float a = g * sigmoid_f32(g);
+                  a = a * u;
+                  a = a * __ldg(p.weights + v);
+                  hb = f32_to_bf16_bits(a);
+                } else {
+                  const float sg = bf16_round(sigmoid_f32(g));
+                  const float a = bf16_round(g * sg);
+                  hb = f32_to_bf16_bits(a * u);
+                }
+                p.out_bf16[hr * p.rows + pos] = hb;
+              } else {
+                float a = g * sigmoid_f32(g);
+                a = a * u;
+                const uint16_t hb = f32_to_bf16_bits(a);
+                p.out_bf16[hr * p.rows + pos] = hb;
+                p.out_bf16[(hr + p.shared_lo_off) * p.rows + pos] =
+                    f32_to_bf16_bits(a - bf16_bits_to_f32(hb));
+              }
+            }
+          }
+          named_bar(2 + half, 128);  // the chunk buffer is reused
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dempty + db);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, ST::kTmemCols);
+  }
+}
+
+}  // namespace mr

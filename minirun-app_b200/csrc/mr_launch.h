@@ -5,6 +5,7 @@
 #include "mr_gemv.cuh"
 #include "mr_gemv_tma.cuh"
 #include "mr_gemv_umma.cuh"
+#include "mr_gemm_umma.cuh"
 
 namespace mr {
 
@@ -36,6 +37,21 @@ inline cudaError_t launch_umma(const GemvParams& p, const UmMaps& m, int bits, i
     case 2: return launch_umma_b2(p, m, sd, epi, grid, s);
     case 4: return launch_umma_b4(p, m, sd, epi, grid, s);
     case 8: return launch_umma_b8(p, m, sd, epi, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// tcgen05 prefill GEMM (4/8-bit, in % 256 == 0, activations through tensor maps).
+cudaError_t launch_pf_b4(const GemvParams& p, const UmMaps& m, int sd, int epi, int grid,
+                         cudaStream_t s);
+cudaError_t launch_pf_b8(const GemvParams& p, const UmMaps& m, int sd, int epi, int grid,
+                         cudaStream_t s);
+
+inline cudaError_t launch_pf(const GemvParams& p, const UmMaps& m, int bits, int sd, int epi,
+                             int grid, cudaStream_t s) {
+  switch (bits) {
+    case 4: return launch_pf_b4(p, m, sd, epi, grid, s);
+    case 8: return launch_pf_b8(p, m, sd, epi, grid, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -119,7 +135,43 @@ inline cudaError_t launch_umma_epi(const GemvParams& p, const UmMaps& m, int epi
   }
 }
 
+template <int BITS, int SD, int EPI>
+inline cudaError_t launch_pf_inst(const GemvParams& p, const UmMaps& m, int grid,
+                                  cudaStream_t s) {
+  static bool done[64] = {};  // one per instantiation
+  const int nst = pf_stages<BITS, SD, EPI>();
+  const int smem = pf_smem_bytes<BITS, SD, EPI>(nst);
+  auto kern = gemm_umma_kernel<BITS, SD, EPI>;
+  cudaError_t e = opt_in_smem(kern, smem, done);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kPfThreads, smem, s>>>(p, m, nst);
+  return cudaGetLastError();
+}
+
+template <int BITS, int SD>
+inline cudaError_t launch_pf_epi(const GemvParams& p, const UmMaps& m, int epi, int grid,
+                                 cudaStream_t s) {
+  switch (epi) {
+    case EPI_STORE: return launch_pf_inst<BITS, SD, EPI_STORE>(p, m, grid, s);
+    case EPI_SWIGLU: return launch_pf_inst<BITS, SD, EPI_SWIGLU>(p, m, grid, s);
+    default: return launch_pf_inst<BITS, SD, EPI_PARTIAL>(p, m, grid, s);
+  }
+}
+
 }  // namespace mr
+
+// Instantiates launch_pf_b<BITS> in a translation unit.
+#define MR_DEFINE_PF_LAUNCHER(BITS)                                                           \
+  namespace mr {                                                                              \
+  cudaError_t launch_pf_b##BITS(const GemvParams& p, const UmMaps& m, int sd, int epi,        \
+                                int grid, cudaStream_t s) {                                   \
+    switch (sd) {                                                                             \
+      case MR_DTYPE_BF16: return launch_pf_epi<BITS, MR_DTYPE_BF16>(p, m, epi, grid, s);      \
+      case MR_DTYPE_F16: return launch_pf_epi<BITS, MR_DTYPE_F16>(p, m, epi, grid, s);        \
+      default: return launch_pf_epi<BITS, MR_DTYPE_F32>(p, m, epi, grid, s);                  \
+    }                                                                                         \
+  }                                                                                           \
+  }
 
 // Instantiates launch_umma_b<BITS> in a translation unit.
 #define MR_DEFINE_UMMA_LAUNCHER(BITS)                                                         \

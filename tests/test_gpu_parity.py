@@ -309,3 +309,24 @@ def test_expert_table_equals_stack():
     b, _ = tl(x)
     M.Context.get(0).set_kernel_path("auto")
     assert torch.equal(a, b)
+
+
+# ------------------------------------------------------ prefill-size batches
+
+@pytest.mark.parametrize("variant", [dict(), dict(weight_after_down=True), dict(shared_inter=0),
+                                     dict(bits=8), dict(swiglu_limit=0.75)])
+def test_prefill_gemm_matches_oracle(variant):
+    """T = 320 on config 0 (40 routed columns per expert on average) runs the
+    tcgen05 grouped GEMM, which rounds each dequantised weight to bf16 as
+    MLX's large-batch quantised matmul does: within the 1e-2 layer bound."""
+    cfg = dataclasses.replace(O.CONFIGS[0], **variant)
+    L = O.gen_layer(cfg)
+    if cfg.shared_inter == 0:
+        L.sgate = L.sup = L.sdown = None
+    x = O.gen_x(cfg, 320, batch=5)
+    out, f, ids, w, m = O.moe_layer_forward(L, x)
+    gout, sel = gpu_layer_from_oracle(L)(t_u16(x))
+    assert_ids_match(sel.ids.cpu().numpy(), ids, m)
+    err = rel_l2(O.bf16_to_f32(n_u16(gout)), f)
+    assert err < REL_L2, err
+    M.Context.get(0).sync_check()
