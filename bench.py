@@ -37,6 +37,7 @@ sys.path.insert(0, os.path.join(ROOT, "minirun-app_b200"))
 
 METRIC = ("MoE-layer decode tokens/s; dequant-GEMV HBM GB/s (% of ~8 TB/s) at 1/2/4/8 GPUs")
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 # kernels one layer forward launches: logits(+prep), top-k(+plan), gate/up, down, combine;
 # expert-parallel: logits, top-k, routed gate/up and down, partial sums, shared gate/up and
 # down, combine (the NCCL collectives are not counted)
@@ -60,6 +61,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--kernel-path", choices=["auto", "register", "tma", "umma"], default="auto",
                    help="dequant-GEMV implementation (mr_ctx_set_kernel_path)")
+    p.add_argument("--prefill-tokens", type=int, default=4096,
+                   help="config-3 prefill batch measured beside the decode line (0 = skip)")
     return p.parse_args()
 
 
@@ -78,6 +81,15 @@ def peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def tensor_peak():
+    """Dense bf16 TFLOP/s (burst: the kernels are timed alone)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
 
 
 class ClockSampler:
@@ -279,6 +291,10 @@ def run_ours(args, world, rank, local):
                            "layer_frac_of_hbm": b2 / (m2 / K / 1e3) / 1e9 / hbm,
                            "distinct_experts_avg": sum(u2) / len(u2)}
 
+    prefill = None
+    if not ep and args.prefill_tokens > 0:
+        prefill = prefill_run(args, S, M, torch, ctx, local, dev)
+
     e2e = e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local,
                   group if ep else None)
     ctx.sync_check()
@@ -318,6 +334,7 @@ def run_ours(args, world, rank, local):
             "layer_frac_of_hbm": avg_bytes / (ms_step / 1e3) / 1e9 / hbm,
             "kernels": kern,
             "sweep": sweep,
+            "prefill": prefill,
         },
         "roofline": {
             "bound": "hbm",
@@ -342,6 +359,58 @@ def run_ours(args, world, rank, local):
         dist.barrier()
         group.close()
         dist.destroy_process_group()
+
+
+def prefill_run(args, S, M, torch, ctx, local, dev):
+    """Config 3: one prefill-size batch (T tokens, Zipf-skewed routing) through
+    the same layer call; reports tokens/s and the tcgen05 GEMMs' TFLOP/s
+    against the dense bf16 peak (tensor-bound). Algorithmic FLOPs: 2*H*I per
+    (token, expert) and projection, over the k routed slots and the shared
+    expert; the measured experts are whatever the router picked."""
+    spec = S.CONFIGS[3]
+    if args.experts:
+        import dataclasses
+        spec = dataclasses.replace(spec, experts=args.experts)
+    T = args.prefill_tokens
+    lay = S.synth_layer(spec, layer=0, device=local)
+    x = S.synth_x(spec, T, layer=0, batch=0, device=local)
+    out = torch.empty((T, spec.hidden), dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        lay.forward(x, out=out, selection=False)
+    torch.cuda.synchronize()
+    steps = 5
+    ctx.profile(True)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        lay.forward(x, out=out, selection=False)
+    e1.record()
+    torch.cuda.synchronize()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    ms = e0.elapsed_time(e1) / steps
+    _, sel = lay.forward(x, out=out)
+    distinct = len(set(sel.ids.cpu().view(-1).tolist()))
+    slots = T * (spec.top_k + (1 if spec.shared_inter else 0))
+    gu_flops = slots * 2 * (2 * spec.hidden * spec.inter)
+    dn_flops = slots * 2 * spec.hidden * spec.inter
+    gu_ms = prof["gate_up"][0] / max(prof["gate_up"][1], 1)
+    dn_ms = prof["down_combine"][0] / max(prof["down_combine"][1], 1)
+    peak, kind = tensor_peak()
+    gu_tf = gu_flops / (gu_ms / 1e3) / 1e12
+    return {
+        "workload": f"config3 prefill T={T}: config-1 layer, router biased to Zipf(1.1)",
+        "tokens_per_s": T / (ms / 1e3),
+        "ms_per_step": ms,
+        "distinct_experts": distinct,
+        "gate_up_ms": gu_ms,
+        "down_combine_ms": dn_ms,
+        "roofline": {"bound": "tensor", "kernel": "gemm gate/up (+SwiGLU), tcgen05",
+                     "achieved": gu_tf, "peak": peak, "peak_kind": kind, "unit": "TFLOP/s",
+                     "frac": gu_tf / peak, "algorithmic_flops_per_launch": gu_flops},
+        "down_tflops": dn_flops / (dn_ms / 1e3) / 1e12,
+    }
 
 
 def e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local, group=None):

@@ -275,16 +275,27 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int64_t grow = (int64_t)info.rb * ST::kBoxRows + mrow;
       const bool row_ok = grow < p.rows;
       const int64_t srow = (row_ok ? grow : 0) * ngroups;
-      for (int st = 0; st < nstages; ++st, ++j) {
-        const uint32_t ab = j & 1u;
-        // this warp's groups' scales and biases (global, L2-resident)
-        uint32_t s2[ST::kGpw], z2[ST::kGpw];
+      // this warp's groups' scales and biases (global, L2-resident), loaded
+      // one stage ahead so their latency hides behind a stage's work
+      uint32_t sr[ST::kGpw], zr[ST::kGpw];
+      auto load_scales = [&](int st) {
 #pragma unroll
         for (int i = 0; i < ST::kGpw; ++i) {
           const int gi = st * ST::kGroups + half * ST::kGpw + i;
-          s2[i] = scale_pair<SD>(scale_to_f32<SD>(load_scale_raw<SD>(pp.scales, srow + gi)));
-          z2[i] = scale_pair<SD>(scale_to_f32<SD>(load_scale_raw<SD>(pp.biases, srow + gi)));
+          sr[i] = load_scale_raw<SD>(pp.scales, srow + gi);
+          zr[i] = load_scale_raw<SD>(pp.biases, srow + gi);
         }
+      };
+      load_scales(0);
+      for (int st = 0; st < nstages; ++st, ++j) {
+        const uint32_t ab = j & 1u;
+        uint32_t s2[ST::kGpw], z2[ST::kGpw];
+#pragma unroll
+        for (int i = 0; i < ST::kGpw; ++i) {
+          s2[i] = scale_pair<SD>(scale_to_f32<SD>(sr[i]));
+          z2[i] = scale_pair<SD>(scale_to_f32<SD>(zr[i]));
+        }
+        if (st + 1 < nstages) load_scales(st + 1);
         warp_wait_sleep(full + slot, phase, flags, p.error);
         // the A buffer was last read by the MMAs of stage j-2
         if (j >= 2) warp_wait_sleep(aempty + ab, ((j >> 1) & 1u) ^ 1u, flags, p.error);
