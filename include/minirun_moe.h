@@ -308,6 +308,59 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* la
                                   const uint16_t* x, int64_t tokens, uint16_t* out,
                                   int32_t* ids_out, void* stream);
 
+/* ----------------------------------------------------------- expert cache
+ * An HBM cache of routed experts under a byte budget, filled from host
+ * memory on a side stream: the device replacement of StorageCore's buffer
+ * pool and tile reader on the expert path
+ * (Sources/StorageCore/BufferPool.swift:279-531, TileReader.swift:216-340).
+ * A slot holds one expert's three projections; slots are reused least
+ * recently used first. Host arrays should be pinned (cudaHostAlloc /
+ * cudaHostRegister) for the copies to be asynchronous. */
+typedef struct mr_cache mr_cache;
+
+/* One expert's three projections (gate, up, down) in host memory: the arrays
+ * an mr_affine_desc of that expert would point to. */
+typedef struct mr_expert_host {
+  const void* packed[3];
+  const void* scales[3];
+  const void* biases[3];
+  size_t packed_bytes[3];
+  size_t scale_bytes[3]; /* scales and biases each */
+} mr_expert_host;
+
+typedef struct mr_cache_stats {
+  int64_t slots;        /* experts the budget holds */
+  int64_t resident;     /* experts resident now */
+  int64_t hits;         /* (layer, expert) requests served from HBM */
+  int64_t misses;       /* requests copied from host */
+  int64_t evictions;
+  int64_t bytes_copied; /* host -> device */
+} mr_cache_stats;
+
+/* A cache of floor(budget_bytes / slot_bytes) slots of slot_bytes (at least
+ * one expert's arrays, each 256-byte aligned) on the context's device. */
+mr_status mr_cache_create(mr_ctx* ctx, size_t budget_bytes, size_t slot_bytes,
+                          mr_cache** out);
+mr_status mr_cache_destroy(mr_cache* cache);
+/* Where (layer, expert) lives on the host; the arrays must stay valid. */
+mr_status mr_cache_register(mr_cache* cache, int32_t layer, int32_t expert,
+                            const mr_expert_host* host);
+mr_status mr_cache_get_stats(const mr_cache* cache, mr_cache_stats* out);
+/* mr_moe_layer_forward with the routed experts of `layer_id` served by the
+ * cache: layer->gate/up/down give shapes and formats only (their pointers
+ * and expert_table are ignored); router and shared expert as usual. The
+ * routed ids decide what to copy, so the call synchronises `stream` once
+ * after routing; misses are copied on the cache's copy stream into free or
+ * least-recently-used slots, and the GEMVs read the experts through a device
+ * pointer table. Calls must come from one host thread on one stream (a slot
+ * is reused only after the previous call's work on that stream is done).
+ * Results are byte-identical whatever the budget. MR_ERR_BUDGET when one
+ * call needs more distinct experts than the cache has slots. */
+mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* cache, int32_t layer_id,
+                                      const mr_moe_layer* layer, const uint16_t* x,
+                                      int64_t tokens, uint16_t* out, int32_t* ids_out,
+                                      void* stream);
+
 /* ----------------------------------------------------------- profiling
  * CUDA-event timing of the kernels mr_moe_layer_forward launches (off by
  * default; the events are recorded on the caller's stream around each

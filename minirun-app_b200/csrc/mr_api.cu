@@ -11,6 +11,9 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <unordered_map>
+#include <vector>
+
 #include "mr_launch.h"
 #include "mr_router.cuh"
 
@@ -1859,6 +1862,324 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
     st = cuda_check(ctx,
                     cudaMemcpyAsync(ids_out, ids + (int64_t)rank * T * k, T * k * sizeof(int32_t),
                                     cudaMemcpyDeviceToDevice, s),
+                    "copy ids");
+  return st;
+}
+
+}  // extern "C"
+
+// ----------------------------------------------------------- expert cache
+
+struct mr_cache {
+  struct Reg {
+    mr_expert_host host;
+    size_t off[9];  // slot offsets: packed, scales, biases of gate, up, down
+    int slot = -1;
+  };
+  struct Slot {
+    uint64_t key = ~0ull;
+    uint64_t last_use = 0;
+  };
+  mr_ctx* ctx = nullptr;
+  size_t slot_bytes = 0;
+  char* pool = nullptr;
+  std::vector<Slot> slots;
+  std::unordered_map<uint64_t, Reg> regs;
+  uint64_t clock = 0;
+  mr_cache_stats stats{};
+  cudaStream_t copy = nullptr;
+  cudaEvent_t done = nullptr;
+  // pinned host staging: routed ids read back, the expert pointer table
+  int32_t* ids_h = nullptr;
+  size_t ids_cap = 0;
+  mr_expert_ptrs* table_h = nullptr;
+  size_t table_cap = 0;
+};
+
+namespace {
+
+uint64_t cache_key(int32_t layer, int32_t expert) {
+  return ((uint64_t)(uint32_t)layer << 32) | (uint32_t)expert;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+template <class T>
+mr_status grow_pinned(mr_ctx* ctx, T** p, size_t* cap, size_t n, const char* what) {
+  if (n <= *cap) return MR_OK;
+  if (*p) cudaFreeHost(*p);
+  *p = nullptr;
+  *cap = 0;
+  mr_status st = cuda_check(ctx, cudaHostAlloc(reinterpret_cast<void**>(p), n * sizeof(T),
+                                               cudaHostAllocDefault),
+                            what);
+  if (!st) *cap = n;
+  return st;
+}
+
+}  // namespace
+
+extern "C" {
+
+mr_status mr_cache_create(mr_ctx* ctx, size_t budget_bytes, size_t slot_bytes, mr_cache** out) {
+  if (!ctx || !out) return MR_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  slot_bytes = align256(slot_bytes);
+  if (slot_bytes == 0 || budget_bytes < slot_bytes)
+    return fail(ctx, MR_ERR_BUDGET, "the budget holds no expert slot");
+  mr_cache* c = new mr_cache;
+  c->ctx = ctx;
+  c->slot_bytes = slot_bytes;
+  const size_t n = budget_bytes / slot_bytes;
+  mr_status st = cuda_check(ctx, cudaMalloc(&c->pool, n * slot_bytes), "cudaMalloc(cache pool)");
+  if (!st) st = cuda_check(ctx, cudaStreamCreateWithFlags(&c->copy, cudaStreamNonBlocking),
+                           "cudaStreamCreate(cache copies)");
+  if (!st) st = cuda_check(ctx, cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming),
+                           "cudaEventCreate(cache)");
+  if (st) {
+    mr_cache_destroy(c);
+    return st;
+  }
+  c->slots.resize(n);
+  c->stats.slots = (int64_t)n;
+  *out = c;
+  return MR_OK;
+}
+
+mr_status mr_cache_destroy(mr_cache* c) {
+  if (!c) return MR_OK;
+  if (c->copy) cudaStreamSynchronize(c->copy);
+  if (c->pool) cudaFree(c->pool);
+  if (c->copy) cudaStreamDestroy(c->copy);
+  if (c->done) cudaEventDestroy(c->done);
+  if (c->ids_h) cudaFreeHost(c->ids_h);
+  if (c->table_h) cudaFreeHost(c->table_h);
+  delete c;
+  return MR_OK;
+}
+
+mr_status mr_cache_register(mr_cache* c, int32_t layer, int32_t expert, const mr_expert_host* h) {
+  if (!c || !h || layer < 0 || expert < 0) return MR_ERR_INVALID_ARGUMENT;
+  mr_cache::Reg r;
+  r.host = *h;
+  size_t off = 0;
+  for (int p = 0; p < 3; ++p) {
+    if (!h->packed[p] || !h->scales[p] || !h->biases[p] || !h->packed_bytes[p] ||
+        !h->scale_bytes[p])
+      return fail(c->ctx, MR_ERR_INVALID_ARGUMENT, "an expert projection's host array is missing");
+    r.off[3 * p] = off;
+    off = align256(off + h->packed_bytes[p]);
+    r.off[3 * p + 1] = off;
+    off = align256(off + h->scale_bytes[p]);
+    r.off[3 * p + 2] = off;
+    off = align256(off + h->scale_bytes[p]);
+  }
+  if (off > c->slot_bytes)
+    return fail(c->ctx, MR_ERR_INVALID_ARGUMENT,
+                "expert needs " + std::to_string(off) + " bytes, slots hold " +
+                    std::to_string(c->slot_bytes));
+  const uint64_t key = cache_key(layer, expert);
+  auto it = c->regs.find(key);
+  if (it != c->regs.end() && it->second.slot >= 0) {  // re-registered: drop the copy
+    c->slots[it->second.slot] = mr_cache::Slot{};
+    --c->stats.resident;
+  }
+  c->regs[key] = r;
+  return MR_OK;
+}
+
+mr_status mr_cache_get_stats(const mr_cache* c, mr_cache_stats* out) {
+  if (!c || !out) return MR_ERR_INVALID_ARGUMENT;
+  *out = c->stats;
+  return MR_OK;
+}
+
+mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* c, int32_t layer_id,
+                                      const mr_moe_layer* L, const uint16_t* x, int64_t T,
+                                      uint16_t* out, int32_t* ids_out, void* stream) {
+  if (!ctx || !c || !L) return fail(ctx, MR_ERR_INVALID_ARGUMENT, "context, cache and layer required");
+  if (c->ctx != ctx) return fail(ctx, MR_ERR_STATE, "the cache belongs to another context");
+  // routed pointers come from the cache's table; validate shapes only
+  mr_moe_layer Lt = *L;
+  static const mr_expert_ptrs dummy_table[1] = {};
+  Lt.expert_table = dummy_table;
+  std::string why;
+  mr_status st = validate_layer(&Lt, why);
+  if (st) return fail(ctx, st, why);
+  if (T <= 0 || !x || !out)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "input must be a non-empty [tokens, hidden] matrix");
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0)
+    return fail(ctx, MR_ERR_UNSUPPORTED, "x must be 16-byte aligned");
+  const int E = L->router.experts, k = L->router.top_k;
+  const int64_t H = L->hidden, I = L->inter, Tk = T * k;
+  const bool has_shared = L->shared_inter > 0;
+  const int64_t R = Tk + (has_shared ? 2 * T : 0);
+  const int seg_cols = pick_seg_cols(T);
+  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / seg_cols + 1;
+  const LogitsShape ls = logits_shape(ctx, T, E, H);
+  if (Tk > (int64_t)1 << 28) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
+
+  uint16_t *xperm = nullptr, *h = nullptr;
+  float *xsum = nullptr, *part = nullptr, *wts = nullptr, *hsum = nullptr, *part2 = nullptr;
+  int32_t* ids = nullptr;
+  int *nseg = nullptr, *cols = nullptr;
+  int4* segs = nullptr;
+  mr_expert_ptrs* table = nullptr;
+  Bump b{nullptr};
+  for (int pass = 0; pass < 2; ++pass) {
+    b.off = 0;
+    part = b.take<float>((size_t)ls.kq * T * E);
+    xperm = b.take<uint16_t>(T * H);
+    xsum = b.take<float>(T * (H / kGroup));
+    ids = b.take<int32_t>(Tk);
+    wts = b.take<float>(Tk);
+    nseg = b.take<int>(4);
+    segs = b.take<int4>(max_seg);
+    cols = b.take<int>(Tk);
+    h = b.take<uint16_t>(R * I);
+    hsum = b.take<float>(R * (I / 32));
+    part2 = b.take<float>(R * H);
+    table = b.take<mr_expert_ptrs>(E);
+    if (pass == 0) {
+      if ((st = ensure_workspace(ctx, b.off))) return st;
+      b.base = reinterpret_cast<char*>(ctx->ws);
+    }
+  }
+  if ((st = grow_pinned(ctx, &c->ids_h, &c->ids_cap, (size_t)Tk, "cudaHostAlloc(ids)"))) return st;
+  if ((st = grow_pinned(ctx, &c->table_h, &c->table_cap, (size_t)E, "cudaHostAlloc(table)")))
+    return st;
+  cudaStream_t s = as_stream(stream);
+
+  // route; the selection decides which experts must be resident
+  const RoutePlan rp{nseg, segs, cols, seg_cols, 0, E, false};
+  if ((st = route_tokens(ctx, L, x, T, ls, part, xperm, xsum, ids, wts, nullptr, rp, s)))
+    return st;
+  if ((st = cuda_check(ctx, cudaMemcpyAsync(c->ids_h, ids, Tk * sizeof(int32_t),
+                                            cudaMemcpyDeviceToHost, s),
+                       "copy ids to host")))
+    return st;
+  if ((st = cuda_check(ctx, cudaStreamSynchronize(s), "synchronise routing"))) return st;
+  std::vector<int> need;
+  need.reserve((size_t)std::min<int64_t>(Tk, E));
+  {
+    std::vector<char> seen((size_t)E, 0);
+    for (int64_t i = 0; i < Tk; ++i) {
+      const int e = c->ids_h[i];
+      if (e < 0 || e >= E) return fail(ctx, MR_ERR_DEVICE, "router produced an expert id out of range");
+      if (!seen[e]) {
+        seen[e] = 1;
+        need.push_back(e);
+      }
+    }
+  }
+  if ((int64_t)need.size() > (int64_t)c->slots.size())
+    return fail(ctx, MR_ERR_BUDGET,
+                "this call routes to " + std::to_string(need.size()) + " distinct experts; the " +
+                    "budget holds " + std::to_string(c->slots.size()));
+  ++c->clock;
+  // hits first, so that misses never evict an expert this call uses
+  std::vector<mr_cache::Reg*> regs(need.size(), nullptr);
+  for (size_t i = 0; i < need.size(); ++i) {
+    auto it = c->regs.find(cache_key(layer_id, need[i]));
+    if (it == c->regs.end())
+      return fail(ctx, MR_ERR_STATE,
+                  "expert " + std::to_string(need[i]) + " of layer " + std::to_string(layer_id) +
+                      " is not registered with the cache");
+    regs[i] = &it->second;
+    if (it->second.slot >= 0) {
+      c->slots[it->second.slot].last_use = c->clock;
+      ++c->stats.hits;
+    }
+  }
+  memset(c->table_h, 0, (size_t)E * sizeof(mr_expert_ptrs));
+  for (size_t i = 0; i < need.size(); ++i) {
+    mr_cache::Reg& r = *regs[i];
+    if (r.slot < 0) {
+      // a free slot, else the least recently used one not needed now
+      int pick = -1;
+      for (size_t j = 0; j < c->slots.size(); ++j) {
+        const mr_cache::Slot& sl = c->slots[j];
+        if (sl.key == ~0ull) {
+          pick = (int)j;
+          break;
+        }
+        if (sl.last_use < c->clock && (pick < 0 || sl.last_use < c->slots[pick].last_use))
+          pick = (int)j;
+      }
+      if (pick < 0) return fail(ctx, MR_ERR_BUDGET, "no cache slot is free for this call");
+      mr_cache::Slot& sl = c->slots[pick];
+      if (sl.key != ~0ull) {
+        c->regs[sl.key].slot = -1;
+        ++c->stats.evictions;
+      } else {
+        ++c->stats.resident;
+      }
+      sl.key = cache_key(layer_id, need[i]);
+      sl.last_use = c->clock;
+      r.slot = pick;
+      ++c->stats.misses;
+      char* base = c->pool + (size_t)pick * c->slot_bytes;
+      const void* src[9];
+      size_t bytes[9];
+      for (int p = 0; p < 3; ++p) {
+        src[3 * p] = r.host.packed[p];
+        bytes[3 * p] = r.host.packed_bytes[p];
+        src[3 * p + 1] = r.host.scales[p];
+        src[3 * p + 2] = r.host.biases[p];
+        bytes[3 * p + 1] = bytes[3 * p + 2] = r.host.scale_bytes[p];
+      }
+      for (int a = 0; a < 9; ++a) {
+        if ((st = cuda_check(ctx, cudaMemcpyAsync(base + r.off[a], src[a], bytes[a],
+                                                  cudaMemcpyHostToDevice, c->copy),
+                             "copy expert to HBM")))
+          return st;
+        c->stats.bytes_copied += (int64_t)bytes[a];
+      }
+    }
+    const char* base = c->pool + (size_t)r.slot * c->slot_bytes;
+    mr_expert_ptrs& t = c->table_h[need[i]];
+    for (int p = 0; p < 3; ++p) {
+      t.packed[p] = reinterpret_cast<const uint32_t*>(base + r.off[3 * p]);
+      t.scales[p] = base + r.off[3 * p + 1];
+      t.biases[p] = base + r.off[3 * p + 2];
+    }
+  }
+  if ((st = cuda_check(ctx, cudaMemcpyAsync(table, c->table_h, (size_t)E * sizeof(mr_expert_ptrs),
+                                            cudaMemcpyHostToDevice, c->copy),
+                       "copy expert table")))
+    return st;
+  if ((st = cuda_check(ctx, cudaEventRecord(c->done, c->copy), "record cache copies"))) return st;
+  if ((st = cuda_check(ctx, cudaStreamWaitEvent(s, c->done, 0), "wait for cache copies")))
+    return st;
+
+  // the routed experts through the table, the shared expert from its stacks
+  Lt.expert_table = table;
+  ExpertsRun r{};
+  r.xperm = xperm;
+  r.xsum = xsum;
+  r.tokens = T;
+  r.shared_tokens = has_shared ? T : 0;
+  r.Tk = Tk;
+  r.k = k;
+  r.nseg = nseg;
+  r.segs = segs;
+  r.cols = cols;
+  r.max_seg = max_seg;
+  r.seg_cols = seg_cols;
+  r.wts = wts;
+  r.h = h;
+  r.hsum = hsum;
+  r.part2 = part2;
+  if ((st = run_experts(ctx, &Lt, r, s))) return st;
+  const int64_t n_out = T * H;
+  const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 4 * ctx->sm_count));
+  combine_kernel<<<cgrid, 256, 0, s>>>(part2, wts, (int)T, k, H,
+                                        L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0,
+                                        has_shared ? 1 : 0, out);
+  if ((st = cuda_check(ctx, cudaGetLastError(), "combine_kernel"))) return st;
+  if (ids_out)
+    st = cuda_check(ctx, cudaMemcpyAsync(ids_out, ids, Tk * sizeof(int32_t),
+                                         cudaMemcpyDeviceToDevice, s),
                     "copy ids");
   return st;
 }

@@ -8,6 +8,7 @@ no CPU fallback.
 from ._lib import LIB_PATH, LibraryMissing, load as load_library
 from .bridge import (AffineBridgeError, AffineWeights, Context, MoeError, Selection,
                      affine_dequantize, affine_gather_mm, affine_mm, validate_desc)
+from .cache import CachedLayer, ExpertCache
 from .ep import ExpertGroup, MoELayerShard
 from .moe import (MoELayer, ResidentExpertBackend, RouterConfig, router_select,
                   router_select_logits)
@@ -16,5 +17,5 @@ __all__ = [
     "LIB_PATH", "LibraryMissing", "load_library", "AffineBridgeError", "AffineWeights",
     "Context", "MoeError", "Selection", "affine_dequantize", "affine_gather_mm", "affine_mm",
     "validate_desc", "MoELayer", "ResidentExpertBackend", "RouterConfig", "router_select",
-    "router_select_logits", "ExpertGroup", "MoELayerShard",
+    "router_select_logits", "ExpertGroup", "MoELayerShard", "CachedLayer", "ExpertCache",
 ]

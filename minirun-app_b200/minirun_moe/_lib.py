@@ -60,6 +60,16 @@ class mr_moe_layer(C.Structure):
                 ("swiglu_limit", C.c_float), ("weight_placement", C.c_int)]
 
 
+class mr_expert_host(C.Structure):
+    _fields_ = [("packed", vp * 3), ("scales", vp * 3), ("biases", vp * 3),
+                ("packed_bytes", C.c_size_t * 3), ("scale_bytes", C.c_size_t * 3)]
+
+
+class mr_cache_stats(C.Structure):
+    _fields_ = [("slots", C.c_int64), ("resident", C.c_int64), ("hits", C.c_int64),
+                ("misses", C.c_int64), ("evictions", C.c_int64), ("bytes_copied", C.c_int64)]
+
+
 # name -> (restype, argtypes); the complete exported surface of the header
 SIGNATURES = {
     "mr_abi_version": (C.c_int, []),
@@ -94,6 +104,12 @@ SIGNATURES = {
     "mr_ep_destroy": (C.c_int, [vp]),
     "mr_moe_layer_forward_ep": (C.c_int, [vp, vp, C.POINTER(mr_moe_layer), vp, C.c_int64, vp, vp,
                                           vp]),
+    "mr_cache_create": (C.c_int, [vp, C.c_size_t, C.c_size_t, C.POINTER(vp)]),
+    "mr_cache_destroy": (C.c_int, [vp]),
+    "mr_cache_register": (C.c_int, [vp, C.c_int32, C.c_int32, C.POINTER(mr_expert_host)]),
+    "mr_cache_get_stats": (C.c_int, [vp, C.POINTER(mr_cache_stats)]),
+    "mr_moe_layer_forward_cached": (C.c_int, [vp, vp, C.c_int32, C.POINTER(mr_moe_layer), vp,
+                                              C.c_int64, vp, vp, vp]),
     "mr_ctx_profile": (C.c_int, [vp, C.c_int]),
     "mr_ctx_profile_read": (C.c_int, [vp, C.POINTER(C.c_double), C.POINTER(C.c_int64), C.c_int]),
     "mr_synth_label": (C.c_uint64, [C.c_uint32] * 4),

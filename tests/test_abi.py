@@ -53,7 +53,9 @@ def test_struct_layout_matches_c_compiler(tmp_path):
               ("mr_router_config", ["top_k", "renorm_eps", "correction_bias"]),
               ("mr_expert_ptrs", ["scales", "biases"]),
               ("mr_moe_layer", ["router", "router_w", "gate", "expert_table", "shared_down",
-                                "swiglu_limit", "weight_placement"])]
+                                "swiglu_limit", "weight_placement"]),
+              ("mr_expert_host", ["scales", "biases", "packed_bytes", "scale_bytes"]),
+              ("mr_cache_stats", ["resident", "hits", "evictions", "bytes_copied"])]
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "minirun_moe.h"',
              "int main(void) {"]
     for s, fields in checks:
