@@ -29,7 +29,10 @@ namespace mr {
 
 constexpr int kTmaRows = 64;
 constexpr int kTmaGps = 8;  // groups per stage
-constexpr int kTmaConsumerWarps = 16;                   // 4 m-tiles x kKSplit
+#ifndef MR_TMA_CONSUMER_WARPS
+#define MR_TMA_CONSUMER_WARPS 16
+#endif
+constexpr int kTmaConsumerWarps = MR_TMA_CONSUMER_WARPS;  // 4 m-tiles x kKSplit
 constexpr int kKSplit = kTmaConsumerWarps / 4;           // warps sharing an m-tile
 constexpr int kGpw = kTmaGps / kKSplit;                  // groups per warp per stage
 constexpr int kTmaConsumers = kTmaConsumerWarps * 32;
@@ -164,18 +167,66 @@ MR_DEVICE void lds_scale2(float (&v)[2], const char* p) {
   }
 }
 
-// Group sums of x for 2 consecutive groups; with XP == 2 each group's sum is
-// stored as two 32-row partials, added here in order.
-template <int XP>
-MR_DEVICE void ldg_xsum2(float (&X)[2], const float* p) {
-  if constexpr (XP == 1) {
+// Group sums of x for N (2 or 4) consecutive groups; with XP == 2 each
+// group's sum is stored as two 32-row partials, added here in order.
+template <int XP, int N>
+MR_DEVICE void ldg_xsum(float (&X)[N], const float* p) {
+  static_assert(N == 2 || N == 4, "2 or 4 groups");
+  if constexpr (XP == 1 && N == 2) {
     const float2 a = __ldg(reinterpret_cast<const float2*>(p));
     X[0] = a.x;
     X[1] = a.y;
-  } else {
+  } else if constexpr (XP == 1) {
     const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-    X[0] = a.x + a.y;
-    X[1] = a.z + a.w;
+    X[0] = a.x;
+    X[1] = a.y;
+    X[2] = a.z;
+    X[3] = a.w;
+  } else {
+#pragma unroll
+    for (int h = 0; h < N / 2; ++h) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(p) + h);
+      X[2 * h] = a.x + a.y;
+      X[2 * h + 1] = a.z + a.w;
+    }
+  }
+}
+
+// N (2 or 4) consecutive scales (or biases) from shared memory, as fp32.
+template <int SD, int N>
+MR_DEVICE void lds_scales(float (&v)[N], uint32_t a) {
+  static_assert(N == 2 || N == 4, "2 or 4 groups");
+  if constexpr (SD == MR_DTYPE_F32) {
+    if constexpr (N == 2) {
+      const uint2 u = lds_b64(a);
+      v[0] = __uint_as_float(u.x);
+      v[1] = __uint_as_float(u.y);
+    } else {
+      const uint4 u = lds_b128(a);
+      v[0] = __uint_as_float(u.x);
+      v[1] = __uint_as_float(u.y);
+      v[2] = __uint_as_float(u.z);
+      v[3] = __uint_as_float(u.w);
+    }
+  } else {
+    uint32_t w[N / 2];
+    if constexpr (N == 2) {
+      w[0] = lds_b32(a);
+    } else {
+      const uint2 u = lds_b64(a);
+      w[0] = u.x;
+      w[1] = u.y;
+    }
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      if constexpr (SD == MR_DTYPE_BF16) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      } else {
+        v[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xffffu)));
+        v[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
+      }
+    }
   }
 }
 
@@ -356,32 +407,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         wb[j][0] = v.x; wb[j][1] = v.y; wb[j][2] = v.z; wb[j][3] = v.w;
       }
     }
-    if constexpr (SD == MR_DTYPE_F32) {
-      const uint2 s0 = lds_b64(stg + offSa), z0 = lds_b64(stg + offSa + ST::kSBytes);
-      const uint2 s1 = lds_b64(stg + offSb), z1 = lds_b64(stg + offSb + ST::kSBytes);
-      sa[0] = __uint_as_float(s0.x); sa[1] = __uint_as_float(s0.y);
-      za[0] = __uint_as_float(z0.x); za[1] = __uint_as_float(z0.y);
-      sb[0] = __uint_as_float(s1.x); sb[1] = __uint_as_float(s1.y);
-      zb[0] = __uint_as_float(z1.x); zb[1] = __uint_as_float(z1.y);
-    } else {
-      const uint32_t s0 = lds_b32(stg + offSa), z0 = lds_b32(stg + offSa + ST::kSBytes);
-      const uint32_t s1 = lds_b32(stg + offSb), z1 = lds_b32(stg + offSb + ST::kSBytes);
-      if constexpr (SD == MR_DTYPE_BF16) {
-        sa[0] = __uint_as_float(s0 << 16); sa[1] = __uint_as_float(s0 & 0xffff0000u);
-        za[0] = __uint_as_float(z0 << 16); za[1] = __uint_as_float(z0 & 0xffff0000u);
-        sb[0] = __uint_as_float(s1 << 16); sb[1] = __uint_as_float(s1 & 0xffff0000u);
-        zb[0] = __uint_as_float(z1 << 16); zb[1] = __uint_as_float(z1 & 0xffff0000u);
-      } else {
-        sa[0] = __half2float(__ushort_as_half((unsigned short)(s0 & 0xffffu)));
-        sa[1] = __half2float(__ushort_as_half((unsigned short)(s0 >> 16)));
-        za[0] = __half2float(__ushort_as_half((unsigned short)(z0 & 0xffffu)));
-        za[1] = __half2float(__ushort_as_half((unsigned short)(z0 >> 16)));
-        sb[0] = __half2float(__ushort_as_half((unsigned short)(s1 & 0xffffu)));
-        sb[1] = __half2float(__ushort_as_half((unsigned short)(s1 >> 16)));
-        zb[0] = __half2float(__ushort_as_half((unsigned short)(z1 & 0xffffu)));
-        zb[1] = __half2float(__ushort_as_half((unsigned short)(z1 >> 16)));
-      }
-    }
+    lds_scales<SD, kGpw>(sa, stg + offSa);
+    lds_scales<SD, kGpw>(za, stg + offSa + ST::kSBytes);
+    lds_scales<SD, kGpw>(sb, stg + offSb);
+    lds_scales<SD, kGpw>(zb, stg + offSb + ST::kSBytes);
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + slot);  // this warp's stage data is in registers
     if (++slot == (uint32_t)nst) {
@@ -482,7 +511,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           xb[j][4] = v1.x; xb[j][5] = v1.y; xb[j][6] = v1.z; xb[j][7] = v1.w;
         }
         float X[kGpw];
-        ldg_xsum2<XP>(X, xs);
+        ldg_xsum<XP, kGpw>(X, xs);
         xq += kTmaGps * kGroup;
         xs += kTmaGps * XP;
         float acc[kGpw][4];
@@ -522,8 +551,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
               xb[j][4] = v1.x; xb[j][5] = v1.y; xb[j][6] = v1.z; xb[j][7] = v1.w;
             }
             float X0[kGpw], X1[kGpw];
-            ldg_xsum2<XP>(X0, xp0[t]);
-            ldg_xsum2<XP>(X1, xp1[t]);
+            ldg_xsum<XP, kGpw>(X0, xp0[t]);
+            ldg_xsum<XP, kGpw>(X1, xp1[t]);
             float acc[kGpw][4];
 #pragma unroll
             for (int j = 0; j < kGpw; ++j) {
