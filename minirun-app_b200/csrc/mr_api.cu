@@ -801,7 +801,7 @@ static LogitsShape logits_shape(const mr_ctx* ctx, int64_t T, int E, int64_t H) 
   const int64_t base = (int64_t)s.mtiles * s.tblocks;
   const int64_t target = 8LL * ctx->sm_count;  // warps
   int64_t ks = std::max<int64_t>(1, target / std::max<int64_t>(base, 1));
-  ks = std::min<int64_t>(ks, std::max<int64_t>(1, H / 256));
+  ks = std::min<int64_t>(ks, std::max<int64_t>(1, H / 128));
   int64_t chunk = (H + ks - 1) / ks;
   chunk = (chunk + 31) / 32 * 32;
   s.kchunk = (int)chunk;

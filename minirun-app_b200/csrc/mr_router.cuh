@@ -327,15 +327,23 @@ __global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
     unsigned nonfinite = 0;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) sc[i] = 0.0f;
-    // partial logits summed in partial order; the loads of one partial are
-    // independent of each other
-    for (int s = 0; s < p.ks; ++s) {
-      const float* ps = p.part + ((int64_t)s * p.T + t) * p.E;
-      float v[kPer];
+    // partial logits summed in partial order; four partials' loads are in
+    // flight together
+    for (int s0 = 0; s0 < p.ks; s0 += 4) {
+      float v[4][kPer];
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) v[i] = (lane + 32 * i < p.E) ? __ldcg(ps + lane + 32 * i) : 0.0f;
+      for (int u = 0; u < 4; ++u) {
+        const float* ps = p.part + ((int64_t)(s0 + u) * p.T + t) * p.E;
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) sc[i] += v[i];
+        for (int i = 0; i < kPer; ++i)
+          v[u][i] = (s0 + u < p.ks && lane + 32 * i < p.E) ? __ldcg(ps + lane + 32 * i) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (s0 + u < p.ks) {
+#pragma unroll
+          for (int i = 0; i < kPer; ++i) sc[i] += v[u][i];
+        }
     }
     if (p.logits_out) {
 #pragma unroll
@@ -453,6 +461,12 @@ __global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
     }
   }
   if (!p.build_plan) return;
+  if (gridDim.x == 1) {
+    // the only CTA: its ids are visible to all its threads after the barrier
+    __syncthreads();
+    build_plan_cta<256>(p.plan);
+    return;
+  }
   __shared__ int s_last;
   __syncthreads();
   if (threadIdx.x == 0) {
