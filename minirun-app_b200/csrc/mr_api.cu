@@ -169,6 +169,7 @@ static cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 __global__ void combine_kernel(const float* __restrict__ part, const float* __restrict__ weights,
                                int T, int k, int64_t H, int weight_after_down, int has_shared,
                                uint16_t* __restrict__ out) {
+  pdl_wait_and_release();
   const int64_t n = (int64_t)T * H;
   const int Tk = T * k;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -842,14 +843,15 @@ static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
   tp.counter = ctx->d_counters + (kMaxCounters - 1);
   const int grid = (int)((T + 7) / 8);
   const int epl = (c->experts + 31) / 32;
-  if (epl <= 1) topk_kernel<1><<<grid, 256, 0, s>>>(tp);
-  else if (epl <= 2) topk_kernel<2><<<grid, 256, 0, s>>>(tp);
-  else if (epl <= 4) topk_kernel<4><<<grid, 256, 0, s>>>(tp);
-  else if (epl <= 8) topk_kernel<8><<<grid, 256, 0, s>>>(tp);
-  else if (epl <= 12) topk_kernel<12><<<grid, 256, 0, s>>>(tp);
-  else if (epl <= 16) topk_kernel<16><<<grid, 256, 0, s>>>(tp);
-  else topk_kernel<32><<<grid, 256, 0, s>>>(tp);
-  return cuda_check(ctx, cudaGetLastError(), "topk_kernel");
+  cudaError_t st;
+  if (epl <= 1) st = launch_pdl(topk_kernel<1>, grid, 256, 0, s, tp);
+  else if (epl <= 2) st = launch_pdl(topk_kernel<2>, grid, 256, 0, s, tp);
+  else if (epl <= 4) st = launch_pdl(topk_kernel<4>, grid, 256, 0, s, tp);
+  else if (epl <= 8) st = launch_pdl(topk_kernel<8>, grid, 256, 0, s, tp);
+  else if (epl <= 12) st = launch_pdl(topk_kernel<12>, grid, 256, 0, s, tp);
+  else if (epl <= 16) st = launch_pdl(topk_kernel<16>, grid, 256, 0, s, tp);
+  else st = launch_pdl(topk_kernel<32>, grid, 256, 0, s, tp);
+  return cuda_check(ctx, st, "topk_kernel");
 }
 
 mr_status mr_router_select(mr_ctx* ctx, const uint16_t* x, int64_t T, int64_t H,
@@ -883,8 +885,8 @@ mr_status mr_router_select(mr_ctx* ctx, const uint16_t* x, int64_t T, int64_t H,
   lp.part = part;
   lp.logit_blocks = ls.blocks;
   lp.do_prep = 0;
-  logits_kernel<<<ls.blocks, 128, 0, s>>>(lp);
-  if ((st = cuda_check(ctx, cudaGetLastError(), "logits_kernel"))) return st;
+  if ((st = cuda_check(ctx, launch_pdl(logits_kernel, ls.blocks, 128, 0, s, lp), "logits_kernel")))
+    return st;
   return topk_launch(ctx, part, ls.kq, T, cfg, ids, weights, margins, logits_out, false, nullptr,
                      nullptr, nullptr, 8, s);
 }
@@ -962,11 +964,12 @@ static mr_status route_tokens(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t
   lp.do_prep = 1;
   const int64_t chunks = T * (H / 16);
   const int prep_blocks = (int)std::min<int64_t>((chunks + 127) / 128, 2 * ctx->sm_count);
+  mr_status st;
   {
     ProfScope ps(ctx, MR_KERNEL_ROUTER_LOGITS, s);
-    logits_kernel<<<ls.blocks + prep_blocks, 128, 0, s>>>(lp);
+    st = cuda_check(ctx, launch_pdl(logits_kernel, ls.blocks + prep_blocks, 128, 0, s, lp),
+                    "logits_kernel");
   }
-  mr_status st = cuda_check(ctx, cudaGetLastError(), "logits_kernel");
   if (st) return st;
   ProfScope ps(ctx, MR_KERNEL_TOPK_PLAN, s);
   return topk_launch(ctx, part, ls.kq, T, &L->router, ids, wts, margins, nullptr, true, rp.nseg,
@@ -1257,10 +1260,12 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   if ((st = run_experts(ctx, L, r, s))) return st;
   const int64_t n_out = T * H;
   const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 4 * ctx->sm_count));
-  combine_kernel<<<cgrid, 256, 0, s>>>(part2, wts, (int)T, k, H,
-                                        L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0,
-                                        has_shared ? 1 : 0, out);
-  return cuda_check(ctx, cudaGetLastError(), "combine_kernel");
+  return cuda_check(ctx,
+                    launch_pdl(combine_kernel, cgrid, 256, 0, s, (const float*)part2,
+                               (const float*)wts, (int)T, k, H,
+                               L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0,
+                               has_shared ? 1 : 0, out),
+                    "combine_kernel");
 }
 
 mr_status mr_moe_layer_forward_host(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x_host,
@@ -2173,10 +2178,13 @@ mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* c, int32_t layer_id
   if ((st = run_experts(ctx, &Lt, r, s))) return st;
   const int64_t n_out = T * H;
   const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 4 * ctx->sm_count));
-  combine_kernel<<<cgrid, 256, 0, s>>>(part2, wts, (int)T, k, H,
-                                        L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0,
-                                        has_shared ? 1 : 0, out);
-  if ((st = cuda_check(ctx, cudaGetLastError(), "combine_kernel"))) return st;
+  if ((st = cuda_check(ctx,
+                       launch_pdl(combine_kernel, cgrid, 256, 0, s, (const float*)part2,
+                                  (const float*)wts, (int)T, k, H,
+                                  L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0,
+                                  has_shared ? 1 : 0, out),
+                       "combine_kernel")))
+    return st;
   if (ids_out)
     st = cuda_check(ctx, cudaMemcpyAsync(ids_out, ids, Tk * sizeof(int32_t),
                                          cudaMemcpyDeviceToDevice, s),

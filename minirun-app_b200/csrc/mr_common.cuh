@@ -12,6 +12,8 @@
 
 #include "minirun_moe.h"
 
+#include <utility>
+
 #define MR_DEVICE __device__ __forceinline__
 
 namespace mr {
@@ -107,6 +109,15 @@ MR_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
                : "memory");
 }
 // Makes initialised barriers visible to the async (TMA) proxy.
+// Programmatic dependent launch (kernels launched with launch_pdl): wait
+// until the previous kernel in the stream has completed and its memory is
+// visible, then let the next kernel in the stream start launching. No-ops
+// for a kernel launched without the attribute.
+MR_DEVICE void pdl_wait_and_release() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 MR_DEVICE void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -257,4 +268,24 @@ constexpr int kMaxCounters = 4096;
 mr_status fail(mr_ctx* ctx, mr_status st, const std::string& msg);
 mr_status cuda_check(mr_ctx* ctx, cudaError_t err, const char* what);
 mr_status ensure_workspace(mr_ctx* ctx, size_t bytes);
+// Launches `kernel` with programmatic stream serialization: it may begin
+// launching while the previous kernel in the stream is still running; the
+// kernel's pdl_wait_and_release() orders it after that kernel's completion.
+// This hides the launch gap between the short kernels of a decode step.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 }  // namespace mr

@@ -257,6 +257,7 @@ MR_DEVICE void warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_fla
 template <int BITS, int SD, int EPI, int NT>
 __global__ void __launch_bounds__(kTmaThreads, 1)
     gemv_tma_kernel(const GemvParams p, const __grid_constant__ TmaMaps maps, const int nst) {
+  pdl_wait_and_release();
   using ST = TmaStage<BITS, SD, EPI>;
   constexpr int LW = QTraits<BITS>::kLaneWords;
   constexpr float kC = QTraits<BITS>::kMagic;

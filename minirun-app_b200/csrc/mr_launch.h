@@ -108,8 +108,7 @@ inline cudaError_t launch_tma_inst(const GemvParams& p, const TmaMaps& m, int gr
   auto kern = gemv_tma_kernel<BITS, SD, EPI, NT>;
   cudaError_t e = opt_in_smem(kern, smem, done);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kTmaThreads, smem, s>>>(p, m, nst);
-  return cudaGetLastError();
+  return launch_pdl(kern, grid, kTmaThreads, smem, s, p, m, nst);
 }
 
 template <int BITS, int SD, int EPI>

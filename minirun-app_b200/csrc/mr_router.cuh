@@ -94,6 +94,7 @@ struct LogitsParams {
 };
 
 __global__ void __launch_bounds__(128) logits_kernel(const LogitsParams p) {
+  pdl_wait_and_release();
   if ((int)blockIdx.x >= p.logit_blocks) {
     if (!p.do_prep) return;
     const int64_t nb = gridDim.x - p.logit_blocks;
@@ -319,6 +320,7 @@ MR_DEVICE bool better(float va, int ia, float vb, int ib) {
 // (Operators/MoE.swift:128, Operators/DeepSeekV4Routing.swift:215-219).
 template <int EPL>  // experts per lane (E <= 32 * EPL)
 __global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
+  pdl_wait_and_release();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t < p.T) {
