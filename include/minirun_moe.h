@@ -52,7 +52,9 @@ typedef enum mr_status {
   MR_ERR_TIMEOUT = 6,          /* a bounded device/host wait expired       */
   MR_ERR_BUDGET = 7,           /* refused: byte budget cannot hold the set */
   MR_ERR_NCCL = 8,             /* an NCCL call failed                      */
-  MR_ERR_STATE = 9             /* call out of order (e.g. EP not initialised) */
+  MR_ERR_STATE = 9,            /* call out of order (e.g. EP not initialised) */
+  MR_ERR_IO = 10,              /* a file could not be opened or read whole */
+  MR_ERR_INTEGRITY = 11        /* read bytes fail their recorded SHA-256   */
 } mr_status;
 
 typedef enum mr_dtype {
@@ -360,6 +362,83 @@ mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* cache, int32_t laye
                                       const mr_moe_layer* layer, const uint16_t* x,
                                       int64_t tokens, uint16_t* out, int32_t* ids_out,
                                       void* stream);
+
+/* ------------------------------------------------------- tile containers
+ * MNRNTIL1, the reference's on-disk quantized tile format
+ * (Sources/StorageCore/Container/QuantizedTileContainer.swift:378-1181): a
+ * 16 KiB header, then tiles of output rows, each [packed | scales | biases
+ * (affine only)] with every tile and sub-region on a 16 KiB boundary, and an
+ * optional SHA-256 per tile in the header. Versions 1-3 are read; a header
+ * is accepted only if every derivable field agrees with its geometry (the
+ * reference reader's rules). Host code only: no GPU needed. */
+typedef struct mr_tiles mr_tiles; /* an open container */
+
+#define MR_TILE_MODE_MXFP4 0      /* e2m1 codes, e8m0 scale per 32 */
+#define MR_TILE_MODE_AFFINE 1     /* MLX affine: scale and bias per group */
+#define MR_TILE_MODE_FP8_BLOCK 2  /* e4m3 codes, 2-D e8m0 block scales */
+#define MR_TILE_SCALE_E8M0 0
+#define MR_TILE_SCALE_F16 1
+#define MR_TILE_SCALE_BF16 2
+#define MR_TILE_SCALE_F32 3
+#define MR_TILE_FLAG_BIASES 1u
+#define MR_TILE_FLAG_DIGESTS 2u
+#define MR_TILE_FLAG_BLOCK_SCALES_2D 4u
+#define MR_TILE_FLAG_PADDED 8u
+#define MR_TILE_CONTENT_SYNTHETIC 0
+#define MR_TILE_CONTENT_CHECKPOINT 1
+
+/* A container's geometry (TileGeometry) and the layout derived from it
+ * (QuantizedTileContainer.Layout); byte offsets within a tile. */
+typedef struct mr_tile_layout {
+  int32_t rows, cols, group_size, bits;
+  int32_t quant_mode, scale_dtype, scale_block_rows;
+  int32_t version, content_kind;
+  uint32_t feature_flags;
+  int64_t tile_count;
+  uint64_t seed;
+  int64_t packed_bytes, scale_bytes, bias_bytes; /* bias_bytes 0 without biases */
+  int64_t scale_offset, bias_offset;              /* bias_offset 0 without biases */
+  int64_t tile_stride, first_tile_offset, total_bytes;
+  int64_t packed_region_bytes, scale_region_bytes;
+} mr_tile_layout;
+
+/* QuantizedTileContainer.open(path:) (:789-832): read and validate the
+ * header, check the file holds every tile. verify_digests: mr_tiles_read
+ * checks each tile against its recorded SHA-256 (when the file has them).
+ * MR_ERR_IO (missing / truncated), MR_ERR_INVALID_ARGUMENT (bad magic,
+ * version, malformed or contradictory header), message in msg. */
+mr_status mr_tiles_open(const char* path, int verify_digests, mr_tiles** out, char* msg,
+                        size_t msg_len);
+mr_status mr_tiles_close(mr_tiles* tiles);
+mr_status mr_tiles_get_layout(const mr_tiles* tiles, mr_tile_layout* out);
+/* One whole tile (tile_stride bytes) into dst: one pread, then the digest
+ * check (verifyTileDigest, :1153-1181) -> MR_ERR_INTEGRITY on mismatch. */
+mr_status mr_tiles_read(mr_tiles* tiles, int64_t tile, void* dst, size_t dst_bytes, char* msg,
+                        size_t msg_len);
+/* QuantizedTileContainer.layout(geometry:tileCount:...) (:441-580): fill the
+ * derived fields of `lay` from its geometry fields (rows, cols, group_size,
+ * bits, quant_mode, scale_dtype, scale_block_rows, content_kind, seed);
+ * MR_ERR_UNSUPPORTED with the reason for a geometry the format rejects. */
+mr_status mr_tiles_layout_for(mr_tile_layout* lay, int64_t tile_count, int with_digests,
+                              char* msg, size_t msg_len);
+/* QuantizedTileContainer.encodedHeader (:725-784): the 16384-byte header of
+ * a layout (digests: tile_count x 32 bytes when the layout records them),
+ * for writers that stream the tile bytes themselves. */
+mr_status mr_tiles_encode_header(const mr_tile_layout* lay, const uint8_t* digests,
+                                 uint8_t* header, char* msg, size_t msg_len);
+/* FIPS 180-4 SHA-256 (the tile digest). */
+mr_status mr_sha256(const void* data, size_t bytes, uint8_t out[32]);
+
+/* Registers (layer, expert) with the cache as three affine tiles (gate,
+ * up, down) of open containers — the expert path's TileReader
+ * (Sources/StorageCore/Pager/TileReader.swift:216-340,
+ * ModelAdapters/Loading/QwenExpertBackends.swift:377-505): on a miss the
+ * cache reads each tile with one pread into pinned host staging, checks its
+ * digest when the container was opened with verification, and copies the
+ * packed / scale / bias sub-regions to the expert's HBM slot. The
+ * containers must stay open while registered. */
+mr_status mr_cache_register_tiles(mr_cache* cache, int32_t layer, int32_t expert,
+                                  mr_tiles* const containers[3], const int64_t tiles[3]);
 
 /* ----------------------------------------------------------- profiling
  * CUDA-event timing of the kernels mr_moe_layer_forward launches (off by

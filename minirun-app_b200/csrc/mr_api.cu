@@ -14,6 +14,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "mr_tiles.h"
 #include "mr_launch.h"
 #include "mr_router.cuh"
 
@@ -456,6 +457,8 @@ const char* mr_status_string(mr_status st) {
     case MR_ERR_BUDGET: return "budget refused";
     case MR_ERR_NCCL: return "NCCL error";
     case MR_ERR_STATE: return "call out of order";
+    case MR_ERR_IO: return "file could not be read";
+    case MR_ERR_INTEGRITY: return "integrity check failed";
   }
   return "unknown status";
 }
@@ -1880,6 +1883,8 @@ struct mr_cache {
     mr_expert_host host;
     size_t off[9];  // slot offsets: packed, scales, biases of gate, up, down
     int slot = -1;
+    mr_tiles* src[3] = {nullptr, nullptr, nullptr};  // file-backed: tiles of open containers
+    int64_t tile[3] = {0, 0, 0};
   };
   struct Slot {
     uint64_t key = ~0ull;
@@ -1899,6 +1904,8 @@ struct mr_cache {
   size_t ids_cap = 0;
   mr_expert_ptrs* table_h = nullptr;
   size_t table_cap = 0;
+  char* stage_h = nullptr;  // tiles read from containers, on their way to HBM
+  size_t stage_cap = 0;
 };
 
 namespace {
@@ -1959,19 +1966,21 @@ mr_status mr_cache_destroy(mr_cache* c) {
   if (c->done) cudaEventDestroy(c->done);
   if (c->ids_h) cudaFreeHost(c->ids_h);
   if (c->table_h) cudaFreeHost(c->table_h);
+  if (c->stage_h) cudaFreeHost(c->stage_h);
   delete c;
   return MR_OK;
 }
 
-mr_status mr_cache_register(mr_cache* c, int32_t layer, int32_t expert, const mr_expert_host* h) {
-  if (!c || !h || layer < 0 || expert < 0) return MR_ERR_INVALID_ARGUMENT;
-  mr_cache::Reg r;
-  r.host = *h;
+}  // extern "C"
+
+namespace {
+
+// Slot offsets of a registration (host sizes already set); stores it under
+// (layer, expert), dropping a resident copy of an earlier registration.
+mr_status cache_store_reg(mr_cache* c, int32_t layer, int32_t expert, mr_cache::Reg& r) {
+  const mr_expert_host* h = &r.host;
   size_t off = 0;
   for (int p = 0; p < 3; ++p) {
-    if (!h->packed[p] || !h->scales[p] || !h->biases[p] || !h->packed_bytes[p] ||
-        !h->scale_bytes[p])
-      return fail(c->ctx, MR_ERR_INVALID_ARGUMENT, "an expert projection's host array is missing");
     r.off[3 * p] = off;
     off = align256(off + h->packed_bytes[p]);
     r.off[3 * p + 1] = off;
@@ -1991,6 +2000,44 @@ mr_status mr_cache_register(mr_cache* c, int32_t layer, int32_t expert, const mr
   }
   c->regs[key] = r;
   return MR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+mr_status mr_cache_register(mr_cache* c, int32_t layer, int32_t expert, const mr_expert_host* h) {
+  if (!c || !h || layer < 0 || expert < 0) return MR_ERR_INVALID_ARGUMENT;
+  for (int p = 0; p < 3; ++p)
+    if (!h->packed[p] || !h->scales[p] || !h->biases[p] || !h->packed_bytes[p] ||
+        !h->scale_bytes[p])
+      return fail(c->ctx, MR_ERR_INVALID_ARGUMENT, "an expert projection's host array is missing");
+  mr_cache::Reg r;
+  r.host = *h;
+  return cache_store_reg(c, layer, expert, r);
+}
+
+mr_status mr_cache_register_tiles(mr_cache* c, int32_t layer, int32_t expert,
+                                  mr_tiles* const containers[3], const int64_t tiles[3]) {
+  if (!c || !containers || !tiles || layer < 0 || expert < 0) return MR_ERR_INVALID_ARGUMENT;
+  mr_cache::Reg r;
+  memset(&r.host, 0, sizeof r.host);
+  for (int p = 0; p < 3; ++p) {
+    mr_tiles* t = containers[p];
+    if (!t) return fail(c->ctx, MR_ERR_INVALID_ARGUMENT, "a projection's container is missing");
+    const mr_tile_layout& L = t->layout;
+    if (L.quant_mode != MR_TILE_MODE_AFFINE)
+      return fail(c->ctx, MR_ERR_UNSUPPORTED,
+                  "expert tiles must be affine; '" + t->path + "' is not");
+    if (tiles[p] < 0 || tiles[p] >= L.tile_count)
+      return fail(c->ctx, MR_ERR_INVALID_ARGUMENT,
+                  "tile " + std::to_string(tiles[p]) + " is outside '" + t->path + "'");
+    r.src[p] = t;
+    r.tile[p] = tiles[p];
+    r.host.packed_bytes[p] = (size_t)L.packed_bytes;
+    r.host.scale_bytes[p] = (size_t)L.scale_bytes;
+  }
+  return cache_store_reg(c, layer, expert, r);
 }
 
 mr_status mr_cache_get_stats(const mr_cache* c, mr_cache_stats* out) {
@@ -2097,6 +2144,8 @@ mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* c, int32_t layer_id
     }
   }
   memset(c->table_h, 0, (size_t)E * sizeof(mr_expert_ptrs));
+  // misses registered as container tiles: read after the slots are chosen
+  std::vector<std::pair<mr_cache::Reg*, char*>> file_misses;
   for (size_t i = 0; i < need.size(); ++i) {
     mr_cache::Reg& r = *regs[i];
     if (r.slot < 0) {
@@ -2124,21 +2173,25 @@ mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* c, int32_t layer_id
       r.slot = pick;
       ++c->stats.misses;
       char* base = c->pool + (size_t)pick * c->slot_bytes;
-      const void* src[9];
-      size_t bytes[9];
-      for (int p = 0; p < 3; ++p) {
-        src[3 * p] = r.host.packed[p];
-        bytes[3 * p] = r.host.packed_bytes[p];
-        src[3 * p + 1] = r.host.scales[p];
-        src[3 * p + 2] = r.host.biases[p];
-        bytes[3 * p + 1] = bytes[3 * p + 2] = r.host.scale_bytes[p];
-      }
-      for (int a = 0; a < 9; ++a) {
-        if ((st = cuda_check(ctx, cudaMemcpyAsync(base + r.off[a], src[a], bytes[a],
-                                                  cudaMemcpyHostToDevice, c->copy),
-                             "copy expert to HBM")))
-          return st;
-        c->stats.bytes_copied += (int64_t)bytes[a];
+      if (r.src[0]) {
+        file_misses.emplace_back(&r, base);
+      } else {
+        const void* src[9];
+        size_t bytes[9];
+        for (int p = 0; p < 3; ++p) {
+          src[3 * p] = r.host.packed[p];
+          bytes[3 * p] = r.host.packed_bytes[p];
+          src[3 * p + 1] = r.host.scales[p];
+          src[3 * p + 2] = r.host.biases[p];
+          bytes[3 * p + 1] = bytes[3 * p + 2] = r.host.scale_bytes[p];
+        }
+        for (int a = 0; a < 9; ++a) {
+          if ((st = cuda_check(ctx, cudaMemcpyAsync(base + r.off[a], src[a], bytes[a],
+                                                    cudaMemcpyHostToDevice, c->copy),
+                               "copy expert to HBM")))
+            return st;
+          c->stats.bytes_copied += (int64_t)bytes[a];
+        }
       }
     }
     const char* base = c->pool + (size_t)r.slot * c->slot_bytes;
@@ -2147,6 +2200,50 @@ mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* c, int32_t layer_id
       t.packed[p] = reinterpret_cast<const uint32_t*>(base + r.off[3 * p]);
       t.scales[p] = base + r.off[3 * p + 1];
       t.biases[p] = base + r.off[3 * p + 2];
+    }
+  }
+  if (!file_misses.empty()) {
+    // one pread per tile into pinned staging (the previous call's copies out
+    // of it finished before this call's routing synchronisation), the digest
+    // check when enabled, then the three sub-regions of each tile to the slot
+    size_t need_bytes = 0;
+    for (auto& fm : file_misses)
+      for (int p = 0; p < 3; ++p) need_bytes += (size_t)fm.first->src[p]->layout.tile_stride;
+    if ((st = grow_pinned(ctx, &c->stage_h, &c->stage_cap, need_bytes, "cudaHostAlloc(tiles)")))
+      return st;
+    char* stage = c->stage_h;
+    for (auto& fm : file_misses) {
+      mr_cache::Reg& r = *fm.first;
+      for (int p = 0; p < 3; ++p) {
+        mr_tiles* t = r.src[p];
+        const mr_tile_layout& TL = t->layout;
+        char msg[512];
+        const mr_status rs = mr_tiles_read(t, r.tile[p], stage, (size_t)TL.tile_stride, msg, sizeof msg);
+        if (rs) {
+          // the slots chosen for this call's file misses hold nothing usable
+          for (auto& undo : file_misses) {
+            mr_cache::Reg& u = *undo.first;
+            if (u.slot >= 0) {
+              c->slots[u.slot] = mr_cache::Slot{};
+              u.slot = -1;
+              --c->stats.resident;
+              --c->stats.misses;
+            }
+          }
+          return fail(ctx, rs, msg);
+        }
+        const char* src[3] = {stage, stage + TL.scale_offset, stage + TL.bias_offset};
+        const size_t bytes[3] = {(size_t)TL.packed_bytes, (size_t)TL.scale_bytes,
+                                 (size_t)TL.bias_bytes};
+        for (int a = 0; a < 3; ++a) {
+          if ((st = cuda_check(ctx, cudaMemcpyAsync(fm.second + r.off[3 * p + a], src[a], bytes[a],
+                                                    cudaMemcpyHostToDevice, c->copy),
+                               "copy expert tile to HBM")))
+            return st;
+          c->stats.bytes_copied += (int64_t)bytes[a];
+        }
+        stage += TL.tile_stride;
+      }
     }
   }
   if ((st = cuda_check(ctx, cudaMemcpyAsync(table, c->table_h, (size_t)E * sizeof(mr_expert_ptrs),

@@ -12,10 +12,14 @@ from .cache import CachedLayer, ExpertCache
 from .ep import ExpertGroup, MoELayerShard
 from .moe import (MoELayer, ResidentExpertBackend, RouterConfig, router_select,
                   router_select_logits)
+from .tiles import (ExpertContainers, TileContainer, TileContainerError, write_container,
+                    write_expert_containers)
 
 __all__ = [
     "LIB_PATH", "LibraryMissing", "load_library", "AffineBridgeError", "AffineWeights",
     "Context", "MoeError", "Selection", "affine_dequantize", "affine_gather_mm", "affine_mm",
     "validate_desc", "MoELayer", "ResidentExpertBackend", "RouterConfig", "router_select",
     "router_select_logits", "ExpertGroup", "MoELayerShard", "CachedLayer", "ExpertCache",
+    "ExpertContainers", "TileContainer", "TileContainerError", "write_container",
+    "write_expert_containers",
 ]

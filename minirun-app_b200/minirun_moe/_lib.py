@@ -24,6 +24,8 @@ MR_ERR_TIMEOUT = 6
 MR_ERR_BUDGET = 7
 MR_ERR_NCCL = 8
 MR_ERR_STATE = 9
+MR_ERR_IO = 10
+MR_ERR_INTEGRITY = 11
 
 MR_DTYPE_BF16, MR_DTYPE_F16, MR_DTYPE_F32 = 0, 1, 2
 MR_SCORING_SIGMOID, MR_SCORING_SOFTMAX, MR_SCORING_SQRT_SOFTPLUS = 0, 1, 2
@@ -63,6 +65,19 @@ class mr_moe_layer(C.Structure):
 class mr_expert_host(C.Structure):
     _fields_ = [("packed", vp * 3), ("scales", vp * 3), ("biases", vp * 3),
                 ("packed_bytes", C.c_size_t * 3), ("scale_bytes", C.c_size_t * 3)]
+
+
+class mr_tile_layout(C.Structure):
+    _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("group_size", C.c_int32),
+                ("bits", C.c_int32), ("quant_mode", C.c_int32), ("scale_dtype", C.c_int32),
+                ("scale_block_rows", C.c_int32), ("version", C.c_int32),
+                ("content_kind", C.c_int32), ("feature_flags", C.c_uint32),
+                ("tile_count", C.c_int64), ("seed", C.c_uint64),
+                ("packed_bytes", C.c_int64), ("scale_bytes", C.c_int64),
+                ("bias_bytes", C.c_int64), ("scale_offset", C.c_int64),
+                ("bias_offset", C.c_int64), ("tile_stride", C.c_int64),
+                ("first_tile_offset", C.c_int64), ("total_bytes", C.c_int64),
+                ("packed_region_bytes", C.c_int64), ("scale_region_bytes", C.c_int64)]
 
 
 class mr_cache_stats(C.Structure):
@@ -108,6 +123,16 @@ SIGNATURES = {
     "mr_cache_destroy": (C.c_int, [vp]),
     "mr_cache_register": (C.c_int, [vp, C.c_int32, C.c_int32, C.POINTER(mr_expert_host)]),
     "mr_cache_get_stats": (C.c_int, [vp, C.POINTER(mr_cache_stats)]),
+    "mr_cache_register_tiles": (C.c_int, [vp, C.c_int32, C.c_int32, vp * 3, C.c_int64 * 3]),
+    "mr_tiles_open": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(vp), C.c_char_p, C.c_size_t]),
+    "mr_tiles_close": (C.c_int, [vp]),
+    "mr_tiles_get_layout": (C.c_int, [vp, C.POINTER(mr_tile_layout)]),
+    "mr_tiles_read": (C.c_int, [vp, C.c_int64, vp, C.c_size_t, C.c_char_p, C.c_size_t]),
+    "mr_tiles_layout_for": (C.c_int, [C.POINTER(mr_tile_layout), C.c_int64, C.c_int,
+                                      C.c_char_p, C.c_size_t]),
+    "mr_tiles_encode_header": (C.c_int, [C.POINTER(mr_tile_layout), vp, vp, C.c_char_p,
+                                         C.c_size_t]),
+    "mr_sha256": (C.c_int, [vp, C.c_size_t, vp]),
     "mr_moe_layer_forward_cached": (C.c_int, [vp, vp, C.c_int32, C.POINTER(mr_moe_layer), vp,
                                               C.c_int64, vp, vp, vp]),
     "mr_ctx_profile": (C.c_int, [vp, C.c_int]),
