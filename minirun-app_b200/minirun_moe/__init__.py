@@ -12,6 +12,7 @@ from .cache import CachedLayer, ExpertCache
 from .ep import ExpertGroup, MoELayerShard
 from .moe import (MoELayer, ResidentExpertBackend, RouterConfig, router_select,
                   router_select_logits)
+from .checkpoint import Checkpoint, SafetensorsError, SafetensorsFile, write_safetensors
 from .tiles import (ExpertContainers, TileContainer, TileContainerError, write_container,
                     write_expert_containers)
 
@@ -21,5 +22,6 @@ __all__ = [
     "validate_desc", "MoELayer", "ResidentExpertBackend", "RouterConfig", "router_select",
     "router_select_logits", "ExpertGroup", "MoELayerShard", "CachedLayer", "ExpertCache",
     "ExpertContainers", "TileContainer", "TileContainerError", "write_container",
-    "write_expert_containers",
+    "write_expert_containers", "Checkpoint", "SafetensorsError", "SafetensorsFile",
+    "write_safetensors",
 ]
