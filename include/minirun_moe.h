@@ -68,6 +68,7 @@ typedef enum mr_dtype {
 #define MR_DEVERR_NONFINITE_SCORE 0x2u /* router produced NaN/Inf score  */
 #define MR_DEVERR_RENORM_ZERO 0x4u     /* selected weights sum <= 0      */
 #define MR_DEVERR_TIMEOUT 0x8u         /* a bounded device wait expired  */
+#define MR_DEVERR_BAD_TOKEN_ID 0x10u   /* hash routing: token id outside the table */
 
 typedef struct mr_ctx mr_ctx;
 
@@ -268,6 +269,35 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* layer,
                                const uint16_t* x, int64_t tokens, uint16_t* out,
                                int32_t* ids_out, float* weights_out,
                                float* margins_out, void* stream);
+
+/* ------------------------------------------------------ token-hash routing
+ * DeepSeek V4's first layers choose experts by token id, not by score
+ * (Sources/ModelAdapters/Operators/DeepSeekV4Routing.swift:4-64, :231-256):
+ * token t's experts are token_map[token_ids[t] * k + j], j < k, from a
+ * [vocab, k] int32 table; their weights are the router's scores (scoring as
+ * configured, without the correction bias) at those experts, renormalised
+ * and scaled as configured. No margins are produced. A token id outside
+ * [0, vocab) sets MR_DEVERR_BAD_TOKEN_ID (see mr_ctx_check). */
+
+/* DeepSeekV4TokenExpertMap.init (:14-52): host table [vocab, k]; each entry
+ * in [0, experts), no expert twice in a row; slot j's range check precedes
+ * its duplicate check. MR_ERR_INVALID_ARGUMENT with the first violation. */
+mr_status mr_token_map_validate(const int32_t* table, int64_t vocab, int32_t k,
+                                int32_t experts, char* msg, size_t msg_len);
+/* mr_router_select with the .tokenHash choice; token_ids [T] and token_map
+ * [vocab, k] in device memory. */
+mr_status mr_router_select_hashed(mr_ctx* ctx, const uint16_t* x, int64_t tokens,
+                                  int64_t hidden, const uint16_t* router_w,
+                                  const mr_router_config* cfg, const int32_t* token_ids,
+                                  const int32_t* token_map, int64_t vocab, int32_t* ids,
+                                  float* weights, float* logits_out, void* stream);
+/* mr_moe_layer_forward with token-hash routing (DeepSeekV4MoEFFN's hash
+ * layers, Model/DeepSeekV4HashFFN.swift:75-106). */
+mr_status mr_moe_layer_forward_hashed(mr_ctx* ctx, const mr_moe_layer* layer,
+                                      const uint16_t* x, const int32_t* token_ids,
+                                      int64_t tokens, const int32_t* token_map, int64_t vocab,
+                                      uint16_t* out, int32_t* ids_out, float* weights_out,
+                                      void* stream);
 
 /* Host-buffer form of mr_moe_layer_forward, the view of a caller that holds
  * arrays in host memory (the reference's per-layer `eval` boundary,

@@ -815,11 +815,19 @@ static LogitsShape logits_shape(const mr_ctx* ctx, int64_t T, int E, int64_t H) 
   return s;
 }
 
+// Token-hash routing of one call: device table [vocab, k] and token ids [T].
+struct HashChoice {
+  const int32_t* table;
+  const int32_t* token_ids;
+  int64_t vocab;
+};
+
 static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
                              const mr_router_config* c, int32_t* ids, float* weights,
                              float* margins, float* logits_out, bool plan, int* nseg, int4* segs,
                              int* cols, int seg_cols, cudaStream_t s, int plan_base = 0,
-                             int plan_experts = -1, bool foreign_ok = false) {
+                             int plan_experts = -1, bool foreign_ok = false,
+                             const HashChoice* hc = nullptr) {
   TopkParams tp{};
   tp.part = part;
   tp.ks = ks;
@@ -844,6 +852,11 @@ static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
                        seg_cols, plan_base,
                        foreign_ok ? 1 : 0};
   tp.counter = ctx->d_counters + (kMaxCounters - 1);
+  if (hc) {
+    tp.hash_map = hc->table;
+    tp.token_ids = hc->token_ids;
+    tp.vocab = hc->vocab;
+  }
   const int grid = (int)((T + 7) / 8);
   const int epl = (c->experts + 31) / 32;
   cudaError_t st;
@@ -857,9 +870,12 @@ static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
   return cuda_check(ctx, st, "topk_kernel");
 }
 
-mr_status mr_router_select(mr_ctx* ctx, const uint16_t* x, int64_t T, int64_t H,
-                           const uint16_t* router_w, const mr_router_config* cfg, int32_t* ids,
-                           float* weights, float* margins, float* logits_out, void* stream) {
+}  // extern "C"
+
+static mr_status router_select(mr_ctx* ctx, const uint16_t* x, int64_t T, int64_t H,
+                               const uint16_t* router_w, const mr_router_config* cfg,
+                               int32_t* ids, float* weights, float* margins, float* logits_out,
+                               void* stream, const HashChoice* hc) {
   if (!ctx) return MR_ERR_INVALID_ARGUMENT;
   std::string why;
   mr_status st = validate_router(cfg, why);
@@ -891,7 +907,30 @@ mr_status mr_router_select(mr_ctx* ctx, const uint16_t* x, int64_t T, int64_t H,
   if ((st = cuda_check(ctx, launch_pdl(logits_kernel, ls.blocks, 128, 0, s, lp), "logits_kernel")))
     return st;
   return topk_launch(ctx, part, ls.kq, T, cfg, ids, weights, margins, logits_out, false, nullptr,
-                     nullptr, nullptr, 8, s);
+                     nullptr, nullptr, 8, s, 0, -1, false, hc);
+}
+
+extern "C" {
+
+mr_status mr_router_select(mr_ctx* ctx, const uint16_t* x, int64_t T, int64_t H,
+                           const uint16_t* router_w, const mr_router_config* cfg, int32_t* ids,
+                           float* weights, float* margins, float* logits_out, void* stream) {
+  return router_select(ctx, x, T, H, router_w, cfg, ids, weights, margins, logits_out, stream,
+                       nullptr);
+}
+
+mr_status mr_router_select_hashed(mr_ctx* ctx, const uint16_t* x, int64_t T, int64_t H,
+                                  const uint16_t* router_w, const mr_router_config* cfg,
+                                  const int32_t* token_ids, const int32_t* token_map,
+                                  int64_t vocab, int32_t* ids, float* weights, float* logits_out,
+                                  void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  if (!token_ids || !token_map || vocab <= 0)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "hash routing needs the token ids and the token-to-expert table");
+  const HashChoice hc{token_map, token_ids, vocab};
+  return router_select(ctx, x, T, H, router_w, cfg, ids, weights, nullptr, logits_out, stream,
+                       &hc);
 }
 
 mr_status mr_router_select_logits(mr_ctx* ctx, const float* logits, int64_t T,
@@ -948,7 +987,7 @@ struct RoutePlan {
 static mr_status route_tokens(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x, int64_t T,
                               const LogitsShape& ls, float* part, uint16_t* xperm, float* xsum,
                               int32_t* ids, float* wts, float* margins, const RoutePlan& rp,
-                              cudaStream_t s) {
+                              cudaStream_t s, const HashChoice* hc = nullptr) {
   const int E = L->router.experts;
   const int64_t H = L->hidden;
   LogitsParams lp{};
@@ -976,7 +1015,7 @@ static mr_status route_tokens(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t
   if (st) return st;
   ProfScope ps(ctx, MR_KERNEL_TOPK_PLAN, s);
   return topk_launch(ctx, part, ls.kq, T, &L->router, ids, wts, margins, nullptr, true, rp.nseg,
-                     rp.segs, rp.cols, rp.seg_cols, s, rp.base, rp.experts, rp.foreign_ok);
+                     rp.segs, rp.cols, rp.seg_cols, s, rp.base, rp.experts, rp.foreign_ok, hc);
 }
 
 // One K1 (gate/up + SwiGLU -> h, hsum) and K2 (down -> per-slot partials)
@@ -1123,13 +1162,9 @@ static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRu
                              "gemv(down)");
 }
 
-}  // namespace mr
-
-extern "C" {
-
-mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x,
-                               int64_t T, uint16_t* out, int32_t* ids_out, float* weights_out,
-                               float* margins_out, void* stream) {
+static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x, int64_t T,
+                               uint16_t* out, int32_t* ids_out, float* weights_out,
+                               float* margins_out, void* stream, const HashChoice* hc) {
   if (!ctx) return MR_ERR_INVALID_ARGUMENT;
   std::string why;
   mr_status st = validate_layer(L, why);
@@ -1227,7 +1262,8 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   // K0a + K0b: router logits (+ permuted input), top-k, routing plan
   {
     const RoutePlan rp{nseg, segs, cols, seg_cols, 0, E, false};
-    if ((st = route_tokens(ctx, L, x, T, ls, part, xperm, xsum, ids, wts, margins_out, rp, s)))
+    if ((st = route_tokens(ctx, L, x, T, ls, part, xperm, xsum, ids, wts, margins_out, rp, s,
+                           hc)))
       return st;
   }
   if ((um && !um_dense) || pf) {
@@ -1269,6 +1305,58 @@ mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
                                L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0,
                                has_shared ? 1 : 0, out),
                     "combine_kernel");
+}
+
+}  // namespace mr
+
+extern "C" {
+
+mr_status mr_moe_layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x,
+                               int64_t T, uint16_t* out, int32_t* ids_out, float* weights_out,
+                               float* margins_out, void* stream) {
+  return layer_forward(ctx, L, x, T, out, ids_out, weights_out, margins_out, stream, nullptr);
+}
+
+mr_status mr_token_map_validate(const int32_t* table, int64_t vocab, int32_t k, int32_t experts,
+                                char* msg, size_t msg_len) {
+  std::string why;
+  mr_status st = MR_OK;
+  if (!table || vocab <= 0 || k <= 0 || experts <= 0) {
+    why = "vocabulary size, experts per token, and expert count must be positive";
+    st = MR_ERR_INVALID_ARGUMENT;
+  }
+  // slot j's range check precedes its duplicate check, and both precede
+  // slot j+1 (DeepSeekV4Routing.swift:25-45)
+  for (int64_t t = 0; !st && t < vocab; ++t) {
+    const int32_t* row = table + t * k;
+    for (int j = 0; !st && j < k; ++j) {
+      if (row[j] < 0 || row[j] >= experts) {
+        why = "token " + std::to_string(t) + " slot " + std::to_string(j) + " names expert " +
+              std::to_string(row[j]) + ", outside 0..<" + std::to_string(experts);
+        st = MR_ERR_INVALID_ARGUMENT;
+      }
+      for (int i = 0; !st && i < j; ++i)
+        if (row[i] == row[j]) {
+          why = "token " + std::to_string(t) + " names expert " + std::to_string(row[j]) +
+                " more than once";
+          st = MR_ERR_INVALID_ARGUMENT;
+        }
+    }
+  }
+  set_msg(msg, msg_len, why);
+  return st;
+}
+
+mr_status mr_moe_layer_forward_hashed(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x,
+                                      const int32_t* token_ids, int64_t T,
+                                      const int32_t* token_map, int64_t vocab, uint16_t* out,
+                                      int32_t* ids_out, float* weights_out, void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  if (!token_ids || !token_map || vocab <= 0)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "hash routing needs the token ids and the token-to-expert table");
+  const HashChoice hc{token_map, token_ids, vocab};
+  return layer_forward(ctx, L, x, T, out, ids_out, weights_out, nullptr, stream, &hc);
 }
 
 mr_status mr_moe_layer_forward_host(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x_host,

@@ -310,6 +310,11 @@ struct TopkParams {
   int build_plan;
   PlanParams plan;
   unsigned* counter;
+  // token-hash choice (DeepSeek V4's first layers) — optional: token t's
+  // experts are hash_map[token_ids[t] * k + j], j < k
+  const int32_t* hash_map;
+  const int32_t* token_ids;
+  int64_t vocab;
 };
 
 MR_DEVICE bool better(float va, int ia, float vb, int ib) {
@@ -393,7 +398,33 @@ __global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
     unsigned taken = 0;
     int my_id = 0;
     float my_w = 0.0f, kth = 0.0f, rej = 0.0f;
-    for (int r = 0; r <= p.k; ++r) {
+    if (p.hash_map) {
+      // the choice comes from the token's row of the table; the weights are
+      // still the (unbiased) scores of the chosen experts
+      // (Operators/DeepSeekV4Routing.swift:231-256)
+      int id = 0;
+      if (lane < p.k) {
+        const int tok = __ldg(p.token_ids + t);
+        if (tok < 0 || (int64_t)tok >= p.vocab) {
+          atomicOr(p.error, MR_DEVERR_BAD_TOKEN_ID);
+        } else {
+          id = __ldg(p.hash_map + (int64_t)tok * p.k + lane);
+          if (id < 0 || id >= p.E) {
+            atomicOr(p.error, MR_DEVERR_BAD_EXPERT_ID);
+            id = 0;
+          }
+        }
+      }
+      float s_un = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const float v = __shfl_sync(0xffffffffu, sc[i], id & 31);
+        if ((id >> 5) == i) s_un = v;
+      }
+      my_id = id;
+      my_w = s_un;
+    }
+    for (int r = 0; !p.hash_map && r <= p.k; ++r) {
       float bv = -INFINITY;
       int bi = 0x7fffffff, bslot = -1;
 #pragma unroll
@@ -456,7 +487,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
       p.ids[(int64_t)t * p.k + lane] = my_id;
       p.weights[(int64_t)t * p.k + lane] = w;
     }
-    if (p.margins && lane == 0) {
+    if (p.margins && lane == 0 && !p.hash_map) {
       const double a = (double)kth, b = (double)rej;
       const double s = fmax(fabs(a), fabs(b));
       p.margins[t] = (float)(s > 0 ? (a - b) / s : 0.0);

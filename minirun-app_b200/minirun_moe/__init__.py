@@ -10,8 +10,8 @@ from .bridge import (AffineBridgeError, AffineWeights, Context, MoeError, Select
                      affine_dequantize, affine_gather_mm, affine_mm, validate_desc)
 from .cache import CachedLayer, ExpertCache
 from .ep import ExpertGroup, MoELayerShard
-from .moe import (MoELayer, ResidentExpertBackend, RouterConfig, router_select,
-                  router_select_logits)
+from .moe import (MoELayer, ResidentExpertBackend, RouterConfig, TokenExpertMap, router_select,
+                  router_select_hashed, router_select_logits)
 from .checkpoint import Checkpoint, SafetensorsError, SafetensorsFile, write_safetensors
 from .tiles import (ExpertContainers, TileContainer, TileContainerError, write_container,
                     write_expert_containers)
@@ -23,5 +23,5 @@ __all__ = [
     "router_select_logits", "ExpertGroup", "MoELayerShard", "CachedLayer", "ExpertCache",
     "ExpertContainers", "TileContainer", "TileContainerError", "write_container",
     "write_expert_containers", "Checkpoint", "SafetensorsError", "SafetensorsFile",
-    "write_safetensors",
+    "write_safetensors", "TokenExpertMap", "router_select_hashed",
 ]

@@ -26,6 +26,7 @@ MR_ERR_NCCL = 8
 MR_ERR_STATE = 9
 MR_ERR_IO = 10
 MR_ERR_INTEGRITY = 11
+MR_DEVERR_BAD_TOKEN_ID = 0x10
 
 MR_DTYPE_BF16, MR_DTYPE_F16, MR_DTYPE_F32 = 0, 1, 2
 MR_SCORING_SIGMOID, MR_SCORING_SOFTMAX, MR_SCORING_SQRT_SOFTPLUS = 0, 1, 2
@@ -133,6 +134,13 @@ SIGNATURES = {
     "mr_tiles_encode_header": (C.c_int, [C.POINTER(mr_tile_layout), vp, vp, C.c_char_p,
                                          C.c_size_t]),
     "mr_sha256": (C.c_int, [vp, C.c_size_t, vp]),
+    "mr_token_map_validate": (C.c_int, [vp, C.c_int64, C.c_int32, C.c_int32, C.c_char_p,
+                                        C.c_size_t]),
+    "mr_router_select_hashed": (C.c_int, [vp, vp, C.c_int64, C.c_int64, vp,
+                                          C.POINTER(mr_router_config), vp, vp, C.c_int64, vp,
+                                          vp, vp, vp]),
+    "mr_moe_layer_forward_hashed": (C.c_int, [vp, C.POINTER(mr_moe_layer), vp, vp, C.c_int64,
+                                              vp, C.c_int64, vp, vp, vp, vp]),
     "mr_moe_layer_forward_cached": (C.c_int, [vp, vp, C.c_int32, C.POINTER(mr_moe_layer), vp,
                                               C.c_int64, vp, vp, vp]),
     "mr_ctx_profile": (C.c_int, [vp, C.c_int]),

@@ -103,6 +103,56 @@ def router_select(x: torch.Tensor, router_w: torch.Tensor, cfg: RouterConfig,
     return Selection(ids, w, m, lg)
 
 
+class TokenExpertMap:
+    """DeepSeek V4's token -> experts table for its hash-routed layers
+    (Operators/DeepSeekV4Routing.swift:4-64): int32 [vocab, k], validated on
+    the host as the reference's initializer does, then kept on the device."""
+
+    def __init__(self, table, experts: int, device=None):
+        t = torch.as_tensor(table, dtype=torch.int32).contiguous().cpu()
+        if t.dim() != 2:
+            raise AffineBridgeError("token-to-expert table must be [vocabulary, expertsPerToken]")
+        self.vocab, self.k = t.shape
+        self.experts = experts
+        buf = C.create_string_buffer(256)
+        st = L.load().mr_token_map_validate(t.data_ptr(), self.vocab, self.k, experts, buf, 256)
+        if st != L.MR_OK:
+            raise AffineBridgeError(buf.value.decode())
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        self.table = t.to(dev)
+
+
+def _hashed_args(cfg: RouterConfig, token_ids: torch.Tensor, token_map: TokenExpertMap, T: int):
+    if token_map.k != cfg.top_k or token_map.experts != cfg.experts:
+        raise AffineBridgeError("token-to-expert table geometry does not match this router")
+    if token_ids.shape != (T,):
+        raise AffineBridgeError(f"hash routing has {token_ids.numel()} token ids for {T} rows")
+    return token_ids.to(torch.int32).contiguous()
+
+
+def router_select_hashed(x: torch.Tensor, router_w: torch.Tensor, cfg: RouterConfig,
+                         token_ids: torch.Tensor, token_map: TokenExpertMap,
+                         want_logits: bool = False) -> Selection:
+    """The .tokenHash choice of DeepSeekV4Router.select (:231-256): experts from
+    the table, weights from the scores at those experts. No margins."""
+    if x.dim() != 2 or x.dtype != torch.bfloat16 or router_w.dtype != torch.bfloat16:
+        raise AffineBridgeError("x [T, H] and router weight [E, H] must be bfloat16")
+    x = x.contiguous()
+    T = x.shape[0]
+    tok = _hashed_args(cfg, token_ids, token_map, T)
+    dev = x.device
+    ids = torch.empty((T, cfg.top_k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, cfg.top_k), dtype=torch.float32, device=dev)
+    lg = torch.empty((T, cfg.experts), dtype=torch.float32, device=dev) if want_logits else None
+    ctx = Context.get(dev.index)
+    c = cfg.c()
+    ctx.check("mr_router_select_hashed", L.load().mr_router_select_hashed(
+        ctx.handle, _ptr(x), T, x.shape[1], _ptr(router_w.contiguous()), C.byref(c), _ptr(tok),
+        _ptr(token_map.table), token_map.vocab, _ptr(ids), _ptr(w), _ptr(lg),
+        C.c_void_p(_stream())))
+    return Selection(ids, w, None, lg)
+
+
 def router_select_logits(logits: torch.Tensor, cfg: RouterConfig) -> Selection:
     """The same selection from logits produced elsewhere (MoE.swift:98-150)."""
     if logits.dim() != 2 or logits.shape[1] != cfg.experts or logits.dtype != torch.float32:
@@ -216,6 +266,29 @@ class MoELayer:
         return out, sel
 
     __call__ = forward
+
+    def forward_hashed(self, x: torch.Tensor, token_ids: torch.Tensor,
+                       token_map: TokenExpertMap,
+                       out: torch.Tensor | None = None) -> tuple[torch.Tensor, Selection]:
+        """The layer with token-hash routing (mr_moe_layer_forward_hashed)."""
+        if x.dim() != 2 or x.shape[1] != self.hidden or x.dtype != torch.bfloat16:
+            raise AffineBridgeError(f"input must be a non-empty [tokens, {self.hidden}] bfloat16 "
+                                    "matrix")
+        x = x.contiguous()
+        T = x.shape[0]
+        tok = _hashed_args(self.router, token_ids, token_map, T)
+        dev = x.device
+        if out is None:
+            out = torch.empty((T, self.hidden), dtype=torch.bfloat16, device=dev)
+        k = self.router.top_k
+        sel = Selection(torch.empty((T, k), dtype=torch.int32, device=dev),
+                        torch.empty((T, k), dtype=torch.float32, device=dev), None)
+        ctx = Context.get(dev.index)
+        ctx.check("mr_moe_layer_forward_hashed", L.load().mr_moe_layer_forward_hashed(
+            ctx.handle, C.byref(self._c), _ptr(x), _ptr(tok), T, _ptr(token_map.table),
+            token_map.vocab, _ptr(out), _ptr(sel.ids), _ptr(sel.weights),
+            C.c_void_p(_stream())))
+        return out, sel
 
     def forward_host(self, x_host: torch.Tensor, out_host: torch.Tensor,
                      ids_host: torch.Tensor | None = None, device: int | None = None) -> None:

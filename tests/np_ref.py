@@ -88,15 +88,47 @@ def sigmoid32(g):
     return (1.0 / (1.0 + np.exp(-g.astype(np.float64)))).astype(np.float32)
 
 
-def layer(Lw, x_bf16):
+def router_hashed(logits, table, token_ids, scoring="sqrt_softplus", renorm="plain", eps=1e-20,
+                  scale=1.0):
+    """The .tokenHash choice (DeepSeekV4Routing.swift:231-256): experts from
+    the table row of each token id, weights = the scores at those experts."""
+    l = logits.astype(np.float64)
+    if scoring == "sigmoid":
+        s = 1.0 / (1.0 + np.exp(-l))
+    elif scoring == "softmax":
+        e = np.exp(l - l.max(axis=1, keepdims=True))
+        s = e / e.sum(axis=1, keepdims=True)
+    else:
+        s = np.sqrt(np.maximum(l, 0) + np.log1p(np.exp(-np.abs(l))))
+    s = s.astype(np.float32)
+    ids = table[token_ids].astype(np.int32)
+    w = np.take_along_axis(s, ids, axis=1).astype(np.float32)
+    T, k = ids.shape
+    den = np.zeros(T, np.float32)
+    for j in range(k):
+        den = (den + w[:, j]).astype(np.float32)
+    if renorm == "plain":
+        w = (w / den[:, None]).astype(np.float32)
+    elif renorm == "eps" and k > 1:
+        w = (w / (den + np.float32(eps))[:, None]).astype(np.float32)
+    return ids, (w * np.float32(scale)).astype(np.float32)
+
+
+def layer(Lw, x_bf16, hashed=None):
     """Router -> routed (weight before w2, DeepSeekV4ExpertBackend.swift:311-342)
-    -> shared (DeepSeekV4HashFFN.swift:223-255) -> sum."""
+    -> shared (DeepSeekV4HashFFN.swift:223-255) -> sum. hashed = (table,
+    token_ids) routes by token id instead."""
     c = Lw.cfg
     x64 = bf16_to_f32(x_bf16).astype(np.float64)
     r64 = bf16_to_f32(Lw.router_w).astype(np.float64)
     logits = (x64 @ r64.T).astype(np.float32)
-    ids, w, m = router(logits, c.top_k, c.scoring, Lw.correction_bias, c.renorm, c.renorm_eps,
-                       c.routed_scale)
+    if hashed is None:
+        ids, w, m = router(logits, c.top_k, c.scoring, Lw.correction_bias, c.renorm,
+                           c.renorm_eps, c.routed_scale)
+    else:
+        ids, w = router_hashed(logits, hashed[0], hashed[1], c.scoring, c.renorm, c.renorm_eps,
+                               c.routed_scale)
+        m = None
     gb, _ = gather_mm(x_bf16, Lw.gate, ids)
     ub, _ = gather_mm(x_bf16, Lw.up, ids)
     g = bf16_to_f32(gb)
