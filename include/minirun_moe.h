@@ -60,7 +60,8 @@ typedef enum mr_status {
 typedef enum mr_dtype {
   MR_DTYPE_BF16 = 0,
   MR_DTYPE_F16 = 1,
-  MR_DTYPE_F32 = 2
+  MR_DTYPE_F32 = 2,
+  MR_DTYPE_E8M0 = 3 /* MXFP4 scales (uint8 exponents, 2^(e-127)); mr_mxfp4_* only */
 } mr_dtype;
 
 /* Device error word bits (mr_ctx_check). */
@@ -167,6 +168,48 @@ mr_status mr_affine_gather_mm_noalloc(const uint16_t* x, int64_t tokens,
                                       const int32_t* ids, int32_t top_k,
                                       const mr_affine_desc* w, uint16_t* out,
                                       void* stream, char* msg, size_t msg_len);
+
+/* ------------------------------------------------------ MXFP4 op API
+ * Mirrors Sources/MLXBridge/MXFP4Weights.swift and MXFP4Matmul.swift: OCP MX
+ * FP4, e2m1 codes (element 0 of a uint32 word in the low nibble, the byte
+ * image of the checkpoint's uint8 stream) with one e8m0 exponent per 32
+ * input elements, w = e2m1 * 2^(e - 127), no bias. */
+
+/* MXFP4Weights (MXFP4Weights.swift:65-140). experts == 0 means a single
+ * [out, in] matrix; experts > 0 an expert stack. */
+typedef struct mr_mxfp4_desc {
+  const uint32_t* packed; /* [experts?, out, in/8]                         */
+  const uint8_t* scales;  /* [experts?, out, in/32] e8m0 exponents          */
+  int32_t experts;
+  int64_t out_features;
+  int64_t in_features;
+} mr_mxfp4_desc;
+
+/* Host-only validation, the checks of MXFP4Weights.init
+ * (MXFP4Weights.swift:86-140): in a multiple of 8 (the uint32 packing) and of
+ * the group size 32, positive shape, non-NULL pointers. The matmuls of this
+ * build further need in % 512 == 0 and 16-byte aligned packed and scales
+ * (MR_ERR_UNSUPPORTED otherwise; mr_mxfp4_dequantize does not). */
+mr_status mr_mxfp4_validate(const mr_mxfp4_desc* w, char* msg, size_t msg_len);
+
+/* mxfp4MM (MXFP4Matmul.swift:17-34): out[T, out] = x[T, in] . W^T; x, out
+ * bf16, fp32 accumulation, output rounded to bf16. */
+mr_status mr_mxfp4_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens,
+                      const mr_mxfp4_desc* w, uint16_t* out, void* stream);
+
+/* mxfp4GatherMM (MXFP4Matmul.swift:74-112): out[t, j, :] = W[ids[t, j]] .
+ * x[t, :], ids int32 [T, k] on the device (unsorted, repeats allowed), out
+ * bf16 [T, k, out]. An id outside [0, experts) sets MR_DEVERR_BAD_EXPERT_ID
+ * and leaves that row unwritten. */
+mr_status mr_mxfp4_gather_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens,
+                             const int32_t* ids, int32_t top_k,
+                             const mr_mxfp4_desc* w, uint16_t* out, void* stream);
+
+/* mxfp4Dequantize (MXFP4Matmul.swift:114-136): dense fp32 [experts?, out, in]
+ * copy, exact (e2m1 * 2^(e-127) is representable; e = 255 gives NaN).
+ * Validation only. */
+mr_status mr_mxfp4_dequantize(mr_ctx* ctx, const mr_mxfp4_desc* w, float* out,
+                              void* stream);
 
 /* ---------------------------------------------------------------- router
  * K3Router.select (Sources/ModelAdapters/Operators/MoE.swift:77-150),

@@ -258,7 +258,8 @@ static EncodeTiledFn encode_fn() {
 // kind 0: packed codes (uint32 words, 32-word x box_rows boxes, 128-byte
 // swizzle); kind 1/2/3: bf16/f16/f32 scales or biases (8 x box_rows boxes);
 // kind 4: bf16 activation rows (64 x box_rows boxes, 128-byte swizzle);
-// kind 5/6: f32 group sums (8 / 16 x box_rows boxes).
+// kind 5/6: f32 group sums (8 / 16 x box_rows boxes); kind 7: e8m0 MXFP4
+// exponents (16 bytes x box_rows boxes).
 static bool tensor_map(mr_ctx* ctx, CUtensorMap* out, const void* base, int64_t rows,
                        int64_t width, int box_rows, int kind) {
   const mr_ctx::MapKey key{base, rows, width, box_rows, kind};
@@ -269,14 +270,18 @@ static bool tensor_map(mr_ctx* ctx, CUtensorMap* out, const void* base, int64_t 
     }
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
-  const int esz = (kind == 0 || kind == 3 || kind >= 5) ? 4 : 2;
+  const int esz = kind == 7 ? 1 : (kind == 0 || kind == 3 || kind >= 5) ? 4 : 2;
   const CUtensorMapDataType dt = kind == 0                 ? CU_TENSOR_MAP_DATA_TYPE_UINT32
                                  : (kind == 1 || kind == 4) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : kind == 2               ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                 : kind == 7               ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   const cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)(width * esz)};
-  const int inner = kind == 0 ? 32 : kind == 4 ? kGroup : kind == 6 ? 2 * kTmaGps : kTmaGps;
+  const int inner = kind == 0                 ? 32
+                    : kind == 4               ? kGroup
+                    : (kind == 6 || kind == 7) ? 2 * kTmaGps
+                                              : kTmaGps;
   const cuuint32_t box[2] = {(cuuint32_t)inner, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(out, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
@@ -789,6 +794,207 @@ mr_status mr_affine_dequantize(mr_ctx* ctx, const mr_affine_desc* w, float* out,
     default: dequant_kernel<MR_DTYPE_F32><<<grid, 256, 0, s>>>(*w, n, out); break;
   }
   return cuda_check(ctx, cudaGetLastError(), "dequant_kernel");
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ MXFP4
+
+// MXFP4Weights.init (Sources/MLXBridge/MXFP4Weights.swift:86-140): the shape
+// checks a C descriptor can fail (dtypes are fixed by the pointer types, and
+// one descriptor cannot disagree with itself on rank, experts or rows).
+static mr_status validate_mxfp4(const mr_mxfp4_desc* w, std::string& why) {
+  if (!w) {
+    why = "MXFP4 descriptor is NULL";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (w->experts < 0 || w->out_features <= 0 || w->in_features <= 0) {
+    why = "packed shape must be positive (experts " + std::to_string(w->experts) + ", out " +
+          std::to_string(w->out_features) + ", in " + std::to_string(w->in_features) + ")";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (w->in_features % 8 != 0) {
+    why = "inFeatures " + std::to_string(w->in_features) +
+          " is not a multiple of 8 (eight 4-bit elements per uint32 word)";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (w->in_features % 32 != 0) {
+    why = "inFeatures " + std::to_string(w->in_features) +
+          " is not a multiple of groupSize 32; partial final groups are not supported";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (!w->packed || !w->scales) {
+    why = "packed and scales pointers must be non-NULL";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  return MR_OK;
+}
+
+// The matmul kernel's own limits: whole 512-element TMA stages, 16-byte
+// aligned tensor bases.
+static mr_status mxfp4_mm_limits(const mr_mxfp4_desc* w, std::string& why) {
+  if (w->in_features % (kTmaGps * kGroup) != 0) {
+    why = "inFeatures " + std::to_string(w->in_features) +
+          " is valid MXFP4 but the matmul of this build needs a multiple of 512";
+    return MR_ERR_UNSUPPORTED;
+  }
+  if (!aligned16(w->packed) || !aligned16(w->scales)) {
+    why = "packed and scales must be 16-byte aligned";
+    return MR_ERR_UNSUPPORTED;
+  }
+  return MR_OK;
+}
+
+static mr_status mxfp4_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const int32_t* ids,
+                              int32_t k, const mr_mxfp4_desc* w, uint16_t* out, void* stream,
+                              bool dense) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  std::string why;
+  mr_status st = validate_mxfp4(w, why);
+  if (!st) st = mxfp4_mm_limits(w, why);
+  if (st) return fail(ctx, st, why);
+  if (dense && w->experts != 0)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "mxfp4MM needs a single matrix; use mxfp4GatherMM for an expert stack");
+  if (!dense && w->experts == 0)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "mxfp4GatherMM needs a stacked MXFP4Weights; use mxfp4MM for a single matrix");
+  if (T <= 0 || !x || !out || (!dense && (!ids || k <= 0)))
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "x must be [tokens, inFeatures] with tokens > 0 and ids [tokens, k] with k > 0");
+  if (!aligned16(x)) return fail(ctx, MR_ERR_UNSUPPORTED, "x must be 16-byte aligned");
+  const int kk = dense ? 1 : k;
+  const int64_t Tk = T * kk;
+  if (Tk > (int64_t)1 << 30) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
+  const int E = dense ? 1 : w->experts;
+  if (!dense && E > kMaxExperts)
+    return fail(ctx, MR_ERR_UNSUPPORTED, "expert stacks larger than 1024 are not built here");
+  const int64_t in = w->in_features;
+  const int seg_cols = pick_seg_cols(Tk);
+  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / seg_cols + 1;
+
+  Bump b{nullptr};
+  for (int pass = 0; pass < 2; ++pass) {
+    b.off = 0;
+    b.take<uint16_t>(T * in);
+    b.take<float>(T * (in / kGroup) * 2);
+    b.take<int>(4);
+    b.take<int4>(max_seg);
+    b.take<int>(Tk);
+    if (pass == 0) {
+      st = ensure_workspace(ctx, b.off);
+      if (st) return st;
+      b.base = reinterpret_cast<char*>(ctx->ws);
+    }
+  }
+  b.off = 0;
+  uint16_t* xperm = b.take<uint16_t>(T * in);
+  float* xscale = b.take<float>(T * (in / kGroup) * 2);
+  int* nseg = b.take<int>(4);
+  int4* segs = b.take<int4>(max_seg);
+  int* cols = b.take<int>(Tk);
+  cudaStream_t s = as_stream(stream);
+
+  TmaMaps tm;
+  memset(&tm, 0, sizeof tm);
+  const int64_t rows = (int64_t)E * w->out_features;
+  if (!tensor_map(ctx, &tm.a_packed, w->packed, rows, in / 8, kTmaRows, 0) ||
+      !tensor_map(ctx, &tm.a_scales, w->scales, rows, in / 32, kTmaRows, 7))
+    return fail(ctx, MR_ERR_CUDA, "tensor map encoding of the MXFP4 operands failed");
+  tm.b_packed = tm.sa_packed = tm.sb_packed = tm.a_packed;
+  tm.b_scales = tm.sa_scales = tm.sb_scales = tm.a_scales;
+
+  PrepMxParams pp{x, T, in, xperm, xscale};
+  const int64_t chunks = T * (in / 16);
+  const int pgrid = (int)std::min<int64_t>((chunks + 255) / 256, 4 * ctx->sm_count);
+  prep_mx_kernel<<<pgrid, 256, 0, s>>>(pp);
+  if ((st = cuda_check(ctx, cudaGetLastError(), "prep_mx_kernel"))) return st;
+  if (dense) {
+    dense_plan_kernel<<<(int)std::min<int64_t>((T + 255) / 256, 1024), 256, 0, s>>>(
+        (int)T, seg_cols, nseg, segs, cols);
+  } else {
+    PlanParams plan{ids, (int)Tk, E, nseg, segs, cols, ctx->d_error, seg_cols};
+    plan_kernel<<<1, 256, 0, s>>>(plan);
+  }
+  if ((st = cuda_check(ctx, cudaGetLastError(), "plan kernel"))) return st;
+
+  GemvParams g{};
+  g.rows = w->out_features;
+  g.in = in;
+  g.n_routed_segments = nseg;
+  g.segments = segs;
+  g.cols = cols;
+  g.Tk = (int)Tk;
+  g.in_div = kk;
+  g.xperm = xperm;
+  g.xsum = xscale;
+  g.xsum_parts = 2;
+  g.error = ctx->d_error;
+  g.out_bf16 = out;
+  g.seg_cols = seg_cols;
+  g.rb_count = (int)((g.rows + kTmaRows - 1) / kTmaRows);
+  const int64_t items = max_seg * g.rb_count;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
+  return cuda_check(ctx, launch_tma_mx(g, tm, seg_cols / 8, grid, s), "gemv(mxfp4)");
+}
+
+namespace mr {
+// One thread per packed word: eight elements through the same e2m1 -> f16
+// conversion the GEMV uses, times the group's power of two.
+__global__ void dequant_mx_kernel(mr_mxfp4_desc w, int64_t n_words, float* out) {
+  const int64_t wpr = w.in_features / 8;
+  const int64_t gpr = w.in_features / 32;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_words;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / wpr;  // includes the expert index
+    const int64_t wd = i - row * wpr;
+    uint32_t r[4];
+    e2m1x8_to_f16x2(__ldg(w.packed + i), r);
+    const float sc = e8m0_to_f32(__ldg(w.scales + row * gpr + wd / 4));
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&r[j]));
+      o[2 * j] = f.x * sc;
+      o[2 * j + 1] = f.y * sc;
+    }
+    float4* dst = reinterpret_cast<float4*>(out + i * 8);
+    dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+  }
+}
+}  // namespace mr
+
+extern "C" {
+
+mr_status mr_mxfp4_validate(const mr_mxfp4_desc* w, char* msg, size_t msg_len) {
+  std::string why;
+  mr_status st = validate_mxfp4(w, why);
+  set_msg(msg, msg_len, why);
+  return st;
+}
+
+mr_status mr_mxfp4_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens, const mr_mxfp4_desc* w,
+                      uint16_t* out, void* stream) {
+  return mxfp4_common(ctx, x, tokens, nullptr, 1, w, out, stream, true);
+}
+
+mr_status mr_mxfp4_gather_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens, const int32_t* ids,
+                             int32_t top_k, const mr_mxfp4_desc* w, uint16_t* out, void* stream) {
+  return mxfp4_common(ctx, x, tokens, ids, top_k, w, out, stream, false);
+}
+
+mr_status mr_mxfp4_dequantize(mr_ctx* ctx, const mr_mxfp4_desc* w, float* out, void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  std::string why;
+  mr_status st = validate_mxfp4(w, why);
+  if (st) return fail(ctx, st, why);
+  if (!out || (reinterpret_cast<uintptr_t>(out) & 15u) != 0)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "output must be a 16-byte aligned device buffer");
+  const int64_t n_words = std::max<int32_t>(w->experts, 1) * w->out_features * w->in_features / 8;
+  const int grid = (int)std::min<int64_t>((n_words + 255) / 256, 16 * ctx->sm_count);
+  dequant_mx_kernel<<<grid, 256, 0, as_stream(stream)>>>(*w, n_words, out);
+  return cuda_check(ctx, cudaGetLastError(), "dequant_mx_kernel");
 }
 
 // ------------------------------------------------------------------ router

@@ -38,8 +38,27 @@ MR_DEVICE float bf16_round(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f
 // Scale/bias element size by dtype.
 template <int SD>
 struct ScaleT {
-  static constexpr int kBytes = (SD == MR_DTYPE_F32) ? 4 : 2;
+  static constexpr int kBytes = (SD == MR_DTYPE_F32) ? 4 : (SD == MR_DTYPE_E8M0 ? 1 : 2);
 };
+
+// An OCP MX e8m0 scale: 2^(e-127); e = 0 is 2^-127 (an fp32 subnormal),
+// e = 255 is NaN.
+MR_DEVICE float e8m0_to_f32(uint32_t e) {
+  return __uint_as_float(e == 0 ? 0x00400000u : (e == 255 ? 0x7FC00000u : e << 23));
+}
+
+// Eight e2m1 codes of a word (element j at bits 4j) as four f16x2 pairs:
+// r[b] = (element 2b, element 2b+1) — exact, e2m1 values are f16 values.
+MR_DEVICE void e2m1x8_to_f16x2(uint32_t w, uint32_t (&r)[4]) {
+  asm("{ .reg .b8 b0, b1, b2, b3;\n"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n"
+      "cvt.rn.f16x2.e2m1x2 %3, b3; }"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(w));
+}
 
 template <int SD>
 MR_DEVICE uint32_t load_scale_raw(const void* p, int64_t i) {
@@ -94,6 +113,15 @@ MR_DEVICE void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t 
                               uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+MR_DEVICE void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                             uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));

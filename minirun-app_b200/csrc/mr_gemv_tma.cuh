@@ -19,6 +19,15 @@
 // then sums the slots in order.
 // Requires in % 512 == 0 (whole stages) and expert stacks addressable by one
 // 2-D tensor map per projection (stack base + expert * rows).
+//
+// SD == MR_DTYPE_E8M0 is the MXFP4 form (OCP MX: e2m1 codes, one e8m0
+// exponent per 32 elements, no bias). The stage then carries 16 exponent
+// bytes per row and no bias region; a lane takes words c and c + 4 of each
+// 64-element span (one per 32-element half), widens the codes to f16 with
+// cvt.f16x2.e2m1x2 (exact), and runs f16 mma.m16n8k16 per half against
+// activations that the MX prep stored as f16 scaled by 2^-k per half (k
+// puts the half's largest magnitude in [2^14, 2^15)). The fold is
+// y += (2^(e-127) * 2^k) * acc per half; only the store epilogue is built.
 #pragma once
 
 #include <cuda.h>
@@ -50,16 +59,20 @@ struct TmaMaps {
 
 template <int BITS, int SD, int EPI>
 struct TmaStage {
+  static constexpr bool kMx = SD == MR_DTYPE_E8M0;
+  static_assert(!kMx || (BITS == 4 && EPI == EPI_STORE), "MXFP4: 4-bit codes, store epilogue");
   static constexpr int kMats = (EPI == EPI_SWIGLU) ? 2 : 1;
   static constexpr int kBoxRows = kTmaRows / kMats;  // rows per box
   static constexpr int kBoxBytes = kBoxRows * 128;   // one 128-byte-wide box
   static constexpr int kBoxes = BITS / 2;            // boxes per matrix per stage (64*bits B)
   static constexpr int kGroupBytes = 8 * BITS;       // packed bytes per row per group
   static constexpr int kEsz = ScaleT<SD>::kBytes;
+  static constexpr int kSpg = kMx ? 2 : 1;            // scales per 64-element group
   static constexpr int kABytes = kMats * kBoxes * kBoxBytes;
-  static constexpr int kSBytes = kTmaRows * kTmaGps * kEsz;  // scales (or biases)
-  static constexpr int kBytes = (kABytes + 2 * kSBytes + 1023) / 1024 * 1024;
-  static constexpr uint32_t kTx = kABytes + 2 * kSBytes;
+  static constexpr int kSBytes = kTmaRows * kTmaGps * kSpg * kEsz;  // scales (or biases)
+  static constexpr int kZBytes = kMx ? 0 : kSBytes;                 // biases
+  static constexpr int kBytes = (kABytes + kSBytes + kZBytes + 1023) / 1024 * 1024;
+  static constexpr uint32_t kTx = kABytes + kSBytes + kZBytes;
 };
 
 template <int NT>
@@ -230,6 +243,60 @@ MR_DEVICE void lds_scales(float (&v)[N], uint32_t a) {
   }
 }
 
+// MX: N groups' e8m0 exponents of one row from shared memory (2 bytes per
+// group: first half, second half), as fp32 powers of two.
+template <int N>
+MR_DEVICE void lds_e8m0(float (&lo)[N], float (&hi)[N], uint32_t a) {
+  static_assert(N == 2 || N == 4, "2 or 4 groups");
+  uint32_t w[N / 2];
+  if constexpr (N == 2) {
+    w[0] = lds_b32(a);
+  } else {
+    const uint2 u = lds_b64(a);
+    w[0] = u.x;
+    w[1] = u.y;
+  }
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    const uint32_t v = w[j >> 1] >> ((j & 1) * 16);
+    lo[j] = e8m0_to_f32(v & 0xffu);
+    hi[j] = e8m0_to_f32((v >> 8) & 0xffu);
+  }
+}
+
+// MX: N groups' activation factors of one column (2 floats per group).
+template <int N>
+MR_DEVICE void ldg_xscale(float (&lo)[N], float (&hi)[N], const float* p) {
+  static_assert(N == 2 || N == 4, "2 or 4 groups");
+#pragma unroll
+  for (int h = 0; h < N / 2; ++h) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p) + h);
+    lo[2 * h] = a.x;
+    hi[2 * h] = a.y;
+    lo[2 * h + 1] = a.z;
+    hi[2 * h + 1] = a.w;
+  }
+}
+
+// MX: one 64-element group of two rows (wa: this lane's words c and c + 4 of
+// row a, wb of row b) against 8 columns: four f16 mma.m16n8k16, the first
+// pair into `lo` (elements 0-31), the second into `hi` (32-63). xb holds the
+// column's matching activations as f16 pairs: xb[0..3] = word c's eight
+// elements, xb[4..7] = word c + 4's. Fragment k positions (2c, 2c+1, 2c+8,
+// 2c+9) map to elements (4h, 4h+1, 4h+2, 4h+3) of the word, for A and B alike.
+MR_DEVICE void group_mma_mx(float (&lo)[4], float (&hi)[4], const uint32_t (&wa)[2],
+                            const uint32_t (&wb)[2], const uint32_t (&xb)[8]) {
+  uint32_t ra[4], rb[4];
+  e2m1x8_to_f16x2(wa[0], ra);
+  e2m1x8_to_f16x2(wb[0], rb);
+  mma_f16_16816(lo, ra[0], rb[0], ra[1], rb[1], xb[0], xb[1]);
+  mma_f16_16816(lo, ra[2], rb[2], ra[3], rb[3], xb[2], xb[3]);
+  e2m1x8_to_f16x2(wa[1], ra);
+  e2m1x8_to_f16x2(wb[1], rb);
+  mma_f16_16816(hi, ra[0], rb[0], ra[1], rb[1], xb[4], xb[5]);
+  mma_f16_16816(hi, ra[2], rb[2], ra[3], rb[3], xb[6], xb[7]);
+}
+
 // Bounded wait. On expiry (or once another thread has flagged an abort) it
 // sets the device error word and the CTA's abort flag and returns, so the
 // caller carries on to every barrier it owes: results are then garbage but
@@ -318,9 +385,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             for (int j = 0; j < ST::kBoxes; ++j)
               tma_load_2d(A + (m * ST::kBoxes + j) * ST::kBoxBytes, mp[m],
                           (st * ST::kBoxes + j) * 32, y0, full + slot);
-            const int sbytes = ST::kBoxRows * kTmaGps * ST::kEsz;
-            tma_load_2d(S + m * sbytes, ms[m], st * kTmaGps, y0, full + slot);
-            tma_load_2d(Z + m * sbytes, mz[m], st * kTmaGps, y0, full + slot);
+            const int sbytes = ST::kBoxRows * kTmaGps * ST::kSpg * ST::kEsz;
+            tma_load_2d(S + m * sbytes, ms[m], st * kTmaGps * ST::kSpg, y0, full + slot);
+            if constexpr (!ST::kMx) tma_load_2d(Z + m * sbytes, mz[m], st * kTmaGps, y0, full + slot);
           }
           if (++slot == (uint32_t)nst) {
             slot = 0;
@@ -359,23 +426,31 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     mb = 0;
     rbr = ra + 8;
   }
-  // xsum granularity: K2 reads h's two 32-row partial sums per group
-  constexpr int XP = (EPI == EPI_PARTIAL) ? 2 : 1;
+  // xsum granularity: K2 reads h's two 32-row partial sums per group; the
+  // MX form reads two activation scale factors per group (one per half)
+  constexpr int XP = (EPI == EPI_PARTIAL || ST::kMx) ? 2 : 1;
   // Per-lane shared-memory offsets inside a stage, fixed for the whole
   // kernel: the swizzled positions of this lane's codes for its groups, and
   // of its rows' consecutive scales (biases are kSBytes further).
-  uint32_t offA[kGpw], offB[kGpw];
+  // (MX: word c and word c + 4 of the group's 8, at offA / offA2.)
+  uint32_t offA[kGpw], offB[kGpw], offA2[kGpw], offB2[kGpw];
 #pragma unroll
   for (int j = 0; j < kGpw; ++j) {
-    const int b = (kq * kGpw + j) * ST::kGroupBytes + c * LW * 4;  // byte in the stage row
-    const int box = b >> 7, bb = b & 127;
+    const int b = (kq * kGpw + j) * ST::kGroupBytes + c * (ST::kMx ? 1 : LW) * 4;  // stage-row byte
+    const int box = b >> 7, bb = b & 127, bb2 = bb + 16;
     offA[j] = (ma * ST::kBoxes + box) * ST::kBoxBytes + ra * 128 +
               ((((bb >> 4) ^ ra) & 7) << 4) + (bb & 15);
     offB[j] = (mb * ST::kBoxes + box) * ST::kBoxBytes + rbr * 128 +
               ((((bb >> 4) ^ rbr) & 7) << 4) + (bb & 15);
+    offA2[j] = (ma * ST::kBoxes + box) * ST::kBoxBytes + ra * 128 +
+               ((((bb2 >> 4) ^ ra) & 7) << 4) + (bb2 & 15);
+    offB2[j] = (mb * ST::kBoxes + box) * ST::kBoxBytes + rbr * 128 +
+               ((((bb2 >> 4) ^ rbr) & 7) << 4) + (bb2 & 15);
   }
-  const uint32_t offSa = ST::kABytes + ((ma * ST::kBoxRows + ra) * kTmaGps + kq * kGpw) * ST::kEsz;
-  const uint32_t offSb = ST::kABytes + ((mb * ST::kBoxRows + rbr) * kTmaGps + kq * kGpw) * ST::kEsz;
+  const uint32_t offSa =
+      ST::kABytes + ((ma * ST::kBoxRows + ra) * kTmaGps + kq * kGpw) * ST::kSpg * ST::kEsz;
+  const uint32_t offSb =
+      ST::kABytes + ((mb * ST::kBoxRows + rbr) * kTmaGps + kq * kGpw) * ST::kSpg * ST::kEsz;
   const uint32_t sbase = smem_u32(smem);
   uint32_t slot = 0, phase = 0, stg = sbase;
 
@@ -393,7 +468,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
 #pragma unroll
     for (int j = 0; j < kGpw; ++j) {
-      if constexpr (LW == 1) {
+      if constexpr (ST::kMx) {
+        wa[j][0] = lds_b32(stg + offA[j]);
+        wa[j][1] = lds_b32(stg + offA2[j]);
+        wb[j][0] = lds_b32(stg + offB[j]);
+        wb[j][1] = lds_b32(stg + offB2[j]);
+      } else if constexpr (LW == 1) {
         wa[j][0] = lds_b32(stg + offA[j]);
         wb[j][0] = lds_b32(stg + offB[j]);
       } else if constexpr (LW == 2) {
@@ -408,10 +488,15 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         wb[j][0] = v.x; wb[j][1] = v.y; wb[j][2] = v.z; wb[j][3] = v.w;
       }
     }
-    lds_scales<SD, kGpw>(sa, stg + offSa);
-    lds_scales<SD, kGpw>(za, stg + offSa + ST::kSBytes);
-    lds_scales<SD, kGpw>(sb, stg + offSb);
-    lds_scales<SD, kGpw>(zb, stg + offSb + ST::kSBytes);
+    if constexpr (ST::kMx) {  // sa / sb: first-half exponents, za / zb: second-half
+      lds_e8m0<kGpw>(sa, za, stg + offSa);
+      lds_e8m0<kGpw>(sb, zb, stg + offSb);
+    } else {
+      lds_scales<SD, kGpw>(sa, stg + offSa);
+      lds_scales<SD, kGpw>(za, stg + offSa + ST::kSBytes);
+      lds_scales<SD, kGpw>(sb, stg + offSb);
+      lds_scales<SD, kGpw>(zb, stg + offSb + ST::kSBytes);
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + slot);  // this warp's stage data is in registers
     if (++slot == (uint32_t)nst) {
@@ -421,10 +506,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     } else {
       stg += ST::kBytes;
     }
+    if constexpr (!ST::kMx) {
 #pragma unroll
-    for (int j = 0; j < kGpw; ++j) {
-      za[j] = fmaf(-kC, sa[j], za[j]);
-      zb[j] = fmaf(-kC, sb[j], zb[j]);
+      for (int j = 0; j < kGpw; ++j) {
+        za[j] = fmaf(-kC, sa[j], za[j]);
+        zb[j] = fmaf(-kC, sb[j], zb[j]);
+      }
     }
   };
 
@@ -476,7 +563,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const bool shared = info.shared;
     const int ncols = info.ncols;
     const int ntiles = (ncols + 7) >> 3;
-    const bool single = ncols == 1;  // FMA path instead of an 8-column mma tile
+    const bool single = !ST::kMx && ncols == 1;  // FMA path instead of an 8-column mma tile
     // activation pointers at this warp's first group, walked one stage at a time
     const uint16_t* xr[NT];
     const float* xp0[NT];
@@ -492,48 +579,50 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     for (int t = 0; t < NT; ++t) y[t][0] = y[t][1] = y[t][2] = y[t][3] = 0.0f;
 
     if (single) {
-      // One column: fp32 FMAs of this lane's 16 codes per row and group
-      // against the matching 16 activations; the group's bias term is added
-      // once per quad (lane c == 0); the quad is summed after the K loop.
-      const bool add_bias = c == 0;
-      const uint16_t* xq = xr[0];
-      const float* xs = xp0[0];
-      for (int st = 0; st < nstages; ++st) {
-        if (st == 1 && has_next) fetch_cols(nxt);
-        uint32_t wa[kGpw][LW], wb[kGpw][LW];
-        float sa[kGpw], za[kGpw], sb[kGpw], zb[kGpw];
-        take_stage(wa, wb, sa, za, sb, zb);
-        uint32_t xb[kGpw][8];
+      if constexpr (!ST::kMx) {  // (MX items always take the mma path)
+        // One column: fp32 FMAs of this lane's 16 codes per row and group
+        // against the matching 16 activations; the group's bias term is added
+        // once per quad (lane c == 0); the quad is summed after the K loop.
+        const bool add_bias = c == 0;
+        const uint16_t* xq = xr[0];
+        const float* xs = xp0[0];
+        for (int st = 0; st < nstages; ++st) {
+          if (st == 1 && has_next) fetch_cols(nxt);
+          uint32_t wa[kGpw][LW], wb[kGpw][LW];
+          float sa[kGpw], za[kGpw], sb[kGpw], zb[kGpw];
+          take_stage(wa, wb, sa, za, sb, zb);
+          uint32_t xb[kGpw][8];
 #pragma unroll
-        for (int j = 0; j < kGpw; ++j) {
-          const uint4 v0 = ldg_u128(xq + j * kGroup);
-          const uint4 v1 = ldg_u128(xq + j * kGroup + 8);
-          xb[j][0] = v0.x; xb[j][1] = v0.y; xb[j][2] = v0.z; xb[j][3] = v0.w;
-          xb[j][4] = v1.x; xb[j][5] = v1.y; xb[j][6] = v1.z; xb[j][7] = v1.w;
-        }
-        float X[kGpw];
-        ldg_xsum<XP, kGpw>(X, xs);
-        xq += kTmaGps * kGroup;
-        xs += kTmaGps * XP;
-        float acc[kGpw][4];
+          for (int j = 0; j < kGpw; ++j) {
+            const uint4 v0 = ldg_u128(xq + j * kGroup);
+            const uint4 v1 = ldg_u128(xq + j * kGroup + 8);
+            xb[j][0] = v0.x; xb[j][1] = v0.y; xb[j][2] = v0.z; xb[j][3] = v0.w;
+            xb[j][4] = v1.x; xb[j][5] = v1.y; xb[j][6] = v1.z; xb[j][7] = v1.w;
+          }
+          float X[kGpw];
+          ldg_xsum<XP, kGpw>(X, xs);
+          xq += kTmaGps * kGroup;
+          xs += kTmaGps * XP;
+          float acc[kGpw][4];
 #pragma unroll
-        for (int j = 0; j < kGpw; ++j) {
-          acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-          group_fma<BITS>(acc[j], wa[j], wb[j], xb[j]);
-        }
+          for (int j = 0; j < kGpw; ++j) {
+            acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+            group_fma<BITS>(acc[j], wa[j], wb[j], xb[j]);
+          }
 #pragma unroll
-        for (int j = 0; j < kGpw; ++j) {
-          y[0][0] = fmaf(sa[j], acc[j][0] + acc[j][1], y[0][0]);
-          y[0][2] = fmaf(sb[j], acc[j][2] + acc[j][3], y[0][2]);
-          y[0][0] = fmaf(add_bias ? za[j] : 0.0f, X[j], y[0][0]);
-          y[0][2] = fmaf(add_bias ? zb[j] : 0.0f, X[j], y[0][2]);
+          for (int j = 0; j < kGpw; ++j) {
+            y[0][0] = fmaf(sa[j], acc[j][0] + acc[j][1], y[0][0]);
+            y[0][2] = fmaf(sb[j], acc[j][2] + acc[j][3], y[0][2]);
+            y[0][0] = fmaf(add_bias ? za[j] : 0.0f, X[j], y[0][0]);
+            y[0][2] = fmaf(add_bias ? zb[j] : 0.0f, X[j], y[0][2]);
+          }
         }
+        // sum the quad's partial dot products (same order on every lane)
+        y[0][0] += __shfl_xor_sync(0xffffffffu, y[0][0], 1);
+        y[0][2] += __shfl_xor_sync(0xffffffffu, y[0][2], 1);
+        y[0][0] += __shfl_xor_sync(0xffffffffu, y[0][0], 2);
+        y[0][2] += __shfl_xor_sync(0xffffffffu, y[0][2], 2);
       }
-      // sum the quad's partial dot products (same order on every lane)
-      y[0][0] += __shfl_xor_sync(0xffffffffu, y[0][0], 1);
-      y[0][2] += __shfl_xor_sync(0xffffffffu, y[0][2], 1);
-      y[0][0] += __shfl_xor_sync(0xffffffffu, y[0][0], 2);
-      y[0][2] += __shfl_xor_sync(0xffffffffu, y[0][2], 2);
     } else {
       for (int st = 0; st < nstages; ++st) {
         if (st == 1 && has_next) fetch_cols(nxt);
@@ -551,21 +640,41 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
               xb[j][0] = v0.x; xb[j][1] = v0.y; xb[j][2] = v0.z; xb[j][3] = v0.w;
               xb[j][4] = v1.x; xb[j][5] = v1.y; xb[j][6] = v1.z; xb[j][7] = v1.w;
             }
-            float X0[kGpw], X1[kGpw];
-            ldg_xsum<XP, kGpw>(X0, xp0[t]);
-            ldg_xsum<XP, kGpw>(X1, xp1[t]);
-            float acc[kGpw][4];
+            if constexpr (ST::kMx) {
+              float L0[kGpw], H0[kGpw], L1[kGpw], H1[kGpw];  // activation factors per half
+              ldg_xscale<kGpw>(L0, H0, xp0[t]);
+              ldg_xscale<kGpw>(L1, H1, xp1[t]);
+              float lo[kGpw][4], hi[kGpw][4];
 #pragma unroll
-            for (int j = 0; j < kGpw; ++j) {
-              acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-              group_mma<BITS>(acc[j], wa[j], wb[j], xb[j]);
-            }
+              for (int j = 0; j < kGpw; ++j) {
 #pragma unroll
-            for (int j = 0; j < kGpw; ++j) {
-              y[t][0] = fmaf(sa[j], acc[j][0], fmaf(za[j], X0[j], y[t][0]));
-              y[t][1] = fmaf(sa[j], acc[j][1], fmaf(za[j], X1[j], y[t][1]));
-              y[t][2] = fmaf(sb[j], acc[j][2], fmaf(zb[j], X0[j], y[t][2]));
-              y[t][3] = fmaf(sb[j], acc[j][3], fmaf(zb[j], X1[j], y[t][3]));
+                for (int i = 0; i < 4; ++i) lo[j][i] = hi[j][i] = 0.0f;
+                group_mma_mx(lo[j], hi[j], wa[j], wb[j], xb[j]);
+              }
+#pragma unroll
+              for (int j = 0; j < kGpw; ++j) {
+                y[t][0] = fmaf(sa[j] * L0[j], lo[j][0], fmaf(za[j] * H0[j], hi[j][0], y[t][0]));
+                y[t][1] = fmaf(sa[j] * L1[j], lo[j][1], fmaf(za[j] * H1[j], hi[j][1], y[t][1]));
+                y[t][2] = fmaf(sb[j] * L0[j], lo[j][2], fmaf(zb[j] * H0[j], hi[j][2], y[t][2]));
+                y[t][3] = fmaf(sb[j] * L1[j], lo[j][3], fmaf(zb[j] * H1[j], hi[j][3], y[t][3]));
+              }
+            } else {
+              float X0[kGpw], X1[kGpw];
+              ldg_xsum<XP, kGpw>(X0, xp0[t]);
+              ldg_xsum<XP, kGpw>(X1, xp1[t]);
+              float acc[kGpw][4];
+#pragma unroll
+              for (int j = 0; j < kGpw; ++j) {
+                acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+                group_mma<BITS>(acc[j], wa[j], wb[j], xb[j]);
+              }
+#pragma unroll
+              for (int j = 0; j < kGpw; ++j) {
+                y[t][0] = fmaf(sa[j], acc[j][0], fmaf(za[j], X0[j], y[t][0]));
+                y[t][1] = fmaf(sa[j], acc[j][1], fmaf(za[j], X1[j], y[t][1]));
+                y[t][2] = fmaf(sb[j], acc[j][2], fmaf(zb[j], X0[j], y[t][2]));
+                y[t][3] = fmaf(sb[j], acc[j][3], fmaf(zb[j], X1[j], y[t][3]));
+              }
             }
           }
           xr[t] += kTmaGps * kGroup;

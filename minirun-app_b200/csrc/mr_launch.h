@@ -23,6 +23,10 @@ cudaError_t launch_tma_b4(const GemvParams& p, const TmaMaps& m, int sd, int epi
 cudaError_t launch_tma_b8(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, int grid,
                           cudaStream_t s);
 
+// MXFP4 form of the TMA kernel (in % 512 == 0, store epilogue, nt == 1).
+cudaError_t launch_tma_mx(const GemvParams& p, const TmaMaps& m, int nt, int grid,
+                          cudaStream_t s);
+
 // tcgen05 kernel (in % 512 == 0, activations through tensor maps).
 cudaError_t launch_umma_b2(const GemvParams& p, const UmMaps& m, int sd, int epi, int grid,
                            cudaStream_t s);

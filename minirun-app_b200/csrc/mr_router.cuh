@@ -72,6 +72,75 @@ __global__ void prep_kernel(const PrepParams p) {
   prep_range(p, (int64_t)blockIdx.x * blockDim.x + threadIdx.x, (int64_t)gridDim.x * blockDim.x);
 }
 
+// ------------------------------------------------------------- MX prep
+// Activations of the MXFP4 GEMV. Per 32-element half of each 64-element
+// group: k = floor(log2(largest finite |x|)) - 14 (k = 0 when the half has no
+// nonzero finite value), xperm holds f16(x * 2^-k) — exact for every element
+// of at least 2^-29 times the half's largest magnitude (bf16 carries 8
+// significant bits, f16 normals 11) — and xscale[t][2g + half] = 2^k. Each group's 64 f16 are stored as four
+// 16-element lane segments: segment c = elements [8c, 8c+8) then
+// [32+8c, 32+8c+8) (words c and c + 4 of the packed row).
+struct PrepMxParams {
+  const uint16_t* x;
+  int64_t rows;
+  int64_t in;
+  uint16_t* xperm;
+  float* xscale;
+};
+
+// Called by whole warps: the two chunks of a half exchange their maxima by
+// shuffle; lanes past the end pass valid == false.
+MR_DEVICE void prep_mx_chunk(const PrepMxParams& p, int64_t chunk, bool valid) {
+  const int64_t per_row = p.in / 16;
+  if (!valid) chunk = 0;
+  const int64_t r = chunk / per_row;
+  const int64_t c16 = chunk - r * per_row;
+  const int q = (int)(c16 & 3);  // chunk of the group: elements [16q, 16q+16), half q >> 1
+  const uint16_t* src = p.x + r * p.in + c16 * 16;
+  const uint4 v0 = ldg_u128(src);
+  const uint4 v1 = ldg_u128(src + 8);
+  uint16_t e[16];
+  memcpy(e, &v0, 16);
+  memcpy(e + 8, &v1, 16);
+  float f[16];
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    f[i] = bf16_bits_to_f32(e[i]);
+    const float a = fabsf(f[i]);
+    if (a <= 3.402823466e38f) m = fmaxf(m, a);  // finite values only
+  }
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  int k = 0;
+  if (m > 0.0f) {
+    int ex;
+    (void)frexpf(m, &ex);  // m = f * 2^ex, f in [0.5, 1)
+    k = ex - 1 - 14;
+  }
+  uint16_t o[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i] = __half_as_ushort(__float2half_rn(ldexpf(f[i], -k)));
+  if (valid) {
+    uint16_t* g = p.xperm + r * p.in + (c16 >> 2) * 64;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int w = 2 * q + h;  // word of the group's packed row
+      uint4 u;
+      memcpy(&u, o + 8 * h, 16);
+      *reinterpret_cast<uint4*>(g + (w & 3) * 16 + (w >> 2) * 8) = u;
+    }
+    if ((q & 1) == 0) p.xscale[r * (p.in / kGroup) * 2 + (c16 >> 2) * 2 + (q >> 1)] = ldexpf(1.0f, k);
+  }
+}
+
+__global__ void prep_mx_kernel(const PrepMxParams p) {
+  const int64_t n = p.rows * (p.in / 16);
+  const int64_t n_round = (n + 31) / 32 * 32;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_round; i += stride)
+    prep_mx_chunk(p, i, i < n);
+}
+
 // ---------------------------------------------------------------- logits
 // part[kc][t][e] = sum over the kc-th K chunk of x[t,:] . W_r[e,:] (fp32),
 // on the tensor core (bf16 products are exact in fp32). Chunks are summed in

@@ -13,6 +13,8 @@ from .ep import ExpertGroup, MoELayerShard
 from .moe import (MoELayer, ResidentExpertBackend, RouterConfig, TokenExpertMap, router_select,
                   router_select_hashed, router_select_logits)
 from .checkpoint import Checkpoint, SafetensorsError, SafetensorsFile, write_safetensors
+from .mxfp4 import (MXFP4BridgeError, MXFP4Weights, mxfp4_dequantize, mxfp4_gather_mm,
+                    mxfp4_mm, mxfp4_validate)
 from .tiles import (ExpertContainers, TileContainer, TileContainerError, write_container,
                     write_expert_containers)
 
@@ -23,5 +25,6 @@ __all__ = [
     "router_select_logits", "ExpertGroup", "MoELayerShard", "CachedLayer", "ExpertCache",
     "ExpertContainers", "TileContainer", "TileContainerError", "write_container",
     "write_expert_containers", "Checkpoint", "SafetensorsError", "SafetensorsFile",
-    "write_safetensors", "TokenExpertMap", "router_select_hashed",
+    "write_safetensors", "TokenExpertMap", "router_select_hashed", "MXFP4BridgeError",
+    "MXFP4Weights", "mxfp4_dequantize", "mxfp4_gather_mm", "mxfp4_mm", "mxfp4_validate",
 ]

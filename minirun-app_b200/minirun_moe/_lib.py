@@ -28,7 +28,7 @@ MR_ERR_IO = 10
 MR_ERR_INTEGRITY = 11
 MR_DEVERR_BAD_TOKEN_ID = 0x10
 
-MR_DTYPE_BF16, MR_DTYPE_F16, MR_DTYPE_F32 = 0, 1, 2
+MR_DTYPE_BF16, MR_DTYPE_F16, MR_DTYPE_F32, MR_DTYPE_E8M0 = 0, 1, 2, 3
 MR_SCORING_SIGMOID, MR_SCORING_SOFTMAX, MR_SCORING_SQRT_SOFTPLUS = 0, 1, 2
 MR_RENORM_NONE, MR_RENORM_PLAIN, MR_RENORM_EPS = 0, 1, 2
 MR_WEIGHT_BEFORE_DOWN, MR_WEIGHT_AFTER_DOWN = 0, 1
@@ -41,6 +41,11 @@ class mr_affine_desc(C.Structure):
     _fields_ = [("packed", vp), ("scales", vp), ("biases", vp), ("experts", C.c_int32),
                 ("out_features", C.c_int64), ("in_features", C.c_int64),
                 ("group_size", C.c_int32), ("bits", C.c_int32), ("scale_dtype", C.c_int)]
+
+
+class mr_mxfp4_desc(C.Structure):
+    _fields_ = [("packed", vp), ("scales", vp), ("experts", C.c_int32),
+                ("out_features", C.c_int64), ("in_features", C.c_int64)]
 
 
 class mr_router_config(C.Structure):
@@ -104,6 +109,11 @@ SIGNATURES = {
     "mr_affine_gather_mm_noalloc": (C.c_int, [vp, C.c_int64, vp, C.c_int32,
                                               C.POINTER(mr_affine_desc), vp, vp, C.c_char_p,
                                               C.c_size_t]),
+    "mr_mxfp4_validate": (C.c_int, [C.POINTER(mr_mxfp4_desc), C.c_char_p, C.c_size_t]),
+    "mr_mxfp4_mm": (C.c_int, [vp, vp, C.c_int64, C.POINTER(mr_mxfp4_desc), vp, vp]),
+    "mr_mxfp4_gather_mm": (C.c_int, [vp, vp, C.c_int64, vp, C.c_int32,
+                                     C.POINTER(mr_mxfp4_desc), vp, vp]),
+    "mr_mxfp4_dequantize": (C.c_int, [vp, C.POINTER(mr_mxfp4_desc), vp, vp]),
     "mr_router_config_validate": (C.c_int, [C.POINTER(mr_router_config), C.c_char_p,
                                             C.c_size_t]),
     "mr_router_select": (C.c_int, [vp, vp, C.c_int64, C.c_int64, vp,

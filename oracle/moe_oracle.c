@@ -320,6 +320,131 @@ int mro_affine_gather_mm(const mro_affine* w, const uint16_t* x, int64_t T,
   return 0;
 }
 
+/* ------------------------------------------------------------------ MXFP4 */
+
+/* e2m1 value of a 4-bit code, from the OCP MX v1.0 element encoding. */
+double mro_e2m1_value(int code) {
+  const int ef = (code >> 1) & 3, m = code & 1;
+  const double mag = ef == 0 ? 0.5 * m : ldexp(1.0 + 0.5 * m, ef - 1);
+  return (code & 8) ? -mag : mag;
+}
+
+/* e8m0 scale: 2^(e-127); 255 is NaN. */
+double mro_e8m0_value(int e) { return e == 255 ? NAN : ldexp(1.0, e - 127); }
+
+int mro_mxfp4_validate(const mro_mxfp4* w, char* msg, int msg_len) {
+  if (w->experts < 0 || w->out <= 0 || w->in <= 0) {
+    snprintf(msg, (size_t)msg_len, "packed shape must be positive");
+    return 1;
+  }
+  if (w->in % 8 != 0) {
+    snprintf(msg, (size_t)msg_len, "inFeatures %lld is not a multiple of 8", (long long)w->in);
+    return 1;
+  }
+  if (w->in % 32 != 0) {
+    snprintf(msg, (size_t)msg_len,
+             "inFeatures %lld is not a multiple of groupSize 32; partial final groups are not "
+             "supported",
+             (long long)w->in);
+    return 1;
+  }
+  if (msg_len > 0) msg[0] = 0;
+  return 0;
+}
+
+/* One row of expert e as doubles: e2m1 * 2^(e8m0 - 127), exact. */
+static void mx_row(const mro_mxfp4* w, int64_t e, int64_t r, double* q) {
+  const uint32_t* p = w->packed + (e * w->out + r) * (w->in / 8);
+  const uint8_t* sc = w->scales + (e * w->out + r) * (w->in / 32);
+  for (int64_t i = 0; i < w->in; ++i)
+    q[i] = mro_e2m1_value((int)((p[i / 8] >> ((i % 8) * 4)) & 15u)) *
+           mro_e8m0_value(sc[i / 32]);
+}
+
+void mro_mxfp4_dequantize(const mro_mxfp4* w, float* out) {
+  const int64_t E = w->experts > 0 ? w->experts : 1;
+#pragma omp parallel
+  {
+    double* q = (double*)malloc(sizeof(double) * (size_t)w->in);
+#pragma omp for collapse(2) schedule(static)
+    for (int64_t e = 0; e < E; ++e)
+      for (int64_t r = 0; r < w->out; ++r) {
+        mx_row(w, e, r, q);
+        float* o = out + (e * w->out + r) * w->in;
+        for (int64_t i = 0; i < w->in; ++i) o[i] = (float)q[i];
+      }
+    free(q);
+  }
+}
+
+/* y[n][out] = W[e] . xd[n][in] in double (products of a bf16 and an e2m1
+ * times a power of two are exact; the sums round at 2^-53). */
+static void mx_expert_dot(const mro_mxfp4* w, int64_t e, const double* xd, int64_t n,
+                          double* y) {
+#pragma omp parallel
+  {
+    double* q = (double*)malloc(sizeof(double) * (size_t)w->in);
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < w->out; ++r) {
+      mx_row(w, e, r, q);
+      for (int64_t t = 0; t < n; ++t) {
+        const double* xr = xd + t * w->in;
+        double acc = 0;
+        for (int64_t i = 0; i < w->in; ++i) acc += q[i] * xr[i];
+        y[t * w->out + r] = acc;
+      }
+    }
+    free(q);
+  }
+}
+
+void mro_mxfp4_mm(const mro_mxfp4* w, int64_t expert, const uint16_t* x, int64_t T,
+                  uint16_t* out, float* out_f32) {
+  double* xd = (double*)malloc(sizeof(double) * (size_t)(T * w->in));
+  double* y = (double*)malloc(sizeof(double) * (size_t)(T * w->out));
+  for (int64_t i = 0; i < T * w->in; ++i) xd[i] = (double)mro_bf16_to_f32(x[i]);
+  mx_expert_dot(w, expert, xd, T, y);
+  for (int64_t i = 0; i < T * w->out; ++i) {
+    float f = (float)y[i];
+    if (out) out[i] = mro_f32_to_bf16(f);
+    if (out_f32) out_f32[i] = f;
+  }
+  free(xd);
+  free(y);
+}
+
+/* Experts visited in ascending id order (the order does not change values). */
+int mro_mxfp4_gather_mm(const mro_mxfp4* w, const uint16_t* x, int64_t T,
+                        const int32_t* ids, int64_t k, uint16_t* out, float* out_f32) {
+  const int64_t E = w->experts, in = w->in, outf = w->out;
+  for (int64_t i = 0; i < T * k; ++i)
+    if (ids[i] < 0 || ids[i] >= E) return -1;
+  int64_t* order = (int64_t*)malloc(sizeof(int64_t) * (size_t)(T * k));
+  double* xd = (double*)malloc(sizeof(double) * (size_t)(T * k * in));
+  double* y = (double*)malloc(sizeof(double) * (size_t)(T * k * outf));
+  for (int64_t e = 0; e < E; ++e) {
+    int64_t n = 0;
+    for (int64_t p = 0; p < T * k; ++p)
+      if (ids[p] == e) order[n++] = p;
+    if (n == 0) continue;
+    for (int64_t i = 0; i < n; ++i) {
+      const uint16_t* xr = x + (order[i] / k) * in;
+      for (int64_t c = 0; c < in; ++c) xd[i * in + c] = (double)mro_bf16_to_f32(xr[c]);
+    }
+    mx_expert_dot(w, e, xd, n, y);
+    for (int64_t i = 0; i < n; ++i)
+      for (int64_t r = 0; r < outf; ++r) {
+        float f = (float)y[i * outf + r];
+        if (out) out[order[i] * outf + r] = mro_f32_to_bf16(f);
+        if (out_f32) out_f32[order[i] * outf + r] = f;
+      }
+  }
+  free(order);
+  free(xd);
+  free(y);
+  return 0;
+}
+
 /* ------------------------------------------------------------------ router */
 
 /* k3Linear(x.f32, W.f32) (Sources/ModelAdapters/Operators/Linear.swift:55-57),

@@ -74,6 +74,34 @@ int mro_affine_gather_mm(const mro_affine* w, const uint16_t* x, int64_t T,
                          const int32_t* ids, int64_t k, uint16_t* out,
                          float* out_f32);
 
+/* MXFP4 (MLX `mode: .mxfp4`, the un-vendored dependency; layout contract in
+ * Sources/MLXBridge/MXFP4Weights.swift:33-63, operators in MXFP4Matmul.swift).
+ * OCP Microscaling Formats (MX) v1.0: an e2m1 code c has sign bit 3,
+ * exponent field (c >> 1) & 3 with bias 1 and mantissa bit c & 1 (field 0 is
+ * subnormal: 0.5 * mantissa); an e8m0 exponent e scales by 2^(e - 127), and
+ * e = 255 is NaN. Element j of a row sits in nibble j % 8 of word j / 8, low
+ * nibble first; one exponent per 32 elements; no bias. */
+typedef struct mro_mxfp4 {
+  const uint32_t* packed; /* [experts?, out, in/8] */
+  const uint8_t* scales;  /* [experts?, out, in/32] */
+  int64_t experts;        /* 0 = single matrix */
+  int64_t out;
+  int64_t in;
+} mro_mxfp4;
+
+double mro_e2m1_value(int code);
+double mro_e8m0_value(int e);
+/* MXFP4Weights.init's shape checks (MXFP4Weights.swift:86-140). */
+int mro_mxfp4_validate(const mro_mxfp4* w, char* msg, int msg_len);
+/* mxfp4Dequantize (MXFP4Matmul.swift:114-136): fp32, exact. */
+void mro_mxfp4_dequantize(const mro_mxfp4* w, float* out);
+/* mxfp4MM (MXFP4Matmul.swift:17-34): bf16 out (and optional f32). */
+void mro_mxfp4_mm(const mro_mxfp4* w, int64_t expert, const uint16_t* x, int64_t T,
+                  uint16_t* out, float* out_f32);
+/* mxfp4GatherMM (MXFP4Matmul.swift:74-112). -1 on an id out of range. */
+int mro_mxfp4_gather_mm(const mro_mxfp4* w, const uint16_t* x, int64_t T,
+                        const int32_t* ids, int64_t k, uint16_t* out, float* out_f32);
+
 /* Router. scoring: 0 sigmoid, 1 softmax, 2 sqrt-softplus.
  * renorm: 0 none, 1 plain, 2 eps (k > 1 only). */
 void mro_router_logits(const uint16_t* x, const uint16_t* router_w, int64_t T,

@@ -66,6 +66,16 @@ def lib():
             L.mro_affine_mm_f32.argtypes = [vp, i64, vp, i64, vp]
             L.mro_affine_gather_mm.restype = C.c_int
             L.mro_affine_gather_mm.argtypes = [vp, vp, i64, vp, i64, vp, vp]
+            L.mro_e2m1_value.restype = f64
+            L.mro_e2m1_value.argtypes = [C.c_int]
+            L.mro_e8m0_value.restype = f64
+            L.mro_e8m0_value.argtypes = [C.c_int]
+            L.mro_mxfp4_validate.restype = C.c_int
+            L.mro_mxfp4_validate.argtypes = [vp, C.c_char_p, C.c_int]
+            L.mro_mxfp4_dequantize.argtypes = [vp, vp]
+            L.mro_mxfp4_mm.argtypes = [vp, i64, vp, i64, vp, vp]
+            L.mro_mxfp4_gather_mm.restype = C.c_int
+            L.mro_mxfp4_gather_mm.argtypes = [vp, vp, i64, vp, i64, vp, vp]
             L.mro_router_logits.argtypes = [vp, vp, i64, i64, i64, vp]
             L.mro_router_select.restype = C.c_int
             L.mro_router_select.argtypes = [
@@ -255,6 +265,95 @@ def affine_gather_mm(x_bf16: np.ndarray, w: Affine, ids: np.ndarray):
     if rc:
         raise ValueError("expert id out of range")
     return out, f
+
+
+# ------------------------------------------------------------------ MXFP4
+
+class _Mxfp4(C.Structure):
+    _fields_ = [("packed", C.c_void_p), ("scales", C.c_void_p), ("experts", C.c_int64),
+                ("out", C.c_int64), ("inn", C.c_int64)]
+
+
+@dataclass
+class Mxfp4:
+    """MXFP4 weights: packed uint32 [E?, out, in/8], e8m0 uint8 [E?, out, in/32]."""
+    packed: np.ndarray
+    scales: np.ndarray
+
+    @property
+    def experts(self) -> int:
+        return self.packed.shape[0] if self.packed.ndim == 3 else 0
+
+    @property
+    def out_features(self) -> int:
+        return self.packed.shape[-2]
+
+    @property
+    def in_features(self) -> int:
+        return self.packed.shape[-1] * 8
+
+    def c(self) -> _Mxfp4:
+        self.packed = np.ascontiguousarray(self.packed, np.uint32)
+        self.scales = np.ascontiguousarray(self.scales, np.uint8)
+        return _Mxfp4(self.packed.ctypes.data, self.scales.ctypes.data, self.experts,
+                      self.out_features, self.in_features)
+
+
+def e2m1_value(code: int) -> float:
+    return lib().mro_e2m1_value(code)
+
+
+def e8m0_value(e: int) -> float:
+    return lib().mro_e8m0_value(e)
+
+
+def mxfp4_validate(w: Mxfp4) -> tuple[int, str]:
+    buf = C.create_string_buffer(256)
+    cw = w.c()
+    rc = lib().mro_mxfp4_validate(C.byref(cw), buf, 256)
+    return rc, buf.value.decode()
+
+
+def mxfp4_dequantize(w: Mxfp4) -> np.ndarray:
+    out = np.empty(w.packed.shape[:-1] + (w.in_features,), np.float32)
+    cw = w.c()
+    lib().mro_mxfp4_dequantize(C.byref(cw), _p(out))
+    return out
+
+
+def mxfp4_mm(x_bf16: np.ndarray, w: Mxfp4, expert: int = 0):
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    T = x.shape[0]
+    out = np.empty((T, w.out_features), np.uint16)
+    f = np.empty((T, w.out_features), np.float32)
+    cw = w.c()
+    lib().mro_mxfp4_mm(C.byref(cw), expert, _p(x), T, _p(out), _p(f))
+    return out, f
+
+
+def mxfp4_gather_mm(x_bf16: np.ndarray, w: Mxfp4, ids: np.ndarray):
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    ids = np.ascontiguousarray(ids, np.int32)
+    T, k = ids.shape
+    out = np.empty((T, k, w.out_features), np.uint16)
+    f = np.empty((T, k, w.out_features), np.float32)
+    cw = w.c()
+    rc = lib().mro_mxfp4_gather_mm(C.byref(cw), _p(x), T, _p(ids), k, _p(out), _p(f))
+    if rc:
+        raise ValueError("expert id out of range")
+    return out, f
+
+
+def gen_mxfp4(seed: int, experts: int, out: int, inn: int, e_lo: int = 117,
+              e_hi: int = 128) -> Mxfp4:
+    """Seeded MXFP4 stack (experts == 0: one matrix): uniform codes from the
+    oracle's word stream, e8m0 exponents uniform in [e_lo, e_hi]."""
+    E = max(experts, 1)
+    words = gen_words(seed, E * out * inn // 8)
+    ex = sm_stream(sm_derive(seed, 0xE8), E * out * inn // 32)
+    scales = (e_lo + (ex % np.uint64(e_hi - e_lo + 1))).astype(np.uint8)
+    shp = (experts,) if experts else ()
+    return Mxfp4(words.reshape(shp + (out, inn // 8)), scales.reshape(shp + (out, inn // 32)))
 
 
 def router_logits(x_bf16: np.ndarray, router_w: np.ndarray) -> np.ndarray:

@@ -57,7 +57,8 @@ def test_struct_layout_matches_c_compiler(tmp_path):
               ("mr_expert_host", ["scales", "biases", "packed_bytes", "scale_bytes"]),
               ("mr_cache_stats", ["resident", "hits", "evictions", "bytes_copied"]),
               ("mr_tile_layout", ["bits", "feature_flags", "tile_count", "seed", "packed_bytes",
-                                  "bias_offset", "total_bytes", "scale_region_bytes"])]
+                                  "bias_offset", "total_bytes", "scale_region_bytes"]),
+              ("mr_mxfp4_desc", ["packed", "scales", "experts", "out_features", "in_features"])]
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "minirun_moe.h"',
              "int main(void) {"]
     for s, fields in checks:
