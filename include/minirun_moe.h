@@ -205,6 +205,17 @@ mr_status mr_mxfp4_gather_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens,
                              const int32_t* ids, int32_t top_k,
                              const mr_mxfp4_desc* w, uint16_t* out, void* stream);
 
+/* The same two with fp32 x and fp32 out ("float32 in gives float32 out",
+ * MXFP4Matmul.swift:7-8), the form K3's latent MoE runs in. Each activation
+ * enters the tensor core as two f16 terms (22 significant bits of the
+ * element, relative to the largest magnitude of its 32-element group);
+ * products are exact, accumulation fp32. x must be 16-byte aligned. */
+mr_status mr_mxfp4_mm_f32(mr_ctx* ctx, const float* x, int64_t tokens,
+                          const mr_mxfp4_desc* w, float* out, void* stream);
+mr_status mr_mxfp4_gather_mm_f32(mr_ctx* ctx, const float* x, int64_t tokens,
+                                 const int32_t* ids, int32_t top_k,
+                                 const mr_mxfp4_desc* w, float* out, void* stream);
+
 /* mxfp4Dequantize (MXFP4Matmul.swift:114-136): dense fp32 [experts?, out, in]
  * copy, exact (e2m1 * 2^(e-127) is representable; e = 255 gives NaN).
  * Validation only. */
@@ -261,6 +272,74 @@ mr_status mr_router_select_logits(mr_ctx* ctx, const float* logits,
                                   int64_t tokens, const mr_router_config* cfg,
                                   int32_t* ids, float* weights, float* margins,
                                   void* stream);
+
+/* ------------------------------------------------- K3 latent MoE block
+ * K3MoE.forward (Sources/ModelAdapters/Operators/MoE.swift:152-272,
+ * KimiSparseMoeBlock.forward): router on the full hidden state, routed
+ * experts (MXFP4) in a narrower latent, the weighted slot sum RMS-normalised
+ * in the latent and projected back, plus a shared expert on the original
+ * hidden state. All fp32, as the reference pins it. */
+
+/* k3Linear (Operators/Linear.swift:47-57) / K3Projection.dense:
+ * out[T, out] = x[T, in] . W^T, x and out fp32, W bf16 or fp32 [out, in]
+ * (fp32 products and sums). Needs in % 8 == 0 and 16-byte aligned x and W. */
+mr_status mr_dense_mm_f32(mr_ctx* ctx, const float* x, int64_t tokens, const void* w,
+                          mr_dtype w_dtype, int64_t out_features, int64_t in_features,
+                          float* out, void* stream);
+
+/* K3Activation.situ (Operators/Activations.swift:15-47): x [rows, 2d] is the
+ * concatenation [gate | up]; out [rows, d] =
+ * (beta * tanh(gate / beta) * sigmoid(gate)) * (lb * tanh(up / lb)), with the
+ * up branch left linear when linear_beta <= 0. fp32. */
+mr_status mr_k3_situ(mr_ctx* ctx, const float* x, int64_t rows, int64_t d, float beta,
+                     float linear_beta, float* out, void* stream);
+
+typedef enum mr_k3_proj_kind {
+  MR_K3_PROJ_DENSE = 0, /* K3Projection.dense: bf16 or fp32 [out, in] */
+  MR_K3_PROJ_MXFP4 = 1  /* K3Projection.mxfp4: a single MXFP4 matrix   */
+} mr_k3_proj_kind;
+
+/* K3Projection (Operators/Linear.swift:19-45). */
+typedef struct mr_k3_projection {
+  int32_t kind;           /* mr_k3_proj_kind */
+  const void* dense;      /* DENSE: [out_features, in_features]        */
+  mr_dtype dense_dtype;   /* DENSE: MR_DTYPE_BF16 or MR_DTYPE_F32      */
+  int64_t out_features;   /* DENSE                                      */
+  int64_t in_features;    /* DENSE                                      */
+  mr_mxfp4_desc mx;       /* MXFP4: experts == 0                        */
+} mr_k3_projection;
+
+/* K3MoE.Weights (MoE.swift:168-201) with TinyK3Config's block settings. */
+typedef struct mr_k3_moe {
+  mr_router_config router;      /* sigmoid; correction_bias; K3: renorm EPS
+                                   1e-20 when moe_renormalize, else NONE   */
+  const void* gate_weight;      /* router [experts, hidden]                 */
+  mr_dtype gate_dtype;          /* bf16 or fp32 (the logits are fp32)       */
+  mr_k3_projection routed_down; /* routed_expert_down_proj [latent, hidden] */
+  mr_k3_projection routed_up;   /* routed_expert_up_proj [hidden, latent]   */
+  const void* routed_norm;      /* routed_expert_norm [latent], or NULL when
+                                   latent_moe_use_norm is false             */
+  mr_dtype norm_dtype;          /* bf16 or fp32                             */
+  float rms_eps;
+  mr_mxfp4_desc w1, w3, w2;     /* [E, inter, latent] x2, [E, latent, inter] */
+  mr_k3_projection shared_gate; /* [shared_inter, hidden]                   */
+  mr_k3_projection shared_up;   /* [shared_inter, hidden]                   */
+  mr_k3_projection shared_down; /* [hidden, shared_inter]                   */
+  int64_t hidden, latent, inter, shared_inter; /* shared_inter 0: none      */
+  float situ_beta;              /* activation_situ_beta                     */
+  float situ_linear_beta;       /* activation_situ_linear_beta; <= 0: none  */
+} mr_k3_moe;
+
+/* Host-only checks of the block (shapes, dtypes, this build's limits: MXFP4
+ * operands need in % 512 == 0). */
+mr_status mr_k3_moe_validate(const mr_k3_moe* block, char* msg, size_t msg_len);
+
+/* out[T, hidden] fp32 = K3MoE.forward(x[T, hidden] fp32). ids_out int32
+ * [T, top_k] and weights_out fp32 [T, top_k] (either may be NULL) receive the
+ * selection. x and out 16-byte aligned device buffers. */
+mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* block, const float* x,
+                            int64_t tokens, float* out, int32_t* ids_out,
+                            float* weights_out, void* stream);
 
 /* ------------------------------------------------------------- MoE layer
  * DeepSeekV4MoEFFN router -> routed -> shared section

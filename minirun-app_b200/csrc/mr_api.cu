@@ -499,6 +499,7 @@ mr_status mr_ctx_destroy(mr_ctx* ctx) {
   cudaDeviceSynchronize();
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->io) cudaFree(ctx->io);
+  if (ctx->aux) cudaFree(ctx->aux);
   if (ctx->fixed) cudaFree(ctx->fixed);
   for (auto& p : ctx->pending) {
     cudaEventDestroy(p.a);
@@ -845,9 +846,11 @@ static mr_status mxfp4_mm_limits(const mr_mxfp4_desc* w, std::string& why) {
   return MR_OK;
 }
 
-static mr_status mxfp4_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const int32_t* ids,
-                              int32_t k, const mr_mxfp4_desc* w, uint16_t* out, void* stream,
-                              bool dense) {
+// x / out: bf16 (x_f32 false) or fp32 (x_f32 true) — mxfp4MM's "float32 in
+// gives float32 out".
+static mr_status mxfp4_common(mr_ctx* ctx, const void* x, bool x_f32, int64_t T,
+                              const int32_t* ids, int32_t k, const mr_mxfp4_desc* w, void* out,
+                              void* stream, bool dense) {
   if (!ctx) return MR_ERR_INVALID_ARGUMENT;
   std::string why;
   mr_status st = validate_mxfp4(w, why);
@@ -876,7 +879,7 @@ static mr_status mxfp4_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const i
   Bump b{nullptr};
   for (int pass = 0; pass < 2; ++pass) {
     b.off = 0;
-    b.take<uint16_t>(T * in);
+    b.take<uint16_t>(T * in * (x_f32 ? 2 : 1));
     b.take<float>(T * (in / kGroup) * 2);
     b.take<int>(4);
     b.take<int4>(max_seg);
@@ -888,7 +891,7 @@ static mr_status mxfp4_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const i
     }
   }
   b.off = 0;
-  uint16_t* xperm = b.take<uint16_t>(T * in);
+  uint16_t* xperm = b.take<uint16_t>(T * in * (x_f32 ? 2 : 1));
   float* xscale = b.take<float>(T * (in / kGroup) * 2);
   int* nseg = b.take<int>(4);
   int4* segs = b.take<int4>(max_seg);
@@ -904,7 +907,8 @@ static mr_status mxfp4_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const i
   tm.b_packed = tm.sa_packed = tm.sb_packed = tm.a_packed;
   tm.b_scales = tm.sa_scales = tm.sb_scales = tm.a_scales;
 
-  PrepMxParams pp{x, T, in, xperm, xscale};
+  PrepMxParams pp{x_f32 ? nullptr : static_cast<const uint16_t*>(x),
+                  x_f32 ? static_cast<const float*>(x) : nullptr, T, in, xperm, xscale};
   const int64_t chunks = T * (in / 16);
   const int pgrid = (int)std::min<int64_t>((chunks + 255) / 256, 4 * ctx->sm_count);
   prep_mx_kernel<<<pgrid, 256, 0, s>>>(pp);
@@ -930,12 +934,16 @@ static mr_status mxfp4_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const i
   g.xsum = xscale;
   g.xsum_parts = 2;
   g.error = ctx->d_error;
-  g.out_bf16 = out;
+  if (x_f32)
+    g.out_f32 = static_cast<float*>(out);
+  else
+    g.out_bf16 = static_cast<uint16_t*>(out);
   g.seg_cols = seg_cols;
   g.rb_count = (int)((g.rows + kTmaRows - 1) / kTmaRows);
   const int64_t items = max_seg * g.rb_count;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
-  return cuda_check(ctx, launch_tma_mx(g, tm, seg_cols / 8, grid, s), "gemv(mxfp4)");
+  return cuda_check(ctx, launch_tma_mx(g, tm, seg_cols / 8, x_f32 ? 2 : 1, grid, s),
+                    "gemv(mxfp4)");
 }
 
 namespace mr {
@@ -976,12 +984,23 @@ mr_status mr_mxfp4_validate(const mr_mxfp4_desc* w, char* msg, size_t msg_len) {
 
 mr_status mr_mxfp4_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens, const mr_mxfp4_desc* w,
                       uint16_t* out, void* stream) {
-  return mxfp4_common(ctx, x, tokens, nullptr, 1, w, out, stream, true);
+  return mxfp4_common(ctx, x, false, tokens, nullptr, 1, w, out, stream, true);
 }
 
 mr_status mr_mxfp4_gather_mm(mr_ctx* ctx, const uint16_t* x, int64_t tokens, const int32_t* ids,
                              int32_t top_k, const mr_mxfp4_desc* w, uint16_t* out, void* stream) {
-  return mxfp4_common(ctx, x, tokens, ids, top_k, w, out, stream, false);
+  return mxfp4_common(ctx, x, false, tokens, ids, top_k, w, out, stream, false);
+}
+
+mr_status mr_mxfp4_mm_f32(mr_ctx* ctx, const float* x, int64_t tokens, const mr_mxfp4_desc* w,
+                          float* out, void* stream) {
+  return mxfp4_common(ctx, x, true, tokens, nullptr, 1, w, out, stream, true);
+}
+
+mr_status mr_mxfp4_gather_mm_f32(mr_ctx* ctx, const float* x, int64_t tokens, const int32_t* ids,
+                                 int32_t top_k, const mr_mxfp4_desc* w, float* out,
+                                 void* stream) {
+  return mxfp4_common(ctx, x, true, tokens, ids, top_k, w, out, stream, false);
 }
 
 mr_status mr_mxfp4_dequantize(mr_ctx* ctx, const mr_mxfp4_desc* w, float* out, void* stream) {

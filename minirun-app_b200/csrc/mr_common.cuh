@@ -279,6 +279,10 @@ struct mr_ctx {
   // device staging of the host-buffer entry point
   void* io = nullptr;
   size_t io_bytes = 0;
+  // block-level intermediates of composite forwards (K3 latent MoE), kept
+  // apart from `ws`, which the ops they call use
+  void* aux = nullptr;
+  size_t aux_bytes = 0;
   // CUDA-event profiling of layer launches (mr_ctx_profile)
   struct Pending {
     int cls;

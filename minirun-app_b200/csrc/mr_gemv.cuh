@@ -78,6 +78,7 @@ struct GemvParams {
   unsigned* error;        // device error word
   // epilogues
   uint16_t* out_bf16;     // STORE: [*, rows]; SWIGLU: h [*, rows] permuted
+  float* out_f32;         // STORE (MXFP4 kernel): fp32 output instead of out_bf16
   float* hsum;            // SWIGLU: [*, rows/64]
   float* part;            // PARTIAL: [*, rows]
   const float* weights;   // routing weights [Tk]

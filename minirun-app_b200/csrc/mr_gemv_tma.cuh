@@ -28,6 +28,10 @@
 // activations that the MX prep stored as f16 scaled by 2^-k per half (k
 // puts the half's largest magnitude in [2^14, 2^15)). The fold is
 // y += (2^(e-127) * 2^k) * acc per half; only the store epilogue is built.
+// XS == 2 takes fp32 activations as two f16 terms per element (hi =
+// f16(x * 2^-k), lo = f16(x * 2^-k - hi): 22 significant bits), both
+// accumulated into the same fragment; the store is bf16 or, with
+// p.out_f32, fp32.
 #pragma once
 
 #include <cuda.h>
@@ -297,6 +301,26 @@ MR_DEVICE void group_mma_mx(float (&lo)[4], float (&hi)[4], const uint32_t (&wa)
   mma_f16_16816(hi, ra[2], rb[2], ra[3], rb[3], xb[6], xb[7]);
 }
 
+// MX with fp32 activations: the same four products against both f16 terms
+// of the activations (xh, xl), accumulated into the same fragments.
+MR_DEVICE void group_mma_mx2(float (&lo)[4], float (&hi)[4], const uint32_t (&wa)[2],
+                             const uint32_t (&wb)[2], const uint32_t (&xh)[8],
+                             const uint32_t (&xl)[8]) {
+  uint32_t ra[4], rb[4];
+  e2m1x8_to_f16x2(wa[0], ra);
+  e2m1x8_to_f16x2(wb[0], rb);
+  mma_f16_16816(lo, ra[0], rb[0], ra[1], rb[1], xh[0], xh[1]);
+  mma_f16_16816(lo, ra[2], rb[2], ra[3], rb[3], xh[2], xh[3]);
+  mma_f16_16816(lo, ra[0], rb[0], ra[1], rb[1], xl[0], xl[1]);
+  mma_f16_16816(lo, ra[2], rb[2], ra[3], rb[3], xl[2], xl[3]);
+  e2m1x8_to_f16x2(wa[1], ra);
+  e2m1x8_to_f16x2(wb[1], rb);
+  mma_f16_16816(hi, ra[0], rb[0], ra[1], rb[1], xh[4], xh[5]);
+  mma_f16_16816(hi, ra[2], rb[2], ra[3], rb[3], xh[6], xh[7]);
+  mma_f16_16816(hi, ra[0], rb[0], ra[1], rb[1], xl[4], xl[5]);
+  mma_f16_16816(hi, ra[2], rb[2], ra[3], rb[3], xl[6], xl[7]);
+}
+
 // Bounded wait. On expiry (or once another thread has flagged an abort) it
 // sets the device error word and the CTA's abort flag and returns, so the
 // caller carries on to every barrier it owes: results are then garbage but
@@ -321,9 +345,10 @@ MR_DEVICE void warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_fla
   (void)mbar_try_wait(bar, parity);
 }
 
-template <int BITS, int SD, int EPI, int NT>
+template <int BITS, int SD, int EPI, int NT, int XS = 1>
 __global__ void __launch_bounds__(kTmaThreads, 1)
     gemv_tma_kernel(const GemvParams p, const __grid_constant__ TmaMaps maps, const int nst) {
+  static_assert(XS == 1 || SD == MR_DTYPE_E8M0, "split activations: MXFP4 only");
   pdl_wait_and_release();
   using ST = TmaStage<BITS, SD, EPI>;
   constexpr int LW = QTraits<BITS>::kLaneWords;
@@ -570,7 +595,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const float* xp1[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
-      xr[t] = p.xperm + in_row(cur.vb[t]) * p.in + c * 16 + kq * kGpw * kGroup;
+      xr[t] = p.xperm + (in_row(cur.vb[t]) * p.in + kq * kGpw * kGroup) * XS + c * 16;
       xp0[t] = p.xsum + in_row(cur.v0[t]) * ngroups * XP + kq * kGpw * XP;
       xp1[t] = p.xsum + in_row(cur.v1[t]) * ngroups * XP + kq * kGpw * XP;
     }
@@ -635,8 +660,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             uint32_t xb[kGpw][8];
 #pragma unroll
             for (int j = 0; j < kGpw; ++j) {
-              const uint4 v0 = ldg_u128(xr[t] + j * kGroup);
-              const uint4 v1 = ldg_u128(xr[t] + j * kGroup + 8);
+              const uint4 v0 = ldg_u128(xr[t] + j * kGroup * XS);
+              const uint4 v1 = ldg_u128(xr[t] + j * kGroup * XS + 8);
               xb[j][0] = v0.x; xb[j][1] = v0.y; xb[j][2] = v0.z; xb[j][3] = v0.w;
               xb[j][4] = v1.x; xb[j][5] = v1.y; xb[j][6] = v1.z; xb[j][7] = v1.w;
             }
@@ -649,7 +674,14 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
               for (int j = 0; j < kGpw; ++j) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) lo[j][i] = hi[j][i] = 0.0f;
-                group_mma_mx(lo[j], hi[j], wa[j], wb[j], xb[j]);
+                if constexpr (XS == 1) {
+                  group_mma_mx(lo[j], hi[j], wa[j], wb[j], xb[j]);
+                } else {
+                  const uint4 u0 = ldg_u128(xr[t] + j * kGroup * XS + kGroup);
+                  const uint4 u1 = ldg_u128(xr[t] + j * kGroup * XS + kGroup + 8);
+                  const uint32_t xl[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+                  group_mma_mx2(lo[j], hi[j], wa[j], wb[j], xb[j], xl);
+                }
               }
 #pragma unroll
               for (int j = 0; j < kGpw; ++j) {
@@ -677,7 +709,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
               }
             }
           }
-          xr[t] += kTmaGps * kGroup;
+          xr[t] += kTmaGps * kGroup * XS;
           xp0[t] += kTmaGps * XP;
           xp1[t] += kTmaGps * XP;
         }
@@ -719,8 +751,14 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
             if (t < ntiles && ci < ncols) {
               const int64_t v = i ? cur.v1[t] : cur.v0[t];
               if constexpr (EPI == EPI_STORE) {
-                if (row_a < p.rows) p.out_bf16[v * p.rows + row_a] = f32_to_bf16_bits(y[t][i]);
-                if (row_b < p.rows) p.out_bf16[v * p.rows + row_b] = f32_to_bf16_bits(y[t][2 + i]);
+                if (ST::kMx && p.out_f32) {
+                  if (row_a < p.rows) p.out_f32[v * p.rows + row_a] = y[t][i];
+                  if (row_b < p.rows) p.out_f32[v * p.rows + row_b] = y[t][2 + i];
+                } else {
+                  if (row_a < p.rows) p.out_bf16[v * p.rows + row_a] = f32_to_bf16_bits(y[t][i]);
+                  if (row_b < p.rows)
+                    p.out_bf16[v * p.rows + row_b] = f32_to_bf16_bits(y[t][2 + i]);
+                }
               } else {
                 // routed slots are the w2 gather's bf16 output; the shared
                 // expert's hi/lo columns stay fp32

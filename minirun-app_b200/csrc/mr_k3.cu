@@ -1,0 +1,435 @@
+// mr_k3.cu — K3's latent MoE block (Sources/ModelAdapters/Operators/MoE.swift:
+// 152-272, `KimiSparseMoeBlock.forward`) and the fp32 pieces around the
+// MXFP4 gathers it runs in: the dense fp32 projection (k3Linear,
+// Operators/Linear.swift:47-57), the situ activation
+// (Operators/Activations.swift:15-47), and the slot-weighted sum followed by
+// the latent RMSNorm (MoE.swift:250-260, Operators/Normalization.swift:15-19).
+//
+// Everything here computes in fp32, as the reference pins it. The block
+// runs on one stream: router logits -> top-k -> latent down projection ->
+// gate and up gathers (MXFP4, fp32 activations) -> situ -> down gather per
+// (token, slot) -> weighted sum + norm -> latent up projection, plus the
+// shared expert on the original hidden state, added at the end.
+#include <algorithm>
+#include <string>
+
+#include "mr_common.cuh"
+#include "mr_gemv.cuh"
+
+namespace mr {
+
+// ------------------------------------------------------ dense projection
+// y[t][r] = sum_k x[t][k] * W[r][k] (fp32 FMA, fixed order: per lane over its
+// k positions, then a warp tree). W is bf16 (WF32 false) or fp32 [out, in];
+// 4 rows per warp, 8 warps (32 rows) per CTA, TT tokens per CTA (grid.y
+// walks token tiles). Requires in % 8 == 0 and 16-byte aligned rows.
+template <bool WF32, int TT>
+__global__ void __launch_bounds__(256) dense_f32_kernel(const float* __restrict__ x, int64_t T,
+                                                        const void* __restrict__ w, int64_t out,
+                                                        int64_t in, float* __restrict__ y) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row0 = ((int64_t)blockIdx.x * 8 + warp) * 4;
+  const int64_t t0 = (int64_t)blockIdx.y * TT;
+  if (row0 >= out) return;
+  float acc[4][TT];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int t = 0; t < TT; ++t) acc[r][t] = 0.0f;
+#pragma unroll 2
+  for (int64_t k = lane * 8; k < in; k += 256) {
+    float wv[4][8];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int64_t row = min(row0 + r, out - 1);  // rows past the end compute row out-1, unused
+      if constexpr (WF32) {
+        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(w) + row * in + k);
+        const float4 a = __ldg(p), b = __ldg(p + 1);
+        wv[r][0] = a.x; wv[r][1] = a.y; wv[r][2] = a.z; wv[r][3] = a.w;
+        wv[r][4] = b.x; wv[r][5] = b.y; wv[r][6] = b.z; wv[r][7] = b.w;
+      } else {
+        const uint4 u = ldg_u128(static_cast<const uint16_t*>(w) + row * in + k);
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          wv[r][2 * i] = __uint_as_float(q[i] << 16);
+          wv[r][2 * i + 1] = __uint_as_float(q[i] & 0xffff0000u);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      const int64_t tok = min(t0 + t, T - 1);
+      const float4* px = reinterpret_cast<const float4*>(x + tok * in + k);
+      const float4 a = __ldg(px), b = __ldg(px + 1);
+      const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[r][t] = fmaf(wv[r][i], xv[i], acc[r][t]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      float v = acc[r][t];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      acc[r][t] = v;
+    }
+  if (lane == 0) {
+#pragma unroll
+    for (int t = 0; t < TT; ++t)
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        if (t0 + t < T && row0 + r < out) y[(t0 + t) * out + row0 + r] = acc[r][t];
+  }
+}
+
+// ------------------------------------------------------------------ situ
+// out = (beta * tanh(g / beta) * sigmoid(g)) * (lb * tanh(u / lb)), or
+// * u when lb <= 0, in the reference's evaluation order
+// (Activations.swift:39-46): ((tanh(g / beta) * beta) * sigmoid(g)) * up.
+__global__ void situ_kernel(const float* __restrict__ g, const float* __restrict__ u,
+                            int64_t ld_in, int64_t rows, int64_t d, float beta, float lb,
+                            float* __restrict__ out) {
+  const int64_t n = rows * d;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / d, c = i - r * d;
+    const float gv = __ldg(g + r * ld_in + c);
+    float uv = __ldg(u + r * ld_in + c);
+    const float a = tanhf(gv / beta) * beta * sigmoid_f32(gv);
+    if (lb > 0.0f) uv = tanhf(uv / lb) * lb;
+    out[i] = a * uv;
+  }
+}
+
+// ------------------------------------------- weighted slot sum + RMSNorm
+// One CTA per token: rs[j] = sum_s w[t,s] * eo[t*k+s][j] (slot order), then,
+// with a norm weight, out[j] = weight[j] * (rs[j] * rsqrt(mean(rs^2) + eps))
+// (mean of squares summed per thread over j = tid, tid + 256, ..., then a
+// fixed tree). Dynamic shared memory: L floats.
+template <bool WF32>
+__global__ void __launch_bounds__(256) slot_sum_norm_kernel(const float* __restrict__ eo,
+                                                            const float* __restrict__ wts, int k,
+                                                            int64_t L, const void* norm_w,
+                                                            float eps, float* __restrict__ out) {
+  extern __shared__ float rs[];
+  __shared__ float red[256];
+  const int64_t t = blockIdx.x;
+  float sq = 0.0f;
+  for (int64_t j = threadIdx.x; j < L; j += blockDim.x) {
+    float s = 0.0f;
+    for (int sl = 0; sl < k; ++sl) s += __ldg(eo + (t * k + sl) * L + j) * __ldg(wts + t * k + sl);
+    rs[j] = s;
+    sq = fmaf(s, s, sq);
+  }
+  if (!norm_w) {
+    for (int64_t j = threadIdx.x; j < L; j += blockDim.x) out[t * L + j] = rs[j];
+    return;
+  }
+  red[threadIdx.x] = sq;
+  __syncthreads();
+  for (int h = 128; h > 0; h >>= 1) {
+    if ((int)threadIdx.x < h) red[threadIdx.x] += red[threadIdx.x + h];
+    __syncthreads();
+  }
+  const float scale = rsqrtf(red[0] / (float)L + eps);
+  for (int64_t j = threadIdx.x; j < L; j += blockDim.x) {
+    const float wv = WF32 ? __ldg(static_cast<const float*>(norm_w) + j)
+                          : bf16_bits_to_f32(__ldg(static_cast<const uint16_t*>(norm_w) + j));
+    out[t * L + j] = wv * (rs[j] * scale);
+  }
+}
+
+__global__ void add_f32_kernel(const float* __restrict__ a, float* __restrict__ y, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = y[i] + __ldg(a + i);
+}
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <bool WF32>
+static cudaError_t launch_dense(const float* x, int64_t T, const void* w, int64_t out, int64_t in,
+                                float* y, cudaStream_t s) {
+  const int tt = T >= 8 ? 8 : T >= 4 ? 4 : T >= 2 ? 2 : 1;
+  const dim3 grid((unsigned)((out + 31) / 32), (unsigned)((T + tt - 1) / tt));
+  switch (tt) {
+    case 8: dense_f32_kernel<WF32, 8><<<grid, 256, 0, s>>>(x, T, w, out, in, y); break;
+    case 4: dense_f32_kernel<WF32, 4><<<grid, 256, 0, s>>>(x, T, w, out, in, y); break;
+    case 2: dense_f32_kernel<WF32, 2><<<grid, 256, 0, s>>>(x, T, w, out, in, y); break;
+    default: dense_f32_kernel<WF32, 1><<<grid, 256, 0, s>>>(x, T, w, out, in, y); break;
+  }
+  return cudaGetLastError();
+}
+
+static mr_status dense_checks(const void* w, mr_dtype dt, int64_t out, int64_t in,
+                              std::string& why) {
+  if (!w || out <= 0 || in <= 0) {
+    why = "dense weight must be a non-NULL [out, in] matrix with positive sizes";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (dt != MR_DTYPE_BF16 && dt != MR_DTYPE_F32) {
+    why = "dense weights must be bfloat16 or float32";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (in % 8 != 0 || !al16(w)) {
+    why = "dense projection needs in % 8 == 0 and a 16-byte aligned weight";
+    return MR_ERR_UNSUPPORTED;
+  }
+  return MR_OK;
+}
+
+static mr_status dense_run(mr_ctx* ctx, const float* x, int64_t T, const void* w, mr_dtype dt,
+                           int64_t out, int64_t in, float* y, cudaStream_t s) {
+  if (!al16(x)) return fail(ctx, MR_ERR_UNSUPPORTED, "x must be 16-byte aligned");
+  const cudaError_t e = dt == MR_DTYPE_F32 ? launch_dense<true>(x, T, w, out, in, y, s)
+                                           : launch_dense<false>(x, T, w, out, in, y, s);
+  return cuda_check(ctx, e, "dense_f32_kernel");
+}
+
+static mr_status ensure_aux(mr_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->aux_bytes) return MR_OK;
+  if (ctx->aux) {
+    cudaError_t e = cudaFree(ctx->aux);
+    ctx->aux = nullptr;
+    ctx->aux_bytes = 0;
+    if (e != cudaSuccess) return cuda_check(ctx, e, "cudaFree(block buffers)");
+  }
+  const size_t want = bytes + bytes / 4 + (1 << 20);
+  cudaError_t e = cudaMalloc(&ctx->aux, want);
+  if (e != cudaSuccess) {
+    ctx->aux = nullptr;
+    return cuda_check(ctx, e, "cudaMalloc(block buffers)");
+  }
+  ctx->aux_bytes = want;
+  return MR_OK;
+}
+
+static mr_status validate_proj(const mr_k3_projection* p, int64_t out, int64_t in,
+                               const char* name, std::string& why) {
+  mr_status st = MR_OK;
+  if (p->kind == MR_K3_PROJ_DENSE) {
+    st = dense_checks(p->dense, p->dense_dtype, p->out_features, p->in_features, why);
+    if (!st && (p->out_features != out || p->in_features != in)) {
+      why = "must be [" + std::to_string(out) + ", " + std::to_string(in) + "]";
+      st = MR_ERR_INVALID_ARGUMENT;
+    }
+  } else if (p->kind == MR_K3_PROJ_MXFP4) {
+    char buf[256];
+    st = mr_mxfp4_validate(&p->mx, buf, sizeof buf);
+    why = buf;
+    if (!st && (p->mx.experts != 0 || p->mx.out_features != out || p->mx.in_features != in)) {
+      why = "must be a single [" + std::to_string(out) + ", " + std::to_string(in) + "] matrix";
+      st = MR_ERR_INVALID_ARGUMENT;
+    }
+    if (!st && in % 512 != 0) {
+      why = "MXFP4 projections of this build need in % 512 == 0";
+      st = MR_ERR_UNSUPPORTED;
+    }
+  } else {
+    why = "unknown projection kind";
+    st = MR_ERR_INVALID_ARGUMENT;
+  }
+  if (st) why = std::string(name) + ": " + why;
+  return st;
+}
+
+static mr_status validate_k3(const mr_k3_moe* L, std::string& why) {
+  if (!L) {
+    why = "block is NULL";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  char buf[256];
+  mr_status st = mr_router_config_validate(&L->router, buf, sizeof buf);
+  if (st) {
+    why = std::string("router: ") + buf;
+    return st;
+  }
+  if (L->router.scoring != MR_SCORING_SIGMOID) {
+    why = "K3's router scores with sigmoid (MoE.swift:106)";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (L->hidden <= 0 || L->latent <= 0 || L->inter <= 0 || L->shared_inter < 0) {
+    why = "hidden, latent and intermediate sizes must be positive";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if (!(L->situ_beta > 0.0f) || !std::isfinite(L->situ_beta) ||
+      !std::isfinite(L->situ_linear_beta) || !(L->rms_eps >= 0.0f)) {
+    why = "situ beta must be positive and finite, linear beta finite, eps nonnegative";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  if ((st = dense_checks(L->gate_weight, L->gate_dtype, L->router.experts, L->hidden, why))) {
+    why = "router gate: " + why;
+    return st;
+  }
+  if ((st = validate_proj(&L->routed_down, L->latent, L->hidden, "routed down", why)) ||
+      (st = validate_proj(&L->routed_up, L->hidden, L->latent, "routed up", why)))
+    return st;
+  if (L->routed_norm && L->norm_dtype != MR_DTYPE_BF16 && L->norm_dtype != MR_DTYPE_F32) {
+    why = "routed norm weight must be bfloat16 or float32";
+    return MR_ERR_INVALID_ARGUMENT;
+  }
+  const mr_mxfp4_desc* ds[3] = {&L->w1, &L->w3, &L->w2};
+  const int64_t outs[3] = {L->inter, L->inter, L->latent};
+  const int64_t ins[3] = {L->latent, L->latent, L->inter};
+  const char* names[3] = {"w1", "w3", "w2"};
+  for (int i = 0; i < 3; ++i) {
+    st = mr_mxfp4_validate(ds[i], buf, sizeof buf);
+    why = buf;
+    if (!st && (ds[i]->experts != L->router.experts || ds[i]->out_features != outs[i] ||
+                ds[i]->in_features != ins[i])) {
+      why = "stack must be [" + std::to_string(L->router.experts) + ", " +
+            std::to_string(outs[i]) + ", " + std::to_string(ins[i]) + "]";
+      st = MR_ERR_INVALID_ARGUMENT;
+    }
+    if (!st && ins[i] % 512 != 0) {
+      why = "MXFP4 gathers of this build need in % 512 == 0";
+      st = MR_ERR_UNSUPPORTED;
+    }
+    if (st) {
+      why = std::string(names[i]) + ": " + why;
+      return st;
+    }
+  }
+  if (L->shared_inter > 0 &&
+      ((st = validate_proj(&L->shared_gate, L->shared_inter, L->hidden, "shared gate", why)) ||
+       (st = validate_proj(&L->shared_up, L->shared_inter, L->hidden, "shared up", why)) ||
+       (st = validate_proj(&L->shared_down, L->hidden, L->shared_inter, "shared down", why))))
+    return st;
+  return MR_OK;
+}
+
+static mr_status project(mr_ctx* ctx, const mr_k3_projection* p, const float* x, int64_t T,
+                         float* y, cudaStream_t s) {
+  if (p->kind == MR_K3_PROJ_MXFP4) return mr_mxfp4_mm_f32(ctx, x, T, &p->mx, y, s);
+  return dense_run(ctx, x, T, p->dense, p->dense_dtype, p->out_features, p->in_features, y, s);
+}
+
+static mr_status situ_run(mr_ctx* ctx, const float* g, const float* u, int64_t ld, int64_t rows,
+                          int64_t d, float beta, float lb, float* out, cudaStream_t s) {
+  const int64_t n = rows * d;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8 * ctx->sm_count));
+  situ_kernel<<<grid, 256, 0, s>>>(g, u, ld, rows, d, beta, lb, out);
+  return cuda_check(ctx, cudaGetLastError(), "situ_kernel");
+}
+
+}  // namespace mr
+
+using namespace mr;
+
+extern "C" {
+
+mr_status mr_dense_mm_f32(mr_ctx* ctx, const float* x, int64_t tokens, const void* w,
+                          mr_dtype w_dtype, int64_t out_features, int64_t in_features, float* out,
+                          void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  std::string why;
+  mr_status st = dense_checks(w, w_dtype, out_features, in_features, why);
+  if (st) return fail(ctx, st, why);
+  if (tokens <= 0 || !x || !out)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "x must be [tokens, inFeatures] with tokens > 0");
+  return dense_run(ctx, x, tokens, w, w_dtype, out_features, in_features, out,
+                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+mr_status mr_k3_situ(mr_ctx* ctx, const float* x, int64_t rows, int64_t d, float beta,
+                     float linear_beta, float* out, void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  if (!x || !out || rows <= 0 || d <= 0)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "situ needs [rows, 2d] input with rows, d > 0");
+  if (!(beta > 0.0f) || !std::isfinite(beta) || !std::isfinite(linear_beta))
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "situ beta must be positive and finite");
+  return situ_run(ctx, x, x + d, 2 * d, rows, d, beta, linear_beta, out,
+                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+mr_status mr_k3_moe_validate(const mr_k3_moe* block, char* msg, size_t msg_len) {
+  std::string why;
+  const mr_status st = validate_k3(block, why);
+  if (msg && msg_len > 0) snprintf(msg, msg_len, "%s", why.c_str());
+  return st;
+}
+
+mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int64_t T,
+                            float* out, int32_t* ids_out, float* weights_out, void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  std::string why;
+  mr_status st = validate_k3(L, why);
+  if (st) return fail(ctx, st, why);
+  if (T <= 0 || !x || !out) return fail(ctx, MR_ERR_INVALID_ARGUMENT, "x must hold tokens > 0");
+  if (!al16(x) || !al16(out))
+    return fail(ctx, MR_ERR_UNSUPPORTED, "x and out must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t E = L->router.experts, k = L->router.top_k, Tk = T * k;
+  const int64_t H = L->hidden, Lt = L->latent, I = L->inter, S = L->shared_inter;
+
+  size_t off = 0;
+  auto take = [&](int64_t n) {
+    off = (off + 255) & ~size_t(255);
+    const size_t at = off;
+    off += (size_t)n * 4;
+    return at;
+  };
+  const size_t o_logits = take(T * E), o_ids = take(Tk), o_w = take(Tk), o_lat = take(T * Lt),
+               o_g = take(Tk * I), o_u = take(Tk * I), o_act = take(Tk * I),
+               o_eo = take(Tk * Lt), o_rs = take(T * Lt), o_ru = take(T * H),
+               o_sg = take(T * S), o_su = take(T * S), o_sa = take(T * S);
+  if ((st = ensure_aux(ctx, off))) return st;
+  char* base = static_cast<char*>(ctx->aux);
+  auto F = [&](size_t o) { return reinterpret_cast<float*>(base + o); };
+  int32_t* ids = ids_out ? ids_out : reinterpret_cast<int32_t*>(base + o_ids);
+  float* wts = weights_out ? weights_out : F(o_w);
+
+  // 1. router: fp32 logits of the FULL hidden state, sigmoid + bias choice
+  if ((st = dense_run(ctx, x, T, L->gate_weight, L->gate_dtype, E, H, F(o_logits), s))) return st;
+  if ((st = mr_router_select_logits(ctx, F(o_logits), T, &L->router, ids, wts, nullptr, s)))
+    return st;
+  // 2. routed: latent down projection, gate/up gathers, situ, down gather
+  if ((st = project(ctx, &L->routed_down, x, T, F(o_lat), s))) return st;
+  if ((st = mr_mxfp4_gather_mm_f32(ctx, F(o_lat), T, ids, (int32_t)k, &L->w1, F(o_g), s)) ||
+      (st = mr_mxfp4_gather_mm_f32(ctx, F(o_lat), T, ids, (int32_t)k, &L->w3, F(o_u), s)))
+    return st;
+  if ((st = situ_run(ctx, F(o_g), F(o_u), I, Tk, I, L->situ_beta, L->situ_linear_beta,
+                     F(o_act), s)))
+    return st;
+  // each (token, slot) row is its own column with one expert: ids as [Tk, 1]
+  if ((st = mr_mxfp4_gather_mm_f32(ctx, F(o_act), Tk, ids, 1, &L->w2, F(o_eo), s))) return st;
+  // 3. weighted slot sum in fp32, latent RMSNorm, up projection
+  const size_t smem = (size_t)Lt * 4;
+  if (smem > 200 * 1024) return fail(ctx, MR_ERR_UNSUPPORTED, "latent width too large");
+  if (L->norm_dtype == MR_DTYPE_F32) {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(slot_sum_norm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+    slot_sum_norm_kernel<true><<<(unsigned)T, 256, smem, s>>>(F(o_eo), wts, (int)k, Lt,
+                                                              L->routed_norm, L->rms_eps, F(o_rs));
+  } else {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(slot_sum_norm_kernel<false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    slot_sum_norm_kernel<false><<<(unsigned)T, 256, smem, s>>>(F(o_eo), wts, (int)k, Lt,
+                                                               L->routed_norm, L->rms_eps, F(o_rs));
+  }
+  if ((st = cuda_check(ctx, cudaGetLastError(), "slot_sum_norm_kernel"))) return st;
+  // 4. shared expert on the original hidden state, then the sum
+  if (S > 0) {
+    if ((st = project(ctx, &L->shared_gate, x, T, F(o_sg), s)) ||
+        (st = project(ctx, &L->shared_up, x, T, F(o_su), s)) ||
+        (st = situ_run(ctx, F(o_sg), F(o_su), S, T, S, L->situ_beta, L->situ_linear_beta,
+                       F(o_sa), s)) ||
+        (st = project(ctx, &L->shared_down, F(o_sa), T, out, s)) ||
+        (st = project(ctx, &L->routed_up, F(o_rs), T, F(o_ru), s)))
+      return st;
+    const int64_t n = T * H;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
+    add_f32_kernel<<<grid, 256, 0, s>>>(F(o_ru), out, n);
+    return cuda_check(ctx, cudaGetLastError(), "add_f32_kernel");
+  }
+  return project(ctx, &L->routed_up, F(o_rs), T, out, s);
+}
+
+}  // extern "C"

@@ -23,8 +23,9 @@ cudaError_t launch_tma_b4(const GemvParams& p, const TmaMaps& m, int sd, int epi
 cudaError_t launch_tma_b8(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, int grid,
                           cudaStream_t s);
 
-// MXFP4 form of the TMA kernel (in % 512 == 0, store epilogue, nt == 1).
-cudaError_t launch_tma_mx(const GemvParams& p, const TmaMaps& m, int nt, int grid,
+// MXFP4 form of the TMA kernel (in % 512 == 0, store epilogue, nt == 1);
+// xs = 1: bf16 activations, xs = 2: fp32 activations as two f16 terms.
+cudaError_t launch_tma_mx(const GemvParams& p, const TmaMaps& m, int nt, int xs, int grid,
                           cudaStream_t s);
 
 // tcgen05 kernel (in % 512 == 0, activations through tensor maps).
@@ -103,13 +104,13 @@ inline cudaError_t opt_in_smem(K kernel, int bytes, bool (&done)[64]) {
   return e;
 }
 
-template <int BITS, int SD, int EPI, int NT>
+template <int BITS, int SD, int EPI, int NT, int XS = 1>
 inline cudaError_t launch_tma_inst(const GemvParams& p, const TmaMaps& m, int grid,
                                    cudaStream_t s) {
   static bool done[64] = {};  // one per instantiation
   const int nst = tma_stages<BITS, SD, EPI, NT>();
   const int smem = tma_smem_bytes<BITS, SD, EPI, NT>(nst);
-  auto kern = gemv_tma_kernel<BITS, SD, EPI, NT>;
+  auto kern = gemv_tma_kernel<BITS, SD, EPI, NT, XS>;
   cudaError_t e = opt_in_smem(kern, smem, done);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, grid, kTmaThreads, smem, s, p, m, nst);

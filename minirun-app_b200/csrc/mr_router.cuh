@@ -80,12 +80,16 @@ __global__ void prep_kernel(const PrepParams p) {
 // significant bits, f16 normals 11) — and xscale[t][2g + half] = 2^k. Each group's 64 f16 are stored as four
 // 16-element lane segments: segment c = elements [8c, 8c+8) then
 // [32+8c, 32+8c+8) (words c and c + 4 of the packed row).
+// With fp32 input (xf non-NULL) each element becomes two f16 terms, hi =
+// f16(x * 2^-k) and lo = f16(x * 2^-k - hi); a row then holds, per group,
+// the 64 hi values in the layout above followed by the 64 lo values.
 struct PrepMxParams {
-  const uint16_t* x;
+  const uint16_t* x;   // bf16 input, or NULL
+  const float* xf;     // fp32 input, or NULL
   int64_t rows;
   int64_t in;
-  uint16_t* xperm;
-  float* xscale;
+  uint16_t* xperm;     // [rows, in] (bf16 input) or [rows, 2 * in] (fp32 input)
+  float* xscale;       // [rows, in / 32]
 };
 
 // Called by whole warps: the two chunks of a half exchange their maxima by
@@ -96,17 +100,31 @@ MR_DEVICE void prep_mx_chunk(const PrepMxParams& p, int64_t chunk, bool valid) {
   const int64_t r = chunk / per_row;
   const int64_t c16 = chunk - r * per_row;
   const int q = (int)(c16 & 3);  // chunk of the group: elements [16q, 16q+16), half q >> 1
-  const uint16_t* src = p.x + r * p.in + c16 * 16;
-  const uint4 v0 = ldg_u128(src);
-  const uint4 v1 = ldg_u128(src + 8);
-  uint16_t e[16];
-  memcpy(e, &v0, 16);
-  memcpy(e + 8, &v1, 16);
+  const bool split = p.xf != nullptr;
   float f[16];
+  if (split) {
+    const float4* src = reinterpret_cast<const float4*>(p.xf + r * p.in + c16 * 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = __ldg(src + i);
+      f[4 * i] = v.x;
+      f[4 * i + 1] = v.y;
+      f[4 * i + 2] = v.z;
+      f[4 * i + 3] = v.w;
+    }
+  } else {
+    const uint16_t* src = p.x + r * p.in + c16 * 16;
+    const uint4 v0 = ldg_u128(src);
+    const uint4 v1 = ldg_u128(src + 8);
+    uint16_t e[16];
+    memcpy(e, &v0, 16);
+    memcpy(e + 8, &v1, 16);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) f[i] = bf16_bits_to_f32(e[i]);
+  }
   float m = 0.0f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    f[i] = bf16_bits_to_f32(e[i]);
     const float a = fabsf(f[i]);
     if (a <= 3.402823466e38f) m = fmaxf(m, a);  // finite values only
   }
@@ -117,17 +135,28 @@ MR_DEVICE void prep_mx_chunk(const PrepMxParams& p, int64_t chunk, bool valid) {
     (void)frexpf(m, &ex);  // m = f * 2^ex, f in [0.5, 1)
     k = ex - 1 - 14;
   }
-  uint16_t o[16];
+  uint16_t o[16], ol[16];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i] = __half_as_ushort(__float2half_rn(ldexpf(f[i], -k)));
+  for (int i = 0; i < 16; ++i) {
+    const float v = ldexpf(f[i], -k);
+    const __half h = __float2half_rn(v);
+    o[i] = __half_as_ushort(h);
+    ol[i] = __half_as_ushort(__float2half_rn(v - __half2float(h)));
+  }
   if (valid) {
-    uint16_t* g = p.xperm + r * p.in + (c16 >> 2) * 64;
+    const int xs = split ? 2 : 1;
+    uint16_t* g = p.xperm + (r * p.in + (c16 >> 2) * 64) * xs;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int w = 2 * q + h;  // word of the group's packed row
+      const int at = (w & 3) * 16 + (w >> 2) * 8;
       uint4 u;
       memcpy(&u, o + 8 * h, 16);
-      *reinterpret_cast<uint4*>(g + (w & 3) * 16 + (w >> 2) * 8) = u;
+      *reinterpret_cast<uint4*>(g + at) = u;
+      if (split) {
+        memcpy(&u, ol + 8 * h, 16);
+        *reinterpret_cast<uint4*>(g + 64 + at) = u;
+      }
     }
     if ((q & 1) == 0) p.xscale[r * (p.in / kGroup) * 2 + (c16 >> 2) * 2 + (q >> 1)] = ldexpf(1.0f, k);
   }

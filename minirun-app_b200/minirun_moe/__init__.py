@@ -14,7 +14,8 @@ from .moe import (MoELayer, ResidentExpertBackend, RouterConfig, TokenExpertMap,
                   router_select_hashed, router_select_logits)
 from .checkpoint import Checkpoint, SafetensorsError, SafetensorsFile, write_safetensors
 from .mxfp4 import (MXFP4BridgeError, MXFP4Weights, mxfp4_dequantize, mxfp4_gather_mm,
-                    mxfp4_mm, mxfp4_validate)
+                    mxfp4_gather_mm_f32, mxfp4_mm, mxfp4_mm_f32, mxfp4_validate)
+from .k3 import K3MoE, K3Projection, dense_mm_f32, situ
 from .tiles import (ExpertContainers, TileContainer, TileContainerError, write_container,
                     write_expert_containers)
 
@@ -27,4 +28,5 @@ __all__ = [
     "write_expert_containers", "Checkpoint", "SafetensorsError", "SafetensorsFile",
     "write_safetensors", "TokenExpertMap", "router_select_hashed", "MXFP4BridgeError",
     "MXFP4Weights", "mxfp4_dequantize", "mxfp4_gather_mm", "mxfp4_mm", "mxfp4_validate",
+    "mxfp4_gather_mm_f32", "mxfp4_mm_f32", "K3MoE", "K3Projection", "dense_mm_f32", "situ",
 ]

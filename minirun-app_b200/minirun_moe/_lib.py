@@ -54,6 +54,25 @@ class mr_router_config(C.Structure):
                 ("correction_bias", vp)]
 
 
+class mr_k3_projection(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("dense", vp), ("dense_dtype", C.c_int),
+                ("out_features", C.c_int64), ("in_features", C.c_int64), ("mx", mr_mxfp4_desc)]
+
+
+class mr_k3_moe(C.Structure):
+    _fields_ = [("router", mr_router_config), ("gate_weight", vp), ("gate_dtype", C.c_int),
+                ("routed_down", mr_k3_projection), ("routed_up", mr_k3_projection),
+                ("routed_norm", vp), ("norm_dtype", C.c_int), ("rms_eps", C.c_float),
+                ("w1", mr_mxfp4_desc), ("w3", mr_mxfp4_desc), ("w2", mr_mxfp4_desc),
+                ("shared_gate", mr_k3_projection), ("shared_up", mr_k3_projection),
+                ("shared_down", mr_k3_projection), ("hidden", C.c_int64), ("latent", C.c_int64),
+                ("inter", C.c_int64), ("shared_inter", C.c_int64), ("situ_beta", C.c_float),
+                ("situ_linear_beta", C.c_float)]
+
+
+MR_K3_PROJ_DENSE, MR_K3_PROJ_MXFP4 = 0, 1
+
+
 class mr_expert_ptrs(C.Structure):
     _fields_ = [("packed", vp * 3), ("scales", vp * 3), ("biases", vp * 3)]
 
@@ -114,6 +133,13 @@ SIGNATURES = {
     "mr_mxfp4_gather_mm": (C.c_int, [vp, vp, C.c_int64, vp, C.c_int32,
                                      C.POINTER(mr_mxfp4_desc), vp, vp]),
     "mr_mxfp4_dequantize": (C.c_int, [vp, C.POINTER(mr_mxfp4_desc), vp, vp]),
+    "mr_mxfp4_mm_f32": (C.c_int, [vp, vp, C.c_int64, C.POINTER(mr_mxfp4_desc), vp, vp]),
+    "mr_mxfp4_gather_mm_f32": (C.c_int, [vp, vp, C.c_int64, vp, C.c_int32,
+                                         C.POINTER(mr_mxfp4_desc), vp, vp]),
+    "mr_dense_mm_f32": (C.c_int, [vp, vp, C.c_int64, vp, C.c_int, C.c_int64, C.c_int64, vp, vp]),
+    "mr_k3_situ": (C.c_int, [vp, vp, C.c_int64, C.c_int64, C.c_float, C.c_float, vp, vp]),
+    "mr_k3_moe_validate": (C.c_int, [C.POINTER(mr_k3_moe), C.c_char_p, C.c_size_t]),
+    "mr_k3_moe_forward": (C.c_int, [vp, C.POINTER(mr_k3_moe), vp, C.c_int64, vp, vp, vp, vp]),
     "mr_router_config_validate": (C.c_int, [C.POINTER(mr_router_config), C.c_char_p,
                                             C.c_size_t]),
     "mr_router_select": (C.c_int, [vp, vp, C.c_int64, C.c_int64, vp,

@@ -145,6 +145,46 @@ def mxfp4_gather_mm(x: torch.Tensor, weights: MXFP4Weights, rhs_indices: torch.T
     return out
 
 
+def _check_xf(x: torch.Tensor, in_features: int) -> None:
+    if x.dim() != 2 or x.dtype != torch.float32 or x.shape[1] != in_features or not x.is_cuda:
+        raise MXFP4BridgeError(f"x must be a CUDA fp32 [tokens, {in_features}] tensor")
+
+
+def mxfp4_mm_f32(x: torch.Tensor, weights: MXFP4Weights) -> torch.Tensor:
+    """``mxfp4MM`` with fp32 x: fp32 out (MXFP4Matmul.swift:7-8)."""
+    if weights.experts is not None:
+        raise MXFP4BridgeError("mxfp4MM needs a single matrix; use mxfp4GatherMM for a stack")
+    _check_xf(x, weights.in_features)
+    x = x.contiguous()
+    out = torch.empty((x.shape[0], weights.out_features), dtype=torch.float32, device=x.device)
+    ctx = Context.get(x.device.index)
+    d = weights.desc()
+    ctx.check("mr_mxfp4_mm_f32", L.load().mr_mxfp4_mm_f32(
+        ctx.handle, _ptr(x), x.shape[0], C.byref(d), _ptr(out), C.c_void_p(_stream())))
+    return out
+
+
+def mxfp4_gather_mm_f32(x: torch.Tensor, weights: MXFP4Weights,
+                        rhs_indices: torch.Tensor) -> torch.Tensor:
+    """``mxfp4GatherMM`` with fp32 x: fp32 ``[tokens, k, out]``."""
+    if weights.experts is None:
+        raise MXFP4BridgeError(
+            "mxfp4GatherMM needs a stacked MXFP4Weights; use mxfp4MM for a single matrix")
+    _check_xf(x, weights.in_features)
+    if rhs_indices.dim() != 2 or rhs_indices.shape[0] != x.shape[0]:
+        raise MXFP4BridgeError(
+            "rhsIndices must be [tokens, expertsPerToken] matching x's token count")
+    x = x.contiguous()
+    ids = rhs_indices.to(device=x.device, dtype=torch.int32).contiguous()
+    T, k = ids.shape
+    out = torch.empty((T, k, weights.out_features), dtype=torch.float32, device=x.device)
+    ctx = Context.get(x.device.index)
+    d = weights.desc()
+    ctx.check("mr_mxfp4_gather_mm_f32", L.load().mr_mxfp4_gather_mm_f32(
+        ctx.handle, _ptr(x), T, _ptr(ids), k, C.byref(d), _ptr(out), C.c_void_p(_stream())))
+    return out
+
+
 def mxfp4_dequantize(weights: MXFP4Weights) -> torch.Tensor:
     """Dense fp32 ``e2m1 * 2**(e-127)`` (MXFP4Matmul.swift:114-136), exact.
     Validation only."""

@@ -445,6 +445,34 @@ int mro_mxfp4_gather_mm(const mro_mxfp4* w, const uint16_t* x, int64_t T,
   return 0;
 }
 
+void mro_mxfp4_mm_f32(const mro_mxfp4* w, int64_t expert, const float* x, int64_t T,
+                      float* out) {
+  double* xd = (double*)malloc(sizeof(double) * (size_t)(T * w->in));
+  double* y = (double*)malloc(sizeof(double) * (size_t)(T * w->out));
+  for (int64_t i = 0; i < T * w->in; ++i) xd[i] = (double)x[i];
+  mx_expert_dot(w, expert, xd, T, y);
+  for (int64_t i = 0; i < T * w->out; ++i) out[i] = (float)y[i];
+  free(xd);
+  free(y);
+}
+
+int mro_mxfp4_gather_mm_f32(const mro_mxfp4* w, const float* x, int64_t T,
+                            const int32_t* ids, int64_t k, float* out) {
+  const int64_t E = w->experts, in = w->in, outf = w->out;
+  for (int64_t i = 0; i < T * k; ++i)
+    if (ids[i] < 0 || ids[i] >= E) return -1;
+  double* xd = (double*)malloc(sizeof(double) * (size_t)in);
+  double* y = (double*)malloc(sizeof(double) * (size_t)outf);
+  for (int64_t p = 0; p < T * k; ++p) {
+    for (int64_t c = 0; c < in; ++c) xd[c] = (double)x[(p / k) * in + c];
+    mx_expert_dot(w, ids[p], xd, 1, y);
+    for (int64_t r = 0; r < outf; ++r) out[p * outf + r] = (float)y[r];
+  }
+  free(xd);
+  free(y);
+  return 0;
+}
+
 /* ------------------------------------------------------------------ router */
 
 /* k3Linear(x.f32, W.f32) (Sources/ModelAdapters/Operators/Linear.swift:55-57),

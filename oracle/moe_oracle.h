@@ -102,6 +102,12 @@ void mro_mxfp4_mm(const mro_mxfp4* w, int64_t expert, const uint16_t* x, int64_t
 int mro_mxfp4_gather_mm(const mro_mxfp4* w, const uint16_t* x, int64_t T,
                         const int32_t* ids, int64_t k, uint16_t* out, float* out_f32);
 
+/* fp32 x, fp32 out ("float32 in gives float32 out", MXFP4Matmul.swift:7-8). */
+void mro_mxfp4_mm_f32(const mro_mxfp4* w, int64_t expert, const float* x, int64_t T,
+                      float* out);
+int mro_mxfp4_gather_mm_f32(const mro_mxfp4* w, const float* x, int64_t T,
+                            const int32_t* ids, int64_t k, float* out);
+
 /* Router. scoring: 0 sigmoid, 1 softmax, 2 sqrt-softplus.
  * renorm: 0 none, 1 plain, 2 eps (k > 1 only). */
 void mro_router_logits(const uint16_t* x, const uint16_t* router_w, int64_t T,

@@ -76,6 +76,9 @@ def lib():
             L.mro_mxfp4_mm.argtypes = [vp, i64, vp, i64, vp, vp]
             L.mro_mxfp4_gather_mm.restype = C.c_int
             L.mro_mxfp4_gather_mm.argtypes = [vp, vp, i64, vp, i64, vp, vp]
+            L.mro_mxfp4_mm_f32.argtypes = [vp, i64, vp, i64, vp]
+            L.mro_mxfp4_gather_mm_f32.restype = C.c_int
+            L.mro_mxfp4_gather_mm_f32.argtypes = [vp, vp, i64, vp, i64, vp]
             L.mro_router_logits.argtypes = [vp, vp, i64, i64, i64, vp]
             L.mro_router_select.restype = C.c_int
             L.mro_router_select.argtypes = [
@@ -342,6 +345,25 @@ def mxfp4_gather_mm(x_bf16: np.ndarray, w: Mxfp4, ids: np.ndarray):
     if rc:
         raise ValueError("expert id out of range")
     return out, f
+
+
+def mxfp4_mm_f32(x: np.ndarray, w: Mxfp4, expert: int = 0) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty((x.shape[0], w.out_features), np.float32)
+    cw = w.c()
+    lib().mro_mxfp4_mm_f32(C.byref(cw), expert, _p(x), x.shape[0], _p(out))
+    return out
+
+
+def mxfp4_gather_mm_f32(x: np.ndarray, w: Mxfp4, ids: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    ids = np.ascontiguousarray(ids, np.int32)
+    T, k = ids.shape
+    out = np.empty((T, k, w.out_features), np.float32)
+    cw = w.c()
+    if lib().mro_mxfp4_gather_mm_f32(C.byref(cw), _p(x), T, _p(ids), k, _p(out)):
+        raise ValueError("expert id out of range")
+    return out
 
 
 def gen_mxfp4(seed: int, experts: int, out: int, inn: int, e_lo: int = 117,

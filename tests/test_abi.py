@@ -58,7 +58,10 @@ def test_struct_layout_matches_c_compiler(tmp_path):
               ("mr_cache_stats", ["resident", "hits", "evictions", "bytes_copied"]),
               ("mr_tile_layout", ["bits", "feature_flags", "tile_count", "seed", "packed_bytes",
                                   "bias_offset", "total_bytes", "scale_region_bytes"]),
-              ("mr_mxfp4_desc", ["packed", "scales", "experts", "out_features", "in_features"])]
+              ("mr_mxfp4_desc", ["packed", "scales", "experts", "out_features", "in_features"]),
+              ("mr_k3_projection", ["kind", "dense", "dense_dtype", "in_features", "mx"]),
+              ("mr_k3_moe", ["router", "gate_weight", "routed_down", "routed_norm", "rms_eps",
+                             "w1", "w2", "shared_down", "shared_inter", "situ_linear_beta"])]
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "minirun_moe.h"',
              "int main(void) {"]
     for s, fields in checks:
