@@ -846,16 +846,108 @@ static mr_status mxfp4_mm_limits(const mr_mxfp4_desc* w, std::string& why) {
   return MR_OK;
 }
 
+namespace mr {
+
+// Both sizes are whole multiples of 256 bytes, so regions placed back to back
+// keep the 256-byte alignment their bump allocation assumes.
+size_t mx_plan_bytes(int64_t Tk, int E) {
+  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / pick_seg_cols(Tk) + 1;
+  const size_t n = 256 * 3 + 16 + (size_t)max_seg * 16 + (size_t)Tk * 4;
+  return (n + 255) & ~size_t(255);
+}
+
+size_t mx_act_bytes(int64_t rows, int64_t in, bool split) {
+  const size_t n =
+      256 * 2 + (size_t)rows * in * 2 * (split ? 2 : 1) + (size_t)rows * (in / kGroup) * 8;
+  return (n + 255) & ~size_t(255);
+}
+
+mr_status mx_plan_build(mr_ctx* ctx, const int32_t* ids, int64_t Tk, int E, bool dense, void* mem,
+                        MxPlan* pl, cudaStream_t s) {
+  Bump b{static_cast<char*>(mem)};
+  pl->seg_cols = pick_seg_cols(Tk);
+  pl->max_seg = std::min<int64_t>(E, Tk) + Tk / pl->seg_cols + 1;
+  pl->Tk = Tk;
+  pl->nseg = b.take<int>(4);
+  pl->segs = b.take<int4>(pl->max_seg);
+  pl->cols = b.take<int>(Tk);
+  if (dense) {
+    dense_plan_kernel<<<(int)std::min<int64_t>((Tk + 255) / 256, 1024), 256, 0, s>>>(
+        (int)Tk, pl->seg_cols, pl->nseg, pl->segs, pl->cols);
+  } else {
+    PlanParams plan{ids, (int)Tk, E, pl->nseg, pl->segs, pl->cols, ctx->d_error, pl->seg_cols};
+    plan_kernel<<<1, 256, 0, s>>>(plan);
+  }
+  return cuda_check(ctx, cudaGetLastError(), "plan kernel");
+}
+
+mr_status mx_prep(mr_ctx* ctx, const void* x, bool x_f32, int64_t rows, int64_t in, void* mem,
+                  MxAct* a, cudaStream_t s) {
+  Bump b{static_cast<char*>(mem)};
+  a->split = x_f32;
+  a->xperm = b.take<uint16_t>(rows * in * (x_f32 ? 2 : 1));
+  a->xscale = b.take<float>(rows * (in / kGroup) * 2);
+  PrepMxParams pp{x_f32 ? nullptr : static_cast<const uint16_t*>(x),
+                  x_f32 ? static_cast<const float*>(x) : nullptr, rows, in, a->xperm, a->xscale};
+  const int64_t chunks = rows * (in / 16);
+  const int pgrid = (int)std::max<int64_t>(1, std::min<int64_t>((chunks + 255) / 256, 4 * ctx->sm_count));
+  prep_mx_kernel<<<pgrid, 256, 0, s>>>(pp);
+  return cuda_check(ctx, cudaGetLastError(), "prep_mx_kernel");
+}
+
+mr_status mx_gemv(mr_ctx* ctx, const MxPlan& pl, const MxAct& a, int in_div,
+                  const mr_mxfp4_desc* w, void* out, cudaStream_t s) {
+  const int E = w->experts > 0 ? w->experts : 1;
+  const int64_t in = w->in_features;
+  TmaMaps tm;
+  memset(&tm, 0, sizeof tm);
+  const int64_t rows = (int64_t)E * w->out_features;
+  if (!tensor_map(ctx, &tm.a_packed, w->packed, rows, in / 8, kTmaRows, 0) ||
+      !tensor_map(ctx, &tm.a_scales, w->scales, rows, in / 32, kTmaRows, 7))
+    return fail(ctx, MR_ERR_CUDA, "tensor map encoding of the MXFP4 operands failed");
+  tm.b_packed = tm.sa_packed = tm.sb_packed = tm.a_packed;
+  tm.b_scales = tm.sa_scales = tm.sb_scales = tm.a_scales;
+  GemvParams g{};
+  g.rows = w->out_features;
+  g.in = in;
+  g.n_routed_segments = pl.nseg;
+  g.segments = pl.segs;
+  g.cols = pl.cols;
+  g.Tk = (int)pl.Tk;
+  g.in_div = in_div;
+  g.xperm = a.xperm;
+  g.xsum = a.xscale;
+  g.xsum_parts = 2;
+  g.error = ctx->d_error;
+  if (a.split)
+    g.out_f32 = static_cast<float*>(out);
+  else
+    g.out_bf16 = static_cast<uint16_t*>(out);
+  g.seg_cols = pl.seg_cols;
+  g.rb_count = (int)((g.rows + kTmaRows - 1) / kTmaRows);
+  const int64_t items = pl.max_seg * g.rb_count;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
+  return cuda_check(ctx, launch_tma_mx(g, tm, pl.seg_cols / 8, a.split ? 2 : 1, grid, s),
+                    "gemv(mxfp4)");
+}
+
+mr_status mx_check_mm(mr_ctx* ctx, const mr_mxfp4_desc* w) {
+  std::string why;
+  mr_status st = validate_mxfp4(w, why);
+  if (!st) st = mxfp4_mm_limits(w, why);
+  return st ? fail(ctx, st, why) : MR_OK;
+}
+
+}  // namespace mr
+
 // x / out: bf16 (x_f32 false) or fp32 (x_f32 true) — mxfp4MM's "float32 in
 // gives float32 out".
 static mr_status mxfp4_common(mr_ctx* ctx, const void* x, bool x_f32, int64_t T,
                               const int32_t* ids, int32_t k, const mr_mxfp4_desc* w, void* out,
                               void* stream, bool dense) {
   if (!ctx) return MR_ERR_INVALID_ARGUMENT;
-  std::string why;
-  mr_status st = validate_mxfp4(w, why);
-  if (!st) st = mxfp4_mm_limits(w, why);
-  if (st) return fail(ctx, st, why);
+  mr_status st = mx_check_mm(ctx, w);
+  if (st) return st;
   if (dense && w->experts != 0)
     return fail(ctx, MR_ERR_INVALID_ARGUMENT,
                 "mxfp4MM needs a single matrix; use mxfp4GatherMM for an expert stack");
@@ -872,78 +964,16 @@ static mr_status mxfp4_common(mr_ctx* ctx, const void* x, bool x_f32, int64_t T,
   const int E = dense ? 1 : w->experts;
   if (!dense && E > kMaxExperts)
     return fail(ctx, MR_ERR_UNSUPPORTED, "expert stacks larger than 1024 are not built here");
-  const int64_t in = w->in_features;
-  const int seg_cols = pick_seg_cols(Tk);
-  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / seg_cols + 1;
-
-  Bump b{nullptr};
-  for (int pass = 0; pass < 2; ++pass) {
-    b.off = 0;
-    b.take<uint16_t>(T * in * (x_f32 ? 2 : 1));
-    b.take<float>(T * (in / kGroup) * 2);
-    b.take<int>(4);
-    b.take<int4>(max_seg);
-    b.take<int>(Tk);
-    if (pass == 0) {
-      st = ensure_workspace(ctx, b.off);
-      if (st) return st;
-      b.base = reinterpret_cast<char*>(ctx->ws);
-    }
-  }
-  b.off = 0;
-  uint16_t* xperm = b.take<uint16_t>(T * in * (x_f32 ? 2 : 1));
-  float* xscale = b.take<float>(T * (in / kGroup) * 2);
-  int* nseg = b.take<int>(4);
-  int4* segs = b.take<int4>(max_seg);
-  int* cols = b.take<int>(Tk);
+  const size_t act_bytes = mx_act_bytes(T, w->in_features, x_f32);
+  if ((st = ensure_workspace(ctx, act_bytes + mx_plan_bytes(Tk, E)))) return st;
+  char* ws = static_cast<char*>(ctx->ws);
   cudaStream_t s = as_stream(stream);
-
-  TmaMaps tm;
-  memset(&tm, 0, sizeof tm);
-  const int64_t rows = (int64_t)E * w->out_features;
-  if (!tensor_map(ctx, &tm.a_packed, w->packed, rows, in / 8, kTmaRows, 0) ||
-      !tensor_map(ctx, &tm.a_scales, w->scales, rows, in / 32, kTmaRows, 7))
-    return fail(ctx, MR_ERR_CUDA, "tensor map encoding of the MXFP4 operands failed");
-  tm.b_packed = tm.sa_packed = tm.sb_packed = tm.a_packed;
-  tm.b_scales = tm.sa_scales = tm.sb_scales = tm.a_scales;
-
-  PrepMxParams pp{x_f32 ? nullptr : static_cast<const uint16_t*>(x),
-                  x_f32 ? static_cast<const float*>(x) : nullptr, T, in, xperm, xscale};
-  const int64_t chunks = T * (in / 16);
-  const int pgrid = (int)std::min<int64_t>((chunks + 255) / 256, 4 * ctx->sm_count);
-  prep_mx_kernel<<<pgrid, 256, 0, s>>>(pp);
-  if ((st = cuda_check(ctx, cudaGetLastError(), "prep_mx_kernel"))) return st;
-  if (dense) {
-    dense_plan_kernel<<<(int)std::min<int64_t>((T + 255) / 256, 1024), 256, 0, s>>>(
-        (int)T, seg_cols, nseg, segs, cols);
-  } else {
-    PlanParams plan{ids, (int)Tk, E, nseg, segs, cols, ctx->d_error, seg_cols};
-    plan_kernel<<<1, 256, 0, s>>>(plan);
-  }
-  if ((st = cuda_check(ctx, cudaGetLastError(), "plan kernel"))) return st;
-
-  GemvParams g{};
-  g.rows = w->out_features;
-  g.in = in;
-  g.n_routed_segments = nseg;
-  g.segments = segs;
-  g.cols = cols;
-  g.Tk = (int)Tk;
-  g.in_div = kk;
-  g.xperm = xperm;
-  g.xsum = xscale;
-  g.xsum_parts = 2;
-  g.error = ctx->d_error;
-  if (x_f32)
-    g.out_f32 = static_cast<float*>(out);
-  else
-    g.out_bf16 = static_cast<uint16_t*>(out);
-  g.seg_cols = seg_cols;
-  g.rb_count = (int)((g.rows + kTmaRows - 1) / kTmaRows);
-  const int64_t items = max_seg * g.rb_count;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
-  return cuda_check(ctx, launch_tma_mx(g, tm, seg_cols / 8, x_f32 ? 2 : 1, grid, s),
-                    "gemv(mxfp4)");
+  MxAct a;
+  MxPlan pl;
+  if ((st = mx_prep(ctx, x, x_f32, T, w->in_features, ws, &a, s)) ||
+      (st = mx_plan_build(ctx, ids, Tk, E, dense, ws + act_bytes, &pl, s)))
+    return st;
+  return mx_gemv(ctx, pl, a, kk, w, out, s);
 }
 
 namespace mr {

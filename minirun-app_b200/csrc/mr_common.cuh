@@ -297,6 +297,33 @@ struct mr_ctx {
 
 namespace mr {
 constexpr int kMaxCounters = 4096;
+
+// MXFP4 gather pieces shared by the op entry points and composite blocks:
+// a routing plan (columns grouped by expert, built on the device), the
+// prepared activations, and the TMA dequant-GEMV launch over them.
+struct MxPlan {
+  int* nseg;
+  int4* segs;
+  int* cols;
+  int64_t max_seg;
+  int64_t Tk;
+  int seg_cols;
+};
+struct MxAct {
+  uint16_t* xperm;
+  float* xscale;
+  bool split;  // fp32 activations as two f16 terms
+};
+size_t mx_plan_bytes(int64_t Tk, int E);
+size_t mx_act_bytes(int64_t rows, int64_t in, bool split);
+mr_status mx_check_mm(mr_ctx* ctx, const mr_mxfp4_desc* w);
+mr_status mx_plan_build(mr_ctx* ctx, const int32_t* ids, int64_t Tk, int E, bool dense, void* mem,
+                        MxPlan* plan, cudaStream_t s);
+mr_status mx_prep(mr_ctx* ctx, const void* x, bool x_f32, int64_t rows, int64_t in, void* mem,
+                  MxAct* act, cudaStream_t s);
+// out[v][r] for plan column v, reading activation row v / in_div.
+mr_status mx_gemv(mr_ctx* ctx, const MxPlan& plan, const MxAct& act, int in_div,
+                  const mr_mxfp4_desc* w, void* out, cudaStream_t s);
 mr_status fail(mr_ctx* ctx, mr_status st, const std::string& msg);
 mr_status cuda_check(mr_ctx* ctx, cudaError_t err, const char* what);
 mr_status ensure_workspace(mr_ctx* ctx, size_t bytes);

@@ -19,71 +19,84 @@
 namespace mr {
 
 // ------------------------------------------------------ dense projection
-// y[t][r] = sum_k x[t][k] * W[r][k] (fp32 FMA, fixed order: per lane over its
-// k positions, then a warp tree). W is bf16 (WF32 false) or fp32 [out, in];
-// 4 rows per warp, 8 warps (32 rows) per CTA, TT tokens per CTA (grid.y
-// walks token tiles). Requires in % 8 == 0 and 16-byte aligned rows.
-template <bool WF32, int TT>
+// y[t][r] = sum_k x[t][k] * W[r][k] in fp32 FMA, W bf16 (WF32 false) or fp32
+// [out, in]. A CTA of 8 warps covers (8 / KS) row groups of R rows; the KS
+// warps of a row group split K into KS slices of whole 256-element steps.
+// Each lane walks its slice 8 elements at a time, the warp sums its lanes by
+// a shuffle tree, and the slices are added in slice order through shared
+// memory — a fixed order, so results do not depend on the launch shape's
+// token tiling. TT tokens per CTA (grid.y walks token tiles). Requires
+// in % 8 == 0 and 16-byte aligned rows.
+template <bool WF32, int TT, int R>
 __global__ void __launch_bounds__(256) dense_f32_kernel(const float* __restrict__ x, int64_t T,
                                                         const void* __restrict__ w, int64_t out,
-                                                        int64_t in, float* __restrict__ y) {
+                                                        int64_t in, int ks, int64_t kchunk,
+                                                        float* __restrict__ y) {
+  __shared__ float red[8][R][TT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row0 = ((int64_t)blockIdx.x * 8 + warp) * 4;
+  const int groups = 8 / ks;
+  const int rg = warp / ks, sl = warp - rg * ks;
+  const int64_t row0 = ((int64_t)blockIdx.x * groups + rg) * R;
   const int64_t t0 = (int64_t)blockIdx.y * TT;
-  if (row0 >= out) return;
-  float acc[4][TT];
+  const int64_t k0 = sl * kchunk, k1 = min(k0 + kchunk, in);
+  float acc[R][TT];
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+  for (int r = 0; r < R; ++r)
 #pragma unroll
     for (int t = 0; t < TT; ++t) acc[r][t] = 0.0f;
-#pragma unroll 2
-  for (int64_t k = lane * 8; k < in; k += 256) {
-    float wv[4][8];
+  if (row0 < out) {
+#pragma unroll 4
+    for (int64_t k = k0 + lane * 8; k < k1; k += 256) {
+      float wv[R][8];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int64_t row = min(row0 + r, out - 1);  // rows past the end compute row out-1, unused
-      if constexpr (WF32) {
-        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(w) + row * in + k);
-        const float4 a = __ldg(p), b = __ldg(p + 1);
-        wv[r][0] = a.x; wv[r][1] = a.y; wv[r][2] = a.z; wv[r][3] = a.w;
-        wv[r][4] = b.x; wv[r][5] = b.y; wv[r][6] = b.z; wv[r][7] = b.w;
-      } else {
-        const uint4 u = ldg_u128(static_cast<const uint16_t*>(w) + row * in + k);
-        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+      for (int r = 0; r < R; ++r) {
+        const int64_t row = min(row0 + r, out - 1);  // rows past the end recompute row out-1
+        if constexpr (WF32) {
+          const float4* p =
+              reinterpret_cast<const float4*>(static_cast<const float*>(w) + row * in + k);
+          const float4 a = __ldg(p), b = __ldg(p + 1);
+          wv[r][0] = a.x; wv[r][1] = a.y; wv[r][2] = a.z; wv[r][3] = a.w;
+          wv[r][4] = b.x; wv[r][5] = b.y; wv[r][6] = b.z; wv[r][7] = b.w;
+        } else {
+          const uint4 u = ldg_u128(static_cast<const uint16_t*>(w) + row * in + k);
+          const uint32_t q[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          wv[r][2 * i] = __uint_as_float(q[i] << 16);
-          wv[r][2 * i + 1] = __uint_as_float(q[i] & 0xffff0000u);
+          for (int i = 0; i < 4; ++i) {
+            wv[r][2 * i] = __uint_as_float(q[i] << 16);
+            wv[r][2 * i + 1] = __uint_as_float(q[i] & 0xffff0000u);
+          }
         }
       }
-    }
 #pragma unroll
-    for (int t = 0; t < TT; ++t) {
-      const int64_t tok = min(t0 + t, T - 1);
-      const float4* px = reinterpret_cast<const float4*>(x + tok * in + k);
-      const float4 a = __ldg(px), b = __ldg(px + 1);
-      const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      for (int t = 0; t < TT; ++t) {
+        const int64_t tok = min(t0 + t, T - 1);
+        const float4* px = reinterpret_cast<const float4*>(x + tok * in + k);
+        const float4 a = __ldg(px), b = __ldg(px + 1);
+        const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-      for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < R; ++r)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[r][t] = fmaf(wv[r][i], xv[i], acc[r][t]);
+          for (int i = 0; i < 8; ++i) acc[r][t] = fmaf(wv[r][i], xv[i], acc[r][t]);
+      }
     }
   }
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+  for (int r = 0; r < R; ++r)
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
       float v = acc[r][t];
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      acc[r][t] = v;
+      if (lane == 0) red[warp][r][t] = v;
     }
-  if (lane == 0) {
-#pragma unroll
-    for (int t = 0; t < TT; ++t)
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-        if (t0 + t < T && row0 + r < out) y[(t0 + t) * out + row0 + r] = acc[r][t];
+  __syncthreads();
+  for (int i = threadIdx.x; i < groups * R * TT; i += blockDim.x) {
+    const int g = i / (R * TT), r = (i / TT) % R, t = i % TT;
+    const int64_t row = ((int64_t)blockIdx.x * groups + g) * R + r;
+    if (row >= out || t0 + t >= T) continue;
+    float v = 0.0f;
+    for (int q = 0; q < ks; ++q) v += red[g * ks + q][r][t];
+    y[(t0 + t) * out + row] = v;
   }
 }
 
@@ -107,22 +120,32 @@ __global__ void situ_kernel(const float* __restrict__ g, const float* __restrict
 }
 
 // ------------------------------------------- weighted slot sum + RMSNorm
-// One CTA per token: rs[j] = sum_s w[t,s] * eo[t*k+s][j] (slot order), then,
+// One CTA of 1024 threads per token: rs[j] = sum_s w[t,s] * eo[t*k+s][j]
+// (slots added in order; eight slot loads issued before their adds), then,
 // with a norm weight, out[j] = weight[j] * (rs[j] * rsqrt(mean(rs^2) + eps))
-// (mean of squares summed per thread over j = tid, tid + 256, ..., then a
-// fixed tree). Dynamic shared memory: L floats.
+// (squares summed per thread over j = tid, tid + 1024, ..., then a fixed
+// tree). Dynamic shared memory: L floats.
 template <bool WF32>
-__global__ void __launch_bounds__(256) slot_sum_norm_kernel(const float* __restrict__ eo,
-                                                            const float* __restrict__ wts, int k,
-                                                            int64_t L, const void* norm_w,
-                                                            float eps, float* __restrict__ out) {
+__global__ void __launch_bounds__(1024) slot_sum_norm_kernel(const float* __restrict__ eo,
+                                                             const float* __restrict__ wts, int k,
+                                                             int64_t L, const void* norm_w,
+                                                             float eps, float* __restrict__ out) {
   extern __shared__ float rs[];
-  __shared__ float red[256];
+  __shared__ float red[1024];
   const int64_t t = blockIdx.x;
+  const float* base = eo + t * k * L;
   float sq = 0.0f;
   for (int64_t j = threadIdx.x; j < L; j += blockDim.x) {
     float s = 0.0f;
-    for (int sl = 0; sl < k; ++sl) s += __ldg(eo + (t * k + sl) * L + j) * __ldg(wts + t * k + sl);
+    int sl = 0;
+    for (; sl + 8 <= k; sl += 8) {
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[q] = __ldg(base + (sl + q) * L + j);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) s += v[q] * __ldg(wts + t * k + sl + q);
+    }
+    for (; sl < k; ++sl) s += __ldg(base + sl * L + j) * __ldg(wts + t * k + sl);
     rs[j] = s;
     sq = fmaf(s, s, sq);
   }
@@ -132,7 +155,7 @@ __global__ void __launch_bounds__(256) slot_sum_norm_kernel(const float* __restr
   }
   red[threadIdx.x] = sq;
   __syncthreads();
-  for (int h = 128; h > 0; h >>= 1) {
+  for (int h = 512; h > 0; h >>= 1) {
     if ((int)threadIdx.x < h) red[threadIdx.x] += red[threadIdx.x + h];
     __syncthreads();
   }
@@ -152,17 +175,34 @@ __global__ void add_f32_kernel(const float* __restrict__ a, float* __restrict__ 
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+template <bool WF32, int TT, int R>
+static void launch_dense_tt(const float* x, int64_t T, const void* w, int64_t out, int64_t in,
+                            float* y, int sms, cudaStream_t s) {
+  // K slices: enough warps for about 24 per SM at one token tile of 2-row
+  // groups, at most 8 (one CTA's warps). It depends on the matrix alone, so
+  // a token's sum runs in the same order whatever the batch.
+  const int64_t ttiles = (T + TT - 1) / TT;
+  const int64_t want = (int64_t)sms * 24;
+  int ks = 1;
+  while (ks < 8 && (out + 1) / 2 * ks < want && in / (ks * 2) >= 256) ks *= 2;
+  const int64_t steps = (in + 255) / 256;
+  const int64_t kchunk = (steps + ks - 1) / ks * 256;
+  const int64_t per_cta = (8 / ks) * R;
+  const dim3 grid((unsigned)((out + per_cta - 1) / per_cta), (unsigned)ttiles);
+  dense_f32_kernel<WF32, TT, R><<<grid, 256, 0, s>>>(x, T, w, out, in, ks, kchunk, y);
+}
+
 template <bool WF32>
 static cudaError_t launch_dense(const float* x, int64_t T, const void* w, int64_t out, int64_t in,
-                                float* y, cudaStream_t s) {
-  const int tt = T >= 8 ? 8 : T >= 4 ? 4 : T >= 2 ? 2 : 1;
-  const dim3 grid((unsigned)((out + 31) / 32), (unsigned)((T + tt - 1) / tt));
-  switch (tt) {
-    case 8: dense_f32_kernel<WF32, 8><<<grid, 256, 0, s>>>(x, T, w, out, in, y); break;
-    case 4: dense_f32_kernel<WF32, 4><<<grid, 256, 0, s>>>(x, T, w, out, in, y); break;
-    case 2: dense_f32_kernel<WF32, 2><<<grid, 256, 0, s>>>(x, T, w, out, in, y); break;
-    default: dense_f32_kernel<WF32, 1><<<grid, 256, 0, s>>>(x, T, w, out, in, y); break;
-  }
+                                float* y, int sms, cudaStream_t s) {
+  if (T >= 8)
+    launch_dense_tt<WF32, 8, 4>(x, T, w, out, in, y, sms, s);
+  else if (T >= 4)
+    launch_dense_tt<WF32, 4, 2>(x, T, w, out, in, y, sms, s);
+  else if (T >= 2)
+    launch_dense_tt<WF32, 2, 2>(x, T, w, out, in, y, sms, s);
+  else
+    launch_dense_tt<WF32, 1, 2>(x, T, w, out, in, y, sms, s);
   return cudaGetLastError();
 }
 
@@ -186,8 +226,9 @@ static mr_status dense_checks(const void* w, mr_dtype dt, int64_t out, int64_t i
 static mr_status dense_run(mr_ctx* ctx, const float* x, int64_t T, const void* w, mr_dtype dt,
                            int64_t out, int64_t in, float* y, cudaStream_t s) {
   if (!al16(x)) return fail(ctx, MR_ERR_UNSUPPORTED, "x must be 16-byte aligned");
-  const cudaError_t e = dt == MR_DTYPE_F32 ? launch_dense<true>(x, T, w, out, in, y, s)
-                                           : launch_dense<false>(x, T, w, out, in, y, s);
+  const cudaError_t e = dt == MR_DTYPE_F32
+                            ? launch_dense<true>(x, T, w, out, in, y, ctx->sm_count, s)
+                            : launch_dense<false>(x, T, w, out, in, y, ctx->sm_count, s);
   return cuda_check(ctx, e, "dense_f32_kernel");
 }
 
@@ -377,7 +418,10 @@ mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int
   const size_t o_logits = take(T * E), o_ids = take(Tk), o_w = take(Tk), o_lat = take(T * Lt),
                o_g = take(Tk * I), o_u = take(Tk * I), o_act = take(Tk * I),
                o_eo = take(Tk * Lt), o_rs = take(T * Lt), o_ru = take(T * H),
-               o_sg = take(T * S), o_su = take(T * S), o_sa = take(T * S);
+               o_sg = take(T * S), o_su = take(T * S), o_sa = take(T * S),
+               o_plan = take((int64_t)mx_plan_bytes(Tk, (int)E) / 4),
+               o_a1 = take((int64_t)mx_act_bytes(T, Lt, true) / 4),
+               o_a2 = take((int64_t)mx_act_bytes(Tk, I, true) / 4);
   if ((st = ensure_aux(ctx, off))) return st;
   char* base = static_cast<char*>(ctx->aux);
   auto F = [&](size_t o) { return reinterpret_cast<float*>(base + o); };
@@ -388,16 +432,27 @@ mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int
   if ((st = dense_run(ctx, x, T, L->gate_weight, L->gate_dtype, E, H, F(o_logits), s))) return st;
   if ((st = mr_router_select_logits(ctx, F(o_logits), T, &L->router, ids, wts, nullptr, s)))
     return st;
-  // 2. routed: latent down projection, gate/up gathers, situ, down gather
+  // 2. routed: latent down projection, gate/up gathers, situ, down gather.
+  // One plan serves all three gathers (columns are the (token, slot) pairs
+  // grouped by expert); w1 and w3 share one prepared latent.
+  if ((st = mx_check_mm(ctx, &L->w1)) || (st = mx_check_mm(ctx, &L->w3)) ||
+      (st = mx_check_mm(ctx, &L->w2)))
+    return st;
+  MxPlan pl;
+  MxAct a1, a2;
+  if ((st = mx_plan_build(ctx, ids, Tk, (int)E, false, base + o_plan, &pl, s))) return st;
   if ((st = project(ctx, &L->routed_down, x, T, F(o_lat), s))) return st;
-  if ((st = mr_mxfp4_gather_mm_f32(ctx, F(o_lat), T, ids, (int32_t)k, &L->w1, F(o_g), s)) ||
-      (st = mr_mxfp4_gather_mm_f32(ctx, F(o_lat), T, ids, (int32_t)k, &L->w3, F(o_u), s)))
+  if ((st = mx_prep(ctx, F(o_lat), true, T, Lt, base + o_a1, &a1, s)) ||
+      (st = mx_gemv(ctx, pl, a1, (int)k, &L->w1, F(o_g), s)) ||
+      (st = mx_gemv(ctx, pl, a1, (int)k, &L->w3, F(o_u), s)))
     return st;
   if ((st = situ_run(ctx, F(o_g), F(o_u), I, Tk, I, L->situ_beta, L->situ_linear_beta,
                      F(o_act), s)))
     return st;
-  // each (token, slot) row is its own column with one expert: ids as [Tk, 1]
-  if ((st = mr_mxfp4_gather_mm_f32(ctx, F(o_act), Tk, ids, 1, &L->w2, F(o_eo), s))) return st;
+  // each (token, slot) row is its own column: activation row v, in_div 1
+  if ((st = mx_prep(ctx, F(o_act), true, Tk, I, base + o_a2, &a2, s)) ||
+      (st = mx_gemv(ctx, pl, a2, 1, &L->w2, F(o_eo), s)))
+    return st;
   // 3. weighted slot sum in fp32, latent RMSNorm, up projection
   const size_t smem = (size_t)Lt * 4;
   if (smem > 200 * 1024) return fail(ctx, MR_ERR_UNSUPPORTED, "latent width too large");
@@ -405,13 +460,13 @@ mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(slot_sum_norm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem);
-    slot_sum_norm_kernel<true><<<(unsigned)T, 256, smem, s>>>(F(o_eo), wts, (int)k, Lt,
+    slot_sum_norm_kernel<true><<<(unsigned)T, 1024, smem, s>>>(F(o_eo), wts, (int)k, Lt,
                                                               L->routed_norm, L->rms_eps, F(o_rs));
   } else {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(slot_sum_norm_kernel<false>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    slot_sum_norm_kernel<false><<<(unsigned)T, 256, smem, s>>>(F(o_eo), wts, (int)k, Lt,
+    slot_sum_norm_kernel<false><<<(unsigned)T, 1024, smem, s>>>(F(o_eo), wts, (int)k, Lt,
                                                                L->routed_norm, L->rms_eps, F(o_rs));
   }
   if ((st = cuda_check(ctx, cudaGetLastError(), "slot_sum_norm_kernel"))) return st;
