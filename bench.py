@@ -18,9 +18,11 @@ launching stream; `cpu_baseline` times the CPU oracle on the host cores.
 Under torchrun (N > 1) the layer is expert-parallel: rank r holds routed
 experts [r*E/N, (r+1)*E/N) of every layer and T tokens of an N*T-token
 global batch (weak scaling: T per GPU fixed); one step = NCCL all-gather of
-the tokens, router over all of them, the rank's experts, NCCL reduce-scatter
-of the per-token sums, shared expert and combine. The time is the max over
-ranks; `value` counts all N*T tokens.
+the tokens, router over all of them, the rank's experts — whose down GEMV
+stores each routed partial straight into the token's home GPU over NVLink —
+then the shared expert and the slot-ordered combine on the home GPU
+(`--ep-nccl`: per-token sums and an NCCL reduce-scatter instead). The time
+is the max over ranks; `value` counts all N*T tokens.
 """
 from __future__ import annotations
 
@@ -63,6 +65,14 @@ def parse():
                    help="dequant-GEMV implementation (mr_ctx_set_kernel_path)")
     p.add_argument("--prefill-tokens", type=int, default=4096,
                    help="config-3 prefill batch measured beside the decode line (0 = skip)")
+    p.add_argument("--k3-tokens", default="1,16",
+                   help="token counts of the K3 latent-MoE layer line ('' = skip)")
+    p.add_argument("--k3-experts", type=int, default=896,
+                   help="routed experts of the K3 layer (flagship: 896)")
+    p.add_argument("--ep-nccl", action="store_true",
+                   help="expert parallel: NCCL reduce-scatter instead of the fused peer stores")
+    p.add_argument("--k3-only", action="store_true",
+                   help="measure only the K3 latent-MoE layer (profiling driver)")
     return p.parse_args()
 
 
@@ -189,6 +199,8 @@ def run_ours(args, world, rank, local):
     ctx = M.Context.get(local)
     ctx.set_kernel_path(args.kernel_path)
     group = M.ExpertGroup(local, rank, world) if ep else None
+    if group is not None:
+        group.set_fused(not args.ep_nccl)
     torch.cuda.synchronize()
 
     def step(lay, x, out, ids=None):
@@ -294,6 +306,9 @@ def run_ours(args, world, rank, local):
     prefill = None
     if not ep and args.prefill_tokens > 0:
         prefill = prefill_run(args, S, M, torch, ctx, local, dev)
+    k3 = None
+    if not ep and args.k3_tokens:
+        k3 = k3_run(args, M, torch, dev, hbm)
 
     e2e = e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local,
                   group if ep else None)
@@ -327,7 +342,10 @@ def run_ours(args, world, rank, local):
                   "(>= 227 MB each)",
             "parallelism": "single GPU" if world == 1 else
                            f"ep{world}: {spec.experts // world} routed experts per GPU, NCCL "
-                           "all-gather of tokens + reduce-scatter of expert outputs",
+                           "all-gather of tokens, " +
+                           ("NCCL reduce-scatter of per-token sums" if args.ep_nccl else
+                            "down GEMV storing routed partials into their home GPU over "
+                            "NVLink (fused), slot-ordered combine there"),
             "distinct_experts_avg": sum(us) / len(us),
             "layer_bytes_per_step": avg_bytes,
             "layer_gbs": avg_bytes / (ms_step / 1e3) / 1e9,
@@ -335,6 +353,7 @@ def run_ours(args, world, rank, local):
             "kernels": kern,
             "sweep": sweep,
             "prefill": prefill,
+            "k3_latent_moe": k3,
         },
         "roofline": {
             "bound": "hbm",
@@ -411,6 +430,64 @@ def prefill_run(args, S, M, torch, ctx, local, dev):
                      "frac": gu_tf / peak, "algorithmic_flops_per_launch": gu_flops},
         "down_tflops": dn_flops / (dn_ms / 1e3) / 1e12,
     }
+
+
+def k3_run(args, M, torch, dev, hbm):
+    """K3's latent MoE layer (K3MoE.forward, MoE.swift:219-272) at the flagship
+    geometry (hidden 7168, latent 3584, intermediate 3072, top-16, MXFP4 routed
+    experts, bf16 dense latent projections and a 6144-wide bf16 shared expert),
+    fp32 activations, seeded random weights generated on the GPU. One step =
+    one layer forward over T tokens; L2 is flushed (a 256 MB write) between
+    steps, outside the timed events."""
+    E, H, Lt, I, S, k = args.k3_experts, 7168, 3584, 3072, 6144, 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(20260801)
+
+    def mx(e, o, i):
+        shape = (e, o) if e else (o,)
+        p = torch.randint(-2**31, 2**31 - 1, shape + (i // 8,), dtype=torch.int32, device=dev,
+                          generator=g)
+        sc = torch.randint(118, 122, shape + (i // 32,), dtype=torch.uint8, device=dev,
+                           generator=g)
+        return M.MXFP4Weights(p, sc)
+
+    def dense(o, i):
+        return (torch.randn(o, i, device=dev, generator=g) / i ** 0.5).to(torch.bfloat16)
+
+    blk = M.K3MoE(dense(E, H), torch.zeros(E, device=dev), M.K3Projection(dense(Lt, H)),
+                  M.K3Projection(dense(H, Lt)), torch.ones(Lt, device=dev), mx(E, I, Lt),
+                  mx(E, I, Lt), mx(E, Lt, I),
+                  (M.K3Projection(dense(S, H)), M.K3Projection(dense(S, H)),
+                   M.K3Projection(dense(H, S))), k)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    dense_bytes = (E * H + 2 * Lt * H + 3 * S * H) * 2
+    out = {}
+    for T in [int(t) for t in args.k3_tokens.split(",") if t]:
+        x = torch.randn(T, H, device=dev, generator=g)
+        for _ in range(max(3, args.warmup)):
+            blk.forward(x)
+        times, us = [], []
+        for _ in range(args.steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            _, sel = blk.forward(x)
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+            us.append(len(torch.unique(sel.ids)))
+        ms = sum(times) / len(times)
+        U = sum(us) / len(us)
+        byt = U * 3 * I * Lt * (0.5 + 1 / 32) + dense_bytes
+        out[str(T)] = {"ms_per_layer": ms, "tokens_per_s": T / (ms / 1e3),
+                       "distinct_experts_avg": U, "layer_bytes": byt,
+                       "layer_gbs": byt / (ms / 1e3) / 1e9,
+                       "layer_frac_of_hbm": byt / (ms / 1e3) / 1e9 / hbm}
+    return {"workload": f"K3 latent MoE layer: {E} MXFP4 experts, hidden {H}, latent {Lt}, "
+                        f"inter {I}, top-{k}, bf16 dense projections, fp32 activations",
+            "l2": "flushed between steps (256 MB write, outside the timed events)",
+            "by_tokens": out}
 
 
 def e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local, group=None):
@@ -559,6 +636,13 @@ def main():
     world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, world, rank, local)
+    elif args.k3_only:
+        import torch
+        import minirun_moe as M
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        hbm, _ = peaks()
+        print(json.dumps({"k3_latent_moe": k3_run(args, M, torch, dev, hbm)}), flush=True)
     else:
         run_ours(args, world, rank, local)
 

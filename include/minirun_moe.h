@@ -440,8 +440,16 @@ mr_status mr_moe_layer_forward_host(mr_ctx* ctx, const mr_moe_layer* layer,
  * Sources/ModelAdapters/Operators/MoE.swift:22-51), which has no multi-GPU
  * form. One forward = NCCL all-gather of the ranks' tokens, the router over
  * all of them (identical on every rank), this rank's experts' GEMVs over the
- * pairs routed to them, per-token partial sums, NCCL reduce-scatter back to
- * the tokens' home ranks, then the shared expert and the combine there.
+ * pairs routed to them, then the way back to the tokens' home ranks:
+ *   - fused (default, TMA GEMV layouts): the down GEMV's epilogue stores each
+ *     routed (token, slot) partial straight into the home rank's receive
+ *     buffer over NVLink (CUDA IPC peer mapping), and its last CTA publishes
+ *     a step epoch to every rank (system-scope release); the home rank runs
+ *     its shared expert, waits for every rank's epoch (bounded; a timeout sets
+ *     MR_DEVERR_TIMEOUT) and combines in slot order — the one-GPU arithmetic,
+ *     so results equal mr_moe_layer_forward bit for bit;
+ *   - NCCL (mr_ep_set_fused(ep, 0), or layouts the TMA GEMV cannot stream):
+ *     per-token partial sums of the local slots and an NCCL reduce-scatter.
  * NCCL (libnccl.so.2) is loaded when the first group is created. */
 typedef struct mr_ep mr_ep;
 #define MR_EP_ID_BYTES 128
@@ -452,12 +460,16 @@ mr_status mr_ep_unique_id(void* id);
  * until every rank has joined. */
 mr_status mr_ep_create(mr_ctx* ctx, const void* id, int rank, int world, mr_ep** out);
 mr_status mr_ep_destroy(mr_ep* ep);
+/* 1 (default): fused down GEMV + peer stores; 0: NCCL reduce-scatter. Every
+ * rank of the group must choose the same. */
+mr_status mr_ep_set_fused(mr_ep* ep, int fused);
 /* Expert-parallel mr_moe_layer_forward. layer->gate/up/down are this rank's
  * E/world experts (experts == router.experts / world, stacks only);
  * everything else as mr_moe_layer_forward. Every rank passes the same
  * `tokens` T; out [T, H] and ids_out [T, k] (optional) are this rank's
  * tokens. Results equal mr_moe_layer_forward over all ranks' tokens on one
- * GPU up to fp32 summation order of the routed slots. */
+ * GPU: bit for bit on the fused path, up to the fp32 order of the routed-slot
+ * sums on the NCCL path. */
 mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* layer,
                                   const uint16_t* x, int64_t tokens, uint16_t* out,
                                   int32_t* ids_out, void* stream);

@@ -1295,6 +1295,9 @@ struct ExpertsRun {
   bool pf;                // tcgen05 prefill GEMM (maps in um1 / um2)
   const UmMaps* um1;
   const UmMaps* um2;
+  // expert parallel, fused: the down GEMV stores routed partials into their
+  // home ranks' buffers (GemvParams::peer_*); nullptr elsewhere
+  const GemvParams* peer;
 };
 
 static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRun& r,
@@ -1405,6 +1408,16 @@ static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRu
                                      (!has_shared || tma_layout_ok(I, &L->shared_down, false)));
   d.um_dense = 0;
   d.sh_row0 = (int)r.Tk;
+  if (r.peer) {
+    if (!tma2) return fail(ctx, MR_ERR_UNSUPPORTED, "fused expert parallel needs the TMA GEMV");
+    d.peer_part = r.peer->peer_part;
+    d.peer_cols = r.peer->peer_cols;
+    d.peer_flags = r.peer->peer_flags;
+    d.peer_done = r.peer->peer_done;
+    d.peer_n = r.peer->peer_n;
+    d.peer_rank = r.peer->peer_rank;
+    d.peer_epoch = r.peer->peer_epoch;
+  }
   ProfScope ps(ctx, MR_KERNEL_DOWN_COMBINE, s);
   const MapSpec maps[4] = {{&L->down, E}, {nullptr, 0},
                            {has_shared ? &L->shared_down : nullptr, 1}, {nullptr, 0}};
@@ -2025,6 +2038,54 @@ __global__ void ep_combine_kernel(const float* __restrict__ y, const float* __re
   }
 }
 
+// Fused expert parallel, home rank: wait (bounded) until every rank has
+// published this step's epoch — all routed partials of this rank's tokens
+// have then landed in `part` — and run the one-GPU combine over them: the
+// same slot order, so the result equals the one-GPU layer's bit for bit.
+__global__ void ep_wait_combine_kernel(const float* __restrict__ part,
+                                       const float* __restrict__ weights, int T, int k,
+                                       int64_t H, int weight_after_down, int has_shared,
+                                       const unsigned* flags, int world, unsigned epoch,
+                                       unsigned* error, uint16_t* __restrict__ out) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    for (int j = 0; j < world && ok; ++j) {
+      uint32_t i = 0;
+      while (ld_acquire_sys(flags + j) < epoch) {
+        if (++i >= kSpinLimit) {
+          atomicOr(error, MR_DEVERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+  }
+  __syncthreads();
+  const int64_t n = (int64_t)T * H;
+  const int Tk = T * k;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / H);
+    const int64_t row = i - (int64_t)t * H;
+    float s = 0.0f;
+    if (!weight_after_down) {
+      for (int j = 0; j < k; ++j) s += part[(int64_t)(t * k + j) * H + row];
+      s = bf16_round(s);
+    } else {
+      for (int j = 0; j < k; ++j)
+        s += part[(int64_t)(t * k + j) * H + row] * __ldg(weights + t * k + j);
+    }
+    if (has_shared) {
+      const float hi = part[(int64_t)(Tk + t) * H + row];
+      const float lo = part[(int64_t)(Tk + T + t) * H + row];
+      s = s + (hi + lo);
+    }
+    out[i] = f32_to_bf16_bits(ok ? s : 0.0f);
+  }
+}
+
 }  // namespace
 
 struct mr_ep {
@@ -2032,6 +2093,16 @@ struct mr_ep {
   int rank = 0;
   int world = 1;
   int device = 0;
+  // fused path: this rank's receive buffer (flags | partials), mapped by
+  // every rank through CUDA IPC; device tables of every rank's pointers
+  bool fused = true;
+  void* buf = nullptr;       // [256 B of flags][partials]
+  size_t buf_bytes = 0;
+  std::vector<void*> opened;  // peers' buffers opened here
+  float** d_parts = nullptr;  // [world]
+  unsigned** d_flags = nullptr;
+  unsigned* d_done = nullptr;
+  unsigned epoch = 0;
 };
 
 extern "C" {
@@ -2068,13 +2139,115 @@ mr_status mr_ep_create(mr_ctx* ctx, const void* id, int rank, int world, mr_ep**
   return MR_OK;
 }
 
+mr_status mr_ep_set_fused(mr_ep* ep, int fused) {
+  if (!ep) return MR_ERR_INVALID_ARGUMENT;
+  ep->fused = fused != 0;
+  return MR_OK;
+}
+
 mr_status mr_ep_destroy(mr_ep* ep) {
   if (!ep) return MR_OK;
   mr_status st = MR_OK;
+  cudaSetDevice(ep->device);
+  cudaDeviceSynchronize();
+  for (void* p : ep->opened) cudaIpcCloseMemHandle(p);
+  if (ep->buf) cudaFree(ep->buf);
+  if (ep->d_parts) cudaFree(ep->d_parts);
   if (ep->comm && nccl_api().comm_destroy(ep->comm) != ncclSuccess) st = MR_ERR_NCCL;
   delete ep;
   return st;
 }
+
+}  // extern "C"
+
+// Fused path: (re)creates this rank's receive buffer when `need` bytes do not
+// fit and maps every rank's through CUDA IPC. Collective: every rank calls it
+// in the same forward (the shapes are the same on every rank), so the NCCL
+// steps below line up. Old buffers are released only after a barrier, once no
+// rank can still be writing into them.
+static mr_status ep_peer_setup(mr_ctx* ctx, mr_ep* ep, size_t need, cudaStream_t s) {
+  if (ep->buf && ep->buf_bytes >= need) return MR_OK;
+  const NcclApi& api = nccl_api();
+  const int W = ep->world;
+  mr_status st;
+  void* tmp = nullptr;
+  if ((st = cuda_check(ctx, cudaMalloc(&tmp, (size_t)(W + 1) * sizeof(cudaIpcMemHandle_t)),
+                       "cudaMalloc(ipc handles)")))
+    return st;
+  char* send = static_cast<char*>(tmp);
+  char* recv = send + sizeof(cudaIpcMemHandle_t);
+  auto cleanup = [&] { cudaFree(tmp); };
+  // barrier: every rank has finished its previous steps (and writes into the old buffers)
+  if ((st = cuda_check(ctx, cudaStreamSynchronize(s), "sync")) ||
+      (st = nccl_check(ctx, api.all_gather(send, recv, sizeof(cudaIpcMemHandle_t), ncclInt8,
+                                           ep->comm, s),
+                       "ncclAllGather(barrier)")) ||
+      (st = cuda_check(ctx, cudaStreamSynchronize(s), "sync"))) {
+    cleanup();
+    return st;
+  }
+  for (void* p : ep->opened) cudaIpcCloseMemHandle(p);
+  ep->opened.clear();
+  if (ep->buf) cudaFree(ep->buf);
+  if (ep->d_parts) cudaFree(ep->d_parts);
+  ep->buf = nullptr;
+  ep->d_parts = nullptr;
+  ep->buf_bytes = 0;
+  const size_t bytes = need + need / 4 + (1 << 20);
+  cudaIpcMemHandle_t mine;
+  if ((st = cuda_check(ctx, cudaMalloc(&ep->buf, bytes), "cudaMalloc(peer buffer)")) ||
+      (st = cuda_check(ctx, cudaMemset(ep->buf, 0, bytes), "clear peer buffer")) ||
+      (st = cuda_check(ctx, cudaIpcGetMemHandle(&mine, ep->buf), "cudaIpcGetMemHandle")) ||
+      (st = cuda_check(ctx, cudaMemcpy(send, &mine, sizeof mine, cudaMemcpyHostToDevice),
+                       "stage ipc handle")) ||
+      (st = nccl_check(ctx, api.all_gather(send, recv, sizeof(cudaIpcMemHandle_t), ncclInt8,
+                                           ep->comm, s),
+                       "ncclAllGather(ipc handles)")) ||
+      (st = cuda_check(ctx, cudaStreamSynchronize(s), "sync"))) {
+    cleanup();
+    return st;
+  }
+  std::vector<cudaIpcMemHandle_t> all(W);
+  st = cuda_check(ctx, cudaMemcpy(all.data(), recv, W * sizeof(cudaIpcMemHandle_t),
+                                  cudaMemcpyDeviceToHost),
+                  "read ipc handles");
+  cleanup();
+  if (st) return st;
+  std::vector<void*> bases(W);
+  for (int j = 0; j < W; ++j) {
+    if (j == ep->rank) {
+      bases[j] = ep->buf;
+      continue;
+    }
+    void* p = nullptr;
+    if ((st = cuda_check(ctx, cudaIpcOpenMemHandle(&p, all[j], cudaIpcMemLazyEnablePeerAccess),
+                         "cudaIpcOpenMemHandle")))
+      return st;
+    ep->opened.push_back(p);
+    bases[j] = p;
+  }
+  // device tables: part pointers, flag pointers, the done counter
+  std::vector<uint64_t> tab(2 * W + 1, 0);
+  for (int j = 0; j < W; ++j) {
+    tab[j] = reinterpret_cast<uint64_t>(static_cast<char*>(bases[j]) + 256);
+    tab[W + j] = reinterpret_cast<uint64_t>(bases[j]);
+  }
+  void* d = nullptr;
+  if ((st = cuda_check(ctx, cudaMalloc(&d, tab.size() * 8), "cudaMalloc(peer tables)"))) return st;
+  if ((st = cuda_check(ctx, cudaMemcpy(d, tab.data(), tab.size() * 8, cudaMemcpyHostToDevice),
+                       "upload peer tables"))) {
+    cudaFree(d);
+    return st;
+  }
+  ep->d_parts = static_cast<float**>(d);
+  ep->d_flags = reinterpret_cast<unsigned**>(static_cast<uint64_t*>(d) + W);
+  ep->d_done = reinterpret_cast<unsigned*>(static_cast<uint64_t*>(d) + 2 * W);
+  ep->buf_bytes = bytes;
+  ep->epoch = 0;  // flags were cleared with the buffers, on every rank
+  return MR_OK;
+}
+
+extern "C" {
 
 mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
                                   const uint16_t* x, int64_t T, uint16_t* out, int32_t* ids_out,
@@ -2167,47 +2340,96 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
   r.h = h;
   r.hsum = hsum;
   r.part2 = part2;
-  if ((st = run_experts(ctx, L, r, s))) return st;
   const int wad = L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0;
-  {
-    const int64_t n = NT * H;
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
-    ep_partial_kernel<<<grid, 256, 0, s>>>(part2, ids, wts, (int)NT, k, H, base, El, wad, ypart);
-    if ((st = cuda_check(ctx, cudaGetLastError(), "ep_partial_kernel"))) return st;
-  }
-  // each token's sum over all ranks, back on its home rank
-  if ((st = nccl_check(ctx,
-                       api.reduce_scatter(ypart, yred, (size_t)(T * H), ncclFloat32, ncclSum,
-                                          ep->comm, s),
-                       "ncclReduceScatter")))
-    return st;
-  // shared expert over this rank's own tokens
-  if (has_shared) {
-    if ((st = cuda_check(ctx, cudaMemsetAsync(zero, 0, 4 * sizeof(int), s), "clear count")))
-      return st;
-    ExpertsRun sh{};
-    sh.xperm = xperm + (int64_t)rank * T * H;
-    sh.xsum = xsum + (int64_t)rank * T * (H / kGroup);
-    sh.tokens = T;
-    sh.shared_tokens = T;
-    sh.Tk = 0;
-    sh.k = k;
-    sh.nseg = zero;
-    sh.segs = segs;
-    sh.cols = cols;
-    sh.max_seg = 0;
-    sh.seg_cols = seg_cols;
-    sh.wts = wts;
-    sh.h = hs;
-    sh.hsum = hss;
-    sh.part2 = psh;
-    if ((st = run_experts(ctx, L, sh, s))) return st;
-  }
-  {
+  const bool fused = ep->fused && W > 1 &&
+                     use_tma(ctx, tma_layout_ok(I, &L->down, false) &&
+                                      (!has_shared || tma_layout_ok(I, &L->shared_down, false)));
+  if (fused) {
+    // routed partials straight into their home ranks' buffers over NVLink,
+    // then the one-GPU combine on each home rank
+    const int64_t Tk = T * k, rows = Tk + (has_shared ? 2 * T : 0);
+    if ((st = ep_peer_setup(ctx, ep, 256 + (size_t)rows * H * sizeof(float), s))) return st;
+    ++ep->epoch;
+    GemvParams peer{};
+    peer.peer_part = ep->d_parts;
+    peer.peer_cols = (int)Tk;
+    peer.peer_flags = ep->d_flags;
+    peer.peer_done = ep->d_done;
+    peer.peer_n = W;
+    peer.peer_rank = rank;
+    peer.peer_epoch = ep->epoch;
+    r.peer = &peer;
+    if ((st = run_experts(ctx, L, r, s))) return st;
+    float* mine = reinterpret_cast<float*>(static_cast<char*>(ep->buf) + 256);
+    if (has_shared) {
+      if ((st = cuda_check(ctx, cudaMemsetAsync(zero, 0, 4 * sizeof(int), s), "clear count")))
+        return st;
+      ExpertsRun sh{};
+      sh.xperm = xperm + (int64_t)rank * T * H;
+      sh.xsum = xsum + (int64_t)rank * T * (H / kGroup);
+      sh.tokens = T;
+      sh.shared_tokens = T;
+      sh.Tk = 0;
+      sh.k = k;
+      sh.nseg = zero;
+      sh.segs = segs;
+      sh.cols = cols;
+      sh.max_seg = 0;
+      sh.seg_cols = seg_cols;
+      sh.wts = wts;
+      sh.h = hs;
+      sh.hsum = hss;
+      sh.part2 = mine + Tk * H;  // rows Tk .. Tk + 2T of the home buffer
+      if ((st = run_experts(ctx, L, sh, s))) return st;
+    }
     const int64_t n = T * H;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
-    ep_combine_kernel<<<grid, 256, 0, s>>>(yred, psh, (int)T, H, wad, has_shared ? 1 : 0, out);
-    if ((st = cuda_check(ctx, cudaGetLastError(), "ep_combine_kernel"))) return st;
+    ep_wait_combine_kernel<<<grid, 256, 0, s>>>(
+        mine, wts + (int64_t)rank * Tk, (int)T, k, H, wad, has_shared ? 1 : 0,
+        static_cast<const unsigned*>(ep->buf), W, ep->epoch, ctx->d_error, out);
+    if ((st = cuda_check(ctx, cudaGetLastError(), "ep_wait_combine_kernel"))) return st;
+  } else {  // NCCL: per-token local sums, reduce-scatter to the home ranks
+    if ((st = run_experts(ctx, L, r, s))) return st;
+    {
+      const int64_t n = NT * H;
+      const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
+      ep_partial_kernel<<<grid, 256, 0, s>>>(part2, ids, wts, (int)NT, k, H, base, El, wad, ypart);
+      if ((st = cuda_check(ctx, cudaGetLastError(), "ep_partial_kernel"))) return st;
+    }
+    // each token's sum over all ranks, back on its home rank
+    if ((st = nccl_check(ctx,
+                         api.reduce_scatter(ypart, yred, (size_t)(T * H), ncclFloat32, ncclSum,
+                                            ep->comm, s),
+                         "ncclReduceScatter")))
+      return st;
+    // shared expert over this rank's own tokens
+    if (has_shared) {
+      if ((st = cuda_check(ctx, cudaMemsetAsync(zero, 0, 4 * sizeof(int), s), "clear count")))
+        return st;
+      ExpertsRun sh{};
+      sh.xperm = xperm + (int64_t)rank * T * H;
+      sh.xsum = xsum + (int64_t)rank * T * (H / kGroup);
+      sh.tokens = T;
+      sh.shared_tokens = T;
+      sh.Tk = 0;
+      sh.k = k;
+      sh.nseg = zero;
+      sh.segs = segs;
+      sh.cols = cols;
+      sh.max_seg = 0;
+      sh.seg_cols = seg_cols;
+      sh.wts = wts;
+      sh.h = hs;
+      sh.hsum = hss;
+      sh.part2 = psh;
+      if ((st = run_experts(ctx, L, sh, s))) return st;
+    }
+    {
+      const int64_t n = T * H;
+      const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
+      ep_combine_kernel<<<grid, 256, 0, s>>>(yred, psh, (int)T, H, wad, has_shared ? 1 : 0, out);
+      if ((st = cuda_check(ctx, cudaGetLastError(), "ep_combine_kernel"))) return st;
+    }
   }
   if (ids_out)
     st = cuda_check(ctx,

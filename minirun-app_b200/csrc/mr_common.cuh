@@ -217,6 +217,17 @@ MR_DEVICE void named_bar(int id, int count) {
 // reports MR_DEVERR_TIMEOUT and returns.
 constexpr uint32_t kSpinLimit = 1u << 22;
 
+// System-scope release store / acquire load of a flag another GPU reads or
+// writes through peer memory.
+MR_DEVICE void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+MR_DEVICE unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // ------------------------------------------------------------ structures
 
 // How a GEMV finds the weights of expert e: a stack (base + e*stride) or a

@@ -79,6 +79,17 @@ struct GemvParams {
   // epilogues
   uint16_t* out_bf16;     // STORE: [*, rows]; SWIGLU: h [*, rows] permuted
   float* out_f32;         // STORE (MXFP4 kernel): fp32 output instead of out_bf16
+  // PARTIAL, expert parallel (TMA kernel): routed column v's partial goes to
+  // rank v / peer_cols's buffer peer_part[...] at row v % peer_cols (an
+  // NVLink store when that rank is another GPU); when every CTA is done the
+  // last one publishes peer_epoch into peer_flags[j][peer_rank] of every rank j
+  float* const* peer_part;
+  int peer_cols;
+  unsigned* const* peer_flags;
+  unsigned* peer_done;
+  int peer_n;
+  int peer_rank;
+  unsigned peer_epoch;
   float* hsum;            // SWIGLU: [*, rows/64]
   float* part;            // PARTIAL: [*, rows]
   const float* weights;   // routing weights [Tk]

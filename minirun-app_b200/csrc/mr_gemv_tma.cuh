@@ -763,10 +763,17 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
                 // routed slots are the w2 gather's bf16 output; the shared
                 // expert's hi/lo columns stay fp32
                 const bool routed = v < p.Tk;
+                float* dst = p.part;
+                int64_t vv = v;
+                if (p.peer_part && routed) {  // the pair's home rank (possibly a peer GPU)
+                  const int home = (int)(v / p.peer_cols);
+                  dst = p.peer_part[home];
+                  vv = v - (int64_t)home * p.peer_cols;
+                }
                 if (row_a < p.rows)
-                  p.part[v * p.rows + row_a] = routed ? bf16_round(y[t][i]) : y[t][i];
+                  dst[vv * p.rows + row_a] = routed ? bf16_round(y[t][i]) : y[t][i];
                 if (row_b < p.rows)
-                  p.part[v * p.rows + row_b] = routed ? bf16_round(y[t][2 + i]) : y[t][2 + i];
+                  dst[vv * p.rows + row_b] = routed ? bf16_round(y[t][2 + i]) : y[t][2 + i];
               }
             }
           }
@@ -854,6 +861,22 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     }
     named_bar(1, kTmaConsumers);  // red / hs reused by the next item
     if (has_next) cur = nxt;
+  }
+  if constexpr (EPI == EPI_PARTIAL) {
+    // expert parallel: once every CTA's stores are out, tell every rank
+    if (p.peer_flags) {
+      __threadfence_system();  // this thread's peer stores, before the CTA's count
+      named_bar(1, kTmaConsumers);
+    }
+    if (p.peer_flags && ctid == 0) {
+      __threadfence_system();
+      const unsigned prev = atomicAdd(p.peer_done, 1u);
+      if (prev == gridDim.x - 1) {
+        *p.peer_done = 0;  // for the next launch on this GPU
+        __threadfence_system();
+        for (int j = 0; j < p.peer_n; ++j) st_release_sys(p.peer_flags[j] + p.peer_rank, p.peer_epoch);
+      }
+    }
   }
 }
 

@@ -45,38 +45,70 @@ __global__ void __launch_bounds__(256) dense_f32_kernel(const float* __restrict_
 #pragma unroll
     for (int t = 0; t < TT; ++t) acc[r][t] = 0.0f;
   if (row0 < out) {
-#pragma unroll 4
-    for (int64_t k = k0 + lane * 8; k < k1; k += 256) {
-      float wv[R][8];
+    // U steps of raw weight loads are issued before any of them is used
+    constexpr int U = 4;
+    const void* rowp[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int64_t row = min(row0 + r, out - 1);  // rows past the end recompute row out-1
-        if constexpr (WF32) {
-          const float4* p =
-              reinterpret_cast<const float4*>(static_cast<const float*>(w) + row * in + k);
-          const float4 a = __ldg(p), b = __ldg(p + 1);
-          wv[r][0] = a.x; wv[r][1] = a.y; wv[r][2] = a.z; wv[r][3] = a.w;
-          wv[r][4] = b.x; wv[r][5] = b.y; wv[r][6] = b.z; wv[r][7] = b.w;
-        } else {
-          const uint4 u = ldg_u128(static_cast<const uint16_t*>(w) + row * in + k);
-          const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+    for (int r = 0; r < R; ++r) {
+      const int64_t row = min(row0 + r, out - 1);  // rows past the end recompute row out-1
+      rowp[r] = WF32 ? static_cast<const void*>(static_cast<const float*>(w) + row * in)
+                     : static_cast<const void*>(static_cast<const uint16_t*>(w) + row * in);
+    }
+    for (int64_t kb = k0 + lane * 8; kb < k1; kb += 256 * U) {
+      uint4 raw[U][R][WF32 ? 2 : 1];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            wv[r][2 * i] = __uint_as_float(q[i] << 16);
-            wv[r][2 * i + 1] = __uint_as_float(q[i] & 0xffff0000u);
+      for (int u = 0; u < U; ++u) {
+        const int64_t k = kb + u * 256;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          if (k < k1) {
+            if constexpr (WF32) {
+              const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(rowp[r]) + k);
+              raw[u][r][0] = __ldg(p);
+              raw[u][r][WF32 ? 1 : 0] = __ldg(p + 1);
+            } else {
+              raw[u][r][0] = ldg_u128(static_cast<const uint16_t*>(rowp[r]) + k);
+            }
+          } else {
+            raw[u][r][0] = make_uint4(0, 0, 0, 0);
+            raw[u][r][WF32 ? 1 : 0] = make_uint4(0, 0, 0, 0);
           }
         }
       }
 #pragma unroll
-      for (int t = 0; t < TT; ++t) {
-        const int64_t tok = min(t0 + t, T - 1);
-        const float4* px = reinterpret_cast<const float4*>(x + tok * in + k);
-        const float4 a = __ldg(px), b = __ldg(px + 1);
-        const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      for (int u = 0; u < U; ++u) {
+        const int64_t k = kb + u * 256;
+        if (k >= k1) break;
+        float wv[R][8];
 #pragma unroll
-        for (int r = 0; r < R; ++r)
+        for (int r = 0; r < R; ++r) {
+          if constexpr (WF32) {
+            const uint4 a = raw[u][r][0], b = raw[u][r][WF32 ? 1 : 0];
+            wv[r][0] = __uint_as_float(a.x); wv[r][1] = __uint_as_float(a.y);
+            wv[r][2] = __uint_as_float(a.z); wv[r][3] = __uint_as_float(a.w);
+            wv[r][4] = __uint_as_float(b.x); wv[r][5] = __uint_as_float(b.y);
+            wv[r][6] = __uint_as_float(b.z); wv[r][7] = __uint_as_float(b.w);
+          } else {
+            const uint32_t q[4] = {raw[u][r][0].x, raw[u][r][0].y, raw[u][r][0].z,
+                                   raw[u][r][0].w};
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[r][t] = fmaf(wv[r][i], xv[i], acc[r][t]);
+            for (int i = 0; i < 4; ++i) {
+              wv[r][2 * i] = __uint_as_float(q[i] << 16);
+              wv[r][2 * i + 1] = __uint_as_float(q[i] & 0xffff0000u);
+            }
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          const int64_t tok = min(t0 + t, T - 1);
+          const float4* px = reinterpret_cast<const float4*>(x + tok * in + k);
+          const float4 a = __ldg(px), b = __ldg(px + 1);
+          const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[r][t] = fmaf(wv[r][i], xv[i], acc[r][t]);
+        }
       }
     }
   }
@@ -120,51 +152,61 @@ __global__ void situ_kernel(const float* __restrict__ g, const float* __restrict
 }
 
 // ------------------------------------------- weighted slot sum + RMSNorm
-// One CTA of 1024 threads per token: rs[j] = sum_s w[t,s] * eo[t*k+s][j]
-// (slots added in order; eight slot loads issued before their adds), then,
-// with a norm weight, out[j] = weight[j] * (rs[j] * rsqrt(mean(rs^2) + eps))
-// (squares summed per thread over j = tid, tid + 1024, ..., then a fixed
-// tree). Dynamic shared memory: L floats.
-template <bool WF32>
-__global__ void __launch_bounds__(1024) slot_sum_norm_kernel(const float* __restrict__ eo,
-                                                             const float* __restrict__ wts, int k,
-                                                             int64_t L, const void* norm_w,
-                                                             float eps, float* __restrict__ out) {
-  extern __shared__ float rs[];
-  __shared__ float red[1024];
+// Two launches over a (token, 256-wide chunk) grid, so a single token still
+// spreads over many SMs. slot_sum_kernel: rs[t][j] = sum_s w[t,s] *
+// eo[t*k+s][j] (slots added in order, eight loads issued before their adds)
+// and the chunk's sum of rs^2 by a fixed tree into part[t][chunk]; without a
+// norm weight rs is the output. norm_kernel: every CTA of the token adds the
+// chunk partials in chunk order, then out[j] = weight[j] * (rs[j] *
+// rsqrt(mean + eps)) (Normalization.swift:15-19).
+__global__ void __launch_bounds__(256) slot_sum_kernel(const float* __restrict__ eo,
+                                                       const float* __restrict__ wts, int k,
+                                                       int64_t L, float* __restrict__ rs,
+                                                       float* __restrict__ part) {
+  __shared__ float red[256];
   const int64_t t = blockIdx.x;
+  const int64_t j = (int64_t)blockIdx.y * 256 + threadIdx.x;
   const float* base = eo + t * k * L;
-  float sq = 0.0f;
-  for (int64_t j = threadIdx.x; j < L; j += blockDim.x) {
-    float s = 0.0f;
+  float s = 0.0f;
+  if (j < L) {
     int sl = 0;
     for (; sl + 8 <= k; sl += 8) {
-      float v[8];
+      float v[8], w[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) v[q] = __ldg(base + (sl + q) * L + j);
+      for (int q = 0; q < 8; ++q) {
+        v[q] = __ldg(base + (sl + q) * L + j);
+        w[q] = __ldg(wts + t * k + sl + q);
+      }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) s += v[q] * __ldg(wts + t * k + sl + q);
+      for (int q = 0; q < 8; ++q) s += v[q] * w[q];
     }
     for (; sl < k; ++sl) s += __ldg(base + sl * L + j) * __ldg(wts + t * k + sl);
-    rs[j] = s;
-    sq = fmaf(s, s, sq);
+    rs[t * L + j] = s;
   }
-  if (!norm_w) {
-    for (int64_t j = threadIdx.x; j < L; j += blockDim.x) out[t * L + j] = rs[j];
-    return;
-  }
-  red[threadIdx.x] = sq;
+  if (!part) return;
+  red[threadIdx.x] = s * s;
   __syncthreads();
-  for (int h = 512; h > 0; h >>= 1) {
+  for (int h = 128; h > 0; h >>= 1) {
     if ((int)threadIdx.x < h) red[threadIdx.x] += red[threadIdx.x + h];
     __syncthreads();
   }
-  const float scale = rsqrtf(red[0] / (float)L + eps);
-  for (int64_t j = threadIdx.x; j < L; j += blockDim.x) {
-    const float wv = WF32 ? __ldg(static_cast<const float*>(norm_w) + j)
-                          : bf16_bits_to_f32(__ldg(static_cast<const uint16_t*>(norm_w) + j));
-    out[t * L + j] = wv * (rs[j] * scale);
-  }
+  if (threadIdx.x == 0) part[t * gridDim.y + blockIdx.y] = red[0];
+}
+
+template <bool WF32>
+__global__ void __launch_bounds__(256) norm_kernel(const float* __restrict__ rs,
+                                                   const float* __restrict__ part, int nchunk,
+                                                   int64_t L, const void* norm_w, float eps,
+                                                   float* __restrict__ out) {
+  const int64_t t = blockIdx.x;
+  const int64_t j = (int64_t)blockIdx.y * 256 + threadIdx.x;
+  if (j >= L) return;
+  float ss = 0.0f;
+  for (int c = 0; c < nchunk; ++c) ss += __ldg(part + t * nchunk + c);
+  const float scale = rsqrtf(ss / (float)L + eps);
+  const float wv = WF32 ? __ldg(static_cast<const float*>(norm_w) + j)
+                        : bf16_bits_to_f32(__ldg(static_cast<const uint16_t*>(norm_w) + j));
+  out[t * L + j] = wv * (__ldg(rs + t * L + j) * scale);
 }
 
 __global__ void add_f32_kernel(const float* __restrict__ a, float* __restrict__ y, int64_t n) {
@@ -421,7 +463,8 @@ mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int
                o_sg = take(T * S), o_su = take(T * S), o_sa = take(T * S),
                o_plan = take((int64_t)mx_plan_bytes(Tk, (int)E) / 4),
                o_a1 = take((int64_t)mx_act_bytes(T, Lt, true) / 4),
-               o_a2 = take((int64_t)mx_act_bytes(Tk, I, true) / 4);
+               o_a2 = take((int64_t)mx_act_bytes(Tk, I, true) / 4), o_ssum = take(T * Lt),
+               o_part = take(T * ((Lt + 255) / 256));
   if ((st = ensure_aux(ctx, off))) return st;
   char* base = static_cast<char*>(ctx->aux);
   auto F = [&](size_t o) { return reinterpret_cast<float*>(base + o); };
@@ -454,22 +497,22 @@ mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int
       (st = mx_gemv(ctx, pl, a2, 1, &L->w2, F(o_eo), s)))
     return st;
   // 3. weighted slot sum in fp32, latent RMSNorm, up projection
-  const size_t smem = (size_t)Lt * 4;
-  if (smem > 200 * 1024) return fail(ctx, MR_ERR_UNSUPPORTED, "latent width too large");
-  if (L->norm_dtype == MR_DTYPE_F32) {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(slot_sum_norm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-    slot_sum_norm_kernel<true><<<(unsigned)T, 1024, smem, s>>>(F(o_eo), wts, (int)k, Lt,
-                                                              L->routed_norm, L->rms_eps, F(o_rs));
-  } else {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(slot_sum_norm_kernel<false>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    slot_sum_norm_kernel<false><<<(unsigned)T, 1024, smem, s>>>(F(o_eo), wts, (int)k, Lt,
-                                                               L->routed_norm, L->rms_eps, F(o_rs));
+  {
+    const int nchunk = (int)((Lt + 255) / 256);
+    const dim3 grid((unsigned)T, (unsigned)nchunk);
+    const bool norm = L->routed_norm != nullptr;
+    slot_sum_kernel<<<grid, 256, 0, s>>>(F(o_eo), wts, (int)k, Lt, norm ? F(o_ssum) : F(o_rs),
+                                         norm ? F(o_part) : nullptr);
+    if (norm) {
+      if (L->norm_dtype == MR_DTYPE_F32)
+        norm_kernel<true><<<grid, 256, 0, s>>>(F(o_ssum), F(o_part), nchunk, Lt, L->routed_norm,
+                                               L->rms_eps, F(o_rs));
+      else
+        norm_kernel<false><<<grid, 256, 0, s>>>(F(o_ssum), F(o_part), nchunk, Lt,
+                                                L->routed_norm, L->rms_eps, F(o_rs));
+    }
+    if ((st = cuda_check(ctx, cudaGetLastError(), "slot sum / norm"))) return st;
   }
-  if ((st = cuda_check(ctx, cudaGetLastError(), "slot_sum_norm_kernel"))) return st;
   // 4. shared expert on the original hidden state, then the sum
   if (S > 0) {
     if ((st = project(ctx, &L->shared_gate, x, T, F(o_sg), s)) ||

@@ -74,6 +74,13 @@ class ExpertGroup:
                        L.load().mr_ep_create(self.ctx.handle, idbuf, rank, world, C.byref(h)))
         self.handle = h
 
+    def set_fused(self, fused: bool) -> None:
+        """True (default): the down GEMV stores routed partials into their
+        home ranks' buffers over NVLink and the home rank combines them in slot
+        order (bit-identical to one GPU); False: NCCL reduce-scatter of
+        per-token sums. Every rank must choose the same."""
+        self.ctx.check("mr_ep_set_fused", L.load().mr_ep_set_fused(self.handle, 1 if fused else 0))
+
     def forward(self, shard: MoELayerShard, x: torch.Tensor, out: torch.Tensor | None = None,
                 ids: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's T tokens in, their layer outputs out (same T on all ranks)."""

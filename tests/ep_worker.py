@@ -1,7 +1,10 @@
 """One rank of the expert-parallel parity check (run by tests/test_ep_gpu.py
 under torchrun). Each rank holds its shard of a seeded layer and the whole
 layer; the expert-parallel forward of its tokens must equal the one-GPU
-forward of all ranks' tokens, restricted to its own rows."""
+forward of all ranks' tokens, restricted to its own rows — bit for bit on
+the fused path (routed partials stored into the home rank over NVLink),
+within fp32 summation order on the NCCL path. Both run on the TMA GEMV, the
+same kernel as the one-GPU reference here."""
 import dataclasses
 import json
 import os
@@ -31,6 +34,7 @@ def main():
     import datetime
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     group = M.ExpertGroup(rank, rank, world)
+    M.Context.get(rank).set_kernel_path("tma")
     cases = [
         ("config0", S.CONFIGS[0], 4),
         ("config0_after_down", dataclasses.replace(S.CONFIGS[0], weight_after_down=True), 5),
@@ -43,17 +47,23 @@ def main():
         shard = S.synth_layer(spec, layer=1, device=rank, shard=(rank, world))
         xall = S.synth_x(spec, T * world, layer=1, batch=7, device=rank)
         x = xall[rank * T:(rank + 1) * T].contiguous()
-        ids = torch.empty((T, spec.top_k), dtype=torch.int32, device=dev)
-        out = group.forward(shard, x, ids=ids)
         ref, sel = full(xall)
         torch.cuda.synchronize()
         mine = ref[rank * T:(rank + 1) * T]
-        results[name] = {
-            "rel_l2": rel_l2(out, mine),
-            "ids_equal": bool(torch.equal(ids, sel.ids[rank * T:(rank + 1) * T].int())),
-            "finite": bool(torch.isfinite(out.float()).all()),
-        }
-        M.Context.get(rank).sync_check()
+        for fused in (True, False):
+            group.set_fused(fused)
+            ids = torch.empty((T, spec.top_k), dtype=torch.int32, device=dev)
+            for _ in range(3):  # repeated steps reuse the peer buffers and epochs
+                out = group.forward(shard, x, ids=ids)
+            torch.cuda.synchronize()
+            results[name + ("_fused" if fused else "_nccl")] = {
+                "fused": fused,
+                "rel_l2": rel_l2(out, mine),
+                "bit_equal": bool(torch.equal(out, mine)),
+                "ids_equal": bool(torch.equal(ids, sel.ids[rank * T:(rank + 1) * T].int())),
+                "finite": bool(torch.isfinite(out.float()).all()),
+            }
+            M.Context.get(rank).sync_check()
     group.close()
     dist.barrier()
     dist.destroy_process_group()

@@ -1,7 +1,8 @@
 """Expert parallelism on 2 GPUs through the C ABI (mr_moe_layer_forward_ep):
-each rank's outputs equal the one-GPU layer over all ranks' tokens (fp32
-summation order of the routed slots aside), and the expert ids are the
-same. Runs tests/ep_worker.py as two torchrun ranks; skipped with fewer than
+each rank's outputs equal the one-GPU layer over all ranks' tokens — bit
+for bit on the fused path (down GEMV storing routed partials into the home
+rank over NVLink), within fp32 summation order on the NCCL path — and the
+expert ids are the same. Runs tests/ep_worker.py as two torchrun ranks; skipped with fewer than
 two GPUs."""
 import json
 import os
@@ -39,3 +40,5 @@ def test_expert_parallel_two_ranks_match_one_gpu():
             assert r["finite"], (res["rank"], name)
             assert r["ids_equal"], (res["rank"], name)
             assert r["rel_l2"] < REL_L2, (res["rank"], name, r["rel_l2"])
+            if r["fused"]:
+                assert r["bit_equal"], (res["rank"], name, r["rel_l2"])
