@@ -851,7 +851,7 @@ namespace mr {
 // Both sizes are whole multiples of 256 bytes, so regions placed back to back
 // keep the 256-byte alignment their bump allocation assumes.
 size_t mx_plan_bytes(int64_t Tk, int E) {
-  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / pick_seg_cols(Tk) + 1;
+  const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / 4 + 1;  // segments of >= 4 columns
   const size_t n = 256 * 3 + 16 + (size_t)max_seg * 16 + (size_t)Tk * 4;
   return (n + 255) & ~size_t(255);
 }
@@ -862,10 +862,10 @@ size_t mx_act_bytes(int64_t rows, int64_t in, bool split) {
   return (n + 255) & ~size_t(255);
 }
 
-mr_status mx_plan_build(mr_ctx* ctx, const int32_t* ids, int64_t Tk, int E, bool dense, void* mem,
-                        MxPlan* pl, cudaStream_t s) {
+mr_status mx_plan_build(mr_ctx* ctx, const int32_t* ids, int64_t Tk, int E, bool dense,
+                        bool split, void* mem, MxPlan* pl, cudaStream_t s) {
   Bump b{static_cast<char*>(mem)};
-  pl->seg_cols = pick_seg_cols(Tk);
+  pl->seg_cols = split ? 4 : 8;  // one 8-column mma tile: 4 tokens x 2 terms when split
   pl->max_seg = std::min<int64_t>(E, Tk) + Tk / pl->seg_cols + 1;
   pl->Tk = Tk;
   pl->nseg = b.take<int>(4);
@@ -927,8 +927,9 @@ mr_status mx_gemv(mr_ctx* ctx, const MxPlan& pl, const MxAct& a, int in_div,
   g.rb_count = (int)((g.rows + kTmaRows - 1) / kTmaRows);
   const int64_t items = pl.max_seg * g.rb_count;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
-  return cuda_check(ctx, launch_tma_mx(g, tm, pl.seg_cols / 8, a.split ? 2 : 1, grid, s),
-                    "gemv(mxfp4)");
+  if (pl.seg_cols != (a.split ? 4 : 8))
+    return fail(ctx, MR_ERR_STATE, "MXFP4 plan built for the other activation form");
+  return cuda_check(ctx, launch_tma_mx(g, tm, 1, a.split ? 2 : 1, grid, s), "gemv(mxfp4)");
 }
 
 mr_status mx_check_mm(mr_ctx* ctx, const mr_mxfp4_desc* w) {
@@ -971,7 +972,7 @@ static mr_status mxfp4_common(mr_ctx* ctx, const void* x, bool x_f32, int64_t T,
   MxAct a;
   MxPlan pl;
   if ((st = mx_prep(ctx, x, x_f32, T, w->in_features, ws, &a, s)) ||
-      (st = mx_plan_build(ctx, ids, Tk, E, dense, ws + act_bytes, &pl, s)))
+      (st = mx_plan_build(ctx, ids, Tk, E, dense, x_f32, ws + act_bytes, &pl, s)))
     return st;
   return mx_gemv(ctx, pl, a, kk, w, out, s);
 }

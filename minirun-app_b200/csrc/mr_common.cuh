@@ -328,8 +328,10 @@ struct MxAct {
 size_t mx_plan_bytes(int64_t Tk, int E);
 size_t mx_act_bytes(int64_t rows, int64_t in, bool split);
 mr_status mx_check_mm(mr_ctx* ctx, const mr_mxfp4_desc* w);
-mr_status mx_plan_build(mr_ctx* ctx, const int32_t* ids, int64_t Tk, int E, bool dense, void* mem,
-                        MxPlan* plan, cudaStream_t s);
+// split: segments of at most 4 columns (fp32 activations, two mma columns per
+// token), else 8
+mr_status mx_plan_build(mr_ctx* ctx, const int32_t* ids, int64_t Tk, int E, bool dense,
+                        bool split, void* mem, MxPlan* plan, cudaStream_t s);
 mr_status mx_prep(mr_ctx* ctx, const void* x, bool x_f32, int64_t rows, int64_t in, void* mem,
                   MxAct* act, cudaStream_t s);
 // out[v][r] for plan column v, reading activation row v / in_div.

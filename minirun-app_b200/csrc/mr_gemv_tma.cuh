@@ -29,9 +29,11 @@
 // puts the half's largest magnitude in [2^14, 2^15)). The fold is
 // y += (2^(e-127) * 2^k) * acc per half; only the store epilogue is built.
 // XS == 2 takes fp32 activations as two f16 terms per element (hi =
-// f16(x * 2^-k), lo = f16(x * 2^-k - hi): 22 significant bits), both
-// accumulated into the same fragment; the store is bf16 or, with
-// p.out_f32, fp32.
+// f16(x * 2^-k), lo = f16(x * 2^-k - hi): 22 significant bits) as two mma
+// columns of the same token: an 8-column tile holds 4 tokens (segments of at
+// most 4 columns), B column n is term n & 1 of the tile's token n >> 1, and a
+// lane's accumulator pair (2c, 2c+1) is token c's hi and lo products, added
+// before the fold. The store is bf16 or, with p.out_f32, fp32.
 #pragma once
 
 #include <cuda.h>
@@ -301,26 +303,6 @@ MR_DEVICE void group_mma_mx(float (&lo)[4], float (&hi)[4], const uint32_t (&wa)
   mma_f16_16816(hi, ra[2], rb[2], ra[3], rb[3], xb[6], xb[7]);
 }
 
-// MX with fp32 activations: the same four products against both f16 terms
-// of the activations (xh, xl), accumulated into the same fragments.
-MR_DEVICE void group_mma_mx2(float (&lo)[4], float (&hi)[4], const uint32_t (&wa)[2],
-                             const uint32_t (&wb)[2], const uint32_t (&xh)[8],
-                             const uint32_t (&xl)[8]) {
-  uint32_t ra[4], rb[4];
-  e2m1x8_to_f16x2(wa[0], ra);
-  e2m1x8_to_f16x2(wb[0], rb);
-  mma_f16_16816(lo, ra[0], rb[0], ra[1], rb[1], xh[0], xh[1]);
-  mma_f16_16816(lo, ra[2], rb[2], ra[3], rb[3], xh[2], xh[3]);
-  mma_f16_16816(lo, ra[0], rb[0], ra[1], rb[1], xl[0], xl[1]);
-  mma_f16_16816(lo, ra[2], rb[2], ra[3], rb[3], xl[2], xl[3]);
-  e2m1x8_to_f16x2(wa[1], ra);
-  e2m1x8_to_f16x2(wb[1], rb);
-  mma_f16_16816(hi, ra[0], rb[0], ra[1], rb[1], xh[4], xh[5]);
-  mma_f16_16816(hi, ra[2], rb[2], ra[3], rb[3], xh[6], xh[7]);
-  mma_f16_16816(hi, ra[0], rb[0], ra[1], rb[1], xl[4], xl[5]);
-  mma_f16_16816(hi, ra[2], rb[2], ra[3], rb[3], xl[6], xl[7]);
-}
-
 // Bounded wait. On expiry (or once another thread has flagged an abort) it
 // sets the device error word and the CTA's abort flag and returns, so the
 // caller carries on to every barrier it owes: results are then garbage but
@@ -550,13 +532,16 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     int vb[NT], v0[NT], v1[NT];
     float w0[NT], w1[NT];
   };
+  // split fp32 activations: 4 tokens per tile, B column = (token, term)
+  constexpr bool kSplit = XS == 2;
+  constexpr int kTileCols = kSplit ? 4 : 8;
   auto fetch_cols = [&](Meta& m) {
     const int nc = m.info.ncols;
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
-      const int cb = min(t * 8 + r8, nc - 1);
-      const int c0 = min(t * 8 + 2 * c, nc - 1);
-      const int c1 = min(t * 8 + 2 * c + 1, nc - 1);
+      const int cb = min(kSplit ? t * 4 + (r8 >> 1) : t * 8 + r8, nc - 1);
+      const int c0 = min(kSplit ? t * 4 + c : t * 8 + 2 * c, nc - 1);
+      const int c1 = min(kSplit ? t * 4 + c : t * 8 + 2 * c + 1, nc - 1);
       if (m.info.shared) {
         m.vb[t] = p.Tk + m.info.col0 + cb;
         m.v0[t] = p.Tk + m.info.col0 + c0;
@@ -587,7 +572,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const ItemInfo& info = cur.info;
     const bool shared = info.shared;
     const int ncols = info.ncols;
-    const int ntiles = (ncols + 7) >> 3;
+    const int ntiles = (ncols + kTileCols - 1) / kTileCols;
     const bool single = !ST::kMx && ncols == 1;  // FMA path instead of an 8-column mma tile
     // activation pointers at this warp's first group, walked one stage at a time
     const uint16_t* xr[NT];
@@ -595,7 +580,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const float* xp1[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
-      xr[t] = p.xperm + (in_row(cur.vb[t]) * p.in + kq * kGpw * kGroup) * XS + c * 16;
+      xr[t] = p.xperm + (in_row(cur.vb[t]) * p.in + kq * kGpw * kGroup) * XS + c * 16 +
+              (kSplit ? (r8 & 1) * kGroup : 0);  // split: this column's term plane
       xp0[t] = p.xsum + in_row(cur.v0[t]) * ngroups * XP + kq * kGpw * XP;
       xp1[t] = p.xsum + in_row(cur.v1[t]) * ngroups * XP + kq * kGpw * XP;
     }
@@ -674,21 +660,24 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
               for (int j = 0; j < kGpw; ++j) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) lo[j][i] = hi[j][i] = 0.0f;
-                if constexpr (XS == 1) {
-                  group_mma_mx(lo[j], hi[j], wa[j], wb[j], xb[j]);
-                } else {
-                  const uint4 u0 = ldg_u128(xr[t] + j * kGroup * XS + kGroup);
-                  const uint4 u1 = ldg_u128(xr[t] + j * kGroup * XS + kGroup + 8);
-                  const uint32_t xl[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-                  group_mma_mx2(lo[j], hi[j], wa[j], wb[j], xb[j], xl);
-                }
+                group_mma_mx(lo[j], hi[j], wa[j], wb[j], xb[j]);
               }
+              if constexpr (kSplit) {  // columns 2c, 2c+1 = token c's two terms
 #pragma unroll
-              for (int j = 0; j < kGpw; ++j) {
-                y[t][0] = fmaf(sa[j] * L0[j], lo[j][0], fmaf(za[j] * H0[j], hi[j][0], y[t][0]));
-                y[t][1] = fmaf(sa[j] * L1[j], lo[j][1], fmaf(za[j] * H1[j], hi[j][1], y[t][1]));
-                y[t][2] = fmaf(sb[j] * L0[j], lo[j][2], fmaf(zb[j] * H0[j], hi[j][2], y[t][2]));
-                y[t][3] = fmaf(sb[j] * L1[j], lo[j][3], fmaf(zb[j] * H1[j], hi[j][3], y[t][3]));
+                for (int j = 0; j < kGpw; ++j) {
+                  y[t][0] = fmaf(sa[j] * L0[j], lo[j][0] + lo[j][1],
+                                 fmaf(za[j] * H0[j], hi[j][0] + hi[j][1], y[t][0]));
+                  y[t][2] = fmaf(sb[j] * L0[j], lo[j][2] + lo[j][3],
+                                 fmaf(zb[j] * H0[j], hi[j][2] + hi[j][3], y[t][2]));
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < kGpw; ++j) {
+                  y[t][0] = fmaf(sa[j] * L0[j], lo[j][0], fmaf(za[j] * H0[j], hi[j][0], y[t][0]));
+                  y[t][1] = fmaf(sa[j] * L1[j], lo[j][1], fmaf(za[j] * H1[j], hi[j][1], y[t][1]));
+                  y[t][2] = fmaf(sb[j] * L0[j], lo[j][2], fmaf(zb[j] * H0[j], hi[j][2], y[t][2]));
+                  y[t][3] = fmaf(sb[j] * L1[j], lo[j][3], fmaf(zb[j] * H1[j], hi[j][3], y[t][3]));
+                }
               }
             } else {
               float X0[kGpw], X1[kGpw];
@@ -746,8 +735,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
 #pragma unroll
         for (int t = 0; t < NT; ++t)
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const int ci = t * 8 + 2 * c + i;
+          for (int i = 0; i < (kSplit ? 1 : 2); ++i) {
+            const int ci = kSplit ? t * 4 + c : t * 8 + 2 * c + i;
             if (t < ntiles && ci < ncols) {
               const int64_t v = i ? cur.v1[t] : cur.v0[t];
               if constexpr (EPI == EPI_STORE) {

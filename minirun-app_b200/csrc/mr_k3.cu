@@ -483,7 +483,7 @@ mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int
     return st;
   MxPlan pl;
   MxAct a1, a2;
-  if ((st = mx_plan_build(ctx, ids, Tk, (int)E, false, base + o_plan, &pl, s))) return st;
+  if ((st = mx_plan_build(ctx, ids, Tk, (int)E, false, true, base + o_plan, &pl, s))) return st;
   if ((st = project(ctx, &L->routed_down, x, T, F(o_lat), s))) return st;
   if ((st = mx_prep(ctx, F(o_lat), true, T, Lt, base + o_a1, &a1, s)) ||
       (st = mx_gemv(ctx, pl, a1, (int)k, &L->w1, F(o_g), s)) ||
