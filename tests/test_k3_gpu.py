@@ -37,9 +37,11 @@ def mx_dev(m):
                           torch.from_numpy(np.ascontiguousarray(m.scales)).to(dev()))
 
 
-@pytest.mark.parametrize("T", [1, 3, 9, 20])
+@pytest.mark.parametrize("T", [1, 3, 4, 9, 20])
 @pytest.mark.parametrize("wdt", [torch.bfloat16, torch.float32])
 def test_dense_mm_f32(T, wdt):
+    """T < 4 and fp32 weights: the FMA kernel; bf16 weights from T = 4: the
+    tensor-core kernel (activations as three bf16 terms)."""
     rng = np.random.default_rng(T)
     w = rng.standard_normal((200, 1024)).astype(np.float32)
     wt = torch.from_numpy(w).to(dev()).to(wdt)
@@ -47,6 +49,16 @@ def test_dense_mm_f32(T, wdt):
     x = rng.standard_normal((T, 1024)).astype(np.float32)
     y = M.dense_mm_f32(torch.from_numpy(x).to(dev()), wt).cpu().numpy()
     ref = x.astype(np.float64) @ wf.T
+    assert rel_l2(y, ref) < 1e-6
+
+
+def test_dense_mm_f32_width_not_multiple_of_32():
+    rng = np.random.default_rng(5)
+    w = torch.from_numpy(rng.standard_normal((96, 1000)).astype(np.float32)).to(dev())
+    wt = w.to(torch.bfloat16)
+    x = rng.standard_normal((9, 1000)).astype(np.float32)
+    y = M.dense_mm_f32(torch.from_numpy(x).to(dev()), wt).cpu().numpy()
+    ref = x.astype(np.float64) @ wt.float().cpu().numpy().astype(np.float64).T
     assert rel_l2(y, ref) < 1e-6
 
 
