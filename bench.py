@@ -595,7 +595,7 @@ def run_reference(args, world, rank, local):
     O.moe_layer_forward(L, x)
     est = time.perf_counter() - t0
     K = max(2, min(args.steps, int(150 / max(est, 1e-3))))
-    W = max(1, min(args.warmup, 1))
+    W = max(3, min(args.warmup, int(60 / max(est, 1e-3))))  # >= 3 untimed steps
     for _ in range(W):
         O.moe_layer_forward(L, x)
     t0 = time.perf_counter()

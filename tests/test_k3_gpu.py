@@ -135,8 +135,15 @@ def test_block_variants(variant):
 def test_block_wider_and_batch_invariant():
     B, raw = k3_case.make(seed=13, E=64, H=2048, Lt=1024, I=1024, S=1024, k=8)
     got = _check_block(B, raw, 12, 13)
-    # a token's output does not depend on the rest of the batch
+    # a token's output does not depend on the rest of the batch: bit for bit
+    # while the batch size keeps the dense projections on the same kernel
+    # (tensor core from 4 tokens), to fp32 rounding across that switch (1.3e-6
+    # measured on this case)
     blk = k3_case.to_gpu(B, raw, dev())
     x = k3_case.x_for(13, 12, 2048)
+    six, _ = blk.forward(torch.from_numpy(x[4:10]).to(dev()))
+    np.testing.assert_array_equal(six.cpu().numpy(), got[4:10])
     one, _ = blk.forward(torch.from_numpy(x[5:6]).to(dev()))
-    np.testing.assert_array_equal(one.cpu().numpy()[0], got[5])
+    two, _ = blk.forward(torch.from_numpy(x[5:7]).to(dev()))
+    np.testing.assert_array_equal(two.cpu().numpy()[0], one.cpu().numpy()[0])
+    assert rel_l2(one.cpu().numpy()[0], got[5]) < 1e-5
