@@ -47,6 +47,9 @@ constexpr int kTmaGps = 8;  // groups per stage
 #ifndef MR_TMA_CONSUMER_WARPS
 #define MR_TMA_CONSUMER_WARPS 16
 #endif
+#ifndef MR_TMA_SINGLE_FMA
+#define MR_TMA_SINGLE_FMA 1
+#endif
 constexpr int kTmaConsumerWarps = MR_TMA_CONSUMER_WARPS;  // 4 m-tiles x kKSplit
 constexpr int kKSplit = kTmaConsumerWarps / 4;           // warps sharing an m-tile
 constexpr int kGpw = kTmaGps / kKSplit;                  // groups per warp per stage
@@ -573,7 +576,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     const bool shared = info.shared;
     const int ncols = info.ncols;
     const int ntiles = (ncols + kTileCols - 1) / kTileCols;
-    const bool single = !ST::kMx && ncols == 1;  // FMA path instead of an 8-column mma tile
+    // one column: FMA path instead of an 8-column mma tile, for the down
+    // projection only — measured at T = 64 on config 1, gate/up runs 1.19 ms
+    // with single columns on the mma path against 1.25 ms on the FMA path,
+    // the down projection 0.87 against 0.83 ms (-DMR_TMA_SINGLE_FMA=0: the
+    // mma path everywhere)
+    const bool single = MR_TMA_SINGLE_FMA && !ST::kMx && EPI != EPI_SWIGLU && ncols == 1;
     // activation pointers at this warp's first group, walked one stage at a time
     const uint16_t* xr[NT];
     const float* xp0[NT];
