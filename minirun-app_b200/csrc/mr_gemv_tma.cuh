@@ -139,6 +139,28 @@ MR_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint
       : "memory");
 }
 
+// The same load with an L2 cache policy (createpolicy), for weight tiles
+// that are read once: evict-first keeps them from displacing the
+// activations and partials that other CTAs re-read.
+MR_DEVICE void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+MR_DEVICE uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+#ifndef MR_TMA_EVICT_FIRST
+#define MR_TMA_EVICT_FIRST 1
+#endif
+
 // Byte b (< 128) of row r of a 128-byte-swizzled box (box base 1024-aligned).
 MR_DEVICE const char* swz128(const char* box, int r, int b) {
   return box + r * 128 + ((((b >> 4) ^ r) & 7) << 4) + (b & 15);
@@ -368,6 +390,15 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t it = 0, slot = 0, phase = 0;
+      // weight tiles: streamed once (evict-first in L2 unless built with
+      // -DMR_TMA_EVICT_FIRST=0)
+      const uint64_t wpol = MR_TMA_EVICT_FIRST ? l2_evict_first_policy() : 0;
+      auto tma_load_w = [&](void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+        if (MR_TMA_EVICT_FIRST)
+          tma_load_2d_hint(dst, map, x, y, bar, wpol);
+        else
+          tma_load_2d(dst, map, x, y, bar);
+      };
       for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         const ItemInfo info = decode_item(p, n_routed, item);
         const CUtensorMap* mp[2];
@@ -393,11 +424,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           for (int m = 0; m < ST::kMats; ++m) {
 #pragma unroll
             for (int j = 0; j < ST::kBoxes; ++j)
-              tma_load_2d(A + (m * ST::kBoxes + j) * ST::kBoxBytes, mp[m],
+              tma_load_w(A + (m * ST::kBoxes + j) * ST::kBoxBytes, mp[m],
                           (st * ST::kBoxes + j) * 32, y0, full + slot);
             const int sbytes = ST::kBoxRows * kTmaGps * ST::kSpg * ST::kEsz;
-            tma_load_2d(S + m * sbytes, ms[m], st * kTmaGps * ST::kSpg, y0, full + slot);
-            if constexpr (!ST::kMx) tma_load_2d(Z + m * sbytes, mz[m], st * kTmaGps, y0, full + slot);
+            tma_load_w(S + m * sbytes, ms[m], st * kTmaGps * ST::kSpg, y0, full + slot);
+            if constexpr (!ST::kMx) tma_load_w(Z + m * sbytes, mz[m], st * kTmaGps, y0, full + slot);
           }
           if (++slot == (uint32_t)nst) {
             slot = 0;
