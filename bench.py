@@ -71,6 +71,13 @@ def parse():
                    help="routed experts of the K3 layer (flagship: 896)")
     p.add_argument("--ep-nccl", action="store_true",
                    help="expert parallel: NCCL reduce-scatter instead of the fused peer stores")
+    p.add_argument("--cache-layers", type=int, default=0,
+                   help="config 4: budgeted decode through this many layers via the HBM "
+                        "expert cache (58 in BASELINE; 0 = skip)")
+    p.add_argument("--cache-budget-gb", type=float, default=40.0,
+                   help="config 4: HBM byte budget of the expert cache")
+    p.add_argument("--cache-only", action="store_true",
+                   help="measure only the config-4 cached decode line")
     p.add_argument("--k3-only", action="store_true",
                    help="measure only the K3 latent-MoE layer (profiling driver)")
     return p.parse_args()
@@ -490,6 +497,79 @@ def k3_run(args, M, torch, dev, hbm):
             "by_tokens": out}
 
 
+def cache_run(args, M, S, torch, dev):
+    """Config 4: one-token decode through `--cache-layers` config-1 layers whose
+    routed experts live in pinned host memory and reach the GPU through the
+    HBM expert cache (`mr_moe_layer_forward_cached`) under `--cache-budget-gb`.
+    Each layer has its own seeded router (and so its own routing); to keep
+    host memory at one layer's 6.4 GB, every layer registers the same seeded
+    expert arrays under its own (layer, expert) keys, so the cache sees 58 x
+    256 distinct experts and copies each miss from host memory as it would
+    distinct weights. The shared expert stays resident. A step = one token
+    position through all layers, each layer routing a seeded token of its own:
+    with the BASELINE weight distributions (codes uniform, bias -8 * scale, so
+    every weight has mean -scale/2) a layer's output is dominated by one
+    common-mode direction, and chained layers would route every token to the
+    same experts. Independent tokens make the routing as diverse as random
+    choice, the hard case for the cache."""
+    spec = S.CONFIGS[1]
+    NL = args.cache_layers
+    base = S.synth_layer(spec, layer=0, device=dev.index)
+    E, H = spec.experts, spec.hidden
+    slot = M.ExpertCache.slot_bytes_for(base.gate, base.up, base.down)
+    cache = M.ExpertCache(dev.index, int(args.cache_budget_gb * 1e9), slot)
+    t0 = time.perf_counter()
+    host = [tuple(tuple(t[e].contiguous().cpu().pin_memory() for t in (w.packed, w.scales,
+                                                                        w.biases))
+                  for w in (base.gate, base.up, base.down)) for e in range(E)]
+    layers = []
+    for l in range(NL):
+        rw = torch.empty((E, H), dtype=torch.bfloat16, device=dev)
+        S.synth_normal_bf16(S.derive(spec.seed, S.label(l, S.KIND_ROUTER, 0, 0)), E * H,
+                            1.0 / 32.0, False, rw)
+        layers.append(M.CachedLayer(rw, base.router, H, spec.inter, spec.bits, spec.group,
+                                    shared=base.shared))
+        for e in range(E):
+            cache.register(l, e, host[e])
+    setup_s = time.perf_counter() - t0
+    steps = max(3, min(args.steps, 10))
+    W = max(3, args.warmup)
+    # a seeded token per (step, layer)
+    xs = [[S.synth_x(spec, 1, layer=l, batch=i, device=dev.index) for l in range(NL)]
+          for i in range(W + steps)]
+    out = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
+
+    def token(i):
+        for l, lay in enumerate(layers):
+            cache.forward(l, lay, xs[i][l], out=out)
+
+    for i in range(W):  # first fills of the cache
+        token(i)
+    torch.cuda.synchronize()
+    s0 = cache.stats()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(W, W + steps):
+        token(i)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    s1 = cache.stats()
+    d = {k: s1[k] - s0[k] for k in ("hits", "misses", "bytes_copied") if k in s1}
+    uses = d.get("hits", 0) + d.get("misses", 0)
+    cache.close()
+    return {"workload": f"config4: {NL} config-1 layers, 1-token decode, {E} routed experts "
+                        f"per layer in pinned host memory, HBM cache budget "
+                        f"{args.cache_budget_gb:g} GB ({int(args.cache_budget_gb * 1e9) // slot}"
+                        f" slots of {slot} B)",
+            "tokens_per_s": 1e3 / ms, "ms_per_token": ms, "steps": steps,
+            "hit_rate": d.get("hits", 0) / max(uses, 1),
+            "h2d_gbs": d.get("bytes_copied", 0) / steps / (ms / 1e3) / 1e9,
+            "setup_s": setup_s,
+            "note": "every layer registers the same seeded host arrays under its own keys"}
+
+
 def e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local, group=None):
     """Same metric with host buffers: pinned host x in, host out, both copies
     inside the timed region — through the host-buffer C-ABI call on one GPU,
@@ -636,6 +716,14 @@ def main():
     world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, world, rank, local)
+    elif args.cache_only:
+        import torch
+        import minirun_moe as M
+        from minirun_moe import synth as S
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        print(json.dumps({"config4_cached_decode": cache_run(args, M, S, torch, dev)}),
+              flush=True)
     elif args.k3_only:
         import torch
         import minirun_moe as M
