@@ -71,6 +71,9 @@ def parse():
                    help="routed experts of the K3 layer (flagship: 896)")
     p.add_argument("--ep-nccl", action="store_true",
                    help="expert parallel: NCCL reduce-scatter instead of the fused peer stores")
+    p.add_argument("--config", default="1", choices=["1", "2b2", "2b8"],
+                   help="decode layer: config 1 (the headline) or config 2's wide 2-/8-bit "
+                        "layers (384 experts)")
     p.add_argument("--cache-layers", type=int, default=0,
                    help="config 4: budgeted decode through this many layers via the HBM "
                         "expert cache (58 in BASELINE; 0 = skip)")
@@ -183,7 +186,7 @@ def run_ours(args, world, rank, local):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev,
                                 timeout=__import__("datetime").timedelta(seconds=300))
-    spec = S.CONFIGS[1]
+    spec = S.CONFIGS[1 if args.config == "1" else args.config]
     if args.experts:
         import dataclasses
         spec = dataclasses.replace(spec, experts=args.experts)
@@ -297,7 +300,8 @@ def run_ours(args, world, rank, local):
     gu_bytes = sum(gate_up_bytes(T, u) for u in us) / len(us)
     achieved = gu_bytes / (gu_step_ms / 1e3) / 1e9
     kern = {k: {"ms_per_launch": v[0] / max(v[1], 1), "launches": v[1]} for k, v in prof.items()}
-    traffic = read_traffic(gu_bytes)
+    # the ncu traffic summary is of the config-1 (4-bit) kernel
+    traffic = read_traffic(gu_bytes) if args.config == "1" else None
 
     sweep = {}
     for tok in token_counts[1:]:
@@ -336,12 +340,14 @@ def run_ours(args, world, rank, local):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16 activations, 4-bit affine weights (u4 codes, bf16 scale/bias), fp32 "
+        "dtype": f"bf16 activations, {spec.bits}-bit affine weights (u{spec.bits} codes, bf16 "
+                 "scale/bias), fp32 "
                  "accumulate",
         "data": "synthetic (SplitMix64-seeded, BASELINE config 1 distributions)",
         "config": {
-            "workload": f"config1 decode T={T}: H7168, {spec.experts}+1 experts, top-8, I2048, "
-                        "4-bit g64",
+            "workload": f"config{args.config[0]} decode T={T}: H{spec.hidden}, "
+                        f"{spec.experts}+1 experts, top-{spec.top_k}, I{spec.inter}, "
+                        f"{spec.bits}-bit g{spec.group}",
             "tokens": T,
             "global_batch": world * T,
             "layers_cycled": NL,
