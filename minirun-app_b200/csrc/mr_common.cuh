@@ -323,7 +323,8 @@ struct MxPlan {
 struct MxAct {
   uint16_t* xperm;
   float* xscale;
-  bool split;  // fp32 activations as two f16 terms
+  bool split;    // two f16 terms per element, two mma columns per token
+  bool out_f32;  // fp32 activations in, fp32 out (else bf16)
 };
 size_t mx_plan_bytes(int64_t Tk, int E);
 size_t mx_act_bytes(int64_t rows, int64_t in, bool split);
@@ -332,8 +333,9 @@ mr_status mx_check_mm(mr_ctx* ctx, const mr_mxfp4_desc* w);
 // token), else 8
 mr_status mx_plan_build(mr_ctx* ctx, const int32_t* ids, int64_t Tk, int E, bool dense,
                         bool split, void* mem, MxPlan* plan, cudaStream_t s);
-mr_status mx_prep(mr_ctx* ctx, const void* x, bool x_f32, int64_t rows, int64_t in, void* mem,
-                  MxAct* act, cudaStream_t s);
+// split: the two-column layout (forced for fp32 x)
+mr_status mx_prep(mr_ctx* ctx, const void* x, bool x_f32, bool split, int64_t rows, int64_t in,
+                  void* mem, MxAct* act, cudaStream_t s);
 // out[v][r] for plan column v, reading activation row v / in_div.
 mr_status mx_gemv(mr_ctx* ctx, const MxPlan& plan, const MxAct& act, int in_div,
                   const mr_mxfp4_desc* w, void* out, cudaStream_t s);

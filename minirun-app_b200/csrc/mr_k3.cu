@@ -591,7 +591,7 @@ mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int
   MxAct a1, a2;
   if ((st = mx_plan_build(ctx, ids, Tk, (int)E, false, true, base + o_plan, &pl, s))) return st;
   if ((st = project(ctx, &L->routed_down, x, T, F(o_lat), s))) return st;
-  if ((st = mx_prep(ctx, F(o_lat), true, T, Lt, base + o_a1, &a1, s)) ||
+  if ((st = mx_prep(ctx, F(o_lat), true, true, T, Lt, base + o_a1, &a1, s)) ||
       (st = mx_gemv(ctx, pl, a1, (int)k, &L->w1, F(o_g), s)) ||
       (st = mx_gemv(ctx, pl, a1, (int)k, &L->w3, F(o_u), s)))
     return st;
@@ -599,7 +599,7 @@ mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int
                      F(o_act), s)))
     return st;
   // each (token, slot) row is its own column: activation row v, in_div 1
-  if ((st = mx_prep(ctx, F(o_act), true, Tk, I, base + o_a2, &a2, s)) ||
+  if ((st = mx_prep(ctx, F(o_act), true, true, Tk, I, base + o_a2, &a2, s)) ||
       (st = mx_gemv(ctx, pl, a2, 1, &L->w2, F(o_eo), s)))
     return st;
   // 3. weighted slot sum in fp32, latent RMSNorm, up projection

@@ -88,8 +88,9 @@ struct PrepMxParams {
   const float* xf;     // fp32 input, or NULL
   int64_t rows;
   int64_t in;
-  uint16_t* xperm;     // [rows, in] (bf16 input) or [rows, 2 * in] (fp32 input)
+  uint16_t* xperm;     // [rows, in], or [rows, 2 * in] with split
   float* xscale;       // [rows, in / 32]
+  int split;           // two f16 terms per element (always for fp32 input)
 };
 
 // Called by whole warps: the two chunks of a half exchange their maxima by
@@ -100,9 +101,9 @@ MR_DEVICE void prep_mx_chunk(const PrepMxParams& p, int64_t chunk, bool valid) {
   const int64_t r = chunk / per_row;
   const int64_t c16 = chunk - r * per_row;
   const int q = (int)(c16 & 3);  // chunk of the group: elements [16q, 16q+16), half q >> 1
-  const bool split = p.xf != nullptr;
+  const bool split = p.split != 0;
   float f[16];
-  if (split) {
+  if (p.xf) {
     const float4* src = reinterpret_cast<const float4*>(p.xf + r * p.in + c16 * 16);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
