@@ -871,14 +871,15 @@ mr_status mx_plan_build(mr_ctx* ctx, const int32_t* ids, int64_t Tk, int E, bool
   pl->nseg = b.take<int>(4);
   pl->segs = b.take<int4>(pl->max_seg);
   pl->cols = b.take<int>(Tk);
+  cudaError_t e;
   if (dense) {
-    dense_plan_kernel<<<(int)std::min<int64_t>((Tk + 255) / 256, 1024), 256, 0, s>>>(
-        (int)Tk, pl->seg_cols, pl->nseg, pl->segs, pl->cols);
+    e = launch_pdl(dense_plan_kernel, dim3((unsigned)std::min<int64_t>((Tk + 255) / 256, 1024)),
+                   dim3(256), 0, s, (int)Tk, pl->seg_cols, pl->nseg, pl->segs, pl->cols);
   } else {
     PlanParams plan{ids, (int)Tk, E, pl->nseg, pl->segs, pl->cols, ctx->d_error, pl->seg_cols};
-    plan_kernel<<<1, 256, 0, s>>>(plan);
+    e = launch_pdl(plan_kernel, dim3(1), dim3(256), 0, s, plan);
   }
-  return cuda_check(ctx, cudaGetLastError(), "plan kernel");
+  return cuda_check(ctx, e, "plan kernel");
 }
 
 mr_status mx_prep(mr_ctx* ctx, const void* x, bool x_f32, bool split, int64_t rows, int64_t in,
@@ -895,8 +896,8 @@ mr_status mx_prep(mr_ctx* ctx, const void* x, bool x_f32, bool split, int64_t ro
                   rows, in, a->xperm, a->xscale, split ? 1 : 0};
   const int64_t chunks = rows * (in / 16);
   const int pgrid = (int)std::max<int64_t>(1, std::min<int64_t>((chunks + 255) / 256, 4 * ctx->sm_count));
-  prep_mx_kernel<<<pgrid, 256, 0, s>>>(pp);
-  return cuda_check(ctx, cudaGetLastError(), "prep_mx_kernel");
+  return cuda_check(ctx, launch_pdl(prep_mx_kernel, dim3(pgrid), dim3(256), 0, s, pp),
+                    "prep_mx_kernel");
 }
 
 mr_status mx_gemv(mr_ctx* ctx, const MxPlan& pl, const MxAct& a, int in_div,

@@ -32,6 +32,7 @@ __global__ void __launch_bounds__(256) dense_f32_kernel(const float* __restrict_
                                                         const void* __restrict__ w, int64_t out,
                                                         int64_t in, int ks, int64_t kchunk,
                                                         float* __restrict__ y) {
+  pdl_wait_and_release();
   __shared__ float red[8][R][TT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = 8 / ks;
@@ -145,6 +146,7 @@ __global__ void __launch_bounds__(256) dense_f32_kernel(const float* __restrict_
 // K slices (chosen from the matrix alone) are added in slice order through
 // shared memory. Requires in % 32 == 0 and 16-byte aligned rows.
 __global__ void split3_kernel(const float* __restrict__ x, int64_t n, uint16_t* __restrict__ xs) {
+  pdl_wait_and_release();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float v = __ldg(x + i);
@@ -162,6 +164,7 @@ __global__ void __launch_bounds__(256) dense_tc_kernel(const uint16_t* __restric
                                                        const uint16_t* __restrict__ w,
                                                        int64_t out, int64_t in, int ks,
                                                        int64_t kchunk, float* __restrict__ y) {
+  pdl_wait_and_release();
   __shared__ float red[8][32][4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -222,6 +225,7 @@ __global__ void __launch_bounds__(256) dense_tc_kernel(const uint16_t* __restric
 __global__ void situ_kernel(const float* __restrict__ g, const float* __restrict__ u,
                             int64_t ld_in, int64_t rows, int64_t d, float beta, float lb,
                             float* __restrict__ out) {
+  pdl_wait_and_release();
   const int64_t n = rows * d;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -246,6 +250,7 @@ __global__ void __launch_bounds__(256) slot_sum_kernel(const float* __restrict__
                                                        const float* __restrict__ wts, int k,
                                                        int64_t L, float* __restrict__ rs,
                                                        float* __restrict__ part) {
+  pdl_wait_and_release();
   __shared__ float red[256];
   const int64_t t = blockIdx.x;
   const int64_t j = (int64_t)blockIdx.y * 256 + threadIdx.x;
@@ -281,6 +286,7 @@ __global__ void __launch_bounds__(256) norm_kernel(const float* __restrict__ rs,
                                                    const float* __restrict__ part, int nchunk,
                                                    int64_t L, const void* norm_w, float eps,
                                                    float* __restrict__ out) {
+  pdl_wait_and_release();
   const int64_t t = blockIdx.x;
   const int64_t j = (int64_t)blockIdx.y * 256 + threadIdx.x;
   if (j >= L) return;
@@ -293,6 +299,7 @@ __global__ void __launch_bounds__(256) norm_kernel(const float* __restrict__ rs,
 }
 
 __global__ void add_f32_kernel(const float* __restrict__ a, float* __restrict__ y, int64_t n) {
+  pdl_wait_and_release();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     y[i] = y[i] + __ldg(a + i);
@@ -314,7 +321,7 @@ static void launch_dense_tt(const float* x, int64_t T, const void* w, int64_t ou
   const int64_t kchunk = (steps + ks - 1) / ks * 256;
   const int64_t per_cta = (8 / ks) * R;
   const dim3 grid((unsigned)((out + per_cta - 1) / per_cta), (unsigned)ttiles);
-  dense_f32_kernel<WF32, TT, R><<<grid, 256, 0, s>>>(x, T, w, out, in, ks, kchunk, y);
+  launch_pdl(dense_f32_kernel<WF32, TT, R>, grid, dim3(256), 0, s, x, T, w, out, in, ks, kchunk, y);
 }
 
 template <bool WF32>
@@ -361,7 +368,7 @@ static mr_status dense_run(mr_ctx* ctx, const float* x, int64_t T, const void* w
     uint16_t* xs = static_cast<uint16_t*>(ctx->ws);
     const int64_t n = T * in;
     const int pg = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
-    split3_kernel<<<pg, 256, 0, s>>>(x, n, xs);
+    launch_pdl(split3_kernel, dim3(pg), dim3(256), 0, s, x, n, xs);
     // K slices: about 24 warps per SM over the 16-row groups, at most 8
     const int64_t rgroups = (out + 15) / 16;
     int ks = 1;
@@ -370,8 +377,8 @@ static mr_status dense_run(mr_ctx* ctx, const float* x, int64_t T, const void* w
     const int64_t kchunk = (steps + ks - 1) / ks * 32;
     const int64_t per_cta = (8 / ks) * 16;
     const dim3 grid((unsigned)((out + per_cta - 1) / per_cta), (unsigned)((T + 7) / 8));
-    dense_tc_kernel<<<grid, 256, 0, s>>>(xs, T, static_cast<const uint16_t*>(w), out, in, ks,
-                                         kchunk, y);
+    launch_pdl(dense_tc_kernel, grid, dim3(256), 0, s, static_cast<const uint16_t*>(xs), T,
+               static_cast<const uint16_t*>(w), out, in, ks, kchunk, y);
     return cuda_check(ctx, cudaGetLastError(), "dense_tc_kernel");
   }
   const cudaError_t e = dt == MR_DTYPE_F32
@@ -502,7 +509,7 @@ static mr_status situ_run(mr_ctx* ctx, const float* g, const float* u, int64_t l
                           int64_t d, float beta, float lb, float* out, cudaStream_t s) {
   const int64_t n = rows * d;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8 * ctx->sm_count));
-  situ_kernel<<<grid, 256, 0, s>>>(g, u, ld, rows, d, beta, lb, out);
+  launch_pdl(situ_kernel, dim3(grid), dim3(256), 0, s, g, u, ld, rows, d, beta, lb, out);
   return cuda_check(ctx, cudaGetLastError(), "situ_kernel");
 }
 
@@ -607,15 +614,18 @@ mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int
     const int nchunk = (int)((Lt + 255) / 256);
     const dim3 grid((unsigned)T, (unsigned)nchunk);
     const bool norm = L->routed_norm != nullptr;
-    slot_sum_kernel<<<grid, 256, 0, s>>>(F(o_eo), wts, (int)k, Lt, norm ? F(o_ssum) : F(o_rs),
-                                         norm ? F(o_part) : nullptr);
+    launch_pdl(slot_sum_kernel, grid, dim3(256), 0, s, static_cast<const float*>(F(o_eo)),
+               static_cast<const float*>(wts), (int)k, Lt, norm ? F(o_ssum) : F(o_rs),
+               norm ? F(o_part) : nullptr);
     if (norm) {
       if (L->norm_dtype == MR_DTYPE_F32)
-        norm_kernel<true><<<grid, 256, 0, s>>>(F(o_ssum), F(o_part), nchunk, Lt, L->routed_norm,
-                                               L->rms_eps, F(o_rs));
+        launch_pdl(norm_kernel<true>, grid, dim3(256), 0, s, static_cast<const float*>(F(o_ssum)),
+                   static_cast<const float*>(F(o_part)), nchunk, Lt, L->routed_norm, L->rms_eps,
+                   F(o_rs));
       else
-        norm_kernel<false><<<grid, 256, 0, s>>>(F(o_ssum), F(o_part), nchunk, Lt,
-                                                L->routed_norm, L->rms_eps, F(o_rs));
+        launch_pdl(norm_kernel<false>, grid, dim3(256), 0, s,
+                   static_cast<const float*>(F(o_ssum)), static_cast<const float*>(F(o_part)),
+                   nchunk, Lt, L->routed_norm, L->rms_eps, F(o_rs));
     }
     if ((st = cuda_check(ctx, cudaGetLastError(), "slot sum / norm"))) return st;
   }
@@ -630,7 +640,7 @@ mr_status mr_k3_moe_forward(mr_ctx* ctx, const mr_k3_moe* L, const float* x, int
       return st;
     const int64_t n = T * H;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
-    add_f32_kernel<<<grid, 256, 0, s>>>(F(o_ru), out, n);
+    launch_pdl(add_f32_kernel, dim3(grid), dim3(256), 0, s, static_cast<const float*>(F(o_ru)), out, n);
     return cuda_check(ctx, cudaGetLastError(), "add_f32_kernel");
   }
   return project(ctx, &L->routed_up, F(o_rs), T, out, s);

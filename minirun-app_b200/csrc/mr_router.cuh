@@ -164,6 +164,7 @@ MR_DEVICE void prep_mx_chunk(const PrepMxParams& p, int64_t chunk, bool valid) {
 }
 
 __global__ void prep_mx_kernel(const PrepMxParams p) {
+  pdl_wait_and_release();
   const int64_t n = p.rows * (p.in / 16);
   const int64_t n_round = (n + 31) / 32 * 32;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -375,11 +376,15 @@ __device__ void build_plan_cta(const PlanParams& p) {
   }
 }
 
-__global__ void __launch_bounds__(256) plan_kernel(const PlanParams p) { build_plan_cta<256>(p); }
+__global__ void __launch_bounds__(256) plan_kernel(const PlanParams p) {
+  pdl_wait_and_release();
+  build_plan_cta<256>(p);
+}
 
 // Dense affineMM plan: one expert (0), columns = tokens.
 __global__ void dense_plan_kernel(int T, int seg_cols, int* n_segments, int4* segments,
                                   int* cols) {
+  pdl_wait_and_release();
   const int nseg = (T + seg_cols - 1) / seg_cols;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < T; i += gridDim.x * blockDim.x) {
     cols[i] = i;
