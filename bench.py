@@ -83,6 +83,20 @@ def parse():
                    help="measure only the config-4 cached decode line")
     p.add_argument("--k3-only", action="store_true",
                    help="measure only the K3 latent-MoE layer (profiling driver)")
+    p.add_argument("--strong-tokens", type=int, default=64,
+                   help="global batch of the strong-scaling line (64 / N tokens per GPU)")
+    p.add_argument("--no-parity", action="store_true",
+                   help="skip the in-run correctness check (oracle / one-GPU comparison)")
+    p.add_argument("--parity-tokens", type=int, default=4,
+                   help="tokens of every rank's batch checked against the CPU oracle")
+    p.add_argument("--config2-tokens", type=int, default=64,
+                   help="config-2 sub-line (2-/8-bit, 384 experts) at this global batch "
+                        "(0 = skip)")
+    p.add_argument("--config4-layers", type=int, default=8,
+                   help="config-4 sub-line: budgeted decode through this many layers, budget "
+                        "scaled from 40 GB for 58 layers (0 = skip)")
+    p.add_argument("--config4-budget-gb", type=float, default=0.0,
+                   help="config-4 sub-line budget (0 = 40 GB * layers / 58)")
     return p.parse_args()
 
 
@@ -199,7 +213,11 @@ def run_ours(args, world, rank, local):
     layers = [S.synth_layer(spec, layer=l, device=local, shard=(rank, world) if ep else None)
               for l in range(NL)]
     NB = NL + 1
+    # strong scaling: 64 tokens in the global batch whatever N is (64 / N per rank)
+    Ts = args.strong_tokens // world if args.strong_tokens % world == 0 else 0
     token_counts = [T] + [int(t) for t in args.sweep.split(",") if t and int(t) != T]
+    if Ts and Ts not in token_counts:
+        token_counts.append(Ts)
 
     def xrows(t, b):
         full = S.synth_x(spec, t * world, layer=0, batch=b, device=local)
@@ -229,6 +247,13 @@ def run_ours(args, world, rank, local):
     def schedule(i):
         return layers[i % NL], i % NB
 
+    def max_over_ranks(v):
+        if world > 1:
+            t = torch.tensor([v], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            v = float(t.item())
+        return v
+
     def timed(tok, steps, warm):
         outs = torch.empty((tok, spec.hidden), dtype=torch.bfloat16, device=dev)
         for i in range(warm):
@@ -237,21 +262,16 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         barrier()
         st = torch.cuda.current_stream()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(st)
+        a = torch.cuda.Event(enable_timing=True)
+        z = torch.cuda.Event(enable_timing=True)
+        a.record(st)
         for i in range(steps):
             lay, b = schedule(i)
             step(lay, xs[tok][b], outs)
-        e1.record(st)
+        z.record(st)
         torch.cuda.synchronize()
         barrier()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return max_over_ranks(a.elapsed_time(z))
 
     def distinct_experts(tok, steps):
         """Distinct routed experts this GPU streams per step (its own range,
@@ -280,6 +300,19 @@ def run_ours(args, world, rank, local):
 
     hbm, peak_kind = peaks()
     K, W = args.steps, max(3, args.warmup)
+
+    def phases(tok):
+        """Per-step device time of each kernel class (CUDA events around each
+        launch on the launching stream, max over ranks), and the gate/up
+        roofline of this GPU's share."""
+        ctx.profile(True)
+        timed(tok, K, 0)
+        prof = ctx.profile_read()
+        ctx.profile(False)
+        per = {k: {"ms_per_step": max_over_ranks(v[0] / K), "launches_per_step": v[1] / K}
+               for k, v in prof.items() if v[1]}
+        return prof, per
+
     with ClockSampler(local) as clk:
         ms = timed(T, K, W)
     clocks = clk.summary()
@@ -289,10 +322,7 @@ def run_ours(args, world, rank, local):
     value = world * T * K / (ms / 1e3)
 
     # per-kernel durations (CUDA events around each launch, same stream)
-    ctx.profile(True)
-    timed(T, K, 0)
-    prof = ctx.profile_read()
-    ctx.profile(False)
+    prof, per_phase = phases(T)
     # gate/up time per step (expert-parallel steps launch it twice: the
     # rank's routed experts, then the shared expert) against its bytes per step
     gu_ms, gu_n = prof["gate_up"]
@@ -314,12 +344,67 @@ def run_ours(args, world, rank, local):
                            "layer_frac_of_hbm": b2 / (m2 / K / 1e3) / 1e9 / hbm,
                            "distinct_experts_avg": sum(u2) / len(u2)}
 
+    # strong scaling: the same 64-token global batch on N GPUs, with its
+    # per-phase split and, at N > 1, a one-GPU run of the whole layer on rank 0
+    # in this same job (the speed-up is measured, not inferred across runs)
+    strong = None
+    full_layers = None
+    if Ts:
+        sw = sweep.get(str(Ts)) if Ts != T else {"tokens_per_s": value, "ms_per_step": ms_step,
+                                                 "distinct_experts_avg": sum(us) / len(us)}
+        sprof, sper = phases(Ts) if Ts != T else (prof, per_phase)
+        su = distinct_experts(Ts, K) if Ts != T else us
+        sgu = sum(gate_up_bytes(Ts, u) for u in su) / len(su)
+        s_gu_ms = max_over_ranks(sprof["gate_up"][0] / K)
+        strong = {"global_tokens": args.strong_tokens, "tokens_per_rank": Ts,
+                  "tokens_per_s": sw["tokens_per_s"], "ms_per_step": sw["ms_per_step"],
+                  "distinct_experts_per_gpu_avg": sum(su) / len(su),
+                  "gate_up_frac_of_hbm_per_gpu": sgu / (s_gu_ms / 1e3) / 1e9 / hbm,
+                  "phases_ms_per_step": {k: v["ms_per_step"] for k, v in sper.items()}}
+        if world > 1:
+            one = None
+            if rank == 0:
+                full_layers = [S.synth_layer(spec, layer=l, device=local) for l in range(NL)]
+                x1 = [S.synth_x(spec, args.strong_tokens, layer=0, batch=b, device=local)
+                      for b in range(NB)]
+                o1 = torch.empty((args.strong_tokens, spec.hidden), dtype=torch.bfloat16,
+                                 device=dev)
+                for i in range(W):
+                    full_layers[i % NL].forward(x1[i % NB], out=o1, selection=False)
+                torch.cuda.synchronize()
+                a = torch.cuda.Event(enable_timing=True)
+                z = torch.cuda.Event(enable_timing=True)
+                a.record()
+                for i in range(K):
+                    full_layers[i % NL].forward(x1[i % NB], out=o1, selection=False)
+                z.record()
+                torch.cuda.synchronize()
+                one = args.strong_tokens * K / (a.elapsed_time(z) / 1e3)
+            barrier()
+            if rank == 0:
+                strong["one_gpu_tokens_per_s"] = one
+                strong["speedup_vs_one_gpu"] = strong["tokens_per_s"] / one
+
+    parity = parity_check(args, spec, S, M, torch, dist, world, rank, local, dev, layers,
+                          full_layers, step, xs, T) if not args.no_parity else None
+    if full_layers is not None:
+        del full_layers
+        torch.cuda.empty_cache()
+
     prefill = None
     if not ep and args.prefill_tokens > 0:
         prefill = prefill_run(args, S, M, torch, ctx, local, dev)
     k3 = None
     if not ep and args.k3_tokens:
         k3 = k3_run(args, M, torch, dev, hbm)
+    config2 = None
+    if args.config == "1" and args.config2_tokens > 0:
+        config2 = config2_run(args, S, M, torch, dist, world, rank, local, dev, group, hbm,
+                              max_over_ranks, barrier)
+    config4 = None
+    if not ep and args.config4_layers > 0 and args.config == "1":
+        config4 = cache_run(args, M, S, torch, dev, layers_n=args.config4_layers,
+                            budget_gb=args.config4_budget_gb, check_identity=True)
 
     e2e = e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local,
                   group if ep else None)
@@ -364,9 +449,13 @@ def run_ours(args, world, rank, local):
             "layer_gbs": avg_bytes / (ms_step / 1e3) / 1e9,
             "layer_frac_of_hbm": avg_bytes / (ms_step / 1e3) / 1e9 / hbm,
             "kernels": kern,
+            "phases_ms_per_step": {k: v["ms_per_step"] for k, v in per_phase.items()},
             "sweep": sweep,
+            "strong_T64": strong,
             "prefill": prefill,
             "k3_latent_moe": k3,
+            "config2": config2,
+            "config4": config4,
         },
         "roofline": {
             "bound": "hbm",
@@ -380,6 +469,7 @@ def run_ours(args, world, rank, local):
             "launches_per_step": gu_n / K,
             "traffic": traffic,
         },
+        "parity": parity,
         "e2e": e2e,
         "gpu_launches": K * (LAUNCHES_PER_STEP_EP if ep else LAUNCHES_PER_STEP),
         "clocks": clocks,
@@ -391,6 +481,152 @@ def run_ours(args, world, rank, local):
         dist.barrier()
         group.close()
         dist.destroy_process_group()
+
+
+def rel_l2(a, b):
+    import numpy as np
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def parity_check(args, spec, S, M, torch, dist, world, rank, local, dev, layers, full_layers,
+                 step, xs, T):
+    """Correctness of the measured configuration, checked in the same run.
+
+    vs_oracle: the first `--parity-tokens` tokens of every rank's batch (layer
+    0, batch 0 of the bench's inputs) against the CPU oracle: expert ids equal
+    as sets per token (a difference only where the oracle's margin shows a
+    tie below 1e-5) and the outputs within the 1e-2 relative-L2 bound.
+    vs_one_gpu (N > 1): the whole global batch of the expert-parallel step
+    against the one-GPU layer on rank 0: ids identical and outputs
+    bit-identical (fused path) or within 2e-3 (NCCL reduce-scatter path)."""
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+    out = torch.empty((T, spec.hidden), dtype=torch.bfloat16, device=dev)
+    ids = torch.empty((T, spec.top_k), dtype=torch.int32, device=dev)
+    step(layers[0], xs[T][0], out, ids)
+    torch.cuda.synchronize()
+    if world > 1:
+        outs = [torch.empty_like(out) for _ in range(world)]
+        idss = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(outs, out)
+        dist.all_gather(idss, ids)
+        gout, gids = torch.cat(outs), torch.cat(idss)
+    else:
+        gout, gids = out, ids
+    res = {"ok": True}
+    if rank == 0:
+        xg = S.synth_x(spec, T * world, layer=0, batch=0, device=local)
+        if world > 1:
+            fl = full_layers[0] if full_layers else S.synth_layer(spec, layer=0, device=local)
+            ref, sel = fl.forward(xg)
+            torch.cuda.synchronize()
+            same_ids = bool(torch.equal(torch.sort(sel.ids, 1)[0], torch.sort(gids, 1)[0]))
+            bit = bool(torch.equal(ref, gout))
+            err = rel_l2(gout.float().cpu().numpy(), ref.float().cpu().numpy())
+            ok = same_ids and (bit if not args.ep_nccl else err < 2e-3)
+            res["vs_one_gpu"] = {"tokens": T * world, "ids_equal": same_ids,
+                                 "bit_identical": bit, "rel_l2": err,
+                                 "bound": "bit-identical" if not args.ep_nccl else 2e-3,
+                                 "ok": ok}
+            res["ok"] = res["ok"] and ok
+            del fl
+        if args.config == "1" and args.parity_tokens > 0:
+            cfg = O.CONFIGS[1]
+            pick = sorted({r * T + j for r in range(world) for j in range(min(args.parity_tokens, T))})
+            xn = xg.cpu().view(torch.int16).numpy().view(np.uint16)[pick]
+            L = O.gen_layer(cfg, layer=0, experts=O.selected_experts(cfg, xn))
+            o_out, o_f, o_ids, o_w, o_m = O.moe_layer_forward(L, xn)
+            g = gout.cpu().view(torch.int16).numpy().view(np.uint16)[pick]
+            gi = gids.cpu().numpy()[pick]
+            flips, bad = 0, 0
+            for t in range(len(pick)):
+                if set(gi[t].tolist()) != set(o_ids[t].tolist()):
+                    if abs(o_m[t]) < 1e-5:
+                        flips += 1
+                    else:
+                        bad += 1
+            err = rel_l2(O.bf16_to_f32(g), o_f)
+            ok = bad == 0 and err < 1e-2
+            res["vs_oracle"] = {"tokens": len(pick), "token_rows": pick[:16],
+                                "ids_sets_equal": bad == 0 and flips == 0,
+                                "excused_tie_flips": flips, "unexcused_flips": bad,
+                                "rel_l2": err, "bound": 1e-2, "ok": ok}
+            res["ok"] = res["ok"] and ok
+    if world > 1:
+        dist.barrier()
+    return res if rank == 0 else None
+
+
+def config2_run(args, S, M, torch, dist, world, rank, local, dev, group, hbm, max_over_ranks,
+                barrier):
+    """Config 2: the wide layer (384 routed + 1 shared experts, 2-bit and
+    8-bit) at `--config2-tokens` global tokens; on N GPUs expert-parallel,
+    384 / N experts per GPU (48 at N = 8). Two resident layers alternate so
+    that consecutive steps stream different experts."""
+    out = {}
+    G = args.config2_tokens
+    if G % world:
+        return None
+    t = G // world
+    K, W = args.steps, max(3, args.warmup)
+    for name in ("2b2", "2b8"):
+        spec = S.CONFIGS[name]
+        ep = world > 1
+        lays = [S.synth_layer(spec, layer=l, device=local, shard=(rank, world) if ep else None)
+                for l in range(2)]
+        xb = [S.synth_x(spec, G, layer=0, batch=b, device=local)[rank * t:(rank + 1) * t]
+              .contiguous() for b in range(3)]
+        o = torch.empty((t, spec.hidden), dtype=torch.bfloat16, device=dev)
+        ids = torch.empty((t, spec.top_k), dtype=torch.int32, device=dev)
+
+        def fwd(i, want_ids=False):
+            lay, x = lays[i % 2], xb[i % 3]
+            if ep:
+                group.forward(lay, x, out=o, ids=ids if want_ids else None)
+            elif want_ids:
+                _, sel = lay.forward(x, out=o)
+                ids.copy_(sel.ids)
+            else:
+                lay.forward(x, out=o, selection=False)
+
+        for i in range(W):
+            fwd(i)
+        torch.cuda.synchronize()
+        barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        z = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(K):
+            fwd(i)
+        z.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(a.elapsed_time(z)) / K
+        e0, e1 = rank * spec.experts // world, (rank + 1) * spec.experts // world
+        us = []
+        for i in range(min(K, 6)):
+            fwd(i, True)
+            allids = ids
+            if ep:
+                parts = [torch.empty_like(ids) for _ in range(world)]
+                dist.all_gather(parts, ids)
+                allids = torch.cat(parts)
+            us.append(len({e for e in allids.cpu().view(-1).tolist() if e0 <= e < e1}))
+        U = sum(us) / len(us)
+        byt = (U + 1) * spec.expert_bytes() + spec.router_bytes() + 2 * t * spec.hidden * 2
+        out[name] = {"bits": spec.bits, "tokens_per_s": G / (ms / 1e3), "ms_per_step": ms,
+                     "experts_per_gpu": spec.experts // world,
+                     "distinct_experts_per_gpu_avg": U,
+                     "layer_gbs_per_gpu": byt / (ms / 1e3) / 1e9,
+                     "layer_frac_of_hbm_per_gpu": byt / (ms / 1e3) / 1e9 / hbm}
+        del lays, xb
+        torch.cuda.empty_cache()
+    return {"workload": f"config2 decode, {G} global tokens: H7168, 384+1 experts, top-8, "
+                        f"I2048, g64; {384 // world} routed experts per GPU",
+            "by_bits": out}
 
 
 def prefill_run(args, S, M, torch, ctx, local, dev):
@@ -503,27 +739,32 @@ def k3_run(args, M, torch, dev, hbm):
             "by_tokens": out}
 
 
-def cache_run(args, M, S, torch, dev):
-    """Config 4: one-token decode through `--cache-layers` config-1 layers whose
+def cache_run(args, M, S, torch, dev, layers_n=None, budget_gb=None, check_identity=False):
+    """Config 4: one-token decode through `layers_n` config-1 layers whose
     routed experts live in pinned host memory and reach the GPU through the
-    HBM expert cache (`mr_moe_layer_forward_cached`) under `--cache-budget-gb`.
+    HBM expert cache (`mr_moe_layer_forward_cached`) under `budget_gb`.
     Each layer has its own seeded router (and so its own routing); to keep
     host memory at one layer's 6.4 GB, every layer registers the same seeded
-    expert arrays under its own (layer, expert) keys, so the cache sees 58 x
-    256 distinct experts and copies each miss from host memory as it would
-    distinct weights. The shared expert stays resident. A step = one token
-    position through all layers, each layer routing a seeded token of its own:
-    with the BASELINE weight distributions (codes uniform, bias -8 * scale, so
-    every weight has mean -scale/2) a layer's output is dominated by one
-    common-mode direction, and chained layers would route every token to the
-    same experts. Independent tokens make the routing as diverse as random
-    choice, the hard case for the cache."""
+    expert arrays under its own (layer, expert) keys, so the cache sees
+    layers x 256 distinct experts and copies each miss from host memory as it
+    would distinct weights. The shared expert stays resident. A step = one
+    token position through all layers, each layer routing a seeded token of
+    its own: with the BASELINE weight distributions (codes uniform, bias
+    -8 * scale, so every weight has mean -scale/2) a layer's output is
+    dominated by one common-mode direction, and chained layers would route
+    every token to the same experts. Independent tokens make the routing as
+    diverse as random choice, the hard case for the cache.
+    With `check_identity`, the same tokens also run through a second cache
+    whose budget holds every expert (all resident after the first pass), and
+    the outputs of the timed steps must be byte-identical."""
     spec = S.CONFIGS[1]
-    NL = args.cache_layers
+    NL = layers_n if layers_n is not None else args.cache_layers
+    gb = budget_gb if budget_gb is not None else args.cache_budget_gb
+    if not gb:
+        gb = 40.0 * NL / 58.0  # the BASELINE resident fraction (40 GB of 58 layers)
     base = S.synth_layer(spec, layer=0, device=dev.index)
     E, H = spec.experts, spec.hidden
     slot = M.ExpertCache.slot_bytes_for(base.gate, base.up, base.down)
-    cache = M.ExpertCache(dev.index, int(args.cache_budget_gb * 1e9), slot)
     t0 = time.perf_counter()
     host = [tuple(tuple(t[e].contiguous().cpu().pin_memory() for t in (w.packed, w.scales,
                                                                         w.biases))
@@ -535,44 +776,63 @@ def cache_run(args, M, S, torch, dev):
                             1.0 / 32.0, False, rw)
         layers.append(M.CachedLayer(rw, base.router, H, spec.inter, spec.bits, spec.group,
                                     shared=base.shared))
-        for e in range(E):
-            cache.register(l, e, host[e])
+
+    def make_cache(budget_bytes):
+        c = M.ExpertCache(dev.index, int(budget_bytes), slot)
+        for l in range(NL):
+            for e in range(E):
+                c.register(l, e, host[e])
+        return c
+
+    cache = make_cache(gb * 1e9)
     setup_s = time.perf_counter() - t0
     steps = max(3, min(args.steps, 10))
     W = max(3, args.warmup)
     # a seeded token per (step, layer)
     xs = [[S.synth_x(spec, 1, layer=l, batch=i, device=dev.index) for l in range(NL)]
           for i in range(W + steps)]
-    out = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
+    outs = [[torch.empty((1, H), dtype=torch.bfloat16, device=dev) for _ in range(NL)]
+            for _ in range(W + steps)]
 
-    def token(i):
+    def token(c, i):
         for l, lay in enumerate(layers):
-            cache.forward(l, lay, xs[i][l], out=out)
+            c.forward(l, lay, xs[i][l], out=outs[i][l])
 
     for i in range(W):  # first fills of the cache
-        token(i)
+        token(cache, i)
     torch.cuda.synchronize()
     s0 = cache.stats()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     a.record()
     for i in range(W, W + steps):
-        token(i)
+        token(cache, i)
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / steps
     s1 = cache.stats()
     d = {k: s1[k] - s0[k] for k in ("hits", "misses", "bytes_copied") if k in s1}
     uses = d.get("hits", 0) + d.get("misses", 0)
+    slots = int(gb * 1e9) // slot
     cache.close()
+    identity = None
+    if check_identity:
+        got = [torch.cat(outs[i]).clone() for i in range(W, W + steps)]
+        big = make_cache(NL * E * slot + slot)  # every expert fits
+        for i in range(W + steps):
+            token(big, i)
+        torch.cuda.synchronize()
+        same = all(torch.equal(got[j], torch.cat(outs[W + j])) for j in range(steps))
+        big.close()
+        identity = {"vs_all_resident_budget_gb": (NL * E * slot + slot) / 1e9,
+                    "byte_identical": same}
     return {"workload": f"config4: {NL} config-1 layers, 1-token decode, {E} routed experts "
                         f"per layer in pinned host memory, HBM cache budget "
-                        f"{args.cache_budget_gb:g} GB ({int(args.cache_budget_gb * 1e9) // slot}"
-                        f" slots of {slot} B)",
+                        f"{gb:g} GB ({slots} slots of {slot} B)",
             "tokens_per_s": 1e3 / ms, "ms_per_token": ms, "steps": steps,
             "hit_rate": d.get("hits", 0) / max(uses, 1),
             "h2d_gbs": d.get("bytes_copied", 0) / steps / (ms / 1e3) / 1e9,
-            "setup_s": setup_s,
+            "setup_s": setup_s, "identity": identity,
             "note": "every layer registers the same seeded host arrays under its own keys"}
 
 
@@ -652,6 +912,7 @@ def cpu_baseline(T: int, steps: int = 1):
     """The CPU oracle (C, OpenMP, all host threads) on config 1 with T tokens."""
     sys.path.insert(0, ROOT)
     from oracle import oracle as O
+    O.set_num_threads(os.cpu_count() or 1)
     cfg = O.CONFIGS[1]
     x = O.gen_x(cfg, T, layer=0, batch=0)
     L = O.gen_layer(cfg, layer=0, experts=O.selected_experts(cfg, x))
@@ -673,6 +934,9 @@ def run_reference(args, world, rank, local):
         return
     sys.path.insert(0, ROOT)
     from oracle import oracle as O
+    # torchrun sets OMP_NUM_THREADS=1 for every rank; the reference arm runs
+    # on rank 0 alone and takes every host thread
+    O.set_num_threads(os.cpu_count() or 1)
     cfg = O.CONFIGS[1]
     T = args.tokens
     x = O.gen_x(cfg, T, layer=0, batch=0)

@@ -157,7 +157,10 @@ mr_status mr_affine_dequantize(mr_ctx* ctx, const mr_affine_desc* w, float* out,
  *     bytes plus the routing plan) does not fit are rejected with
  *     MR_ERR_UNSUPPORTED and the needed size in `msg`.
  *   - The first call on a device resolves the array's address on that device
- *     (no allocation); make that first call before any stream capture.
+ *     (no allocation); make that first call before any stream capture. The
+ *     address is kept for the life of the process: after cudaDeviceReset (or
+ *     any teardown of the device's primary context) this entry point must not
+ *     be called again in that process.
  *   - Every call on a device shares the one array and finds the previous
  *     call's contents in it: calls whose work overlaps on the GPU (other
  *     streams, other host threads) race and corrupt each other's results.
@@ -482,6 +485,17 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* la
  * A slot holds one expert's three projections; slots are reused least
  * recently used first. Host arrays should be pinned (cudaHostAlloc /
  * cudaHostRegister) for the copies to be asynchronous. */
+/* Test hook, with no counterpart in the reference: runs the home-rank
+ * wait-and-combine kernel of the fused expert-parallel path over `tokens`
+ * zero rows of width `hidden`, against an epoch flag that nothing publishes,
+ * polling at most `spin_limit` times (each poll followed by a ~128 ns sleep;
+ * 0 < spin_limit <= 2^22, the kernels' own limit). The wait expires: the
+ * kernel sets MR_DEVERR_TIMEOUT (read by mr_ctx_check) and writes zeros to
+ * out [tokens, hidden] bf16 instead of waiting on. It lets a test exercise the
+ * failure path of a bounded device wait on one GPU without a fault or hang. */
+mr_status mr_test_expire_ep_wait(mr_ctx* ctx, int64_t tokens, int64_t hidden,
+                                 uint32_t spin_limit, uint16_t* out, void* stream);
+
 typedef struct mr_cache mr_cache;
 
 /* One expert's three projections (gate, up, down) in host memory: the arrays
@@ -611,8 +625,10 @@ mr_status mr_cache_register_tiles(mr_cache* cache, int32_t layer, int32_t expert
 #define MR_KERNEL_ROUTER_LOGITS 0
 #define MR_KERNEL_TOPK_PLAN 1
 #define MR_KERNEL_GATE_UP 2
-#define MR_KERNEL_DOWN_COMBINE 3
-#define MR_KERNEL_CLASSES 4
+#define MR_KERNEL_DOWN_COMBINE 3 /* the down GEMV (+ fused peer stores under EP) */
+#define MR_KERNEL_EXCHANGE 4     /* expert parallel: NCCL token / partial exchange */
+#define MR_KERNEL_COMBINE 5      /* slot-ordered combine (+ the EP wait / partial sums) */
+#define MR_KERNEL_CLASSES 6
 
 mr_status mr_ctx_profile(mr_ctx* ctx, int enable);
 /* Wait for the recorded launches, then return per class the accumulated

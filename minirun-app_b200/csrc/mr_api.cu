@@ -531,6 +531,8 @@ mr_status mr_ctx_check(mr_ctx* ctx, void* stream, uint32_t* bits_out) {
     if (bits & MR_DEVERR_BAD_EXPERT_ID) m += " (expert id out of range)";
     if (bits & MR_DEVERR_NONFINITE_SCORE) m += " (non-finite router score)";
     if (bits & MR_DEVERR_RENORM_ZERO) m += " (selected router scores cannot be normalized)";
+    if (bits & MR_DEVERR_TIMEOUT) m += " (a bounded device wait expired)";
+    if (bits & MR_DEVERR_BAD_TOKEN_ID) m += " (token id outside the hash table)";
     return fail(ctx, MR_ERR_DEVICE, m);
   }
   return MR_OK;
@@ -1577,6 +1579,7 @@ static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   if ((st = run_experts(ctx, L, r, s))) return st;
   const int64_t n_out = T * H;
   const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 4 * ctx->sm_count));
+  ProfScope pc(ctx, MR_KERNEL_COMBINE, s);
   return cuda_check(ctx,
                     launch_pdl(combine_kernel, cgrid, 256, 0, s, (const float*)part2,
                                (const float*)wts, (int)T, k, H,
@@ -1977,6 +1980,7 @@ struct NcclApi {
   decltype(&ncclCommDestroy) comm_destroy = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
   decltype(&ncclReduceScatter) reduce_scatter = nullptr;
+  decltype(&ncclAllReduce) all_reduce = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
   bool ok = false;
 };
@@ -1994,10 +1998,11 @@ const NcclApi& nccl_api() {
     api.all_gather = reinterpret_cast<decltype(&ncclAllGather)>(dlsym(h, "ncclAllGather"));
     api.reduce_scatter =
         reinterpret_cast<decltype(&ncclReduceScatter)>(dlsym(h, "ncclReduceScatter"));
+    api.all_reduce = reinterpret_cast<decltype(&ncclAllReduce)>(dlsym(h, "ncclAllReduce"));
     api.error_string =
         reinterpret_cast<decltype(&ncclGetErrorString)>(dlsym(h, "ncclGetErrorString"));
     api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_gather &&
-             api.reduce_scatter && api.error_string;
+             api.reduce_scatter && api.all_reduce && api.error_string;
   });
   return api;
 }
@@ -2056,14 +2061,15 @@ __global__ void ep_wait_combine_kernel(const float* __restrict__ part,
                                        const float* __restrict__ weights, int T, int k,
                                        int64_t H, int weight_after_down, int has_shared,
                                        const unsigned* flags, int world, unsigned epoch,
-                                       unsigned* error, uint16_t* __restrict__ out) {
+                                       uint32_t spin_limit, unsigned* error,
+                                       uint16_t* __restrict__ out) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     ok = 1;
     for (int j = 0; j < world && ok; ++j) {
       uint32_t i = 0;
       while (ld_acquire_sys(flags + j) < epoch) {
-        if (++i >= kSpinLimit) {
+        if (++i >= spin_limit) {
           atomicOr(error, MR_DEVERR_TIMEOUT);
           ok = 0;
           break;
@@ -2106,7 +2112,8 @@ struct mr_ep {
   // fused path: this rank's receive buffer (flags | partials), mapped by
   // every rank through CUDA IPC; device tables of every rank's pointers
   bool fused = true;
-  void* buf = nullptr;       // [256 B of flags][partials]
+  void* buf = nullptr;       // [256 B of flags: one word per rank, W <= 64][partials]
+  bool peer_failed = false;  // some rank could not map a peer buffer: NCCL path
   size_t buf_bytes = 0;
   std::vector<void*> opened;  // peers' buffers opened here
   float** d_parts = nullptr;  // [world]
@@ -2224,17 +2231,46 @@ static mr_status ep_peer_setup(mr_ctx* ctx, mr_ep* ep, size_t need, cudaStream_t
   cleanup();
   if (st) return st;
   std::vector<void*> bases(W);
-  for (int j = 0; j < W; ++j) {
+  int open_failed = 0;
+  for (int j = 0; j < W && !open_failed; ++j) {
     if (j == ep->rank) {
       bases[j] = ep->buf;
       continue;
     }
     void* p = nullptr;
-    if ((st = cuda_check(ctx, cudaIpcOpenMemHandle(&p, all[j], cudaIpcMemLazyEnablePeerAccess),
-                         "cudaIpcOpenMemHandle")))
-      return st;
+    if (cudaIpcOpenMemHandle(&p, all[j], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      (void)cudaGetLastError();
+      open_failed = 1;
+      break;
+    }
     ep->opened.push_back(p);
     bases[j] = p;
+  }
+  // every rank learns whether any rank could not map a peer (e.g. ranks on
+  // different nodes): then all of them take the NCCL path, in step
+  {
+    int* flag = nullptr;
+    if ((st = cuda_check(ctx, cudaMalloc(&flag, sizeof(int)), "cudaMalloc(open flag)"))) return st;
+    int any = 0;
+    if ((st = cuda_check(ctx, cudaMemcpy(flag, &open_failed, sizeof(int), cudaMemcpyHostToDevice),
+                         "stage open flag")) ||
+        (st = nccl_check(ctx, nccl_api().all_reduce(flag, flag, 1, ncclInt32, ncclMax, ep->comm, s),
+                         "ncclAllReduce(open flag)")) ||
+        (st = cuda_check(ctx, cudaMemcpyAsync(&any, flag, sizeof(int), cudaMemcpyDeviceToHost, s),
+                         "read open flag")) ||
+        (st = cuda_check(ctx, cudaStreamSynchronize(s), "sync"))) {
+      cudaFree(flag);
+      return st;
+    }
+    cudaFree(flag);
+    if (any) {
+      for (void* q : ep->opened) cudaIpcCloseMemHandle(q);
+      ep->opened.clear();
+      cudaFree(ep->buf);
+      ep->buf = nullptr;
+      ep->peer_failed = true;
+      return MR_OK;
+    }
   }
   // device tables: part pointers, flag pointers, the done counter
   std::vector<uint64_t> tab(2 * W + 1, 0);
@@ -2326,9 +2362,12 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
   const NcclApi& api = nccl_api();
 
   // every rank's tokens, in rank order
-  if ((st = nccl_check(ctx, api.all_gather(x, xall, (size_t)(T * H), ncclBfloat16, ep->comm, s),
-                       "ncclAllGather")))
-    return st;
+  {
+    ProfScope ps(ctx, MR_KERNEL_EXCHANGE, s);
+    if ((st = nccl_check(ctx, api.all_gather(x, xall, (size_t)(T * H), ncclBfloat16, ep->comm, s),
+                         "ncclAllGather")))
+      return st;
+  }
   // router over all tokens (the same on every rank); plan of this rank's experts
   const RoutePlan rp{nseg, segs, cols, seg_cols, base, El, true};
   if ((st = route_tokens(ctx, L, xall, NT, ls, part, xperm, xsum, ids, wts, nullptr, rp, s)))
@@ -2351,14 +2390,28 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
   r.hsum = hsum;
   r.part2 = part2;
   const int wad = L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0;
-  const bool fused = ep->fused && W > 1 &&
-                     use_tma(ctx, tma_layout_ok(I, &L->down, false) &&
-                                      (!has_shared || tma_layout_ok(I, &L->shared_down, false)));
+  // the flag area of a receive buffer holds one word per rank (256 B)
+  bool fused = ep->fused && W > 1 && W <= 64 && !ep->peer_failed &&
+               use_tma(ctx, tma_layout_ok(I, &L->down, false) &&
+                                (!has_shared || tma_layout_ok(I, &L->shared_down, false)));
   if (fused) {
-    // routed partials straight into their home ranks' buffers over NVLink,
-    // then the one-GPU combine on each home rank
+    // collective: the same decision on every rank (same shapes, and a failed
+    // peer mapping on any rank is agreed on inside)
     const int64_t Tk = T * k, rows = Tk + (has_shared ? 2 * T : 0);
     if ((st = ep_peer_setup(ctx, ep, 256 + (size_t)rows * H * sizeof(float), s))) return st;
+    fused = !ep->peer_failed;
+  }
+  if (fused) {
+    // routed partials straight into their home ranks' buffers over NVLink,
+    // then the one-GPU combine on each home rank.
+    // Cross-step ordering: a peer's down GEMV of step e+1 must not store into
+    // this rank's buffer before this rank's wait-and-combine of step e has
+    // read it. What orders them is the NCCL all-gather of the tokens at the
+    // start of every forward, on this same stream: no rank starts step e+1's
+    // GEMVs before every rank has enqueued (and, through the collective,
+    // reached) the all-gather, which follows its step-e combine. Skipping that
+    // all-gather or moving it to another stream would need another barrier.
+    const int64_t Tk = T * k;
     ++ep->epoch;
     GemvParams peer{};
     peer.peer_part = ep->d_parts;
@@ -2394,24 +2447,29 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
     }
     const int64_t n = T * H;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
+    ProfScope pc(ctx, MR_KERNEL_COMBINE, s);
     ep_wait_combine_kernel<<<grid, 256, 0, s>>>(
         mine, wts + (int64_t)rank * Tk, (int)T, k, H, wad, has_shared ? 1 : 0,
-        static_cast<const unsigned*>(ep->buf), W, ep->epoch, ctx->d_error, out);
+        static_cast<const unsigned*>(ep->buf), W, ep->epoch, kSpinLimit, ctx->d_error, out);
     if ((st = cuda_check(ctx, cudaGetLastError(), "ep_wait_combine_kernel"))) return st;
   } else {  // NCCL: per-token local sums, reduce-scatter to the home ranks
     if ((st = run_experts(ctx, L, r, s))) return st;
     {
       const int64_t n = NT * H;
       const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
+      ProfScope pc(ctx, MR_KERNEL_COMBINE, s);
       ep_partial_kernel<<<grid, 256, 0, s>>>(part2, ids, wts, (int)NT, k, H, base, El, wad, ypart);
       if ((st = cuda_check(ctx, cudaGetLastError(), "ep_partial_kernel"))) return st;
     }
     // each token's sum over all ranks, back on its home rank
-    if ((st = nccl_check(ctx,
-                         api.reduce_scatter(ypart, yred, (size_t)(T * H), ncclFloat32, ncclSum,
-                                            ep->comm, s),
-                         "ncclReduceScatter")))
-      return st;
+    {
+      ProfScope px(ctx, MR_KERNEL_EXCHANGE, s);
+      if ((st = nccl_check(ctx,
+                           api.reduce_scatter(ypart, yred, (size_t)(T * H), ncclFloat32, ncclSum,
+                                              ep->comm, s),
+                           "ncclReduceScatter")))
+        return st;
+    }
     // shared expert over this rank's own tokens
     if (has_shared) {
       if ((st = cuda_check(ctx, cudaMemsetAsync(zero, 0, 4 * sizeof(int), s), "clear count")))
@@ -2437,6 +2495,7 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
     {
       const int64_t n = T * H;
       const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
+      ProfScope pc(ctx, MR_KERNEL_COMBINE, s);
       ep_combine_kernel<<<grid, 256, 0, s>>>(yred, psh, (int)T, H, wad, has_shared ? 1 : 0, out);
       if ((st = cuda_check(ctx, cudaGetLastError(), "ep_combine_kernel"))) return st;
     }
@@ -2450,6 +2509,39 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
 }
 
 }  // extern "C"
+
+// ------------------------------------------------- bounded-wait test hook
+
+extern "C" mr_status mr_test_expire_ep_wait(mr_ctx* ctx, int64_t tokens, int64_t hidden,
+                                            uint32_t spin_limit, uint16_t* out, void* stream) {
+  if (!ctx) return MR_ERR_INVALID_ARGUMENT;
+  if (tokens <= 0 || hidden <= 0 || !out || spin_limit == 0 || spin_limit > kSpinLimit)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "tokens, hidden > 0, out non-NULL and 0 < spin_limit <= the kernels' own limit");
+  // workspace: one flag word (zero: no rank ever publishes), zeroed partial
+  // rows and routing weights of a one-slot layer without a shared expert
+  Bump b{nullptr};
+  unsigned* flags = nullptr;
+  float *part = nullptr, *wts = nullptr;
+  mr_status st;
+  for (int pass = 0; pass < 2; ++pass) {
+    b.off = 0;
+    flags = b.take<unsigned>(64);
+    part = b.take<float>(tokens * hidden);
+    wts = b.take<float>(tokens);
+    if (pass == 0) {
+      if ((st = ensure_workspace(ctx, b.off))) return st;
+      b.base = reinterpret_cast<char*>(ctx->ws);
+    }
+  }
+  cudaStream_t s = as_stream(stream);
+  if ((st = cuda_check(ctx, cudaMemsetAsync(ctx->ws, 0, b.off, s), "clear workspace"))) return st;
+  const int64_t n = tokens * hidden;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
+  ep_wait_combine_kernel<<<grid, 256, 0, s>>>(part, wts, (int)tokens, 1, hidden, 0, 0, flags, 1,
+                                              1u, spin_limit, ctx->d_error, out);
+  return cuda_check(ctx, cudaGetLastError(), "ep_wait_combine_kernel");
+}
 
 // ----------------------------------------------------------- expert cache
 

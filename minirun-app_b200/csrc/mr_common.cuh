@@ -302,8 +302,8 @@ struct mr_ctx {
   bool profiling = false;
   std::vector<Pending> pending;
   std::vector<cudaEvent_t> event_pool;
-  double prof_ms[MR_KERNEL_CLASSES] = {0, 0, 0, 0};
-  int64_t prof_n[MR_KERNEL_CLASSES] = {0, 0, 0, 0};
+  double prof_ms[MR_KERNEL_CLASSES] = {};
+  int64_t prof_n[MR_KERNEL_CLASSES] = {};
 };
 
 namespace mr {

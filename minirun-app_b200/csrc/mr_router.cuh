@@ -142,7 +142,11 @@ MR_DEVICE void prep_mx_chunk(const PrepMxParams& p, int64_t chunk, bool valid) {
     const float v = ldexpf(f[i], -k);
     const __half h = __float2half_rn(v);
     o[i] = __half_as_ushort(h);
-    ol[i] = __half_as_ushort(__float2half_rn(v - __half2float(h)));
+    // bf16 input: the low term is zero, so the two-column form (taken when
+    // experts average <= 2 columns) gives exactly the one-column result and a
+    // token's output does not depend on the batch size; the residual of the
+    // f16 subnormal tail (below 2^-31 of the half's maximum) is dropped in both
+    ol[i] = p.xf ? __half_as_ushort(__float2half_rn(v - __half2float(h))) : (uint16_t)0;
   }
   if (valid) {
     const int xs = split ? 2 : 1;

@@ -93,7 +93,8 @@ class Context:
         self.check("mr_ctx_set_kernel_path", L.load().mr_ctx_set_kernel_path(
             self.handle, self.KERNEL_PATHS[path]))
 
-    KERNEL_CLASSES = ("router_logits", "topk_plan", "gate_up", "down_combine")
+    KERNEL_CLASSES = ("router_logits", "topk_plan", "gate_up", "down_combine", "exchange",
+                      "combine")
 
     def profile(self, enable: bool) -> None:
         self.check("mr_ctx_profile", L.load().mr_ctx_profile(self.handle, int(enable)))

@@ -17,6 +17,7 @@ reinterpreted (viewed), never converted.
 from __future__ import annotations
 
 import json
+import math
 import os
 from dataclasses import dataclass
 
@@ -96,7 +97,8 @@ class SafetensorsFile:
             item = ITEM_SIZE.get(ent["dtype"])
             if item is None:
                 raise SafetensorsError(f"tensor '{name}' has unsupported dtype {ent['dtype']}")
-            need = int(np.prod(shape, dtype=np.int64)) * item if shape else item
+            # Python ints: a crafted shape cannot wrap to a small byte count
+            need = math.prod(shape) * item
             if end - begin != need:
                 raise SafetensorsError(
                     f"tensor '{name}' spans {end - begin} bytes, but shape {list(shape)} at "

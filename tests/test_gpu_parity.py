@@ -70,9 +70,14 @@ def rel_l2(a, b):
 
 
 def assert_ids_match(gpu_ids, ref_ids, ref_margins):
+    """Ids equal as sets per token; returns the number of tokens whose set
+    differs at an oracle margin below TIE_MARGIN (excused ties)."""
+    flips = 0
     for t in range(ref_ids.shape[0]):
         if set(gpu_ids[t].tolist()) != set(ref_ids[t].tolist()):
             assert abs(ref_margins[t]) < TIE_MARGIN, (t, gpu_ids[t], ref_ids[t], ref_margins[t])
+            flips += 1
+    return flips
 
 
 # ------------------------------------------------------------------ affine ops
@@ -250,6 +255,32 @@ def test_layer_config1_matches_oracle(T, kernel_path):
     assert_ids_match(sel.ids.cpu().numpy(), ids, m)
     err = rel_l2(O.bf16_to_f32(n_u16(gout)), f)
     assert err < 5e-3, err
+    M.Context.get(0).sync_check()
+
+
+def test_layer_config1_T64_matches_oracle():
+    """The headline configuration itself: config 1 at T = 64 (all 64 tokens,
+    ~230 distinct experts) on the default kernels against the oracle. Ids
+    equal as sets per token; the tokens excused at a tie are counted and
+    printed, and may only be the tokens whose oracle margin is below 1e-5."""
+    cfg = O.CONFIGS[1]
+    x = O.gen_x(cfg, 64, batch=64)
+    L = O.gen_layer(cfg, experts=O.selected_experts(cfg, x))
+    out, f, ids, w, m = O.moe_layer_forward(L, x)
+    layer = S.synth_layer(S.CONFIGS[1])
+    gout, sel = layer(t_u16(x))
+    gids = sel.ids.cpu().numpy()
+    flips = assert_ids_match(gids, ids, m)
+    close = int(np.sum(np.abs(m) < TIE_MARGIN))
+    err = rel_l2(O.bf16_to_f32(n_u16(gout)), f)
+    print(f"config1 T=64: rel_l2={err:.3e} excused_flips={flips} "
+          f"tokens_with_margin_below_{TIE_MARGIN:g}={close}")
+    assert flips <= close
+    assert err < 5e-3, err
+    # tokens whose routing agrees are held to the same bound on their own rows
+    same = [t for t in range(64) if set(gids[t].tolist()) == set(ids[t].tolist())]
+    err_same = rel_l2(O.bf16_to_f32(n_u16(gout))[same], f[same])
+    assert err_same < 5e-3, err_same
     M.Context.get(0).sync_check()
 
 

@@ -113,6 +113,25 @@ def test_wide_dynamic_range_activations():
     assert np.all(err <= 1e-5 * bound + np.abs(reff) * 2.0 ** -8), float(np.max(err / bound))
 
 
+def test_batch_invariance_across_two_column_switch():
+    """bf16 gathers take the two-column form while experts average at most
+    two columns (Tk <= 2E) and the one-column form above. A token's output
+    is bit-identical either way, also when a 32-element half spans a wide
+    dynamic range (elements far below 2^-31 of the half's maximum fall into
+    the f16 subnormal tail of the scaled activation)."""
+    E, out, inn, k = 4, 128, 1024, 2
+    w = O.gen_mxfp4(53, E, out, inn)
+    rng = np.random.default_rng(11)
+    xf = rng.standard_normal((5, inn)).astype(np.float32) * 2.0 ** -40
+    xf[:, ::32] = rng.standard_normal((5, inn // 32)) * 64.0  # one large element per half
+    x = t_u16(O.f32_to_bf16(xf.astype(np.float32)))
+    ids = torch.from_numpy(rng.integers(0, E, size=(5, k)).astype(np.int32)).to(dev())
+    wd = to_dev(w)
+    small = M.mxfp4_gather_mm(x[:4], wd, ids[:4])  # Tk = 8 = 2E: two-column form
+    large = M.mxfp4_gather_mm(x, wd, ids)          # Tk = 10: one-column form
+    assert torch.equal(small, large[:4])
+
+
 def test_nan_exponent_poisons_its_row_only():
     E, out, inn = 2, 64, 512
     w = O.gen_mxfp4(61, E, out, inn)
