@@ -61,7 +61,8 @@ def parse():
                    help="routed experts (0 = config 1's 256); smaller values only for "
                         "profiling captures that must fit a few GB")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--kernel-path", choices=["auto", "register", "tma", "umma"], default="auto",
+    p.add_argument("--kernel-path", choices=["auto", "register", "tma", "umma", "v2"],
+                   default="auto",
                    help="dequant-GEMV implementation (mr_ctx_set_kernel_path)")
     p.add_argument("--prefill-tokens", type=int, default=4096,
                    help="config-3 prefill batch measured beside the decode line (0 = skip)")

@@ -89,11 +89,15 @@ const char* mr_last_error(const mr_ctx* ctx);
  * MR_ERR_DEVICE (and writes the bits to *bits_out if non-NULL) when set. */
 mr_status mr_ctx_check(mr_ctx* ctx, void* stream, uint32_t* bits_out);
 /* Selects the dequant-GEMV implementation (a tuning/testing knob; results
- * agree to fp32 summation order): 0 auto (= 2, the fastest for decode
- * batches), 1 register-streaming, 2 TMA-pipelined with mma.sync / FMA
+ * agree to fp32 summation order): 0 auto (= 4 for decode batches, the tcgen05
+ * grouped GEMM for prefill-size ones), 1 register-streaming, 2 TMA-pipelined
+ * with mma.sync / FMA and per-stage activation loads from global memory
  * (where in % 512 == 0 and scale/bias rows are 16-byte aligned), 3 tcgen05
- * (tensor-memory MMA; MoE layer only, elsewhere as 2). Each falls back to
- * the next simpler one where its layout conditions do not hold. */
+ * (tensor-memory MMA; MoE layer only, elsewhere as 2), 4 TMA-pipelined with
+ * the activations staged in shared memory beside the weights and up to two
+ * mma tiles per dequantised fragment (same layout conditions as 2). Each
+ * falls back to the next simpler one where its layout conditions do not
+ * hold. */
 mr_status mr_ctx_set_kernel_path(mr_ctx* ctx, int path);
 /* Pre-size the workspace for layers up to these sizes (graph capture needs
  * a workspace that will not grow). */

@@ -209,6 +209,17 @@ static bool use_tma(const mr_ctx* ctx, bool layout_ok) {
   return ctx->kernel_path != 1 && layout_ok;
 }
 
+// The staged-activation TMA kernel (gemv_v2_kernel) serves TMA-streamable
+// affine projections by default; path 2 forces the first TMA kernel.
+static bool use_v2(const mr_ctx* ctx) { return ctx->kernel_path == 0 || ctx->kernel_path == 4; }
+
+// Columns per decode segment: one 8-column mma tile, or two when the experts
+// average more than 8 columns and the staged kernel runs (it dequantises
+// each fragment once for both tiles; the other kernels re-read per tile).
+static int decode_seg_cols(const mr_ctx* ctx, int64_t Tk, int64_t E) {
+  return (use_v2(ctx) && Tk > 8 * E) ? 16 : pick_seg_cols(Tk);
+}
+
 // Activation rows of routed columns in plan order (tcgen05 layer path with
 // more than 16 tokens): xg[c] = x_perm[cols[c] / in_div], and its group sums.
 // Positions past the plan's valid columns may hold stale ids; rows outside
@@ -385,6 +396,11 @@ static cudaError_t run_gemv(mr_ctx* ctx, GemvParams g, int64_t max_segments, boo
       g.rb_count = (int)(epi == EPI_SWIGLU ? g.rows / 32 : (g.rows + kTmaRows - 1) / kTmaRows);
       const int64_t items = (max_segments + g.shared_segments) * g.rb_count;
       const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
+      if (use_v2(ctx)) {
+        g.dq_magic_lo = 0x43004300u;
+        g.dq_magic_hi = 0x45004500u;
+        return launch_v2(g, tm, bits, sd, epi, nt, grid, s);
+      }
       return launch_tma(g, tm, bits, sd, epi, nt, grid, s);
     }
     // no driver entry point / map refused: stream with the register kernel
@@ -668,7 +684,7 @@ static mr_status affine_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const 
   if (!dense && E > kMaxExperts)
     return fail(ctx, MR_ERR_UNSUPPORTED, "expert stacks larger than 1024 are not built here");
   const int64_t in = w->in_features;
-  const int seg_cols = pick_seg_cols(Tk);
+  const int seg_cols = decode_seg_cols(ctx, Tk, E);
   const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / seg_cols + 1;
 
   Bump b{nullptr};
@@ -739,8 +755,8 @@ static mr_status affine_common(mr_ctx* ctx, const uint16_t* x, int64_t T, const 
 
 mr_status mr_ctx_set_kernel_path(mr_ctx* ctx, int path) {
   if (!ctx) return MR_ERR_INVALID_ARGUMENT;
-  if (path < 0 || path > 3)
-    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "kernel path must be 0, 1, 2 or 3");
+  if (path < 0 || path > 4)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "kernel path must be 0, 1, 2, 3 or 4");
   ctx->kernel_path = path;
   return MR_OK;
 }
@@ -1537,7 +1553,7 @@ static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
     um = encode_umma(ctx, m1, EPI_SWIGLU, H, xa, ActSpec{xperm, T, xsum}, &um1) &&
          encode_umma(ctx, m2, EPI_PARTIAL, I, ActSpec{h, R, hsum}, ActSpec{h, R, hsum}, &um2);
   }
-  const int seg_cols = pf ? kPfN : um ? kUmN : pick_seg_cols(T);
+  const int seg_cols = pf ? kPfN : um ? kUmN : decode_seg_cols(ctx, Tk, E);
 
   // K0a + K0b: router logits (+ permuted input), top-k, routing plan
   {
@@ -2322,7 +2338,7 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
   const int64_t NT = T * W, NTk = NT * k;
   if (NTk > (int64_t)1 << 28) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
   const bool has_shared = L->shared_inter > 0;
-  const int seg_cols = pick_seg_cols(NT);
+  const int seg_cols = decode_seg_cols(ctx, NTk, E);
   const int64_t max_seg = std::min<int64_t>(El, NTk) + NTk / seg_cols + 1;
   const LogitsShape ls = logits_shape(ctx, NT, E, H);
 

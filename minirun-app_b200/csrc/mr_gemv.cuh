@@ -96,6 +96,11 @@ struct GemvParams {
   int weight_after_down;
   float swiglu_limit;
   int h_bits;             // SWIGLU: bits of the consumer (down projection)
+  // staged kernel: the bf16 magic words 0x43004300 (C = 128) and 0x45004500
+  // (2048), passed at run time so that the compiler keeps them in registers
+  // and (q & mask) | magic stays one three-input logic op per code pair
+  uint32_t dq_magic_lo;
+  uint32_t dq_magic_hi;
   int shared_lo_off;      // SWIGLU: shared lo row = hi row + shared_lo_off
   // combine (PARTIAL)
   unsigned* counters;

@@ -1,0 +1,652 @@
+// mr_gemv_v2.cuh — staged-activation form of the TMA dequant-GEMV (affine
+// 2/4/8-bit codes), the default decode kernel.
+//
+// Same work items, plan, weight pipeline and epilogues as gemv_tma_kernel
+// (mr_gemv_tma.cuh): one CTA per SM loops over items = (segment of <= 8*NT
+// columns sharing an expert) x (64 rows: 64 plain rows, or 32 gate + 32 up
+// rows for SwiGLU); a producer warp streams each item's packed codes and
+// scale/bias boxes with 2-D tensor TMA into an NST-deep shared-memory ring.
+// What changes is everything the consumers touch besides the codes:
+//
+//  - Activations. Besides the weight boxes, every stage slot holds the
+//    stage's 512 permuted activations of each of the item's columns and
+//    their group sums. The producer warp's 32 lanes copy them with 16-byte
+//    cp.async from the activation rows (x_perm / h, L2-resident) and attach
+//    their completion to the stage's "full" mbarrier (cp.async.mbarrier.
+//    arrive.noinc: 1 TMA arrival + 32 lane arrivals per phase). The
+//    consumers then read B fragments from shared memory (16-byte loads,
+//    bank-conflict-free with a 16-byte pad per column) instead of issuing
+//    dependent global loads at the start of each stage.
+//  - Columns. A segment holds up to NT mma tiles of 8 columns. Each A
+//    fragment (16 rows x 16 codes) is dequantised once and fed to all NT
+//    tiles, so an expert with 9-16 columns costs one dequantisation.
+//  - Loop. One path for every segment width (no single-column FMA path), the
+//    first mma of each group takes a zero accumulator, and per-stage scale
+//    unpacking happens once per warp.
+//
+// Dequantisation and fold are those of the other kernels: a LOP3 turns a code
+// pair into the bf16 pair (C + q) (C = 128, or 2048*hi + 128 + lo for 8-bit),
+// mma.m16n8k16 accumulates sum((C + q) * x) over one 64-element group in fp32
+// and the fold y += s*acc + (z - C*s)*sum(x) applies scale and bias, which is
+// sum((s*q + z)*x) up to fp32 rounding. The four K quarters of an item are
+// summed in a fixed order, so results are deterministic and independent of
+// the other columns of the batch.
+#pragma once
+
+#include "mr_gemv_tma.cuh"
+
+namespace mr {
+
+// 16-byte global -> shared copy (cp.async, L2 only), completion tracked by
+// the thread's later cp.async.mbarrier.arrive.
+MR_DEVICE void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// The executing thread's prior cp.async copies arrive on `bar` when they
+// complete (the arrival was counted in the barrier's initial count).
+MR_DEVICE void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+MR_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// D = A * B with a zero accumulator (the first k-step of a group).
+MR_DEVICE void mma_bf16_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+// Two consecutive scales (or biases) from shared memory as fp32, by plain
+// pointer load.
+template <int SD>
+MR_DEVICE void lds2_scales(float (&v)[2], const char* p) {
+  if constexpr (SD == MR_DTYPE_F32) {
+    const float2 f = *reinterpret_cast<const float2*>(p);
+    v[0] = f.x;
+    v[1] = f.y;
+  } else {
+    const uint32_t r = *reinterpret_cast<const uint32_t*>(p);
+    if constexpr (SD == MR_DTYPE_BF16) {
+      v[0] = __uint_as_float(r << 16);
+      v[1] = __uint_as_float(r & 0xffff0000u);
+    } else {
+      v[0] = __half2float(__ushort_as_half((unsigned short)(r & 0xffffu)));
+      v[1] = __half2float(__ushort_as_half((unsigned short)(r >> 16)));
+    }
+  }
+}
+
+// Producer warps: each owns every kV2Producers-th stage of the ring (its
+// lane 0 issues that stage's tensor loads, its 32 lanes the activation
+// copies), so several stages' loads are issued at once. One issuing thread
+// streams this box pattern at well under the HBM rate; a tensor load
+// occupies its issuing thread for on the order of a hundred cycles.
+// Suspend-time hint (ns) of the consumers' slow-path barrier waits; 0: plain
+// try_wait polls.
+#ifndef MR_V2_SLEEP_NS
+#define MR_V2_SLEEP_NS 0
+#endif
+#ifndef MR_V2_PRODUCERS
+#define MR_V2_PRODUCERS 4
+#endif
+constexpr int kV2Producers = MR_V2_PRODUCERS;
+constexpr int kV2Threads = kTmaConsumers + 32 * kV2Producers;
+
+template <int BITS, int SD, int EPI, int NT>
+struct V2Stage {
+  using W = TmaStage<BITS, SD, EPI>;  // the weight boxes, as the TMA kernel
+  static constexpr int kCols = 8 * NT;
+  static constexpr int kXP = EPI == EPI_PARTIAL ? 2 : 1;  // group-sum parts
+  static constexpr int kColBytes = kTmaGps * kGroup * 2 + 16;  // one column's 512 bf16 + pad
+  static constexpr int kWBytes = W::kABytes + W::kSBytes + W::kZBytes;
+  static constexpr int kXOff = kWBytes;                          // activations
+  static constexpr int kSumOff = kXOff + kCols * kColBytes;      // group sums
+  static constexpr int kSumColBytes = kTmaGps * kXP * 4;         // per column
+  static constexpr int kBytes = (kSumOff + kCols * kSumColBytes + 1023) / 1024 * 1024;
+  static_assert(kWBytes % 16 == 0 && kSumOff % 16 == 0, "16-byte cp.async destinations");
+};
+
+template <int BITS, int SD, int EPI, int NT>
+inline int v2_stages() {
+  const int fixed = TmaFixed<NT>::kBytes + 2 * 16 * 8 + 1024;
+  int n = (kSmemBudget - fixed) / V2Stage<BITS, SD, EPI, NT>::kBytes;
+  return n > 12 ? 12 : n;
+}
+template <int BITS, int SD, int EPI, int NT>
+inline int v2_smem_bytes(int nst) {
+  return 1024 + nst * V2Stage<BITS, SD, EPI, NT>::kBytes + TmaFixed<NT>::kBytes + 2 * nst * 8;
+}
+
+// Dequantised A fragment of k16 step s (0..3) of one 64-element group:
+// lane words wa (row r8) and wb (row r8 + 8). 8-bit codes give two
+// fragments (low and high nibbles, magic 128 and 2048) per step.
+// (v & mask) | magic as one lop3 (immLut 0xEA = (a & b) | c), the mask an
+// immediate and the magic a register.
+template <uint32_t MASK>
+MR_DEVICE uint32_t and_or(uint32_t v, uint32_t magic) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(v), "n"(MASK), "r"(magic));
+  return d;
+}
+
+template <int BITS>
+MR_DEVICE void dq_step(uint32_t (&a)[4], uint32_t (&ah)[4],
+                       const uint32_t (&wa)[QTraits<BITS>::kLaneWords],
+                       const uint32_t (&wb)[QTraits<BITS>::kLaneWords], int s, uint32_t mlo,
+                       uint32_t mhi) {
+  if constexpr (BITS == 4) {
+    const int wi = s >> 1, sh = 8 * (s & 1);
+    a[0] = and_or<0x000F000Fu>(wa[wi] >> sh, mlo);
+    a[1] = and_or<0x000F000Fu>(wb[wi] >> sh, mlo);
+    a[2] = and_or<0x000F000Fu>(wa[wi] >> (sh + 4), mlo);
+    a[3] = and_or<0x000F000Fu>(wb[wi] >> (sh + 4), mlo);
+    (void)ah;
+    (void)mhi;
+  } else if constexpr (BITS == 2) {
+    const int sh = 4 * s;
+    a[0] = and_or<0x00030003u>(wa[0] >> sh, mlo);
+    a[1] = and_or<0x00030003u>(wb[0] >> sh, mlo);
+    a[2] = and_or<0x00030003u>(wa[0] >> (sh + 2), mlo);
+    a[3] = and_or<0x00030003u>(wb[0] >> (sh + 2), mlo);
+    (void)ah;
+    (void)mhi;
+  } else {
+    a[0] = and_or<0x000F000Fu>(wa[s], mlo);
+    a[1] = and_or<0x000F000Fu>(wb[s], mlo);
+    a[2] = and_or<0x000F000Fu>(wa[s] >> 8, mlo);
+    a[3] = and_or<0x000F000Fu>(wb[s] >> 8, mlo);
+    ah[0] = and_or<0x000F000Fu>(wa[s] >> 4, mhi);
+    ah[1] = and_or<0x000F000Fu>(wb[s] >> 4, mhi);
+    ah[2] = and_or<0x000F000Fu>(wa[s] >> 12, mhi);
+    ah[3] = and_or<0x000F000Fu>(wb[s] >> 12, mhi);
+  }
+}
+
+template <int BITS, int SD, int EPI, int NT>
+__global__ void __launch_bounds__(kV2Threads, 1)
+    gemv_v2_kernel(const GemvParams p, const __grid_constant__ TmaMaps maps, const int nst) {
+  pdl_wait_and_release();
+  using VS = V2Stage<BITS, SD, EPI, NT>;
+  using ST = typename VS::W;
+  static_assert(!ST::kMx, "affine codes only");
+  static_assert(kGpw == 2, "two groups per consumer warp and stage");
+  constexpr int LW = QTraits<BITS>::kLaneWords;
+  constexpr float kC = QTraits<BITS>::kMagic;
+  constexpr int XP = VS::kXP;
+  extern __shared__ char smem_raw[];
+  // 1024-byte aligned (128-byte swizzle atoms); derived by pointer arithmetic
+  // so that loads through it stay shared-memory loads
+  char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  float* red = reinterpret_cast<float*>(smem + nst * VS::kBytes);
+  float* hs = red + TmaFixed<NT>::kRedFloats;
+  volatile int* flags = reinterpret_cast<volatile int*>(hs + TmaFixed<NT>::kHsFloats);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * VS::kBytes + TmaFixed<NT>::kBytes);
+  uint64_t* empty = full + nst;
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int ngroups = (int)(p.in / kGroup);
+  const int nstages = ngroups / kTmaGps;
+  const int n_routed = *p.n_routed_segments;
+  const int n_items = (n_routed + p.shared_segments) * p.rb_count;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nst; ++s) {
+      mbar_init(full + s, 1 + 32);  // the TMA byte count + the 32 copier lanes
+      mbar_init(empty + s, kTmaConsumerWarps);
+    }
+    flags[0] = 0;  // abort
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto in_row = [&](int v) -> int64_t {
+    return v < p.Tk ? (int64_t)(v / p.in_div) : (int64_t)(v - p.shared_in_off);
+  };
+
+  if (warp >= kTmaConsumerWarps) {
+    // ----------------------------------------------------------- producers
+    // producer pw issues global stages it = pw, pw + P, ... of this CTA's
+    // sequence (items in order, nstages each); stage it uses ring slot
+    // it % nst in phase (it / nst) & 1
+    const int pw = warp - kTmaConsumerWarps;
+    uint32_t it = 0;
+    const uint64_t wpol = l2_evict_first_policy();
+    const uint32_t sbase = smem_u32(smem);
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+      const ItemInfo info = decode_item(p, n_routed, item);
+      const int ncols = info.ncols;
+      // lane j < ncols: the activation row of the item's column j
+      int64_t arow = 0;
+      if (lane < ncols) {
+        const int v = info.shared ? p.Tk + info.col0 + lane : __ldg(p.cols + info.col0 + lane);
+        arow = in_row(v);
+      }
+      const CUtensorMap* mp[2];
+      const CUtensorMap* ms[2];
+      const CUtensorMap* mz[2];
+      int y0;
+      if (!info.shared) {
+        mp[0] = &maps.a_packed; ms[0] = &maps.a_scales; mz[0] = &maps.a_biases;
+        mp[1] = &maps.b_packed; ms[1] = &maps.b_scales; mz[1] = &maps.b_biases;
+        y0 = info.expert * (int)p.rows + info.rb * ST::kBoxRows;
+      } else {
+        mp[0] = &maps.sa_packed; ms[0] = &maps.sa_scales; mz[0] = &maps.sa_biases;
+        mp[1] = &maps.sb_packed; ms[1] = &maps.sb_scales; mz[1] = &maps.sb_biases;
+        y0 = info.rb * ST::kBoxRows;
+      }
+      for (int st = 0; st < nstages; ++st, ++it) {
+        if ((int)(it % kV2Producers) != pw) continue;
+        const uint32_t slot = it % (uint32_t)nst, phase = (it / (uint32_t)nst) & 1u;
+        if (lane == 0) wait_bounded(empty + slot, phase ^ 1u, flags, p.error);
+        __syncwarp();
+        char* A = smem + slot * VS::kBytes;
+        if (lane == 0) {
+          char* S = A + ST::kABytes;
+          char* Z = S + ST::kSBytes;
+          mbar_arrive_expect_tx(full + slot, ST::kTx);
+#pragma unroll
+          for (int m = 0; m < ST::kMats; ++m) {
+#pragma unroll
+            for (int j = 0; j < ST::kBoxes; ++j)
+              tma_load_2d_hint(A + (m * ST::kBoxes + j) * ST::kBoxBytes, mp[m],
+                               (st * ST::kBoxes + j) * 32, y0, full + slot, wpol);
+            const int sbytes = ST::kBoxRows * kTmaGps * ST::kEsz;
+            tma_load_2d_hint(S + m * sbytes, ms[m], st * kTmaGps, y0, full + slot, wpol);
+            tma_load_2d_hint(Z + m * sbytes, mz[m], st * kTmaGps, y0, full + slot, wpol);
+          }
+        }
+        // activations: 64 16-byte chunks per column (lanes take 2 each), and
+        // 2 * XP chunks of group sums
+        const uint32_t xdst = sbase + slot * VS::kBytes + VS::kXOff;
+        const uint32_t sdst = sbase + slot * VS::kBytes + VS::kSumOff;
+        for (int j = 0; j < ncols; ++j) {
+          const int64_t r = __shfl_sync(0xffffffffu, arow, j);
+          const uint16_t* src = p.xperm + r * p.in + (int64_t)st * (kTmaGps * kGroup);
+          cp_async16(xdst + j * VS::kColBytes + lane * 16, src + lane * 8);
+          cp_async16(xdst + j * VS::kColBytes + 512 + lane * 16, src + 256 + lane * 8);
+          if (lane < 2 * XP)
+            cp_async16(sdst + j * VS::kSumColBytes + lane * 16,
+                       p.xsum + (r * ngroups + (int64_t)st * kTmaGps) * XP + lane * 4);
+        }
+        cp_async_mbar_arrive_noinc(full + slot);
+      }
+    }
+    cp_async_wait_all();
+    if (lane == 0 && flags[0]) {
+      // after an abort, let every tensor load this producer issued land
+      // before it exits (the last nst stages may still be in flight)
+      const uint32_t issued = it;
+      for (uint32_t j = (issued > (uint32_t)nst ? issued - nst : 0); j < issued; ++j) {
+        if ((int)(j % kV2Producers) != pw) continue;
+        for (uint32_t i = 0; i < kSpinLimit; ++i)
+          if (mbar_try_wait(full + (j % nst), (j / nst) & 1u)) break;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int r8 = lane >> 2;
+  const int c = lane & 3;
+  const int mt = warp & 3;
+  const int kq = warp >> 2;  // K quarter: groups [2kq, 2kq + 2) of a stage
+  const int ctid = threadIdx.x;
+  int ma, ra, mb, rbr;
+  if constexpr (EPI == EPI_SWIGLU) {
+    ma = 0;
+    ra = mt * 8 + r8;
+    mb = 1;
+    rbr = mt * 8 + r8;
+  } else {
+    ma = 0;
+    ra = mt * 16 + r8;
+    mb = 0;
+    rbr = ra + 8;
+  }
+  // per-lane shared-memory offsets inside a stage, fixed for the kernel
+  uint32_t offA[kGpw], offB[kGpw];
+#pragma unroll
+  for (int j = 0; j < kGpw; ++j) {
+    const int b = (kq * kGpw + j) * ST::kGroupBytes + c * LW * 4;  // stage-row byte
+    const int box = b >> 7, bb = b & 127;
+    offA[j] = (ma * ST::kBoxes + box) * ST::kBoxBytes + ra * 128 + ((((bb >> 4) ^ ra) & 7) << 4) +
+              (bb & 15);
+    offB[j] = (mb * ST::kBoxes + box) * ST::kBoxBytes + rbr * 128 +
+              ((((bb >> 4) ^ rbr) & 7) << 4) + (bb & 15);
+  }
+  const uint32_t offSa = ST::kABytes + ((ma * ST::kBoxRows + ra) * kTmaGps + kq * kGpw) * ST::kEsz;
+  const uint32_t offSb = ST::kABytes + ((mb * ST::kBoxRows + rbr) * kTmaGps + kq * kGpw) * ST::kEsz;
+  // B fragments: column r8 (+ 8t), elements [16c, 16c + 16) of each group
+  const uint32_t offX = VS::kXOff + r8 * VS::kColBytes + (kq * kGpw * kGroup + c * 16) * 2;
+  // group sums of accumulator columns 2c, 2c + 1 (+ 8t), groups 2kq, 2kq + 1
+  const uint32_t offX0 = VS::kSumOff + (2 * c) * VS::kSumColBytes + kq * kGpw * XP * 4;
+  uint32_t slot = 0, phase = 0;
+  const uint32_t mlo = p.dq_magic_lo, mhi = p.dq_magic_hi;
+
+  struct Meta {
+    ItemInfo info;
+    int v0[NT], v1[NT];
+    float w0[NT], w1[NT];
+  };
+  auto fetch_cols = [&](Meta& m) {
+    const int nc = m.info.ncols;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int c0 = min(t * 8 + 2 * c, nc - 1);
+      const int c1 = min(t * 8 + 2 * c + 1, nc - 1);
+      if (m.info.shared) {
+        m.v0[t] = p.Tk + m.info.col0 + c0;
+        m.v1[t] = p.Tk + m.info.col0 + c1;
+      } else {
+        m.v0[t] = __ldg(p.cols + m.info.col0 + c0);
+        m.v1[t] = __ldg(p.cols + m.info.col0 + c1);
+      }
+      if constexpr (EPI == EPI_SWIGLU) {
+        m.w0[t] = m.info.shared ? 1.0f : __ldg(p.weights + m.v0[t]);
+        m.w1[t] = m.info.shared ? 1.0f : __ldg(p.weights + m.v1[t]);
+      }
+    }
+  };
+
+  Meta cur, nxt;
+  if ((int)blockIdx.x < n_items) {
+    cur.info = decode_item(p, n_routed, blockIdx.x);
+    fetch_cols(cur);
+  }
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const bool has_next = item + (int)gridDim.x < n_items;
+    if (has_next) nxt.info = decode_item(p, n_routed, item + gridDim.x);
+    const ItemInfo& info = cur.info;
+    const bool shared = info.shared;
+    const int ncols = info.ncols;
+    const int ntiles = (ncols + 7) >> 3;
+    float y[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) y[t][0] = y[t][1] = y[t][2] = y[t][3] = 0.0f;
+
+    for (int st = 0; st < nstages; ++st) {
+      if (st == 1 && has_next) fetch_cols(nxt);
+      if (!mbar_try_wait(full + slot, phase)) {
+        // slow path: bounded, checks the abort flag every 256 polls
+        uint32_t i = 0;
+        for (;;) {
+#if MR_V2_SLEEP_NS
+          if (mbar_try_wait_sleep(full + slot, phase, MR_V2_SLEEP_NS)) break;
+#else
+          if (mbar_try_wait(full + slot, phase)) break;
+#endif
+          if ((++i & 255u) == 0u) {
+            if (flags[0]) break;
+            if (i >= kSpinLimit) {
+              flags[0] = 1;
+              atomicOr(p.error, MR_DEVERR_TIMEOUT);
+              break;
+            }
+          }
+        }
+      }
+      // Plain shared-memory loads (not volatile asm): the compiler may
+      // schedule them anywhere after the wait above and before the release
+      // below, both of which clobber memory.
+      const char* sp = smem + slot * VS::kBytes;
+      uint32_t wa[kGpw][LW], wb[kGpw][LW];
+#pragma unroll
+      for (int j = 0; j < kGpw; ++j) {
+        if constexpr (LW == 1) {
+          wa[j][0] = *reinterpret_cast<const uint32_t*>(sp + offA[j]);
+          wb[j][0] = *reinterpret_cast<const uint32_t*>(sp + offB[j]);
+        } else if constexpr (LW == 2) {
+          const uint2 u = *reinterpret_cast<const uint2*>(sp + offA[j]);
+          const uint2 v = *reinterpret_cast<const uint2*>(sp + offB[j]);
+          wa[j][0] = u.x; wa[j][1] = u.y;
+          wb[j][0] = v.x; wb[j][1] = v.y;
+        } else {
+          const uint4 u = *reinterpret_cast<const uint4*>(sp + offA[j]);
+          const uint4 v = *reinterpret_cast<const uint4*>(sp + offB[j]);
+          wa[j][0] = u.x; wa[j][1] = u.y; wa[j][2] = u.z; wa[j][3] = u.w;
+          wb[j][0] = v.x; wb[j][1] = v.y; wb[j][2] = v.z; wb[j][3] = v.w;
+        }
+      }
+      float sa[kGpw], za[kGpw], sb[kGpw], zb[kGpw];
+      lds2_scales<SD>(sa, sp + offSa);
+      lds2_scales<SD>(za, sp + offSa + ST::kSBytes);
+      lds2_scales<SD>(sb, sp + offSb);
+      lds2_scales<SD>(zb, sp + offSb + ST::kSBytes);
+#pragma unroll
+      for (int j = 0; j < kGpw; ++j) {
+        za[j] = fmaf(-kC, sa[j], za[j]);
+        zb[j] = fmaf(-kC, sb[j], zb[j]);
+      }
+      // group sums of this lane's accumulator columns for both groups
+      float X0[NT][kGpw], X1[NT][kGpw];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (t == 0 || t < ntiles) {
+          const char* s0 = sp + offX0 + t * 8 * VS::kSumColBytes;
+          if constexpr (XP == 1) {
+            const float2 u = *reinterpret_cast<const float2*>(s0);
+            const float2 v = *reinterpret_cast<const float2*>(s0 + VS::kSumColBytes);
+            X0[t][0] = u.x; X0[t][1] = u.y;
+            X1[t][0] = v.x; X1[t][1] = v.y;
+          } else {  // two 32-row partial sums per group, added in order
+            const float4 u = *reinterpret_cast<const float4*>(s0);
+            const float4 v = *reinterpret_cast<const float4*>(s0 + VS::kSumColBytes);
+            X0[t][0] = u.x + u.y; X0[t][1] = u.z + u.w;
+            X1[t][0] = v.x + v.y; X1[t][1] = v.z + v.w;
+          }
+        }
+      }
+      // one group at a time: its B fragments, then each dequantised A
+      // fragment feeds every live tile
+#pragma unroll
+      for (int j = 0; j < kGpw; ++j) {
+        uint32_t xb[NT][8];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          if (t == 0 || t < ntiles) {
+            const char* a = sp + offX + t * 8 * VS::kColBytes + j * kGroup * 2;
+            const uint4 v0 = *reinterpret_cast<const uint4*>(a);
+            const uint4 v1 = *reinterpret_cast<const uint4*>(a + 16);
+            xb[t][0] = v0.x; xb[t][1] = v0.y; xb[t][2] = v0.z; xb[t][3] = v0.w;
+            xb[t][4] = v1.x; xb[t][5] = v1.y; xb[t][6] = v1.z; xb[t][7] = v1.w;
+          }
+        }
+        float acc[NT][4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          uint32_t a[4], ah[4];
+          dq_step<BITS>(a, ah, wa[j], wb[j], s, mlo, mhi);
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            if (t == 0 || t < ntiles) {
+              if (s == 0)
+                mma_bf16_16816_z(acc[t], a[0], a[1], a[2], a[3], xb[t][0], xb[t][1]);
+              else
+                mma_bf16_16816(acc[t], a[0], a[1], a[2], a[3], xb[t][2 * s], xb[t][2 * s + 1]);
+              if constexpr (BITS == 8)
+                mma_bf16_16816(acc[t], ah[0], ah[1], ah[2], ah[3], xb[t][2 * s],
+                               xb[t][2 * s + 1]);
+            }
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          if (t == 0 || t < ntiles) {
+            y[t][0] = fmaf(sa[j], acc[t][0], fmaf(za[j], X0[t][j], y[t][0]));
+            y[t][1] = fmaf(sa[j], acc[t][1], fmaf(za[j], X1[t][j], y[t][1]));
+            y[t][2] = fmaf(sb[j], acc[t][2], fmaf(zb[j], X0[t][j], y[t][2]));
+            y[t][3] = fmaf(sb[j], acc[t][3], fmaf(zb[j], X1[t][j], y[t][3]));
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + slot);  // this warp's share of the slot is consumed
+      if (++slot == (uint32_t)nst) {
+        slot = 0;
+        phase ^= 1u;
+      }
+    }
+    if (nstages <= 1 && has_next) fetch_cols(nxt);
+
+    // ---------------------------------------- K-split reduction (fixed order)
+    if (kq > 0) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < ntiles)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            red[((((kq - 1) * 4 + mt) * NT + t) * 32 + lane) * 4 + i] = y[t][i];
+    }
+    named_bar(1, kTmaConsumers);
+    if (kq == 0) {
+#pragma unroll
+      for (int q = 0; q < kKSplit - 1; ++q)
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+          if (t < ntiles)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) y[t][i] += red[(((q * 4 + mt) * NT + t) * 32 + lane) * 4 + i];
+    }
+
+    // ------------------------------------------------------------ epilogues
+    if constexpr (EPI == EPI_STORE || EPI == EPI_PARTIAL) {
+      if (kq == 0) {
+        const int64_t row_a = (int64_t)info.rb * kTmaRows + mt * 16 + r8;
+        const int64_t row_b = row_a + 8;
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int ci = t * 8 + 2 * c + i;
+            if (t < ntiles && ci < ncols) {
+              const int64_t v = i ? cur.v1[t] : cur.v0[t];
+              if constexpr (EPI == EPI_STORE) {
+                if (row_a < p.rows) p.out_bf16[v * p.rows + row_a] = f32_to_bf16_bits(y[t][i]);
+                if (row_b < p.rows) p.out_bf16[v * p.rows + row_b] = f32_to_bf16_bits(y[t][2 + i]);
+              } else {
+                // routed slots are the w2 gather's bf16 output; the shared
+                // expert's hi/lo columns stay fp32
+                const bool routed = v < p.Tk;
+                float* dst = p.part;
+                int64_t vv = v;
+                if (p.peer_part && routed) {  // the pair's home rank (possibly a peer GPU)
+                  const int home = (int)(v / p.peer_cols);
+                  dst = p.peer_part[home];
+                  vv = v - (int64_t)home * p.peer_cols;
+                }
+                if (row_a < p.rows)
+                  dst[vv * p.rows + row_a] = routed ? bf16_round(y[t][i]) : y[t][i];
+                if (row_b < p.rows)
+                  dst[vv * p.rows + row_b] = routed ? bf16_round(y[t][2 + i]) : y[t][2 + i];
+              }
+            }
+          }
+      }
+    } else {  // EPI_SWIGLU
+      if (kq == 0) {
+        const int hrow = info.rb * 32 + mt * 8 + r8;  // intermediate index (< rows)
+        const int pos = perm_pos(hrow, p.h_bits);
+        const float lim = p.swiglu_limit;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int ci = t * 8 + 2 * c + i;
+            float shi = 0.0f, slo = 0.0f;
+            if (t < ntiles && ci < ncols) {
+              const int v = i ? cur.v1[t] : cur.v0[t];
+              float g = bf16_round(y[t][i]);
+              float u = bf16_round(y[t][2 + i]);
+              if (lim > 0.0f) {
+                g = fminf(g, lim);
+                u = fminf(fmaxf(u, -lim), lim);
+              }
+              uint16_t hb;
+              if (!shared) {
+                if (!p.weight_after_down) {
+                  float a = g * sigmoid_f32(g);
+                  a = a * u;
+                  a = a * (i ? cur.w1[t] : cur.w0[t]);
+                  hb = f32_to_bf16_bits(a);
+                } else {
+                  const float sg = bf16_round(sigmoid_f32(g));
+                  const float a = bf16_round(g * sg);
+                  hb = f32_to_bf16_bits(a * u);
+                }
+                p.out_bf16[(int64_t)v * p.rows + pos] = hb;
+                shi = bf16_bits_to_f32(hb);
+              } else {
+                float a = g * sigmoid_f32(g);
+                a = a * u;
+                hb = f32_to_bf16_bits(a);
+                const uint16_t lb16 = f32_to_bf16_bits(a - bf16_bits_to_f32(hb));
+                p.out_bf16[(int64_t)v * p.rows + pos] = hb;
+                p.out_bf16[(int64_t)(v + p.shared_lo_off) * p.rows + pos] = lb16;
+                shi = bf16_bits_to_f32(hb);
+                slo = bf16_bits_to_f32(lb16);
+              }
+            }
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+              shi += __shfl_xor_sync(0xffffffffu, shi, off);
+              slo += __shfl_xor_sync(0xffffffffu, slo, off);
+            }
+            if (r8 == 0 && t < ntiles && ci < ncols) {
+              hs[(mt * kMaxCols + ci) * 2 + 0] = shi;
+              hs[(mt * kMaxCols + ci) * 2 + 1] = slo;
+            }
+          }
+        }
+      }
+      // thread ci < ncols of warp 0 sums column ci over the 4 m-tiles; the
+      // column's value sits in lane (ci & 7) >> 1 of any warp (v0 or v1)
+      int vci = 0;
+      if (warp == 0) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const int src = (lane & 7) >> 1;
+          const int a = __shfl_sync(0xffffffffu, cur.v0[t], src);
+          const int b = __shfl_sync(0xffffffffu, cur.v1[t], src);
+          if ((lane >> 3) == t) vci = (lane & 1) ? b : a;
+        }
+      }
+      named_bar(1, kTmaConsumers);
+      if (ctid < ncols) {
+        float shi = 0.0f, slo = 0.0f;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          shi += hs[(m * kMaxCols + ctid) * 2 + 0];
+          slo += hs[(m * kMaxCols + ctid) * 2 + 1];
+        }
+        const int64_t hp = p.rows / 32;  // 32-row partial sums per h row
+        p.hsum[(int64_t)vci * hp + info.rb] = shi;
+        if (shared) p.hsum[(int64_t)(vci + p.shared_lo_off) * hp + info.rb] = slo;
+      }
+    }
+    named_bar(1, kTmaConsumers);  // red / hs reused by the next item
+    if (has_next) cur = nxt;
+  }
+  if constexpr (EPI == EPI_PARTIAL) {
+    // expert parallel: once every CTA's stores are out, tell every rank
+    if (p.peer_flags) {
+      __threadfence_system();  // this thread's peer stores, before the CTA's count
+      named_bar(1, kTmaConsumers);
+    }
+    if (p.peer_flags && ctid == 0) {
+      __threadfence_system();
+      const unsigned prev = atomicAdd(p.peer_done, 1u);
+      if (prev == gridDim.x - 1) {
+        *p.peer_done = 0;  // for the next launch on this GPU
+        __threadfence_system();
+        for (int j = 0; j < p.peer_n; ++j) st_release_sys(p.peer_flags[j] + p.peer_rank, p.peer_epoch);
+      }
+    }
+  }
+}
+
+}  // namespace mr

@@ -4,6 +4,7 @@
 
 #include "mr_gemv.cuh"
 #include "mr_gemv_tma.cuh"
+#include "mr_gemv_v2.cuh"
 #include "mr_gemv_umma.cuh"
 #include "mr_gemm_umma.cuh"
 
@@ -22,6 +23,25 @@ cudaError_t launch_tma_b4(const GemvParams& p, const TmaMaps& m, int sd, int epi
                           cudaStream_t s);
 cudaError_t launch_tma_b8(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, int grid,
                           cudaStream_t s);
+
+// Staged-activation TMA kernel (in % 512 == 0, 2-D tensor-map stacks; nt = 1
+// or 2 mma tiles of 8 columns per segment).
+cudaError_t launch_v2_b2(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, int grid,
+                         cudaStream_t s);
+cudaError_t launch_v2_b4(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, int grid,
+                         cudaStream_t s);
+cudaError_t launch_v2_b8(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, int grid,
+                         cudaStream_t s);
+
+inline cudaError_t launch_v2(const GemvParams& p, const TmaMaps& m, int bits, int sd, int epi,
+                             int nt, int grid, cudaStream_t s) {
+  switch (bits) {
+    case 2: return launch_v2_b2(p, m, sd, epi, nt, grid, s);
+    case 4: return launch_v2_b4(p, m, sd, epi, nt, grid, s);
+    case 8: return launch_v2_b8(p, m, sd, epi, nt, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
 
 // MXFP4 form of the TMA kernel (in % 512 == 0, store epilogue, nt == 1);
 // xs = 1: bf16 activations, xs = 2: fp32 activations as two f16 terms.
@@ -114,6 +134,18 @@ inline cudaError_t launch_tma_inst(const GemvParams& p, const TmaMaps& m, int gr
   cudaError_t e = opt_in_smem(kern, smem, done);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, grid, kTmaThreads, smem, s, p, m, nst);
+}
+
+template <int BITS, int SD, int EPI, int NT>
+inline cudaError_t launch_v2_inst(const GemvParams& p, const TmaMaps& m, int grid,
+                                  cudaStream_t s) {
+  static bool done[64] = {};  // one per instantiation
+  const int nst = v2_stages<BITS, SD, EPI, NT>();
+  const int smem = v2_smem_bytes<BITS, SD, EPI, NT>(nst);
+  auto kern = gemv_v2_kernel<BITS, SD, EPI, NT>;
+  cudaError_t e = opt_in_smem(kern, smem, done);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(kern, grid, kV2Threads, smem, s, p, m, nst);
 }
 
 template <int BITS, int SD, int EPI>
@@ -237,5 +269,28 @@ inline cudaError_t launch_pf_epi(const GemvParams& p, const UmMaps& m, int epi, 
   cudaError_t launch_tma_b##BITS(const GemvParams& p, const TmaMaps& m, int sd, int epi,       \
                                  int nt, int grid, cudaStream_t s) {                           \
     return dispatch_##BITS(p, &m, sd, epi, nt, grid, s);                                       \
+  }                                                                                            \
+  template <int SD, int EPI>                                                                   \
+  static cudaError_t v2_nt_##BITS(const GemvParams& p, const TmaMaps& m, int nt, int grid,     \
+                                  cudaStream_t s) {                                            \
+    return nt == 1 ? launch_v2_inst<BITS, SD, EPI, 1>(p, m, grid, s)                           \
+                   : launch_v2_inst<BITS, SD, EPI, 2>(p, m, grid, s);                          \
+  }                                                                                            \
+  template <int SD>                                                                            \
+  static cudaError_t v2_epi_##BITS(const GemvParams& p, const TmaMaps& m, int epi, int nt,     \
+                                   int grid, cudaStream_t s) {                                 \
+    switch (epi) {                                                                             \
+      case EPI_STORE: return v2_nt_##BITS<SD, EPI_STORE>(p, m, nt, grid, s);                   \
+      case EPI_SWIGLU: return v2_nt_##BITS<SD, EPI_SWIGLU>(p, m, nt, grid, s);                 \
+      default: return v2_nt_##BITS<SD, EPI_PARTIAL>(p, m, nt, grid, s);                        \
+    }                                                                                          \
+  }                                                                                            \
+  cudaError_t launch_v2_b##BITS(const GemvParams& p, const TmaMaps& m, int sd, int epi, int nt, \
+                                int grid, cudaStream_t s) {                                    \
+    switch (sd) {                                                                              \
+      case MR_DTYPE_BF16: return v2_epi_##BITS<MR_DTYPE_BF16>(p, m, epi, nt, grid, s);         \
+      case MR_DTYPE_F16: return v2_epi_##BITS<MR_DTYPE_F16>(p, m, epi, nt, grid, s);           \
+      default: return v2_epi_##BITS<MR_DTYPE_F32>(p, m, epi, nt, grid, s);                     \
+    }                                                                                          \
   }                                                                                            \
   }

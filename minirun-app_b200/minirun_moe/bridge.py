@@ -87,7 +87,7 @@ class Context:
         self.check("mr_ctx_reserve", L.load().mr_ctx_reserve(
             self.handle, max_tokens, top_k, experts, hidden, inter))
 
-    KERNEL_PATHS = {"auto": 0, "register": 1, "tma": 2, "umma": 3}
+    KERNEL_PATHS = {"auto": 0, "register": 1, "tma": 2, "umma": 3, "v2": 4}
 
     def set_kernel_path(self, path: str) -> None:
         self.check("mr_ctx_set_kernel_path", L.load().mr_ctx_set_kernel_path(

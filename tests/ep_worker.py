@@ -34,7 +34,7 @@ def main():
     import datetime
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     group = M.ExpertGroup(rank, rank, world)
-    M.Context.get(rank).set_kernel_path("tma")
+    M.Context.get(rank).set_kernel_path("auto")
     cases = [
         ("config0", S.CONFIGS[0], 4),
         ("config0_after_down", dataclasses.replace(S.CONFIGS[0], weight_after_down=True), 5),

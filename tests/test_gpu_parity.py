@@ -54,7 +54,7 @@ def oracle_with_scales(w: O.Affine, scale_dtype) -> O.Affine:
     return O.Affine(w.packed, s.float().numpy(), b.float().numpy(), w.group, w.bits, 2)
 
 
-@pytest.fixture(params=["register", "tma", "umma"])
+@pytest.fixture(params=["register", "tma", "umma", "v2"])
 def kernel_path(request):
     """Runs a test once per dequant-GEMV implementation."""
     ctx = M.Context.get(0)
@@ -139,6 +139,33 @@ def test_gather_many_columns_per_expert():
     ref, reff = O.affine_gather_mm(x, w, ids)
     y = M.affine_gather_mm(t_u16(x), to_dev(w), torch.from_numpy(ids).to(dev()))
     assert rel_l2(O.bf16_to_f32(n_u16(y)), reff) < 2e-3
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("scale_dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_staged_kernel_two_tile_segments(bits, scale_dtype):
+    """The staged-activation kernel (path "v2") takes two 8-column mma tiles
+    per segment once experts average more than 8 columns: each dequantised
+    fragment feeds both tiles. Checked against the oracle, and a token's
+    output must be bit-identical to its output in a small batch (one-tile
+    segments), since every column goes through the same mma and fold."""
+    ctx = M.Context.get(0)
+    ctx.set_kernel_path("v2")
+    try:
+        E, out, inn, T, k = 3, 192, 1024, 40, 2  # Tk = 80 > 8E: 16-column segments
+        w = O._stack([O.gen_affine(47, 0, e, 1, out, inn, bits, 64) for e in range(E)])
+        wo = oracle_with_scales(w, scale_dtype) if scale_dtype != torch.bfloat16 else w
+        x = O.gen_normal_bf16(13, T * inn, 1.0).reshape(T, inn)
+        ids = np.random.default_rng(bits).integers(0, E, size=(T, k)).astype(np.int32)
+        ref, reff = O.affine_gather_mm(x, wo, ids)
+        wd = to_dev(w, scale_dtype)
+        y = M.affine_gather_mm(t_u16(x), wd, torch.from_numpy(ids).to(dev()))
+        assert rel_l2(O.bf16_to_f32(n_u16(y)), reff) < 2e-3
+        small = M.affine_gather_mm(t_u16(x[:5]), wd, torch.from_numpy(ids[:5]).to(dev()))
+        assert torch.equal(small, y[:5])
+        ctx.sync_check()
+    finally:
+        ctx.set_kernel_path("auto")
 
 
 @pytest.mark.parametrize("bits", [2, 4, 8])
@@ -287,16 +314,16 @@ def test_layer_config1_T64_matches_oracle():
 def test_layer_batch_invariance_config1_T64(kernel_path):
     """Each token's output depends only on that token (size-independent
     property at the full config-1 shape): a 64-token batch matches one-token
-    calls — bit-identically on the register kernel (every column goes
-    through the same mma), and within fp32 summation order on the TMA kernel,
-    whose one-column items use fp32 FMAs instead of an mma tile."""
+    calls — bit-identically on the register and staged kernels (every column
+    goes through the same mma), and within fp32 summation order on the first
+    TMA kernel, whose one-column items use fp32 FMAs instead of an mma tile."""
     layer = S.synth_layer(S.CONFIGS[1])
     x = S.synth_x(S.CONFIGS[1], 64, batch=7)
     out, sel = layer(x)
     for t in range(0, 64, 9):
         o1, s1 = layer(x[t:t + 1])
         assert torch.equal(s1.ids[0], sel.ids[t])
-        if kernel_path == "register":
+        if kernel_path in ("register", "v2"):
             assert torch.equal(o1[0], out[t])
         else:
             assert rel_l2(o1[0].float().cpu().numpy(), out[t].float().cpu().numpy()) < 2e-3
