@@ -50,6 +50,28 @@ MR_DEVICE void cp_async_mbar_arrive_noinc(uint64_t* bar) {
 }
 MR_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// Up to 1024 try_waits on (bar, parity), four per counter step; true once
+// the phase has completed. Each try_wait may itself suspend the thread for
+// a short hardware time limit.
+MR_DEVICE bool mbar_poll_1024(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n .reg .u32 n;\n mov.u32 n, 256;\n"
+      "POLL%=:\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n @p bra DONE%=;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n @p bra DONE%=;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n @p bra DONE%=;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n @p bra DONE%=;\n"
+      " sub.u32 n, n, 1;\n setp.ne.u32 p, n, 0;\n @p bra POLL%=;\n"
+      " mov.u32 %0, 0;\n bra END%=;\n"
+      "DONE%=:\n mov.u32 %0, 1;\n"
+      "END%=:\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // D = A * B with a zero accumulator (the first k-step of a group).
 MR_DEVICE void mma_bf16_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                 uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -372,21 +394,17 @@ __global__ void __launch_bounds__(kV2Threads, 1)
     for (int st = 0; st < nstages; ++st) {
       if (st == 1 && has_next) fetch_cols(nxt);
       if (!mbar_try_wait(full + slot, phase)) {
-        // slow path: bounded, checks the abort flag every 256 polls
+        // slow path: rounds of up to 1024 polls (one try_wait and a branch
+        // each), the abort flag checked between rounds, kSpinLimit in total
         uint32_t i = 0;
         for (;;) {
-#if MR_V2_SLEEP_NS
-          if (mbar_try_wait_sleep(full + slot, phase, MR_V2_SLEEP_NS)) break;
-#else
-          if (mbar_try_wait(full + slot, phase)) break;
-#endif
-          if ((++i & 255u) == 0u) {
-            if (flags[0]) break;
-            if (i >= kSpinLimit) {
-              flags[0] = 1;
-              atomicOr(p.error, MR_DEVERR_TIMEOUT);
-              break;
-            }
+          if (mbar_poll_1024(full + slot, phase)) break;
+          i += 1024u;
+          if (flags[0]) break;
+          if (i >= kSpinLimit) {
+            flags[0] = 1;
+            atomicOr(p.error, MR_DEVERR_TIMEOUT);
+            break;
           }
         }
       }
