@@ -40,11 +40,13 @@ sys.path.insert(0, os.path.join(ROOT, "minirun-app_b200"))
 METRIC = ("MoE-layer decode tokens/s; dequant-GEMV HBM GB/s (% of ~8 TB/s) at 1/2/4/8 GPUs")
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
-# kernels one layer forward launches: logits(+prep), top-k(+plan), gate/up, down, combine;
-# expert-parallel: logits, top-k, routed gate/up and down, partial sums, shared gate/up and
-# down, combine (the NCCL collectives are not counted)
+# kernels one layer forward launches: logits(+prep), top-k(+plan), gate/up, down, combine.
+# Expert parallel (NCCL collectives not counted): all-gather modes: logits, top-k, routed
+# gate/up and down, shared gate/up and down, wait+combine (+ the partial-sum kernel on the
+# NCCL path); all-to-all: logits, top-k, dispatch plan, dispatch copy, receive, prep, plan,
+# routed gate/up and down, shared gate/up and down, wait+combine
 LAUNCHES_PER_STEP = 5
-LAUNCHES_PER_STEP_EP = 8
+LAUNCHES_PER_STEP_EP = {"allgather": 7, "nccl": 8, "alltoall": 12}
 
 
 def parse():
@@ -71,7 +73,14 @@ def parse():
     p.add_argument("--k3-experts", type=int, default=896,
                    help="routed experts of the K3 layer (flagship: 896)")
     p.add_argument("--ep-nccl", action="store_true",
-                   help="expert parallel: NCCL reduce-scatter instead of the fused peer stores")
+                   help="expert parallel: NCCL reduce-scatter instead of the fused peer stores "
+                        "(same as --ep-mode nccl)")
+    p.add_argument("--ep-mode", choices=["allgather", "nccl", "alltoall"], default="alltoall",
+                   help="expert-parallel token exchange: NCCL all-gather + fused peer combine, "
+                        "NCCL all-gather + reduce-scatter, or peer all-to-all dispatch + fused "
+                        "peer combine")
+    p.add_argument("--no-ep-compare", action="store_true",
+                   help="N > 1: skip timing the other exchange modes beside the headline")
     p.add_argument("--config", default="1", choices=["1", "2b2", "2b8"],
                    help="decode layer: config 1 (the headline) or config 2's wide 2-/8-bit "
                         "layers (384 experts)")
@@ -227,9 +236,11 @@ def run_ours(args, world, rank, local):
     xs = {t: [xrows(t, b) for b in range(NB)] for t in token_counts}
     ctx = M.Context.get(local)
     ctx.set_kernel_path(args.kernel_path)
+    if args.ep_nccl:
+        args.ep_mode = "nccl"
     group = M.ExpertGroup(local, rank, world) if ep else None
     if group is not None:
-        group.set_fused(not args.ep_nccl)
+        group.set_mode(args.ep_mode)
     torch.cuda.synchronize()
 
     def step(lay, x, out, ids=None):
@@ -393,8 +404,22 @@ def run_ours(args, world, rank, local):
         torch.cuda.empty_cache()
 
     prefill = None
-    if not ep and args.prefill_tokens > 0:
-        prefill = prefill_run(args, S, M, torch, ctx, local, dev)
+    # the exchange modes side by side (same run, same inputs): T per GPU and
+    # the strong-scaling batch
+    ep_modes = None
+    if ep and not args.no_ep_compare:
+        ep_modes = {}
+        for mode in ("allgather", "nccl", "alltoall"):
+            group.set_mode(mode)
+            row = {}
+            for tok in sorted({T, Ts} - {0}):
+                m3 = timed(tok, K, W)
+                row[str(tok)] = {"tokens_per_s": world * tok * K / (m3 / 1e3),
+                                 "ms_per_step": m3 / K}
+            ep_modes[mode] = row
+        group.set_mode(args.ep_mode)
+    if args.prefill_tokens > 0:
+        prefill = prefill_run(args, S, M, torch, ctx, local, dev, group, world, rank, dist)
     k3 = None
     if not ep and args.k3_tokens:
         k3 = k3_run(args, M, torch, dev, hbm)
@@ -440,11 +465,16 @@ def run_ours(args, world, rank, local):
             "l2": "inputs larger than L2: consecutive steps read different layers' experts "
                   "(>= 227 MB each)",
             "parallelism": "single GPU" if world == 1 else
-                           f"ep{world}: {spec.experts // world} routed experts per GPU, NCCL "
-                           "all-gather of tokens, " +
-                           ("NCCL reduce-scatter of per-token sums" if args.ep_nccl else
-                            "down GEMV storing routed partials into their home GPU over "
-                            "NVLink (fused), slot-ordered combine there"),
+                           f"ep{world}: {spec.experts // world} routed experts per GPU, " +
+                           {"nccl": "NCCL all-gather of tokens, NCCL reduce-scatter of per-token "
+                                    "sums",
+                            "allgather": "NCCL all-gather of tokens, down GEMV storing routed "
+                                         "partials into their home GPU over NVLink (fused), "
+                                         "slot-ordered combine there",
+                            "alltoall": "each GPU routes its own tokens and stores their rows "
+                                        "into the GPUs holding their experts (NVLink peer "
+                                        "all-to-all), down GEMV storing routed partials into "
+                                        "their home GPU, slot-ordered combine there"}[args.ep_mode],
             "distinct_experts_avg": sum(us) / len(us),
             "layer_bytes_per_step": avg_bytes,
             "layer_gbs": avg_bytes / (ms_step / 1e3) / 1e9,
@@ -453,6 +483,7 @@ def run_ours(args, world, rank, local):
             "phases_ms_per_step": {k: v["ms_per_step"] for k, v in per_phase.items()},
             "sweep": sweep,
             "strong_T64": strong,
+            "ep_modes": ep_modes,
             "prefill": prefill,
             "k3_latent_moe": k3,
             "config2": config2,
@@ -472,7 +503,7 @@ def run_ours(args, world, rank, local):
         },
         "parity": parity,
         "e2e": e2e,
-        "gpu_launches": K * (LAUNCHES_PER_STEP_EP if ep else LAUNCHES_PER_STEP),
+        "gpu_launches": K * (LAUNCHES_PER_STEP_EP[args.ep_mode] if ep else LAUNCHES_PER_STEP),
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
@@ -527,10 +558,11 @@ def parity_check(args, spec, S, M, torch, dist, world, rank, local, dev, layers,
             same_ids = bool(torch.equal(torch.sort(sel.ids, 1)[0], torch.sort(gids, 1)[0]))
             bit = bool(torch.equal(ref, gout))
             err = rel_l2(gout.float().cpu().numpy(), ref.float().cpu().numpy())
-            ok = same_ids and (bit if not args.ep_nccl else err < 2e-3)
+            exact = args.ep_mode != "nccl"
+            ok = same_ids and (bit if exact else err < 2e-3)
             res["vs_one_gpu"] = {"tokens": T * world, "ids_equal": same_ids,
                                  "bit_identical": bit, "rel_l2": err,
-                                 "bound": "bit-identical" if not args.ep_nccl else 2e-3,
+                                 "bound": "bit-identical" if exact else 2e-3,
                                  "ok": ok}
             res["ok"] = res["ok"] and ok
             del fl
@@ -630,55 +662,122 @@ def config2_run(args, S, M, torch, dist, world, rank, local, dev, group, hbm, ma
             "by_bits": out}
 
 
-def prefill_run(args, S, M, torch, ctx, local, dev):
-    """Config 3: one prefill-size batch (T tokens, Zipf-skewed routing) through
-    the same layer call; reports tokens/s and the tcgen05 GEMMs' TFLOP/s
-    against the dense bf16 peak (tensor-bound). Algorithmic FLOPs: 2*H*I per
-    (token, expert) and projection, over the k routed slots and the shared
-    expert; the measured experts are whatever the router picked."""
+def prefill_run(args, S, M, torch, ctx, local, dev, group=None, world=1, rank=0, dist=None):
+    """Config 3: one prefill-size batch (T tokens per GPU, Zipf-skewed
+    routing) through the same layer call; reports tokens/s and the tcgen05
+    GEMMs' TFLOP/s against the dense bf16 peak (tensor-bound). Algorithmic
+    FLOPs: 2*H*I per (token, expert) and projection, over the k routed slots
+    and the shared expert; the measured experts are whatever the router
+    picked. On N GPUs the layer is expert-parallel through `group` (its
+    current exchange mode; the all-to-all dispatch sends each GPU only the
+    rows routed to it); rank 0's outputs are checked bit for bit against the
+    one-GPU layer on the same tokens."""
     spec = S.CONFIGS[3]
     if args.experts:
         import dataclasses
         spec = dataclasses.replace(spec, experts=args.experts)
     T = args.prefill_tokens
-    lay = S.synth_layer(spec, layer=0, device=local)
-    x = S.synth_x(spec, T, layer=0, batch=0, device=local)
+    ep = world > 1
+    # the Zipf router favours low expert ids: strided placement spreads the
+    # hot experts over the GPUs (contiguous ranges would put them all on one)
+    if ep:
+        group.set_placement("strided")
+    lay = S.synth_layer(spec, layer=0, device=local, shard=(rank, world) if ep else None,
+                        strided=ep)
+    x = S.synth_x(spec, T * world, layer=0, batch=0, device=local)[rank * T:(rank + 1) * T]
+    x = x.contiguous()
     out = torch.empty((T, spec.hidden), dtype=torch.bfloat16, device=dev)
+    ids = torch.empty((T, spec.top_k), dtype=torch.int32, device=dev)
+
+    def fwd(want_ids=False):
+        if ep:
+            group.forward(lay, x, out=out, ids=ids if want_ids else None)
+        elif want_ids:
+            _, sel = lay.forward(x, out=out)
+            ids.copy_(sel.ids)
+        else:
+            lay.forward(x, out=out, selection=False)
+
+    def barrier():
+        if ep:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if ep:
+            t = torch.tensor([v], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            v = float(t.item())
+        return v
+
     for _ in range(3):
-        lay.forward(x, out=out, selection=False)
+        fwd()
     torch.cuda.synchronize()
+    barrier()
     steps = 5
     ctx.profile(True)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
-        lay.forward(x, out=out, selection=False)
+        fwd()
     e1.record()
     torch.cuda.synchronize()
+    barrier()
     prof = ctx.profile_read()
     ctx.profile(False)
-    ms = e0.elapsed_time(e1) / steps
-    _, sel = lay.forward(x, out=out)
-    distinct = len(set(sel.ids.cpu().view(-1).tolist()))
-    slots = T * (spec.top_k + (1 if spec.shared_inter else 0))
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    fwd(True)
+    torch.cuda.synchronize()
+    allids = ids
+    if ep:
+        parts = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(parts, ids)
+        allids = torch.cat(parts)
+    hist = torch.bincount(allids.view(-1).long(), minlength=spec.experts).cpu().tolist()
+    distinct = sum(1 for c in hist if c)
+    slots = world * T * (spec.top_k + (1 if spec.shared_inter else 0))
     gu_flops = slots * 2 * (2 * spec.hidden * spec.inter)
     dn_flops = slots * 2 * spec.hidden * spec.inter
-    gu_ms = prof["gate_up"][0] / max(prof["gate_up"][1], 1)
-    dn_ms = prof["down_combine"][0] / max(prof["down_combine"][1], 1)
+    gu_ms = max_over_ranks(prof["gate_up"][0] / steps)   # per step (routed + shared launches)
+    dn_ms = max_over_ranks(prof["down_combine"][0] / steps)
     peak, kind = tensor_peak()
-    gu_tf = gu_flops / (gu_ms / 1e3) / 1e12
+    gu_tf = gu_flops / world / (gu_ms / 1e3) / 1e12        # per GPU
+    one = None
+    if ep:
+        # rank 0's tokens through the one-GPU layer (routing is per token)
+        same = None
+        if rank == 0:
+            full = S.synth_layer(spec, layer=0, device=local)
+            ref, _ = full.forward(x)
+            torch.cuda.synchronize()
+            same = bool(torch.equal(ref, out))
+            del full, ref
+            torch.cuda.empty_cache()
+        barrier()
+        one = {"tokens": T, "bit_identical": same}
+    per_rank = None
+    if ep:
+        per_rank = [sum(hist[r::world]) for r in range(world)]
+        group.set_placement("contiguous")
     return {
-        "workload": f"config3 prefill T={T}: config-1 layer, router biased to Zipf(1.1)",
-        "tokens_per_s": T / (ms / 1e3),
+        "workload": f"config3 prefill T={T} per GPU: config-1 layer, router biased to Zipf(1.1)"
+                    + (f", ep{world}, strided expert placement (expert e on GPU e % {world})"
+                       if ep else ""),
+        "tokens_per_s": world * T / (ms / 1e3),
         "ms_per_step": ms,
         "distinct_experts": distinct,
+        "top_expert_share": max(hist) / max(sum(hist), 1),
+        "routed_pairs_per_gpu": per_rank,
         "gate_up_ms": gu_ms,
         "down_combine_ms": dn_ms,
         "roofline": {"bound": "tensor", "kernel": "gemm gate/up (+SwiGLU), tcgen05",
                      "achieved": gu_tf, "peak": peak, "peak_kind": kind, "unit": "TFLOP/s",
-                     "frac": gu_tf / peak, "algorithmic_flops_per_launch": gu_flops},
-        "down_tflops": dn_flops / (dn_ms / 1e3) / 1e12,
+                     "frac": gu_tf / peak, "algorithmic_flops_per_step": gu_flops / world,
+                     "note": "per GPU: the group's gate/up FLOPs / N over the slowest GPU's "
+                             "gate/up time" if ep else "one GPU"},
+        "layer_tflops_per_gpu": (gu_flops + dn_flops) / world / (ms / 1e3) / 1e12,
+        "down_tflops": dn_flops / world / (dn_ms / 1e3) / 1e12,
+        "vs_one_gpu": one,
     }
 
 

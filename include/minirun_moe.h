@@ -457,19 +457,46 @@ mr_status mr_moe_layer_forward_host(mr_ctx* ctx, const mr_moe_layer* layer,
  *     so results equal mr_moe_layer_forward bit for bit;
  *   - NCCL (mr_ep_set_fused(ep, 0), or layouts the TMA GEMV cannot stream):
  *     per-token partial sums of the local slots and an NCCL reduce-scatter.
+ * The all-to-all mode (mr_ep_set_mode(ep, MR_EP_MODE_ALLTOALL)) replaces the
+ * all-gather: each rank routes only its own tokens and stores each token's
+ * row, once, into the receive slab of every rank that holds one of its
+ * experts (NVLink peer stores), with its k expert ids and weights; a
+ * dispatch epoch per source rank (bounded wait) tells the receiver that the
+ * rows are complete. The receiver runs its experts over the pairs sent to
+ * it and the way back is the fused one above (bit-identical to one GPU).
  * NCCL (libnccl.so.2) is loaded when the first group is created. */
 typedef struct mr_ep mr_ep;
 #define MR_EP_ID_BYTES 128
+#define MR_EP_MODE_ALLGATHER 0 /* NCCL all-gather of tokens, fused peer combine */
+#define MR_EP_MODE_NCCL 1      /* NCCL all-gather + NCCL reduce-scatter        */
+#define MR_EP_MODE_ALLTOALL 2  /* peer all-to-all dispatch, fused peer combine */
+#define MR_EP_PLACE_CONTIGUOUS 0 /* rank r holds experts [r*E/W, (r+1)*E/W)       */
+#define MR_EP_PLACE_STRIDED 1    /* rank r holds experts r, r+W, r+2W, ... (E/W)  */
 
 /* A new group id (one rank creates it; the host gives its bytes to all). */
 mr_status mr_ep_unique_id(void* id);
 /* Join the group with this rank's context (its device). Collective: blocks
  * until every rank has joined. */
 mr_status mr_ep_create(mr_ctx* ctx, const void* id, int rank, int world, mr_ep** out);
+/* The same over a communicator the caller already has (an ncclComm_t of
+ * `world` ranks in which this process is `rank`, on this context's device):
+ * no second communicator is built; the caller keeps ownership and destroys
+ * it after mr_ep_destroy. For a host engine that already runs NCCL and
+ * hands its communicator to the expert backend. */
+mr_status mr_ep_init(mr_ctx* ctx, void* nccl_comm, int rank, int world, mr_ep** out);
 mr_status mr_ep_destroy(mr_ep* ep);
 /* 1 (default): fused down GEMV + peer stores; 0: NCCL reduce-scatter. Every
  * rank of the group must choose the same. */
 mr_status mr_ep_set_fused(mr_ep* ep, int fused);
+/* MR_EP_MODE_*; every rank must choose the same. The all-to-all mode needs
+ * the staged GEMV (kernel path 0 or 4) and TMA-streamable stacks; otherwise
+ * the all-gather form runs. */
+mr_status mr_ep_set_mode(mr_ep* ep, int mode);
+/* MR_EP_PLACE_*: which E/world global experts this rank's stacks hold, in
+ * increasing id order (default contiguous). Strided placement spreads
+ * routers that favour low expert ids (a skewed load) over every rank. Every
+ * rank must choose the same, before its first forward with that layout. */
+mr_status mr_ep_set_placement(mr_ep* ep, int placement);
 /* Expert-parallel mr_moe_layer_forward. layer->gate/up/down are this rank's
  * E/world experts (experts == router.experts / world, stacks only);
  * everything else as mr_moe_layer_forward. Every rank passes the same

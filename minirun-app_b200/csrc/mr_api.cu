@@ -1110,7 +1110,7 @@ static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
                              float* margins, float* logits_out, bool plan, int* nseg, int4* segs,
                              int* cols, int seg_cols, cudaStream_t s, int plan_base = 0,
                              int plan_experts = -1, bool foreign_ok = false,
-                             const HashChoice* hc = nullptr) {
+                             const HashChoice* hc = nullptr, int plan_stride = 1) {
   TopkParams tp{};
   tp.part = part;
   tp.ks = ks;
@@ -1133,7 +1133,7 @@ static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
                        nseg,    segs,
                        cols,    ctx->d_error,
                        seg_cols, plan_base,
-                       foreign_ok ? 1 : 0};
+                       foreign_ok ? 1 : 0, plan_stride};
   tp.counter = ctx->d_counters + (kMaxCounters - 1);
   if (hc) {
     tp.hash_map = hc->table;
@@ -1263,6 +1263,7 @@ struct RoutePlan {
   int base;
   int experts;
   bool foreign_ok;
+  int stride = 1;  // strided expert placement: local e = global base + e * stride
 };
 
 // Router logits (fused with the activation prep: permuted x and group sums),
@@ -1298,7 +1299,8 @@ static mr_status route_tokens(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t
   if (st) return st;
   ProfScope ps(ctx, MR_KERNEL_TOPK_PLAN, s);
   return topk_launch(ctx, part, ls.kq, T, &L->router, ids, wts, margins, nullptr, true, rp.nseg,
-                     rp.segs, rp.cols, rp.seg_cols, s, rp.base, rp.experts, rp.foreign_ok, hc);
+                     rp.segs, rp.cols, rp.seg_cols, s, rp.base, rp.experts, rp.foreign_ok, hc,
+                     rp.stride);
 }
 
 // One K1 (gate/up + SwiGLU -> h, hsum) and K2 (down -> per-slot partials)
@@ -1445,6 +1447,12 @@ static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRu
     d.peer_n = r.peer->peer_n;
     d.peer_rank = r.peer->peer_rank;
     d.peer_epoch = r.peer->peer_epoch;
+    d.peer_row_tok = r.peer->peer_row_tok;
+    d.peer_rows = r.peer->peer_rows;
+    if (d.peer_row_tok && !r.pf && !use_v2(ctx))
+      return fail(ctx, MR_ERR_UNSUPPORTED,
+                  "the all-to-all dispatch needs the staged GEMV (kernel path 0 or 4)");
+    if (r.um) return fail(ctx, MR_ERR_UNSUPPORTED, "expert parallel: no tcgen05 GEMV path");
   }
   ProfScope ps(ctx, MR_KERNEL_DOWN_COMBINE, s);
   const MapSpec maps[4] = {{&L->down, E}, {nullptr, 0},
@@ -2032,7 +2040,7 @@ mr_status nccl_check(mr_ctx* ctx, ncclResult_t r, const char* what) {
 // (ids in [base, base + local)), in slot order; other slots contribute 0.
 __global__ void ep_partial_kernel(const float* __restrict__ part, const int32_t* __restrict__ ids,
                                   const float* __restrict__ weights, int T, int k, int64_t H,
-                                  int base, int local, int weight_after_down,
+                                  int base, int local, int stride, int weight_after_down,
                                   float* __restrict__ y) {
   const int64_t n = (int64_t)T * H;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -2042,8 +2050,8 @@ __global__ void ep_partial_kernel(const float* __restrict__ part, const int32_t*
     float s = 0.0f;
     for (int j = 0; j < k; ++j) {
       const int p = t * k + j;
-      const int e = __ldg(ids + p) - base;
-      if (e < 0 || e >= local) continue;
+      const int g = __ldg(ids + p) - base;
+      if (g < 0 || g % stride != 0 || g / stride >= local) continue;
       const float v = __ldg(part + (int64_t)p * H + row);
       s += weight_after_down ? v * __ldg(weights + p) : v;
     }
@@ -2118,23 +2126,198 @@ __global__ void ep_wait_combine_kernel(const float* __restrict__ part,
   }
 }
 
+// ---------------------------------------------------------------------------
+// All-to-all dispatch over peer memory. A rank routes only its own tokens and
+// sends each token's row (once) to every rank that holds one of its experts,
+// with the token's k expert ids and weights and its index; the receiving
+// rank runs its experts over the received pairs and its down GEMV stores
+// each pair's partial back into the home rank's combine buffer.
+//
+// Dispatch area of a rank's receive buffer (per source rank r, Tcap rows):
+//   rows [W][Tcap][H] bf16 | ids [W][Tcap][k] int32 | wts [W][Tcap][k] f32 |
+//   tok [W][Tcap] int32 (the row's index among its home rank's tokens)
+struct A2ALayout {
+  int64_t rows, ids, wts, tok, bytes;  // byte offsets and total
+};
+A2ALayout a2a_layout(int W, int64_t Tcap, int k, int64_t H) {
+  auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
+  A2ALayout l;
+  l.rows = 0;
+  l.ids = up(l.rows + (int64_t)W * Tcap * H * 2);
+  l.wts = up(l.ids + (int64_t)W * Tcap * k * 4);
+  l.tok = up(l.wts + (int64_t)W * Tcap * k * 4);
+  l.bytes = up(l.tok + (int64_t)W * Tcap * 4);
+  return l;
+}
+
+// One CTA per destination rank d: pos[d][t] = the compact position of this
+// rank's token t among its tokens with a slot on one of d's experts (tokens
+// in order), -1 for the others; count[d] = how many. Rank of expert g:
+// g / El (contiguous placement) or g % W (strided, stride = W).
+__global__ void a2a_plan_kernel(const int32_t* __restrict__ ids, int T, int k, int El,
+                                int stride, int* __restrict__ pos, int* __restrict__ count) {
+  const int d = blockIdx.x;
+  __shared__ int wsum[32];
+  __shared__ int carry;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+    const int t = t0 + tid;
+    int f = 0;
+    if (t < T)
+      for (int j = 0; j < k; ++j) {
+        const int g = __ldg(ids + (int64_t)t * k + j);  // its rank: g / El, or g % W strided
+        if (stride > 1 ? (g % stride == d) : ((unsigned)(g - d * El) < (unsigned)El)) f = 1;
+      }
+    int incl = f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) wsum[wid] = incl;
+    __syncthreads();
+    int before = carry;
+    for (int w = 0; w < wid; ++w) before += wsum[w];
+    if (t < T) pos[(int64_t)d * T + t] = f ? before + incl - f : -1;
+    __syncthreads();  // carry and wsum read by every thread
+    if (tid == 0) {
+      int tot = 0;
+      for (int w = 0; w < nw; ++w) tot += wsum[w];
+      carry += tot;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) count[d] = carry;
+}
+
+struct A2ADispatch {
+  const uint16_t* x;
+  const int32_t* ids;
+  const float* wts;
+  const int* pos;
+  const int* count;
+  char* const* disp;  // every rank's dispatch area
+  unsigned* const* dflags;
+  unsigned* const* dcount;
+  unsigned* done;     // CTA counter (zero between launches)
+  int T, k, W, rank, rows_per_cta;
+  int64_t H, Tcap;
+  A2ALayout lay;
+  unsigned epoch;
+};
+
+// Grid (token chunks, destination ranks): a warp per token stores its row,
+// ids, weights and index into the destination's slab of this rank (NVLink
+// stores for other GPUs). The last CTA publishes, into every destination,
+// this rank's row count and then the step epoch (system-scope release).
+__global__ void a2a_copy_kernel(const A2ADispatch p) {
+  const int d = blockIdx.y;
+  char* base = p.disp[d];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int t0 = blockIdx.x * p.rows_per_cta;
+  const int t1 = min(p.T, t0 + p.rows_per_cta);
+  const int64_t chunks = p.H / 8;  // 16-byte chunks per row
+  for (int t = t0 + warp; t < t1; t += nwarps) {
+    const int q = __ldg(p.pos + (int64_t)d * p.T + t);
+    if (q < 0) continue;
+    const int64_t row = (int64_t)p.rank * p.Tcap + q;
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + (int64_t)t * p.H);
+    uint4* dst = reinterpret_cast<uint4*>(base + p.lay.rows + row * p.H * 2);
+    for (int64_t c = lane; c < chunks; c += 32) dst[c] = __ldg(src + c);
+    if (lane < p.k) {
+      reinterpret_cast<int32_t*>(base + p.lay.ids)[row * p.k + lane] =
+          __ldg(p.ids + (int64_t)t * p.k + lane);
+      reinterpret_cast<float*>(base + p.lay.wts)[row * p.k + lane] =
+          __ldg(p.wts + (int64_t)t * p.k + lane);
+    }
+    if (lane == 0) reinterpret_cast<int32_t*>(base + p.lay.tok)[row] = t;
+  }
+  __threadfence_system();  // this thread's stores, before the CTA's count
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned prev = atomicAdd(p.done, 1u);
+    if (prev == gridDim.x * gridDim.y - 1) {
+      *p.done = 0;  // for the next launch on this GPU
+      __threadfence_system();
+      for (int j = 0; j < p.W; ++j) {
+        p.dcount[j][p.rank] = (unsigned)__ldg(p.count + j);
+        st_release_sys(p.dflags[j] + p.rank, p.epoch);  // orders the count store before it
+      }
+    }
+  }
+}
+
+// Receiving rank, one CTA: bounded wait until every source rank has published
+// this step's epoch (a timeout sets MR_DEVERR_TIMEOUT and leaves every row
+// empty), then the expert ids of the received rows for the routing plan: the
+// slab's ids where a row was sent this step, -1 (no local expert) elsewhere.
+__global__ void a2a_receive_kernel(const unsigned* dflags, const unsigned* dcount, int W,
+                                   unsigned epoch, uint32_t spin_limit,
+                                   const int32_t* slab_ids, int64_t Tcap, int k,
+                                   int32_t* __restrict__ ids_out, unsigned* error) {
+  __shared__ int n[64];
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    for (int j = 0; j < W && ok; ++j) {
+      uint32_t i = 0;
+      while (ld_acquire_sys(dflags + j) < epoch) {
+        if (++i >= spin_limit) {
+          atomicOr(error, MR_DEVERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    for (int j = 0; j < W; ++j) n[j] = ok ? (int)ld_acquire_sys(dcount + j) : 0;
+  }
+  __syncthreads();
+  const int64_t total = (int64_t)W * Tcap * k;
+  for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+    const int64_t row = i / k;
+    const int r = (int)(row / Tcap);
+    const int64_t q = row - (int64_t)r * Tcap;
+    ids_out[i] = q < n[r] ? slab_ids[i] : -1;
+  }
+}
+
 }  // namespace
 
 struct mr_ep {
   ncclComm_t comm = nullptr;
+  bool owns_comm = true;  // false: a caller's communicator (mr_ep_init)
   int rank = 0;
   int world = 1;
   int device = 0;
-  // fused path: this rank's receive buffer (flags | partials), mapped by
-  // every rank through CUDA IPC; device tables of every rank's pointers
-  bool fused = true;
-  void* buf = nullptr;       // [256 B of flags: one word per rank, W <= 64][partials]
+  // MR_EP_MODE_*: all-gather + fused peer combine, NCCL reduce-scatter, or
+  // peer all-to-all dispatch + fused peer combine
+  int mode = MR_EP_MODE_ALLGATHER;
+  int placement = MR_EP_PLACE_CONTIGUOUS;  // which global experts this rank's stacks hold
+  // peer paths: this rank's receive buffer, mapped by every rank through
+  // CUDA IPC:
+  //   [0, 256)     combine epochs, one word per source rank (W <= 64)
+  //   [256, 512)   dispatch epochs, one word per source rank
+  //   [512, 768)   dispatch row counts, one word per source rank
+  //   [1024, ...)  partial rows of this rank's (token, slot) pairs and
+  //                shared-expert rows, then (all-to-all) the dispatch slabs
+  void* buf = nullptr;
   bool peer_failed = false;  // some rank could not map a peer buffer: NCCL path
   size_t buf_bytes = 0;
   std::vector<void*> opened;  // peers' buffers opened here
+  std::vector<char*> bases;   // every rank's buffer as mapped here
+  // device tables of every rank's pointers, for the current layout
   float** d_parts = nullptr;  // [world]
   unsigned** d_flags = nullptr;
+  unsigned** d_dflags = nullptr;
+  unsigned** d_dcount = nullptr;
+  char** d_disp = nullptr;
   unsigned* d_done = nullptr;
+  unsigned* d_ddone = nullptr;  // the dispatch kernel's CTA counter
+  size_t tab_parts_bytes = ~(size_t)0;  // layout the tables were built for
   unsigned epoch = 0;
 };
 
@@ -2172,9 +2355,40 @@ mr_status mr_ep_create(mr_ctx* ctx, const void* id, int rank, int world, mr_ep**
   return MR_OK;
 }
 
+mr_status mr_ep_init(mr_ctx* ctx, void* nccl_comm, int rank, int world, mr_ep** out) {
+  if (!ctx || !nccl_comm || !out || world < 1 || rank < 0 || rank >= world)
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                "expert-parallel group needs a communicator and 0 <= rank < world");
+  *out = nullptr;
+  const NcclApi& api = nccl_api();
+  if (!api.ok) return fail(ctx, MR_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  mr_ep* ep = new mr_ep;
+  ep->comm = static_cast<ncclComm_t>(nccl_comm);
+  ep->owns_comm = false;
+  ep->rank = rank;
+  ep->world = world;
+  ep->device = ctx->device;
+  *out = ep;
+  return MR_OK;
+}
+
 mr_status mr_ep_set_fused(mr_ep* ep, int fused) {
   if (!ep) return MR_ERR_INVALID_ARGUMENT;
-  ep->fused = fused != 0;
+  ep->mode = fused ? MR_EP_MODE_ALLGATHER : MR_EP_MODE_NCCL;
+  return MR_OK;
+}
+
+mr_status mr_ep_set_mode(mr_ep* ep, int mode) {
+  if (!ep || mode < MR_EP_MODE_ALLGATHER || mode > MR_EP_MODE_ALLTOALL)
+    return MR_ERR_INVALID_ARGUMENT;
+  ep->mode = mode;
+  return MR_OK;
+}
+
+mr_status mr_ep_set_placement(mr_ep* ep, int placement) {
+  if (!ep || (placement != MR_EP_PLACE_CONTIGUOUS && placement != MR_EP_PLACE_STRIDED))
+    return MR_ERR_INVALID_ARGUMENT;
+  ep->placement = placement;
   return MR_OK;
 }
 
@@ -2186,127 +2400,410 @@ mr_status mr_ep_destroy(mr_ep* ep) {
   for (void* p : ep->opened) cudaIpcCloseMemHandle(p);
   if (ep->buf) cudaFree(ep->buf);
   if (ep->d_parts) cudaFree(ep->d_parts);
-  if (ep->comm && nccl_api().comm_destroy(ep->comm) != ncclSuccess) st = MR_ERR_NCCL;
+  if (ep->comm && ep->owns_comm && nccl_api().comm_destroy(ep->comm) != ncclSuccess)
+    st = MR_ERR_NCCL;
   delete ep;
   return st;
 }
 
 }  // extern "C"
 
-// Fused path: (re)creates this rank's receive buffer when `need` bytes do not
-// fit and maps every rank's through CUDA IPC. Collective: every rank calls it
-// in the same forward (the shapes are the same on every rank), so the NCCL
-// steps below line up. Old buffers are released only after a barrier, once no
-// rank can still be writing into them.
-static mr_status ep_peer_setup(mr_ctx* ctx, mr_ep* ep, size_t need, cudaStream_t s) {
-  if (ep->buf && ep->buf_bytes >= need) return MR_OK;
+// Peer paths: (re)creates this rank's receive buffer when `need` bytes (after
+// its 1 KiB header) do not fit and maps every rank's through CUDA IPC, then
+// (re)builds the device pointer tables for a layout whose partial rows take
+// `parts_bytes` (the dispatch slabs follow them). Collective: every rank
+// calls it in the same forward (the shapes are the same on every rank), so
+// the NCCL steps below line up. Old buffers are released only after a
+// barrier, once no rank can still be writing into them. A peer that cannot
+// be mapped on any rank sets peer_failed on every rank (agreed by an
+// all-reduce); the group then takes the NCCL path.
+static mr_status ep_peer_setup(mr_ctx* ctx, mr_ep* ep, size_t need, size_t parts_bytes,
+                               cudaStream_t s) {
   const NcclApi& api = nccl_api();
   const int W = ep->world;
   mr_status st;
-  void* tmp = nullptr;
-  if ((st = cuda_check(ctx, cudaMalloc(&tmp, (size_t)(W + 1) * sizeof(cudaIpcMemHandle_t)),
-                       "cudaMalloc(ipc handles)")))
-    return st;
-  char* send = static_cast<char*>(tmp);
-  char* recv = send + sizeof(cudaIpcMemHandle_t);
-  auto cleanup = [&] { cudaFree(tmp); };
-  // barrier: every rank has finished its previous steps (and writes into the old buffers)
-  if ((st = cuda_check(ctx, cudaStreamSynchronize(s), "sync")) ||
-      (st = nccl_check(ctx, api.all_gather(send, recv, sizeof(cudaIpcMemHandle_t), ncclInt8,
-                                           ep->comm, s),
-                       "ncclAllGather(barrier)")) ||
-      (st = cuda_check(ctx, cudaStreamSynchronize(s), "sync"))) {
-    cleanup();
-    return st;
-  }
-  for (void* p : ep->opened) cudaIpcCloseMemHandle(p);
-  ep->opened.clear();
-  if (ep->buf) cudaFree(ep->buf);
-  if (ep->d_parts) cudaFree(ep->d_parts);
-  ep->buf = nullptr;
-  ep->d_parts = nullptr;
-  ep->buf_bytes = 0;
-  const size_t bytes = need + need / 4 + (1 << 20);
-  cudaIpcMemHandle_t mine;
-  if ((st = cuda_check(ctx, cudaMalloc(&ep->buf, bytes), "cudaMalloc(peer buffer)")) ||
-      (st = cuda_check(ctx, cudaMemset(ep->buf, 0, bytes), "clear peer buffer")) ||
-      (st = cuda_check(ctx, cudaIpcGetMemHandle(&mine, ep->buf), "cudaIpcGetMemHandle")) ||
-      (st = cuda_check(ctx, cudaMemcpy(send, &mine, sizeof mine, cudaMemcpyHostToDevice),
-                       "stage ipc handle")) ||
-      (st = nccl_check(ctx, api.all_gather(send, recv, sizeof(cudaIpcMemHandle_t), ncclInt8,
-                                           ep->comm, s),
-                       "ncclAllGather(ipc handles)")) ||
-      (st = cuda_check(ctx, cudaStreamSynchronize(s), "sync"))) {
-    cleanup();
-    return st;
-  }
-  std::vector<cudaIpcMemHandle_t> all(W);
-  st = cuda_check(ctx, cudaMemcpy(all.data(), recv, W * sizeof(cudaIpcMemHandle_t),
-                                  cudaMemcpyDeviceToHost),
-                  "read ipc handles");
-  cleanup();
-  if (st) return st;
-  std::vector<void*> bases(W);
-  int open_failed = 0;
-  for (int j = 0; j < W && !open_failed; ++j) {
-    if (j == ep->rank) {
-      bases[j] = ep->buf;
-      continue;
-    }
-    void* p = nullptr;
-    if (cudaIpcOpenMemHandle(&p, all[j], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-      (void)cudaGetLastError();
-      open_failed = 1;
-      break;
-    }
-    ep->opened.push_back(p);
-    bases[j] = p;
-  }
-  // every rank learns whether any rank could not map a peer (e.g. ranks on
-  // different nodes): then all of them take the NCCL path, in step
-  {
-    int* flag = nullptr;
-    if ((st = cuda_check(ctx, cudaMalloc(&flag, sizeof(int)), "cudaMalloc(open flag)"))) return st;
-    int any = 0;
-    if ((st = cuda_check(ctx, cudaMemcpy(flag, &open_failed, sizeof(int), cudaMemcpyHostToDevice),
-                         "stage open flag")) ||
-        (st = nccl_check(ctx, nccl_api().all_reduce(flag, flag, 1, ncclInt32, ncclMax, ep->comm, s),
-                         "ncclAllReduce(open flag)")) ||
-        (st = cuda_check(ctx, cudaMemcpyAsync(&any, flag, sizeof(int), cudaMemcpyDeviceToHost, s),
-                         "read open flag")) ||
+  need += 1024;
+  if (!ep->buf || ep->buf_bytes < need) {
+    void* tmp = nullptr;
+    if ((st = cuda_check(ctx, cudaMalloc(&tmp, (size_t)(W + 1) * sizeof(cudaIpcMemHandle_t)),
+                         "cudaMalloc(ipc handles)")))
+      return st;
+    char* send = static_cast<char*>(tmp);
+    char* recv = send + sizeof(cudaIpcMemHandle_t);
+    auto cleanup = [&] { cudaFree(tmp); };
+    // barrier: every rank has finished its previous steps (and writes into the old buffers)
+    if ((st = cuda_check(ctx, cudaStreamSynchronize(s), "sync")) ||
+        (st = nccl_check(ctx, api.all_gather(send, recv, sizeof(cudaIpcMemHandle_t), ncclInt8,
+                                             ep->comm, s),
+                         "ncclAllGather(barrier)")) ||
         (st = cuda_check(ctx, cudaStreamSynchronize(s), "sync"))) {
-      cudaFree(flag);
+      cleanup();
       return st;
     }
-    cudaFree(flag);
-    if (any) {
-      for (void* q : ep->opened) cudaIpcCloseMemHandle(q);
-      ep->opened.clear();
-      cudaFree(ep->buf);
-      ep->buf = nullptr;
-      ep->peer_failed = true;
-      return MR_OK;
+    for (void* p : ep->opened) cudaIpcCloseMemHandle(p);
+    ep->opened.clear();
+    ep->bases.clear();
+    if (ep->buf) cudaFree(ep->buf);
+    ep->buf = nullptr;
+    ep->buf_bytes = 0;
+    ep->tab_parts_bytes = ~(size_t)0;
+    const size_t bytes = need + need / 4 + (1 << 20);
+    cudaIpcMemHandle_t mine;
+    if ((st = cuda_check(ctx, cudaMalloc(&ep->buf, bytes), "cudaMalloc(peer buffer)")) ||
+        (st = cuda_check(ctx, cudaMemset(ep->buf, 0, bytes), "clear peer buffer")) ||
+        (st = cuda_check(ctx, cudaIpcGetMemHandle(&mine, ep->buf), "cudaIpcGetMemHandle")) ||
+        (st = cuda_check(ctx, cudaMemcpy(send, &mine, sizeof mine, cudaMemcpyHostToDevice),
+                         "stage ipc handle")) ||
+        (st = nccl_check(ctx, api.all_gather(send, recv, sizeof(cudaIpcMemHandle_t), ncclInt8,
+                                             ep->comm, s),
+                         "ncclAllGather(ipc handles)")) ||
+        (st = cuda_check(ctx, cudaStreamSynchronize(s), "sync"))) {
+      cleanup();
+      return st;
+    }
+    std::vector<cudaIpcMemHandle_t> all(W);
+    st = cuda_check(ctx, cudaMemcpy(all.data(), recv, W * sizeof(cudaIpcMemHandle_t),
+                                    cudaMemcpyDeviceToHost),
+                    "read ipc handles");
+    cleanup();
+    if (st) return st;
+    std::vector<char*> bases(W, nullptr);
+    int open_failed = 0;
+    for (int j = 0; j < W && !open_failed; ++j) {
+      if (j == ep->rank) {
+        bases[j] = static_cast<char*>(ep->buf);
+        continue;
+      }
+      void* p = nullptr;
+      if (cudaIpcOpenMemHandle(&p, all[j], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        (void)cudaGetLastError();
+        open_failed = 1;
+        break;
+      }
+      ep->opened.push_back(p);
+      bases[j] = static_cast<char*>(p);
+    }
+    // every rank learns whether any rank could not map a peer (e.g. ranks on
+    // different nodes): then all of them take the NCCL path, in step
+    {
+      int* flag = nullptr;
+      if ((st = cuda_check(ctx, cudaMalloc(&flag, sizeof(int)), "cudaMalloc(open flag)")))
+        return st;
+      int any = 0;
+      if ((st = cuda_check(ctx, cudaMemcpy(flag, &open_failed, sizeof(int),
+                                           cudaMemcpyHostToDevice),
+                           "stage open flag")) ||
+          (st = nccl_check(ctx, api.all_reduce(flag, flag, 1, ncclInt32, ncclMax, ep->comm, s),
+                           "ncclAllReduce(open flag)")) ||
+          (st = cuda_check(ctx, cudaMemcpyAsync(&any, flag, sizeof(int), cudaMemcpyDeviceToHost,
+                                                s),
+                           "read open flag")) ||
+          (st = cuda_check(ctx, cudaStreamSynchronize(s), "sync"))) {
+        cudaFree(flag);
+        return st;
+      }
+      cudaFree(flag);
+      if (any) {
+        for (void* q : ep->opened) cudaIpcCloseMemHandle(q);
+        ep->opened.clear();
+        cudaFree(ep->buf);
+        ep->buf = nullptr;
+        ep->peer_failed = true;
+        return MR_OK;
+      }
+    }
+    ep->bases = bases;
+    ep->buf_bytes = bytes;
+    ep->epoch = 0;  // flags were cleared with the buffers, on every rank
+  }
+  if (ep->tab_parts_bytes != parts_bytes) {
+    // device tables: partials, combine epochs, dispatch epochs, dispatch
+    // counts, dispatch slabs (per rank), then the two CTA counters
+    if ((st = cuda_check(ctx, cudaStreamSynchronize(s), "sync"))) return st;
+    std::vector<uint64_t> tab(5 * W + 2, 0);
+    for (int j = 0; j < W; ++j) {
+      char* b = ep->bases[j];
+      tab[j] = reinterpret_cast<uint64_t>(b + 1024);
+      tab[W + j] = reinterpret_cast<uint64_t>(b);
+      tab[2 * W + j] = reinterpret_cast<uint64_t>(b + 256);
+      tab[3 * W + j] = reinterpret_cast<uint64_t>(b + 512);
+      tab[4 * W + j] = reinterpret_cast<uint64_t>(b + 1024 + parts_bytes);
+    }
+    if (!ep->d_parts) {
+      void* d = nullptr;
+      if ((st = cuda_check(ctx, cudaMalloc(&d, tab.size() * 8), "cudaMalloc(peer tables)")))
+        return st;
+      ep->d_parts = static_cast<float**>(d);
+    }
+    if ((st = cuda_check(ctx, cudaMemcpy(ep->d_parts, tab.data(), tab.size() * 8,
+                                         cudaMemcpyHostToDevice),
+                         "upload peer tables")))
+      return st;
+    uint64_t* t = reinterpret_cast<uint64_t*>(ep->d_parts);
+    ep->d_flags = reinterpret_cast<unsigned**>(t + W);
+    ep->d_dflags = reinterpret_cast<unsigned**>(t + 2 * W);
+    ep->d_dcount = reinterpret_cast<unsigned**>(t + 3 * W);
+    ep->d_disp = reinterpret_cast<char**>(t + 4 * W);
+    ep->d_done = reinterpret_cast<unsigned*>(t + 5 * W);
+    ep->d_ddone = reinterpret_cast<unsigned*>(t + 5 * W + 1);
+    ep->tab_parts_bytes = parts_bytes;
+  }
+  return MR_OK;
+}
+
+// All-to-all form of mr_moe_layer_forward_ep (mode MR_EP_MODE_ALLTOALL):
+// route this rank's T tokens, dispatch their rows to the ranks that hold
+// their experts (peer stores + epochs), receive, prep and plan the rows sent
+// here, run this rank's experts over them with the down GEMV storing each
+// pair's partial into its home rank's combine buffer, then the shared expert
+// and the slot-ordered combine on the home rank (bit-identical to one GPU).
+// Cross-step ordering: a rank's dispatch of step e+1 follows its combine of
+// step e, which waited for every rank's step-e down GEMV, which ran after that
+// rank had read its step-e slabs (prep, plan, gate/up): no slab is
+// overwritten while in use. A down GEMV of step e+1 follows its rank's wait
+// for every rank's step-e+1 dispatch, which each rank issues after its own
+// step-e combine: no combine buffer is overwritten while in use.
+static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, const uint16_t* x,
+                                int64_t T, uint16_t* out, int32_t* ids_out, cudaStream_t s) {
+  const int W = ep->world, rank = ep->rank;
+  const int E = L->router.experts, k = L->router.top_k;
+  const int El = E / W;
+  const int stride = ep->placement == MR_EP_PLACE_STRIDED ? W : 1;
+  const int base = stride > 1 ? rank : rank * El;
+  const int64_t H = L->hidden, I = L->inter;
+  const int64_t Tk = T * k, R = (int64_t)W * T, RK = R * k;  // received rows / pair ids
+  const bool has_shared = L->shared_inter > 0;
+  const int wad = L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0;
+  if (RK > (int64_t)1 << 28) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
+  if (k > 32) return fail(ctx, MR_ERR_UNSUPPORTED, "the all-to-all dispatch takes top-k <= 32");
+  const int seg_own = pick_seg_cols(Tk);
+  const int64_t max_own = std::min<int64_t>(E, Tk) + Tk / seg_own + 1;
+  // prefill-size batches (>= 32 routed columns per expert on average over the
+  // group's tokens): the tcgen05 grouped GEMM, as one GPU would choose
+  const int bits = L->gate.bits;
+  bool pf = (ctx->kernel_path == 0 || ctx->kernel_path == 3) && H % 512 == 0 && I % 512 == 0 &&
+            (bits == 4 || bits == 8) && L->up.bits == bits && L->down.bits == bits &&
+            (!has_shared || (L->shared_gate.bits == bits && L->shared_up.bits == bits &&
+                             L->shared_down.bits == bits)) &&
+            (int64_t)T * W * k >= 32 * (int64_t)E;
+  const bool pf_sh = pf && has_shared && T >= 32;  // the shared expert's own launch
+  int seg_cols = pf ? kPfN : decode_seg_cols(ctx, (int64_t)T * W * k, E);
+  const int64_t max_seg = std::min<int64_t>(El, RK) + RK / 8 + 1;
+  const LogitsShape ls = logits_shape(ctx, T, E, H);
+  mr_status st;
+
+  // peer buffer: combine rows of this rank's pairs (+ shared), then the slabs
+  const int64_t rows = Tk + (has_shared ? 2 * T : 0);
+  const size_t parts = ((size_t)rows * H * sizeof(float) + 255) / 256 * 256;
+  const A2ALayout lay = a2a_layout(W, T, k, H);
+  if ((st = ep_peer_setup(ctx, ep, parts + (size_t)lay.bytes, parts, s))) return st;
+  if (ep->peer_failed) return MR_ERR_STATE;  // caller falls back to the NCCL path
+
+  uint16_t *xperm = nullptr, *xrecv = nullptr, *h = nullptr, *hs = nullptr;
+  float *part = nullptr, *xsum = nullptr, *xsrecv = nullptr, *wts = nullptr, *hsum = nullptr;
+  float *hss = nullptr, *dummy = nullptr;
+  int32_t *ids = nullptr, *ids_recv = nullptr;
+  int *nseg0 = nullptr, *cols0 = nullptr, *nseg = nullptr, *cols = nullptr, *zero = nullptr;
+  int *pos = nullptr, *count = nullptr;
+  int4 *segs0 = nullptr, *segs = nullptr;
+  uint16_t* xg = nullptr;
+  float* xsg = nullptr;
+  Bump b{nullptr};
+  for (int pass = 0; pass < 2; ++pass) {
+    b.off = 0;
+    if (pf) {  // routed activation rows in plan order (tcgen05 GEMM)
+      xg = b.take<uint16_t>(RK * H);
+      xsg = b.take<float>(RK * (H / kGroup));
+    }
+    part = b.take<float>((size_t)ls.kq * T * E);
+    xperm = b.take<uint16_t>(T * H);
+    xsum = b.take<float>(T * (H / kGroup));
+    ids = b.take<int32_t>(Tk);
+    wts = b.take<float>(Tk);
+    nseg0 = b.take<int>(4);
+    segs0 = b.take<int4>(max_own);
+    cols0 = b.take<int>(Tk);
+    pos = b.take<int>((int64_t)W * T);
+    count = b.take<int>(W);
+    ids_recv = b.take<int32_t>(RK);
+    xrecv = b.take<uint16_t>(R * H);
+    xsrecv = b.take<float>(R * (H / kGroup));
+    nseg = b.take<int>(4);
+    zero = b.take<int>(4);
+    segs = b.take<int4>(max_seg);
+    cols = b.take<int>(RK);
+    h = b.take<uint16_t>(RK * I);
+    hsum = b.take<float>(RK * (I / 32));
+    hs = b.take<uint16_t>(2 * T * I);
+    hss = b.take<float>(2 * T * (I / 32));
+    dummy = b.take<float>(64);
+    if (pass == 0) {
+      if ((st = ensure_workspace(ctx, b.off))) return st;
+      b.base = reinterpret_cast<char*>(ctx->ws);
     }
   }
-  // device tables: part pointers, flag pointers, the done counter
-  std::vector<uint64_t> tab(2 * W + 1, 0);
-  for (int j = 0; j < W; ++j) {
-    tab[j] = reinterpret_cast<uint64_t>(static_cast<char*>(bases[j]) + 256);
-    tab[W + j] = reinterpret_cast<uint64_t>(bases[j]);
+  char* mybuf = static_cast<char*>(ep->buf);
+  float* mine = reinterpret_cast<float*>(mybuf + 1024);
+  char* slab = mybuf + 1024 + parts;
+  // tensor maps of the tcgen05 launches, before anything is enqueued (a map
+  // the driver refuses keeps the staged GEMV)
+  UmMaps um1, um2, us1, us2;
+  if (pf) {
+    const MapSpec m1[4] = {{&L->gate, El}, {&L->up, El}, {nullptr, 0}, {nullptr, 0}};
+    const MapSpec m2[4] = {{&L->down, El}, {nullptr, 0}, {nullptr, 0}, {nullptr, 0}};
+    pf = encode_umma(ctx, m1, EPI_SWIGLU, H, ActSpec{xg, RK, xsg}, ActSpec{xg, RK, xsg}, &um1,
+                     kPfN) &&
+         encode_umma(ctx, m2, EPI_PARTIAL, I, ActSpec{h, RK, hsum}, ActSpec{h, RK, hsum}, &um2,
+                     kPfN);
+    if (!pf) seg_cols = decode_seg_cols(ctx, (int64_t)T * W * k, E);
   }
-  void* d = nullptr;
-  if ((st = cuda_check(ctx, cudaMalloc(&d, tab.size() * 8), "cudaMalloc(peer tables)"))) return st;
-  if ((st = cuda_check(ctx, cudaMemcpy(d, tab.data(), tab.size() * 8, cudaMemcpyHostToDevice),
-                       "upload peer tables"))) {
-    cudaFree(d);
-    return st;
+  bool shared_pf = pf && pf_sh;
+  if (shared_pf) {
+    const MapSpec m1[4] = {{&L->gate, El}, {&L->up, El}, {&L->shared_gate, 1}, {&L->shared_up, 1}};
+    const MapSpec m2[4] = {{&L->down, El}, {nullptr, 0}, {&L->shared_down, 1}, {nullptr, 0}};
+    shared_pf = encode_umma(ctx, m1, EPI_SWIGLU, H, ActSpec{xperm, T, xsum},
+                            ActSpec{xperm, T, xsum}, &us1, kPfN) &&
+                encode_umma(ctx, m2, EPI_PARTIAL, I, ActSpec{hs, 2 * T, hss},
+                            ActSpec{hs, 2 * T, hss}, &us2, kPfN);
   }
-  ep->d_parts = static_cast<float**>(d);
-  ep->d_flags = reinterpret_cast<unsigned**>(static_cast<uint64_t*>(d) + W);
-  ep->d_done = reinterpret_cast<unsigned*>(static_cast<uint64_t*>(d) + 2 * W);
-  ep->buf_bytes = bytes;
-  ep->epoch = 0;  // flags were cleared with the buffers, on every rank
-  return MR_OK;
+  ++ep->epoch;
+
+  // 1. route this rank's tokens (the prep also gives the shared expert's rows)
+  {
+    const RoutePlan rp{nseg0, segs0, cols0, seg_own, 0, E, false};
+    if ((st = route_tokens(ctx, L, x, T, ls, part, xperm, xsum, ids, wts, nullptr, rp, s)))
+      return st;
+  }
+  // 2. dispatch: compact positions per destination, then rows + metadata
+  {
+    ProfScope ps(ctx, MR_KERNEL_EXCHANGE, s);
+    a2a_plan_kernel<<<W, 256, 0, s>>>(ids, (int)T, k, El, stride, pos, count);
+    if ((st = cuda_check(ctx, cudaGetLastError(), "a2a_plan_kernel"))) return st;
+    A2ADispatch dp{};
+    dp.x = x;
+    dp.ids = ids;
+    dp.wts = wts;
+    dp.pos = pos;
+    dp.count = count;
+    dp.disp = ep->d_disp;
+    dp.dflags = ep->d_dflags;
+    dp.dcount = ep->d_dcount;
+    dp.done = ep->d_ddone;
+    dp.T = (int)T;
+    dp.k = k;
+    dp.W = W;
+    dp.rank = rank;
+    dp.rows_per_cta = 8;
+    dp.H = H;
+    dp.Tcap = T;
+    dp.lay = lay;
+    dp.epoch = ep->epoch;
+    const dim3 grid((unsigned)((T + 7) / 8), (unsigned)W);
+    a2a_copy_kernel<<<grid, 256, 0, s>>>(dp);
+    if ((st = cuda_check(ctx, cudaGetLastError(), "a2a_copy_kernel"))) return st;
+    // 3. receive: every source's rows of this step, as expert ids per pair
+    a2a_receive_kernel<<<1, 1024, 0, s>>>(
+        reinterpret_cast<const unsigned*>(mybuf + 256), reinterpret_cast<const unsigned*>(mybuf + 512),
+        W, ep->epoch, kSpinLimit, reinterpret_cast<const int32_t*>(slab + lay.ids), T, k, ids_recv,
+        ctx->d_error);
+    if ((st = cuda_check(ctx, cudaGetLastError(), "a2a_receive_kernel"))) return st;
+  }
+  // 4. prep of the received rows and the plan of this rank's experts
+  {
+    PrepParams pp{reinterpret_cast<const uint16_t*>(slab + lay.rows), R, H, L->gate.bits, xrecv,
+                  xsrecv};
+    const int64_t chunks = R * (H / 16);
+    const int pgrid = (int)std::max<int64_t>(
+        1, std::min<int64_t>((chunks + 255) / 256, 4 * (int64_t)ctx->sm_count));
+    prep_kernel<<<pgrid, 256, 0, s>>>(pp);
+    if ((st = cuda_check(ctx, cudaGetLastError(), "prep_kernel"))) return st;
+    PlanParams plan{ids_recv, (int)RK, El, nseg, segs, cols, ctx->d_error, seg_cols, base, 1,
+                    stride};
+    plan_kernel<<<1, 256, 0, s>>>(plan);
+    if ((st = cuda_check(ctx, cudaGetLastError(), "plan_kernel"))) return st;
+    if (pf) {
+      const int64_t n = RK * (H / 8 + H / kGroup);
+      const int grid =
+          (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 8 * ctx->sm_count));
+      gather_act_kernel<<<grid, 256, 0, s>>>(xrecv, xsrecv, cols, (int)RK, k, (int)R, H, xg, xsg);
+      if ((st = cuda_check(ctx, cudaGetLastError(), "gather_act_kernel"))) return st;
+    }
+  }
+  // 5. this rank's experts; partials straight into the home ranks' buffers
+  {
+    ExpertsRun r{};
+    r.xperm = xrecv;
+    r.xsum = xsrecv;
+    r.tokens = R;
+    r.shared_tokens = 0;
+    r.Tk = RK;
+    r.k = k;
+    r.nseg = nseg;
+    r.segs = segs;
+    r.cols = cols;
+    r.max_seg = max_seg;
+    r.seg_cols = seg_cols;
+    r.wts = reinterpret_cast<const float*>(slab + lay.wts);
+    r.h = h;
+    r.hsum = hsum;
+    r.part2 = dummy;
+    r.pf = pf;
+    r.um1 = &um1;
+    r.um2 = &um2;
+    GemvParams peer{};
+    peer.peer_part = ep->d_parts;
+    peer.peer_cols = (int)Tk;
+    peer.peer_flags = ep->d_flags;
+    peer.peer_done = ep->d_done;
+    peer.peer_n = W;
+    peer.peer_rank = rank;
+    peer.peer_epoch = ep->epoch;
+    peer.peer_row_tok = reinterpret_cast<const int*>(slab + lay.tok);
+    peer.peer_rows = (int)T;
+    r.peer = &peer;
+    if ((st = run_experts(ctx, L, r, s))) return st;
+  }
+  // 6. shared expert over this rank's tokens, into its own combine rows
+  if (has_shared) {
+    if ((st = cuda_check(ctx, cudaMemsetAsync(zero, 0, 4 * sizeof(int), s), "clear count")))
+      return st;
+    ExpertsRun sh{};
+    sh.xperm = xperm;
+    sh.xsum = xsum;
+    sh.tokens = T;
+    sh.shared_tokens = T;
+    sh.Tk = 0;
+    sh.k = k;
+    sh.nseg = zero;
+    sh.segs = segs;
+    sh.cols = cols;
+    sh.max_seg = 0;
+    sh.seg_cols = seg_cols;
+    sh.wts = wts;
+    sh.h = hs;
+    sh.hsum = hss;
+    sh.part2 = mine + Tk * H;
+    sh.pf = shared_pf;
+    sh.um1 = &us1;
+    sh.um2 = &us2;
+    if (shared_pf) sh.seg_cols = kPfN;
+    if ((st = run_experts(ctx, L, sh, s))) return st;
+  }
+  // 7. wait for every rank's partials of this step, combine in slot order
+  {
+    const int64_t n = T * H;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
+    ProfScope pc(ctx, MR_KERNEL_COMBINE, s);
+    ep_wait_combine_kernel<<<grid, 256, 0, s>>>(mine, wts, (int)T, k, H, wad, has_shared ? 1 : 0,
+                                                reinterpret_cast<const unsigned*>(mybuf), W,
+                                                ep->epoch, kSpinLimit, ctx->d_error, out);
+    if ((st = cuda_check(ctx, cudaGetLastError(), "ep_wait_combine_kernel"))) return st;
+  }
+  if (ids_out)
+    st = cuda_check(ctx, cudaMemcpyAsync(ids_out, ids, Tk * sizeof(int32_t),
+                                         cudaMemcpyDeviceToDevice, s),
+                    "copy ids");
+  return st;
 }
 
 extern "C" {
@@ -2333,11 +2830,25 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
     return fail(ctx, MR_ERR_INVALID_ARGUMENT, "input must be a non-empty [tokens, hidden] matrix");
   if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0)
     return fail(ctx, MR_ERR_UNSUPPORTED, "x must be 16-byte aligned");
-  const int El = E / W, base = rank * El;
+  const int El = E / W;
+  // contiguous placement: experts [rank*El, (rank+1)*El); strided: rank, rank+W, ...
+  const int stride = ep->placement == MR_EP_PLACE_STRIDED ? W : 1;
+  const int base = stride > 1 ? rank : rank * El;
   const int64_t H = L->hidden, I = L->inter;
   const int64_t NT = T * W, NTk = NT * k;
   if (NTk > (int64_t)1 << 28) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
   const bool has_shared = L->shared_inter > 0;
+  // all-to-all dispatch: peer paths, the staged GEMV streaming both projections
+  if (ep->mode == MR_EP_MODE_ALLTOALL && W > 1 && W <= 64 && !ep->peer_failed &&
+      use_v2(ctx) && tma_layout_ok(H, &L->gate, false) && tma_layout_ok(H, &L->up, false) &&
+      tma_layout_ok(I, &L->down, false) &&
+      (!has_shared || (tma_layout_ok(H, &L->shared_gate, false) &&
+                       tma_layout_ok(H, &L->shared_up, false) &&
+                       tma_layout_ok(I, &L->shared_down, false)))) {
+    st = ep_forward_a2a(ctx, ep, L, x, T, out, ids_out, as_stream(stream));
+    if (st != MR_ERR_STATE || !ep->peer_failed) return st;
+    // a peer mapping failed on some rank (agreed by all): the NCCL path below
+  }
   const int seg_cols = decode_seg_cols(ctx, NTk, E);
   const int64_t max_seg = std::min<int64_t>(El, NTk) + NTk / seg_cols + 1;
   const LogitsShape ls = logits_shape(ctx, NT, E, H);
@@ -2385,7 +2896,7 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
       return st;
   }
   // router over all tokens (the same on every rank); plan of this rank's experts
-  const RoutePlan rp{nseg, segs, cols, seg_cols, base, El, true};
+  const RoutePlan rp{nseg, segs, cols, seg_cols, base, El, true, stride};
   if ((st = route_tokens(ctx, L, xall, NT, ls, part, xperm, xsum, ids, wts, nullptr, rp, s)))
     return st;
   // this rank's experts over the pairs routed to them
@@ -2407,14 +2918,15 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
   r.part2 = part2;
   const int wad = L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0;
   // the flag area of a receive buffer holds one word per rank (256 B)
-  bool fused = ep->fused && W > 1 && W <= 64 && !ep->peer_failed &&
+  bool fused = ep->mode != MR_EP_MODE_NCCL && W > 1 && W <= 64 && !ep->peer_failed &&
                use_tma(ctx, tma_layout_ok(I, &L->down, false) &&
                                 (!has_shared || tma_layout_ok(I, &L->shared_down, false)));
   if (fused) {
     // collective: the same decision on every rank (same shapes, and a failed
     // peer mapping on any rank is agreed on inside)
     const int64_t Tk = T * k, rows = Tk + (has_shared ? 2 * T : 0);
-    if ((st = ep_peer_setup(ctx, ep, 256 + (size_t)rows * H * sizeof(float), s))) return st;
+    const size_t parts = (size_t)rows * H * sizeof(float);
+    if ((st = ep_peer_setup(ctx, ep, parts, parts, s))) return st;
     fused = !ep->peer_failed;
   }
   if (fused) {
@@ -2439,7 +2951,7 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
     peer.peer_epoch = ep->epoch;
     r.peer = &peer;
     if ((st = run_experts(ctx, L, r, s))) return st;
-    float* mine = reinterpret_cast<float*>(static_cast<char*>(ep->buf) + 256);
+    float* mine = reinterpret_cast<float*>(static_cast<char*>(ep->buf) + 1024);
     if (has_shared) {
       if ((st = cuda_check(ctx, cudaMemsetAsync(zero, 0, 4 * sizeof(int), s), "clear count")))
         return st;
@@ -2474,7 +2986,8 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
       const int64_t n = NT * H;
       const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
       ProfScope pc(ctx, MR_KERNEL_COMBINE, s);
-      ep_partial_kernel<<<grid, 256, 0, s>>>(part2, ids, wts, (int)NT, k, H, base, El, wad, ypart);
+      ep_partial_kernel<<<grid, 256, 0, s>>>(part2, ids, wts, (int)NT, k, H, base, El, stride,
+                                             wad, ypart);
       if ((st = cuda_check(ctx, cudaGetLastError(), "ep_partial_kernel"))) return st;
     }
     // each token's sum over all ranks, back on its home rank

@@ -369,10 +369,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             if (jj >= nc) break;  // warp-uniform
             const int v = __shfl_sync(0xffffffffu, mv, jj);
             if (row_ok) {
-              if constexpr (EPI == EPI_STORE)
+              if constexpr (EPI == EPI_STORE) {
                 p.out_bf16[(int64_t)v * p.rows + grow] = f32_to_bf16_bits(d[jj]);
-              else
-                p.part[(int64_t)v * p.rows + grow] = (v < p.Tk) ? bf16_round(d[jj]) : d[jj];
+              } else {
+                float* dst = p.part;
+                int64_t vv = v;
+                if (p.peer_part && v < p.Tk) {  // the pair's home rank (possibly a peer GPU)
+                  if (p.peer_row_tok) {
+                    const int q = v / p.k;
+                    const int home = q / p.peer_rows;
+                    dst = p.peer_part[home];
+                    vv = (int64_t)__ldg(p.peer_row_tok + q) * p.k + (v - q * p.k);
+                  } else {
+                    const int home = v / p.peer_cols;
+                    dst = p.peer_part[home];
+                    vv = v - (int64_t)home * p.peer_cols;
+                  }
+                }
+                dst[vv * p.rows + grow] = (v < p.Tk) ? bf16_round(d[jj]) : d[jj];
+              }
             }
           }
         } else {
@@ -430,11 +445,26 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   }
 
+  if constexpr (EPI == EPI_PARTIAL) {
+    if (p.peer_flags) __threadfence_system();  // this thread's peer stores, before the count
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, ST::kTmemCols);
+  }
+  if constexpr (EPI == EPI_PARTIAL) {
+    // expert parallel: once every CTA's stores are out, tell every rank
+    if (p.peer_flags && threadIdx.x == 0) {
+      __threadfence_system();
+      const unsigned prev = atomicAdd(p.peer_done, 1u);
+      if (prev == gridDim.x - 1) {
+        *p.peer_done = 0;  // for the next launch on this GPU
+        __threadfence_system();
+        for (int j = 0; j < p.peer_n; ++j) st_release_sys(p.peer_flags[j] + p.peer_rank, p.peer_epoch);
+      }
+    }
   }
 }
 

@@ -85,6 +85,12 @@ struct GemvParams {
   // last one publishes peer_epoch into peer_flags[j][peer_rank] of every rank j
   float* const* peer_part;
   int peer_cols;
+  // all-to-all dispatch (staged kernel): routed column v is slot v % k of
+  // received row v / k; row q came from rank q / peer_rows, where it was
+  // token peer_row_tok[q], so its partial goes to that rank's pair
+  // peer_row_tok[q] * k + v % k (NULL: the all-gather layout above)
+  const int* peer_row_tok;
+  int peer_rows;
   unsigned* const* peer_flags;
   unsigned* peer_done;
   int peer_n;

@@ -553,9 +553,16 @@ __global__ void __launch_bounds__(kV2Threads, 1)
                 float* dst = p.part;
                 int64_t vv = v;
                 if (p.peer_part && routed) {  // the pair's home rank (possibly a peer GPU)
-                  const int home = (int)(v / p.peer_cols);
-                  dst = p.peer_part[home];
-                  vv = v - (int64_t)home * p.peer_cols;
+                  if (p.peer_row_tok) {        // received rows of the all-to-all dispatch
+                    const int q = (int)(v / p.k);
+                    const int home = q / p.peer_rows;
+                    dst = p.peer_part[home];
+                    vv = (int64_t)__ldg(p.peer_row_tok + q) * p.k + (v - (int64_t)q * p.k);
+                  } else {
+                    const int home = (int)(v / p.peer_cols);
+                    dst = p.peer_part[home];
+                    vv = v - (int64_t)home * p.peer_cols;
+                  }
                 }
                 if (row_a < p.rows)
                   dst[vv * p.rows + row_a] = routed ? bf16_round(y[t][i]) : y[t][i];

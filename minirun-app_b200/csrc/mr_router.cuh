@@ -296,7 +296,19 @@ struct PlanParams {
   int seg_cols;     // columns per segment (8 or 16)
   int expert_base;  // ids are global; expert e here is id expert_base + e
   int foreign_ok;   // ids outside [base, base + E) belong to other ranks: skipped
+  int expert_stride;  // > 1: expert e here is id expert_base + e * stride (strided placement)
 };
+
+// The local expert of global id `id` under a plan's placement, or -1.
+MR_DEVICE int plan_local_expert(const PlanParams& p, int id) {
+  const int g = id - p.expert_base;
+  if (p.expert_stride > 1) {
+    if (g < 0 || g % p.expert_stride != 0) return -1;
+    const int e = g / p.expert_stride;
+    return e < p.E ? e : -1;
+  }
+  return (g >= 0 && g < p.E) ? g : -1;
+}
 
 template <int NTHREADS>
 __device__ void build_plan_cta(const PlanParams& p) {
@@ -308,8 +320,8 @@ __device__ void build_plan_cta(const PlanParams& p) {
   for (int e = tid; e < p.E; e += NTHREADS) cnt[e] = 0;
   __syncthreads();
   for (int i = tid; i < p.Tk; i += NTHREADS) {
-    const int e = __ldcg(p.ids + i) - p.expert_base;
-    if (e >= 0 && e < p.E) {
+    const int e = plan_local_expert(p, __ldcg(p.ids + i));
+    if (e >= 0) {
       atomicAdd(&cnt[e], 1);
     } else if (!p.foreign_ok) {
       atomicOr(p.error, MR_DEVERR_BAD_EXPERT_ID);
@@ -372,8 +384,8 @@ __device__ void build_plan_cta(const PlanParams& p) {
   for (int e = tid; e < p.E; e += NTHREADS) cnt[e] = 0;
   __syncthreads();
   for (int i = tid; i < p.Tk; i += NTHREADS) {
-    const int e = __ldcg(p.ids + i) - p.expert_base;
-    if (e >= 0 && e < p.E) {
+    const int e = plan_local_expert(p, __ldcg(p.ids + i));
+    if (e >= 0) {
       const int pos = atomicAdd(&cnt[e], 1);
       p.cols[colofs[e] + pos] = i;
     }

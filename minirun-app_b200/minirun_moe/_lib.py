@@ -129,6 +129,9 @@ SIGNATURES = {
                                               C.POINTER(mr_affine_desc), vp, vp, C.c_char_p,
                                               C.c_size_t]),
     "mr_ep_set_fused": (C.c_int, [vp, C.c_int]),
+    "mr_ep_set_mode": (C.c_int, [vp, C.c_int]),
+    "mr_ep_set_placement": (C.c_int, [vp, C.c_int]),
+    "mr_ep_init": (C.c_int, [vp, vp, C.c_int, C.c_int, C.POINTER(vp)]),
     "mr_test_expire_ep_wait": (C.c_int, [vp, C.c_int64, C.c_int64, C.c_uint32, vp, vp]),
     "mr_mxfp4_validate": (C.c_int, [C.POINTER(mr_mxfp4_desc), C.c_char_p, C.c_size_t]),
     "mr_mxfp4_mm": (C.c_int, [vp, vp, C.c_int64, C.POINTER(mr_mxfp4_desc), vp, vp]),

@@ -81,6 +81,26 @@ class ExpertGroup:
         per-token sums. Every rank must choose the same."""
         self.ctx.check("mr_ep_set_fused", L.load().mr_ep_set_fused(self.handle, 1 if fused else 0))
 
+    MODES = {"allgather": 0, "nccl": 1, "alltoall": 2}
+
+    def set_mode(self, mode: str) -> None:
+        """"allgather" (default): NCCL all-gather of the tokens, fused peer
+        combine; "nccl": all-gather + NCCL reduce-scatter; "alltoall": each
+        rank routes its own tokens and stores their rows into the ranks that
+        hold their experts (peer memory), fused peer combine. Every rank must
+        choose the same."""
+        self.ctx.check("mr_ep_set_mode", L.load().mr_ep_set_mode(self.handle, self.MODES[mode]))
+
+    PLACEMENTS = {"contiguous": 0, "strided": 1}
+
+    def set_placement(self, placement: str) -> None:
+        """"contiguous" (default): rank r holds experts [r*E/N, (r+1)*E/N);
+        "strided": experts r, r+N, r+2N, ... (build the shard with
+        synth.synth_layer(..., shard=(r, N), strided=True) or the same
+        expert order). Every rank must choose the same."""
+        self.ctx.check("mr_ep_set_placement",
+                       L.load().mr_ep_set_placement(self.handle, self.PLACEMENTS[placement]))
+
     def forward(self, shard: MoELayerShard, x: torch.Tensor, out: torch.Tensor | None = None,
                 ids: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's T tokens in, their layer outputs out (same T on all ranks)."""

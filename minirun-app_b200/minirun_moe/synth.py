@@ -127,10 +127,11 @@ def zipf_bias(experts: int, beta: float, s: float = 1.1) -> list[float]:
 
 
 def synth_layer(spec: LayerSpec, layer: int = 0, device=None,
-                shard: tuple[int, int] | None = None) -> MoELayer:
+                shard: tuple[int, int] | None = None, strided: bool = False) -> MoELayer:
     """The seeded layer; with ``shard=(rank, world)`` only that rank's routed
-    experts [rank*E/world, (rank+1)*E/world) (same seeds as in the full
-    layer), as a MoELayerShard for the expert-parallel forward."""
+    experts [rank*E/world, (rank+1)*E/world) — or, with ``strided``, experts
+    rank, rank+world, ... — (same seeds as in the full layer), as a
+    MoELayerShard for the expert-parallel forward."""
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
     H, E, I, S = spec.hidden, spec.experts, spec.inter, spec.shared_inter
     e0, e1 = 0, E
@@ -145,10 +146,12 @@ def synth_layer(spec: LayerSpec, layer: int = 0, device=None,
     gate = alloc_affine(e1 - e0, I, H, spec.bits, spec.group, dev)
     up = alloc_affine(e1 - e0, I, H, spec.bits, spec.group, dev)
     down = alloc_affine(e1 - e0, H, I, spec.bits, spec.group, dev)
-    for e in range(e0, e1):
+    experts = range(e0, e1)
+    if shard is not None and strided:
+        experts = range(shard[0], E, shard[1])
+    for i, e in enumerate(experts):
         for proj, w in ((PROJ_GATE, gate), (PROJ_UP, up), (PROJ_DOWN, down)):
-            fill_affine(spec, layer, e, proj, w.packed[e - e0], w.scales[e - e0],
-                        w.biases[e - e0])
+            fill_affine(spec, layer, e, proj, w.packed[i], w.scales[i], w.biases[i])
     shared = None
     if S > 0:
         sg = alloc_affine(None, S, H, spec.bits, spec.group, dev)

@@ -36,27 +36,34 @@ def main():
     group = M.ExpertGroup(rank, rank, world)
     M.Context.get(rank).set_kernel_path("auto")
     cases = [
-        ("config0", S.CONFIGS[0], 4),
-        ("config0_after_down", dataclasses.replace(S.CONFIGS[0], weight_after_down=True), 5),
-        ("config0_no_shared", dataclasses.replace(S.CONFIGS[0], shared_inter=0), 3),
-        ("config1_32e", dataclasses.replace(S.CONFIGS[1], experts=32), 8),
+        ("config0", S.CONFIGS[0], 4, False),
+        ("config0_after_down", dataclasses.replace(S.CONFIGS[0], weight_after_down=True), 5,
+         False),
+        ("config0_no_shared", dataclasses.replace(S.CONFIGS[0], shared_inter=0), 3, False),
+        ("config1_32e", dataclasses.replace(S.CONFIGS[1], experts=32), 8, False),
+        ("config0_strided", S.CONFIGS[0], 6, True),
+        ("config1_32e_strided", dataclasses.replace(S.CONFIGS[1], experts=32), 4, True),
+        # prefill-size: the tcgen05 grouped GEMM with the peer epilogue (all-to-all)
+        ("config0_prefill_strided", S.CONFIGS[0], 160, True),
     ]
     results = {}
-    for name, spec, T in cases:
+    for name, spec, T, strided in cases:
+        group.set_placement("strided" if strided else "contiguous")
         full = S.synth_layer(spec, layer=1, device=rank)
-        shard = S.synth_layer(spec, layer=1, device=rank, shard=(rank, world))
+        shard = S.synth_layer(spec, layer=1, device=rank, shard=(rank, world), strided=strided)
         xall = S.synth_x(spec, T * world, layer=1, batch=7, device=rank)
         x = xall[rank * T:(rank + 1) * T].contiguous()
         ref, sel = full(xall)
         torch.cuda.synchronize()
         mine = ref[rank * T:(rank + 1) * T]
-        for fused in (True, False):
-            group.set_fused(fused)
+        for mode in ("allgather", "nccl", "alltoall"):
+            group.set_mode(mode)
+            fused = mode != "nccl"
             ids = torch.empty((T, spec.top_k), dtype=torch.int32, device=dev)
             for _ in range(3):  # repeated steps reuse the peer buffers and epochs
                 out = group.forward(shard, x, ids=ids)
             torch.cuda.synchronize()
-            results[name + ("_fused" if fused else "_nccl")] = {
+            results[name + "_" + mode] = {
                 "fused": fused,
                 "rel_l2": rel_l2(out, mine),
                 "bit_equal": bool(torch.equal(out, mine)),

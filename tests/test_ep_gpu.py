@@ -1,8 +1,9 @@
 """Expert parallelism on 2 GPUs through the C ABI (mr_moe_layer_forward_ep):
 each rank's outputs equal the one-GPU layer over all ranks' tokens — bit
-for bit on the fused path (down GEMV storing routed partials into the home
-rank over NVLink), within fp32 summation order on the NCCL path — and the
-expert ids are the same. Runs tests/ep_worker.py as two torchrun ranks; skipped with fewer than
+for bit on the fused paths (down GEMV storing routed partials into the home
+rank over NVLink, after an NCCL all-gather of the tokens or a peer
+all-to-all dispatch of them), within fp32 summation order on the NCCL path —
+and the expert ids are the same. Runs tests/ep_worker.py as two torchrun ranks; skipped with fewer than
 two GPUs."""
 import json
 import os

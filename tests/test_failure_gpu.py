@@ -71,3 +71,14 @@ def test_spin_limit_is_validated():
     assert lib.mr_test_expire_ep_wait(ctx.handle, 1, 64, 0, C.c_void_p(out.data_ptr()), s) == 1
     assert lib.mr_test_expire_ep_wait(ctx.handle, 1, 64, (1 << 22) + 1,
                                       C.c_void_p(out.data_ptr()), s) == 1
+
+
+def test_ep_init_and_mode_validate_arguments():
+    """mr_ep_init refuses a missing communicator or an impossible rank before
+    touching NCCL; mr_ep_set_mode refuses unknown modes."""
+    ctx = M.Context.get(0)
+    lib = L.load()
+    h = C.c_void_p()
+    assert lib.mr_ep_init(ctx.handle, None, 0, 2, C.byref(h)) == 1
+    assert lib.mr_ep_init(ctx.handle, C.c_void_p(8), 2, 2, C.byref(h)) == 1
+    assert lib.mr_ep_set_mode(None, 0) == 1
