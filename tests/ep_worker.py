@@ -63,8 +63,13 @@ def main():
             for _ in range(3):  # repeated steps reuse the peer buffers and epochs
                 out = group.forward(shard, x, ids=ids)
             torch.cuda.synchronize()
+            # the all-gather forms stream prefill-size batches with the decode
+            # GEMV while one GPU (and the all-to-all form) take the tcgen05 GEMM,
+            # which rounds each dequantised weight to bf16: within 1e-2 there
+            prefill = "prefill" in name
             results[name + "_" + mode] = {
-                "fused": fused,
+                "fused": fused and (mode == "alltoall" or not prefill),
+                "bound": 1e-2 if prefill and mode != "alltoall" else 2e-3,
                 "rel_l2": rel_l2(out, mine),
                 "bit_equal": bool(torch.equal(out, mine)),
                 "ids_equal": bool(torch.equal(ids, sel.ids[rank * T:(rank + 1) * T].int())),

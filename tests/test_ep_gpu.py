@@ -40,6 +40,6 @@ def test_expert_parallel_two_ranks_match_one_gpu():
         for name, r in res["results"].items():
             assert r["finite"], (res["rank"], name)
             assert r["ids_equal"], (res["rank"], name)
-            assert r["rel_l2"] < REL_L2, (res["rank"], name, r["rel_l2"])
+            assert r["rel_l2"] < r.get("bound", REL_L2), (res["rank"], name, r["rel_l2"])
             if r["fused"]:
                 assert r["bit_equal"], (res["rank"], name, r["rel_l2"])
