@@ -107,6 +107,9 @@ def parse():
                         "scaled from 40 GB for 58 layers (0 = skip)")
     p.add_argument("--config4-budget-gb", type=float, default=0.0,
                    help="config-4 sub-line budget (0 = 40 GB * layers / 58)")
+    p.add_argument("--config4-ep-layers", type=int, default=58,
+                   help="N >= 4: config-4 decode with every expert resident across the GPUs "
+                        "(all-to-all mode, the token on GPU 0), this many layers (0 = skip)")
     return p.parse_args()
 
 
@@ -431,6 +434,9 @@ def run_ours(args, world, rank, local):
     if not ep and args.config4_layers > 0 and args.config == "1":
         config4 = cache_run(args, M, S, torch, dev, layers_n=args.config4_layers,
                             budget_gb=args.config4_budget_gb, check_identity=True)
+    elif ep and world >= 4 and args.config4_ep_layers > 0 and args.config == "1":
+        config4 = config4_ep_run(args, S, M, torch, world, rank, local, dev, group,
+                                 max_over_ranks, barrier)
 
     e2e = e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local,
                   group if ep else None)
@@ -934,6 +940,69 @@ def cache_run(args, M, S, torch, dev, layers_n=None, budget_gb=None, check_ident
             "h2d_gbs": d.get("bytes_copied", 0) / steps / (ms / 1e3) / 1e9,
             "setup_s": setup_s, "identity": identity,
             "note": "every layer registers the same seeded host arrays under its own keys"}
+
+
+def config4_ep_run(args, S, M, torch, world, rank, local, dev, group, max_over_ranks, barrier):
+    """Config 4 on N GPUs with every expert resident: `--config4-ep-layers`
+    seeded config-1 layers, each GPU holding E/N routed experts of every
+    layer; a one-token decode whose token lives on GPU 0 (the others pass no
+    tokens, all-to-all mode with capacity 1). As in the one-GPU line each
+    layer routes a seeded token of its own. GPU 0's outputs of the first two
+    layers are checked bit for bit against the one-GPU layer."""
+    spec = S.CONFIGS[1]
+    NL = args.config4_ep_layers
+    group.set_mode("alltoall")
+    group.set_placement("contiguous")
+    group.set_capacity(1)
+    layers = [S.synth_layer(spec, layer=l, device=local, shard=(rank, world)) for l in range(NL)]
+    steps = max(3, min(args.steps, 10))
+    W = max(3, args.warmup)
+    H = spec.hidden
+    empty = torch.empty((0, H), dtype=torch.bfloat16, device=dev)
+    xs = [[S.synth_x(spec, 1, layer=l, batch=i, device=local) if rank == 0 else empty
+           for l in range(NL)] for i in range(W + steps)]
+    outs = [torch.empty((1 if rank == 0 else 0, H), dtype=torch.bfloat16, device=dev)
+            for _ in range(NL)]
+
+    def token(i):
+        for l, lay in enumerate(layers):
+            group.forward(lay, xs[i][l], out=outs[l])
+
+    for i in range(W):
+        token(i)
+    torch.cuda.synchronize()
+    barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(W, W + steps):
+        token(i)
+    b.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(a.elapsed_time(b) / steps)
+    same = None
+    if rank == 0:
+        same = True
+        for l in range(min(2, NL)):
+            full = S.synth_layer(spec, layer=l, device=local)
+            ref, _ = full(xs[W + steps - 1][l])
+            torch.cuda.synchronize()
+            same = same and bool(torch.equal(ref, outs[l]))
+            del full
+        torch.cuda.empty_cache()
+    barrier()
+    resident = sum(w.nbytes() for lay in layers for w in (lay.gate, lay.up, lay.down))
+    group.set_capacity(0)
+    group.set_mode(args.ep_mode)
+    del layers
+    torch.cuda.empty_cache()
+    return {"workload": f"config4: {NL} config-1 layers, 1-token decode, every routed expert "
+                        f"resident ({spec.experts // world} per GPU per layer), the token on "
+                        f"GPU 0, all-to-all dispatch",
+            "tokens_per_s": 1e3 / ms, "ms_per_token": ms, "steps": steps,
+            "routed_bytes_resident_per_gpu": resident,
+            "identity": {"vs_one_gpu_layers": min(2, NL), "bit_identical": same}}
 
 
 def e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local, group=None):

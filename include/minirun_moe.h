@@ -497,11 +497,18 @@ mr_status mr_ep_set_mode(mr_ep* ep, int mode);
  * routers that favour low expert ids (a skewed load) over every rank. Every
  * rank must choose the same, before its first forward with that layout. */
 mr_status mr_ep_set_placement(mr_ep* ep, int placement);
+/* All-to-all mode: the most tokens any rank passes to one forward (the size
+ * of the receive slabs). With a capacity set, each rank passes its own
+ * 0 <= tokens <= capacity (x and out may be NULL at 0), e.g. a batch-1
+ * decode whose token lives on one rank while every rank holds experts;
+ * 0 (default): every rank passes the same tokens. Every rank sets the same
+ * value. */
+mr_status mr_ep_set_capacity(mr_ep* ep, int64_t max_tokens);
 /* Expert-parallel mr_moe_layer_forward. layer->gate/up/down are this rank's
  * E/world experts (experts == router.experts / world, stacks only);
  * everything else as mr_moe_layer_forward. Every rank passes the same
- * `tokens` T; out [T, H] and ids_out [T, k] (optional) are this rank's
- * tokens. Results equal mr_moe_layer_forward over all ranks' tokens on one
+ * `tokens` T (all-to-all mode with a capacity: any 0 <= T <= capacity);
+ * out [T, H] and ids_out [T, k] (optional) are this rank's tokens. Results equal mr_moe_layer_forward over all ranks' tokens on one
  * GPU: bit for bit on the fused path, up to the fp32 order of the routed-slot
  * sums on the NCCL path. */
 mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* layer,

@@ -2297,6 +2297,7 @@ struct mr_ep {
   // peer all-to-all dispatch + fused peer combine
   int mode = MR_EP_MODE_ALLGATHER;
   int placement = MR_EP_PLACE_CONTIGUOUS;  // which global experts this rank's stacks hold
+  int64_t capacity = 0;  // all-to-all: tokens per rank at most (0: every rank passes the same T)
   // peer paths: this rank's receive buffer, mapped by every rank through
   // CUDA IPC:
   //   [0, 256)     combine epochs, one word per source rank (W <= 64)
@@ -2382,6 +2383,12 @@ mr_status mr_ep_set_mode(mr_ep* ep, int mode) {
   if (!ep || mode < MR_EP_MODE_ALLGATHER || mode > MR_EP_MODE_ALLTOALL)
     return MR_ERR_INVALID_ARGUMENT;
   ep->mode = mode;
+  return MR_OK;
+}
+
+mr_status mr_ep_set_capacity(mr_ep* ep, int64_t max_tokens) {
+  if (!ep || max_tokens < 0) return MR_ERR_INVALID_ARGUMENT;
+  ep->capacity = max_tokens;
   return MR_OK;
 }
 
@@ -2571,7 +2578,9 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
   const int stride = ep->placement == MR_EP_PLACE_STRIDED ? W : 1;
   const int base = stride > 1 ? rank : rank * El;
   const int64_t H = L->hidden, I = L->inter;
-  const int64_t Tk = T * k, R = (int64_t)W * T, RK = R * k;  // received rows / pair ids
+  // slab rows per source rank: the group's capacity, else every rank's T
+  const int64_t Tcap = ep->capacity > 0 ? ep->capacity : T;
+  const int64_t Tk = T * k, R = (int64_t)W * Tcap, RK = R * k;  // received rows / pair ids
   const bool has_shared = L->shared_inter > 0;
   const int wad = L->weight_placement == MR_WEIGHT_AFTER_DOWN ? 1 : 0;
   if (RK > (int64_t)1 << 28) return fail(ctx, MR_ERR_UNSUPPORTED, "token count too large");
@@ -2585,17 +2594,18 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
             (bits == 4 || bits == 8) && L->up.bits == bits && L->down.bits == bits &&
             (!has_shared || (L->shared_gate.bits == bits && L->shared_up.bits == bits &&
                              L->shared_down.bits == bits)) &&
-            (int64_t)T * W * k >= 32 * (int64_t)E;
+            Tcap * W * k >= 32 * (int64_t)E;
   const bool pf_sh = pf && has_shared && T >= 32;  // the shared expert's own launch
-  int seg_cols = pf ? kPfN : decode_seg_cols(ctx, (int64_t)T * W * k, E);
+  int seg_cols = pf ? kPfN : decode_seg_cols(ctx, Tcap * W * k, E);
   const int64_t max_seg = std::min<int64_t>(El, RK) + RK / 8 + 1;
-  const LogitsShape ls = logits_shape(ctx, T, E, H);
+  const LogitsShape ls = logits_shape(ctx, std::max<int64_t>(T, 1), E, H);
   mr_status st;
 
   // peer buffer: combine rows of this rank's pairs (+ shared), then the slabs
-  const int64_t rows = Tk + (has_shared ? 2 * T : 0);
+  // (sized by the capacity, so every rank has the same layout)
+  const int64_t rows = Tcap * k + (has_shared ? 2 * Tcap : 0);
   const size_t parts = ((size_t)rows * H * sizeof(float) + 255) / 256 * 256;
-  const A2ALayout lay = a2a_layout(W, T, k, H);
+  const A2ALayout lay = a2a_layout(W, Tcap, k, H);
   if ((st = ep_peer_setup(ctx, ep, parts + (size_t)lay.bytes, parts, s))) return st;
   if (ep->peer_failed) return MR_ERR_STATE;  // caller falls back to the NCCL path
 
@@ -2655,7 +2665,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
                      kPfN) &&
          encode_umma(ctx, m2, EPI_PARTIAL, I, ActSpec{h, RK, hsum}, ActSpec{h, RK, hsum}, &um2,
                      kPfN);
-    if (!pf) seg_cols = decode_seg_cols(ctx, (int64_t)T * W * k, E);
+    if (!pf) seg_cols = decode_seg_cols(ctx, Tcap * W * k, E);
   }
   bool shared_pf = pf && pf_sh;
   if (shared_pf) {
@@ -2669,7 +2679,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
   ++ep->epoch;
 
   // 1. route this rank's tokens (the prep also gives the shared expert's rows)
-  {
+  if (T > 0) {
     const RoutePlan rp{nseg0, segs0, cols0, seg_own, 0, E, false};
     if ((st = route_tokens(ctx, L, x, T, ls, part, xperm, xsum, ids, wts, nullptr, rp, s)))
       return st;
@@ -2695,17 +2705,18 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
     dp.rank = rank;
     dp.rows_per_cta = 8;
     dp.H = H;
-    dp.Tcap = T;
+    dp.Tcap = Tcap;
     dp.lay = lay;
     dp.epoch = ep->epoch;
-    const dim3 grid((unsigned)((T + 7) / 8), (unsigned)W);
+    // at least one CTA per destination: it publishes the count (maybe 0) and epoch
+    const dim3 grid((unsigned)std::max<int64_t>(1, (T + 7) / 8), (unsigned)W);
     a2a_copy_kernel<<<grid, 256, 0, s>>>(dp);
     if ((st = cuda_check(ctx, cudaGetLastError(), "a2a_copy_kernel"))) return st;
     // 3. receive: every source's rows of this step, as expert ids per pair
     a2a_receive_kernel<<<1, 1024, 0, s>>>(
         reinterpret_cast<const unsigned*>(mybuf + 256), reinterpret_cast<const unsigned*>(mybuf + 512),
-        W, ep->epoch, kSpinLimit, reinterpret_cast<const int32_t*>(slab + lay.ids), T, k, ids_recv,
-        ctx->d_error);
+        W, ep->epoch, kSpinLimit, reinterpret_cast<const int32_t*>(slab + lay.ids), Tcap, k,
+        ids_recv, ctx->d_error);
     if ((st = cuda_check(ctx, cudaGetLastError(), "a2a_receive_kernel"))) return st;
   }
   // 4. prep of the received rows and the plan of this rank's experts
@@ -2759,12 +2770,12 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
     peer.peer_rank = rank;
     peer.peer_epoch = ep->epoch;
     peer.peer_row_tok = reinterpret_cast<const int*>(slab + lay.tok);
-    peer.peer_rows = (int)T;
+    peer.peer_rows = (int)Tcap;
     r.peer = &peer;
     if ((st = run_experts(ctx, L, r, s))) return st;
   }
   // 6. shared expert over this rank's tokens, into its own combine rows
-  if (has_shared) {
+  if (has_shared && T > 0) {
     if ((st = cuda_check(ctx, cudaMemsetAsync(zero, 0, 4 * sizeof(int), s), "clear count")))
       return st;
     ExpertsRun sh{};
@@ -2790,6 +2801,8 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
     if ((st = run_experts(ctx, L, sh, s))) return st;
   }
   // 7. wait for every rank's partials of this step, combine in slot order
+  // (a rank without tokens still waits: that keeps its next dispatch behind
+  // every rank's down GEMV of this step)
   {
     const int64_t n = T * H;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * ctx->sm_count));
@@ -2799,7 +2812,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
                                                 ep->epoch, kSpinLimit, ctx->d_error, out);
     if ((st = cuda_check(ctx, cudaGetLastError(), "ep_wait_combine_kernel"))) return st;
   }
-  if (ids_out)
+  if (ids_out && T > 0)
     st = cuda_check(ctx, cudaMemcpyAsync(ids_out, ids, Tk * sizeof(int32_t),
                                          cudaMemcpyDeviceToDevice, s),
                     "copy ids");
@@ -2826,8 +2839,12 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
   std::string why;
   mr_status st = validate_layer(&full, why);
   if (st) return fail(ctx, st, why);
-  if (T <= 0 || !x || !out)
-    return fail(ctx, MR_ERR_INVALID_ARGUMENT, "input must be a non-empty [tokens, hidden] matrix");
+  // all-to-all with a capacity: this rank may hold 0..capacity tokens
+  const bool a2a_cap = ep->mode == MR_EP_MODE_ALLTOALL && ep->capacity > 0;
+  if (a2a_cap ? (T < 0 || T > ep->capacity || (T > 0 && (!x || !out))) : (T <= 0 || !x || !out))
+    return fail(ctx, MR_ERR_INVALID_ARGUMENT,
+                a2a_cap ? "tokens must be within [0, capacity] and x, out non-NULL when tokens > 0"
+                        : "input must be a non-empty [tokens, hidden] matrix");
   if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0)
     return fail(ctx, MR_ERR_UNSUPPORTED, "x must be 16-byte aligned");
   const int El = E / W;
@@ -2849,6 +2866,10 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
     if (st != MR_ERR_STATE || !ep->peer_failed) return st;
     // a peer mapping failed on some rank (agreed by all): the NCCL path below
   }
+  if (T == 0)
+    return fail(ctx, MR_ERR_UNSUPPORTED,
+                "ranks without tokens need the all-to-all mode (staged GEMV, TMA-streamable "
+                "stacks, peer mappings)");
   const int seg_cols = decode_seg_cols(ctx, NTk, E);
   const int64_t max_seg = std::min<int64_t>(El, NTk) + NTk / seg_cols + 1;
   const LogitsShape ls = logits_shape(ctx, NT, E, H);

@@ -131,6 +131,7 @@ SIGNATURES = {
     "mr_ep_set_fused": (C.c_int, [vp, C.c_int]),
     "mr_ep_set_mode": (C.c_int, [vp, C.c_int]),
     "mr_ep_set_placement": (C.c_int, [vp, C.c_int]),
+    "mr_ep_set_capacity": (C.c_int, [vp, C.c_int64]),
     "mr_ep_init": (C.c_int, [vp, vp, C.c_int, C.c_int, C.POINTER(vp)]),
     "mr_test_expire_ep_wait": (C.c_int, [vp, C.c_int64, C.c_int64, C.c_uint32, vp, vp]),
     "mr_mxfp4_validate": (C.c_int, [C.POINTER(mr_mxfp4_desc), C.c_char_p, C.c_size_t]),

@@ -101,9 +101,16 @@ class ExpertGroup:
         self.ctx.check("mr_ep_set_placement",
                        L.load().mr_ep_set_placement(self.handle, self.PLACEMENTS[placement]))
 
+    def set_capacity(self, max_tokens: int) -> None:
+        """All-to-all mode: each rank may then pass 0..max_tokens tokens per
+        forward (0: every rank passes the same T). Every rank the same."""
+        self.ctx.check("mr_ep_set_capacity",
+                       L.load().mr_ep_set_capacity(self.handle, int(max_tokens)))
+
     def forward(self, shard: MoELayerShard, x: torch.Tensor, out: torch.Tensor | None = None,
                 ids: torch.Tensor | None = None) -> torch.Tensor:
-        """This rank's T tokens in, their layer outputs out (same T on all ranks)."""
+        """This rank's T tokens in, their layer outputs out (same T on all
+        ranks, or 0..capacity with set_capacity in the all-to-all mode)."""
         if shard.world != self.world:
             raise AffineBridgeError(f"shard of {shard.world} ranks used in a {self.world}-rank group")
         if x.dim() != 2 or x.shape[1] != shard.hidden or x.dtype != torch.bfloat16:

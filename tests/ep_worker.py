@@ -76,6 +76,27 @@ def main():
                 "finite": bool(torch.isfinite(out.float()).all()),
             }
             M.Context.get(rank).sync_check()
+    # all-to-all with a capacity: ranks pass different token counts, some 0
+    # (a batch-1 decode whose token lives on one rank)
+    group.set_mode("alltoall")
+    group.set_placement("contiguous")
+    group.set_capacity(4)
+    spec = dataclasses.replace(S.CONFIGS[1], experts=32)
+    full = S.synth_layer(spec, layer=2, device=rank)
+    shard = S.synth_layer(spec, layer=2, device=rank, shard=(rank, world))
+    for step, counts in enumerate(([1, 0], [0, 3], [4, 2], [1, 0])):
+        Tr = counts[rank % 2]
+        x = S.synth_x(spec, 4, layer=2, batch=20 + step, device=rank)[:Tr].contiguous()
+        out = group.forward(shard, x)
+        torch.cuda.synchronize()
+        if Tr:
+            ref, _ = full(x)
+            torch.cuda.synchronize()
+            results[f"capacity_step{step}"] = {
+                "fused": True, "rel_l2": rel_l2(out, ref), "bit_equal": bool(torch.equal(out, ref)),
+                "ids_equal": True, "finite": bool(torch.isfinite(out.float()).all())}
+        M.Context.get(rank).sync_check()
+    group.set_capacity(0)
     group.close()
     dist.barrier()
     dist.destroy_process_group()
