@@ -553,7 +553,19 @@ typedef struct mr_cache_stats {
   int64_t misses;       /* requests copied from host */
   int64_t evictions;
   int64_t bytes_copied; /* host -> device */
+  int64_t prefetched;   /* experts copied in by mr_cache_prefetch */
 } mr_cache_stats;
+
+/* Admission policies (StorageCore/Pager/BufferPool.swift:95-140, CachePolicy):
+ * LRU admits every expert and evicts the least recently used; NONE retains
+ * nothing (every call copies what it routes to); PINNED_HOT_SET admits only
+ * the given (layer, expert) keys, so a cold expert uses a slot for one call
+ * and never displaces a hot one. Pinning is admission, not a slot lock: hot
+ * experts still compete LRU among themselves when there are more of them
+ * than slots. */
+#define MR_CACHE_POLICY_LRU 0
+#define MR_CACHE_POLICY_NONE 1
+#define MR_CACHE_POLICY_PINNED_HOT_SET 2
 
 /* A cache of floor(budget_bytes / slot_bytes) slots of slot_bytes (at least
  * one expert's arrays, each 256-byte aligned) on the context's device. */
@@ -564,6 +576,22 @@ mr_status mr_cache_destroy(mr_cache* cache);
 mr_status mr_cache_register(mr_cache* cache, int32_t layer, int32_t expert,
                             const mr_expert_host* host);
 mr_status mr_cache_get_stats(const mr_cache* cache, mr_cache_stats* out);
+/* The admission policy; hot_layers / hot_experts (n_hot pairs) name the hot
+ * set of MR_CACHE_POLICY_PINNED_HOT_SET (ignored otherwise). Takes effect at
+ * the next forward or prefetch. */
+mr_status mr_cache_set_policy(mr_cache* cache, int policy, const int32_t* hot_layers,
+                              const int32_t* hot_experts, int64_t n_hot);
+/* RoutedExpertBackend.prefetch(layer:projections:expertIds:)
+ * (Sources/ModelAdapters/Operators/MoE.swift:22-51): starts copying these
+ * experts of `layer` (host ids, n of them) into the cache on its copy stream
+ * and returns; a later mr_moe_layer_forward_cached that routes to them finds
+ * them resident (its GEMVs wait for the copies). `stream` is the stream the
+ * cached forwards run on: a slot is overwritten only after the work queued
+ * there so far. Experts the policy does not admit are skipped; when every
+ * slot holds an expert of this call the rest are skipped too. Container-backed
+ * experts are read from disk before the call returns. */
+mr_status mr_cache_prefetch(mr_cache* cache, int32_t layer, const int32_t* experts, int64_t n,
+                            void* stream);
 /* mr_moe_layer_forward with the routed experts of `layer_id` served by the
  * cache: layer->gate/up/down give shapes and formats only (their pointers
  * and expert_table are ignored); router and shared expert as usual. The

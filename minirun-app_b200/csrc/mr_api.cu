@@ -12,6 +12,7 @@
 #include <nccl.h>
 
 #include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 #include "mr_tiles.h"
@@ -3116,6 +3117,12 @@ struct mr_cache {
   mr_cache_stats stats{};
   cudaStream_t copy = nullptr;
   cudaEvent_t done = nullptr;
+  cudaEvent_t used = nullptr;  // recorded on the caller's stream after each forward
+  // admission (BufferPool.swift:95-140): LRU admits every expert, NONE none,
+  // PINNED_HOT_SET only the keys in `hot`; non-admitted experts use a slot
+  // for one call and go back to free at the next
+  int policy = MR_CACHE_POLICY_LRU;
+  std::unordered_set<uint64_t> hot;
   // pinned host staging: routed ids read back, the expert pointer table
   int32_t* ids_h = nullptr;
   size_t ids_cap = 0;
@@ -3132,6 +3139,56 @@ uint64_t cache_key(int32_t layer, int32_t expert) {
 }
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+bool cache_admits(const mr_cache* c, uint64_t key) {
+  switch (c->policy) {
+    case MR_CACHE_POLICY_NONE: return false;
+    case MR_CACHE_POLICY_PINNED_HOT_SET: return c->hot.count(key) != 0;
+    default: return true;
+  }
+}
+
+// Non-admitted experts held over from earlier calls go back to free.
+void cache_apply_policy(mr_cache* c) {
+  if (c->policy == MR_CACHE_POLICY_LRU) return;
+  for (auto& sl : c->slots) {
+    if (sl.key == ~0ull || cache_admits(c, sl.key)) continue;
+    auto it = c->regs.find(sl.key);
+    if (it != c->regs.end()) it->second.slot = -1;
+    sl = mr_cache::Slot{};
+    --c->stats.resident;
+  }
+}
+
+// A slot for a miss: a free one, else the least recently used one not
+// touched at the current clock (this call's experts); -1 if none.
+int cache_pick_slot(const mr_cache* c) {
+  int pick = -1;
+  for (size_t j = 0; j < c->slots.size(); ++j) {
+    const mr_cache::Slot& sl = c->slots[j];
+    if (sl.key == ~0ull) return (int)j;
+    if (sl.last_use < c->clock && (pick < 0 || sl.last_use < c->slots[pick].last_use))
+      pick = (int)j;
+  }
+  return pick;
+}
+
+// Copies a memory-backed registration's nine arrays into slot `base` on the
+// copy stream.
+mr_status cache_copy_host(mr_cache* c, const mr_cache::Reg& r, char* base) {
+  for (int p = 0; p < 3; ++p) {
+    const void* src[3] = {r.host.packed[p], r.host.scales[p], r.host.biases[p]};
+    const size_t bytes[3] = {r.host.packed_bytes[p], r.host.scale_bytes[p], r.host.scale_bytes[p]};
+    for (int a = 0; a < 3; ++a) {
+      mr_status st = cuda_check(c->ctx, cudaMemcpyAsync(base + r.off[3 * p + a], src[a], bytes[a],
+                                                        cudaMemcpyHostToDevice, c->copy),
+                                "copy expert to HBM");
+      if (st) return st;
+      c->stats.bytes_copied += (int64_t)bytes[a];
+    }
+  }
+  return MR_OK;
+}
 
 template <class T>
 mr_status grow_pinned(mr_ctx* ctx, T** p, size_t* cap, size_t n, const char* what) {
@@ -3165,6 +3222,8 @@ mr_status mr_cache_create(mr_ctx* ctx, size_t budget_bytes, size_t slot_bytes, m
                            "cudaStreamCreate(cache copies)");
   if (!st) st = cuda_check(ctx, cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming),
                            "cudaEventCreate(cache)");
+  if (!st) st = cuda_check(ctx, cudaEventCreateWithFlags(&c->used, cudaEventDisableTiming),
+                           "cudaEventCreate(cache)");
   if (st) {
     mr_cache_destroy(c);
     return st;
@@ -3181,6 +3240,7 @@ mr_status mr_cache_destroy(mr_cache* c) {
   if (c->pool) cudaFree(c->pool);
   if (c->copy) cudaStreamDestroy(c->copy);
   if (c->done) cudaEventDestroy(c->done);
+  if (c->used) cudaEventDestroy(c->used);
   if (c->ids_h) cudaFreeHost(c->ids_h);
   if (c->table_h) cudaFreeHost(c->table_h);
   if (c->stage_h) cudaFreeHost(c->stage_h);
@@ -3345,6 +3405,9 @@ mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* c, int32_t layer_id
     return fail(ctx, MR_ERR_BUDGET,
                 "this call routes to " + std::to_string(need.size()) + " distinct experts; the " +
                     "budget holds " + std::to_string(c->slots.size()));
+  // experts the policy does not admit, held over from the previous call, go
+  // back to free (the routing synchronisation above ran every earlier GEMV)
+  cache_apply_policy(c);
   ++c->clock;
   // hits first, so that misses never evict an expert this call uses
   std::vector<mr_cache::Reg*> regs(need.size(), nullptr);
@@ -3367,16 +3430,7 @@ mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* c, int32_t layer_id
     mr_cache::Reg& r = *regs[i];
     if (r.slot < 0) {
       // a free slot, else the least recently used one not needed now
-      int pick = -1;
-      for (size_t j = 0; j < c->slots.size(); ++j) {
-        const mr_cache::Slot& sl = c->slots[j];
-        if (sl.key == ~0ull) {
-          pick = (int)j;
-          break;
-        }
-        if (sl.last_use < c->clock && (pick < 0 || sl.last_use < c->slots[pick].last_use))
-          pick = (int)j;
-      }
+      const int pick = cache_pick_slot(c);
       if (pick < 0) return fail(ctx, MR_ERR_BUDGET, "no cache slot is free for this call");
       mr_cache::Slot& sl = c->slots[pick];
       if (sl.key != ~0ull) {
@@ -3392,23 +3446,8 @@ mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* c, int32_t layer_id
       char* base = c->pool + (size_t)pick * c->slot_bytes;
       if (r.src[0]) {
         file_misses.emplace_back(&r, base);
-      } else {
-        const void* src[9];
-        size_t bytes[9];
-        for (int p = 0; p < 3; ++p) {
-          src[3 * p] = r.host.packed[p];
-          bytes[3 * p] = r.host.packed_bytes[p];
-          src[3 * p + 1] = r.host.scales[p];
-          src[3 * p + 2] = r.host.biases[p];
-          bytes[3 * p + 1] = bytes[3 * p + 2] = r.host.scale_bytes[p];
-        }
-        for (int a = 0; a < 9; ++a) {
-          if ((st = cuda_check(ctx, cudaMemcpyAsync(base + r.off[a], src[a], bytes[a],
-                                                    cudaMemcpyHostToDevice, c->copy),
-                               "copy expert to HBM")))
-            return st;
-          c->stats.bytes_copied += (int64_t)bytes[a];
-        }
+      } else if ((st = cache_copy_host(c, r, base))) {
+        return st;
       }
     }
     const char* base = c->pool + (size_t)r.slot * c->slot_bytes;
@@ -3499,11 +3538,108 @@ mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* c, int32_t layer_id
                                   has_shared ? 1 : 0, out),
                        "combine_kernel")))
     return st;
+  // the slots this call read are in use until here (prefetch copies wait on it)
+  if ((st = cuda_check(ctx, cudaEventRecord(c->used, s), "record cache use"))) return st;
   if (ids_out)
     st = cuda_check(ctx, cudaMemcpyAsync(ids_out, ids, Tk * sizeof(int32_t),
                                          cudaMemcpyDeviceToDevice, s),
                     "copy ids");
   return st;
+}
+
+mr_status mr_cache_set_policy(mr_cache* c, int policy, const int32_t* hot_layers,
+                              const int32_t* hot_experts, int64_t n_hot) {
+  if (!c || policy < MR_CACHE_POLICY_LRU || policy > MR_CACHE_POLICY_PINNED_HOT_SET || n_hot < 0 ||
+      (n_hot > 0 && (!hot_layers || !hot_experts)))
+    return MR_ERR_INVALID_ARGUMENT;
+  c->policy = policy;
+  c->hot.clear();
+  for (int64_t i = 0; i < n_hot; ++i) c->hot.insert(cache_key(hot_layers[i], hot_experts[i]));
+  return MR_OK;
+}
+
+mr_status mr_cache_prefetch(mr_cache* c, int32_t layer_id, const int32_t* experts, int64_t n,
+                            void* stream) {
+  if (!c || n < 0 || (n > 0 && !experts)) return MR_ERR_INVALID_ARGUMENT;
+  mr_ctx* ctx = c->ctx;
+  mr_status st = MR_OK;
+  // a slot about to be overwritten may still be read by work already queued
+  // on the caller's stream: the copies wait for it
+  if ((st = cuda_check(ctx, cudaEventRecord(c->used, as_stream(stream)), "record cache use")) ||
+      (st = cuda_check(ctx, cudaStreamWaitEvent(c->copy, c->used, 0), "order cache copies")))
+    return st;
+  cache_apply_policy(c);
+  ++c->clock;
+  bool staged = false;
+  for (int64_t i = 0; i < n; ++i) {
+    const uint64_t key = cache_key(layer_id, experts[i]);
+    auto it = c->regs.find(key);
+    if (it == c->regs.end())
+      return fail(ctx, MR_ERR_STATE,
+                  "expert " + std::to_string(experts[i]) + " of layer " +
+                      std::to_string(layer_id) + " is not registered with the cache");
+    mr_cache::Reg& r = it->second;
+    if (!cache_admits(c, key)) continue;  // would go back to free before its use
+    if (r.slot >= 0) {
+      c->slots[r.slot].last_use = c->clock;
+      continue;
+    }
+    const int pick = cache_pick_slot(c);
+    if (pick < 0) break;  // every slot holds an expert of this prefetch
+    mr_cache::Slot& sl = c->slots[pick];
+    if (sl.key != ~0ull) {
+      c->regs[sl.key].slot = -1;
+      ++c->stats.evictions;
+    } else {
+      ++c->stats.resident;
+    }
+    sl.key = key;
+    sl.last_use = c->clock;
+    r.slot = pick;
+    ++c->stats.prefetched;
+    char* base = c->pool + (size_t)pick * c->slot_bytes;
+    if (!r.src[0]) {
+      if ((st = cache_copy_host(c, r, base))) return st;
+      continue;
+    }
+    // container tiles: pinned staging is reused once its earlier copies are done
+    if (!staged) {
+      if ((st = cuda_check(ctx, cudaStreamSynchronize(c->copy), "sync cache copies"))) return st;
+      staged = true;
+    }
+    size_t need_bytes = 0;
+    for (int p = 0; p < 3; ++p) need_bytes += (size_t)r.src[p]->layout.tile_stride;
+    if ((st = grow_pinned(ctx, &c->stage_h, &c->stage_cap, need_bytes, "cudaHostAlloc(tiles)")))
+      return st;
+    char* stage = c->stage_h;
+    for (int p = 0; p < 3; ++p) {
+      const mr_tile_layout& TL = r.src[p]->layout;
+      char msg[512];
+      const mr_status rs =
+          mr_tiles_read(r.src[p], r.tile[p], stage, (size_t)TL.tile_stride, msg, sizeof msg);
+      if (rs) {
+        sl = mr_cache::Slot{};
+        r.slot = -1;
+        --c->stats.resident;
+        --c->stats.prefetched;
+        return fail(ctx, rs, msg);
+      }
+      const char* src[3] = {stage, stage + TL.scale_offset, stage + TL.bias_offset};
+      const size_t bytes[3] = {(size_t)TL.packed_bytes, (size_t)TL.scale_bytes,
+                               (size_t)TL.bias_bytes};
+      for (int a = 0; a < 3; ++a) {
+        if ((st = cuda_check(ctx, cudaMemcpyAsync(base + r.off[3 * p + a], src[a], bytes[a],
+                                                  cudaMemcpyHostToDevice, c->copy),
+                             "copy expert tile to HBM")))
+          return st;
+        c->stats.bytes_copied += (int64_t)bytes[a];
+      }
+      stage += TL.tile_stride;
+    }
+    // the staging is reused by the next tile-backed expert of this call
+    if ((st = cuda_check(ctx, cudaStreamSynchronize(c->copy), "sync cache copies"))) return st;
+  }
+  return MR_OK;
 }
 
 }  // extern "C"

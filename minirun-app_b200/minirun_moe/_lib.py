@@ -107,7 +107,8 @@ class mr_tile_layout(C.Structure):
 
 class mr_cache_stats(C.Structure):
     _fields_ = [("slots", C.c_int64), ("resident", C.c_int64), ("hits", C.c_int64),
-                ("misses", C.c_int64), ("evictions", C.c_int64), ("bytes_copied", C.c_int64)]
+                ("misses", C.c_int64), ("evictions", C.c_int64), ("bytes_copied", C.c_int64),
+                ("prefetched", C.c_int64)]
 
 
 # name -> (restype, argtypes); the complete exported surface of the header
@@ -166,6 +167,8 @@ SIGNATURES = {
     "mr_cache_destroy": (C.c_int, [vp]),
     "mr_cache_register": (C.c_int, [vp, C.c_int32, C.c_int32, C.POINTER(mr_expert_host)]),
     "mr_cache_get_stats": (C.c_int, [vp, C.POINTER(mr_cache_stats)]),
+    "mr_cache_set_policy": (C.c_int, [vp, C.c_int, vp, vp, C.c_int64]),
+    "mr_cache_prefetch": (C.c_int, [vp, C.c_int32, vp, C.c_int64, vp]),
     "mr_cache_register_tiles": (C.c_int, [vp, C.c_int32, C.c_int32, vp * 3, C.c_int64 * 3]),
     "mr_tiles_open": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(vp), C.c_char_p, C.c_size_t]),
     "mr_tiles_close": (C.c_int, [vp]),

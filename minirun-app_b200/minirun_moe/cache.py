@@ -101,6 +101,27 @@ class ExpertCache:
             raise AffineBridgeError("cache stats unavailable")
         return {k: getattr(s, k) for k, _ in L.mr_cache_stats._fields_}
 
+    POLICIES = {"lru": 0, "none": 1, "pinned_hot_set": 2}
+
+    def set_policy(self, policy: str, hot: list[tuple[int, int]] | None = None) -> None:
+        """"lru" (default), "none" (retain nothing), or "pinned_hot_set" with
+        `hot` = [(layer, expert), ...] the only experts admitted
+        (BufferPool.swift CachePolicy)."""
+        hot = hot or []
+        lay = (C.c_int32 * max(1, len(hot)))(*[h[0] for h in hot])
+        exp = (C.c_int32 * max(1, len(hot)))(*[h[1] for h in hot])
+        st = L.load().mr_cache_set_policy(self.handle, self.POLICIES[policy], lay, exp, len(hot))
+        if st != L.MR_OK:
+            raise AffineBridgeError(f"cache policy {policy!r} refused")
+
+    def prefetch(self, layer_id: int, experts) -> None:
+        """Start copying these experts of `layer_id` into the cache (returns
+        before the copies finish; the forward that uses them waits)."""
+        ids = [int(e) for e in experts]
+        arr = (C.c_int32 * max(1, len(ids)))(*ids)
+        self.ctx.check("mr_cache_prefetch", L.load().mr_cache_prefetch(
+            self.handle, layer_id, arr, len(ids), C.c_void_p(_stream())))
+
     def forward(self, layer_id: int, layer: CachedLayer, x: torch.Tensor,
                 out: torch.Tensor | None = None, ids: torch.Tensor | None = None) -> torch.Tensor:
         if x.dim() != 2 or x.shape[1] != layer.hidden or x.dtype != torch.bfloat16:

@@ -84,3 +84,73 @@ def test_cache_refuses_small_budget_and_unknown_experts():
     finally:
         cache.close()
     torch.cuda.synchronize()
+
+
+def _routed(layer, x):
+    _, sel = layer(x)
+    return sorted(set(sel.ids.view(-1).tolist()))
+
+
+def test_cache_policies_keep_outputs_and_follow_admission():
+    """The three admission policies (BufferPool.swift CachePolicy) give the
+    same bytes as LRU; NONE copies every routed expert on every call;
+    PINNED_HOT_SET keeps its hot experts resident however many cold ones
+    pass through, and admits nothing else."""
+    spec, layers, cached, xs, slot = _setup()
+    ref, _ = _run(layers, cached, xs, slot, NL * spec.experts)
+    hot = [(0, e) for e in _routed(layers[0], xs[0])]
+    for policy in ("none", "pinned_hot_set"):
+        cache = M.ExpertCache(0, 12 * slot, slot)
+        try:
+            cache.set_policy(policy, hot if policy == "pinned_hot_set" else None)
+            for l, lay in enumerate(layers):
+                cache.register_layer(l, lay.gate, lay.up, lay.down)
+            outs = []
+            for c, x in zip(CALLS, xs):
+                outs.append(cache.forward(c, cached[c], x).clone())
+            torch.cuda.synchronize()
+            st = cache.stats()
+            for a, b in zip(ref, outs):
+                assert torch.equal(a, b)
+            n_routed = sum(len(_routed(layers[c], x)) for c, x in zip(CALLS, xs))
+            if policy == "none":
+                assert st["hits"] == 0 and st["misses"] == n_routed
+            else:
+                # every later call of layer 0 on the first call's experts hits
+                first0 = [i for i, c in enumerate(CALLS) if c == 0]
+                later = sum(len(set(_routed(layers[0], xs[i])) & {e for _, e in hot})
+                            for i in first0[1:])
+                assert st["hits"] >= later
+                assert st["resident"] <= len(hot) + 8  # cold ones go back to free
+        finally:
+            cache.close()
+    M.Context.get(0).sync_check()
+
+
+def test_cache_prefetch_turns_misses_into_hits():
+    """RoutedExpertBackend.prefetch: experts prefetched before a call are
+    resident when it runs (hits, no new copies), and the outputs are the
+    same bytes as without prefetch."""
+    spec, layers, cached, xs, slot = _setup()
+    ref, _ = _run(layers, cached, xs, slot, NL * spec.experts)
+    cache = M.ExpertCache(0, NL * spec.experts * slot, slot)
+    try:
+        for l, lay in enumerate(layers):
+            cache.register_layer(l, lay.gate, lay.up, lay.down)
+        outs = []
+        for c, x in zip(CALLS, xs):
+            cache.prefetch(c, _routed(layers[c], x))
+            before = cache.stats()
+            outs.append(cache.forward(c, cached[c], x).clone())
+            after = cache.stats()
+            assert after["misses"] == before["misses"]  # all resident already
+        torch.cuda.synchronize()
+        st = cache.stats()
+        assert st["prefetched"] > 0 and st["misses"] == 0
+        for a, b in zip(ref, outs):
+            assert torch.equal(a, b)
+        with pytest.raises(M.MoeError):
+            cache.prefetch(NL + 5, [0])  # unregistered
+    finally:
+        cache.close()
+    M.Context.get(0).sync_check()
