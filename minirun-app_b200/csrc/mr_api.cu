@@ -3160,15 +3160,23 @@ void cache_apply_policy(mr_cache* c) {
   }
 }
 
-// A slot for a miss: a free one, else the least recently used one not
-// touched at the current clock (this call's experts); -1 if none.
+// A slot for a miss: a free one, else among the slots not touched at the
+// current clock (this call's experts) the least recently used one that the
+// policy does not admit (a cold expert), and only then the least recently
+// used admitted one; -1 if none.
 int cache_pick_slot(const mr_cache* c) {
   int pick = -1;
+  bool pick_admitted = true;
   for (size_t j = 0; j < c->slots.size(); ++j) {
     const mr_cache::Slot& sl = c->slots[j];
     if (sl.key == ~0ull) return (int)j;
-    if (sl.last_use < c->clock && (pick < 0 || sl.last_use < c->slots[pick].last_use))
+    if (sl.last_use >= c->clock) continue;
+    const bool adm = cache_admits(c, sl.key);
+    if (pick < 0 || (pick_admitted && !adm) ||
+        (adm == pick_admitted && sl.last_use < c->slots[pick].last_use)) {
       pick = (int)j;
+      pick_admitted = adm;
+    }
   }
   return pick;
 }

@@ -364,17 +364,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (lane < nc) mv = info.shared ? (EPI == EPI_SWIGLU ? 0 : p.sh_row0) + info.col0 + cb + lane
                                         : __ldg(p.cols + info.col0 + cb + lane);
         if constexpr (EPI == EPI_STORE || EPI == EPI_PARTIAL) {
+          if (EPI == EPI_PARTIAL && p.peer_part) {
+            // expert parallel: each routed pair's partial goes to its home rank
+            // (possibly a peer GPU)
 #pragma unroll
-          for (int jj = 0; jj < kPfChunk; ++jj) {
-            if (jj >= nc) break;  // warp-uniform
-            const int v = __shfl_sync(0xffffffffu, mv, jj);
-            if (row_ok) {
-              if constexpr (EPI == EPI_STORE) {
-                p.out_bf16[(int64_t)v * p.rows + grow] = f32_to_bf16_bits(d[jj]);
-              } else {
+            for (int jj = 0; jj < kPfChunk; ++jj) {
+              if (jj >= nc) break;  // warp-uniform
+              const int v = __shfl_sync(0xffffffffu, mv, jj);
+              if (row_ok) {
                 float* dst = p.part;
                 int64_t vv = v;
-                if (p.peer_part && v < p.Tk) {  // the pair's home rank (possibly a peer GPU)
+                if (v < p.Tk) {
                   if (p.peer_row_tok) {
                     const int q = v / p.k;
                     const int home = q / p.peer_rows;
@@ -387,6 +387,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                   }
                 }
                 dst[vv * p.rows + grow] = (v < p.Tk) ? bf16_round(d[jj]) : d[jj];
+              }
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < kPfChunk; ++jj) {
+              if (jj >= nc) break;  // warp-uniform
+              const int v = __shfl_sync(0xffffffffu, mv, jj);
+              if (row_ok) {
+                if constexpr (EPI == EPI_STORE)
+                  p.out_bf16[(int64_t)v * p.rows + grow] = f32_to_bf16_bits(d[jj]);
+                else
+                  p.part[(int64_t)v * p.rows + grow] = (v < p.Tk) ? bf16_round(d[jj]) : d[jj];
               }
             }
           }

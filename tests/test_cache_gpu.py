@@ -100,7 +100,8 @@ def test_cache_policies_keep_outputs_and_follow_admission():
     ref, _ = _run(layers, cached, xs, slot, NL * spec.experts)
     hot = [(0, e) for e in _routed(layers[0], xs[0])]
     for policy in ("none", "pinned_hot_set"):
-        cache = M.ExpertCache(0, 12 * slot, slot)
+        # the hot set plus one call's working set (T * k = 8 experts)
+        cache = M.ExpertCache(0, (len(hot) + 8) * slot, slot)
         try:
             cache.set_policy(policy, hot if policy == "pinned_hot_set" else None)
             for l, lay in enumerate(layers):
