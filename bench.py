@@ -400,8 +400,8 @@ def run_ours(args, world, rank, local):
                 strong["one_gpu_tokens_per_s"] = one
                 strong["speedup_vs_one_gpu"] = strong["tokens_per_s"] / one
 
-    parity = parity_check(args, spec, S, M, torch, dist, world, rank, local, dev, layers,
-                          full_layers, step, xs, T) if not args.no_parity else None
+    parity = guarded("parity", parity_check, args, spec, S, M, torch, dist, world, rank, local,
+                     dev, layers, full_layers, step, xs, T) if not args.no_parity else None
     if full_layers is not None:
         del full_layers
         torch.cuda.empty_cache()
@@ -422,21 +422,23 @@ def run_ours(args, world, rank, local):
             ep_modes[mode] = row
         group.set_mode(args.ep_mode)
     if args.prefill_tokens > 0:
-        prefill = prefill_run(args, S, M, torch, ctx, local, dev, group, world, rank, dist)
+        prefill = guarded("prefill", prefill_run, args, S, M, torch, ctx, local, dev, group, world,
+                          rank, dist)
     k3 = None
     if not ep and args.k3_tokens:
-        k3 = k3_run(args, M, torch, dev, hbm)
+        k3 = guarded("k3", k3_run, args, M, torch, dev, hbm)
     config2 = None
     if args.config == "1" and args.config2_tokens > 0:
-        config2 = config2_run(args, S, M, torch, dist, world, rank, local, dev, group, hbm,
-                              max_over_ranks, barrier)
+        config2 = guarded("config2", config2_run, args, S, M, torch, dist, world, rank, local, dev,
+                          group, hbm, max_over_ranks, barrier)
     config4 = None
     if not ep and args.config4_layers > 0 and args.config == "1":
-        config4 = cache_run(args, M, S, torch, dev, layers_n=args.config4_layers,
-                            budget_gb=args.config4_budget_gb, check_identity=True)
+        config4 = guarded("config4", cache_run, args, M, S, torch, dev,
+                          layers_n=args.config4_layers, budget_gb=args.config4_budget_gb,
+                          check_identity=True)
     elif ep and world >= 4 and args.config4_ep_layers > 0 and args.config == "1":
-        config4 = config4_ep_run(args, S, M, torch, world, rank, local, dev, group,
-                                 max_over_ranks, barrier)
+        config4 = guarded("config4", config4_ep_run, args, S, M, torch, world, rank, local, dev,
+                          group, max_over_ranks, barrier)
 
     e2e = e2e_run(args, spec, T, K, W, xs, schedule, barrier, world, dev, local,
                   group if ep else None)
@@ -519,6 +521,17 @@ def run_ours(args, world, rank, local):
         dist.barrier()
         group.close()
         dist.destroy_process_group()
+
+
+def guarded(name, fn, *a, **k):
+    """Runs one optional sub-line; an exception becomes {"error": ...} in the
+    JSON line instead of costing the headline (every rank takes the same
+    steps, so an error that every rank meets keeps them in step)."""
+    try:
+        return fn(*a, **k)
+    except Exception as e:  # noqa: BLE001 — reported, not swallowed
+        print(f"bench: {name} failed: {type(e).__name__}: {e}", file=sys.stderr, flush=True)
+        return {"error": f"{type(e).__name__}: {e}"}
 
 
 def rel_l2(a, b):
@@ -688,6 +701,15 @@ def prefill_run(args, S, M, torch, ctx, local, dev, group=None, world=1, rank=0,
     # hot experts over the GPUs (contiguous ranges would put them all on one)
     if ep:
         group.set_placement("strided")
+        try:
+            return _prefill(args, S, torch, ctx, local, dev, group, world, rank, dist, spec, T)
+        finally:
+            group.set_placement("contiguous")
+    return _prefill(args, S, torch, ctx, local, dev, group, world, rank, dist, spec, T)
+
+
+def _prefill(args, S, torch, ctx, local, dev, group, world, rank, dist, spec, T):
+    ep = world > 1
     lay = S.synth_layer(spec, layer=0, device=local, shard=(rank, world) if ep else None,
                         strided=ep)
     x = S.synth_x(spec, T * world, layer=0, batch=0, device=local)[rank * T:(rank + 1) * T]
@@ -764,7 +786,6 @@ def prefill_run(args, S, M, torch, ctx, local, dev, group=None, world=1, rank=0,
     per_rank = None
     if ep:
         per_rank = [sum(hist[r::world]) for r in range(world)]
-        group.set_placement("contiguous")
     return {
         "workload": f"config3 prefill T={T} per GPU: config-1 layer, router biased to Zipf(1.1)"
                     + (f", ep{world}, strided expert placement (expert e on GPU e % {world})"
@@ -949,11 +970,21 @@ def config4_ep_run(args, S, M, torch, world, rank, local, dev, group, max_over_r
     tokens, all-to-all mode with capacity 1). As in the one-GPU line each
     layer routes a seeded token of its own. GPU 0's outputs of the first two
     layers are checked bit for bit against the one-GPU layer."""
-    spec = S.CONFIGS[1]
-    NL = args.config4_ep_layers
     group.set_mode("alltoall")
     group.set_placement("contiguous")
     group.set_capacity(1)
+    try:
+        return _config4_ep(args, S, torch, world, rank, local, dev, group, max_over_ranks,
+                           barrier)
+    finally:
+        group.set_capacity(0)
+        group.set_mode(args.ep_mode)
+        torch.cuda.empty_cache()
+
+
+def _config4_ep(args, S, torch, world, rank, local, dev, group, max_over_ranks, barrier):
+    spec = S.CONFIGS[1]
+    NL = args.config4_ep_layers
     layers = [S.synth_layer(spec, layer=l, device=local, shard=(rank, world)) for l in range(NL)]
     steps = max(3, min(args.steps, 10))
     W = max(3, args.warmup)
@@ -992,11 +1023,8 @@ def config4_ep_run(args, S, M, torch, world, rank, local, dev, group, max_over_r
             del full
         torch.cuda.empty_cache()
     barrier()
-    resident = sum(w.nbytes() for lay in layers for w in (lay.gate, lay.up, lay.down))
-    group.set_capacity(0)
-    group.set_mode(args.ep_mode)
+    resident = sum(w.nbytes for lay in layers for w in (lay.gate, lay.up, lay.down))
     del layers
-    torch.cuda.empty_cache()
     return {"workload": f"config4: {NL} config-1 layers, 1-token decode, every routed expert "
                         f"resident ({spec.experts // world} per GPU per layer), the token on "
                         f"GPU 0, all-to-all dispatch",
