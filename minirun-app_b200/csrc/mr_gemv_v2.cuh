@@ -102,9 +102,9 @@ MR_DEVICE void lds2_scales(float (&v)[2], const char* p) {
   }
 }
 
-// Producer warps: each owns every kV2Producers-th stage of the ring (its
-// lane 0 issues that stage's tensor loads, its 32 lanes the activation
-// copies), so several stages' loads are issued at once. One issuing thread
+// Producer warps: each owns every np-th stage of the ring, np = min(this,
+// ring slots) (its lane 0 issues that stage's tensor loads, its 32 lanes the
+// activation copies), so several stages' loads are issued at once. One issuing thread
 // streams this box pattern at well under the HBM rate; a tensor load
 // occupies its issuing thread for on the order of a hundred cycles.
 // Suspend-time hint (ns) of the consumers' slow-path barrier waits; 0: plain
@@ -118,9 +118,52 @@ MR_DEVICE void lds2_scales(float (&v)[2], const char* p) {
 constexpr int kV2Producers = MR_V2_PRODUCERS;
 constexpr int kV2Threads = kTmaConsumers + 32 * kV2Producers;
 
-template <int BITS, int SD, int EPI, int NT>
+// Row tiles (16 rows each) per work item of the down (PARTIAL) launch. The 16
+// consumer warps split an item MT row tiles x (16 / MT) K parts: MT = 16 gives
+// every warp its own rows over the whole K (256-row items, no K reduction
+// and no CTA-wide barrier per item); SwiGLU and store items keep MT = 4.
+// Measured on config 1 (T = 64), down launch: 0.626 ms (MT 4), 0.527 (8),
+// 0.468 (16). 8-bit codes take MT = 8: a 256-row stage of them (128 KB)
+// would leave a one-slot ring (config 2, 8-bit: 22.5 k tokens/s at MT 8,
+// 19.4 k at 16).
+#ifndef MR_V2_DOWN_MT
+#define MR_V2_DOWN_MT 16
+#endif
+constexpr int kV2DownMT = MR_V2_DOWN_MT;
+constexpr int v2_down_mt(int bits) { return bits == 8 && kV2DownMT > 8 ? 8 : kV2DownMT; }
+
+// The weight part of a stage: ROWS rows (gate + up halves for SwiGLU) x 8
+// groups of codes in 128-byte-wide boxes, their scales and biases.
+template <int BITS, int SD, int EPI, int ROWS>
+struct V2W {
+  static constexpr bool kMx = false;
+  static constexpr int kMats = (EPI == EPI_SWIGLU) ? 2 : 1;
+  static constexpr int kRows = ROWS;
+  static constexpr int kBoxRows = ROWS / kMats;      // rows per box (<= 256)
+  static constexpr int kBoxBytes = kBoxRows * 128;   // one 128-byte-wide box
+  static constexpr int kBoxes = BITS / 2;            // boxes per matrix per stage
+  static constexpr int kGroupBytes = 8 * BITS;       // packed bytes per row per group
+  static constexpr int kEsz = ScaleT<SD>::kBytes;
+  static constexpr int kABytes = kMats * kBoxes * kBoxBytes;
+  static constexpr int kSBytes = ROWS * kTmaGps * kEsz;  // scales (or biases)
+  static constexpr int kZBytes = kSBytes;
+  static constexpr uint32_t kTx = kABytes + kSBytes + kZBytes;
+  static_assert(kBoxRows <= 256, "tensor-map boxes hold at most 256 rows");
+};
+
+// Fixed shared memory after the ring: K-part partials of the reduction, the
+// SwiGLU h-sum partials, flags.
+template <int NT, int MT>
+struct V2Fixed {
+  static constexpr int kKS = kTmaConsumerWarps / MT;
+  static constexpr int kRedFloats = (kKS - 1) * MT * NT * 32 * 4;
+  static constexpr int kHsFloats = 4 * kMaxCols * 2;
+  static constexpr int kBytes = (kRedFloats + kHsFloats) * 4 + 16;
+};
+
+template <int BITS, int SD, int EPI, int NT, int MT = 4>
 struct V2Stage {
-  using W = TmaStage<BITS, SD, EPI>;  // the weight boxes, as the TMA kernel
+  using W = V2W<BITS, SD, EPI, (EPI == EPI_SWIGLU ? 64 : MT * 16)>;
   static constexpr int kCols = 8 * NT;
   static constexpr int kXP = EPI == EPI_PARTIAL ? 2 : 1;  // group-sum parts
   static constexpr int kColBytes = kTmaGps * kGroup * 2 + 16;  // one column's 512 bf16 + pad
@@ -132,16 +175,19 @@ struct V2Stage {
   static_assert(kWBytes % 16 == 0 && kSumOff % 16 == 0, "16-byte cp.async destinations");
 };
 
-template <int BITS, int SD, int EPI, int NT>
+template <int BITS, int SD, int EPI, int NT, int MT = 4>
 inline int v2_stages() {
-  const int fixed = TmaFixed<NT>::kBytes + 2 * 16 * 8 + 1024;
-  int n = (kSmemBudget - fixed) / V2Stage<BITS, SD, EPI, NT>::kBytes;
+  const int fixed = V2Fixed<NT, MT>::kBytes + 2 * 16 * 8 + 1024;
+  int n = (kSmemBudget - fixed) / V2Stage<BITS, SD, EPI, NT, MT>::kBytes;
   return n > 12 ? 12 : n;
 }
-template <int BITS, int SD, int EPI, int NT>
+template <int BITS, int SD, int EPI, int NT, int MT = 4>
 inline int v2_smem_bytes(int nst) {
-  return 1024 + nst * V2Stage<BITS, SD, EPI, NT>::kBytes + TmaFixed<NT>::kBytes + 2 * nst * 8;
+  return 1024 + nst * V2Stage<BITS, SD, EPI, NT, MT>::kBytes + V2Fixed<NT, MT>::kBytes +
+         2 * nst * 8;
 }
+// Weight rows per item of a staged launch.
+inline int v2_item_rows(int epi, int bits) { return epi == EPI_PARTIAL ? v2_down_mt(bits) * 16 : 64; }
 
 // Dequantised A fragment of k16 step s (0..3) of one 64-element group:
 // lane words wa (row r8) and wb (row r8 + 8). 8-bit codes give two
@@ -188,14 +234,17 @@ MR_DEVICE void dq_step(uint32_t (&a)[4], uint32_t (&ah)[4],
   }
 }
 
-template <int BITS, int SD, int EPI, int NT>
+template <int BITS, int SD, int EPI, int NT, int MT = 4>
 __global__ void __launch_bounds__(kV2Threads, 1)
     gemv_v2_kernel(const GemvParams p, const __grid_constant__ TmaMaps maps, const int nst) {
+  static_assert(EPI != EPI_SWIGLU || MT == 4, "SwiGLU items: 32 gate + 32 up rows");
   pdl_wait_and_release();
-  using VS = V2Stage<BITS, SD, EPI, NT>;
+  using VS = V2Stage<BITS, SD, EPI, NT, MT>;
   using ST = typename VS::W;
-  static_assert(!ST::kMx, "affine codes only");
-  static_assert(kGpw == 2, "two groups per consumer warp and stage");
+  using FX = V2Fixed<NT, MT>;
+  constexpr int KS = FX::kKS;         // K parts of an item
+  constexpr int kGpw = kTmaGps / KS;  // groups per consumer warp and stage
+  static_assert(KS * MT == kTmaConsumerWarps && kGpw % 2 == 0, "warp split");
   constexpr int LW = QTraits<BITS>::kLaneWords;
   constexpr float kC = QTraits<BITS>::kMagic;
   constexpr int XP = VS::kXP;
@@ -204,9 +253,9 @@ __global__ void __launch_bounds__(kV2Threads, 1)
   // so that loads through it stay shared-memory loads
   char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float* red = reinterpret_cast<float*>(smem + nst * VS::kBytes);
-  float* hs = red + TmaFixed<NT>::kRedFloats;
-  volatile int* flags = reinterpret_cast<volatile int*>(hs + TmaFixed<NT>::kHsFloats);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * VS::kBytes + TmaFixed<NT>::kBytes);
+  float* hs = red + FX::kRedFloats;
+  volatile int* flags = reinterpret_cast<volatile int*>(hs + FX::kHsFloats);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * VS::kBytes + FX::kBytes);
   uint64_t* empty = full + nst;
 
   const int lane = threadIdx.x & 31;
@@ -235,7 +284,14 @@ __global__ void __launch_bounds__(kV2Threads, 1)
     // producer pw issues global stages it = pw, pw + P, ... of this CTA's
     // sequence (items in order, nstages each); stage it uses ring slot
     // it % nst in phase (it / nst) & 1
+    // Slot reuse is ordered by parity waits on the slot's "empty" barrier,
+    // which tell phases apart only one reuse deep: a producer may wait for
+    // stage it - nst only once stage it - 2 * nst is known released. Each
+    // producer's own previous wait (stage it - np - nst) gives that when
+    // np <= nst, so at most nst producer warps take stages.
+    const int np = nst < kV2Producers ? nst : kV2Producers;
     const int pw = warp - kTmaConsumerWarps;
+    if (pw >= np) return;
     uint32_t it = 0;
     const uint64_t wpol = l2_evict_first_policy();
     const uint32_t sbase = smem_u32(smem);
@@ -262,7 +318,7 @@ __global__ void __launch_bounds__(kV2Threads, 1)
         y0 = info.rb * ST::kBoxRows;
       }
       for (int st = 0; st < nstages; ++st, ++it) {
-        if ((int)(it % kV2Producers) != pw) continue;
+        if ((int)(it % (uint32_t)np) != pw) continue;
         const uint32_t slot = it % (uint32_t)nst, phase = (it / (uint32_t)nst) & 1u;
         if (lane == 0) wait_bounded(empty + slot, phase ^ 1u, flags, p.error);
         __syncwarp();
@@ -304,7 +360,7 @@ __global__ void __launch_bounds__(kV2Threads, 1)
       // before it exits (the last nst stages may still be in flight)
       const uint32_t issued = it;
       for (uint32_t j = (issued > (uint32_t)nst ? issued - nst : 0); j < issued; ++j) {
-        if ((int)(j % kV2Producers) != pw) continue;
+        if ((int)(j % (uint32_t)np) != pw) continue;
         for (uint32_t i = 0; i < kSpinLimit; ++i)
           if (mbar_try_wait(full + (j % nst), (j / nst) & 1u)) break;
       }
@@ -315,8 +371,8 @@ __global__ void __launch_bounds__(kV2Threads, 1)
   // -------------------------------------------------------------- consumers
   const int r8 = lane >> 2;
   const int c = lane & 3;
-  const int mt = warp & 3;
-  const int kq = warp >> 2;  // K quarter: groups [2kq, 2kq + 2) of a stage
+  const int mt = warp % MT;
+  const int kq = warp / MT;  // K part: groups [kq * kGpw, (kq + 1) * kGpw) of a stage
   const int ctid = threadIdx.x;
   int ma, ra, mb, rbr;
   if constexpr (EPI == EPI_SWIGLU) {
@@ -410,95 +466,105 @@ __global__ void __launch_bounds__(kV2Threads, 1)
       }
       // Plain shared-memory loads (not volatile asm): the compiler may
       // schedule them anywhere after the wait above and before the release
-      // below, both of which clobber memory.
+      // below, both of which clobber memory. Groups go in pairs (codes,
+      // scales, sums of two groups at a time) to bound the registers when a
+      // warp owns many groups of the stage.
       const char* sp = smem + slot * VS::kBytes;
-      uint32_t wa[kGpw][LW], wb[kGpw][LW];
 #pragma unroll
-      for (int j = 0; j < kGpw; ++j) {
-        if constexpr (LW == 1) {
-          wa[j][0] = *reinterpret_cast<const uint32_t*>(sp + offA[j]);
-          wb[j][0] = *reinterpret_cast<const uint32_t*>(sp + offB[j]);
-        } else if constexpr (LW == 2) {
-          const uint2 u = *reinterpret_cast<const uint2*>(sp + offA[j]);
-          const uint2 v = *reinterpret_cast<const uint2*>(sp + offB[j]);
-          wa[j][0] = u.x; wa[j][1] = u.y;
-          wb[j][0] = v.x; wb[j][1] = v.y;
-        } else {
-          const uint4 u = *reinterpret_cast<const uint4*>(sp + offA[j]);
-          const uint4 v = *reinterpret_cast<const uint4*>(sp + offB[j]);
-          wa[j][0] = u.x; wa[j][1] = u.y; wa[j][2] = u.z; wa[j][3] = u.w;
-          wb[j][0] = v.x; wb[j][1] = v.y; wb[j][2] = v.z; wb[j][3] = v.w;
-        }
-      }
-      float sa[kGpw], za[kGpw], sb[kGpw], zb[kGpw];
-      lds2_scales<SD>(sa, sp + offSa);
-      lds2_scales<SD>(za, sp + offSa + ST::kSBytes);
-      lds2_scales<SD>(sb, sp + offSb);
-      lds2_scales<SD>(zb, sp + offSb + ST::kSBytes);
+      for (int jp = 0; jp < kGpw; jp += 2) {
+        uint32_t wa[2][LW], wb[2][LW];
 #pragma unroll
-      for (int j = 0; j < kGpw; ++j) {
-        za[j] = fmaf(-kC, sa[j], za[j]);
-        zb[j] = fmaf(-kC, sb[j], zb[j]);
-      }
-      // group sums of this lane's accumulator columns for both groups
-      float X0[NT][kGpw], X1[NT][kGpw];
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (t == 0 || t < ntiles) {
-          const char* s0 = sp + offX0 + t * 8 * VS::kSumColBytes;
-          if constexpr (XP == 1) {
-            const float2 u = *reinterpret_cast<const float2*>(s0);
-            const float2 v = *reinterpret_cast<const float2*>(s0 + VS::kSumColBytes);
-            X0[t][0] = u.x; X0[t][1] = u.y;
-            X1[t][0] = v.x; X1[t][1] = v.y;
-          } else {  // two 32-row partial sums per group, added in order
-            const float4 u = *reinterpret_cast<const float4*>(s0);
-            const float4 v = *reinterpret_cast<const float4*>(s0 + VS::kSumColBytes);
-            X0[t][0] = u.x + u.y; X0[t][1] = u.z + u.w;
-            X1[t][0] = v.x + v.y; X1[t][1] = v.z + v.w;
+        for (int u2 = 0; u2 < 2; ++u2) {
+          const int j = jp + u2;
+          if constexpr (LW == 1) {
+            wa[u2][0] = *reinterpret_cast<const uint32_t*>(sp + offA[j]);
+            wb[u2][0] = *reinterpret_cast<const uint32_t*>(sp + offB[j]);
+          } else if constexpr (LW == 2) {
+            const uint2 u = *reinterpret_cast<const uint2*>(sp + offA[j]);
+            const uint2 v = *reinterpret_cast<const uint2*>(sp + offB[j]);
+            wa[u2][0] = u.x; wa[u2][1] = u.y;
+            wb[u2][0] = v.x; wb[u2][1] = v.y;
+          } else {
+            const uint4 u = *reinterpret_cast<const uint4*>(sp + offA[j]);
+            const uint4 v = *reinterpret_cast<const uint4*>(sp + offB[j]);
+            wa[u2][0] = u.x; wa[u2][1] = u.y; wa[u2][2] = u.z; wa[u2][3] = u.w;
+            wb[u2][0] = v.x; wb[u2][1] = v.y; wb[u2][2] = v.z; wb[u2][3] = v.w;
           }
         }
-      }
-      // one group at a time: its B fragments, then each dequantised A
-      // fragment feeds every live tile
+        float sa[2], za[2], sb[2], zb[2];
+        {
+          const int e = jp * ST::kEsz;
+          lds2_scales<SD>(sa, sp + offSa + e);
+          lds2_scales<SD>(za, sp + offSa + ST::kSBytes + e);
+          lds2_scales<SD>(sb, sp + offSb + e);
+          lds2_scales<SD>(zb, sp + offSb + ST::kSBytes + e);
+        }
 #pragma unroll
-      for (int j = 0; j < kGpw; ++j) {
-        uint32_t xb[NT][8];
+        for (int u2 = 0; u2 < 2; ++u2) {
+          za[u2] = fmaf(-kC, sa[u2], za[u2]);
+          zb[u2] = fmaf(-kC, sb[u2], zb[u2]);
+        }
+        // group sums of this lane's accumulator columns for both groups
+        float X0[NT][2], X1[NT][2];
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
           if (t == 0 || t < ntiles) {
-            const char* a = sp + offX + t * 8 * VS::kColBytes + j * kGroup * 2;
-            const uint4 v0 = *reinterpret_cast<const uint4*>(a);
-            const uint4 v1 = *reinterpret_cast<const uint4*>(a + 16);
-            xb[t][0] = v0.x; xb[t][1] = v0.y; xb[t][2] = v0.z; xb[t][3] = v0.w;
-            xb[t][4] = v1.x; xb[t][5] = v1.y; xb[t][6] = v1.z; xb[t][7] = v1.w;
-          }
-        }
-        float acc[NT][4];
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          uint32_t a[4], ah[4];
-          dq_step<BITS>(a, ah, wa[j], wb[j], s, mlo, mhi);
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            if (t == 0 || t < ntiles) {
-              if (s == 0)
-                mma_bf16_16816_z(acc[t], a[0], a[1], a[2], a[3], xb[t][0], xb[t][1]);
-              else
-                mma_bf16_16816(acc[t], a[0], a[1], a[2], a[3], xb[t][2 * s], xb[t][2 * s + 1]);
-              if constexpr (BITS == 8)
-                mma_bf16_16816(acc[t], ah[0], ah[1], ah[2], ah[3], xb[t][2 * s],
-                               xb[t][2 * s + 1]);
+            const char* s0 = sp + offX0 + t * 8 * VS::kSumColBytes + jp * XP * 4;
+            if constexpr (XP == 1) {
+              const float2 u = *reinterpret_cast<const float2*>(s0);
+              const float2 v = *reinterpret_cast<const float2*>(s0 + VS::kSumColBytes);
+              X0[t][0] = u.x; X0[t][1] = u.y;
+              X1[t][0] = v.x; X1[t][1] = v.y;
+            } else {  // two 32-row partial sums per group, added in order
+              const float4 u = *reinterpret_cast<const float4*>(s0);
+              const float4 v = *reinterpret_cast<const float4*>(s0 + VS::kSumColBytes);
+              X0[t][0] = u.x + u.y; X0[t][1] = u.z + u.w;
+              X1[t][0] = v.x + v.y; X1[t][1] = v.z + v.w;
             }
           }
         }
+        // one group at a time: its B fragments, then each dequantised A
+        // fragment feeds every live tile
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (t == 0 || t < ntiles) {
-            y[t][0] = fmaf(sa[j], acc[t][0], fmaf(za[j], X0[t][j], y[t][0]));
-            y[t][1] = fmaf(sa[j], acc[t][1], fmaf(za[j], X1[t][j], y[t][1]));
-            y[t][2] = fmaf(sb[j], acc[t][2], fmaf(zb[j], X0[t][j], y[t][2]));
-            y[t][3] = fmaf(sb[j], acc[t][3], fmaf(zb[j], X1[t][j], y[t][3]));
+        for (int u2 = 0; u2 < 2; ++u2) {
+          const int j = jp + u2;
+          uint32_t xb[NT][8];
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            if (t == 0 || t < ntiles) {
+              const char* a = sp + offX + t * 8 * VS::kColBytes + j * kGroup * 2;
+              const uint4 v0 = *reinterpret_cast<const uint4*>(a);
+              const uint4 v1 = *reinterpret_cast<const uint4*>(a + 16);
+              xb[t][0] = v0.x; xb[t][1] = v0.y; xb[t][2] = v0.z; xb[t][3] = v0.w;
+              xb[t][4] = v1.x; xb[t][5] = v1.y; xb[t][6] = v1.z; xb[t][7] = v1.w;
+            }
+          }
+          float acc[NT][4];
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+            uint32_t a[4], ah[4];
+            dq_step<BITS>(a, ah, wa[u2], wb[u2], s, mlo, mhi);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              if (t == 0 || t < ntiles) {
+                if (s == 0)
+                  mma_bf16_16816_z(acc[t], a[0], a[1], a[2], a[3], xb[t][0], xb[t][1]);
+                else
+                  mma_bf16_16816(acc[t], a[0], a[1], a[2], a[3], xb[t][2 * s], xb[t][2 * s + 1]);
+                if constexpr (BITS == 8)
+                  mma_bf16_16816(acc[t], ah[0], ah[1], ah[2], ah[3], xb[t][2 * s],
+                                 xb[t][2 * s + 1]);
+              }
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            if (t == 0 || t < ntiles) {
+              y[t][0] = fmaf(sa[u2], acc[t][0], fmaf(za[u2], X0[t][u2], y[t][0]));
+              y[t][1] = fmaf(sa[u2], acc[t][1], fmaf(za[u2], X1[t][u2], y[t][1]));
+              y[t][2] = fmaf(sb[u2], acc[t][2], fmaf(zb[u2], X0[t][u2], y[t][2]));
+              y[t][3] = fmaf(sb[u2], acc[t][3], fmaf(zb[u2], X1[t][u2], y[t][3]));
+            }
           }
         }
       }
@@ -512,29 +578,32 @@ __global__ void __launch_bounds__(kV2Threads, 1)
     if (nstages <= 1 && has_next) fetch_cols(nxt);
 
     // ---------------------------------------- K-split reduction (fixed order)
-    if (kq > 0) {
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-        if (t < ntiles)
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            red[((((kq - 1) * 4 + mt) * NT + t) * 32 + lane) * 4 + i] = y[t][i];
-    }
-    named_bar(1, kTmaConsumers);
-    if (kq == 0) {
-#pragma unroll
-      for (int q = 0; q < kKSplit - 1; ++q)
+    if constexpr (KS > 1) {
+      if (kq > 0) {
 #pragma unroll
         for (int t = 0; t < NT; ++t)
           if (t < ntiles)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) y[t][i] += red[(((q * 4 + mt) * NT + t) * 32 + lane) * 4 + i];
+            for (int i = 0; i < 4; ++i)
+              red[((((kq - 1) * MT + mt) * NT + t) * 32 + lane) * 4 + i] = y[t][i];
+      }
+      named_bar(1, kTmaConsumers);
+      if (kq == 0) {
+#pragma unroll
+        for (int q = 0; q < KS - 1; ++q)
+#pragma unroll
+          for (int t = 0; t < NT; ++t)
+            if (t < ntiles)
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                y[t][i] += red[(((q * MT + mt) * NT + t) * 32 + lane) * 4 + i];
+      }
     }
 
     // ------------------------------------------------------------ epilogues
     if constexpr (EPI == EPI_STORE || EPI == EPI_PARTIAL) {
       if (kq == 0) {
-        const int64_t row_a = (int64_t)info.rb * kTmaRows + mt * 16 + r8;
+        const int64_t row_a = (int64_t)info.rb * ST::kRows + mt * 16 + r8;
         const int64_t row_b = row_a + 8;
 #pragma unroll
         for (int t = 0; t < NT; ++t)
@@ -653,7 +722,8 @@ __global__ void __launch_bounds__(kV2Threads, 1)
         if (shared) p.hsum[(int64_t)(vci + p.shared_lo_off) * hp + info.rb] = slo;
       }
     }
-    named_bar(1, kTmaConsumers);  // red / hs reused by the next item
+    // red / hs reused by the next item (a split-free store item shares nothing)
+    if constexpr (KS > 1 || EPI == EPI_SWIGLU) named_bar(1, kTmaConsumers);
     if (has_next) cur = nxt;
   }
   if constexpr (EPI == EPI_PARTIAL) {

@@ -140,9 +140,10 @@ template <int BITS, int SD, int EPI, int NT>
 inline cudaError_t launch_v2_inst(const GemvParams& p, const TmaMaps& m, int grid,
                                   cudaStream_t s) {
   static bool done[64] = {};  // one per instantiation
-  const int nst = v2_stages<BITS, SD, EPI, NT>();
-  const int smem = v2_smem_bytes<BITS, SD, EPI, NT>(nst);
-  auto kern = gemv_v2_kernel<BITS, SD, EPI, NT>;
+  constexpr int MT = EPI == EPI_PARTIAL ? v2_down_mt(BITS) : 4;
+  const int nst = v2_stages<BITS, SD, EPI, NT, MT>();
+  const int smem = v2_smem_bytes<BITS, SD, EPI, NT, MT>(nst);
+  auto kern = gemv_v2_kernel<BITS, SD, EPI, NT, MT>;
   cudaError_t e = opt_in_smem(kern, smem, done);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, grid, kV2Threads, smem, s, p, m, nst);
