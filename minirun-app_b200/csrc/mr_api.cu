@@ -387,7 +387,7 @@ static cudaError_t run_gemv(mr_ctx* ctx, GemvParams g, int64_t max_segments, boo
     TmaMaps tm;
     const bool v2 = use_v2(ctx);
     // item rows: 64 (32 gate + 32 up for SwiGLU); the staged down launch 256
-    const int item_rows = v2 ? v2_item_rows(epi, bits) : kTmaRows;
+    const int item_rows = v2 ? v2_item_rows(epi, bits, g.rows) : kTmaRows;
     const int box_rows = epi == EPI_SWIGLU ? item_rows / 2 : item_rows;
     bool ok = encode_matrix(ctx, maps[0], box_rows, &tm.a_packed, &tm.a_scales, &tm.a_biases);
     const MapSpec& mb = maps[1].d ? maps[1] : maps[0];
@@ -397,7 +397,8 @@ static cudaError_t run_gemv(mr_ctx* ctx, GemvParams g, int64_t max_segments, boo
     ok = ok && encode_matrix(ctx, sa, box_rows, &tm.sa_packed, &tm.sa_scales, &tm.sa_biases);
     ok = ok && encode_matrix(ctx, sb, box_rows, &tm.sb_packed, &tm.sb_scales, &tm.sb_biases);
     if (ok) {
-      g.rb_count = (int)(epi == EPI_SWIGLU ? g.rows / 32 : (g.rows + item_rows - 1) / item_rows);
+      g.rb_count = (int)(epi == EPI_SWIGLU ? g.rows / (item_rows / 2)
+                                           : (g.rows + item_rows - 1) / item_rows);
       const int64_t items = (max_segments + g.shared_segments) * g.rb_count;
       const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
       if (v2) {

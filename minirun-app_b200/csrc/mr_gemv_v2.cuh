@@ -131,6 +131,13 @@ constexpr int kV2Threads = kTmaConsumers + 32 * kV2Producers;
 #endif
 constexpr int kV2DownMT = MR_V2_DOWN_MT;
 constexpr int v2_down_mt(int bits) { return bits == 8 && kV2DownMT > 8 ? 8 : kV2DownMT; }
+// Row tiles per SwiGLU item (each 8 gate + 8 up rows): 4 = 32 + 32 rows with a
+// four-way K split; 16 = 128 + 128 rows, every warp over the whole K.
+#ifndef MR_V2_UP_MT
+#define MR_V2_UP_MT 16
+#endif
+constexpr int kV2UpMT = MR_V2_UP_MT;
+constexpr int v2_up_mt(int bits) { return bits == 8 && kV2UpMT > 8 ? 8 : kV2UpMT; }
 
 // The weight part of a stage: ROWS rows (gate + up halves for SwiGLU) x 8
 // groups of codes in 128-byte-wide boxes, their scales and biases.
@@ -157,13 +164,13 @@ template <int NT, int MT>
 struct V2Fixed {
   static constexpr int kKS = kTmaConsumerWarps / MT;
   static constexpr int kRedFloats = (kKS - 1) * MT * NT * 32 * 4;
-  static constexpr int kHsFloats = 4 * kMaxCols * 2;
+  static constexpr int kHsFloats = (MT > 4 ? MT : 4) * kMaxCols * 2;
   static constexpr int kBytes = (kRedFloats + kHsFloats) * 4 + 16;
 };
 
 template <int BITS, int SD, int EPI, int NT, int MT = 4>
 struct V2Stage {
-  using W = V2W<BITS, SD, EPI, (EPI == EPI_SWIGLU ? 64 : MT * 16)>;
+  using W = V2W<BITS, SD, EPI, MT * 16>;
   static constexpr int kCols = 8 * NT;
   static constexpr int kXP = EPI == EPI_PARTIAL ? 2 : 1;  // group-sum parts
   static constexpr int kColBytes = kTmaGps * kGroup * 2 + 16;  // one column's 512 bf16 + pad
@@ -186,8 +193,16 @@ inline int v2_smem_bytes(int nst) {
   return 1024 + nst * V2Stage<BITS, SD, EPI, NT, MT>::kBytes + V2Fixed<NT, MT>::kBytes +
          2 * nst * 8;
 }
-// Weight rows per item of a staged launch.
-inline int v2_item_rows(int epi, int bits) { return epi == EPI_PARTIAL ? v2_down_mt(bits) * 16 : 64; }
+// Whether a SwiGLU launch over `rows` intermediate rows takes the wide items
+// (their h rows must tile the intermediate exactly: the SwiGLU epilogue has
+// no row bound).
+inline bool v2_up_wide(int bits, int64_t rows) { return rows % (v2_up_mt(bits) * 8) == 0; }
+// Weight rows per item of a staged launch (SwiGLU: gate + up).
+inline int v2_item_rows(int epi, int bits, int64_t rows) {
+  if (epi == EPI_PARTIAL) return v2_down_mt(bits) * 16;
+  if (epi == EPI_SWIGLU && v2_up_wide(bits, rows)) return v2_up_mt(bits) * 16;
+  return 64;
+}
 
 // Dequantised A fragment of k16 step s (0..3) of one 64-element group:
 // lane words wa (row r8) and wb (row r8 + 8). 8-bit codes give two
@@ -237,7 +252,7 @@ MR_DEVICE void dq_step(uint32_t (&a)[4], uint32_t (&ah)[4],
 template <int BITS, int SD, int EPI, int NT, int MT = 4>
 __global__ void __launch_bounds__(kV2Threads, 1)
     gemv_v2_kernel(const GemvParams p, const __grid_constant__ TmaMaps maps, const int nst) {
-  static_assert(EPI != EPI_SWIGLU || MT == 4, "SwiGLU items: 32 gate + 32 up rows");
+  static_assert(EPI != EPI_SWIGLU || MT % 4 == 0, "SwiGLU items: whole 32-row h partials");
   pdl_wait_and_release();
   using VS = V2Stage<BITS, SD, EPI, NT, MT>;
   using ST = typename VS::W;
@@ -643,7 +658,7 @@ __global__ void __launch_bounds__(kV2Threads, 1)
       }
     } else {  // EPI_SWIGLU
       if (kq == 0) {
-        const int hrow = info.rb * 32 + mt * 8 + r8;  // intermediate index (< rows)
+        const int hrow = info.rb * (MT * 8) + mt * 8 + r8;  // intermediate index (< rows)
         const int pos = perm_pos(hrow, p.h_bits);
         const float lim = p.swiglu_limit;
 #pragma unroll
@@ -697,10 +712,12 @@ __global__ void __launch_bounds__(kV2Threads, 1)
           }
         }
       }
-      // thread ci < ncols of warp 0 sums column ci over the 4 m-tiles; the
-      // column's value sits in lane (ci & 7) >> 1 of any warp (v0 or v1)
+      // the item's MT * 8 h rows make MT / 4 partials of 32 rows; lane ci < ncols
+      // of warp q sums column ci over m-tiles 4q .. 4q+3. The column's value
+      // sits in lane (ci & 7) >> 1 of any warp (v0 or v1).
+      constexpr int kParts = MT / 4;
       int vci = 0;
-      if (warp == 0) {
+      if (warp < kParts) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
           const int src = (lane & 7) >> 1;
@@ -710,16 +727,17 @@ __global__ void __launch_bounds__(kV2Threads, 1)
         }
       }
       named_bar(1, kTmaConsumers);
-      if (ctid < ncols) {
+      if (warp < kParts && lane < ncols) {
         float shi = 0.0f, slo = 0.0f;
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
-          shi += hs[(m * kMaxCols + ctid) * 2 + 0];
-          slo += hs[(m * kMaxCols + ctid) * 2 + 1];
+          shi += hs[((warp * 4 + m) * kMaxCols + lane) * 2 + 0];
+          slo += hs[((warp * 4 + m) * kMaxCols + lane) * 2 + 1];
         }
         const int64_t hp = p.rows / 32;  // 32-row partial sums per h row
-        p.hsum[(int64_t)vci * hp + info.rb] = shi;
-        if (shared) p.hsum[(int64_t)(vci + p.shared_lo_off) * hp + info.rb] = slo;
+        const int64_t part = (int64_t)info.rb * kParts + warp;
+        p.hsum[(int64_t)vci * hp + part] = shi;
+        if (shared) p.hsum[(int64_t)(vci + p.shared_lo_off) * hp + part] = slo;
       }
     }
     // red / hs reused by the next item (a split-free store item shares nothing)

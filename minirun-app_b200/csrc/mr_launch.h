@@ -136,11 +136,10 @@ inline cudaError_t launch_tma_inst(const GemvParams& p, const TmaMaps& m, int gr
   return launch_pdl(kern, grid, kTmaThreads, smem, s, p, m, nst);
 }
 
-template <int BITS, int SD, int EPI, int NT>
+template <int BITS, int SD, int EPI, int NT, int MT>
 inline cudaError_t launch_v2_inst(const GemvParams& p, const TmaMaps& m, int grid,
                                   cudaStream_t s) {
   static bool done[64] = {};  // one per instantiation
-  constexpr int MT = EPI == EPI_PARTIAL ? v2_down_mt(BITS) : 4;
   const int nst = v2_stages<BITS, SD, EPI, NT, MT>();
   const int smem = v2_smem_bytes<BITS, SD, EPI, NT, MT>(nst);
   auto kern = gemv_v2_kernel<BITS, SD, EPI, NT, MT>;
@@ -271,11 +270,21 @@ inline cudaError_t launch_pf_epi(const GemvParams& p, const UmMaps& m, int epi, 
                                  int nt, int grid, cudaStream_t s) {                           \
     return dispatch_##BITS(p, &m, sd, epi, nt, grid, s);                                       \
   }                                                                                            \
+  template <int SD, int EPI, int MT>                                                           \
+  static cudaError_t v2_mt_##BITS(const GemvParams& p, const TmaMaps& m, int nt, int grid,     \
+                                  cudaStream_t s) {                                            \
+    return nt == 1 ? launch_v2_inst<BITS, SD, EPI, 1, MT>(p, m, grid, s)                       \
+                   : launch_v2_inst<BITS, SD, EPI, 2, MT>(p, m, grid, s);                      \
+  }                                                                                            \
   template <int SD, int EPI>                                                                   \
   static cudaError_t v2_nt_##BITS(const GemvParams& p, const TmaMaps& m, int nt, int grid,     \
                                   cudaStream_t s) {                                            \
-    return nt == 1 ? launch_v2_inst<BITS, SD, EPI, 1>(p, m, grid, s)                           \
-                   : launch_v2_inst<BITS, SD, EPI, 2>(p, m, grid, s);                          \
+    if constexpr (EPI == EPI_PARTIAL)                                                          \
+      return v2_mt_##BITS<SD, EPI, v2_down_mt(BITS)>(p, m, nt, grid, s);                       \
+    if constexpr (EPI == EPI_SWIGLU) {                                                         \
+      if (v2_up_wide(BITS, p.rows)) return v2_mt_##BITS<SD, EPI, v2_up_mt(BITS)>(p, m, nt, grid, s); \
+    }                                                                                          \
+    return v2_mt_##BITS<SD, EPI, 4>(p, m, nt, grid, s);                                        \
   }                                                                                            \
   template <int SD>                                                                            \
   static cudaError_t v2_epi_##BITS(const GemvParams& p, const TmaMaps& m, int epi, int nt,     \
