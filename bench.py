@@ -1089,7 +1089,7 @@ def read_traffic(algorithmic_bytes):
     rules): its dram read+write bytes and its algorithmic bytes. Traffic grows
     with the weight bytes a launch streams, so the bench launch's traffic is the
     captured ratio times its own algorithmic bytes."""
-    path = os.path.join(ROOT, "profiles", "gemv_gate_up_config1.md")
+    path = os.path.join(ROOT, "profiles", "gemv_v2_gate_up_config1.md")
     vals = {}
     try:
         for line in open(path):
