@@ -1,12 +1,13 @@
 // mr_gemv_v2.cuh — staged-activation form of the TMA dequant-GEMV (affine
 // 2/4/8-bit codes), the default decode kernel.
 //
-// Same work items, plan, weight pipeline and epilogues as gemv_tma_kernel
+// Same plan, weight pipeline and epilogues as gemv_tma_kernel
 // (mr_gemv_tma.cuh): one CTA per SM loops over items = (segment of <= 8*NT
-// columns sharing an expert) x (64 rows: 64 plain rows, or 32 gate + 32 up
-// rows for SwiGLU); a producer warp streams each item's packed codes and
-// scale/bias boxes with 2-D tensor TMA into an NST-deep shared-memory ring.
-// What changes is everything the consumers touch besides the codes:
+// columns sharing an expert) x (a block of rows: MT row tiles of 16 rows, or
+// for SwiGLU MT tiles of 8 gate + 8 up rows); up to four producer warps
+// stream the items' packed codes and scale/bias boxes with 2-D tensor TMA
+// into an NST-deep shared-memory ring. What changes is everything the
+// consumers touch besides the codes:
 //
 //  - Activations. Besides the weight boxes, every stage slot holds the
 //    stage's 512 permuted activations of each of the item's columns and
@@ -20,6 +21,9 @@
 //  - Columns. A segment holds up to NT mma tiles of 8 columns. Each A
 //    fragment (16 rows x 16 codes) is dequantised once and fed to all NT
 //    tiles, so an expert with 9-16 columns costs one dequantisation.
+//  - Rows. The 16 consumer warps split an item MT row tiles x 16/MT K parts;
+//    at MT = 16 (256-row down items, 128 + 128-row gate/up items) every warp
+//    owns its rows over the whole K and an item needs no reduction.
 //  - Loop. One path for every segment width (no single-column FMA path), the
 //    first mma of each group takes a zero accumulator, and per-stage scale
 //    unpacking happens once per warp.
@@ -28,9 +32,9 @@
 // pair into the bf16 pair (C + q) (C = 128, or 2048*hi + 128 + lo for 8-bit),
 // mma.m16n8k16 accumulates sum((C + q) * x) over one 64-element group in fp32
 // and the fold y += s*acc + (z - C*s)*sum(x) applies scale and bias, which is
-// sum((s*q + z)*x) up to fp32 rounding. The four K quarters of an item are
-// summed in a fixed order, so results are deterministic and independent of
-// the other columns of the batch.
+// sum((s*q + z)*x) up to fp32 rounding. K parts of an item are summed in a
+// fixed order, so results are deterministic and independent of the other
+// columns of the batch.
 #pragma once
 
 #include "mr_gemv_tma.cuh"
@@ -177,7 +181,9 @@ struct V2Stage {
   static constexpr int kWBytes = W::kABytes + W::kSBytes + W::kZBytes;
   static constexpr int kXOff = kWBytes;                          // activations
   static constexpr int kSumOff = kXOff + kCols * kColBytes;      // group sums
-  static constexpr int kSumColBytes = kTmaGps * kXP * 4;         // per column
+  // per column, padded by 16 bytes: the columns 2c (c = 0..3) that one load
+  // instruction reads then start in distinct banks
+  static constexpr int kSumColBytes = kTmaGps * kXP * 4 + 16;
   static constexpr int kBytes = (kSumOff + kCols * kSumColBytes + 1023) / 1024 * 1024;
   static_assert(kWBytes % 16 == 0 && kSumOff % 16 == 0, "16-byte cp.async destinations");
 };
@@ -202,6 +208,23 @@ inline int v2_item_rows(int epi, int bits, int64_t rows) {
   if (epi == EPI_PARTIAL) return v2_down_mt(bits) * 16;
   if (epi == EPI_SWIGLU && v2_up_wide(bits, rows)) return v2_up_mt(bits) * 16;
   return 64;
+}
+
+// Weight row (within its 8-row block) of mma fragment row r8. The codes sit in
+// 128-byte-swizzled rows (16-byte chunk index XOR row % 8), and the lanes of
+// one shared-memory phase read the same logical chunks of their rows: rows
+// r8 0..3 (8-byte loads, 4-bit: two chunks per row) or 0..1 (16-byte loads,
+// 8-bit: four chunks per row). Their physical chunks are distinct, and the
+// loads free of bank conflicts, only when those rows differ in the XOR bits
+// above the ones the chunk span covers: rows 0, 2, 4, 6 then 1, 3, 5, 7
+// (4-bit), rows 0, 4 then 1, 5, ... (8-bit). 2-bit rows (one chunk, all eight
+// rows per phase) take the 4-bit order. The epilogues use the same map.
+template <int BITS>
+MR_DEVICE int v2_frag_row(int r8) {
+  if constexpr (BITS == 8)
+    return ((r8 & 1) << 2) | (r8 >> 1);
+  else
+    return ((r8 & 3) << 1) | (r8 >> 2);
 }
 
 // Dequantised A fragment of k16 step s (0..3) of one 64-element group:
@@ -389,29 +412,36 @@ __global__ void __launch_bounds__(kV2Threads, 1)
   const int mt = warp % MT;
   const int kq = warp / MT;  // K part: groups [kq * kGpw, (kq + 1) * kGpw) of a stage
   const int ctid = threadIdx.x;
+  const int rr = v2_frag_row<BITS>(r8);  // this lane's rows: rr (+ 8)
   int ma, ra, mb, rbr;
   if constexpr (EPI == EPI_SWIGLU) {
     ma = 0;
-    ra = mt * 8 + r8;
+    ra = mt * 8 + rr;
     mb = 1;
-    rbr = mt * 8 + r8;
+    rbr = mt * 8 + rr;
   } else {
     ma = 0;
-    ra = mt * 16 + r8;
+    ra = mt * 16 + rr;
     mb = 0;
     rbr = ra + 8;
   }
-  // per-lane shared-memory offsets inside a stage, fixed for the kernel
-  uint32_t offA[kGpw], offB[kGpw];
+  // per-lane shared-memory offsets inside a stage, fixed for the kernel. A
+  // 128-byte box row holds kGpb groups; group j of the warp's share sits in
+  // box j / kGpb at the swizzled chunk of j % kGpb, so kGpb offsets (plus a
+  // constant box stride) cover every group. Row rbr is ra + 8 of the same
+  // box (plain) or row ra of the up box (SwiGLU): the same swizzle, so its
+  // offsets are those of ra plus a constant.
+  constexpr int kGpb = (128 / ST::kGroupBytes) < kGpw ? (128 / ST::kGroupBytes) : kGpw;
+  uint32_t offA[kGpb];
 #pragma unroll
-  for (int j = 0; j < kGpw; ++j) {
+  for (int j = 0; j < kGpb; ++j) {
     const int b = (kq * kGpw + j) * ST::kGroupBytes + c * LW * 4;  // stage-row byte
     const int box = b >> 7, bb = b & 127;
     offA[j] = (ma * ST::kBoxes + box) * ST::kBoxBytes + ra * 128 + ((((bb >> 4) ^ ra) & 7) << 4) +
               (bb & 15);
-    offB[j] = (mb * ST::kBoxes + box) * ST::kBoxBytes + rbr * 128 +
-              ((((bb >> 4) ^ rbr) & 7) << 4) + (bb & 15);
   }
+  const uint32_t dB = (mb - ma) * ST::kBoxes * ST::kBoxBytes + (rbr - ra) * 128;
+  auto off_a = [&](int j) -> uint32_t { return offA[j % kGpb] + (j / kGpb) * ST::kBoxBytes; };
   const uint32_t offSa = ST::kABytes + ((ma * ST::kBoxRows + ra) * kTmaGps + kq * kGpw) * ST::kEsz;
   const uint32_t offSb = ST::kABytes + ((mb * ST::kBoxRows + rbr) * kTmaGps + kq * kGpw) * ST::kEsz;
   // B fragments: column r8 (+ 8t), elements [16c, 16c + 16) of each group
@@ -491,17 +521,18 @@ __global__ void __launch_bounds__(kV2Threads, 1)
 #pragma unroll
         for (int u2 = 0; u2 < 2; ++u2) {
           const int j = jp + u2;
+          const char* pa = sp + off_a(j);
           if constexpr (LW == 1) {
-            wa[u2][0] = *reinterpret_cast<const uint32_t*>(sp + offA[j]);
-            wb[u2][0] = *reinterpret_cast<const uint32_t*>(sp + offB[j]);
+            wa[u2][0] = *reinterpret_cast<const uint32_t*>(pa);
+            wb[u2][0] = *reinterpret_cast<const uint32_t*>(pa + dB);
           } else if constexpr (LW == 2) {
-            const uint2 u = *reinterpret_cast<const uint2*>(sp + offA[j]);
-            const uint2 v = *reinterpret_cast<const uint2*>(sp + offB[j]);
+            const uint2 u = *reinterpret_cast<const uint2*>(pa);
+            const uint2 v = *reinterpret_cast<const uint2*>(pa + dB);
             wa[u2][0] = u.x; wa[u2][1] = u.y;
             wb[u2][0] = v.x; wb[u2][1] = v.y;
           } else {
-            const uint4 u = *reinterpret_cast<const uint4*>(sp + offA[j]);
-            const uint4 v = *reinterpret_cast<const uint4*>(sp + offB[j]);
+            const uint4 u = *reinterpret_cast<const uint4*>(pa);
+            const uint4 v = *reinterpret_cast<const uint4*>(pa + dB);
             wa[u2][0] = u.x; wa[u2][1] = u.y; wa[u2][2] = u.z; wa[u2][3] = u.w;
             wb[u2][0] = v.x; wb[u2][1] = v.y; wb[u2][2] = v.z; wb[u2][3] = v.w;
           }
@@ -618,7 +649,7 @@ __global__ void __launch_bounds__(kV2Threads, 1)
     // ------------------------------------------------------------ epilogues
     if constexpr (EPI == EPI_STORE || EPI == EPI_PARTIAL) {
       if (kq == 0) {
-        const int64_t row_a = (int64_t)info.rb * ST::kRows + mt * 16 + r8;
+        const int64_t row_a = (int64_t)info.rb * ST::kRows + mt * 16 + rr;
         const int64_t row_b = row_a + 8;
 #pragma unroll
         for (int t = 0; t < NT; ++t)
@@ -658,7 +689,7 @@ __global__ void __launch_bounds__(kV2Threads, 1)
       }
     } else {  // EPI_SWIGLU
       if (kq == 0) {
-        const int hrow = info.rb * (MT * 8) + mt * 8 + r8;  // intermediate index (< rows)
+        const int hrow = info.rb * (MT * 8) + mt * 8 + rr;  // intermediate index (< rows)
         const int pos = perm_pos(hrow, p.h_bits);
         const float lim = p.swiglu_limit;
 #pragma unroll
