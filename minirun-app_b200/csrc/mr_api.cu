@@ -221,6 +221,30 @@ static int decode_seg_cols(const mr_ctx* ctx, int64_t Tk, int64_t E) {
   return (use_v2(ctx) && Tk > 8 * E) ? 16 : pick_seg_cols(Tk);
 }
 
+static bool have_encoder();
+
+// Whether a decode forward's gate/up launch (routed and shared experts) takes
+// the f16 activation form of the prep: the staged GEMV streams every gate/up
+// stack (4- or 8-bit codes) and the tensor-map encoder is there. The prep and
+// the launch both follow this one decision; a map the driver then refuses
+// fails the call (the other kernels read the bf16 form only).
+static bool gate_up_f16(const mr_ctx* ctx, const mr_moe_layer* L, bool tcgen05) {
+  if (tcgen05 || !use_v2(ctx) || L->expert_table) return false;
+  const int64_t H = L->hidden;
+  const int bits = L->gate.bits;
+  if ((bits != 4 && bits != 8) || L->up.bits != bits || !tma_layout_ok(H, &L->gate, false) ||
+      !tma_layout_ok(H, &L->up, false))
+    return false;
+  if (L->shared_inter > 0 &&
+      (L->shared_gate.bits != bits || L->shared_up.bits != bits ||
+       !tma_layout_ok(H, &L->shared_gate, false) || !tma_layout_ok(H, &L->shared_up, false)))
+    return false;
+  return have_encoder();
+}
+
+// Floats per group of the prepped activations' sums (bf16 form: 1).
+static int64_t xsum_floats(bool f16) { return f16 ? kPrepF16Floats : 1; }
+
 // Activation rows of routed columns in plan order (tcgen05 layer path with
 // more than 16 tokens): xg[c] = x_perm[cols[c] / in_div], and its group sums.
 // Positions past the plan's valid columns may hold stale ids; rows outside
@@ -266,6 +290,7 @@ static EncodeTiledFn encode_fn() {
   }
   return fn;
 }
+static bool have_encoder() { return encode_fn() != nullptr; }
 
 // kind 0: packed codes (uint32 words, 32-word x box_rows boxes, 128-byte
 // swizzle); kind 1/2/3: bf16/f16/f32 scales or biases (8 x box_rows boxes);
@@ -402,14 +427,18 @@ static cudaError_t run_gemv(mr_ctx* ctx, GemvParams g, int64_t max_segments, boo
       const int64_t items = (max_segments + g.shared_segments) * g.rb_count;
       const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, ctx->sm_count));
       if (v2) {
-        g.dq_magic_lo = 0x43004300u;
-        g.dq_magic_hi = 0x45004500u;
+        // bf16 form: 128 + q (and 2048 + 16q for the high nibble of a byte);
+        // f16 form: 1024 + q, 64 + q for a nibble in bits 4-7
+        g.dq_magic_lo = g.x_f16 ? 0x64006400u : 0x43004300u;
+        g.dq_magic_hi = g.x_f16 ? 0x54005400u : 0x45004500u;
         return launch_v2(g, tm, bits, sd, epi, nt, grid, s);
       }
+      if (g.x_f16) return cudaErrorNotSupported;
       return launch_tma(g, tm, bits, sd, epi, nt, grid, s);
     }
     // no driver entry point / map refused: stream with the register kernel
   }
+  if (g.x_f16) return cudaErrorNotSupported;  // the f16 form is the staged kernel's
   g.rb_count = (int)(epi == EPI_SWIGLU ? g.rows / kRowsUp : (g.rows + kRowsPlain - 1) / kRowsPlain);
   const int64_t items = (max_segments + g.shared_segments) * g.rb_count;
   return launch_gemv(g, bits, sd, epi, nt, (int)items, s);
@@ -1276,7 +1305,7 @@ struct RoutePlan {
 static mr_status route_tokens(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t* x, int64_t T,
                               const LogitsShape& ls, float* part, uint16_t* xperm, float* xsum,
                               int32_t* ids, float* wts, float* margins, const RoutePlan& rp,
-                              cudaStream_t s, const HashChoice* hc = nullptr) {
+                              cudaStream_t s, const HashChoice* hc = nullptr, bool xf16 = false) {
   const int E = L->router.experts;
   const int64_t H = L->hidden;
   LogitsParams lp{};
@@ -1292,6 +1321,7 @@ static mr_status route_tokens(mr_ctx* ctx, const mr_moe_layer* L, const uint16_t
   lp.part = part;
   lp.logit_blocks = ls.blocks;
   lp.prep = PrepParams{x, T, H, L->gate.bits, xperm, xsum};
+  lp.prep.f16 = xf16 ? 1 : 0;
   lp.do_prep = 1;
   const int64_t chunks = T * (H / 16);
   const int prep_blocks = (int)std::min<int64_t>((chunks + 127) / 128, 2 * ctx->sm_count);
@@ -1333,6 +1363,7 @@ struct ExpertsRun {
   // expert parallel, fused: the down GEMV stores routed partials into their
   // home ranks' buffers (GemvParams::peer_*); nullptr elsewhere
   const GemvParams* peer;
+  bool x_f16;  // gate/up activations in the prep's f16 form (staged GEMV)
 };
 
 static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRun& r,
@@ -1373,6 +1404,7 @@ static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRu
   g.xperm = r.xperm;
   g.xsum = r.xsum;
   g.xsum_parts = 1;
+  g.x_f16 = r.x_f16 ? 1 : 0;
   g.error = ctx->d_error;
   g.out_bf16 = r.h;
   g.hsum = r.hsum;
@@ -1502,6 +1534,7 @@ static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
                       (!has_shared || L->shared_gate.bits == L->gate.bits) && Tk >= 32 * (int64_t)E;
   const bool um_try = !pf_try && ctx->kernel_path == 3 && um_layout;
   const bool um_dense = !pf_try && T <= kUmN;  // routed activations are the token rows
+  const bool xf16 = gate_up_f16(ctx, L, pf_try || um_try);
   // segments per expert of seg_cols columns; the workspace holds the plan of
   // the narrowest segments, the width is fixed once the kernels are chosen
   const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / pick_seg_cols(T) + 1;
@@ -1524,7 +1557,7 @@ static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
     }
     part = b.take<float>((size_t)ls.kq * T * E);
     xperm = b.take<uint16_t>(T * H);
-    xsum = b.take<float>(T * (H / kGroup));
+    xsum = b.take<float>(T * (H / kGroup) * xsum_floats(xf16));
     ids = b.take<int32_t>(Tk);
     wts = b.take<float>(Tk);
     nseg = b.take<int>(4);
@@ -1572,7 +1605,7 @@ static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   {
     const RoutePlan rp{nseg, segs, cols, seg_cols, 0, E, false};
     if ((st = route_tokens(ctx, L, x, T, ls, part, xperm, xsum, ids, wts, margins_out, rp, s,
-                           hc)))
+                           hc, xf16)))
       return st;
   }
   if ((um && !um_dense) || pf) {
@@ -1587,6 +1620,7 @@ static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   ExpertsRun r{};
   r.xperm = xperm;
   r.xsum = xsum;
+  r.x_f16 = xf16;
   r.tokens = T;
   r.shared_tokens = has_shared ? T : 0;
   r.Tk = Tk;
@@ -2601,6 +2635,8 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
                              L->shared_down.bits == bits)) &&
             Tcap * W * k >= 32 * (int64_t)E;
   const bool pf_sh = pf && has_shared && T >= 32;  // the shared expert's own launch
+  const bool xf16 = gate_up_f16(ctx, L, pf);
+  const int64_t xsf = xsum_floats(xf16);
   int seg_cols = pf ? kPfN : decode_seg_cols(ctx, Tcap * W * k, E);
   const int64_t max_seg = std::min<int64_t>(El, RK) + RK / 8 + 1;
   const LogitsShape ls = logits_shape(ctx, std::max<int64_t>(T, 1), E, H);
@@ -2632,7 +2668,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
     }
     part = b.take<float>((size_t)ls.kq * T * E);
     xperm = b.take<uint16_t>(T * H);
-    xsum = b.take<float>(T * (H / kGroup));
+    xsum = b.take<float>(T * (H / kGroup) * xsf);
     ids = b.take<int32_t>(Tk);
     wts = b.take<float>(Tk);
     nseg0 = b.take<int>(4);
@@ -2642,7 +2678,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
     count = b.take<int>(W);
     ids_recv = b.take<int32_t>(RK);
     xrecv = b.take<uint16_t>(R * H);
-    xsrecv = b.take<float>(R * (H / kGroup));
+    xsrecv = b.take<float>(R * (H / kGroup) * xsf);
     nseg = b.take<int>(4);
     zero = b.take<int>(4);
     segs = b.take<int4>(max_seg);
@@ -2686,7 +2722,8 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
   // 1. route this rank's tokens (the prep also gives the shared expert's rows)
   if (T > 0) {
     const RoutePlan rp{nseg0, segs0, cols0, seg_own, 0, E, false};
-    if ((st = route_tokens(ctx, L, x, T, ls, part, xperm, xsum, ids, wts, nullptr, rp, s)))
+    if ((st = route_tokens(ctx, L, x, T, ls, part, xperm, xsum, ids, wts, nullptr, rp, s,
+                           nullptr, xf16)))
       return st;
   }
   // 2. dispatch: compact positions per destination, then rows + metadata
@@ -2728,6 +2765,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
   {
     PrepParams pp{reinterpret_cast<const uint16_t*>(slab + lay.rows), R, H, L->gate.bits, xrecv,
                   xsrecv};
+    pp.f16 = xf16 ? 1 : 0;
     const int64_t chunks = R * (H / 16);
     const int pgrid = (int)std::max<int64_t>(
         1, std::min<int64_t>((chunks + 255) / 256, 4 * (int64_t)ctx->sm_count));
@@ -2750,6 +2788,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
     ExpertsRun r{};
     r.xperm = xrecv;
     r.xsum = xsrecv;
+    r.x_f16 = xf16;
     r.tokens = R;
     r.shared_tokens = 0;
     r.Tk = RK;
@@ -2786,6 +2825,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
     ExpertsRun sh{};
     sh.xperm = xperm;
     sh.xsum = xsum;
+    sh.x_f16 = xf16;
     sh.tokens = T;
     sh.shared_tokens = T;
     sh.Tk = 0;
@@ -2878,6 +2918,8 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
   const int seg_cols = decode_seg_cols(ctx, NTk, E);
   const int64_t max_seg = std::min<int64_t>(El, NTk) + NTk / seg_cols + 1;
   const LogitsShape ls = logits_shape(ctx, NT, E, H);
+  const bool xf16 = gate_up_f16(ctx, L, false);
+  const int64_t xsf = xsum_floats(xf16);
 
   uint16_t *xall = nullptr, *xperm = nullptr, *h = nullptr, *hs = nullptr;
   float *part = nullptr, *xsum = nullptr, *wts = nullptr, *hsum = nullptr, *part2 = nullptr;
@@ -2891,7 +2933,7 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
     xall = b.take<uint16_t>(NT * H);
     part = b.take<float>((size_t)ls.kq * NT * E);
     xperm = b.take<uint16_t>(NT * H);
-    xsum = b.take<float>(NT * (H / kGroup));
+    xsum = b.take<float>(NT * (H / kGroup) * xsf);
     ids = b.take<int32_t>(NTk);
     wts = b.take<float>(NTk);
     nseg = b.take<int>(4);
@@ -2923,12 +2965,14 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
   }
   // router over all tokens (the same on every rank); plan of this rank's experts
   const RoutePlan rp{nseg, segs, cols, seg_cols, base, El, true, stride};
-  if ((st = route_tokens(ctx, L, xall, NT, ls, part, xperm, xsum, ids, wts, nullptr, rp, s)))
+  if ((st = route_tokens(ctx, L, xall, NT, ls, part, xperm, xsum, ids, wts, nullptr, rp, s,
+                         nullptr, xf16)))
     return st;
   // this rank's experts over the pairs routed to them
   ExpertsRun r{};
   r.xperm = xperm;
   r.xsum = xsum;
+  r.x_f16 = xf16;
   r.tokens = NT;
   r.shared_tokens = 0;
   r.Tk = NTk;
@@ -2983,7 +3027,8 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
         return st;
       ExpertsRun sh{};
       sh.xperm = xperm + (int64_t)rank * T * H;
-      sh.xsum = xsum + (int64_t)rank * T * (H / kGroup);
+      sh.xsum = xsum + (int64_t)rank * T * (H / kGroup) * xsf;
+      sh.x_f16 = xf16;
       sh.tokens = T;
       sh.shared_tokens = T;
       sh.Tk = 0;
@@ -3031,7 +3076,8 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
         return st;
       ExpertsRun sh{};
       sh.xperm = xperm + (int64_t)rank * T * H;
-      sh.xsum = xsum + (int64_t)rank * T * (H / kGroup);
+      sh.xsum = xsum + (int64_t)rank * T * (H / kGroup) * xsf;
+      sh.x_f16 = xf16;
       sh.tokens = T;
       sh.shared_tokens = T;
       sh.Tk = 0;

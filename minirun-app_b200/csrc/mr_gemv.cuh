@@ -53,6 +53,10 @@ MR_DEVICE int perm_pos(int i, int bits) {
   return (i - e) + (e < h ? 2 * e : 2 * (e - h) + 1);
 }
 
+// Floats per group of the prepped activation sums in the f16 form
+// ({2^k, W, X, 0}; the bf16 form has one).
+constexpr int kPrepF16Floats = 4;
+
 struct GemvParams {
   ExpertSource src_a;  // gate (SwiGLU) or the projection
   ExpertSource src_b;  // up (SwiGLU only)
@@ -107,6 +111,9 @@ struct GemvParams {
   // and (q & mask) | magic stays one three-input logic op per code pair
   uint32_t dq_magic_lo;
   uint32_t dq_magic_hi;
+  // staged gate/up: activations in the f16 form of the prep (xperm f16,
+  // xsum {2^k, W, X, 0} per group)
+  int x_f16;
   int shared_lo_off;      // SWIGLU: shared lo row = hi row + shared_lo_off
   // combine (PARTIAL)
   unsigned* counters;

@@ -172,31 +172,40 @@ struct V2Fixed {
   static constexpr int kBytes = (kRedFloats + kHsFloats) * 4 + 16;
 };
 
-template <int BITS, int SD, int EPI, int NT, int MT = 4>
+// Bytes per column of a stage's group sums: at least `raw`, a multiple of 16
+// (cp.async), and such that the columns 2c (c = 0..3) that one load
+// instruction reads start 8 or 24 banks apart (no bank conflicts).
+constexpr int v2_sum_col_bytes(int raw) {
+  int b = (raw + 15) / 16 * 16;
+  while ((b / 2) % 32 != 8 && (b / 2) % 32 != 24) b += 16;
+  return b;
+}
+
+template <int BITS, int SD, int EPI, int NT, int MT = 4, bool XH = false>
 struct V2Stage {
   using W = V2W<BITS, SD, EPI, MT * 16>;
   static constexpr int kCols = 8 * NT;
-  static constexpr int kXP = EPI == EPI_PARTIAL ? 2 : 1;  // group-sum parts
+  // floats per group and column of the stage's sums: two 32-row partial
+  // sums (down), one sum (gate/up), {2^k, W, X, 0} of the f16 form
+  static constexpr int kXP = EPI == EPI_PARTIAL ? 2 : (XH ? kPrepF16Floats : 1);
   static constexpr int kColBytes = kTmaGps * kGroup * 2 + 16;  // one column's 512 bf16 + pad
   static constexpr int kWBytes = W::kABytes + W::kSBytes + W::kZBytes;
   static constexpr int kXOff = kWBytes;                          // activations
   static constexpr int kSumOff = kXOff + kCols * kColBytes;      // group sums
-  // per column, padded by 16 bytes: the columns 2c (c = 0..3) that one load
-  // instruction reads then start in distinct banks
-  static constexpr int kSumColBytes = kTmaGps * kXP * 4 + 16;
+  static constexpr int kSumColBytes = v2_sum_col_bytes(kTmaGps * kXP * 4);  // per column
   static constexpr int kBytes = (kSumOff + kCols * kSumColBytes + 1023) / 1024 * 1024;
   static_assert(kWBytes % 16 == 0 && kSumOff % 16 == 0, "16-byte cp.async destinations");
 };
 
-template <int BITS, int SD, int EPI, int NT, int MT = 4>
+template <int BITS, int SD, int EPI, int NT, int MT = 4, bool XH = false>
 inline int v2_stages() {
   const int fixed = V2Fixed<NT, MT>::kBytes + 2 * 16 * 8 + 1024;
-  int n = (kSmemBudget - fixed) / V2Stage<BITS, SD, EPI, NT, MT>::kBytes;
+  int n = (kSmemBudget - fixed) / V2Stage<BITS, SD, EPI, NT, MT, XH>::kBytes;
   return n > 12 ? 12 : n;
 }
-template <int BITS, int SD, int EPI, int NT, int MT = 4>
+template <int BITS, int SD, int EPI, int NT, int MT = 4, bool XH = false>
 inline int v2_smem_bytes(int nst) {
-  return 1024 + nst * V2Stage<BITS, SD, EPI, NT, MT>::kBytes + V2Fixed<NT, MT>::kBytes +
+  return 1024 + nst * V2Stage<BITS, SD, EPI, NT, MT, XH>::kBytes + V2Fixed<NT, MT>::kBytes +
          2 * nst * 8;
 }
 // Whether a SwiGLU launch over `rows` intermediate rows takes the wide items
@@ -272,12 +281,51 @@ MR_DEVICE void dq_step(uint32_t (&a)[4], uint32_t (&ah)[4],
   }
 }
 
-template <int BITS, int SD, int EPI, int NT, int MT = 4>
+// f16 form of k16 step s: the code words carry C + q as f16 with C = 1024
+// (magic mlo = 0x64006400: q in mantissa bits 0-7, step 1) or, for a 4-bit
+// code in bits 4-7 of its byte, C = 64 (magic mhi = 0x54005400: bits 4-7 step
+// 1/16, so the field's 16q reads q). 4-bit: one shift per word and step pair
+// (the low and high nibbles of a byte share it); 8-bit: the whole byte in one
+// f16 fragment, one mma per step instead of two.
+template <int BITS>
+MR_DEVICE void dq_step_h(uint32_t (&a)[4], const uint32_t (&wa)[QTraits<BITS>::kLaneWords],
+                         const uint32_t (&wb)[QTraits<BITS>::kLaneWords], int s, uint32_t mlo,
+                         uint32_t mhi) {
+  static_assert(BITS == 4 || BITS == 8, "f16 form: 4- and 8-bit codes");
+  if constexpr (BITS == 4) {
+    const int wi = s >> 1, sh = 8 * (s & 1);
+    const uint32_t u = wa[wi] >> sh, v = wb[wi] >> sh;
+    a[0] = and_or<0x000F000Fu>(u, mlo);
+    a[1] = and_or<0x000F000Fu>(v, mlo);
+    a[2] = and_or<0x00F000F0u>(u, mhi);
+    a[3] = and_or<0x00F000F0u>(v, mhi);
+  } else {
+    (void)mhi;
+    a[0] = and_or<0x00FF00FFu>(wa[s], mlo);
+    a[1] = and_or<0x00FF00FFu>(wb[s], mlo);
+    a[2] = and_or<0x00FF00FFu>(wa[s] >> 8, mlo);
+    a[3] = and_or<0x00FF00FFu>(wb[s] >> 8, mlo);
+  }
+}
+
+// D = A * B (f16 operands) with a zero accumulator.
+MR_DEVICE void mma_f16_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+template <int BITS, int SD, int EPI, int NT, int MT = 4, bool XH = false>
 __global__ void __launch_bounds__(kV2Threads, 1)
     gemv_v2_kernel(const GemvParams p, const __grid_constant__ TmaMaps maps, const int nst) {
   static_assert(EPI != EPI_SWIGLU || MT % 4 == 0, "SwiGLU items: whole 32-row h partials");
   pdl_wait_and_release();
-  using VS = V2Stage<BITS, SD, EPI, NT, MT>;
+  static_assert(!XH || (EPI == EPI_SWIGLU && (BITS == 4 || BITS == 8)),
+                "f16 form: gate/up at 4 and 8 bits");
+  using VS = V2Stage<BITS, SD, EPI, NT, MT, XH>;
   using ST = typename VS::W;
   using FX = V2Fixed<NT, MT>;
   constexpr int KS = FX::kKS;         // K parts of an item
@@ -545,16 +593,19 @@ __global__ void __launch_bounds__(kV2Threads, 1)
           lds2_scales<SD>(sb, sp + offSb + e);
           lds2_scales<SD>(zb, sp + offSb + ST::kSBytes + e);
         }
+        if constexpr (!XH) {
 #pragma unroll
-        for (int u2 = 0; u2 < 2; ++u2) {
-          za[u2] = fmaf(-kC, sa[u2], za[u2]);
-          zb[u2] = fmaf(-kC, sb[u2], zb[u2]);
+          for (int u2 = 0; u2 < 2; ++u2) {
+            za[u2] = fmaf(-kC, sa[u2], za[u2]);
+            zb[u2] = fmaf(-kC, sb[u2], zb[u2]);
+          }
         }
-        // group sums of this lane's accumulator columns for both groups
+        // group sums of this lane's accumulator columns for both groups (the
+        // f16 form reads its per-group terms in the group loop below)
         float X0[NT][2], X1[NT][2];
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-          if (t == 0 || t < ntiles) {
+          if (!XH && (t == 0 || t < ntiles)) {
             const char* s0 = sp + offX0 + t * 8 * VS::kSumColBytes + jp * XP * 4;
             if constexpr (XP == 1) {
               const float2 u = *reinterpret_cast<const float2*>(s0);
@@ -588,6 +639,21 @@ __global__ void __launch_bounds__(kV2Threads, 1)
           float acc[NT][4];
 #pragma unroll
           for (int s = 0; s < 4; ++s) {
+            if constexpr (XH) {
+              uint32_t a[4];
+              dq_step_h<BITS>(a, wa[u2], wb[u2], s, mlo, mhi);
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                if (t == 0 || t < ntiles) {
+                  if (s == 0)
+                    mma_f16_16816_z(acc[t], a[0], a[1], a[2], a[3], xb[t][0], xb[t][1]);
+                  else
+                    mma_f16_16816(acc[t], a[0], a[1], a[2], a[3], xb[t][2 * s],
+                                  xb[t][2 * s + 1]);
+                }
+              }
+              continue;
+            }
             uint32_t a[4], ah[4];
             dq_step<BITS>(a, ah, wa[u2], wb[u2], s, mlo, mhi);
 #pragma unroll
@@ -602,6 +668,24 @@ __global__ void __launch_bounds__(kV2Threads, 1)
                                  xb[t][2 * s + 1]);
               }
             }
+          }
+          if constexpr (XH) {
+            // sum(q * x) = 2^k * acc - W per column, then scale and bias
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              if (t == 0 || t < ntiles) {
+                const char* s0 = sp + offX0 + t * 8 * VS::kSumColBytes + j * XP * 4;
+                const float4 u = *reinterpret_cast<const float4*>(s0);
+                const float4 v = *reinterpret_cast<const float4*>(s0 + VS::kSumColBytes);
+                const float d0 = fmaf(u.x, acc[t][0], -u.y), d1 = fmaf(v.x, acc[t][1], -v.y);
+                const float d2 = fmaf(u.x, acc[t][2], -u.y), d3 = fmaf(v.x, acc[t][3], -v.y);
+                y[t][0] = fmaf(sa[u2], d0, fmaf(za[u2], u.z, y[t][0]));
+                y[t][1] = fmaf(sa[u2], d1, fmaf(za[u2], v.z, y[t][1]));
+                y[t][2] = fmaf(sb[u2], d2, fmaf(zb[u2], u.z, y[t][2]));
+                y[t][3] = fmaf(sb[u2], d3, fmaf(zb[u2], v.z, y[t][3]));
+              }
+            }
+            continue;
           }
 #pragma unroll
           for (int t = 0; t < NT; ++t) {

@@ -136,13 +136,13 @@ inline cudaError_t launch_tma_inst(const GemvParams& p, const TmaMaps& m, int gr
   return launch_pdl(kern, grid, kTmaThreads, smem, s, p, m, nst);
 }
 
-template <int BITS, int SD, int EPI, int NT, int MT>
+template <int BITS, int SD, int EPI, int NT, int MT, bool XH = false>
 inline cudaError_t launch_v2_inst(const GemvParams& p, const TmaMaps& m, int grid,
                                   cudaStream_t s) {
   static bool done[64] = {};  // one per instantiation
-  const int nst = v2_stages<BITS, SD, EPI, NT, MT>();
-  const int smem = v2_smem_bytes<BITS, SD, EPI, NT, MT>(nst);
-  auto kern = gemv_v2_kernel<BITS, SD, EPI, NT, MT>;
+  const int nst = v2_stages<BITS, SD, EPI, NT, MT, XH>();
+  const int smem = v2_smem_bytes<BITS, SD, EPI, NT, MT, XH>(nst);
+  auto kern = gemv_v2_kernel<BITS, SD, EPI, NT, MT, XH>;
   cudaError_t e = opt_in_smem(kern, smem, done);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, grid, kV2Threads, smem, s, p, m, nst);
@@ -273,6 +273,12 @@ inline cudaError_t launch_pf_epi(const GemvParams& p, const UmMaps& m, int epi, 
   template <int SD, int EPI, int MT>                                                           \
   static cudaError_t v2_mt_##BITS(const GemvParams& p, const TmaMaps& m, int nt, int grid,     \
                                   cudaStream_t s) {                                            \
+    if constexpr (EPI == EPI_SWIGLU && (BITS == 4 || BITS == 8)) {                             \
+      if (p.x_f16)                                                                             \
+        return nt == 1 ? launch_v2_inst<BITS, SD, EPI, 1, MT, true>(p, m, grid, s)             \
+                       : launch_v2_inst<BITS, SD, EPI, 2, MT, true>(p, m, grid, s);            \
+    }                                                                                          \
+    if (p.x_f16) return cudaErrorInvalidValue;                                                 \
     return nt == 1 ? launch_v2_inst<BITS, SD, EPI, 1, MT>(p, m, grid, s)                       \
                    : launch_v2_inst<BITS, SD, EPI, 2, MT>(p, m, grid, s);                      \
   }                                                                                            \

@@ -11,6 +11,17 @@ namespace mr {
 // ---------------------------------------------------------------- prep
 // xperm[t][i'] = x[t][src(i')] (halves of each B-block interleaved, B by
 // bits), xsum[t][g] = sum of the group's 64 bf16 values (fp32).
+//
+// f16 form (the staged gate/up GEMV at 4 and 8 bits, f16 = 1): per group of
+// 64, k = floor(log2(largest finite |x|)) - 14 (0 for a group without a
+// nonzero finite value; clamped to [-100, 100]), xperm holds f16(x' = x * 2^-k)
+// in the same order, exact for every element of at least 2^-24 times the
+// group's largest magnitude (bf16 carries 8 significant bits, f16 normals 11),
+// and xsum[t][g] = {2^k, W, X, 0}: X = sum of x, W = sum of C(i') * x with
+// C the constant the GEMV's f16 code words carry at position i': 1024 for
+// positions i' % 4 < 2 and 64 otherwise (4-bit: low and high nibble of a
+// byte), 1024 everywhere for 8-bit codes. The GEMV then folds
+// sum(q * x) = 2^k * acc - W, acc = sum((C + q) * x') from the f16 mma.
 struct PrepParams {
   const uint16_t* x;
   int64_t rows;
@@ -18,6 +29,7 @@ struct PrepParams {
   int bits;
   uint16_t* xperm;
   float* xsum;
+  int f16 = 0;
 };
 
 // Called by whole warps (the group sum is a 4-lane shuffle); lanes past the
@@ -46,6 +58,45 @@ MR_DEVICE void prep_chunk(const PrepParams& p, int64_t chunk, bool valid) {
     const int h = B >> 1;
     const int src_i = base + ((e2 & 1) ? (e2 >> 1) + h : (e2 >> 1));
     o[i] = e[src_i];
+  }
+  if (p.f16) {
+    // the group's largest finite magnitude (4 consecutive lanes)
+    float mx = 0.0f, w = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float v = bf16_bits_to_f32(o[i]);
+      if (fabsf(v) <= 3.4028235e38f) mx = fmaxf(mx, fabsf(v));  // finite
+      const float cst = (p.bits == 8 || (i & 3) < 2) ? 1024.0f : 64.0f;
+      w = fmaf(cst, v, w);
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    int k = 0;
+    if (mx > 0.0f) {
+      k = (int)((__float_as_uint(mx) >> 23) & 0xffu) - 127 - 14;  // 0 exponent field: clamped
+      k = k < -100 ? -100 : (k > 100 ? 100 : k);
+    }
+    const float inv = __uint_as_float((uint32_t)(127 - k) << 23);  // 2^-k, exact
+    uint16_t h[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      h[i] = __half_as_ushort(__float2half_rn(bf16_bits_to_f32(o[i]) * inv));
+    uint4 w0, w1;
+    memcpy(&w0, h, 16);
+    memcpy(&w1, h + 8, 16);
+    uint16_t* dst = p.xperm + r * p.in + c16 * 16;
+    if (valid) {
+      *reinterpret_cast<uint4*>(dst) = w0;
+      *reinterpret_cast<uint4*>(dst + 8) = w1;
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    w += __shfl_xor_sync(0xffffffffu, w, 1);
+    w += __shfl_xor_sync(0xffffffffu, w, 2);
+    if (valid && (c16 & 3) == 0)
+      *reinterpret_cast<float4*>(p.xsum + (r * (p.in / kGroup) + c16 / 4) * kPrepF16Floats) =
+          make_float4(__uint_as_float((uint32_t)(127 + k) << 23), w, s, 0.0f);
+    return;
   }
   uint4 w0, w1;
   memcpy(&w0, o, 16);
