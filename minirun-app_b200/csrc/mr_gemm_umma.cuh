@@ -5,9 +5,11 @@
 // per expert, Y[rows x tokens] = W[rows x K] . X[K x tokens]. One CTA per SM
 // loops over tiles (segment of <= 128 tokens sharing an expert) x (128
 // weight rows: 128 plain rows, or 64 gate + 64 up rows for SwiGLU):
-//   - warp 0, one lane: TMA loads, per stage (one 128-byte box column of codes
-//     = 4 groups at 4 bits, 2 at 8 bits), of the packed codes and, per group,
-//     the 128 x 64 bf16 activation tile (128-byte swizzle);
+//   - warp 0, one lane: TMA loads into two rings: per stage (one 128-byte
+//     box column = 4 groups at 4 bits, 2 at 8 bits) the packed codes into a
+//     3-slot code ring, and per two groups the 128 x 64 bf16 activation
+//     tiles (128-byte swizzle) into a deeper activation ring, so that several
+//     stages' activations are in flight while the tensor core works;
 //   - 8 worker warps (2 per TMEM lane quadrant, each half of a stage's
 //     groups): each thread owns one weight row = one TMEM lane and
 //     dequantises its row's codes to bf16 weights s*q + z (one rounding, as
@@ -39,6 +41,8 @@ constexpr int kPfWorkers = 8;
 constexpr int kPfThreads = (2 + kPfWorkers) * 32;
 constexpr int kPfChunk = 32;   // accumulator columns per epilogue step
 
+constexpr int kPfCodeSlots = 3;  // slots of the code ring
+
 template <int BITS, int SD, int EPI>
 struct PfStage {
   static_assert(BITS == 4 || BITS == 8, "prefill GEMM takes 4- or 8-bit codes");
@@ -46,33 +50,38 @@ struct PfStage {
   static constexpr int kBoxRows = kPfRows / kMats;
   static constexpr int kGroups = 16 / BITS;                 // groups per 128-byte box column
   static constexpr int kChunks = BITS / 2;                  // 16-byte chunks of a row's group
-  static constexpr int kCodeBytes = kPfRows * 128;
+  static constexpr int kCodeBytes = kPfRows * 128;          // one code-ring slot
   static constexpr int kBTile = kPfN * 128;                 // one group's activations
-  static constexpr int kBOff = kCodeBytes;
-  static constexpr int kBytes = kBOff + kGroups * kBTile;   // multiple of 1024
-  static constexpr uint32_t kTx = kCodeBytes + kGroups * kBTile;
+  static constexpr int kXG = 2;                             // groups per activation slot
+  static constexpr int kXBytes = kXG * kBTile;              // one activation-ring slot
+  static constexpr int kXPerStage = kGroups / kXG;
   static constexpr int kGpw = kGroups / 2;                  // groups per warp per stage
   static constexpr int kABuf = kGroups * 32;                // TMEM columns of a stage's A
   static constexpr int kDCol0 = 2 * kABuf;
   static constexpr int kTmemCols = 512;
   static_assert(kDCol0 + 2 * kPfN <= 512, "TMEM holds 512 columns");
-  static_assert(kBytes % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert(kCodeBytes % 1024 == 0 && kXBytes % 1024 == 0,
+                "ring slots keep 1024-byte alignment");
+  static_assert(kGroups % kXG == 0, "whole activation slots per stage");
 };
 
 struct PfFixed {
   static constexpr int kUpBytes = 2 * 64 * (kPfChunk + 1) * 4;  // up rows of one chunk, per half
-  static constexpr int kBarBytes = (2 * 16 + 4 * 2 + 1) * 8;
+  static constexpr int kBarBytes = (2 * 16 + 2 * kPfCodeSlots + 4 * 2 + 1) * 8;
   static constexpr int kBytes = kUpBytes + kBarBytes + 16 + 1024;
 };
 
+// Slots of the activation ring (the code ring has kPfCodeSlots).
 template <int BITS, int SD, int EPI>
 inline int pf_stages() {
-  const int n = (kSmemBudget - PfFixed::kBytes) / PfStage<BITS, SD, EPI>::kBytes;
-  return n > 8 ? 8 : n;
+  using ST = PfStage<BITS, SD, EPI>;
+  const int n = (kSmemBudget - PfFixed::kBytes - kPfCodeSlots * ST::kCodeBytes) / ST::kXBytes;
+  return n > 16 ? 16 : n;
 }
 template <int BITS, int SD, int EPI>
 inline int pf_smem_bytes(int nst) {
-  return PfFixed::kBytes + nst * PfStage<BITS, SD, EPI>::kBytes;
+  using ST = PfStage<BITS, SD, EPI>;
+  return PfFixed::kBytes + kPfCodeSlots * ST::kCodeBytes + nst * ST::kXBytes;
 }
 
 // bf16 pair a - b, a*b + c (round to nearest even).
@@ -131,10 +140,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   using ST = PfStage<BITS, SD, EPI>;
   extern __shared__ char smem_raw[];
   char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* upx = reinterpret_cast<float*>(smem + nst * ST::kBytes);  // [2 halves][64][33]
-  uint64_t* full = reinterpret_cast<uint64_t*>(upx + 2 * 64 * (kPfChunk + 1));
-  uint64_t* empty = full + nst;
-  uint64_t* afull = empty + nst;  // [2] a stage's A written (8 workers)
+  // code ring (kPfCodeSlots x kCodeBytes), activation ring (nst x kXBytes)
+  char* xring = smem + kPfCodeSlots * ST::kCodeBytes;
+  float* upx = reinterpret_cast<float*>(xring + nst * ST::kXBytes);  // [2 halves][64][33]
+  uint64_t* full = reinterpret_cast<uint64_t*>(upx + 2 * 64 * (kPfChunk + 1));  // [nst] activations
+  uint64_t* empty = full + nst;   // [nst] activation slot read by the MMAs (commit)
+  uint64_t* cfull = empty + nst;  // [kPfCodeSlots] a stage's codes landed
+  uint64_t* cempty = cfull + kPfCodeSlots;  // [kPfCodeSlots] codes read (8 workers)
+  uint64_t* afull = cempty + kPfCodeSlots;  // [2] a stage's A written (8 workers)
   uint64_t* aempty = afull + 2;   // [2] a stage's A read by the MMAs (commit)
   uint64_t* dfull = aempty + 2;   // [2] a tile's accumulator complete (commit)
   uint64_t* dempty = dfull + 2;   // [2] a tile's accumulator read out (8 workers)
@@ -152,7 +165,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < nst; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(empty + s, kPfWorkers + 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int s = 0; s < kPfCodeSlots; ++s) {
+      mbar_init(cfull + s, 1);
+      mbar_init(cempty + s, kPfWorkers);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(afull + b, kPfWorkers);
@@ -176,7 +193,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      uint32_t it = 0, slot = 0, phase = 0;
+      uint32_t it = 0, slot = 0, phase = 0;  // activation ring (it: slots issued)
+      uint32_t cit = 0, cslot = 0, cphase = 0;  // code ring
       for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         const ItemInfo info = decode_item(p, n_routed, item);
         const CUtensorMap *mp0, *mp1, *ma;
@@ -194,27 +212,44 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           ma = &maps.act_sh;
           ya = p.sh_row0 + info.col0;
         }
-        for (int st = 0; st < nstages; ++st, ++it) {
-          wait_bounded(empty + slot, phase ^ 1u, flags, p.error);
-          char* S = smem + slot * ST::kBytes;
-          mbar_arrive_expect_tx(full + slot, ST::kTx);
-          tma_load_2d(S, mp0, st * 32, y0, full + slot);
-          if constexpr (ST::kMats == 2) tma_load_2d(S + ST::kBoxRows * 128, mp1, st * 32, y0, full + slot);
+        for (int st = 0; st < nstages; ++st) {
+          // the stage's codes
+          wait_bounded(cempty + cslot, cphase ^ 1u, flags, p.error);
+          char* C = smem + cslot * ST::kCodeBytes;
+          mbar_arrive_expect_tx(cfull + cslot, ST::kCodeBytes);
+          tma_load_2d(C, mp0, st * 32, y0, cfull + cslot);
+          if constexpr (ST::kMats == 2)
+            tma_load_2d(C + ST::kBoxRows * 128, mp1, st * 32, y0, cfull + cslot);
+          ++cit;
+          if (++cslot == (uint32_t)kPfCodeSlots) {
+            cslot = 0;
+            cphase ^= 1u;
+          }
+          // its activation tiles, kXG groups per slot
 #pragma unroll
-          for (int g = 0; g < ST::kGroups; ++g)
-            tma_load_2d(S + ST::kBOff + g * ST::kBTile, ma, (st * ST::kGroups + g) * kGroup, ya,
-                        full + slot);
-          if (++slot == (uint32_t)nst) {
-            slot = 0;
-            phase ^= 1u;
+          for (int xs = 0; xs < ST::kXPerStage; ++xs, ++it) {
+            wait_bounded(empty + slot, phase ^ 1u, flags, p.error);
+            char* X = xring + slot * ST::kXBytes;
+            mbar_arrive_expect_tx(full + slot, ST::kXBytes);
+#pragma unroll
+            for (int g = 0; g < ST::kXG; ++g)
+              tma_load_2d(X + g * ST::kBTile, ma,
+                          (st * ST::kGroups + xs * ST::kXG + g) * kGroup, ya, full + slot);
+            if (++slot == (uint32_t)nst) {
+              slot = 0;
+              phase ^= 1u;
+            }
           }
         }
       }
       if (flags[0]) {
-        const uint32_t issued = it;
-        for (uint32_t j = (issued > (uint32_t)nst ? issued - nst : 0); j < issued; ++j)
+        // after an abort, let the copies in flight land before exiting
+        for (uint32_t j = (it > (uint32_t)nst ? it - nst : 0); j < it; ++j)
           for (uint32_t i = 0; i < kSpinLimit; ++i)
             if (mbar_try_wait(full + (j % nst), (j / nst) & 1u)) break;
+        for (uint32_t j = (cit > (uint32_t)kPfCodeSlots ? cit - kPfCodeSlots : 0); j < cit; ++j)
+          for (uint32_t i = 0; i < kSpinLimit; ++i)
+            if (mbar_try_wait(cfull + (j % kPfCodeSlots), (j / kPfCodeSlots) & 1u)) break;
       }
     }
   } else if (warp == 1) {
@@ -228,24 +263,28 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint32_t d_t = tbase + ST::kDCol0 + db * kPfN;
         for (int st = 0; st < nstages; ++st, ++j) {
           const uint32_t ab = j & 1u;
-          wait_bounded(full + slot, phase, flags, p.error);
           wait_bounded(afull + ab, (j >> 1) & 1u, flags, p.error);
-          tc_fence_after();
-          const uint32_t bt = smem_u32(smem + slot * ST::kBytes + ST::kBOff);
 #pragma unroll
-          for (int g = 0; g < ST::kGroups; ++g) {
-            const uint32_t a_t = tbase + ab * ST::kABuf + g * 32;
+          for (int xs = 0; xs < ST::kXPerStage; ++xs) {
+            wait_bounded(full + slot, phase, flags, p.error);
+            tc_fence_after();
+            const uint32_t bt = smem_u32(xring + slot * ST::kXBytes);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              tc_mma_ts(d_t, a_t + kk * 8, umma_desc_sw128(bt + g * ST::kBTile + kk * 32), idesc,
-                        (st | g | kk) ? 1u : 0u);
+            for (int gg = 0; gg < ST::kXG; ++gg) {
+              const int g = xs * ST::kXG + gg;  // stage-local group
+              const uint32_t a_t = tbase + ab * ST::kABuf + g * 32;
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                tc_mma_ts(d_t, a_t + kk * 8, umma_desc_sw128(bt + gg * ST::kBTile + kk * 32),
+                          idesc, (st | g | kk) ? 1u : 0u);
+            }
+            tc_commit(empty + slot);  // these activation tiles are read
+            if (++slot == (uint32_t)nst) {
+              slot = 0;
+              phase ^= 1u;
+            }
           }
-          tc_commit(aempty + ab);     // the A buffer may be rewritten
-          tc_commit(empty + slot);    // the stage's activation tiles are read
-          if (++slot == (uint32_t)nst) {
-            slot = 0;
-            phase ^= 1u;
-          }
+          tc_commit(aempty + ab);  // the A buffer may be rewritten
         }
         tc_commit(dfull + db);  // the tile's accumulator is complete
       }
@@ -261,7 +300,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const uint32_t sbase = smem_u32(smem);
     const uint32_t rowoff = (uint32_t)row * 128;
     const uint32_t rsw = (uint32_t)(row & 7);
-    uint32_t slot = 0, phase = 0, stg = sbase, j = 0, t = 0;
+    uint32_t slot = 0, phase = 0, stg = sbase, j = 0, t = 0;  // code ring
     float* up = upx + half * 64 * (kPfChunk + 1);
 
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++t) {
@@ -296,7 +335,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           z2[i] = scale_pair<SD>(scale_to_f32<SD>(zr[i]));
         }
         if (st + 1 < nstages) load_scales(st + 1);
-        warp_wait_sleep(full + slot, phase, flags, p.error);
+        warp_wait_sleep(cfull + slot, phase, flags, p.error);
         // the A buffer was last read by the MMAs of stage j-2
         if (j >= 2) warp_wait_sleep(aempty + ab, ((j >> 1) & 1u) ^ 1u, flags, p.error);
         tc_fence_after();
@@ -323,14 +362,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(afull + ab);
-          mbar_arrive(empty + slot);  // this warp's codes are read
+          mbar_arrive(cempty + slot);  // this warp's codes are read
         }
-        if (++slot == (uint32_t)nst) {
+        if (++slot == (uint32_t)kPfCodeSlots) {
           slot = 0;
           phase ^= 1u;
           stg = sbase;
         } else {
-          stg += ST::kBytes;
+          stg += ST::kCodeBytes;
         }
       }
 

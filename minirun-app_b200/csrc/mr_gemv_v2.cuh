@@ -652,20 +652,21 @@ __global__ void __launch_bounds__(kV2Threads, 1)
                                   xb[t][2 * s + 1]);
                 }
               }
-              continue;
-            }
-            uint32_t a[4], ah[4];
-            dq_step<BITS>(a, ah, wa[u2], wb[u2], s, mlo, mhi);
+            } else {
+              uint32_t a[4], ah[4];
+              dq_step<BITS>(a, ah, wa[u2], wb[u2], s, mlo, mhi);
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              if (t == 0 || t < ntiles) {
-                if (s == 0)
-                  mma_bf16_16816_z(acc[t], a[0], a[1], a[2], a[3], xb[t][0], xb[t][1]);
-                else
-                  mma_bf16_16816(acc[t], a[0], a[1], a[2], a[3], xb[t][2 * s], xb[t][2 * s + 1]);
-                if constexpr (BITS == 8)
-                  mma_bf16_16816(acc[t], ah[0], ah[1], ah[2], ah[3], xb[t][2 * s],
-                                 xb[t][2 * s + 1]);
+              for (int t = 0; t < NT; ++t) {
+                if (t == 0 || t < ntiles) {
+                  if (s == 0)
+                    mma_bf16_16816_z(acc[t], a[0], a[1], a[2], a[3], xb[t][0], xb[t][1]);
+                  else
+                    mma_bf16_16816(acc[t], a[0], a[1], a[2], a[3], xb[t][2 * s],
+                                   xb[t][2 * s + 1]);
+                  if constexpr (BITS == 8)
+                    mma_bf16_16816(acc[t], ah[0], ah[1], ah[2], ah[3], xb[t][2 * s],
+                                   xb[t][2 * s + 1]);
+                }
               }
             }
           }
@@ -685,15 +686,15 @@ __global__ void __launch_bounds__(kV2Threads, 1)
                 y[t][3] = fmaf(sb[u2], d3, fmaf(zb[u2], v.z, y[t][3]));
               }
             }
-            continue;
-          }
+          } else {
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            if (t == 0 || t < ntiles) {
-              y[t][0] = fmaf(sa[u2], acc[t][0], fmaf(za[u2], X0[t][u2], y[t][0]));
-              y[t][1] = fmaf(sa[u2], acc[t][1], fmaf(za[u2], X1[t][u2], y[t][1]));
-              y[t][2] = fmaf(sb[u2], acc[t][2], fmaf(zb[u2], X0[t][u2], y[t][2]));
-              y[t][3] = fmaf(sb[u2], acc[t][3], fmaf(zb[u2], X1[t][u2], y[t][3]));
+            for (int t = 0; t < NT; ++t) {
+              if (t == 0 || t < ntiles) {
+                y[t][0] = fmaf(sa[u2], acc[t][0], fmaf(za[u2], X0[t][u2], y[t][0]));
+                y[t][1] = fmaf(sa[u2], acc[t][1], fmaf(za[u2], X1[t][u2], y[t][1]));
+                y[t][2] = fmaf(sb[u2], acc[t][2], fmaf(zb[u2], X0[t][u2], y[t][2]));
+                y[t][3] = fmaf(sb[u2], acc[t][3], fmaf(zb[u2], X1[t][u2], y[t][3]));
+              }
             }
           }
         }
