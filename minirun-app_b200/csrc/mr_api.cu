@@ -172,26 +172,47 @@ __global__ void combine_kernel(const float* __restrict__ part, const float* __re
                                int T, int k, int64_t H, int weight_after_down, int has_shared,
                                uint16_t* __restrict__ out) {
   pdl_wait_and_release();
-  const int64_t n = (int64_t)T * H;
+  // four consecutive rows per thread (H is a multiple of the group size, 64):
+  // 16-byte partial loads
+  const int64_t H4 = H / 4;
+  const int64_t n = (int64_t)T * H4;
   const int Tk = T * k;
+  const float4* p4 = reinterpret_cast<const float4*>(part);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int t = (int)(i / H);
-    const int64_t row = i - (int64_t)t * H;
-    float s = 0.0f;
+    const int t = (int)(i / H4);
+    const int64_t q = i - (int64_t)t * H4;
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int j = 0; j < k; ++j) {
+      const float4 v = __ldg(p4 + (int64_t)(t * k + j) * H4 + q);
+      if (!weight_after_down) {
+        s[0] += v.x; s[1] += v.y; s[2] += v.z; s[3] += v.w;
+      } else {
+        const float w = __ldg(weights + t * k + j);
+        s[0] += v.x * w; s[1] += v.y * w; s[2] += v.z * w; s[3] += v.w * w;
+      }
+    }
     if (!weight_after_down) {
-      for (int j = 0; j < k; ++j) s += __ldg(part + (int64_t)(t * k + j) * H + row);
-      s = bf16_round(s);
-    } else {
-      for (int j = 0; j < k; ++j)
-        s += __ldg(part + (int64_t)(t * k + j) * H + row) * __ldg(weights + t * k + j);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[e] = bf16_round(s[e]);
     }
     if (has_shared) {
-      const float hi = __ldg(part + (int64_t)(Tk + t) * H + row);
-      const float lo = __ldg(part + (int64_t)(Tk + T + t) * H + row);
-      s = s + (hi + lo);
+      const float4 hi = __ldg(p4 + (int64_t)(Tk + t) * H4 + q);
+      const float4 lo = __ldg(p4 + (int64_t)(Tk + T + t) * H4 + q);
+      s[0] = s[0] + (hi.x + lo.x);
+      s[1] = s[1] + (hi.y + lo.y);
+      s[2] = s[2] + (hi.z + lo.z);
+      s[3] = s[3] + (hi.w + lo.w);
     }
-    out[i] = f32_to_bf16_bits(s);
+    if ((reinterpret_cast<uintptr_t>(out) & 7u) == 0) {
+      uint2 o;
+      o.x = (uint32_t)f32_to_bf16_bits(s[0]) | ((uint32_t)f32_to_bf16_bits(s[1]) << 16);
+      o.y = (uint32_t)f32_to_bf16_bits(s[2]) | ((uint32_t)f32_to_bf16_bits(s[3]) << 16);
+      reinterpret_cast<uint2*>(out)[i] = o;
+    } else {  // a caller's output that is only 2-byte aligned
+#pragma unroll
+      for (int e = 0; e < 4; ++e) out[4 * i + e] = f32_to_bf16_bits(s[e]);
+    }
   }
 }
 
@@ -1640,7 +1661,7 @@ static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   r.um1 = &um1;
   r.um2 = &um2;
   if ((st = run_experts(ctx, L, r, s))) return st;
-  const int64_t n_out = T * H;
+  const int64_t n_out = T * H / 4;
   const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 4 * ctx->sm_count));
   ProfScope pc(ctx, MR_KERNEL_COMBINE, s);
   return cuda_check(ctx,
@@ -3587,7 +3608,7 @@ mr_status mr_moe_layer_forward_cached(mr_ctx* ctx, mr_cache* c, int32_t layer_id
   r.hsum = hsum;
   r.part2 = part2;
   if ((st = run_experts(ctx, &Lt, r, s))) return st;
-  const int64_t n_out = T * H;
+  const int64_t n_out = T * H / 4;
   const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n_out + 255) / 256, 4 * ctx->sm_count));
   if ((st = cuda_check(ctx,
                        launch_pdl(combine_kernel, cgrid, 256, 0, s, (const float*)part2,

@@ -21,8 +21,10 @@
 //  - Columns. A segment holds up to NT mma tiles of 8 columns. Each A
 //    fragment (16 rows x 16 codes) is dequantised once and fed to all NT
 //    tiles, so an expert with 9-16 columns costs one dequantisation.
-//  - Rows. The 16 consumer warps split an item MT row tiles x 16/MT K parts;
-//    at MT = 16 (256-row down items, 128 + 128-row gate/up items) every warp
+//  - Rows. An item is MT row tiles x 16/MT K parts; each of the 16/RT
+//    consumer warps takes RT row tiles of one K part (RT = 2: 8 consumer
+//    warps, two tiles' code fragments per load of the activations). At
+//    MT = 16 (256-row down items, 128 + 128-row gate/up items) every warp
 //    owns its rows over the whole K and an item needs no reduction.
 //  - Loop. One path for every segment width (no single-column FMA path), the
 //    first mma of each group takes a zero accumulator, and per-stage scale
@@ -120,10 +122,23 @@ MR_DEVICE void lds2_scales(float (&v)[2], const char* p) {
 #define MR_V2_PRODUCERS 4
 #endif
 constexpr int kV2Producers = MR_V2_PRODUCERS;
-constexpr int kV2Threads = kTmaConsumers + 32 * kV2Producers;
+// Row tiles per consumer warp: RT = 2 halves the consumer warps (8); each
+// holds two tiles' fragments against one load of the activations and sums,
+// with the registers of 12 warps per CTA (up to 168 per thread) instead of 20
+// (96, with spills). Measured on config 1, T = 64: gate/up 0.716 -> 0.672 ms,
+// down 0.371 -> 0.358 ms against RT = 1.
+#ifndef MR_V2_RT
+#define MR_V2_RT 2
+#endif
+constexpr int kV2RT = MR_V2_RT;
+__host__ __device__ constexpr int v2_consumer_warps(int rt) { return kTmaConsumerWarps / rt; }
+__host__ __device__ constexpr int v2_threads(int rt) {
+  return 32 * (v2_consumer_warps(rt) + kV2Producers);
+}
+constexpr int kV2Threads = v2_threads(1);
 
-// Row tiles (16 rows each) per work item of the down (PARTIAL) launch. The 16
-// consumer warps split an item MT row tiles x (16 / MT) K parts: MT = 16 gives
+// Row tiles (16 rows each) per work item of the down (PARTIAL) launch. An
+// item splits into MT row tiles x (16 / MT) K parts: MT = 16 gives
 // every warp its own rows over the whole K (256-row items, no K reduction
 // and no CTA-wide barrier per item); SwiGLU and store items keep MT = 4.
 // Measured on config 1 (T = 64), down launch: 0.626 ms (MT 4), 0.527 (8),
@@ -318,8 +333,8 @@ MR_DEVICE void mma_f16_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
-template <int BITS, int SD, int EPI, int NT, int MT = 4, bool XH = false>
-__global__ void __launch_bounds__(kV2Threads, 1)
+template <int BITS, int SD, int EPI, int NT, int MT = 4, bool XH = false, int RT = 1>
+__global__ void __launch_bounds__(v2_threads(RT), 1)
     gemv_v2_kernel(const GemvParams p, const __grid_constant__ TmaMaps maps, const int nst) {
   static_assert(EPI != EPI_SWIGLU || MT % 4 == 0, "SwiGLU items: whole 32-row h partials");
   pdl_wait_and_release();
@@ -331,6 +346,9 @@ __global__ void __launch_bounds__(kV2Threads, 1)
   constexpr int KS = FX::kKS;         // K parts of an item
   constexpr int kGpw = kTmaGps / KS;  // groups per consumer warp and stage
   static_assert(KS * MT == kTmaConsumerWarps && kGpw % 2 == 0, "warp split");
+  static_assert(MT % RT == 0, "whole row tiles per warp");
+  constexpr int kCW = v2_consumer_warps(RT);  // consumer warps
+  constexpr int kCT = kCW * 32;               // consumer threads
   constexpr int LW = QTraits<BITS>::kLaneWords;
   constexpr float kC = QTraits<BITS>::kMagic;
   constexpr int XP = VS::kXP;
@@ -354,7 +372,7 @@ __global__ void __launch_bounds__(kV2Threads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < nst; ++s) {
       mbar_init(full + s, 1 + 32);  // the TMA byte count + the 32 copier lanes
-      mbar_init(empty + s, kTmaConsumerWarps);
+      mbar_init(empty + s, kCW);
     }
     flags[0] = 0;  // abort
     fence_mbar_init();
@@ -365,7 +383,7 @@ __global__ void __launch_bounds__(kV2Threads, 1)
     return v < p.Tk ? (int64_t)(v / p.in_div) : (int64_t)(v - p.shared_in_off);
   };
 
-  if (warp >= kTmaConsumerWarps) {
+  if (warp >= kCW) {
     // ----------------------------------------------------------- producers
     // producer pw issues global stages it = pw, pw + P, ... of this CTA's
     // sequence (items in order, nstages each); stage it uses ring slot
@@ -376,7 +394,7 @@ __global__ void __launch_bounds__(kV2Threads, 1)
     // producer's own previous wait (stage it - np - nst) gives that when
     // np <= nst, so at most nst producer warps take stages.
     const int np = nst < kV2Producers ? nst : kV2Producers;
-    const int pw = warp - kTmaConsumerWarps;
+    const int pw = warp - kCW;
     if (pw >= np) return;
     uint32_t it = 0;
     const uint64_t wpol = l2_evict_first_policy();
@@ -457,19 +475,24 @@ __global__ void __launch_bounds__(kV2Threads, 1)
   // -------------------------------------------------------------- consumers
   const int r8 = lane >> 2;
   const int c = lane & 3;
-  const int mt = warp % MT;
-  const int kq = warp / MT;  // K part: groups [kq * kGpw, (kq + 1) * kGpw) of a stage
+  constexpr int kMW = MT / RT;  // consumer warps per K part
+  const int mt0 = (warp % kMW) * RT;  // this warp's row tiles: mt0 .. mt0 + RT - 1
+  const int kq = warp / kMW;  // K part: groups [kq * kGpw, (kq + 1) * kGpw) of a stage
   const int ctid = threadIdx.x;
   const int rr = v2_frag_row<BITS>(r8);  // this lane's rows: rr (+ 8)
+  // tile r of the warp sits kTileRows rows (codes, scales) after tile 0
+  constexpr int kTileRows = EPI == EPI_SWIGLU ? 8 : 16;
+  constexpr int kTileCodeBytes = kTileRows * 128;
+  constexpr int kTileScaleBytes = kTileRows * kTmaGps * ST::kEsz;
   int ma, ra, mb, rbr;
   if constexpr (EPI == EPI_SWIGLU) {
     ma = 0;
-    ra = mt * 8 + rr;
+    ra = mt0 * 8 + rr;
     mb = 1;
-    rbr = mt * 8 + rr;
+    rbr = mt0 * 8 + rr;
   } else {
     ma = 0;
-    ra = mt * 16 + rr;
+    ra = mt0 * 16 + rr;
     mb = 0;
     rbr = ra + 8;
   }
@@ -536,9 +559,11 @@ __global__ void __launch_bounds__(kV2Threads, 1)
     const bool shared = info.shared;
     const int ncols = info.ncols;
     const int ntiles = (ncols + 7) >> 3;
-    float y[NT][4];
+    float y[RT][NT][4];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) y[t][0] = y[t][1] = y[t][2] = y[t][3] = 0.0f;
+    for (int r = 0; r < RT; ++r)
+#pragma unroll
+      for (int t = 0; t < NT; ++t) y[r][t][0] = y[r][t][1] = y[r][t][2] = y[r][t][3] = 0.0f;
 
     for (int st = 0; st < nstages; ++st) {
       if (st == 1 && has_next) fetch_cols(nxt);
@@ -565,39 +590,42 @@ __global__ void __launch_bounds__(kV2Threads, 1)
       const char* sp = smem + slot * VS::kBytes;
 #pragma unroll
       for (int jp = 0; jp < kGpw; jp += 2) {
-        uint32_t wa[2][LW], wb[2][LW];
+        uint32_t wa[RT][2][LW], wb[RT][2][LW];
 #pragma unroll
-        for (int u2 = 0; u2 < 2; ++u2) {
-          const int j = jp + u2;
-          const char* pa = sp + off_a(j);
-          if constexpr (LW == 1) {
-            wa[u2][0] = *reinterpret_cast<const uint32_t*>(pa);
-            wb[u2][0] = *reinterpret_cast<const uint32_t*>(pa + dB);
-          } else if constexpr (LW == 2) {
-            const uint2 u = *reinterpret_cast<const uint2*>(pa);
-            const uint2 v = *reinterpret_cast<const uint2*>(pa + dB);
-            wa[u2][0] = u.x; wa[u2][1] = u.y;
-            wb[u2][0] = v.x; wb[u2][1] = v.y;
-          } else {
-            const uint4 u = *reinterpret_cast<const uint4*>(pa);
-            const uint4 v = *reinterpret_cast<const uint4*>(pa + dB);
-            wa[u2][0] = u.x; wa[u2][1] = u.y; wa[u2][2] = u.z; wa[u2][3] = u.w;
-            wb[u2][0] = v.x; wb[u2][1] = v.y; wb[u2][2] = v.z; wb[u2][3] = v.w;
-          }
-        }
-        float sa[2], za[2], sb[2], zb[2];
-        {
-          const int e = jp * ST::kEsz;
-          lds2_scales<SD>(sa, sp + offSa + e);
-          lds2_scales<SD>(za, sp + offSa + ST::kSBytes + e);
-          lds2_scales<SD>(sb, sp + offSb + e);
-          lds2_scales<SD>(zb, sp + offSb + ST::kSBytes + e);
-        }
-        if constexpr (!XH) {
+        for (int r = 0; r < RT; ++r)
 #pragma unroll
           for (int u2 = 0; u2 < 2; ++u2) {
-            za[u2] = fmaf(-kC, sa[u2], za[u2]);
-            zb[u2] = fmaf(-kC, sb[u2], zb[u2]);
+            const int j = jp + u2;
+            const char* pa = sp + off_a(j) + r * kTileCodeBytes;
+            if constexpr (LW == 1) {
+              wa[r][u2][0] = *reinterpret_cast<const uint32_t*>(pa);
+              wb[r][u2][0] = *reinterpret_cast<const uint32_t*>(pa + dB);
+            } else if constexpr (LW == 2) {
+              const uint2 u = *reinterpret_cast<const uint2*>(pa);
+              const uint2 v = *reinterpret_cast<const uint2*>(pa + dB);
+              wa[r][u2][0] = u.x; wa[r][u2][1] = u.y;
+              wb[r][u2][0] = v.x; wb[r][u2][1] = v.y;
+            } else {
+              const uint4 u = *reinterpret_cast<const uint4*>(pa);
+              const uint4 v = *reinterpret_cast<const uint4*>(pa + dB);
+              wa[r][u2][0] = u.x; wa[r][u2][1] = u.y; wa[r][u2][2] = u.z; wa[r][u2][3] = u.w;
+              wb[r][u2][0] = v.x; wb[r][u2][1] = v.y; wb[r][u2][2] = v.z; wb[r][u2][3] = v.w;
+            }
+          }
+        float sa[RT][2], za[RT][2], sb[RT][2], zb[RT][2];
+#pragma unroll
+        for (int r = 0; r < RT; ++r) {
+          const int e = jp * ST::kEsz + r * kTileScaleBytes;
+          lds2_scales<SD>(sa[r], sp + offSa + e);
+          lds2_scales<SD>(za[r], sp + offSa + ST::kSBytes + e);
+          lds2_scales<SD>(sb[r], sp + offSb + e);
+          lds2_scales<SD>(zb[r], sp + offSb + ST::kSBytes + e);
+          if constexpr (!XH) {
+#pragma unroll
+            for (int u2 = 0; u2 < 2; ++u2) {
+              za[r][u2] = fmaf(-kC, sa[r][u2], za[r][u2]);
+              zb[r][u2] = fmaf(-kC, sb[r][u2], zb[r][u2]);
+            }
           }
         }
         // group sums of this lane's accumulator columns for both groups (the
@@ -636,36 +664,41 @@ __global__ void __launch_bounds__(kV2Threads, 1)
               xb[t][4] = v1.x; xb[t][5] = v1.y; xb[t][6] = v1.z; xb[t][7] = v1.w;
             }
           }
-          float acc[NT][4];
+          float acc[RT][NT][4];
 #pragma unroll
           for (int s = 0; s < 4; ++s) {
-            if constexpr (XH) {
-              uint32_t a[4];
-              dq_step_h<BITS>(a, wa[u2], wb[u2], s, mlo, mhi);
+            const bool first = s == 0;
 #pragma unroll
-              for (int t = 0; t < NT; ++t) {
-                if (t == 0 || t < ntiles) {
-                  if (s == 0)
-                    mma_f16_16816_z(acc[t], a[0], a[1], a[2], a[3], xb[t][0], xb[t][1]);
-                  else
-                    mma_f16_16816(acc[t], a[0], a[1], a[2], a[3], xb[t][2 * s],
-                                  xb[t][2 * s + 1]);
+            for (int r = 0; r < RT; ++r) {
+              if constexpr (XH) {
+                uint32_t a[4];
+                dq_step_h<BITS>(a, wa[r][u2], wb[r][u2], s, mlo, mhi);
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                  if (t == 0 || t < ntiles) {
+                    float(&d)[4] = acc[r][t];
+                    if (first)
+                      mma_f16_16816_z(d, a[0], a[1], a[2], a[3], xb[t][2 * s], xb[t][2 * s + 1]);
+                    else
+                      mma_f16_16816(d, a[0], a[1], a[2], a[3], xb[t][2 * s], xb[t][2 * s + 1]);
+                  }
                 }
-              }
-            } else {
-              uint32_t a[4], ah[4];
-              dq_step<BITS>(a, ah, wa[u2], wb[u2], s, mlo, mhi);
+              } else {
+                uint32_t a[4], ah[4];
+                dq_step<BITS>(a, ah, wa[r][u2], wb[r][u2], s, mlo, mhi);
 #pragma unroll
-              for (int t = 0; t < NT; ++t) {
-                if (t == 0 || t < ntiles) {
-                  if (s == 0)
-                    mma_bf16_16816_z(acc[t], a[0], a[1], a[2], a[3], xb[t][0], xb[t][1]);
-                  else
-                    mma_bf16_16816(acc[t], a[0], a[1], a[2], a[3], xb[t][2 * s],
-                                   xb[t][2 * s + 1]);
-                  if constexpr (BITS == 8)
-                    mma_bf16_16816(acc[t], ah[0], ah[1], ah[2], ah[3], xb[t][2 * s],
-                                   xb[t][2 * s + 1]);
+                for (int t = 0; t < NT; ++t) {
+                  if (t == 0 || t < ntiles) {
+                    float(&d)[4] = acc[r][t];
+                    if (first)
+                      mma_bf16_16816_z(d, a[0], a[1], a[2], a[3], xb[t][2 * s],
+                                       xb[t][2 * s + 1]);
+                    else
+                      mma_bf16_16816(d, a[0], a[1], a[2], a[3], xb[t][2 * s], xb[t][2 * s + 1]);
+                    if constexpr (BITS == 8)
+                      mma_bf16_16816(d, ah[0], ah[1], ah[2], ah[3], xb[t][2 * s],
+                                     xb[t][2 * s + 1]);
+                  }
                 }
               }
             }
@@ -678,24 +711,31 @@ __global__ void __launch_bounds__(kV2Threads, 1)
                 const char* s0 = sp + offX0 + t * 8 * VS::kSumColBytes + j * XP * 4;
                 const float4 u = *reinterpret_cast<const float4*>(s0);
                 const float4 v = *reinterpret_cast<const float4*>(s0 + VS::kSumColBytes);
-                const float d0 = fmaf(u.x, acc[t][0], -u.y), d1 = fmaf(v.x, acc[t][1], -v.y);
-                const float d2 = fmaf(u.x, acc[t][2], -u.y), d3 = fmaf(v.x, acc[t][3], -v.y);
-                y[t][0] = fmaf(sa[u2], d0, fmaf(za[u2], u.z, y[t][0]));
-                y[t][1] = fmaf(sa[u2], d1, fmaf(za[u2], v.z, y[t][1]));
-                y[t][2] = fmaf(sb[u2], d2, fmaf(zb[u2], u.z, y[t][2]));
-                y[t][3] = fmaf(sb[u2], d3, fmaf(zb[u2], v.z, y[t][3]));
+#pragma unroll
+                for (int r = 0; r < RT; ++r) {
+                  const float d0 = fmaf(u.x, acc[r][t][0], -u.y);
+                  const float d1 = fmaf(v.x, acc[r][t][1], -v.y);
+                  const float d2 = fmaf(u.x, acc[r][t][2], -u.y);
+                  const float d3 = fmaf(v.x, acc[r][t][3], -v.y);
+                  y[r][t][0] = fmaf(sa[r][u2], d0, fmaf(za[r][u2], u.z, y[r][t][0]));
+                  y[r][t][1] = fmaf(sa[r][u2], d1, fmaf(za[r][u2], v.z, y[r][t][1]));
+                  y[r][t][2] = fmaf(sb[r][u2], d2, fmaf(zb[r][u2], u.z, y[r][t][2]));
+                  y[r][t][3] = fmaf(sb[r][u2], d3, fmaf(zb[r][u2], v.z, y[r][t][3]));
+                }
               }
             }
           } else {
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              if (t == 0 || t < ntiles) {
-                y[t][0] = fmaf(sa[u2], acc[t][0], fmaf(za[u2], X0[t][u2], y[t][0]));
-                y[t][1] = fmaf(sa[u2], acc[t][1], fmaf(za[u2], X1[t][u2], y[t][1]));
-                y[t][2] = fmaf(sb[u2], acc[t][2], fmaf(zb[u2], X0[t][u2], y[t][2]));
-                y[t][3] = fmaf(sb[u2], acc[t][3], fmaf(zb[u2], X1[t][u2], y[t][3]));
+            for (int r = 0; r < RT; ++r)
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                if (t == 0 || t < ntiles) {
+                  y[r][t][0] = fmaf(sa[r][u2], acc[r][t][0], fmaf(za[r][u2], X0[t][u2], y[r][t][0]));
+                  y[r][t][1] = fmaf(sa[r][u2], acc[r][t][1], fmaf(za[r][u2], X1[t][u2], y[r][t][1]));
+                  y[r][t][2] = fmaf(sb[r][u2], acc[r][t][2], fmaf(zb[r][u2], X0[t][u2], y[r][t][2]));
+                  y[r][t][3] = fmaf(sb[r][u2], acc[r][t][3], fmaf(zb[r][u2], X1[t][u2], y[r][t][3]));
+                }
               }
-            }
           }
         }
       }
@@ -712,29 +752,34 @@ __global__ void __launch_bounds__(kV2Threads, 1)
     if constexpr (KS > 1) {
       if (kq > 0) {
 #pragma unroll
-        for (int t = 0; t < NT; ++t)
-          if (t < ntiles)
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              red[((((kq - 1) * MT + mt) * NT + t) * 32 + lane) * 4 + i] = y[t][i];
-      }
-      named_bar(1, kTmaConsumers);
-      if (kq == 0) {
-#pragma unroll
-        for (int q = 0; q < KS - 1; ++q)
+        for (int r = 0; r < RT; ++r)
 #pragma unroll
           for (int t = 0; t < NT; ++t)
             if (t < ntiles)
 #pragma unroll
               for (int i = 0; i < 4; ++i)
-                y[t][i] += red[(((q * MT + mt) * NT + t) * 32 + lane) * 4 + i];
+                red[((((kq - 1) * MT + mt0 + r) * NT + t) * 32 + lane) * 4 + i] = y[r][t][i];
+      }
+      named_bar(1, kCT);
+      if (kq == 0) {
+#pragma unroll
+        for (int q = 0; q < KS - 1; ++q)
+#pragma unroll
+          for (int r = 0; r < RT; ++r)
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+              if (t < ntiles)
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  y[r][t][i] += red[(((q * MT + mt0 + r) * NT + t) * 32 + lane) * 4 + i];
       }
     }
 
     // ------------------------------------------------------------ epilogues
     if constexpr (EPI == EPI_STORE || EPI == EPI_PARTIAL) {
-      if (kq == 0) {
-        const int64_t row_a = (int64_t)info.rb * ST::kRows + mt * 16 + rr;
+#pragma unroll
+      for (int r = 0; r < RT && kq == 0; ++r) {
+        const int64_t row_a = (int64_t)info.rb * ST::kRows + (mt0 + r) * 16 + rr;
         const int64_t row_b = row_a + 8;
 #pragma unroll
         for (int t = 0; t < NT; ++t)
@@ -744,8 +789,8 @@ __global__ void __launch_bounds__(kV2Threads, 1)
             if (t < ntiles && ci < ncols) {
               const int64_t v = i ? cur.v1[t] : cur.v0[t];
               if constexpr (EPI == EPI_STORE) {
-                if (row_a < p.rows) p.out_bf16[v * p.rows + row_a] = f32_to_bf16_bits(y[t][i]);
-                if (row_b < p.rows) p.out_bf16[v * p.rows + row_b] = f32_to_bf16_bits(y[t][2 + i]);
+                if (row_a < p.rows) p.out_bf16[v * p.rows + row_a] = f32_to_bf16_bits(y[r][t][i]);
+                if (row_b < p.rows) p.out_bf16[v * p.rows + row_b] = f32_to_bf16_bits(y[r][t][2 + i]);
               } else {
                 // routed slots are the w2 gather's bf16 output; the shared
                 // expert's hi/lo columns stay fp32
@@ -765,16 +810,17 @@ __global__ void __launch_bounds__(kV2Threads, 1)
                   }
                 }
                 if (row_a < p.rows)
-                  dst[vv * p.rows + row_a] = routed ? bf16_round(y[t][i]) : y[t][i];
+                  dst[vv * p.rows + row_a] = routed ? bf16_round(y[r][t][i]) : y[r][t][i];
                 if (row_b < p.rows)
-                  dst[vv * p.rows + row_b] = routed ? bf16_round(y[t][2 + i]) : y[t][2 + i];
+                  dst[vv * p.rows + row_b] = routed ? bf16_round(y[r][t][2 + i]) : y[r][t][2 + i];
               }
             }
           }
       }
     } else {  // EPI_SWIGLU
-      if (kq == 0) {
-        const int hrow = info.rb * (MT * 8) + mt * 8 + rr;  // intermediate index (< rows)
+#pragma unroll
+      for (int r = 0; r < RT && kq == 0; ++r) {
+        const int hrow = info.rb * (MT * 8) + (mt0 + r) * 8 + rr;  // intermediate index (< rows)
         const int pos = perm_pos(hrow, p.h_bits);
         const float lim = p.swiglu_limit;
 #pragma unroll
@@ -785,8 +831,8 @@ __global__ void __launch_bounds__(kV2Threads, 1)
             float shi = 0.0f, slo = 0.0f;
             if (t < ntiles && ci < ncols) {
               const int v = i ? cur.v1[t] : cur.v0[t];
-              float g = bf16_round(y[t][i]);
-              float u = bf16_round(y[t][2 + i]);
+              float g = bf16_round(y[r][t][i]);
+              float u = bf16_round(y[r][t][2 + i]);
               if (lim > 0.0f) {
                 g = fminf(g, lim);
                 u = fminf(fmaxf(u, -lim), lim);
@@ -822,8 +868,8 @@ __global__ void __launch_bounds__(kV2Threads, 1)
               slo += __shfl_xor_sync(0xffffffffu, slo, off);
             }
             if (r8 == 0 && t < ntiles && ci < ncols) {
-              hs[(mt * kMaxCols + ci) * 2 + 0] = shi;
-              hs[(mt * kMaxCols + ci) * 2 + 1] = slo;
+              hs[((mt0 + r) * kMaxCols + ci) * 2 + 0] = shi;
+              hs[((mt0 + r) * kMaxCols + ci) * 2 + 1] = slo;
             }
           }
         }
@@ -842,7 +888,7 @@ __global__ void __launch_bounds__(kV2Threads, 1)
           if ((lane >> 3) == t) vci = (lane & 1) ? b : a;
         }
       }
-      named_bar(1, kTmaConsumers);
+      named_bar(1, kCT);
       if (warp < kParts && lane < ncols) {
         float shi = 0.0f, slo = 0.0f;
 #pragma unroll
@@ -857,14 +903,14 @@ __global__ void __launch_bounds__(kV2Threads, 1)
       }
     }
     // red / hs reused by the next item (a split-free store item shares nothing)
-    if constexpr (KS > 1 || EPI == EPI_SWIGLU) named_bar(1, kTmaConsumers);
+    if constexpr (KS > 1 || EPI == EPI_SWIGLU) named_bar(1, kCT);
     if (has_next) cur = nxt;
   }
   if constexpr (EPI == EPI_PARTIAL) {
     // expert parallel: once every CTA's stores are out, tell every rank
     if (p.peer_flags) {
       __threadfence_system();  // this thread's peer stores, before the CTA's count
-      named_bar(1, kTmaConsumers);
+      named_bar(1, kCT);
     }
     if (p.peer_flags && ctid == 0) {
       __threadfence_system();

@@ -140,12 +140,13 @@ template <int BITS, int SD, int EPI, int NT, int MT, bool XH = false>
 inline cudaError_t launch_v2_inst(const GemvParams& p, const TmaMaps& m, int grid,
                                   cudaStream_t s) {
   static bool done[64] = {};  // one per instantiation
+  constexpr int RT = MT % kV2RT == 0 ? kV2RT : 1;
   const int nst = v2_stages<BITS, SD, EPI, NT, MT, XH>();
   const int smem = v2_smem_bytes<BITS, SD, EPI, NT, MT, XH>(nst);
-  auto kern = gemv_v2_kernel<BITS, SD, EPI, NT, MT, XH>;
+  auto kern = gemv_v2_kernel<BITS, SD, EPI, NT, MT, XH, RT>;
   cudaError_t e = opt_in_smem(kern, smem, done);
   if (e != cudaSuccess) return e;
-  return launch_pdl(kern, grid, kV2Threads, smem, s, p, m, nst);
+  return launch_pdl(kern, grid, v2_threads(RT), smem, s, p, m, nst);
 }
 
 template <int BITS, int SD, int EPI>
