@@ -1141,13 +1141,14 @@ static LogitsShape logits_shape(const mr_ctx* ctx, int64_t T, int E, int64_t H) 
   s.mtiles = (E + 15) / 16;
   s.tblocks = (int)((T + 63) / 64);
   const int64_t base = (int64_t)s.mtiles * s.tblocks;
-  const int64_t target = 8LL * ctx->sm_count;  // warps
-  int64_t ks = std::max<int64_t>(1, target / std::max<int64_t>(base, 1));
-  ks = std::min<int64_t>(ks, std::max<int64_t>(1, H / 128));
-  int64_t chunk = (H + ks - 1) / ks;
-  chunk = (chunk + 31) / 32 * 32;
-  s.kchunk = (int)chunk;
-  s.ks = (int)((H + chunk - 1) / chunk);
+  // K chunks of 128 elements (the last one may be shorter) at every batch
+  // size: a token's logit is the same chunk partials summed in the same order
+  // whatever else is in the batch, so routing (ids and weights) is
+  // batch-invariant bit for bit, as expert-parallel ranks that route their
+  // own tokens need to match one GPU routing the whole batch
+  (void)ctx;
+  s.kchunk = 128;
+  s.ks = (int)((H + 127) / 128);
   s.kq = (s.ks + 3) / 4;
   s.blocks = (int)(base * s.kq);
   return s;

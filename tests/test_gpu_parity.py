@@ -358,6 +358,26 @@ def test_layer_batch_invariance_config1_T64(kernel_path):
     M.Context.get(0).sync_check()
 
 
+def test_layer_batch_invariance_config1_T512():
+    """A 512-token batch (8 * 64: the 8-GPU weak-scaling group) runs the staged
+    kernel with 16-column segments (two mma tiles); each token's output must
+    still equal its one-token call bit for bit (routing weights included), as
+    the expert-parallel path, whose ranks route their own tokens, relies on."""
+    M.Context.get(0).set_kernel_path("auto")
+    layer = S.synth_layer(S.CONFIGS[1])
+    x = S.synth_x(S.CONFIGS[1], 512, batch=3)
+    out, sel = layer(x)
+    bad = []
+    for t in (0, 1, 100, 257, 511):
+        o1, s1 = layer(x[t:t + 1])
+        assert torch.equal(s1.ids[0], sel.ids[t])
+        assert torch.equal(s1.weights[0], sel.weights[t])  # routing is batch-invariant
+        if not torch.equal(o1[0], out[t]):
+            bad.append((t, rel_l2(o1[0].float().cpu().numpy(), out[t].float().cpu().numpy())))
+    M.Context.get(0).sync_check()
+    assert not bad, bad
+
+
 def test_synth_matches_oracle_generator():
     cfg = O.CONFIGS[0]
     L = O.gen_layer(cfg)
