@@ -266,6 +266,23 @@ static bool gate_up_f16(const mr_ctx* ctx, const mr_moe_layer* L, bool tcgen05) 
 // Floats per group of the prepped activations' sums (bf16 form: 1).
 static int64_t xsum_floats(bool f16) { return f16 ? kPrepF16Floats : 1; }
 
+// Whether the gate/up launch also writes h in that f16 form for the down
+// launch: both on the staged GEMV with 4- or 8-bit codes, and gate/up items
+// of at least one 64-row group of h (the group scale is found inside an item).
+static bool down_f16(const mr_ctx* ctx, const mr_moe_layer* L, bool tcgen05) {
+  if (!gate_up_f16(ctx, L, tcgen05)) return false;
+  const int bits = L->down.bits;
+  if ((bits != 4 && bits != 8) || !v2_up_wide(L->gate.bits, L->inter) ||
+      v2_item_rows(EPI_SWIGLU, L->gate.bits, L->inter) < 2 * kGroup ||
+      !tma_layout_ok(L->inter, &L->down, false))
+    return false;
+  return L->shared_inter <= 0 ||
+         (L->shared_down.bits == bits && tma_layout_ok(L->inter, &L->shared_down, false));
+}
+// Floats of h sums per h row: two 32-row partials per group (bf16 h), or
+// the f16 form's four per group.
+static int64_t hsum_floats(int64_t I, bool f16) { return f16 ? I / kGroup * kPrepF16Floats : I / 32; }
+
 // Activation rows of routed columns in plan order (tcgen05 layer path with
 // more than 16 tokens): xg[c] = x_perm[cols[c] / in_div], and its group sums.
 // Positions past the plan's valid columns may hold stale ids; rows outside
@@ -1386,6 +1403,7 @@ struct ExpertsRun {
   // home ranks' buffers (GemvParams::peer_*); nullptr elsewhere
   const GemvParams* peer;
   bool x_f16;  // gate/up activations in the prep's f16 form (staged GEMV)
+  bool h_f16;  // h (the down launch's activations) in the f16 form too
 };
 
 static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRun& r,
@@ -1427,6 +1445,7 @@ static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRu
   g.xsum = r.xsum;
   g.xsum_parts = 1;
   g.x_f16 = r.x_f16 ? 1 : 0;
+  g.h_f16 = r.h_f16 ? 1 : 0;
   g.error = ctx->d_error;
   g.out_bf16 = r.h;
   g.hsum = r.hsum;
@@ -1485,6 +1504,7 @@ static mr_status run_experts(mr_ctx* ctx, const mr_moe_layer* L, const ExpertsRu
   d.xperm = r.h;
   d.xsum = r.hsum;
   d.xsum_parts = 2;
+  d.x_f16 = r.h_f16 ? 1 : 0;
   d.error = ctx->d_error;
   d.part = r.part2;
   d.weights = r.wts;
@@ -1557,6 +1577,7 @@ static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   const bool um_try = !pf_try && ctx->kernel_path == 3 && um_layout;
   const bool um_dense = !pf_try && T <= kUmN;  // routed activations are the token rows
   const bool xf16 = gate_up_f16(ctx, L, pf_try || um_try);
+  const bool hf16 = down_f16(ctx, L, pf_try || um_try);
   // segments per expert of seg_cols columns; the workspace holds the plan of
   // the narrowest segments, the width is fixed once the kernels are chosen
   const int64_t max_seg = std::min<int64_t>(E, Tk) + Tk / pick_seg_cols(T) + 1;
@@ -1586,7 +1607,7 @@ static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
     segs = b.take<int4>(max_seg);
     cols = b.take<int>(Tk);
     h = b.take<uint16_t>(R * I);
-    hsum = b.take<float>(R * (I / 32));  // two 32-row partial sums per group
+    hsum = b.take<float>(R * hsum_floats(I, hf16));
     part2 = b.take<float>(R * H);
     if (pass == 0) {
       if ((st = ensure_workspace(ctx, b.off))) return st;
@@ -1643,6 +1664,7 @@ static mr_status layer_forward(mr_ctx* ctx, const mr_moe_layer* L, const uint16_
   r.xperm = xperm;
   r.xsum = xsum;
   r.x_f16 = xf16;
+  r.h_f16 = hf16;
   r.tokens = T;
   r.shared_tokens = has_shared ? T : 0;
   r.Tk = Tk;
@@ -2658,6 +2680,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
             Tcap * W * k >= 32 * (int64_t)E;
   const bool pf_sh = pf && has_shared && T >= 32;  // the shared expert's own launch
   const bool xf16 = gate_up_f16(ctx, L, pf);
+  const bool hf16 = down_f16(ctx, L, pf);
   const int64_t xsf = xsum_floats(xf16);
   int seg_cols = pf ? kPfN : decode_seg_cols(ctx, Tcap * W * k, E);
   const int64_t max_seg = std::min<int64_t>(El, RK) + RK / 8 + 1;
@@ -2706,9 +2729,9 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
     segs = b.take<int4>(max_seg);
     cols = b.take<int>(RK);
     h = b.take<uint16_t>(RK * I);
-    hsum = b.take<float>(RK * (I / 32));
+    hsum = b.take<float>(RK * hsum_floats(I, hf16));
     hs = b.take<uint16_t>(2 * T * I);
-    hss = b.take<float>(2 * T * (I / 32));
+    hss = b.take<float>(2 * T * hsum_floats(I, hf16));
     dummy = b.take<float>(64);
     if (pass == 0) {
       if ((st = ensure_workspace(ctx, b.off))) return st;
@@ -2811,6 +2834,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
     r.xperm = xrecv;
     r.xsum = xsrecv;
     r.x_f16 = xf16;
+    r.h_f16 = hf16;
     r.tokens = R;
     r.shared_tokens = 0;
     r.Tk = RK;
@@ -2848,6 +2872,7 @@ static mr_status ep_forward_a2a(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L, c
     sh.xperm = xperm;
     sh.xsum = xsum;
     sh.x_f16 = xf16;
+    sh.h_f16 = hf16;
     sh.tokens = T;
     sh.shared_tokens = T;
     sh.Tk = 0;
@@ -2941,6 +2966,7 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
   const int64_t max_seg = std::min<int64_t>(El, NTk) + NTk / seg_cols + 1;
   const LogitsShape ls = logits_shape(ctx, NT, E, H);
   const bool xf16 = gate_up_f16(ctx, L, false);
+  const bool hf16 = down_f16(ctx, L, false);
   const int64_t xsf = xsum_floats(xf16);
 
   uint16_t *xall = nullptr, *xperm = nullptr, *h = nullptr, *hs = nullptr;
@@ -2963,12 +2989,12 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
     segs = b.take<int4>(max_seg);
     cols = b.take<int>(NTk);
     h = b.take<uint16_t>(NTk * I);
-    hsum = b.take<float>(NTk * (I / 32));
+    hsum = b.take<float>(NTk * hsum_floats(I, hf16));
     part2 = b.take<float>(NTk * H);
     ypart = b.take<float>(NT * H);
     yred = b.take<float>(T * H);
     hs = b.take<uint16_t>(2 * T * I);
-    hss = b.take<float>(2 * T * (I / 32));
+    hss = b.take<float>(2 * T * hsum_floats(I, hf16));
     psh = b.take<float>(2 * T * H);
     if (pass == 0) {
       if ((st = ensure_workspace(ctx, b.off))) return st;
@@ -2995,6 +3021,7 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
   r.xperm = xperm;
   r.xsum = xsum;
   r.x_f16 = xf16;
+  r.h_f16 = hf16;
   r.tokens = NT;
   r.shared_tokens = 0;
   r.Tk = NTk;
@@ -3051,6 +3078,7 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
       sh.xperm = xperm + (int64_t)rank * T * H;
       sh.xsum = xsum + (int64_t)rank * T * (H / kGroup) * xsf;
       sh.x_f16 = xf16;
+      sh.h_f16 = hf16;
       sh.tokens = T;
       sh.shared_tokens = T;
       sh.Tk = 0;
@@ -3100,6 +3128,7 @@ mr_status mr_moe_layer_forward_ep(mr_ctx* ctx, mr_ep* ep, const mr_moe_layer* L,
       sh.xperm = xperm + (int64_t)rank * T * H;
       sh.xsum = xsum + (int64_t)rank * T * (H / kGroup) * xsf;
       sh.x_f16 = xf16;
+      sh.h_f16 = hf16;
       sh.tokens = T;
       sh.shared_tokens = T;
       sh.Tk = 0;

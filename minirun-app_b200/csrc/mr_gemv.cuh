@@ -114,6 +114,9 @@ struct GemvParams {
   // staged gate/up: activations in the f16 form of the prep (xperm f16,
   // xsum {2^k, W, X, 0} per group)
   int x_f16;
+  // staged gate/up: write h (and its sums) in that f16 form for the down
+  // launch (items of >= 64 h rows)
+  int h_f16;
   int shared_lo_off;      // SWIGLU: shared lo row = hi row + shared_lo_off
   // combine (PARTIAL)
   unsigned* counters;

@@ -183,7 +183,9 @@ template <int NT, int MT>
 struct V2Fixed {
   static constexpr int kKS = kTmaConsumerWarps / MT;
   static constexpr int kRedFloats = (kKS - 1) * MT * NT * 32 * 4;
-  static constexpr int kHsFloats = (MT > 4 ? MT : 4) * kMaxCols * 2;
+  // SwiGLU h terms per m-tile and column: two partial sums (bf16 h), or the
+  // max, X and W of the high and low parts (f16 h)
+  static constexpr int kHsFloats = (MT > 4 ? MT : 4) * kMaxCols * 6;
   static constexpr int kBytes = (kRedFloats + kHsFloats) * 4 + 16;
 };
 
@@ -202,7 +204,7 @@ struct V2Stage {
   static constexpr int kCols = 8 * NT;
   // floats per group and column of the stage's sums: two 32-row partial
   // sums (down), one sum (gate/up), {2^k, W, X, 0} of the f16 form
-  static constexpr int kXP = EPI == EPI_PARTIAL ? 2 : (XH ? kPrepF16Floats : 1);
+  static constexpr int kXP = XH ? kPrepF16Floats : (EPI == EPI_PARTIAL ? 2 : 1);
   static constexpr int kColBytes = kTmaGps * kGroup * 2 + 16;  // one column's 512 bf16 + pad
   static constexpr int kWBytes = W::kABytes + W::kSBytes + W::kZBytes;
   static constexpr int kXOff = kWBytes;                          // activations
@@ -338,8 +340,8 @@ __global__ void __launch_bounds__(v2_threads(RT), 1)
     gemv_v2_kernel(const GemvParams p, const __grid_constant__ TmaMaps maps, const int nst) {
   static_assert(EPI != EPI_SWIGLU || MT % 4 == 0, "SwiGLU items: whole 32-row h partials");
   pdl_wait_and_release();
-  static_assert(!XH || (EPI == EPI_SWIGLU && (BITS == 4 || BITS == 8)),
-                "f16 form: gate/up at 4 and 8 bits");
+  static_assert(!XH || (EPI != EPI_STORE && (BITS == 4 || BITS == 8)),
+                "f16 form: gate/up and down at 4 and 8 bits");
   using VS = V2Stage<BITS, SD, EPI, NT, MT, XH>;
   using ST = typename VS::W;
   using FX = V2Fixed<NT, MT>;
@@ -377,6 +379,7 @@ __global__ void __launch_bounds__(v2_threads(RT), 1)
     flags[0] = 0;  // abort
     fence_mbar_init();
   }
+  for (int i = threadIdx.x; i < FX::kHsFloats; i += blockDim.x) hs[i] = 0.0f;
   __syncthreads();
 
   auto in_row = [&](int v) -> int64_t {
@@ -548,6 +551,7 @@ __global__ void __launch_bounds__(v2_threads(RT), 1)
   };
 
   Meta cur, nxt;
+  uint32_t item_par = 0;  // items this CTA has done (parity picks h-max buffers)
   if ((int)blockIdx.x < n_items) {
     cur.info = decode_item(p, n_routed, blockIdx.x);
     fetch_cols(cur);
@@ -818,93 +822,217 @@ __global__ void __launch_bounds__(v2_threads(RT), 1)
           }
       }
     } else {  // EPI_SWIGLU
+      // h values of this lane (bf16-rounded; the shared expert's low parts
+      // in hl), then written in the down launch's activation form
+      float hv[RT][NT][2], hl[RT][NT][2];
+      int pos_r[RT];
 #pragma unroll
-      for (int r = 0; r < RT && kq == 0; ++r) {
+      for (int r = 0; r < RT; ++r) {
         const int hrow = info.rb * (MT * 8) + (mt0 + r) * 8 + rr;  // intermediate index (< rows)
-        const int pos = perm_pos(hrow, p.h_bits);
+        pos_r[r] = perm_pos(hrow, p.h_bits);
         const float lim = p.swiglu_limit;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             const int ci = t * 8 + 2 * c + i;
-            float shi = 0.0f, slo = 0.0f;
-            if (t < ntiles && ci < ncols) {
-              const int v = i ? cur.v1[t] : cur.v0[t];
+            hv[r][t][i] = 0.0f;
+            hl[r][t][i] = 0.0f;
+            if (kq == 0 && t < ntiles && ci < ncols) {
               float g = bf16_round(y[r][t][i]);
               float u = bf16_round(y[r][t][2 + i]);
               if (lim > 0.0f) {
                 g = fminf(g, lim);
                 u = fminf(fmaxf(u, -lim), lim);
               }
-              uint16_t hb;
               if (!shared) {
                 if (!p.weight_after_down) {
                   float a = g * sigmoid_f32(g);
                   a = a * u;
                   a = a * (i ? cur.w1[t] : cur.w0[t]);
-                  hb = f32_to_bf16_bits(a);
+                  hv[r][t][i] = bf16_round(a);
                 } else {
                   const float sg = bf16_round(sigmoid_f32(g));
                   const float a = bf16_round(g * sg);
-                  hb = f32_to_bf16_bits(a * u);
+                  hv[r][t][i] = bf16_round(a * u);
                 }
-                p.out_bf16[(int64_t)v * p.rows + pos] = hb;
-                shi = bf16_bits_to_f32(hb);
               } else {
                 float a = g * sigmoid_f32(g);
                 a = a * u;
-                hb = f32_to_bf16_bits(a);
-                const uint16_t lb16 = f32_to_bf16_bits(a - bf16_bits_to_f32(hb));
-                p.out_bf16[(int64_t)v * p.rows + pos] = hb;
-                p.out_bf16[(int64_t)(v + p.shared_lo_off) * p.rows + pos] = lb16;
-                shi = bf16_bits_to_f32(hb);
-                slo = bf16_bits_to_f32(lb16);
+                hv[r][t][i] = bf16_round(a);
+                hl[r][t][i] = bf16_round(a - hv[r][t][i]);
               }
-            }
-#pragma unroll
-            for (int off = 4; off < 32; off <<= 1) {
-              shi += __shfl_xor_sync(0xffffffffu, shi, off);
-              slo += __shfl_xor_sync(0xffffffffu, slo, off);
-            }
-            if (r8 == 0 && t < ntiles && ci < ncols) {
-              hs[((mt0 + r) * kMaxCols + ci) * 2 + 0] = shi;
-              hs[((mt0 + r) * kMaxCols + ci) * 2 + 1] = slo;
             }
           }
         }
       }
-      // the item's MT * 8 h rows make MT / 4 partials of 32 rows; lane ci < ncols
-      // of warp q sums column ci over m-tiles 4q .. 4q+3. The column's value
-      // sits in lane (ci & 7) >> 1 of any warp (v0 or v1).
-      constexpr int kParts = MT / 4;
+      // the column's value id (v) for lane ci < ncols of any warp: it sits in
+      // lane (ci & 7) >> 1 (v0 or v1)
       int vci = 0;
-      if (warp < kParts) {
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const int src = (lane & 7) >> 1;
-          const int a = __shfl_sync(0xffffffffu, cur.v0[t], src);
-          const int b = __shfl_sync(0xffffffffu, cur.v1[t], src);
-          if ((lane >> 3) == t) vci = (lane & 1) ? b : a;
-        }
+      for (int t = 0; t < NT; ++t) {
+        const int src = (lane & 7) >> 1;
+        const int a = __shfl_sync(0xffffffffu, cur.v0[t], src);
+        const int b = __shfl_sync(0xffffffffu, cur.v1[t], src);
+        if ((lane >> 3) == t) vci = (lane & 1) ? b : a;
       }
-      named_bar(1, kCT);
-      if (warp < kParts && lane < ncols) {
-        float shi = 0.0f, slo = 0.0f;
+      if (!p.h_f16) {
+        // bf16 h; the item's MT * 8 h rows make MT / 4 partial sums of 32 rows
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          shi += hs[((warp * 4 + m) * kMaxCols + lane) * 2 + 0];
-          slo += hs[((warp * 4 + m) * kMaxCols + lane) * 2 + 1];
+        for (int r = 0; r < RT; ++r) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int ci = t * 8 + 2 * c + i;
+              const bool ok = kq == 0 && t < ntiles && ci < ncols;
+              if (ok) {
+                const int v = i ? cur.v1[t] : cur.v0[t];
+                p.out_bf16[(int64_t)v * p.rows + pos_r[r]] = f32_to_bf16_bits(hv[r][t][i]);
+                if (shared)
+                  p.out_bf16[(int64_t)(v + p.shared_lo_off) * p.rows + pos_r[r]] =
+                      f32_to_bf16_bits(hl[r][t][i]);
+              }
+              float shi = hv[r][t][i], slo = hl[r][t][i];
+#pragma unroll
+              for (int off = 4; off < 32; off <<= 1) {
+                shi += __shfl_xor_sync(0xffffffffu, shi, off);
+                slo += __shfl_xor_sync(0xffffffffu, slo, off);
+              }
+              if (r8 == 0 && ok) {
+                hs[((mt0 + r) * kMaxCols + ci) * 2 + 0] = shi;
+                hs[((mt0 + r) * kMaxCols + ci) * 2 + 1] = slo;
+              }
+            }
+          }
         }
-        const int64_t hp = p.rows / 32;  // 32-row partial sums per h row
-        const int64_t part = (int64_t)info.rb * kParts + warp;
-        p.hsum[(int64_t)vci * hp + part] = shi;
-        if (shared) p.hsum[(int64_t)(vci + p.shared_lo_off) * hp + part] = slo;
+        // lane ci < ncols of warp q sums column ci over m-tiles 4q .. 4q+3
+        constexpr int kParts = MT / 4;
+        named_bar(1, kCT);
+        if (warp < kParts && lane < ncols) {
+          float shi = 0.0f, slo = 0.0f;
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            shi += hs[((warp * 4 + m) * kMaxCols + lane) * 2 + 0];
+            slo += hs[((warp * 4 + m) * kMaxCols + lane) * 2 + 1];
+          }
+          const int64_t hp = p.rows / 32;  // 32-row partial sums per h row
+          const int64_t part = (int64_t)info.rb * kParts + warp;
+          p.hsum[(int64_t)vci * hp + part] = shi;
+          if (shared) p.hsum[(int64_t)(vci + p.shared_lo_off) * hp + part] = slo;
+        }
+      } else if constexpr (MT >= 8) {  // (the host asks for it on such items only)
+        // f16 form of h for the down launch (the prep's form of x): per 64-row
+        // group (8 m-tiles) and column, k = floor(log2(max |h|)) - 14,
+        // h' = f16(h * 2^-k), and {2^k, W, X, 0} with X = sum h and W = sum
+        // C(pos) * h (C: 1024, or 64 for a 4-bit code in bits 4-7 of its byte).
+        // hs: X and W of the high and low parts per m-tile and column, then
+        // two buffers (by item parity) of the group maxima (float bits,
+        // atomicMax: order-free) per group, part and column; an item clears
+        // the other parity's buffer, which no warp touches before the next
+        // item.
+        constexpr int kGroupsItem = MT / 8;
+        unsigned* gmx0 = reinterpret_cast<unsigned*>(hs + MT * kMaxCols * 4);
+        unsigned* gmx = gmx0 + (item_par & 1) * kGroupsItem * 2 * kMaxCols;
+        unsigned* gmx_next = gmx0 + ((item_par & 1) ^ 1) * kGroupsItem * 2 * kMaxCols;
+#pragma unroll
+        for (int r = 0; r < RT; ++r) {
+          const float cst = (p.h_bits == 8 || (pos_r[r] & 3) < 2) ? 1024.0f : 64.0f;
+          const int grp = (mt0 + r) >> 3;
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int ci = t * 8 + 2 * c + i;
+              const bool ok = kq == 0 && t < ntiles && ci < ncols;
+              float xh = hv[r][t][i], wh = cst * hv[r][t][i];
+              float xl = hl[r][t][i], wl = cst * hl[r][t][i];
+              float mh = fabsf(hv[r][t][i]), ml = fabsf(hl[r][t][i]);
+              mh = mh <= 3.4028235e38f ? mh : 0.0f;  // finite values only
+              ml = ml <= 3.4028235e38f ? ml : 0.0f;
+#pragma unroll
+              for (int off = 4; off < 32; off <<= 1) {
+                xh += __shfl_xor_sync(0xffffffffu, xh, off);
+                wh += __shfl_xor_sync(0xffffffffu, wh, off);
+                mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, off));
+                if (shared) {
+                  xl += __shfl_xor_sync(0xffffffffu, xl, off);
+                  wl += __shfl_xor_sync(0xffffffffu, wl, off);
+                  ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, off));
+                }
+              }
+              if (ok && r8 == 0) {  // the tile's column terms; the group max across warps
+                atomicMax(gmx + (grp * 2 + 0) * kMaxCols + ci, __float_as_uint(mh));
+                if (shared) atomicMax(gmx + (grp * 2 + 1) * kMaxCols + ci, __float_as_uint(ml));
+                float* q = hs + ((mt0 + r) * kMaxCols + ci) * 4;
+                q[0] = xh; q[1] = wh; q[2] = xl; q[3] = wl;
+              }
+            }
+          }
+        }
+        named_bar(1, kCT);
+        auto group_k = [](unsigned mx_bits) -> int {
+          int k = 0;
+          if (mx_bits != 0u) {
+            k = (int)((mx_bits >> 23) & 0xffu) - 127 - 14;
+            k = k < -100 ? -100 : (k > 100 ? 100 : k);
+          }
+          return k;
+        };
+#pragma unroll
+        for (int r = 0; r < RT; ++r) {
+          const int grp = (mt0 + r) >> 3;
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int ci = t * 8 + 2 * c + i;
+              if (kq == 0 && t < ntiles && ci < ncols) {
+                const int v = i ? cur.v1[t] : cur.v0[t];
+                const int kh = group_k(gmx[(grp * 2 + 0) * kMaxCols + ci]);
+                p.out_bf16[(int64_t)v * p.rows + pos_r[r]] = __half_as_ushort(
+                    __float2half_rn(hv[r][t][i] * __uint_as_float((uint32_t)(127 - kh) << 23)));
+                if (shared) {
+                  const int kl = group_k(gmx[(grp * 2 + 1) * kMaxCols + ci]);
+                  p.out_bf16[(int64_t)(v + p.shared_lo_off) * p.rows + pos_r[r]] =
+                      __half_as_ushort(__float2half_rn(
+                          hl[r][t][i] * __uint_as_float((uint32_t)(127 - kl) << 23)));
+                }
+              }
+            }
+          }
+        }
+        // lane ci < ncols of warp q: column ci's terms of group q of the item,
+        // m-tiles in order
+        if (warp < kGroupsItem && lane < ncols) {
+          float xh = 0.0f, wh = 0.0f, xl = 0.0f, wl = 0.0f;
+#pragma unroll
+          for (int m = 0; m < 8; ++m) {
+            const float* q = hs + ((warp * 8 + m) * kMaxCols + lane) * 4;
+            xh += q[0]; wh += q[1]; xl += q[2]; wl += q[3];
+          }
+          unsigned* gm = gmx + (warp * 2) * kMaxCols + lane;
+          const int kh = group_k(gm[0]), kl = group_k(gm[kMaxCols]);
+          const int64_t ng = p.rows / kGroup;  // groups per h row
+          const int64_t gi = (int64_t)info.rb * kGroupsItem + warp;
+          *reinterpret_cast<float4*>(p.hsum + ((int64_t)vci * ng + gi) * kPrepF16Floats) =
+              make_float4(__uint_as_float((uint32_t)(127 + kh) << 23), wh, xh, 0.0f);
+          if (shared)
+            *reinterpret_cast<float4*>(p.hsum +
+                                       ((int64_t)(vci + p.shared_lo_off) * ng + gi) *
+                                           kPrepF16Floats) =
+                make_float4(__uint_as_float((uint32_t)(127 + kl) << 23), wl, xl, 0.0f);
+        }
+        if (warp < kGroupsItem && lane < kMaxCols) {
+          gmx_next[(warp * 2) * kMaxCols + lane] = 0u;
+          gmx_next[(warp * 2 + 1) * kMaxCols + lane] = 0u;
+        }
       }
     }
     // red / hs reused by the next item (a split-free store item shares nothing)
     if constexpr (KS > 1 || EPI == EPI_SWIGLU) named_bar(1, kCT);
     if (has_next) cur = nxt;
+    ++item_par;
   }
   if constexpr (EPI == EPI_PARTIAL) {
     // expert parallel: once every CTA's stores are out, tell every rank

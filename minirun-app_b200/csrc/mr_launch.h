@@ -274,7 +274,7 @@ inline cudaError_t launch_pf_epi(const GemvParams& p, const UmMaps& m, int epi, 
   template <int SD, int EPI, int MT>                                                           \
   static cudaError_t v2_mt_##BITS(const GemvParams& p, const TmaMaps& m, int nt, int grid,     \
                                   cudaStream_t s) {                                            \
-    if constexpr (EPI == EPI_SWIGLU && (BITS == 4 || BITS == 8)) {                             \
+    if constexpr (EPI != EPI_STORE && (BITS == 4 || BITS == 8)) {                              \
       if (p.x_f16)                                                                             \
         return nt == 1 ? launch_v2_inst<BITS, SD, EPI, 1, MT, true>(p, m, grid, s)             \
                        : launch_v2_inst<BITS, SD, EPI, 2, MT, true>(p, m, grid, s);            \
