@@ -16,12 +16,16 @@
 //     MLX's own large-batch quantised matmul does) into a TMEM A buffer
 //     (tcgen05.st); scales and biases come from global memory one stage
 //     ahead;
+//   - 4 epilogue warps (one per TMEM lane quadrant): a finished tile's
+//     accumulator -> SwiGLU h or per-slot partials, while the workers
+//     dequantise the next tile;
 //   - warp 1, one lane: per stage, 4 tcgen05.mma per group (M 128, N 128,
 //     K 16; A from TMEM, activations from shared memory), all accumulating
 //     into the tile's TMEM accumulator, then one commit.
-// Two A buffers let dequantisation overlap the MMAs; two accumulators let
-// one tile's epilogue (tcgen05.ld in 32-column chunks: SwiGLU -> h, or
-// per-slot partials) overlap the next tile's MMAs. At N = 128 one MMA takes
+// Two A buffers let dequantisation overlap the MMAs; two accumulators and
+// the separate epilogue warps let one tile's epilogue (tcgen05.ld in
+// 32-column chunks: SwiGLU -> h, or per-slot partials) overlap the next
+// tile's dequantisation and MMAs. At N = 128 one MMA takes
 // ~64 cycles, the tensor core's full rate, so the kernel is bound by the
 // tensor pipe (and the L2 -> shared-memory feed of activations), not by the
 // per-instruction cost that limits small-N decode MMAs.
@@ -38,7 +42,8 @@ namespace mr {
 constexpr int kPfRows = 128;   // MMA M
 constexpr int kPfN = 128;      // MMA N: activation rows (tokens) of one tile
 constexpr int kPfWorkers = 8;
-constexpr int kPfThreads = (2 + kPfWorkers) * 32;
+constexpr int kPfEpilogue = 4;  // epilogue warps, one per TMEM lane quadrant
+constexpr int kPfThreads = (2 + kPfWorkers + kPfEpilogue) * 32;
 constexpr int kPfChunk = 32;   // accumulator columns per epilogue step
 
 constexpr int kPfCodeSlots = 3;  // slots of the code ring
@@ -66,7 +71,8 @@ struct PfStage {
 };
 
 struct PfFixed {
-  static constexpr int kUpBytes = 2 * 64 * (kPfChunk + 1) * 4;  // up rows of one chunk, per half
+  // SwiGLU exchange: two buffers x (gate, up) x 64 rows x half a chunk (+1 pad)
+  static constexpr int kUpBytes = 2 * 2 * 64 * (kPfChunk / 2 + 1) * 4;
   static constexpr int kBarBytes = (2 * 16 + 2 * kPfCodeSlots + 4 * 2 + 1) * 8;
   static constexpr int kBytes = kUpBytes + kBarBytes + 16 + 1024;
 };
@@ -142,15 +148,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // code ring (kPfCodeSlots x kCodeBytes), activation ring (nst x kXBytes)
   char* xring = smem + kPfCodeSlots * ST::kCodeBytes;
-  float* upx = reinterpret_cast<float*>(xring + nst * ST::kXBytes);  // [2 halves][64][33]
-  uint64_t* full = reinterpret_cast<uint64_t*>(upx + 2 * 64 * (kPfChunk + 1));  // [nst] activations
+  float* upx = reinterpret_cast<float*>(xring + nst * ST::kXBytes);  // [2][2][64][17]
+  uint64_t* full = reinterpret_cast<uint64_t*>(upx + PfFixed::kUpBytes / 4);  // [nst] activations
   uint64_t* empty = full + nst;   // [nst] activation slot read by the MMAs (commit)
   uint64_t* cfull = empty + nst;  // [kPfCodeSlots] a stage's codes landed
   uint64_t* cempty = cfull + kPfCodeSlots;  // [kPfCodeSlots] codes read (8 workers)
   uint64_t* afull = cempty + kPfCodeSlots;  // [2] a stage's A written (8 workers)
   uint64_t* aempty = afull + 2;   // [2] a stage's A read by the MMAs (commit)
   uint64_t* dfull = aempty + 2;   // [2] a tile's accumulator complete (commit)
-  uint64_t* dempty = dfull + 2;   // [2] a tile's accumulator read out (8 workers)
+  uint64_t* dempty = dfull + 2;   // [2] a tile's accumulator read out (4 epilogue warps)
   uint64_t* drain = dempty + 2;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* flags = reinterpret_cast<volatile int*>(tslot + 1);
@@ -175,7 +181,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(afull + b, kPfWorkers);
       mbar_init(aempty + b, 1);
       mbar_init(dfull + b, 1);
-      mbar_init(dempty + b, kPfWorkers);
+      mbar_init(dempty + b, kPfEpilogue);
     }
     mbar_init(drain, 1);
     flags[0] = 0;
@@ -291,21 +297,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tc_commit(drain);
       wait_bounded(drain, 0, flags, p.error);
     }
-  } else {
+  } else if (warp < 2 + kPfWorkers) {
     // ------------------------------------------------------------- workers
     const int wq = warp & 3;              // TMEM lane quadrant
-    const int half = (warp - 2) >> 2;     // which groups of a stage / columns of a chunk
+    const int half = (warp - 2) >> 2;     // which groups of a stage
     const int row = wq * 32 + lane;       // weight row in the tile = TMEM lane
     const uint32_t lane_t = tbase + ((uint32_t)(wq * 32) << 16);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t rowoff = (uint32_t)row * 128;
     const uint32_t rsw = (uint32_t)(row & 7);
-    uint32_t slot = 0, phase = 0, stg = sbase, j = 0, t = 0;  // code ring
-    float* up = upx + half * 64 * (kPfChunk + 1);
+    uint32_t slot = 0, phase = 0, stg = sbase, j = 0;  // code ring
 
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++t) {
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
       const ItemInfo info = decode_item(p, n_routed, item);
-      const int ncols = info.ncols;
       // this row's scales / biases: expert stack row of gate (rows < 64) or up
       const bool second = ST::kMats == 2 && row >= ST::kBoxRows;
       const int mrow = second ? row - ST::kBoxRows : row;
@@ -372,93 +376,145 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           stg += ST::kCodeBytes;
         }
       }
-
-      // ------------------------------------------------------------ epilogue
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // One warp per TMEM lane quadrant drains its 32 rows of a finished
+    // tile's accumulator (tcgen05.ld, 32 columns at a time) while the
+    // workers dequantise the next tile for the other accumulator.
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_t = tbase + ((uint32_t)(wq * 32) << 16);
+    constexpr int kCh = kPfN / kPfChunk;  // chunks of a tile
+    uint32_t t = 0, cc = 0;  // tiles, chunks (the SwiGLU buffer alternates per chunk)
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++t) {
+      const ItemInfo info = decode_item(p, n_routed, item);
+      const int ncols = info.ncols;
+      const bool second = ST::kMats == 2 && row >= ST::kBoxRows;
+      const int mrow = second ? row - ST::kBoxRows : row;
+      const int64_t grow = (int64_t)info.rb * ST::kBoxRows + mrow;
+      const bool row_ok = grow < p.rows;
+      // before the accumulator is ready: lane l fetches what column
+      // c * 32 + l of each chunk needs (value id, routing weight, or the
+      // expert-parallel destination), so the column loop only shuffles
+      int mv[kCh];
+      float wl[kCh];
+      int dl[kCh];  // EP: home rank of the column's pair (-1: this GPU's own rows)
+#pragma unroll
+      for (int c = 0; c < kCh; ++c) {
+        const int col = c * kPfChunk + lane;
+        mv[c] = 0;
+        wl[c] = 0.0f;
+        dl[c] = -1;
+        if (col < ncols)
+          mv[c] = info.shared ? (EPI == EPI_SWIGLU ? 0 : p.sh_row0) + info.col0 + col
+                              : __ldg(p.cols + info.col0 + col);
+      }
+#pragma unroll
+      for (int c = 0; c < kCh; ++c) {
+        const int col = c * kPfChunk + lane;
+        if constexpr (EPI == EPI_SWIGLU) {
+          if (col < ncols && !info.shared && !p.weight_after_down) wl[c] = __ldg(p.weights + mv[c]);
+        } else if constexpr (EPI == EPI_PARTIAL) {
+          if (col < ncols && p.peer_part && mv[c] < p.Tk) {
+            // expert parallel: the routed pair's partial goes to its home
+            // rank (possibly a peer GPU), row vv there
+            const int v = mv[c];
+            if (p.peer_row_tok) {
+              const int q = v / p.k;
+              dl[c] = q / p.peer_rows;
+              mv[c] = __ldg(p.peer_row_tok + q) * p.k + (v - q * p.k);
+            } else {
+              dl[c] = v / p.peer_cols;
+              mv[c] = v - dl[c] * p.peer_cols;
+            }
+          }
+        }
+      }
       const uint32_t db = t & 1u;
       warp_wait_sleep(dfull + db, (t >> 1) & 1u, flags, p.error);
       tc_fence_after();
-      const uint32_t dcol = tbase + ST::kDCol0 + db * kPfN;
-      for (int cb = half * kPfChunk; cb < ncols; cb += 2 * kPfChunk) {
-        // columns cb .. cb+31 of the accumulator, this warp's lanes
-        uint32_t r[32];
-        float d[kPfChunk];
-        __syncwarp();
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-            "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-            "%28, %29, %30, %31}, [%32];\n\ttcgen05.wait::ld.sync.aligned;"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-              "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-              "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-              "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-              "=r"(r[31])
-            : "r"(lane_t + (dcol - tbase) + cb)
-            : "memory");
+      const uint32_t dcol = ST::kDCol0 + db * kPfN;
 #pragma unroll
-        for (int i = 0; i < kPfChunk; ++i) d[i] = __uint_as_float(r[i]);
-        const int nc = min(kPfChunk, ncols - cb);
-        // value id of column cb + lane (this lane's column of the chunk)
-        int mv = 0;
-        if (lane < nc) mv = info.shared ? (EPI == EPI_SWIGLU ? 0 : p.sh_row0) + info.col0 + cb + lane
-                                        : __ldg(p.cols + info.col0 + cb + lane);
-        if constexpr (EPI == EPI_STORE || EPI == EPI_PARTIAL) {
-          if (EPI == EPI_PARTIAL && p.peer_part) {
-            // expert parallel: each routed pair's partial goes to its home rank
-            // (possibly a peer GPU)
+      for (int c = 0; c < kCh; ++c) {
+        const int cb = c * kPfChunk;
+        if (cb < ncols) {  // warp-uniform
+          uint32_t r[32];
+          float d[kPfChunk];
+          __syncwarp();
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, "
+              "%10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, "
+              "%26, %27, %28, %29, %30, %31}, [%32];\n\ttcgen05.wait::ld.sync.aligned;"
+              : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
+                "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+                "=r"(r[30]), "=r"(r[31])
+              : "r"(lane_t + dcol + cb)
+              : "memory");
 #pragma unroll
-            for (int jj = 0; jj < kPfChunk; ++jj) {
-              if (jj >= nc) break;  // warp-uniform
-              const int v = __shfl_sync(0xffffffffu, mv, jj);
-              if (row_ok) {
-                float* dst = p.part;
-                int64_t vv = v;
-                if (v < p.Tk) {
-                  if (p.peer_row_tok) {
-                    const int q = v / p.k;
-                    const int home = q / p.peer_rows;
-                    dst = p.peer_part[home];
-                    vv = (int64_t)__ldg(p.peer_row_tok + q) * p.k + (v - q * p.k);
-                  } else {
-                    const int home = v / p.peer_cols;
-                    dst = p.peer_part[home];
-                    vv = v - (int64_t)home * p.peer_cols;
-                  }
+          for (int i = 0; i < kPfChunk; ++i) d[i] = __uint_as_float(r[i]);
+          const int nc = min(kPfChunk, ncols - cb);
+          if constexpr (EPI == EPI_STORE || EPI == EPI_PARTIAL) {
+            if (EPI == EPI_PARTIAL && p.peer_part) {
+#pragma unroll
+              for (int jj = 0; jj < kPfChunk; ++jj) {
+                if (jj >= nc) break;  // warp-uniform
+                const int v = __shfl_sync(0xffffffffu, mv[c], jj);
+                const int home = __shfl_sync(0xffffffffu, dl[c], jj);
+                if (row_ok) {
+                  float* dst = home >= 0 ? p.peer_part[home] : p.part;
+                  dst[(int64_t)v * p.rows + grow] = home >= 0 ? bf16_round(d[jj]) : d[jj];
                 }
-                dst[vv * p.rows + grow] = (v < p.Tk) ? bf16_round(d[jj]) : d[jj];
+              }
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < kPfChunk; ++jj) {
+                if (jj >= nc) break;  // warp-uniform
+                const int v = __shfl_sync(0xffffffffu, mv[c], jj);
+                if (row_ok) {
+                  if constexpr (EPI == EPI_STORE)
+                    p.out_bf16[(int64_t)v * p.rows + grow] = f32_to_bf16_bits(d[jj]);
+                  else
+                    p.part[(int64_t)v * p.rows + grow] = (v < p.Tk) ? bf16_round(d[jj]) : d[jj];
+                }
               }
             }
           } else {
+            // SwiGLU, all four warps: gate rows live in quadrants 0, 1 and
+            // up rows in 2, 3 (row r and 64 + r pair up). Gate warps compute
+            // columns 0-15 of the chunk, up warps columns 16-31; each side
+            // hands the other half of its values over through shared memory
+            // (two buffers alternating per chunk, so one barrier per chunk
+            // suffices: a warp has read chunk cc - 2 before it arrives at the
+            // barrier of chunk cc - 1).
+            constexpr int kH = kPfChunk / 2;
+            const bool gate = row < 64;
+            const int r = gate ? row : row - 64;  // gate / intermediate row of the pair
+            float* xg = upx + (cc & 1u) * 2 * 64 * (kH + 1);  // gate values, columns 16-31
+            float* xu = xg + 64 * (kH + 1);                   // up values, columns 0-15
+            if (gate) {
 #pragma unroll
-            for (int jj = 0; jj < kPfChunk; ++jj) {
-              if (jj >= nc) break;  // warp-uniform
-              const int v = __shfl_sync(0xffffffffu, mv, jj);
-              if (row_ok) {
-                if constexpr (EPI == EPI_STORE)
-                  p.out_bf16[(int64_t)v * p.rows + grow] = f32_to_bf16_bits(d[jj]);
-                else
-                  p.part[(int64_t)v * p.rows + grow] = (v < p.Tk) ? bf16_round(d[jj]) : d[jj];
-              }
+              for (int i = 0; i < kH; ++i) xg[r * (kH + 1) + i] = d[kH + i];
+            } else {
+#pragma unroll
+              for (int i = 0; i < kH; ++i) xu[r * (kH + 1) + i] = d[i];
             }
-          }
-        } else {
-          // SwiGLU: the up rows (quadrants 2, 3) hand their values to the
-          // gate rows (quadrants 0, 1) of the same half through shared memory
-          if (row >= 64) {
-#pragma unroll
-            for (int i = 0; i < kPfChunk; ++i) up[(row - 64) * (kPfChunk + 1) + i] = d[i];
-          }
-          named_bar(2 + half, 128);
-          if (row < 64) {
-            const int hrow = info.rb * 64 + row;  // intermediate index
+            named_bar(2, 128);
+            const int hrow = info.rb * 64 + r;  // intermediate index
             const int pos = perm_pos(hrow, p.h_bits);
             const float lim = p.swiglu_limit;
+            const int j0 = gate ? 0 : kH;
 #pragma unroll
-            for (int jj = 0; jj < kPfChunk; ++jj) {
+            for (int i = 0; i < kH; ++i) {
+              const int jj = j0 + i;
               if (jj >= nc) break;  // warp-uniform
-              const int v = __shfl_sync(0xffffffffu, mv, jj);
-              float g = bf16_round(d[jj]);
-              float u = bf16_round(up[row * (kPfChunk + 1) + jj]);
+              const int v = __shfl_sync(0xffffffffu, mv[c], jj);
+              const float wv = __shfl_sync(0xffffffffu, wl[c], jj);
+              float g = bf16_round(gate ? d[i] : xg[r * (kH + 1) + i]);
+              float u = bf16_round(gate ? xu[r * (kH + 1) + i] : d[kH + i]);
               if (lim > 0.0f) {
                 g = fminf(g, lim);
                 u = fminf(fmaxf(u, -lim), lim);
@@ -469,7 +525,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 if (!p.weight_after_down) {
                   float a = g * sigmoid_f32(g);
                   a = a * u;
-                  a = a * __ldg(p.weights + v);
+                  a = a * wv;
                   hb = f32_to_bf16_bits(a);
                 } else {
                   const float sg = bf16_round(sigmoid_f32(g));
@@ -486,8 +542,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     f32_to_bf16_bits(a - bf16_bits_to_f32(hb));
               }
             }
+            ++cc;
           }
-          named_bar(2 + half, 128);  // the chunk buffer is reused
         }
       }
       tc_fence_before();
