@@ -183,13 +183,33 @@ __global__ void combine_kernel(const float* __restrict__ part, const float* __re
     const int t = (int)(i / H4);
     const int64_t q = i - (int64_t)t * H4;
     float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int j = 0; j < k; ++j) {
-      const float4 v = __ldg(p4 + (int64_t)(t * k + j) * H4 + q);
-      if (!weight_after_down) {
-        s[0] += v.x; s[1] += v.y; s[2] += v.z; s[3] += v.w;
-      } else {
-        const float w = __ldg(weights + t * k + j);
-        s[0] += v.x * w; s[1] += v.y * w; s[2] += v.z * w; s[3] += v.w * w;
+    // the slots' loads (and the shared rows') are issued together, 8 slots
+    // at a time, then summed in slot order: one memory latency per 8 slots
+    // instead of one per slot
+    float4 sh_hi = make_float4(0.f, 0.f, 0.f, 0.f), sh_lo = sh_hi;
+    if (has_shared) {
+      sh_hi = __ldg(p4 + (int64_t)(Tk + t) * H4 + q);
+      sh_lo = __ldg(p4 + (int64_t)(Tk + T + t) * H4 + q);
+    }
+    for (int j0 = 0; j0 < k; j0 += 8) {
+      float4 v[8];
+      float w[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (j0 + u < k) {
+          v[u] = __ldg(p4 + (int64_t)(t * k + j0 + u) * H4 + q);
+          w[u] = weight_after_down ? __ldg(weights + t * k + j0 + u) : 1.0f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (j0 + u < k) {
+          if (!weight_after_down) {
+            s[0] += v[u].x; s[1] += v[u].y; s[2] += v[u].z; s[3] += v[u].w;
+          } else {
+            s[0] += v[u].x * w[u]; s[1] += v[u].y * w[u]; s[2] += v[u].z * w[u]; s[3] += v[u].w * w[u];
+          }
+        }
       }
     }
     if (!weight_after_down) {
@@ -197,12 +217,10 @@ __global__ void combine_kernel(const float* __restrict__ part, const float* __re
       for (int e = 0; e < 4; ++e) s[e] = bf16_round(s[e]);
     }
     if (has_shared) {
-      const float4 hi = __ldg(p4 + (int64_t)(Tk + t) * H4 + q);
-      const float4 lo = __ldg(p4 + (int64_t)(Tk + T + t) * H4 + q);
-      s[0] = s[0] + (hi.x + lo.x);
-      s[1] = s[1] + (hi.y + lo.y);
-      s[2] = s[2] + (hi.z + lo.z);
-      s[3] = s[3] + (hi.w + lo.w);
+      s[0] = s[0] + (sh_hi.x + sh_lo.x);
+      s[1] = s[1] + (sh_hi.y + sh_lo.y);
+      s[2] = s[2] + (sh_hi.z + sh_lo.z);
+      s[3] = s[3] + (sh_hi.w + sh_lo.w);
     }
     if ((reinterpret_cast<uintptr_t>(out) & 7u) == 0) {
       uint2 o;
@@ -2193,18 +2211,34 @@ __global__ void ep_wait_combine_kernel(const float* __restrict__ part,
     const int t = (int)(i / H);
     const int64_t row = i - (int64_t)t * H;
     float s = 0.0f;
-    if (!weight_after_down) {
-      for (int j = 0; j < k; ++j) s += part[(int64_t)(t * k + j) * H + row];
-      s = bf16_round(s);
-    } else {
-      for (int j = 0; j < k; ++j)
-        s += part[(int64_t)(t * k + j) * H + row] * __ldg(weights + t * k + j);
-    }
+    // loads issued 8 slots at a time (and the shared rows up front), sums in
+    // slot order: the same result as one load per step, one latency per 8
+    float hi = 0.0f, lo = 0.0f;
     if (has_shared) {
-      const float hi = part[(int64_t)(Tk + t) * H + row];
-      const float lo = part[(int64_t)(Tk + T + t) * H + row];
-      s = s + (hi + lo);
+      hi = part[(int64_t)(Tk + t) * H + row];
+      lo = part[(int64_t)(Tk + T + t) * H + row];
     }
+    for (int j0 = 0; j0 < k; j0 += 8) {
+      float v[8], w[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (j0 + u < k) {
+          v[u] = part[(int64_t)(t * k + j0 + u) * H + row];
+          w[u] = weight_after_down ? __ldg(weights + t * k + j0 + u) : 1.0f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (j0 + u < k) {
+          if (weight_after_down)
+            s += v[u] * w[u];
+          else
+            s += v[u];
+        }
+      }
+    }
+    if (!weight_after_down) s = bf16_round(s);
+    if (has_shared) s = s + (hi + lo);
     out[i] = f32_to_bf16_bits(ok ? s : 0.0f);
   }
 }

@@ -361,8 +361,65 @@ MR_DEVICE int plan_local_expert(const PlanParams& p, int id) {
   return (g >= 0 && g < p.E) ? g : -1;
 }
 
+// The plan of at most 32 (token, slot) pairs by one warp: lane i holds pair
+// i's key (local expert << 5 | i; pairs of other ranks sort last), a bitonic
+// sort puts the keys in ascending order, each run of one expert is split
+// into segments of <= seg_cols columns, and a warp scan gives each run's
+// first segment. Same plan as the CTA version below (columns of an expert in
+// ascending pair order), without its shared-memory passes and barriers.
+MR_DEVICE void build_plan_warp(const PlanParams& p) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  unsigned key = 0xffffffffu;
+  if (lane < p.Tk) {
+    const int e = plan_local_expert(p, __ldcg(p.ids + lane));
+    if (e >= 0) {
+      key = ((unsigned)e << 5) | (unsigned)lane;
+    } else if (!p.foreign_ok) {
+      atomicOr(p.error, MR_DEVERR_BAD_EXPERT_ID);
+    }
+  }
+#pragma unroll
+  for (int kk = 2; kk <= 32; kk <<= 1) {
+#pragma unroll
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      const unsigned o = __shfl_xor_sync(full, key, j);
+      const bool up = (lane & kk) == 0;
+      const bool lower = (lane & j) == 0;
+      key = (lower == up) ? min(key, o) : max(key, o);
+    }
+  }
+  const bool valid = key != 0xffffffffu;
+  const int e = (int)(key >> 5);
+  if (valid) p.cols[lane] = (int)(key & 31u);
+  const int eprev = __shfl_up_sync(full, e, 1);
+  const bool start = valid && (lane == 0 || eprev != e);
+  const unsigned smask = __ballot_sync(full, start);
+  const int nvalid = __popc(__ballot_sync(full, valid));
+  // run length: up to the next run's start (or the last valid pair)
+  const unsigned above = lane < 31 ? (smask >> (lane + 1)) : 0u;
+  const int next = above ? lane + 1 + __ffs(above) - 1 : nvalid;
+  const int len = start ? next - lane : 0;
+  const int sc = p.seg_cols;
+  const int nseg = start ? (len + sc - 1) / sc : 0;
+  int incl = nseg;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int a = __shfl_up_sync(full, incl, off);
+    if (lane >= off) incl += a;
+  }
+  const int first = incl - nseg;
+  for (int q = 0; q < nseg; ++q)
+    p.segments[first + q] = make_int4(e, lane + q * sc, min(sc, len - q * sc), 0);
+  if (lane == 31) *p.n_segments = incl;
+}
+
 template <int NTHREADS>
 __device__ void build_plan_cta(const PlanParams& p) {
+  if (p.Tk <= 32) {
+    if (threadIdx.x < 32) build_plan_warp(p);
+    return;
+  }
   __shared__ int cnt[kMaxExperts];
   __shared__ int colofs[kMaxExperts];
   __shared__ int segofs[kMaxExperts];
@@ -505,19 +562,20 @@ __global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
     unsigned nonfinite = 0;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) sc[i] = 0.0f;
-    // partial logits summed in partial order; four partials' loads are in
-    // flight together
-    for (int s0 = 0; s0 < p.ks; s0 += 4) {
-      float v[4][kPer];
+    // partial logits summed in partial order; NB partials' loads are in
+    // flight together (one memory latency for a 7168-wide router)
+    constexpr int NB = kPer <= 8 ? 16 : 4;
+    for (int s0 = 0; s0 < p.ks; s0 += NB) {
+      float v[NB][kPer];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < NB; ++u) {
         const float* ps = p.part + ((int64_t)(s0 + u) * p.T + t) * p.E;
 #pragma unroll
         for (int i = 0; i < kPer; ++i)
           v[u][i] = (s0 + u < p.ks && lane + 32 * i < p.E) ? __ldcg(ps + lane + 32 * i) : 0.0f;
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < NB; ++u)
         if (s0 + u < p.ks) {
 #pragma unroll
           for (int i = 0; i < kPer; ++i) sc[i] += v[u][i];
