@@ -1234,13 +1234,18 @@ static mr_status topk_launch(mr_ctx* ctx, const float* part, int ks, int64_t T,
   const int grid = (int)((T + 7) / 8);
   const int epl = (c->experts + 31) / 32;
   cudaError_t st;
-  if (epl <= 1) st = launch_pdl(topk_kernel<1>, grid, 256, 0, s, tp);
-  else if (epl <= 2) st = launch_pdl(topk_kernel<2>, grid, 256, 0, s, tp);
-  else if (epl <= 4) st = launch_pdl(topk_kernel<4>, grid, 256, 0, s, tp);
-  else if (epl <= 8) st = launch_pdl(topk_kernel<8>, grid, 256, 0, s, tp);
-  else if (epl <= 12) st = launch_pdl(topk_kernel<12>, grid, 256, 0, s, tp);
-  else if (epl <= 16) st = launch_pdl(topk_kernel<16>, grid, 256, 0, s, tp);
-  else st = launch_pdl(topk_kernel<32>, grid, 256, 0, s, tp);
+  const bool small = T <= 16;
+  if (epl <= 1) st = small ? launch_pdl(topk_kernel<1, 16>, grid, 256, 0, s, tp)
+                           : launch_pdl(topk_kernel<1, 4>, grid, 256, 0, s, tp);
+  else if (epl <= 2) st = small ? launch_pdl(topk_kernel<2, 16>, grid, 256, 0, s, tp)
+                                : launch_pdl(topk_kernel<2, 4>, grid, 256, 0, s, tp);
+  else if (epl <= 4) st = small ? launch_pdl(topk_kernel<4, 16>, grid, 256, 0, s, tp)
+                                : launch_pdl(topk_kernel<4, 4>, grid, 256, 0, s, tp);
+  else if (epl <= 8) st = small ? launch_pdl(topk_kernel<8, 16>, grid, 256, 0, s, tp)
+                                : launch_pdl(topk_kernel<8, 4>, grid, 256, 0, s, tp);
+  else if (epl <= 12) st = launch_pdl(topk_kernel<12, 4>, grid, 256, 0, s, tp);
+  else if (epl <= 16) st = launch_pdl(topk_kernel<16, 4>, grid, 256, 0, s, tp);
+  else st = launch_pdl(topk_kernel<32, 4>, grid, 256, 0, s, tp);
   return cuda_check(ctx, st, "topk_kernel");
 }
 

@@ -551,7 +551,7 @@ MR_DEVICE bool better(float va, int ia, float vb, int ib) {
 
 // One warp per token. Descending choice score, ties to the lower index
 // (Operators/MoE.swift:128, Operators/DeepSeekV4Routing.swift:215-219).
-template <int EPL>  // experts per lane (E <= 32 * EPL)
+template <int EPL, int NB>  // experts per lane (E <= 32 * EPL), partial loads in flight
 __global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
   pdl_wait_and_release();
   const int lane = threadIdx.x & 31;
@@ -563,8 +563,9 @@ __global__ void __launch_bounds__(256) topk_kernel(const TopkParams p) {
 #pragma unroll
     for (int i = 0; i < kPer; ++i) sc[i] = 0.0f;
     // partial logits summed in partial order; NB partials' loads are in
-    // flight together (one memory latency for a 7168-wide router)
-    constexpr int NB = kPer <= 8 ? 16 : 4;
+    // flight together (16 for small batches: one memory latency for a
+    // 7168-wide router; 4 for large ones, whose CTAs share the SMs' load
+    // queues)
     for (int s0 = 0; s0 < p.ks; s0 += NB) {
       float v[NB][kPer];
 #pragma unroll
