@@ -17,12 +17,15 @@ C-ABI call (pinned host x in, host out, copies inside the timed region);
 launching stream; `cpu_baseline` times the CPU oracle on the host cores.
 Under torchrun (N > 1) the layer is expert-parallel: rank r holds routed
 experts [r*E/N, (r+1)*E/N) of every layer and T tokens of an N*T-token
-global batch (weak scaling: T per GPU fixed); one step = NCCL all-gather of
-the tokens, router over all of them, the rank's experts — whose down GEMV
-stores each routed partial straight into the token's home GPU over NVLink —
-then the shared expert and the slot-ordered combine on the home GPU
-(`--ep-nccl`: per-token sums and an NCCL reduce-scatter instead). The time
-is the max over ranks; `value` counts all N*T tokens.
+global batch (weak scaling: T per GPU fixed). The token exchange is one of
+three modes: NCCL all-gather of the tokens with the router over all of them;
+the same with an NCCL reduce-scatter of per-token sums; or a peer all-to-all
+dispatch of each token to the GPUs holding its experts. In the fused modes
+the rank's down GEMV stores each routed partial straight into the token's
+home GPU over NVLink, followed by the shared expert and the slot-ordered
+combine there. `--ep-mode auto` (default) times the three on the headline
+batch after warm-up and runs the headline in the fastest; `ep_modes` reports
+all three. The time is the max over ranks; `value` counts all N*T tokens.
 """
 from __future__ import annotations
 
@@ -75,10 +78,12 @@ def parse():
     p.add_argument("--ep-nccl", action="store_true",
                    help="expert parallel: NCCL reduce-scatter instead of the fused peer stores "
                         "(same as --ep-mode nccl)")
-    p.add_argument("--ep-mode", choices=["allgather", "nccl", "alltoall"], default="alltoall",
+    p.add_argument("--ep-mode", choices=["auto", "allgather", "nccl", "alltoall"],
+                   default="auto",
                    help="expert-parallel token exchange: NCCL all-gather + fused peer combine, "
                         "NCCL all-gather + reduce-scatter, or peer all-to-all dispatch + fused "
-                        "peer combine")
+                        "peer combine; auto (default) times each on the headline batch after "
+                        "warm-up and runs the headline in the fastest")
     p.add_argument("--no-ep-compare", action="store_true",
                    help="N > 1: skip timing the other exchange modes beside the headline")
     p.add_argument("--config", default="1", choices=["1", "2b2", "2b8"],
@@ -242,6 +247,9 @@ def run_ours(args, world, rank, local):
     if args.ep_nccl:
         args.ep_mode = "nccl"
     group = M.ExpertGroup(local, rank, world) if ep else None
+    auto_mode = args.ep_mode == "auto"
+    if auto_mode:
+        args.ep_mode = "alltoall"  # until the probe below has measured the modes
     if group is not None:
         group.set_mode(args.ep_mode)
     torch.cuda.synchronize()
@@ -327,6 +335,18 @@ def run_ours(args, world, rank, local):
         per = {k: {"ms_per_step": max_over_ranks(v[0] / K), "launches_per_step": v[1] / K}
                for k, v in prof.items() if v[1]}
         return prof, per
+
+    # expert parallel, --ep-mode auto: every exchange mode on the headline
+    # batch (same steps and warm-up as the headline, max over ranks, so every
+    # rank picks the same), then the headline in the fastest
+    mode_probe = None
+    if ep and auto_mode:
+        mode_probe = {}
+        for mode in ("allgather", "nccl", "alltoall"):
+            group.set_mode(mode)
+            mode_probe[mode] = world * T * K / (timed(T, K, W) / 1e3)
+        args.ep_mode = max(mode_probe, key=mode_probe.get)
+        group.set_mode(args.ep_mode)
 
     with ClockSampler(local) as clk:
         ms = timed(T, K, W)
@@ -482,6 +502,8 @@ def run_ours(args, world, rank, local):
             "layers_cycled": NL,
             "l2": "inputs larger than L2: consecutive steps read different layers' experts "
                   "(>= 227 MB each)",
+            "exchange_mode": args.ep_mode if ep else None,
+            "exchange_mode_probe_tokens_per_s": mode_probe,
             "parallelism": "single GPU" if world == 1 else
                            f"ep{world}: {spec.experts // world} routed experts per GPU, " +
                            {"nccl": "NCCL all-gather of tokens, NCCL reduce-scatter of per-token "
@@ -710,11 +732,15 @@ def prefill_run(args, S, M, torch, ctx, local, dev, group=None, world=1, rank=0,
     # the Zipf router favours low expert ids: strided placement spreads the
     # hot experts over the GPUs (contiguous ranges would put them all on one)
     if ep:
+        # the all-to-all dispatch: each GPU receives only the rows routed to
+        # its experts (the all-gather modes would hand every GPU all N * T)
         group.set_placement("strided")
+        group.set_mode("alltoall")
         try:
             return _prefill(args, S, torch, ctx, local, dev, group, world, rank, dist, spec, T)
         finally:
             group.set_placement("contiguous")
+            group.set_mode(args.ep_mode)
     return _prefill(args, S, torch, ctx, local, dev, group, world, rank, dist, spec, T)
 
 
