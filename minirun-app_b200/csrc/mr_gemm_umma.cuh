@@ -346,21 +346,27 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // the A buffer was last read by the MMAs of stage j-2
         if (j >= 2) warp_wait(aempty + ab, ((j >> 1) & 1u) ^ 1u, flags, p.error);
         tc_fence_after();
+        // every group's codes of the stage first: the TMEM stores below are
+        // compiler barriers, so loads issued after one would wait for it
+        uint32_t w[ST::kGpw][2 * BITS];
 #pragma unroll
         for (int i = 0; i < ST::kGpw; ++i) {
           const int g = half * ST::kGpw + i;  // stage-local group
-          uint32_t w[2 * BITS];
 #pragma unroll
           for (int c = 0; c < ST::kChunks; ++c) {
             const uint32_t ch = (uint32_t)(g * ST::kChunks + c);
             const uint4 q = lds_b128(stg + rowoff + ((ch ^ rsw) << 4));
-            w[4 * c] = q.x;
-            w[4 * c + 1] = q.y;
-            w[4 * c + 2] = q.z;
-            w[4 * c + 3] = q.w;
+            w[i][4 * c] = q.x;
+            w[i][4 * c + 1] = q.y;
+            w[i][4 * c + 2] = q.z;
+            w[i][4 * c + 3] = q.w;
           }
+        }
+#pragma unroll
+        for (int i = 0; i < ST::kGpw; ++i) {
+          const int g = half * ST::kGpw + i;
           uint32_t wv[32];
-          dequant_full<BITS>(wv, w, s2[i], z2[i]);
+          dequant_full<BITS>(wv, w[i], s2[i], z2[i]);
           __syncwarp();
           tmem_st32(lane_t + ab * ST::kABuf + g * 32, wv);
         }
