@@ -25,10 +25,12 @@
 // Two A buffers let dequantisation overlap the MMAs; two accumulators and
 // the separate epilogue warps let one tile's epilogue (tcgen05.ld in
 // 32-column chunks: SwiGLU -> h, or per-slot partials) overlap the next
-// tile's dequantisation and MMAs. At N = 128 one MMA takes
-// ~64 cycles, the tensor core's full rate, so the kernel is bound by the
-// tensor pipe (and the L2 -> shared-memory feed of activations), not by the
-// per-instruction cost that limits small-N decode MMAs.
+// tile's dequantisation and MMAs. What bounds it (measured with builds that
+// drop one part at a time): the workers' per-stage pipeline — dequantising
+// 128 codes per thread, TMEM stores and their wait, latency-bound at ~0.2
+// instructions per cycle per sub-partition — more than the MMAs (at N = 128
+// close to the tensor core's rate per instruction) or the activation feed
+// (dropping the activation loads changed nothing).
 // Worker and epilogue warps poll their barriers (one lane, then the warp)
 // rather than sleep in try_wait with a suspend hint: the hand-offs here
 // are a few hundred cycles apart, and polling measured 6 % faster.
